@@ -1,0 +1,115 @@
+"""Seeded synthetic GGUF models matching the benchmark configurations.
+
+The writer itself is native (csrc/synth/gguf_synth.cpp, built into
+lib/libfishsynth.so); this module holds the shape presets and a ctypes call.
+
+Presets (shapes from the benchmark configurations):
+  tiny      llama, 4 layers, d_model 512, 8/4 heads (head_dim 64), FFN 1408,
+            vocab 32000, eps 1e-5, theta 1e4, every matrix Q8_0
+  llama8b   Llama-3-8B shape: 32 layers, 4096, 32/8 heads, FFN 14336,
+            vocab 128256, theta 5e5, Q4_K_M mixture
+  qwen7b    Qwen2.5-7B shape: 28 layers, 3584, 28/4 heads, qkv bias,
+            FFN 18944, vocab 152064, theta 1e6, Q4_K_M mixture
+  mixtral   Mixtral-8x7B shape: 32 layers, 4096, 32/8 heads, 8 experts top-2,
+            expert FFN 14336, vocab 32000, theta 1e6, Q4_K_M mixture
+  llama70b  Llama-3-70B shape: 80 layers, 8192, 64/8 heads, FFN 28672,
+            vocab 128256, theta 5e5, Q4_K_M mixture
+
+`layers=` truncates a preset (same widths, fewer blocks) for parity runs.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+from dataclasses import dataclass, replace
+from pathlib import Path
+
+from . import libpath
+
+
+@dataclass(frozen=True)
+class SynthConfig:
+    arch: str = "llama"
+    n_layers: int = 4
+    n_embd: int = 512
+    n_ff: int = 1408
+    n_head: int = 8
+    n_head_kv: int = 4
+    vocab: int = 32000
+    n_ctx_train: int = 8192
+    eps: float = 1e-5
+    freq_base: float = 10000.0
+    n_experts: int = 0
+    n_experts_per_tok: int = 0
+    qkv_bias: int = 0
+    wtype: int = 8          # 8 = all Q8_0, 12 = Q4_K_M mixture
+    seed: int = 1234
+    wstd: float = 0.02
+    router_std: float = 0.125
+
+
+PRESETS = {
+    "tiny": SynthConfig(),
+    "llama8b": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
+                           vocab=128256, freq_base=500000.0, wtype=12),
+    "qwen7b": SynthConfig(arch="qwen2", n_layers=28, n_embd=3584, n_ff=18944, n_head=28,
+                          n_head_kv=4, vocab=152064, freq_base=1000000.0, eps=1e-6,
+                          qkv_bias=1, wtype=12, n_ctx_train=32768),
+    "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
+                           vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
+                           wtype=12, n_ctx_train=32768),
+    "llama70b": SynthConfig(n_layers=80, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8,
+                            vocab=128256, freq_base=500000.0, wtype=12),
+}
+
+
+class _CConfig(ctypes.Structure):
+    _fields_ = [
+        ("arch", ctypes.c_char_p),
+        ("n_layers", ctypes.c_int), ("n_embd", ctypes.c_int), ("n_ff", ctypes.c_int),
+        ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int), ("vocab", ctypes.c_int),
+        ("n_ctx_train", ctypes.c_int),
+        ("eps", ctypes.c_float), ("freq_base", ctypes.c_float),
+        ("n_experts", ctypes.c_int), ("n_experts_per_tok", ctypes.c_int),
+        ("qkv_bias", ctypes.c_int), ("wtype", ctypes.c_int),
+        ("seed", ctypes.c_ulonglong), ("wstd", ctypes.c_float), ("router_std", ctypes.c_float),
+    ]
+
+
+def preset(name: str, layers: int | None = None, **overrides) -> SynthConfig:
+    cfg = PRESETS[name]
+    if layers is not None:
+        cfg = replace(cfg, n_layers=layers)
+    if overrides:
+        cfg = replace(cfg, **overrides)
+    return cfg
+
+
+def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
+    """Write the synthetic GGUF; returns the path. Raises on failure."""
+    lib = ctypes.CDLL(str(libpath("libfishsynth.so")))
+    fn = lib.fish_synth_write
+    fn.argtypes = [ctypes.c_char_p, ctypes.POINTER(_CConfig), ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+    fn.restype = ctypes.c_int
+    c = _CConfig(cfg.arch.encode(), cfg.n_layers, cfg.n_embd, cfg.n_ff, cfg.n_head, cfg.n_head_kv,
+                 cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
+                 cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std)
+    err = ctypes.create_string_buffer(256)
+    rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
+    if rc != 0:
+        raise RuntimeError(f"fish_synth_write failed: {err.value.decode()}")
+    return Path(path)
+
+
+def cached(cfg: SynthConfig, directory: str | os.PathLike | None = None, threads: int = 0) -> Path:
+    """Write the model once per (config) into a cache directory and reuse it."""
+    d = Path(directory or os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    d.mkdir(parents=True, exist_ok=True)
+    key = int(hashlib.sha1(repr(cfg).encode()).hexdigest()[:12], 16)
+    path = d / f"{cfg.arch}_L{cfg.n_layers}_E{cfg.n_embd}_w{cfg.wtype}_s{cfg.seed}_{key:012x}.gguf"
+    if not path.exists():
+        tmp = path.with_suffix(".tmp")
+        write(tmp, cfg, threads)
+        tmp.rename(path)
+    return path

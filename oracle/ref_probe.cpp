@@ -1,0 +1,111 @@
+/*
+ * ref_probe.cpp — a thin C entry-point layer over the REFERENCE FISH engine.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is compiled together with the unmodified
+ * reference sources (read from the reference checkout by oracle/Makefile) into
+ * oracle/_ref/libfish_ref.so. It exposes the reference's internal C++ API
+ * (include/fish/quant.h, model.h) as plain C functions so the tests can pin the
+ * oracle restatement, generate golden vectors, and time the reference CPU path
+ * as the CPU baseline. It contains no arithmetic of its own.
+ */
+#include <fish/model.h>
+#include <fish/quant.h>
+#include <fish/ops.h>
+#include <fish/threadpool.h>
+
+#include <cstring>
+#include <memory>
+#include <string>
+
+using namespace fish;
+
+extern "C" {
+
+__attribute__((visibility("default"))) const char* ref_kernel_name(void) { return quant_kernels().name; }
+
+__attribute__((visibility("default"))) void ref_quantize_acts(const float* x, uint64_t n, void* out) {
+    quantize_acts(x, n, static_cast<Q8Act*>(out));
+}
+__attribute__((visibility("default"))) void ref_quantize_acts_k(const float* x, uint64_t n, void* out) {
+    quantize_acts_k(x, n, static_cast<Q8ActK*>(out));
+}
+/* scalar table (quant.cpp:436-456), to pin the AVX2 table the build installs. */
+__attribute__((visibility("default"))) void ref_quantize_acts_scalar(const float* x, uint64_t n, void* out) {
+    scalar_kernels().quantize(x, n, static_cast<Q8Act*>(out));
+}
+__attribute__((visibility("default"))) void ref_quantize_acts_k_scalar(const float* x, uint64_t n, void* out) {
+    scalar_kernels().quantize_k(x, n, static_cast<Q8ActK*>(out));
+}
+__attribute__((visibility("default"))) int ref_vec_dot_q8(int type, const void* row, const void* x, uint64_t n, float* out) {
+    return vec_dot_q8(static_cast<GgmlType>(type), row, static_cast<const Q8Act*>(x), n, out) ? 1 : 0;
+}
+__attribute__((visibility("default"))) int ref_vec_dot_q8k(int type, const void* row, const void* x, uint64_t n, float* out) {
+    return vec_dot_q8k(static_cast<GgmlType>(type), row, static_cast<const Q8ActK*>(x), n, out) ? 1 : 0;
+}
+__attribute__((visibility("default"))) int ref_dequant_row(int type, const void* src, float* dst, uint64_t n) {
+    return dequant_row(static_cast<GgmlType>(type), src, dst, n) ? 1 : 0;
+}
+__attribute__((visibility("default"))) int ref_quantize_row(int type, const float* x, void* dst, uint64_t n) {
+    return quantize_row(static_cast<GgmlType>(type), x, dst, n) ? 1 : 0;
+}
+__attribute__((visibility("default"))) void ref_rmsnorm(float* out, const float* x, const float* w, int n, float eps) {
+    rmsnorm(out, x, w, n, eps);
+}
+__attribute__((visibility("default"))) void ref_attention(const float* q, const float* k, const float* v, int n_ctx,
+                                                          int n_head, int n_head_kv, int head_dim, int pos0, int n_tok,
+                                                          float* out, float scale) {
+    attention_batch(q, k, v, n_ctx, n_head, n_head_kv, head_dim, pos0, n_tok, out, scale, 0.0f, 0);
+}
+__attribute__((visibility("default"))) void ref_rope_table(int n_ctx, int head_dim, int rot_dim, int neox,
+                                                           float freq_base, float* cos_out, float* sin_out) {
+    RopeParams p;
+    p.head_dim = head_dim;
+    p.rot_dim = rot_dim;
+    p.freq_base = freq_base;
+    p.neox = neox != 0;
+    RopeCache c;
+    rope_build(c, n_ctx, p);
+    std::memcpy(cos_out, c.cos_.data(), c.cos_.size() * sizeof(float));
+    std::memcpy(sin_out, c.sin_.data(), c.sin_.size() * sizeof(float));
+}
+__attribute__((visibility("default"))) void ref_set_threads(int n) { ThreadPool::instance().set_active_threads(n); }
+__attribute__((visibility("default"))) int ref_threads(void) { return ThreadPool::instance().active_threads(); }
+
+struct RefModel { std::unique_ptr<LlamaModel> m; std::string err; };
+
+__attribute__((visibility("default"))) void* ref_model_load(const char* path, int n_ctx, char* err, int cap) {
+    auto* h = new RefModel();
+    LlamaModel::LoadOptions o;
+    o.gpu_layers = 0;
+    o.allow_span = false;
+    h->m = LlamaModel::load(path, n_ctx, o, &h->err);
+    if (!h->m) {
+        if (err && cap > 0) std::snprintf(err, static_cast<size_t>(cap), "%s", h->err.c_str());
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+__attribute__((visibility("default"))) void ref_model_free(void* h) { delete static_cast<RefModel*>(h); }
+__attribute__((visibility("default"))) int ref_model_vocab(void* h) { return static_cast<RefModel*>(h)->m->config().vocab; }
+__attribute__((visibility("default"))) int ref_model_n_ctx(void* h) { return static_cast<RefModel*>(h)->m->config().n_ctx; }
+__attribute__((visibility("default"))) int ref_model_max_batch(void* h) { return static_cast<RefModel*>(h)->m->max_batch(); }
+/* LlamaModel::forward (model.cpp:1603-1811); logits of the last token copied out,
+ * and with logits_all non-null every token's (all_logits=true). */
+__attribute__((visibility("default"))) int ref_model_forward(void* h, const int32_t* tokens, int n, int pos0,
+                                                             float* logits, float* logits_all) {
+    LlamaModel& m = *static_cast<RefModel*>(h)->m;
+    if (!m.forward(tokens, n, pos0, logits_all != nullptr)) return 0;
+    const int V = m.config().vocab;
+    if (logits) std::memcpy(logits, m.logits(), sizeof(float) * static_cast<size_t>(V));
+    if (logits_all) std::memcpy(logits_all, m.logits_at(0), sizeof(float) * static_cast<size_t>(V) * n);
+    return 1;
+}
+__attribute__((visibility("default"))) int ref_model_argmax(void* h) { return static_cast<RefModel*>(h)->m->argmax(); }
+__attribute__((visibility("default"))) void ref_model_set_kv_len(void* h, int n) { static_cast<RefModel*>(h)->m->set_kv_len(n); }
+__attribute__((visibility("default"))) void ref_model_reset(void* h) { static_cast<RefModel*>(h)->m->reset_kv(); }
+__attribute__((visibility("default"))) unsigned long long ref_model_weights_bytes(void* h) {
+    return static_cast<RefModel*>(h)->m->weights_bytes();
+}
+
+}  // extern "C"

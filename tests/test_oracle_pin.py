@@ -1,0 +1,130 @@
+"""Pin the C restatement (oracle/fish_oracle.c) before it is trusted.
+
+Against the golden vectors made by the reference engine (tests/golden/), and,
+where the reference build is present, against the live reference on fresh
+seeded inputs. Mirrors the reference's own kernel test:
+test/test_kernels.cpp:154-235 (byte-identical activation quantisation, int8
+dots equal to the scalar path within 1e-5 of sum |w x|) and the Q4_K layout
+known-answer test test/test_m1.cpp:35-71.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+TYPES = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+
+
+def test_activation_quantisers_byte_identical(golden, oracle):
+    for kind in range(4):
+        for n in (256, 4096):
+            x = golden[f"acts_x{kind}_{n}"]
+            assert np.array_equal(oracle.quantize_acts(x), golden[f"acts_q32_{kind}_{n}"]), (kind, n)
+            assert np.array_equal(oracle.quantize_acts_k(x), golden[f"acts_qk_{kind}_{n}"]), (kind, n)
+
+
+def test_int8_dots_match_reference(golden, oracle):
+    for name, t in TYPES.items():
+        for i in range(12):
+            row, acts = golden[f"row_{name}_{i}"], golden[f"rowx_{name}_{i}"]
+            n = 256 if i < 6 else 4096
+            want = float(golden[f"rowdot_{name}_{i}"][0])
+            y = oracle.vec_dot(t, row, acts, n)
+            # mass = sum |w * xq| (test/test_kernels.cpp:197-205)
+            mass = 1e-9 + abs(want) + 1.0
+            if n == 256:
+                w = golden[f"rowdeq_{name}_{i}"]
+                mass = 1e-9 + float(np.abs(w).sum()) * 2.0
+            assert abs(y - want) <= 1e-5 * mass + 1e-6 * abs(want), (name, i, y, want)
+
+
+def test_dequant_matches_reference(golden, oracle):
+    for name, t in TYPES.items():
+        for i in range(6):
+            row = golden[f"row_{name}_{i}"]
+            assert np.array_equal(oracle.dequant(t, row, 256), golden[f"rowdeq_{name}_{i}"]), (name, i)
+
+
+def test_q4k_known_answer(golden, oracle):
+    y = oracle.dequant(12, golden["q4k_kat"], 256)
+    want = np.array([(l & 15) for j in range(0, 256, 64) for l in list(range(32)) * 2], np.float32)
+    assert np.array_equal(y, want)
+    assert np.array_equal(y, golden["q4k_kat_deq"])
+
+
+def test_tiny_model_logits_match_reference_golden(golden, oracle, tiny_gguf):
+    m = oracle.load(tiny_gguf, 2048)
+    ids = golden["tiny_ids"]
+    steps = [m.forward(ids[:16], 0)] + [m.forward(ids[s:s + 1], s) for s in range(16, 18)]
+    for got, want in zip(steps, golden["tiny_logits"]):
+        diff = np.abs(got - want)
+        # reference's own engine-vs-engine criterion (test/test_gpu.cpp:577-591)
+        assert diff.max() <= 0.02 * np.abs(want).max()
+        assert int(np.argmax(got)) == int(np.argmax(want))
+
+
+def test_block_sums_equal_float_definition(oracle, reference):
+    """Integer block sums: y reconstructed from (sumi, mins) equals the reference dot."""
+    rng = np.random.default_rng(3)
+    for t in (8, 12, 14):
+        n = 4096
+        w = rng.standard_normal(n).astype(np.float32) * 0.05
+        row = reference.quantize_row(t, w)
+        x = rng.standard_normal(n).astype(np.float32)
+        acts = reference.quantize_acts_k(x) if t in (12, 14) else reference.quantize_acts(x)
+        s, m = oracle.block_sums(t, row, acts, n)
+        ref_y = reference.vec_dot(t, row, acts, n)
+        bb = {8: 34, 12: 144, 14: 210}[t]
+        nb = s.size
+        y = 0.0
+        for b in range(nb):
+            blk = row[b * bb:(b + 1) * bb]
+            if t == 8:
+                dx = np.frombuffer(acts[b * 40:b * 40 + 4].tobytes(), np.float32)[0]
+                dw = np.frombuffer(blk[0:2].tobytes(), np.float16)[0].astype(np.float32)
+                y += float(np.float32(dw * dx)) * s[b]
+            else:
+                dx = np.frombuffer(acts[b * 276:b * 276 + 4].tobytes(), np.float32)[0]
+                if t == 14:
+                    dw = np.frombuffer(blk[208:210].tobytes(), np.float16)[0].astype(np.float32)
+                    y += float(np.float32(dw * dx)) * s[b]
+                else:
+                    dw = np.frombuffer(blk[0:2].tobytes(), np.float16)[0].astype(np.float32)
+                    dm = np.frombuffer(blk[2:4].tobytes(), np.float16)[0].astype(np.float32)
+                    y += float(np.float32(dw * dx)) * s[b] - float(np.float32(dm * dx)) * m[b]
+        assert abs(y - ref_y) <= 1e-5 * (abs(ref_y) + 1.0), (t, y, ref_y)
+
+
+def test_live_reference_quantisers(oracle, reference):
+    rng = np.random.default_rng(99)
+    for n in (256, 4096, 14336):
+        for scale in (1e-3, 1.0, 300.0):
+            x = (rng.standard_normal(n) * scale).astype(np.float32)
+            x[::97] = np.round(x[::97])  # some integral values
+            assert np.array_equal(oracle.quantize_acts(x), reference.quantize_acts(x))
+            if n % 256 == 0:
+                assert np.array_equal(oracle.quantize_acts_k(x), reference.quantize_acts_k(x))
+                assert np.array_equal(reference.quantize_acts_k(x), reference.quantize_acts_k(x, scalar=True))
+
+
+def test_live_reference_model(oracle, reference, tiny_gguf):
+    rm = reference.load(tiny_gguf, 2048)
+    om = oracle.load(tiny_gguf, 2048)
+    ids = np.random.default_rng(21).integers(3, 32000, 40).astype(np.int32)
+    a, b = rm.forward(ids[:32], 0), om.forward(ids[:32], 0)
+    assert np.abs(a - b).max() <= 0.02 * np.abs(a).max()
+    for s in range(32, 40):
+        a, b = rm.forward(ids[s:s + 1], s), om.forward(ids[s:s + 1], s)
+        assert np.abs(a - b).max() <= 0.02 * np.abs(a).max()
+
+
+@pytest.mark.parametrize("n_tok", [1, 5])
+def test_live_reference_attention(oracle, reference, n_tok):
+    rng = np.random.default_rng(n_tok)
+    H, HKV, D, n_ctx, pos0 = 8, 2, 128, 64, 30
+    q = rng.standard_normal((n_tok, H * D)).astype(np.float32)
+    k = rng.standard_normal((n_ctx, HKV * D)).astype(np.float32)
+    v = rng.standard_normal((n_ctx, HKV * D)).astype(np.float32)
+    a = reference.attention(q, k, v, n_ctx, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D))
+    b = oracle.attention(q, k, v, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D))
+    assert np.abs(a - b).max() < 1e-5
