@@ -1,0 +1,321 @@
+"""Decode throughput of the B200 FISH engine on the Llama-3-8B-shaped Q4_K_M
+workload (batch 1, prompt 512 random ids, greedy decode), one JSON line.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token. `value` is device-timed (CUDA events on the
+engine's stream around K graph-replayed greedy steps, weights resident);
+`e2e` is the same metric through the C ABI call a user makes per token
+(fish_decode_ids with host buffers: the token id goes up and the argmax comes
+back every step). Under torchrun each rank runs an independent replica on its
+own GPU (the 8B model fits one GPU: replicas only) and the max time over
+ranks is used. `--impl reference` times the reference FISH CPU engine
+(oracle/_ref, its own sources) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+LOCAL_RANK = int(os.environ.get("LOCAL_RANK", "0"))
+RANK = int(os.environ.get("RANK", "0"))
+WORLD = int(os.environ.get("WORLD_SIZE", "1"))
+if WORLD > 1 and "CUDA_VISIBLE_DEVICES" not in os.environ:
+    os.environ["CUDA_VISIBLE_DEVICES"] = str(LOCAL_RANK)
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
+PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
+PROMPT = 512
+N_CTX = 1024
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_init():
+    if WORLD <= 1:
+        return None
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    return dist
+
+
+def max_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def model_path(dist):
+    from imurun_b200 import synth
+    cfg = synth.preset("llama8b")
+    d = os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")
+    if RANK == 0:
+        t0 = time.time()
+        p = synth.cached(cfg, d)
+        log(f"[bench] model {p} ({p.stat().st_size / 1e9:.2f} GB, {time.time() - t0:.1f} s)")
+    barrier(dist)
+    return synth.cached(cfg, d)
+
+
+def peaks():
+    if PEAKS_PATH.exists():
+        p = json.loads(PEAKS_PATH.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles():
+    f = ROOT / "profiles" / "gemv_llama8b_decode.txt"
+    if not f.exists():
+        return None
+    for ln in f.read_text().splitlines():
+        if ln.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(ln.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={os.environ.get('CUDA_VISIBLE_DEVICES', '0').split(',')[0]}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ln in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) >= 8:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_decode(path, n_prompt: int, n_decode: int):
+    """Reference FISH CPU engine (oracle/_ref) with all host threads:
+    prefill n_prompt ids, then time n_decode greedy decode steps."""
+    from oracle.binding import REF_SO, Oracle, Reference
+    cores = os.cpu_count() or 1
+    ids = np.random.default_rng(1).integers(3, 128256, n_prompt).astype(np.int32)
+    if REF_SO.exists():
+        ref = Reference()
+        ref.set_threads(cores)
+        m = ref.load(path, N_CTX)
+        lg = m.prefill(ids)
+        tok = int(np.argmax(lg))
+        t0 = time.perf_counter()
+        for s in range(n_decode):
+            lg = m.forward(np.array([tok], np.int32), n_prompt + s)
+            tok = int(np.argmax(lg))
+        dt = time.perf_counter() - t0
+        m.close()
+        return n_decode / dt, "reference", ref.threads(), dt
+    o = Oracle()
+    m = o.load(path, N_CTX)
+    lg = m.forward(ids, 0)
+    tok = int(np.argmax(lg))
+    t0 = time.perf_counter()
+    for s in range(n_decode):
+        lg = m.forward(np.array([tok], np.int32), n_prompt + s)
+        tok = int(np.argmax(lg))
+    dt = time.perf_counter() - t0
+    return n_decode / dt, "port", 1, dt
+
+
+def run_reference(args):
+    if RANK != 0:
+        return 0
+    from imurun_b200 import synth
+    path = synth.cached(synth.preset("llama8b"), os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    n_prompt = 32
+    k = min(args.steps, 32)
+    w = min(args.warmup, 4)
+    value, kind, cores, dt = cpu_reference_decode(path, n_prompt, k + w)
+    sample = (f"Llama-3-8B-shaped Q4_K_M, prompt {n_prompt} random ids, {k + w} greedy decode steps "
+              f"(steps capped at 32 + 4 for the CPU), batch 1")
+    line = {
+        "impl": "reference", "metric": BASELINE["metric"], "value": round(value, 4), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": k, "warmup": w, "ms_per_step": round(1000.0 / value, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "llama8b-shaped Q4_K_M decode, batch 1 (reference FISH CPU engine)",
+                   "global_batch": 1, "seq_len": n_prompt + k + w, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    from imurun_b200.native import Model
+    dist = dist_init()
+    path = model_path(dist)
+    K, W = args.steps, args.warmup
+    n_ctx = max(N_CTX, (PROMPT + W + K + 64 + 255) // 256 * 256)
+    if n_ctx > 8192:
+        raise SystemExit("steps + warmup too large for the 8192-token context")
+    m = Model(path, n_ctx)
+    rng = np.random.default_rng(1234 + RANK)
+    ids = rng.integers(3, m.vocab, PROMPT).astype(np.int32)
+
+    # prefill (wall clock, host ids in, last logits out)
+    m.prefill(ids[:64], 0)                   # warm the prefill kernels
+    t0 = time.perf_counter()
+    lg = m.prefill(ids, 0)
+    prefill_s = time.perf_counter() - t0
+    first = int(np.argmax(lg))
+
+    # warm-up: W greedy steps (captures the graph)
+    out = m.greedy(first, W)
+    nxt = int(out[-1])
+    pos_start = m.kv_len()
+
+    # timed region: K graph-replayed greedy steps, device-timed
+    barrier(dist)
+    clocks = Clocks()
+    clocks.start()
+    out = m.greedy(nxt, K)
+    eng = json.loads(m.lib.fish_engine_json(m.ctx).decode())
+    dev_ms = float(eng["last_decode_device_ms"])
+    clk = clocks.stop()
+    barrier(dist)
+    dev_ms_max = max_over_ranks(dist, dev_ms)
+    value = WORLD * K / (dev_ms_max / 1000.0)
+
+    # e2e: the per-token C-ABI call with host buffers, same positions
+    m.set_kv_len(pos_start)
+    tok = np.array([nxt], np.int32)
+    am = np.zeros(1, np.int32)
+    barrier(dist)
+    t0 = time.perf_counter()
+    for s in range(K):
+        rc = m.lib.fish_decode_ids(m.ctx, tok.ctypes.data, 1, pos_start + s, None, am.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(m.lib.fish_last_error(m.ctx).decode())
+        tok[0] = am[0]
+    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(dist, e2e_s)
+    e2e_value = WORLD * K / e2e_s
+
+    # roofline of the dominant kernel (the quantised GEMV): per-launch events
+    m.set_kv_len(pos_start)
+    prof = json.loads(m.lib.fish_profile_decode_json(m.ctx, nxt, 16).decode())
+    cls = {c["name"]: c for c in prof["classes"]}
+    g = cls["gemv"]
+    peak, peak_kind = peaks()
+    achieved = (g["bytes"] / g["launches"]) / ((g["ms"] / g["launches"]) / 1e3) / 1e9
+    total_ms = sum(c["ms"] for c in prof["classes"])
+    # whole decode step against HBM: weights (GGUF bytes, embedding row only) + KV read
+    info = m.info
+    kv_row = 2 * info.n_layers * info.n_head_kv * info.head_dim * 2
+    avg_pos = pos_start + K / 2
+    step_bytes = g["bytes"] / prof["steps"] + kv_row * avg_pos
+    step_gbs = step_bytes / (dev_ms / K / 1e3) / 1e9
+    launches_per_step = eng["greedy_graph_kernels"]
+    m.close()
+
+    cpu = None
+    if RANK == 0 and WORLD == 1 and not args.no_cpu:
+        v, kind, cores, dt = cpu_reference_decode(path, 16, 8)
+        cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": kind,
+               "sample": f"same GGUF, prompt 16 random ids, 8 greedy decode steps, {dt:.1f} s of CPU decode"}
+    if RANK == 0:
+        line = {
+            "metric": BASELINE["metric"], "value": round(value, 3), "unit": "tok/s", "n_gpus": WORLD,
+            "steps": K, "warmup": W, "ms_per_step": round(dev_ms_max / K, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {
+                "workload": "llama8b-shaped Q4_K_M (32 L, d 4096, 32/8 heads, FFN 14336, vocab 128256), batch 1, "
+                            f"prompt {PROMPT} random ids, {K} greedy decode steps per replica",
+                "global_batch": WORLD, "seq_len": PROMPT + W + K, "parallelism": f"replicas x{WORLD}",
+                "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)",
+                "prefill_tok_s": round(PROMPT / prefill_s, 1),
+                "decode_step_gbs": round(step_gbs, 1),
+                "decode_step_hbm_frac": round(step_gbs / peak, 4),
+                "profile_ms_per_step": {k: round(v["ms"] / prof["steps"], 4) for k, v in cls.items()},
+                "profile_total_ms_per_step": round(total_ms / prof["steps"], 4),
+            },
+            "e2e": {"value": round(e2e_value, 3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches_per_step * K * WORLD),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
+                         "kernel": "k_gemv<1> (Q4_K/Q6_K decode GEMV)", "peak_kind": peak_kind},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=192)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

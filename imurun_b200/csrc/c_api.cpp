@@ -1,0 +1,693 @@
+// c_api.cpp — the FISH C ABI (include/fish/c_api.h) over the B200 engine.
+//
+// The ABI-4 entry points keep the reference's contracts
+// (model/fish/src/c_api.cpp): one mutex per context, negative error codes
+// plus fish_last_error, "required size" string results, and the generation
+// loop of generate_ids_locked (c_api.cpp:504-794): head+tail prompt fit with
+// a sticky cut, the one-slot KV prefix cache (longest common prefix >= 8,
+// identical prompt -> n-1), prefill in chunks of <= 256, sampled decode with
+// UTF-8-complete streaming callbacks, cancel between forwards, stats.
+#include <fish/c_api.h>
+
+#include <sys/resource.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "sampler.h"
+#include "tokenizer.h"
+
+struct fish_ctx {
+    std::mutex mu;
+    std::unique_ptr<fb::Engine> eng;
+    std::unique_ptr<fb::Tokenizer> tok;
+    fb::Sampler sampler{0};
+    std::string err;
+    std::atomic<bool> cancel{false};
+    fish_stats stats{};
+    std::vector<int32_t> cache_ids;
+    int trunc_head = 0, trunc_drop_end = 0;
+    std::vector<int32_t> trunc_head_ids;
+    std::string adapter_path;
+    float adapter_scale = 1.0f;
+    std::string model_path;
+    int n_ctx_req = 0;
+    std::vector<float> logits;
+};
+
+namespace {
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+double peak_rss_mb() {
+    struct rusage ru {};
+    return getrusage(RUSAGE_SELF, &ru) == 0 ? (double)ru.ru_maxrss / 1024.0 : 0.0;
+}
+
+// Emit only complete UTF-8 sequences (c_api.cpp:81-101).
+void emit_utf8(fish_token_cb cb, void* user, const std::string& bytes, int id, std::string& pending, std::string& sink) {
+    pending += bytes;
+    size_t i = 0, done = 0;
+    while (i < pending.size()) {
+        const unsigned char c = (unsigned char)pending[i];
+        size_t len = 1;
+        if ((c & 0xE0) == 0xC0) len = 2;
+        else if ((c & 0xF0) == 0xE0) len = 3;
+        else if ((c & 0xF8) == 0xF0) len = 4;
+        if (i + len > pending.size()) break;
+        i += len;
+        done = i;
+    }
+    if (!done) return;
+    const std::string ready = pending.substr(0, done);
+    pending.erase(0, done);
+    sink += ready;
+    if (cb) cb(ready.c_str(), id, user);
+}
+
+int write_string(const std::string& s, char* out, int cap) {
+    const int need = (int)s.size();
+    if (out && cap > 0) {
+        const int n = std::min(need, cap - 1);
+        std::memcpy(out, s.data(), (size_t)n);
+        out[n] = '\0';
+    }
+    return need;
+}
+
+fb::Messages to_messages(const char* const* roles, const char* const* contents, int n) {
+    fb::Messages m;
+    for (int i = 0; i < n; ++i)
+        m.emplace_back(roles && roles[i] ? roles[i] : "user", contents && contents[i] ? contents[i] : "");
+    return m;
+}
+
+void fill_load_stats(fish_ctx* ctx, double t_load) {
+    fb::Engine& e = *ctx->eng;
+    fish_stats& s = ctx->stats;
+    s = fish_stats{};
+    s.load_seconds = t_load;
+    s.weights_bytes = e.weights_bytes();
+    s.kv_bytes = e.kv_bytes();
+    s.context_size = e.cfg().n_ctx;
+    s.n_threads = 1;
+    s.gpu_layers = e.cfg().n_layers;
+    s.gpu_bytes = e.device_weight_bytes() + e.kv_bytes();
+    std::snprintf(s.gpu_name, sizeof(s.gpu_name), "%s (cuda sm_100a)", e.device_name().c_str());
+    std::snprintf(s.gpu_mix, sizeof(s.gpu_mix), "all %d layers resident at file precision; paged %s KV, %d-position pages",
+                  e.cfg().n_layers, std::getenv("FISH_KV_F32") ? "f32" : "fp16", e.page_size());
+    std::snprintf(s.placement, sizeof(s.placement), "whole model on GPU %d", e.device());
+    std::snprintf(s.load_profile, sizeof(s.load_profile), "total %.2f s (upload %.2f s)", t_load, e.load_seconds_upload);
+    size_t fr = 0, tot = 0;
+    cudaMemGetInfo(&fr, &tot);
+    s.vram_total = tot;
+    s.vram_free = fr;
+}
+
+int load_locked(fish_ctx* ctx, const char* path, int n_ctx) {
+    const double t0 = now_s();
+    if (!ctx->adapter_path.empty()) {
+        ctx->err = "adapter: LoRA merging is not supported by the B200 engine";
+        ctx->adapter_path.clear();
+        ctx->adapter_scale = 1.0f;
+        return -4;
+    }
+    ctx->eng.reset();
+    ctx->tok.reset();
+    auto eng = std::make_unique<fb::Engine>();
+    std::string err;
+    if (!eng->load(path, n_ctx > 0 ? n_ctx : 4096, &err)) { ctx->err = err; return -2; }
+    auto tok = fb::Tokenizer::create(eng->gguf(), &err);
+    if (!tok) { ctx->err = err; return -3; }
+    ctx->eng = std::move(eng);
+    ctx->tok = std::move(tok);
+    ctx->model_path = path;
+    ctx->n_ctx_req = n_ctx;
+    ctx->cache_ids.clear();
+    ctx->logits.assign((size_t)ctx->eng->cfg().vocab, 0.0f);
+    fill_load_stats(ctx, now_s() - t0);
+    ctx->err.clear();
+    return 0;
+}
+
+// Forward ids[0..n) on the context's sequence in chunks of <= 256
+// (LlamaModel::forward's batch limit); last logits into ctx->logits.
+bool prefill_chunks(fish_ctx* ctx, const int32_t* ids, int n, bool stop_on_cancel, int* done) {
+    fb::Engine& e = *ctx->eng;
+    const int batch = std::min(fb::kMaxBatch, e.cfg().n_ctx);
+    int pos = 0;
+    while (pos < n) {
+        const int m = std::min(batch, n - pos);
+        std::string err;
+        if (!e.forward(0, ids + pos, m, ctx->logits.data(), nullptr, nullptr, &err)) {
+            ctx->err = err;
+            if (done) *done = pos;
+            return false;
+        }
+        pos += m;
+        if (stop_on_cancel && ctx->cancel) break;
+    }
+    if (done) *done = pos;
+    return true;
+}
+
+int generate_ids_locked(fish_ctx* ctx, std::vector<int32_t> ids, int max_tokens, float temperature, int top_k,
+                        float top_p, float repeat_penalty, fish_token_cb cb, void* user, std::string* collected) {
+    if (!ctx->eng || !ctx->tok) { ctx->err = "no model loaded"; return -1; }
+    if (ids.empty()) { ctx->err = "empty prompt"; return -1; }
+    fb::Engine& e = *ctx->eng;
+    const fb::Config& c = e.cfg();
+    if (max_tokens <= 0) max_tokens = c.n_ctx;
+    ctx->stats.truncated = 0;
+    {
+        const int reserve = std::max(64, std::min(max_tokens, c.n_ctx / 4));
+        const int budget = std::max(32, c.n_ctx - reserve);
+        const int n = (int)ids.size();
+        if (n > budget) {
+            int head = ctx->trunc_head, drop_end = ctx->trunc_drop_end;
+            const bool reuse = head > 0 && drop_end > head && drop_end < n && n - (drop_end - head) <= budget &&
+                               (int)ctx->trunc_head_ids.size() == head &&
+                               std::equal(ctx->trunc_head_ids.begin(), ctx->trunc_head_ids.end(), ids.begin());
+            if (!reuse) {
+                head = budget / 4;
+                const int tail = std::max(1, budget - head - budget / 4);
+                drop_end = n - tail;
+                ctx->trunc_head = head;
+                ctx->trunc_drop_end = drop_end;
+                ctx->trunc_head_ids.assign(ids.begin(), ids.begin() + head);
+            }
+            std::vector<int32_t> kept(ids.begin(), ids.begin() + head);
+            kept.insert(kept.end(), ids.begin() + drop_end, ids.end());
+            ids.swap(kept);
+            ctx->stats.truncated = 1;
+        } else {
+            ctx->trunc_head = ctx->trunc_drop_end = 0;
+            ctx->trunc_head_ids.clear();
+        }
+    }
+    ctx->cancel = false;
+    int prefix = 0;
+    {
+        const int lim = (int)std::min(ids.size(), ctx->cache_ids.size());
+        while (prefix < lim && ids[prefix] == ctx->cache_ids[prefix]) ++prefix;
+        if (prefix >= (int)ids.size()) prefix = (int)ids.size() - 1;
+        if (prefix < 8) prefix = 0;
+    }
+    ctx->stats.cached_tokens = prefix;
+    const double t0 = now_s();
+    e.seq_truncate(0, prefix);
+    ctx->cache_ids.resize((size_t)prefix);
+    int done = 0;
+    if (!prefill_chunks(ctx, ids.data() + prefix, (int)ids.size() - prefix, true, &done)) {
+        ctx->err = "prefill failed: " + ctx->err;
+        ctx->cache_ids.clear();
+        e.seq_truncate(0, 0);
+        return -1;
+    }
+    int pos = prefix + done;
+    if (ctx->cancel) ctx->cache_ids.assign(ids.begin(), ids.begin() + pos);
+    else ctx->cache_ids = ids;
+    const double t1 = now_s();
+    const int prefilled = pos - prefix;
+
+    fb::SampleParams sp;
+    sp.temperature = temperature;
+    sp.top_k = top_k;
+    sp.top_p = top_p;
+    sp.repeat_penalty = repeat_penalty;
+    std::string pending, sink;
+    std::vector<int32_t> recent;
+    const size_t recent_cap = 128;
+    for (size_t i = ids.size() > recent_cap ? ids.size() - recent_cap : 0; i < ids.size(); ++i) recent.push_back(ids[i]);
+    int generated = 0;
+    int next = -1;
+    if (!ctx->cancel) next = ctx->sampler.sample(ctx->logits.data(), c.vocab, sp, recent);
+    while (next >= 0 && generated < max_tokens && pos < c.n_ctx) {
+        if (ctx->cancel) break;
+        if (ctx->tok->is_eog(next)) break;
+        emit_utf8(cb, user, ctx->tok->token_text(next), next, pending, sink);
+        recent.push_back(next);
+        if (recent.size() > recent_cap) recent.erase(recent.begin());
+        ++generated;
+        std::string err;
+        if (!e.forward(0, &next, 1, ctx->logits.data(), nullptr, nullptr, &err)) {
+            ctx->err = "decode failed: " + err;
+            ctx->cache_ids.clear();
+            break;
+        }
+        ctx->cache_ids.push_back(next);
+        ++pos;
+        next = ctx->sampler.sample(ctx->logits.data(), c.vocab, sp, recent);
+    }
+    if (!pending.empty()) {
+        sink += pending;
+        if (cb) cb(pending.c_str(), -1, user);
+    }
+    const double t2 = now_s();
+    ctx->stats.prefill_seconds = t1 - t0;
+    ctx->stats.decode_seconds = t2 - t1;
+    ctx->stats.prompt_tokens = (int)ids.size();
+    ctx->stats.generated_tokens = generated;
+    ctx->stats.context_used = pos;
+    ctx->stats.tokens_per_second = ctx->stats.decode_seconds > 0 ? generated / ctx->stats.decode_seconds : 0.0;
+    ctx->stats.prefill_tokens_per_second = ctx->stats.prefill_seconds > 0 ? prefilled / ctx->stats.prefill_seconds : 0.0;
+    if (collected) *collected = sink;
+    return generated;
+}
+
+bool need_model(fish_ctx* ctx) {
+    if (!ctx->eng) { ctx->err = "no model loaded"; return false; }
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fish_version(void) { return "fish-b200 0.1.0"; }
+int fish_abi_version(void) { return FISH_ABI_VERSION; }
+const char* fish_supported_archs(void) { return "llama,qwen2,qwen2moe,qwen3,qwen3moe"; }
+const char* fish_kernel_name(void) { return "cuda-sm100a"; }
+
+fish_ctx* fish_create(void) { return new (std::nothrow) fish_ctx(); }
+
+void fish_destroy(fish_ctx* ctx) {
+    if (!ctx) return;
+    ctx->cancel = true;
+    {
+        std::lock_guard<std::mutex> lock(ctx->mu);
+        ctx->eng.reset();
+        ctx->tok.reset();
+    }
+    delete ctx;
+}
+
+int fish_load(fish_ctx* ctx, const char* path, int n_ctx) {
+    if (!ctx || !path) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    return load_locked(ctx, path, n_ctx);
+}
+
+int fish_loaded(fish_ctx* ctx) {
+    if (!ctx) return 0;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    return (ctx->eng && ctx->tok) ? 1 : 0;
+}
+
+const char* fish_last_error(fish_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int fish_model_info_of(fish_ctx* ctx, fish_model_info* out) {
+    if (!ctx || !out) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->eng || !ctx->tok) return -1;
+    const fb::Config& c = ctx->eng->cfg();
+    std::memset(out, 0, sizeof(*out));
+    std::snprintf(out->arch, sizeof(out->arch), "%s", c.arch.c_str());
+    out->n_layers = c.n_layers;
+    out->n_embd = c.n_embd;
+    out->n_ff = c.n_ff;
+    out->n_head = c.n_head;
+    out->n_head_kv = c.n_head_kv;
+    out->head_dim = c.head_dim;
+    out->n_ctx = c.n_ctx;
+    out->vocab = c.vocab;
+    out->tied_output = c.tied_output ? 1 : 0;
+    out->n_experts = c.n_experts;
+    out->n_experts_per_tok = c.n_experts_per_tok;
+    out->n_ctx_train = c.n_ctx_train;
+    std::snprintf(out->chat_format, sizeof(out->chat_format), "%s", fb::chat_format_name(ctx->tok->format()));
+    std::snprintf(out->tokenizer, sizeof(out->tokenizer), "%s", ctx->tok->spm() ? "spm" : "bpe");
+    std::vector<std::pair<const char*, int>> counts;
+    for (const auto& t : ctx->eng->gguf().tensors()) {
+        const char* n = fb::ggml_type_name(t.type);
+        bool f = false;
+        for (auto& kv : counts) if (std::strcmp(kv.first, n) == 0) { ++kv.second; f = true; break; }
+        if (!f) counts.emplace_back(n, 1);
+    }
+    std::sort(counts.begin(), counts.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+    std::string mix;
+    for (size_t i = 0; i < counts.size() && i < 4; ++i) {
+        if (!mix.empty()) mix += " ";
+        mix += std::string(counts[i].first) + ":" + std::to_string(counts[i].second);
+    }
+    std::snprintf(out->quant, sizeof(out->quant), "%s", mix.c_str());
+    return 0;
+}
+
+int fish_tokenize(fish_ctx* ctx, const char* text, int add_bos, int32_t* out, int cap) {
+    if (!ctx || !text) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) return -1;
+    const auto ids = ctx->tok->encode(text, add_bos != 0, true);
+    if (!out || cap <= 0) return (int)ids.size();
+    const int n = std::min((int)ids.size(), cap);
+    std::memcpy(out, ids.data(), sizeof(int32_t) * (size_t)n);
+    return n;
+}
+
+int fish_detokenize(fish_ctx* ctx, const int32_t* ids, int n, char* out, int cap) {
+    if (!ctx || !ids || n < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) return -1;
+    return write_string(ctx->tok->decode(std::vector<int32_t>(ids, ids + n)), out, cap);
+}
+
+int fish_chat_prompt(fish_ctx* ctx, const char* const* roles, const char* const* contents, int n, char* out, int cap) {
+    if (!ctx || n < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) return -1;
+    return write_string(ctx->tok->apply_chat(to_messages(roles, contents, n), ctx->tok->format()), out, cap);
+}
+
+int fish_count_chat_tokens(fish_ctx* ctx, const char* const* roles, const char* const* contents, int n) {
+    if (!ctx || n < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) return -1;
+    return (int)ctx->tok->encode_chat(to_messages(roles, contents, n)).size();
+}
+
+const char* fish_chat_format(fish_ctx* ctx) {
+    if (!ctx) return "none";
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) return "none";
+    return fb::chat_format_name(ctx->tok->format());
+}
+
+int fish_generate(fish_ctx* ctx, const char* prompt, int add_bos, int max_tokens, float temperature, int top_k,
+                  float top_p, float repeat_penalty, fish_token_cb cb, void* user) {
+    if (!ctx || !prompt) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) { ctx->err = "no model loaded"; return -1; }
+    return generate_ids_locked(ctx, ctx->tok->encode(prompt, add_bos != 0, true), max_tokens, temperature, top_k,
+                               top_p, repeat_penalty, cb, user, nullptr);
+}
+
+int fish_generate_chat(fish_ctx* ctx, const char* const* roles, const char* const* contents, int n, int max_tokens,
+                       float temperature, int top_k, float top_p, float repeat_penalty, fish_token_cb cb, void* user) {
+    if (!ctx || n <= 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) { ctx->err = "no model loaded"; return -1; }
+    return generate_ids_locked(ctx, ctx->tok->encode_chat(to_messages(roles, contents, n)), max_tokens, temperature,
+                               top_k, top_p, repeat_penalty, cb, user, nullptr);
+}
+
+int fish_generate_to(fish_ctx* ctx, const char* prompt, int add_bos, int max_tokens, float temperature, int top_k,
+                     float top_p, float repeat_penalty, char* out, int cap) {
+    if (!ctx || !prompt) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->tok) { ctx->err = "no model loaded"; return -1; }
+    std::string collected;
+    const int n = generate_ids_locked(ctx, ctx->tok->encode(prompt, add_bos != 0, true), max_tokens, temperature,
+                                      top_k, top_p, repeat_penalty, nullptr, nullptr, &collected);
+    if (n < 0) return n;
+    return write_string(collected, out, cap);
+}
+
+void fish_cancel(fish_ctx* ctx) { if (ctx) ctx->cancel = true; }
+
+void fish_reset(fish_ctx* ctx) {
+    if (!ctx) return;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (ctx->eng) ctx->eng->seq_truncate(0, 0);
+    ctx->cache_ids.clear();
+}
+
+void fish_get_stats(fish_ctx* ctx, fish_stats* out) {
+    if (!ctx || !out) return;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    *out = ctx->stats;
+    out->peak_rss_mb = peak_rss_mb();
+    if (ctx->eng) {
+        out->context_used = ctx->eng->seq_len(0);
+        size_t fr = 0, tot = 0;
+        if (cudaMemGetInfo(&fr, &tot) == cudaSuccess) out->vram_free = fr;
+    }
+    out->n_threads = 1;
+}
+
+int fish_set_threads(fish_ctx* ctx, int n) {
+    if (!ctx) return -1;
+    (void)n;   // host threads do not take part in the device forward
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    ctx->stats.n_threads = 1;
+    return 0;
+}
+
+const char* fish_specs_json(fish_ctx* ctx) {
+    thread_local std::string buf;
+    int ndev = 0;
+    cudaGetDeviceCount(&ndev);
+    std::string gpus = "[";
+    for (int i = 0; i < ndev; ++i) {
+        cudaDeviceProp p{};
+        cudaGetDeviceProperties(&p, i);
+        char b[256];
+        std::snprintf(b, sizeof(b), "%s{\"name\":\"%s\",\"memory_bytes\":%zu,\"sms\":%d,\"cc\":\"%d.%d\"}",
+                      i ? "," : "", p.name, (size_t)p.totalGlobalMem, p.multiProcessorCount, p.major, p.minor);
+        gpus += b;
+    }
+    gpus += "]";
+    std::string plan = "null";
+    if (ctx) {
+        std::lock_guard<std::mutex> lock(ctx->mu);
+        if (ctx->eng) {
+            char b[256];
+            std::snprintf(b, sizeof(b), "{\"n_ctx\":%d,\"gpu_layers\":%d,\"kv_bytes\":%llu}", ctx->eng->cfg().n_ctx,
+                          ctx->eng->cfg().n_layers, (unsigned long long)ctx->eng->kv_bytes());
+            plan = b;
+        }
+    }
+    buf = "{\"hardware\":{\"gpus\":" + gpus + "},\"plan\":" + plan + ",\"threads\":1,\"pool_threads\":1,\"kernel\":\"" +
+          std::string(fish_kernel_name()) + "\"}";
+    return buf.c_str();
+}
+
+int fish_set_draft(fish_ctx* ctx, const char* path, int k) {
+    if (!ctx || !path) return -1;
+    (void)k;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->eng) { ctx->err = "load the target model first"; return -1; }
+    ctx->err = "draft: speculative decoding is not available in the B200 engine yet";
+    return -2;
+}
+
+void fish_clear_draft(fish_ctx* ctx) {
+    if (!ctx) return;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    ctx->stats.draft_active = 0;
+}
+
+int fish_set_adapter(fish_ctx* ctx, const char* path, float scale) {
+    if (!ctx || !path || !*path || !(scale == scale)) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->eng) {
+        ctx->adapter_path = path;
+        ctx->adapter_scale = scale;
+        return 0;
+    }
+    ctx->err = "adapter: LoRA merging is not supported by the B200 engine";
+    return -2;
+}
+
+int fish_clear_adapter(fish_ctx* ctx) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    ctx->adapter_path.clear();
+    ctx->adapter_scale = 1.0f;
+    return 0;
+}
+
+int fish_adapter_info_of(fish_ctx* ctx, fish_adapter_info* out) {
+    if (!ctx || !out) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    std::memset(out, 0, sizeof(*out));
+    if (!ctx->adapter_path.empty()) {
+        out->pending = 1;
+        const std::string& p = ctx->adapter_path;
+        const size_t sl = p.find_last_of("/\\");
+        std::snprintf(out->name, sizeof(out->name), "%s", (sl == std::string::npos ? p : p.substr(sl + 1)).c_str());
+        out->scale = ctx->adapter_scale;
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------ ABI 5
+
+int fish_prefill_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0, float* logits) {
+    if (!ctx || !ids || n <= 0 || pos0 < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    fb::Engine& e = *ctx->eng;
+    if (pos0 > e.seq_len(0)) { ctx->err = "pos0 beyond the cached length"; return -1; }
+    e.seq_truncate(0, pos0);
+    ctx->cache_ids.resize(std::min(ctx->cache_ids.size(), (size_t)pos0));
+    if (!prefill_chunks(ctx, ids, n, false, nullptr)) return -2;
+    ctx->cache_ids.insert(ctx->cache_ids.end(), ids, ids + n);
+    if (logits) std::memcpy(logits, ctx->logits.data(), sizeof(float) * ctx->logits.size());
+    return 0;
+}
+
+int fish_decode_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0, float* logits_all, int32_t* argmax_out) {
+    if (!ctx || !ids || n <= 0 || pos0 < 0 || n > fb::kMaxBatch) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    fb::Engine& e = *ctx->eng;
+    if (pos0 > e.seq_len(0)) { ctx->err = "pos0 beyond the cached length"; return -1; }
+    e.seq_truncate(0, pos0);
+    ctx->cache_ids.resize(std::min(ctx->cache_ids.size(), (size_t)pos0));
+    std::string err;
+    if (!e.forward(0, ids, n, ctx->logits.data(), logits_all, argmax_out, &err)) { ctx->err = err; return -2; }
+    ctx->cache_ids.insert(ctx->cache_ids.end(), ids, ids + n);
+    return 0;
+}
+
+int fish_decode_greedy(fish_ctx* ctx, int32_t first, int n_steps, int32_t* out_ids) {
+    if (!ctx || !out_ids || n_steps < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    std::string err;
+    const int n = ctx->eng->decode_greedy(0, first, n_steps, out_ids, &err);
+    if (n < 0) { ctx->err = err; return -2; }
+    ctx->cache_ids.push_back(first);
+    for (int i = 0; i + 1 < n; ++i) ctx->cache_ids.push_back(out_ids[i]);
+    return n;
+}
+
+int fish_kv_len(fish_ctx* ctx) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    return ctx->eng ? ctx->eng->seq_len(0) : -1;
+}
+
+int fish_set_kv_len(fish_ctx* ctx, int n) {
+    if (!ctx || n < 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    ctx->eng->seq_truncate(0, n);
+    ctx->cache_ids.resize(std::min(ctx->cache_ids.size(), (size_t)n));
+    return 0;
+}
+
+int fish_session_open(fish_ctx* ctx) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    const int s = ctx->eng->seq_open();
+    if (s < 0) ctx->err = "too many sessions";
+    return s;
+}
+
+int fish_session_fork(fish_ctx* ctx, int parent, int prefix_len) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    std::string err;
+    const int s = ctx->eng->seq_fork(parent, prefix_len, &err);
+    if (s < 0) ctx->err = err;
+    return s;
+}
+
+int fish_session_close(fish_ctx* ctx, int session) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    if (!ctx->eng->seq_close(session)) { ctx->err = "bad session"; return -1; }
+    if (session == 0) ctx->cache_ids.clear();
+    return 0;
+}
+
+int fish_session_len(fish_ctx* ctx, int session) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    return ctx->eng ? ctx->eng->seq_len(session) : -1;
+}
+
+int fish_session_prefill(fish_ctx* ctx, int session, const int32_t* ids, int n, float* logits) {
+    if (!ctx || !ids || n <= 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    fb::Engine& e = *ctx->eng;
+    int pos = 0;
+    while (pos < n) {
+        const int m = std::min(fb::kMaxBatch, n - pos);
+        std::string err;
+        if (!e.forward(session, ids + pos, m, ctx->logits.data(), nullptr, nullptr, &err)) { ctx->err = err; return -2; }
+        pos += m;
+    }
+    if (session == 0) ctx->cache_ids.insert(ctx->cache_ids.end(), ids, ids + n);
+    if (logits) std::memcpy(logits, ctx->logits.data(), sizeof(float) * ctx->logits.size());
+    return 0;
+}
+
+int fish_decode_batch(fish_ctx* ctx, const int* sessions, const int32_t* ids, int n, int32_t* argmax_out, float* logits) {
+    if (!ctx || !sessions || !ids || n <= 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    std::string err;
+    if (!ctx->eng->decode_batch(sessions, ids, n, argmax_out, logits, &err)) { ctx->err = err; return -2; }
+    for (int i = 0; i < n; ++i) if (sessions[i] == 0) ctx->cache_ids.push_back(ids[i]);
+    return 0;
+}
+
+int fish_session_pages(fish_ctx* ctx, int session, int32_t* out, int cap) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    const std::vector<int> p = ctx->eng->seq_pages(session);
+    if (out && cap >= (int)p.size()) for (size_t i = 0; i < p.size(); ++i) out[i] = p[i];
+    return (int)p.size();
+}
+
+int fish_kv_page_size(fish_ctx* ctx) {
+    (void)ctx;
+    return fb::kPageSize;
+}
+
+const char* fish_engine_json(fish_ctx* ctx) {
+    thread_local std::string buf;
+    if (!ctx) return "{}";
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!ctx->eng) return "{}";
+    fb::Engine& e = *ctx->eng;
+    char b[512];
+    std::snprintf(b, sizeof(b),
+                  "{\"device\":\"%s\",\"kv_page_size\":%d,\"kv_free_pages\":%d,\"kv_bytes\":%llu,"
+                  "\"weights_device_bytes\":%llu,\"greedy_graph_kernels\":%d,\"step_graph_kernels\":%d,"
+                  "\"last_decode_device_ms\":%.6f}",
+                  e.device_name().c_str(), e.page_size(), e.free_pages(), (unsigned long long)e.kv_bytes(),
+                  (unsigned long long)e.device_weight_bytes(), e.graph_kernels(0), e.graph_kernels(1),
+                  (double)e.last_greedy_ms());
+    buf = b;
+    return buf.c_str();
+}
+
+const char* fish_profile_decode_json(fish_ctx* ctx, int32_t first, int n_steps) {
+    thread_local std::string buf;
+    if (!ctx || n_steps <= 0) return nullptr;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return nullptr;
+    std::vector<fb::Engine::ProfClass> cls;
+    std::string err;
+    if (!ctx->eng->profile_decode(0, first, n_steps, &cls, &err)) { ctx->err = err; return nullptr; }
+    buf = "{\"steps\":" + std::to_string(n_steps) + ",\"classes\":[";
+    for (size_t i = 0; i < cls.size(); ++i) {
+        char b[256];
+        std::snprintf(b, sizeof(b), "%s{\"name\":\"%s\",\"launches\":%d,\"ms\":%.6f,\"bytes\":%.0f}", i ? "," : "",
+                      cls[i].name.c_str(), cls[i].launches, cls[i].ms, cls[i].bytes);
+        buf += b;
+    }
+    buf += "]}";
+    return buf.c_str();
+}
+
+}  // extern "C"

@@ -1,0 +1,974 @@
+// engine.cpp — see engine.h.
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+
+namespace fb {
+
+namespace {
+
+const char* cerr_str(int e) { return cudaGetErrorString(static_cast<cudaError_t>(e)); }
+
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        const int rc_ = (int)(call);                                                          \
+        if (rc_ != 0) {                                                                       \
+            if (err) *err = std::string(#call) + ": " + cerr_str(rc_);                        \
+            return false;                                                                     \
+        }                                                                                     \
+    } while (0)
+
+// Like CK, and when a profile is being taken, time the launch on the stream.
+#define CKP(cls, bytes, call)                                                                 \
+    do {                                                                                      \
+        if (prof_) prof_begin();                                                              \
+        const int rc_ = (int)(call);                                                          \
+        if (rc_ != 0) {                                                                       \
+            if (err) *err = std::string(#call) + ": " + cerr_str(rc_);                        \
+            return false;                                                                     \
+        }                                                                                     \
+        if (prof_) prof_end(cls, bytes);                                                      \
+    } while (0)
+
+enum { PC_GEMV = 0, PC_NORMQ = 1, PC_ROPE = 2, PC_ATTN = 3, PC_OTHER = 4 };
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool matmul_type_ok(int t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K || t == T_F32 || t == T_F16; }
+
+// Host dequantisation of a small vector (norm weights, biases, rope factors).
+bool host_vec(const Tensor* t, std::vector<float>& out) {
+    if (!t) return false;
+    const uint64_t n = t->n_elements();
+    out.resize(n);
+    if (t->type == 0) {
+        std::memcpy(out.data(), t->data, n * 4);
+        return true;
+    }
+    if (t->type == 1 || t->type == 30) {
+        for (uint64_t i = 0; i < n; ++i) {
+            uint16_t h;
+            std::memcpy(&h, t->data + 2 * i, 2);
+            if (t->type == 30) {
+                const uint32_t b = (uint32_t)h << 16;
+                std::memcpy(&out[i], &b, 4);
+            } else {
+                const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+                uint32_t e = (h >> 10) & 0x1F, m = h & 0x3FF, bits;
+                if (e == 0) {
+                    if (m == 0) bits = sign;
+                    else {
+                        int ee = 113;
+                        while (!(m & 0x400)) { m <<= 1; --ee; }
+                        bits = sign | ((uint32_t)ee << 23) | ((m & 0x3FF) << 13);
+                    }
+                } else if (e == 31) bits = sign | 0x7F800000u | (m << 13);
+                else bits = sign | ((e + 112) << 23) | (m << 13);
+                std::memcpy(&out[i], &bits, 4);
+            }
+        }
+        return true;
+    }
+    return false;
+}
+
+int env_int(const char* name, int def) {
+    const char* v = std::getenv(name);
+    return v && *v ? std::atoi(v) : def;
+}
+
+}  // namespace
+
+// RoPE cos/sin table [n_ctx][rot/2], angles in double, stored as float times
+// the attention factor (the reference's table, src/ops.cpp:75-124).
+void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, std::vector<float>& sn) {
+    const int rot = c.rot_dim, half = rot / 2;
+    cs.assign((size_t)c.n_ctx * half, 0.0f);
+    sn.assign((size_t)c.n_ctx * half, 0.0f);
+    const bool yarn = c.yarn_factor > 0.0f && c.yarn_orig_ctx > 0;
+    float corr_low = 0, corr_high = 0, ym = 1.0f;
+    auto corr_dim = [&](float n_rot) {
+        return (float)rot * std::log((float)c.yarn_orig_ctx / (n_rot * 2.0f * 3.14159265358979f)) /
+               (2.0f * std::log(c.freq_base));
+    };
+    if (yarn) {
+        corr_low = std::max(0.0f, std::floor(corr_dim(c.yarn_beta_fast)));
+        corr_high = std::min((float)(rot - 1), std::ceil(corr_dim(c.yarn_beta_slow)));
+        ym = c.yarn_attn_factor * (1.0f + 0.1f * std::log(c.yarn_factor));
+    }
+    std::vector<double> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = std::pow((double)c.freq_base, -2.0 * i / (double)rot);
+    for (int pos = 0; pos < c.n_ctx; ++pos) {
+        for (int i = 0; i < half; ++i) {
+            double te = (double)pos * inv[i];
+            if (ff) te /= (ff[i] != 0.0f ? ff[i] : 1.0f);
+            double theta;
+            float m = c.mscale;
+            if (yarn) {
+                const float den = std::max(0.001f, corr_high - corr_low);
+                const float y = std::min(1.0f, std::max(0.0f, ((float)(2 * i) / 2.0f - corr_low) / den));
+                const float ramp = 1.0f - y;
+                theta = (te / c.yarn_factor) * (1.0 - ramp) + te * ramp;
+                m *= ym;
+            } else {
+                theta = te * c.freq_scale;
+            }
+            cs[(size_t)pos * half + i] = (float)std::cos(theta) * m;
+            sn[(size_t)pos * half + i] = (float)std::sin(theta) * m;
+        }
+    }
+}
+
+Engine::~Engine() {
+    drop_graphs();
+    if (device_ >= 0) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (float* p : small_) cudaFree(p);
+    cudaFree(warena_);
+    cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
+    cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
+    cudaFree(act_mem_); cudaFree(att_scratch_);
+    cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_);
+    cudaFree(kv_pool_); cudaFree(pt_arena_);
+    cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
+    if (h_pinned_) cudaFreeHost(h_pinned_);
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    if (pe0_) cudaEventDestroy(pe0_);
+    if (pe1_) cudaEventDestroy(pe1_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+std::string Engine::device_name() const {
+    cudaDeviceProp p{};
+    if (cudaGetDeviceProperties(&p, device_) != cudaSuccess) return "cuda";
+    return p.name;
+}
+
+void Engine::drop_graphs() {
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    graphs_.clear();
+    graph_kernels_.clear();
+}
+
+void Engine::prof_begin() { cudaEventRecord(pe0_, stream_); }
+
+void Engine::prof_end(int cls, double bytes) {
+    cudaEventRecord(pe1_, stream_);
+    cudaEventSynchronize(pe1_);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, pe0_, pe1_);
+    ProfClass& c = (*prof_)[cls];
+    c.launches += 1;
+    c.ms += ms;
+    c.bytes += bytes;
+}
+
+// ------------------------------------------------------------------ load
+
+bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) {
+        if (err) *err = "no CUDA device: the B200 engine has no CPU fallback";
+        return false;
+    }
+    CK(cudaGetDevice(&device_));
+    CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    CK(cudaEventCreate(&ev0_));
+    CK(cudaEventCreate(&ev1_));
+    CK(cudaEventCreate(&pe0_));
+    CK(cudaEventCreate(&pe1_));
+    use_graphs_ = env_int("FISH_NO_GRAPHS", 0) == 0;
+    gguf_ = Gguf::open(path, err);
+    if (!gguf_) return false;
+    const Gguf& g = *gguf_;
+    Config& c = cfg_;
+    // model.cpp:403-470: metadata under the architecture prefix
+    c.arch = g.str("general.architecture", "llama");
+    if (c.arch != "llama" && c.arch != "qwen2" && c.arch != "qwen3" && c.arch != "qwen2moe" && c.arch != "qwen3moe") {
+        if (err) *err = "unsupported architecture: " + c.arch + " (the B200 engine runs llama, qwen2, qwen3 and their MoE variants)";
+        return false;
+    }
+    auto key = [&](const char* k) { return c.arch + "." + k; };
+    c.n_layers = (int)g.u64(key("block_count"), 0);
+    c.n_embd = (int)g.u64(key("embedding_length"), 0);
+    c.n_ff = (int)g.u64(key("feed_forward_length"), 0);
+    c.n_head = (int)g.u64(key("attention.head_count"), 0);
+    c.n_head_kv = (int)g.u64(key("attention.head_count_kv"), (uint64_t)c.n_head);
+    c.eps = (float)g.f64(key("attention.layer_norm_rms_epsilon"), 1e-5);
+    c.freq_base = (float)g.f64(key("rope.freq_base"), 10000.0);
+    c.bos = (int)g.i64("tokenizer.ggml.bos_token_id", 1);
+    c.eos = (int)g.i64("tokenizer.ggml.eos_token_id", 2);
+    c.n_ctx_train = (int)g.u64(key("context_length"), 4096);
+    c.vocab = (int)g.u64(key("vocab_size"), 0);
+    if (c.vocab <= 0) if (const MetaValue* t = g.meta("tokenizer.ggml.tokens")) c.vocab = (int)t->sarr.size();
+    const Tensor* embd = g.find("token_embd.weight");
+    if (!embd) { if (err) *err = "missing token_embd.weight"; return false; }
+    if (c.vocab <= 0 && embd->ne.size() > 1) c.vocab = (int)embd->ne[1];
+    if (c.n_layers <= 0 || c.n_embd <= 0 || c.n_head <= 0 || c.n_ff <= 0 || c.vocab <= 0) {
+        if (err) *err = "incomplete model metadata";
+        return false;
+    }
+    if (c.n_head_kv <= 0 || c.n_head % c.n_head_kv != 0) { if (err) *err = "n_head is not a multiple of n_head_kv"; return false; }
+    c.head_dim = (int)g.u64(key("attention.key_length"), 0);
+    if (c.head_dim <= 0) c.head_dim = c.n_embd / c.n_head;
+    c.n_experts = (int)g.u64(key("expert_count"), 0);
+    c.n_experts_per_tok = (int)g.u64(key("expert_used_count"), 0);
+    c.n_ff_exp = (int)g.u64(key("expert_feed_forward_length"), (uint64_t)c.n_ff);
+    if (c.n_experts > 0 && c.n_experts_per_tok <= 0) c.n_experts_per_tok = 2;
+    if (c.n_experts_per_tok > c.n_experts) c.n_experts_per_tok = c.n_experts;
+    c.expert_weights_norm = g.flag(key("expert_weights_norm"), c.arch != "qwen2moe");
+    c.rot_dim = (int)g.u64(key("rope.dimension_count"), (uint64_t)c.head_dim);
+    if (c.rot_dim <= 0 || c.rot_dim > c.head_dim) c.rot_dim = c.head_dim;
+    c.neox = c.arch != "llama";
+    const int model_ctx = c.n_ctx_train;
+    c.n_ctx = n_ctx > 0 ? std::min(n_ctx, model_ctx > 0 ? model_ctx : n_ctx) : std::min(4096, model_ctx);
+    if (c.n_ctx < 32) { if (err) *err = "context too small"; return false; }
+    if (c.head_dim % 32 != 0 || c.head_dim > 128 || c.n_head / c.n_head_kv > 8) {
+        if (err) *err = "attention shape not supported by the B200 kernels (head_dim must be 32..128, a multiple of 32; <= 8 q heads per kv head)";
+        return false;
+    }
+    {
+        const std::string type = g.str(key("rope.scaling.type"), "none");
+        const float factor = (float)g.f64(key("rope.scaling.factor"), 1.0);
+        const int orig = (int)g.u64(key("rope.scaling.original_context_length"), 0);
+        if (type == "linear" && factor > 0.0f) c.freq_scale = 1.0f / factor;
+        else if (type == "yarn" && factor > 0.0f) {
+            c.yarn_factor = factor;
+            c.yarn_orig_ctx = orig > 0 ? orig : model_ctx;
+            c.yarn_attn_factor = (float)g.f64(key("rope.scaling.attn_factor"), 1.0);
+        }
+    }
+
+    // weights
+    auto bind = [&](const std::string& name, DevW& w, bool required) -> bool {
+        const Tensor* t = g.find(name);
+        if (!t) {
+            if (required && err) *err = "missing tensor " + name;
+            return !required;
+        }
+        if (!matmul_type_ok(t->type)) {
+            if (err) *err = std::string("tensor type ") + ggml_type_name(t->type) + " is not supported on the B200 path yet (" + name + ")";
+            return false;
+        }
+        w.type = t->type;
+        w.n_in = (int)t->ne[0];
+        w.n_out = t->ne.size() > 1 ? (int)t->ne[1] : 1;
+        w.n_exp = t->ne.size() > 2 ? (int)t->ne[2] : 1;
+        w.stride = dev_row_bytes(t->type, w.n_in);
+        w.expert_bytes = w.stride * (size_t)w.n_out;
+        if (t->type == T_Q4_K || t->type == T_Q6_K) {
+            if (w.n_in % 256) { if (err) *err = "K-quant row not a multiple of 256: " + name; return false; }
+        }
+        return true;
+    };
+    if (!bind("token_embd.weight", embd_, true)) return false;
+    if (!bind("output.weight", out_w_, false)) return false;
+    if (out_w_.type < 0) { out_w_ = embd_; c.tied_output = true; }
+    layers_.resize(c.n_layers);
+    for (int i = 0; i < c.n_layers; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        DevLayer& L = layers_[i];
+        if (!bind(p + "attn_q.weight", L.wq, true) || !bind(p + "attn_k.weight", L.wk, true) ||
+            !bind(p + "attn_v.weight", L.wv, true) || !bind(p + "attn_output.weight", L.wo, true))
+            return false;
+        if (c.n_experts > 0) {
+            if (!bind(p + "ffn_gate_inp.weight", L.gate_inp, true) || !bind(p + "ffn_gate_exps.weight", L.gate_exps, true) ||
+                !bind(p + "ffn_up_exps.weight", L.up_exps, true) || !bind(p + "ffn_down_exps.weight", L.down_exps, true))
+                return false;
+            c.n_ff_exp = L.gate_exps.n_out;
+        } else {
+            if (!bind(p + "ffn_gate.weight", L.wg, true) || !bind(p + "ffn_up.weight", L.wu, true) ||
+                !bind(p + "ffn_down.weight", L.wd, true))
+                return false;
+        }
+    }
+    // activation layouts each consumer needs
+    for (const DevLayer& L : layers_) {
+        for (const DevW* w : {&L.wq, &L.wk, &L.wv, &L.wg, &L.wu, &L.gate_exps, &L.up_exps}) {
+            if (w->type == T_Q8_0) want32_e_ = true;
+            if (w->type == T_Q4_K || w->type == T_Q6_K) wantk_e_ = true;
+        }
+        if (L.wo.type == T_Q8_0) want32_q_ = true;
+        if (L.wo.type == T_Q4_K || L.wo.type == T_Q6_K) wantk_q_ = true;
+        for (const DevW* w : {&L.wd, &L.down_exps}) {
+            if (w->type == T_Q8_0) want32_f_ = true;
+            if (w->type == T_Q4_K || w->type == T_Q6_K) wantk_f_ = true;
+        }
+    }
+    if (out_w_.type == T_Q8_0) want32_e_ = true;
+    if (out_w_.type == T_Q4_K || out_w_.type == T_Q6_K) wantk_e_ = true;
+    if (c.n_experts > 0 && c.n_experts_per_tok > 8) { if (err) *err = "more than 8 experts per token"; return false; }
+    for (const Tensor& t : g.tensors()) weights_file_bytes_ += t.nbytes;
+
+    const auto t0 = std::chrono::steady_clock::now();
+    if (!upload_weights(err)) return false;
+    load_seconds_upload = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+
+    // small vectors
+    auto dev_vec = [&](const std::string& name, float** out, bool required) -> bool {
+        const Tensor* t = g.find(name);
+        if (!t) {
+            if (required && err) *err = "missing tensor " + name;
+            return !required;
+        }
+        std::vector<float> v;
+        if (!host_vec(t, v)) { if (err) *err = "bad vector " + name; return false; }
+        float* d = nullptr;
+        CK(cudaMalloc(&d, v.size() * sizeof(float)));
+        CK(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+        small_.push_back(d);
+        *out = d;
+        return true;
+    };
+    for (int i = 0; i < c.n_layers; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        DevLayer& L = layers_[i];
+        if (!dev_vec(p + "attn_norm.weight", &L.attn_norm, true) || !dev_vec(p + "ffn_norm.weight", &L.ffn_norm, true) ||
+            !dev_vec(p + "attn_q.bias", &L.bq, false) || !dev_vec(p + "attn_k.bias", &L.bk, false) ||
+            !dev_vec(p + "attn_v.bias", &L.bv, false) || !dev_vec(p + "attn_q_norm.weight", &L.q_norm, false) ||
+            !dev_vec(p + "attn_k_norm.weight", &L.k_norm, false))
+            return false;
+        if (L.q_norm && L.k_norm) c.qk_norm = true;
+    }
+    {
+        const Tensor* t = g.find("output_norm.weight");
+        std::vector<float> v;
+        if (!t || !host_vec(t, v)) { if (err) *err = "missing output_norm.weight"; return false; }
+        CK(cudaMalloc(&out_norm_, v.size() * sizeof(float)));
+        CK(cudaMemcpy(out_norm_, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    {
+        std::vector<float> ff, cs, sn;
+        const Tensor* rf = g.find("rope_freqs.weight");
+        if (rf && (!host_vec(rf, ff) || (int)ff.size() != c.rot_dim / 2)) { if (err) *err = "bad rope_freqs"; return false; }
+        build_rope_table(c, ff.empty() ? nullptr : ff.data(), cs, sn);
+        CK(cudaMalloc(&rope_cos_, cs.size() * sizeof(float)));
+        CK(cudaMalloc(&rope_sin_, sn.size() * sizeof(float)));
+        CK(cudaMemcpy(rope_cos_, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(rope_sin_, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    if (!alloc_buffers(err)) return false;
+    seqs_.assign(max_seqs_, Seq());
+    seqs_[0].open = true;
+    return true;
+}
+
+bool Engine::upload_weights(std::string* err) {
+    const Gguf& g = *gguf_;
+    struct Job { const Tensor* t; DevW* w; size_t off; };
+    std::vector<Job> jobs;
+    size_t total = 0;
+    auto add = [&](const std::string& name, DevW* w) {
+        if (w->type < 0) return;
+        const Tensor* t = g.find(name);
+        if (!t) return;
+        jobs.push_back({t, w, total});
+        total = align_up(total + w->stride * (size_t)w->n_out * (size_t)w->n_exp, 256);
+    };
+    add("token_embd.weight", &embd_);
+    if (!cfg_.tied_output) add("output.weight", &out_w_);
+    for (int i = 0; i < cfg_.n_layers; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        DevLayer& L = layers_[i];
+        add(p + "attn_q.weight", &L.wq); add(p + "attn_k.weight", &L.wk); add(p + "attn_v.weight", &L.wv);
+        add(p + "attn_output.weight", &L.wo);
+        add(p + "ffn_gate.weight", &L.wg); add(p + "ffn_up.weight", &L.wu); add(p + "ffn_down.weight", &L.wd);
+        add(p + "ffn_gate_inp.weight", &L.gate_inp); add(p + "ffn_gate_exps.weight", &L.gate_exps);
+        add(p + "ffn_up_exps.weight", &L.up_exps); add(p + "ffn_down_exps.weight", &L.down_exps);
+    }
+    weights_dev_bytes_ = total;
+    CK(cudaMalloc(&warena_, total + 256));
+    for (Job& j : jobs) j.w->d = warena_ + j.off;
+    if (cfg_.tied_output) out_w_ = embd_;
+
+    // staged, repacked upload: rows repacked by host threads into pinned
+    // buffers, copied while the next buffer fills.
+    const size_t stage = 64ull << 20;
+    uint8_t* pin[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    CK(cudaMallocHost(&pin[0], stage));
+    CK(cudaMallocHost(&pin[1], stage));
+    CK(cudaEventCreate(&done[0]));
+    CK(cudaEventCreate(&done[1]));
+    const int nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    int cur = 0;
+    bool ok = true;
+    for (const Job& j : jobs) {
+        const DevW& w = *j.w;
+        const uint64_t rows = (uint64_t)w.n_out * (uint64_t)w.n_exp;
+        const size_t src_rb = ggml_row_bytes(j.t->type, (uint64_t)w.n_in);
+        const uint64_t rows_per = std::max<uint64_t>(1, stage / w.stride);
+        for (uint64_t r0 = 0; r0 < rows && ok; r0 += rows_per) {
+            const uint64_t nr = std::min(rows_per, rows - r0);
+            if (cudaEventSynchronize(done[cur]) != cudaSuccess) { ok = false; break; }
+            uint8_t* dst = pin[cur];
+            auto work = [&](int tid) {
+                for (uint64_t r = tid; r < nr; r += nth)
+                    repack_row(j.t->type, j.t->data + (r0 + r) * src_rb, dst + r * w.stride, w.n_in);
+            };
+            std::vector<std::thread> th;
+            for (int i = 1; i < nth; ++i) th.emplace_back(work, i);
+            work(0);
+            for (auto& t : th) t.join();
+            if (cudaMemcpyAsync(w.d + r0 * w.stride, dst, nr * w.stride, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+                cudaEventRecord(done[cur], stream_) != cudaSuccess) {
+                ok = false;
+                break;
+            }
+            cur ^= 1;
+        }
+    }
+    cudaStreamSynchronize(stream_);
+    cudaEventDestroy(done[0]);
+    cudaEventDestroy(done[1]);
+    cudaFreeHost(pin[0]);
+    cudaFreeHost(pin[1]);
+    if (!ok) { if (err) *err = "weight upload failed"; return false; }
+    return true;
+}
+
+bool Engine::alloc_buffers(std::string* err) {
+    const Config& c = cfg_;
+    const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim();
+    const int K = std::max(1, c.n_experts_per_tok);
+    const int F = std::max(c.n_ff, c.n_ff_exp);
+    max_k_ = std::max(std::max(E, Q), F);
+    const int R = kMaxBatch * K;   // rows of the expert-expanded activations
+    const size_t ld = align_up((size_t)max_k_, 16);
+    CK(cudaMalloc(&x_, sizeof(float) * kMaxBatch * E));
+    CK(cudaMalloc(&xb_, sizeof(float) * kMaxBatch * E));
+    CK(cudaMalloc(&q_, sizeof(float) * kMaxBatch * Q));
+    CK(cudaMalloc(&k_, sizeof(float) * kMaxBatch * KV));
+    CK(cudaMalloc(&v_, sizeof(float) * kMaxBatch * KV));
+    CK(cudaMalloc(&attn_, sizeof(float) * kMaxBatch * Q));
+    CK(cudaMalloc(&g_, sizeof(float) * (size_t)R * F));
+    CK(cudaMalloc(&u_, sizeof(float) * (size_t)R * F));
+    CK(cudaMalloc(&logits_, sizeof(float) * (size_t)kMaxBatch * c.vocab));
+    if (c.n_experts > 0) {
+        CK(cudaMalloc(&router_, sizeof(float) * kMaxBatch * c.n_experts));
+        CK(cudaMalloc(&eo_, sizeof(float) * (size_t)R * E));
+        CK(cudaMalloc(&sel_, sizeof(int32_t) * R));
+        CK(cudaMalloc(&wsel_, sizeof(float) * R));
+    }
+    // activation planes: q32 | qk (R x ld each), d32 | s32 | bsk (R x max_k/32), dk (R x max_k/256)
+    const size_t nq = (size_t)R * ld, n32 = (size_t)R * (max_k_ / 32 + 1), n256 = (size_t)R * (max_k_ / 256 + 1);
+    const size_t bytes = 2 * nq + n32 * (4 + 4 + 2) + n256 * 4 + 1024;
+    CK(cudaMalloc(&act_mem_, bytes));
+    uint8_t* p = reinterpret_cast<uint8_t*>(act_mem_);
+    act_.q32 = reinterpret_cast<int8_t*>(p); p += nq;
+    act_.qk = reinterpret_cast<int8_t*>(p); p += nq;
+    act_.d32 = reinterpret_cast<float*>(p); p += align_up(n32 * 4, 16);
+    act_.s32 = reinterpret_cast<int32_t*>(p); p += align_up(n32 * 4, 16);
+    act_.dk = reinterpret_cast<float*>(p); p += align_up(n256 * 4, 16);
+    act_.bsk = reinterpret_cast<int16_t*>(p);
+    act_.ld = (int)ld;
+    // attention scratch for att_chunk_ tokens per launch at the full context
+    const int n_splits = (c.n_ctx + 127) / 128;
+    att_chunk_ = 64;
+    att_scratch_floats_ = (size_t)att_chunk_ * c.n_head * n_splits * (c.head_dim + 2);
+    CK(cudaMalloc(&att_scratch_, sizeof(float) * att_scratch_floats_));
+    CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
+    CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
+    CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
+    CK(cudaMalloc(&argmax_, sizeof(int32_t) * kMaxBatch));
+    CK(cudaMalloc(&greedy_out_, sizeof(int32_t) * greedy_cap_));
+    CK(cudaMalloc(&greedy_step_, sizeof(int32_t)));
+    CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * 3 * kMaxBatch));
+
+    // KV pool
+    kv_f16_ = env_int("FISH_KV_F32", 0) == 0;
+    const size_t esz = kv_f16_ ? 2 : 4;
+    page_elems_ = (size_t)c.n_layers * 2 * c.n_head_kv * kPageSize * c.head_dim;
+    const size_t page_bytes = page_elems_ * esz;
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    long long positions = env_int("FISH_KV_POSITIONS", 0);
+    if (positions <= 0) positions = std::max<long long>(2LL * c.n_ctx, 65536);
+    const long long cap_pos = (long long)((double)free_b * 0.45 / (double)page_bytes) * kPageSize;
+    positions = std::max<long long>(std::min(positions, cap_pos), c.n_ctx + kPageSize);
+    n_pages_ = (int)((positions + kPageSize - 1) / kPageSize);
+    kv_pool_bytes_ = (uint64_t)n_pages_ * page_bytes;
+    CK(cudaMalloc(&kv_pool_, kv_pool_bytes_));
+    page_ref_.assign(n_pages_, 0);
+    free_pages_.clear();
+    for (int i = n_pages_ - 1; i >= 0; --i) free_pages_.push_back(i);
+    max_seqs_ = std::max(1, env_int("FISH_MAX_SESSIONS", 256));
+    pt_stride_ = (c.n_ctx + kPageSize - 1) / kPageSize + 1;
+    CK(cudaMalloc(&pt_arena_, sizeof(int32_t) * (size_t)max_seqs_ * pt_stride_));
+    CK(cudaMemset(pt_arena_, 0, sizeof(int32_t) * (size_t)max_seqs_ * pt_stride_));
+    return true;
+}
+
+KvView Engine::kv_view() const {
+    KvView kv{};
+    const Config& c = cfg_;
+    const size_t head = (size_t)kPageSize * c.head_dim;
+    const size_t vofs = (size_t)c.n_head_kv * head;
+    kv.f16 = kv_f16_ ? 1 : 0;
+    kv.k = kv_pool_;
+    kv.v = kv_f16_ ? (void*)(reinterpret_cast<__half*>(kv_pool_) + vofs) : (void*)(reinterpret_cast<float*>(kv_pool_) + vofs);
+    kv.pt = pt_arena_;
+    kv.pt_stride = pt_stride_;
+    kv.tok_seq = tok_seq_;
+    kv.tok_pos = tok_pos_;
+    kv.page_size = kPageSize;
+    kv.page_stride = page_elems_;
+    kv.layer_stride = 2 * vofs;
+    kv.head_stride = head;
+    return kv;
+}
+
+// ------------------------------------------------------------------ sequences
+
+int Engine::seq_open() {
+    for (int i = 1; i < max_seqs_; ++i) {
+        if (!seqs_[i].open) {
+            seqs_[i] = Seq();
+            seqs_[i].open = true;
+            return i;
+        }
+    }
+    return -1;
+}
+
+bool Engine::seq_close(int sid) {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) return false;
+    seq_truncate(sid, 0);
+    if (sid != 0) seqs_[sid].open = false;
+    return true;
+}
+
+int Engine::seq_len(int sid) const {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) return -1;
+    return seqs_[sid].len;
+}
+
+std::vector<int> Engine::seq_pages(int sid) const {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) return {};
+    return seqs_[sid].pages;
+}
+
+void Engine::write_page_table(int sid) {
+    const Seq& s = seqs_[sid];
+    if (s.pages.empty()) return;
+    // small synchronous copy: page tables change only when a page boundary is crossed
+    std::vector<int32_t> row(s.pages.begin(), s.pages.end());
+    cudaMemcpyAsync(pt_arena_ + (size_t)sid * pt_stride_, row.data(), row.size() * sizeof(int32_t),
+                    cudaMemcpyHostToDevice, stream_);
+    cudaStreamSynchronize(stream_);
+}
+
+bool Engine::seq_truncate(int sid, int n) {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) return false;
+    Seq& s = seqs_[sid];
+    if (n < 0) n = 0;
+    if (n >= s.len) { s.len = std::min(n, s.len); return true; }
+    s.len = n;
+    const int keep = (n + kPageSize - 1) / kPageSize;
+    while ((int)s.pages.size() > keep) {
+        const int p = s.pages.back();
+        s.pages.pop_back();
+        if (--page_ref_[p] == 0) free_pages_.push_back(p);
+    }
+    return true;
+}
+
+bool Engine::ensure_pages(int sid, int new_len, std::string* err) {
+    Seq& s = seqs_[sid];
+    if (new_len > cfg_.n_ctx) {
+        if (err) *err = "context full (" + std::to_string(new_len) + " > " + std::to_string(cfg_.n_ctx) + ")";
+        return false;
+    }
+    bool changed = false;
+    // copy-on-write: the page holding position s.len must be private before appending into it
+    if (s.len % kPageSize != 0 && !s.pages.empty()) {
+        const int pi = s.len / kPageSize;
+        const int p = s.pages[pi];
+        if (page_ref_[p] > 1) {
+            if (free_pages_.empty()) { if (err) *err = "KV pool exhausted"; return false; }
+            const int np = free_pages_.back();
+            free_pages_.pop_back();
+            const size_t pb = page_elems_ * (kv_f16_ ? 2 : 4);
+            if (cudaMemcpyAsync(reinterpret_cast<uint8_t*>(kv_pool_) + (size_t)np * pb,
+                                reinterpret_cast<uint8_t*>(kv_pool_) + (size_t)p * pb, pb, cudaMemcpyDeviceToDevice,
+                                stream_) != cudaSuccess) {
+                if (err) *err = "page copy failed";
+                return false;
+            }
+            --page_ref_[p];
+            page_ref_[np] = 1;
+            s.pages[pi] = np;
+            changed = true;
+        }
+    }
+    const int need = (new_len + kPageSize - 1) / kPageSize;
+    while ((int)s.pages.size() < need) {
+        if (free_pages_.empty()) { if (err) *err = "KV pool exhausted"; return false; }
+        const int p = free_pages_.back();
+        free_pages_.pop_back();
+        page_ref_[p] = 1;
+        s.pages.push_back(p);
+        changed = true;
+    }
+    if (changed) write_page_table(sid);
+    return true;
+}
+
+int Engine::seq_fork(int parent, int prefix_len, std::string* err) {
+    if (parent < 0 || parent >= max_seqs_ || !seqs_[parent].open) { if (err) *err = "bad parent session"; return -1; }
+    const Seq& ps = seqs_[parent];
+    if (prefix_len < 0 || prefix_len > ps.len) { if (err) *err = "prefix longer than the parent"; return -1; }
+    const int sid = seq_open();
+    if (sid < 0) { if (err) *err = "too many sessions"; return -1; }
+    Seq& s = seqs_[sid];
+    const int np = (prefix_len + kPageSize - 1) / kPageSize;
+    for (int i = 0; i < np; ++i) {
+        const int p = seqs_[parent].pages[i];
+        ++page_ref_[p];
+        s.pages.push_back(p);
+    }
+    s.len = prefix_len;
+    write_page_table(sid);
+    return sid;
+}
+
+// ------------------------------------------------------------------ matmuls
+
+static double gemv_bytes(const DevW& w, int T) {
+    // algorithmic bytes of one launch: the weight rows in GGUF encoding
+    // (read once for all T tokens) plus the f32 outputs
+    return (double)ggml_row_bytes(w.type, (uint64_t)w.n_in) * w.n_out + 4.0 * w.n_out * T;
+}
+
+static void set_act_rows(GemvArgs& g, const ActQ& a, int t0, int K) {
+    g.act = a;
+    g.act.K = K;
+    if (a.q32) g.act.q32 = a.q32 + (size_t)t0 * a.ld;
+    if (a.qk) g.act.qk = a.qk + (size_t)t0 * a.ld;
+    if (a.d32) g.act.d32 = a.d32 + (size_t)t0 * (K / 32);
+    if (a.s32) g.act.s32 = a.s32 + (size_t)t0 * (K / 32);
+    if (a.dk) g.act.dk = a.dk + (size_t)t0 * (K / 256);
+    if (a.bsk) g.act.bsk = a.bsk + (size_t)t0 * (K / 32);
+}
+
+bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
+                        const ActQ& a, int T, int epi, std::string* err) {
+    for (int t0 = 0; t0 < T; t0 += 8) {
+        const int nt = std::min(8, T - t0);
+        GemvArgs g{};
+        g.nseg = n;
+        g.K = ws[0]->n_in;
+        g.T = nt;
+        set_act_rows(g, a, t0, g.K);
+        double bytes = 0.0;
+        for (int i = 0; i < n; ++i) {
+            GemvSeg& s = g.seg[i];
+            s.type = ws[i]->type;
+            s.w = ws[i]->d;
+            s.row_stride = ws[i]->stride;
+            s.rows = ws[i]->n_out;
+            s.y = ys[i] + (size_t)t0 * ldys[i];
+            s.ldy = ldys[i];
+            s.bias = biases ? biases[i] : nullptr;
+            s.epi = epi;
+            bytes += gemv_bytes(*ws[i], nt);
+        }
+        CKP(PC_GEMV, bytes, fbk_gemv(&g, stream_));
+    }
+    return true;
+}
+
+bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi, const float* xf,
+                  int ldxf, const int32_t* expert, std::string* err) {
+    for (int t0 = 0; t0 < T; t0 += 8) {
+        const int nt = std::min(8, T - t0);
+        GemvArgs g{};
+        g.nseg = 1;
+        g.K = w.n_in;
+        g.T = nt;
+        set_act_rows(g, a, t0, g.K);
+        g.xf = xf ? xf + (size_t)t0 * ldxf : nullptr;
+        g.ldxf = ldxf;
+        GemvSeg& s = g.seg[0];
+        s.type = w.type;
+        s.w = w.d;
+        s.row_stride = w.stride;
+        s.rows = w.n_out;
+        s.y = y + (size_t)t0 * ldy;
+        s.ldy = ldy;
+        s.bias = bias;
+        s.epi = epi;
+        s.expert = expert;
+        s.expert_bytes = w.expert_bytes;
+        CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
+    }
+    return true;
+}
+
+static ActQ act_row(const ActQ& a, int row, int K) {
+    ActQ r = a;
+    r.K = K;
+    r.q32 = a.q32 + (size_t)row * a.ld;
+    r.qk = a.qk + (size_t)row * a.ld;
+    r.d32 = a.d32 + (size_t)row * (K / 32);
+    r.s32 = a.s32 + (size_t)row * (K / 32);
+    r.dk = a.dk + (size_t)row * (K / 256);
+    r.bsk = a.bsk + (size_t)row * (K / 32);
+    return r;
+}
+
+// ------------------------------------------------------------------ forward
+
+bool Engine::run_layers(int T, int max_ctx, std::string* err) {
+    const Config& c = cfg_;
+    const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim(), H = c.n_head, HKV = c.n_head_kv, D = c.head_dim;
+    const float scale = 1.0f / std::sqrt((float)D);
+    const KvView kv = kv_view();
+    ActQ a = act_;
+    for (int li = 0; li < c.n_layers; ++li) {
+        const DevLayer& L = layers_[li];
+        a.K = E;
+        CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.attn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+        {
+            const DevW* ws[3] = {&L.wq, &L.wk, &L.wv};
+            float* ys[3] = {q_, k_, v_};
+            const int lds[3] = {Q, KV, KV};
+            const float* bs[3] = {L.bq, L.bk, L.bv};
+            if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err)) return false;
+        }
+        if (L.q_norm && L.k_norm) {
+            CKP(PC_OTHER, 0, fbk_head_rmsnorm(q_, Q, T, H, D, L.q_norm, c.eps, stream_));
+            CKP(PC_OTHER, 0, fbk_head_rmsnorm(k_, KV, T, HKV, D, L.k_norm, c.eps, stream_));
+        }
+        CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
+                                        rope_sin_, kv, li, stream_));
+        for (int t0 = 0; t0 < T; t0 += att_chunk_) {
+            const int nt = std::min(att_chunk_, T - t0);
+            KvView kvc = kv;
+            kvc.tok_seq = tok_seq_ + t0;
+            kvc.tok_pos = tok_pos_ + t0;
+            CKP(PC_ATTN, 0, fbk_attention(q_ + (size_t)t0 * Q, Q, nt, H, HKV, D, scale, kvc, li, attn_ + (size_t)t0 * Q, Q,
+                                          att_scratch_, att_scratch_floats_, max_ctx, stream_));
+        }
+        a.K = Q;
+        CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
+        if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+        a.K = E;
+        CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.ffn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+        if (c.n_experts > 0) {
+            const int NE = c.n_experts, K = c.n_experts_per_tok, F = c.n_ff_exp;
+            if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
+            CKP(PC_OTHER, 0, fbk_moe_route(router_, T, NE, K, c.expert_weights_norm ? 1 : 0, sel_, wsel_, stream_));
+            for (int t = 0; t < T; ++t) {
+                const ActQ ar = act_row(a, t, E);
+                for (int k = 0; k < K; ++k) {
+                    const int r = t * K + k;
+                    if (!gemv(L.gate_exps, ar, 1, g_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err) ||
+                        !gemv(L.up_exps, ar, 1, u_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err))
+                        return false;
+                }
+            }
+            a.K = F;
+            CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T * K, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
+            for (int r = 0; r < T * K; ++r) {
+                const ActQ ar = act_row(a, r, F);
+                if (!gemv(L.down_exps, ar, 1, eo_ + (size_t)r * E, E, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err))
+                    return false;
+            }
+            CKP(PC_OTHER, 0, fbk_moe_combine(x_, E, eo_, wsel_, T, K, E, stream_));
+        } else {
+            const int F = c.n_ff;
+            {
+                const DevW* ws[2] = {&L.wg, &L.wu};
+                float* ys[2] = {g_, u_};
+                const int lds[2] = {F, F};
+                if (!gemv_group(ws, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
+            }
+            a.K = F;
+            CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
+            if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+        }
+    }
+    return true;
+}
+
+// Final norm + output projection for x rows [row0, row0+n) into logits rows 0..n-1.
+bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err) {
+    const Config& c = cfg_;
+    const int E = c.n_embd;
+    ActQ a = act_;
+    a.K = E;
+    CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_ + (size_t)row0 * E, E, out_norm_, c.eps, n, E, xb_, E, &a, want32_e_, wantk_e_,
+                                       stream_));
+    return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, xb_, E, nullptr, err);
+}
+
+bool Engine::upload_tokens(const int32_t* ids, const int* sids, const int* pos, int T, std::string* err) {
+    int32_t* hp = h_pinned_;
+    // the previous step's copies from this pinned buffer must have finished
+    CK(cudaStreamSynchronize(stream_));
+    for (int t = 0; t < T; ++t) {
+        hp[t] = ids[t];
+        hp[kMaxBatch + t] = sids[t];
+        hp[2 * kMaxBatch + t] = pos[t];
+    }
+    CK(cudaMemcpyAsync(ids_, hp, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(tok_seq_, hp + kMaxBatch, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(tok_pos_, hp + 2 * kMaxBatch, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
+    return true;
+}
+
+bool Engine::capture_graph(int key, std::string* err) {
+    const int T = key == 0 ? 1 : key;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    std::string e2;
+    bool ok = fbk_embed(embd_.type, embd_.d, embd_.stride, cfg_.n_embd, ids_, T, x_, cfg_.n_embd, stream_) == 0;
+    ok = ok && run_layers(T, cfg_.n_ctx, &e2);
+    ok = ok && run_head(0, T, logits_, &e2);
+    if (key == 0)
+        ok = ok && fbk_greedy_advance(logits_, cfg_.vocab, ids_, tok_pos_, greedy_out_, greedy_step_, stream_) == 0;
+    else
+        ok = ok && fbk_argmax(logits_, cfg_.vocab, T, cfg_.vocab, argmax_, stream_) == 0;
+    const cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
+    if (!ok || ce != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        if (err) *err = "graph capture failed: " + (e2.empty() ? std::string(cudaGetErrorString(ce)) : e2);
+        cudaGetLastError();
+        return false;
+    }
+    size_t nodes = 0;
+    cudaGraphGetNodes(graph, nullptr, &nodes);
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) { if (err) *err = std::string("graph instantiate: ") + cudaGetErrorString(ie); return false; }
+    graphs_[key] = exec;
+    graph_kernels_[key] = (int)nodes;
+    return true;
+}
+
+bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, float* logits_all, int32_t* argmax,
+                     std::string* err) {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session"; return false; }
+    if (T <= 0 || T > kMaxBatch) { if (err) *err = "bad token count"; return false; }
+    const Config& c = cfg_;
+    for (int t = 0; t < T; ++t)
+        if (ids[t] < 0 || ids[t] >= c.vocab) { if (err) *err = "token id out of range"; return false; }
+    Seq& s = seqs_[sid];
+    const int pos0 = s.len;
+    if (!ensure_pages(sid, pos0 + T, err)) return false;
+    std::vector<int> sids(T, sid), pos(T);
+    for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
+    if (!upload_tokens(ids, sids.data(), pos.data(), T, err)) return false;
+    const bool all = logits_all != nullptr || argmax != nullptr;
+    const int nrows = all ? T : 1;
+    if (T == 1 && use_graphs_ && !prof_) {
+        if (!graphs_.count(1) && !capture_graph(1, err)) return false;
+        CK(cudaGraphLaunch(graphs_[1], stream_));
+    } else {
+        CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, embd_.stride, c.n_embd, ids_, T, x_, c.n_embd, stream_));
+        if (!run_layers(T, pos0 + T, err)) return false;
+        const int row0 = all ? 0 : T - 1;
+        if (!run_head(row0, nrows, logits_, err)) return false;
+        if (argmax) CKP(PC_OTHER, 0, fbk_argmax(logits_, c.vocab, nrows, c.vocab, argmax_, stream_));
+    }
+    if (logits_all) CK(cudaMemcpyAsync(logits_all, logits_, sizeof(float) * (size_t)T * c.vocab, cudaMemcpyDeviceToHost, stream_));
+    if (logits_last)
+        CK(cudaMemcpyAsync(logits_last, logits_ + (size_t)(nrows - 1) * c.vocab, sizeof(float) * c.vocab,
+                           cudaMemcpyDeviceToHost, stream_));
+    if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * T, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    s.len = pos0 + T;
+    return true;
+}
+
+bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err) {
+    if (n <= 0 || n > kMaxBatch) { if (err) *err = "bad batch size"; return false; }
+    const Config& c = cfg_;
+    std::vector<int> pos(n);
+    for (int i = 0; i < n; ++i) {
+        const int sid = sids[i];
+        if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session in batch"; return false; }
+        for (int j = 0; j < i; ++j) if (sids[j] == sid) { if (err) *err = "session repeated in one batch"; return false; }
+        if (ids[i] < 0 || ids[i] >= c.vocab) { if (err) *err = "token id out of range"; return false; }
+        if (!ensure_pages(sid, seqs_[sid].len + 1, err)) return false;
+        pos[i] = seqs_[sid].len;
+    }
+    if (!upload_tokens(ids, sids, pos.data(), n, err)) return false;
+    if (use_graphs_) {
+        if (!graphs_.count(n) && !capture_graph(n, err)) return false;
+        CK(cudaGraphLaunch(graphs_[n], stream_));
+    } else {
+        int max_ctx = 0;
+        for (int i = 0; i < n; ++i) max_ctx = std::max(max_ctx, pos[i] + 1);
+        CK(fbk_embed(embd_.type, embd_.d, embd_.stride, c.n_embd, ids_, n, x_, c.n_embd, stream_));
+        if (!run_layers(n, max_ctx, err)) return false;
+        if (!run_head(0, n, logits_, err)) return false;
+        CK(fbk_argmax(logits_, c.vocab, n, c.vocab, argmax_, stream_));
+    }
+    if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, stream_));
+    if (logits) CK(cudaMemcpyAsync(logits, logits_, sizeof(float) * (size_t)n * c.vocab, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    for (int i = 0; i < n; ++i) seqs_[sids[i]].len += 1;
+    return true;
+}
+
+int Engine::decode_greedy(int sid, int32_t first, int n_steps, int32_t* out, std::string* err) {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session"; return -1; }
+    if (n_steps <= 0) return 0;
+    if (n_steps > greedy_cap_) { if (err) *err = "too many steps for one call"; return -1; }
+    if (first < 0 || first >= cfg_.vocab) { if (err) *err = "token id out of range"; return -1; }
+    Seq& s = seqs_[sid];
+    if (!ensure_pages(sid, s.len + n_steps, err)) return -1;
+    const int pos = s.len;
+    if (!upload_tokens(&first, &sid, &pos, 1, err)) return -1;
+    if (cudaMemsetAsync(greedy_step_, 0, sizeof(int32_t), stream_) != cudaSuccess) { if (err) *err = "memset failed"; return -1; }
+    if (!graphs_.count(0) && !capture_graph(0, err)) return -1;
+    cudaGraphExec_t exec = graphs_[0];
+    cudaEventRecord(ev0_, stream_);
+    for (int i = 0; i < n_steps; ++i) {
+        if (cudaGraphLaunch(exec, stream_) != cudaSuccess) {
+            if (err) *err = "graph launch failed";
+            cudaStreamSynchronize(stream_);
+            return -1;
+        }
+    }
+    cudaEventRecord(ev1_, stream_);
+    if (cudaMemcpyAsync(out, greedy_out_, sizeof(int32_t) * n_steps, cudaMemcpyDeviceToHost, stream_) != cudaSuccess ||
+        cudaStreamSynchronize(stream_) != cudaSuccess) {
+        if (err) *err = std::string("decode failed: ") + cudaGetErrorString(cudaGetLastError());
+        return -1;
+    }
+    cudaEventElapsedTime(&last_greedy_ms_, ev0_, ev1_);
+    s.len += n_steps;
+    return n_steps;
+}
+
+bool Engine::profile_decode(int sid, int32_t first, int n_steps, std::vector<ProfClass>* out, std::string* err) {
+    std::vector<ProfClass> cls(5);
+    cls[PC_GEMV].name = "gemv";
+    cls[PC_NORMQ].name = "norm_quant";
+    cls[PC_ROPE].name = "rope_kv_append";
+    cls[PC_ATTN].name = "attention";
+    cls[PC_OTHER].name = "other";
+    prof_ = &cls;
+    int32_t tok = first;
+    bool ok = true;
+    std::vector<int32_t> am(1);
+    for (int i = 0; i < n_steps && ok; ++i) {
+        ok = forward(sid, &tok, 1, nullptr, nullptr, am.data(), err);
+        tok = am[0];
+    }
+    prof_ = nullptr;
+    if (ok) *out = cls;
+    return ok;
+}
+
+}  // namespace fb

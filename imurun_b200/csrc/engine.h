@@ -1,0 +1,198 @@
+// engine.h — the B200 decode/prefill engine behind the FISH C ABI.
+//
+// One Engine owns one model on one GPU: device weights (repacked GGUF
+// blocks), a paged KV pool shared by all sequences of the model, work buffers
+// for up to kMaxBatch tokens per forward, and CUDA graphs for single-token
+// decode. It plays the role of the reference's LlamaModel
+// (model/fish/include/fish/model.h:162-292): load, forward, set_kv_len /
+// reset_kv, logits, argmax.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.h"
+#include "kernels/kernels.h"
+
+namespace fb {
+
+constexpr int kMaxBatch = 256;   // tokens per forward (reference max_batch_, model.h:292)
+constexpr int kPageSize = 16;    // KV positions per page
+
+struct Config {
+    std::string arch = "llama";
+    int n_layers = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, head_dim = 0;
+    int n_ctx = 0, n_ctx_train = 0, vocab = 0, rot_dim = 0;
+    float eps = 1e-5f, freq_base = 10000.0f;
+    int bos = 1, eos = 2;
+    bool tied_output = false, neox = false, qk_norm = false;
+    int n_experts = 0, n_experts_per_tok = 0, n_ff_exp = 0;
+    bool expert_weights_norm = true;
+    // RoPE scaling (src/model.cpp:508-537)
+    float freq_scale = 1.0f, mscale = 1.0f;
+    float yarn_factor = 0.0f, yarn_attn_factor = 1.0f, yarn_beta_fast = 32.0f, yarn_beta_slow = 1.0f;
+    int yarn_orig_ctx = 0;
+    int q_dim() const { return n_head * head_dim; }
+    int kv_dim() const { return n_head_kv * head_dim; }
+};
+
+// RoPE cos/sin table [n_ctx][rot_dim/2] for c (uses n_ctx, rot_dim,
+// freq_base and the scaling fields); ff = per-pair frequency factors or null.
+void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, std::vector<float>& sn);
+
+struct DevW {
+    int type = -1;
+    int n_in = 0, n_out = 0, n_exp = 1;
+    size_t stride = 0;           // device row stride
+    size_t expert_bytes = 0;     // bytes per expert slice (3-D tensors)
+    uint8_t* d = nullptr;
+    bool ok() const { return d != nullptr; }
+};
+
+struct DevLayer {
+    DevW wq, wk, wv, wo, wg, wu, wd, gate_inp, gate_exps, up_exps, down_exps;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct Seq {
+    bool open = false;
+    int len = 0;                 // positions holding valid KV
+    std::vector<int> pages;      // page ids in position order
+};
+
+class Engine {
+public:
+    Engine() = default;
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    bool load(const std::string& path, int n_ctx, std::string* err);
+    const Config& cfg() const { return cfg_; }
+    const Gguf& gguf() const { return *gguf_; }
+    uint64_t weights_bytes() const { return weights_file_bytes_; }
+    uint64_t device_weight_bytes() const { return weights_dev_bytes_; }
+    uint64_t kv_bytes() const { return kv_pool_bytes_; }
+    int device() const { return device_; }
+    std::string device_name() const;
+    double load_seconds_upload = 0.0;
+
+    // ---- sequences (slot 0 always exists: the context's own sequence)
+    int seq_open();
+    int seq_fork(int parent, int prefix_len, std::string* err);
+    bool seq_close(int sid);
+    int seq_len(int sid) const;
+    bool seq_truncate(int sid, int n);      // set_kv_len: drop positions >= n
+    std::vector<int> seq_pages(int sid) const;
+    int page_size() const { return kPageSize; }
+    int free_pages() const { return (int)free_pages_.size(); }
+
+    // Forward T tokens (host ids) onto sequence sid at its current length
+    // (positions len .. len+T-1). Logits of the last token go to logits_last
+    // (host, nullable); all_logits (host, T*vocab) and argmax (host, T)
+    // are optional. Chunking to kMaxBatch is the caller's job.
+    bool forward(int sid, const int32_t* ids, int T, float* logits_last, float* logits_all, int32_t* argmax,
+                 std::string* err);
+    // One token for each of n sequences (n <= kMaxBatch).
+    bool decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err);
+    // Greedy decode of n_steps on the device with a captured CUDA graph.
+    int decode_greedy(int sid, int32_t first, int n_steps, int32_t* out, std::string* err);
+    // Device time (CUDA events on the engine stream) of the last greedy run.
+    float last_greedy_ms() const { return last_greedy_ms_; }
+    // Kernel nodes of the captured step graph for T tokens (0 if none yet).
+    int graph_kernels(int T) const {
+        auto it = graph_kernels_.find(T);
+        return it == graph_kernels_.end() ? 0 : it->second;
+    }
+
+    // Per-launch device timing of non-graph single-token steps: each kernel
+    // launch is bracketed by events on the engine stream and attributed to a
+    // class; GEMV launches also carry their algorithmic bytes.
+    struct ProfClass { std::string name; int launches = 0; double ms = 0.0; double bytes = 0.0; };
+    bool profile_decode(int sid, int32_t first, int n_steps, std::vector<ProfClass>* out, std::string* err);
+
+    // ---- kernel-level access for the parity entry points
+    cudaStream_t stream() const { return stream_; }
+
+private:
+    bool alloc_buffers(std::string* err);
+    bool upload_weights(std::string* err);
+    bool ensure_pages(int sid, int new_len, std::string* err);
+    void write_page_table(int sid);
+    bool run_layers(int T, int max_ctx, std::string* err);
+    bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err);
+    bool gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi,
+              const float* xf, int ldxf, const int32_t* expert, std::string* err);
+    bool gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
+                    const ActQ& a, int T, int epi, std::string* err);
+    KvView kv_view() const;
+    // Step graphs are sequence-agnostic (token -> sequence slot and position
+    // come from device arrays): key T = T-token step with logits + argmax,
+    // key 0 = single-token greedy step that feeds its own argmax back.
+    bool capture_graph(int key, std::string* err);
+    bool upload_tokens(const int32_t* ids, const int* sids, const int* pos, int T, std::string* err);
+    void drop_graphs();
+    void prof_begin();
+    void prof_end(int cls, double bytes);
+
+    Config cfg_;
+    std::unique_ptr<Gguf> gguf_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    uint64_t weights_file_bytes_ = 0, weights_dev_bytes_ = 0, kv_pool_bytes_ = 0;
+
+    // device weights (one arena)
+    uint8_t* warena_ = nullptr;
+    std::vector<DevLayer> layers_;
+    DevW embd_, out_w_;
+    float* out_norm_ = nullptr;
+    float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
+    std::vector<float*> small_;   // small device vectors to free
+    bool want32_e_ = false, wantk_e_ = false;   // activation layouts for E-wide inputs
+    bool want32_q_ = false, wantk_q_ = false;   // ... for the attention output (wo)
+    bool want32_f_ = false, wantk_f_ = false;   // ... for the FFN hidden (down)
+
+    // work buffers
+    int max_k_ = 0;
+    float *x_ = nullptr, *xb_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *attn_ = nullptr;
+    float *g_ = nullptr, *u_ = nullptr, *logits_ = nullptr, *router_ = nullptr, *eo_ = nullptr;
+    int32_t *sel_ = nullptr;
+    float* wsel_ = nullptr;
+    ActQ act_{};
+    int8_t* act_mem_ = nullptr;
+    float* att_scratch_ = nullptr;
+    size_t att_scratch_floats_ = 0;
+    int att_chunk_ = 32;
+    int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;
+    int32_t *greedy_out_ = nullptr, *greedy_step_ = nullptr;
+    int greedy_cap_ = 1 << 16;
+    int32_t* h_pinned_ = nullptr;   // pinned staging for ids / tok_seq / tok_pos
+
+    // KV pool
+    void* kv_pool_ = nullptr;
+    int n_pages_ = 0;
+    size_t page_elems_ = 0;
+    bool kv_f16_ = true;
+    std::vector<int> page_ref_;
+    std::vector<int> free_pages_;
+    int32_t* pt_arena_ = nullptr;   // [max_seqs][pt_stride]
+    int pt_stride_ = 0;
+    int max_seqs_ = 0;
+    std::vector<Seq> seqs_;
+
+    std::map<int, cudaGraphExec_t> graphs_;
+    std::map<int, int> graph_kernels_;
+    bool use_graphs_ = true;
+    float last_greedy_ms_ = 0.0f;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    std::vector<ProfClass>* prof_ = nullptr;
+    cudaEvent_t pe0_ = nullptr, pe1_ = nullptr;
+};
+
+}  // namespace fb

@@ -1,0 +1,361 @@
+// kernel_api.cpp — host-buffer entry points for single kernels
+// (include/fish/fish_kernels.h). Each call allocates its device buffers, runs
+// the production kernel and copies results back; they exist for parity tests.
+#include <fish/fish_kernels.h>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <vector>
+
+#include "engine.h"
+#include "kernels/kernels.h"
+
+using namespace fb;
+
+namespace {
+
+struct DevBuf {
+    void* p = nullptr;
+    ~DevBuf() { if (p) cudaFree(p); }
+    template <class T> T* as() { return static_cast<T*>(p); }
+    int alloc(size_t n) { return (int)cudaMalloc(&p, n ? n : 16); }
+};
+
+#define TRY(x) do { const int rc_ = (int)(x); if (rc_) return rc_; } while (0)
+
+int check_device() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) return (int)cudaErrorNoDevice;
+    return 0;
+}
+
+// Device activation planes for rows x K (both layouts).
+struct DevAct {
+    DevBuf mem;
+    ActQ a{};
+    int make(int rows, int K) {
+        const size_t ld = (size_t)((K + 15) / 16 * 16);
+        const size_t nq = (size_t)rows * ld, n32 = (size_t)rows * (K / 32 + 1), n256 = (size_t)rows * (K / 256 + 1);
+        TRY(mem.alloc(2 * nq + n32 * 12 + n256 * 4 + 256));
+        uint8_t* p = mem.as<uint8_t>();
+        auto al = [](size_t v) { return (v + 15) / 16 * 16; };
+        a.q32 = (int8_t*)p; p += al(nq);
+        a.qk = (int8_t*)p; p += al(nq);
+        a.d32 = (float*)p; p += al(n32 * 4);
+        a.s32 = (int32_t*)p; p += al(n32 * 4);
+        a.dk = (float*)p; p += al(n256 * 4);
+        a.bsk = (int16_t*)p;
+        a.K = K;
+        a.ld = (int)ld;
+        return 0;
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int fbx_quantize_acts(const float* x, int rows, int K, void* q8act, void* q8actk) {
+    if (!x || rows <= 0 || K <= 0 || K % 32) return -1;
+    TRY(check_device());
+    DevBuf dx;
+    DevAct da;
+    TRY(dx.alloc(sizeof(float) * rows * K));
+    TRY(da.make(rows, K));
+    TRY(cudaMemcpy(dx.p, x, sizeof(float) * rows * K, cudaMemcpyHostToDevice));
+    const int wantk = q8actk && K % 256 == 0;
+    TRY(fbk_quantize_rows(dx.as<float>(), K, rows, K, &da.a, q8act ? 1 : 0, wantk, nullptr));
+    TRY(cudaDeviceSynchronize());
+    const size_t ld = (size_t)da.a.ld;
+    std::vector<int8_t> q32((size_t)rows * ld), qk((size_t)rows * ld);
+    std::vector<float> d32((size_t)rows * (K / 32)), dk((size_t)rows * (K / 256) + 1);
+    std::vector<int32_t> s32((size_t)rows * (K / 32));
+    std::vector<int16_t> bs((size_t)rows * (K / 32));
+    TRY(cudaMemcpy(q32.data(), da.a.q32, q32.size(), cudaMemcpyDeviceToHost));
+    TRY(cudaMemcpy(qk.data(), da.a.qk, qk.size(), cudaMemcpyDeviceToHost));
+    TRY(cudaMemcpy(d32.data(), da.a.d32, d32.size() * 4, cudaMemcpyDeviceToHost));
+    TRY(cudaMemcpy(s32.data(), da.a.s32, s32.size() * 4, cudaMemcpyDeviceToHost));
+    TRY(cudaMemcpy(dk.data(), da.a.dk, dk.size() * 4, cudaMemcpyDeviceToHost));
+    TRY(cudaMemcpy(bs.data(), da.a.bsk, bs.size() * 2, cudaMemcpyDeviceToHost));
+    if (q8act) {
+        uint8_t* o = static_cast<uint8_t*>(q8act);
+        for (int r = 0; r < rows; ++r)
+            for (int b = 0; b < K / 32; ++b, o += 40) {
+                std::memcpy(o, &d32[(size_t)r * (K / 32) + b], 4);
+                std::memcpy(o + 4, &s32[(size_t)r * (K / 32) + b], 4);
+                std::memcpy(o + 8, &q32[(size_t)r * ld + 32 * b], 32);
+            }
+    }
+    if (wantk) {
+        uint8_t* o = static_cast<uint8_t*>(q8actk);
+        for (int r = 0; r < rows; ++r)
+            for (int b = 0; b < K / 256; ++b, o += 276) {
+                std::memcpy(o, &dk[(size_t)r * (K / 256) + b], 4);
+                std::memcpy(o + 4, &bs[(size_t)r * (K / 32) + 8 * b], 16);
+                std::memcpy(o + 20, &qk[(size_t)r * ld + 256 * b], 256);
+            }
+    }
+    return 0;
+}
+
+int fbx_rmsnorm(const float* x, const float* w, int rows, int K, float eps, float* out) {
+    if (!x || !w || !out || rows <= 0 || K <= 0) return -1;
+    TRY(check_device());
+    DevBuf dx, dw, dout;
+    DevAct da;
+    TRY(dx.alloc(sizeof(float) * rows * K));
+    TRY(dw.alloc(sizeof(float) * K));
+    TRY(dout.alloc(sizeof(float) * rows * K));
+    TRY(da.make(rows, K));
+    TRY(cudaMemcpy(dx.p, x, sizeof(float) * rows * K, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dw.p, w, sizeof(float) * K, cudaMemcpyHostToDevice));
+    TRY(fbk_rmsnorm_quant(dx.as<float>(), K, dw.as<float>(), eps, rows, K, dout.as<float>(), K, &da.a, 0, 0, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(float) * rows * K, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+static int upload_rows(int type, const void* w, int n_in, int n_out, DevBuf& dw, size_t* stride) {
+    const size_t st = dev_row_bytes(type, n_in);
+    if (!st) return -1;
+    const size_t src_rb = ggml_row_bytes(type, (uint64_t)n_in);
+    std::vector<uint8_t> h(st * (size_t)n_out);
+    for (int r = 0; r < n_out; ++r)
+        repack_row(type, static_cast<const uint8_t*>(w) + (size_t)r * src_rb, h.data() + (size_t)r * st, n_in);
+    TRY(dw.alloc(h.size()));
+    TRY(cudaMemcpy(dw.p, h.data(), h.size(), cudaMemcpyHostToDevice));
+    *stride = st;
+    return 0;
+}
+
+int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int T, float* y) {
+    if (!w || !x || !y || n_in <= 0 || n_out <= 0 || T <= 0 || T > kMaxBatch) return -1;
+    if ((type == T_Q4_K || type == T_Q6_K) && n_in % 256) return -1;
+    if (type == T_Q8_0 && n_in % 32) return -1;
+    TRY(check_device());
+    DevBuf dw, dx, dy;
+    DevAct da;
+    size_t stride = 0;
+    TRY(upload_rows(type, w, n_in, n_out, dw, &stride));
+    TRY(dx.alloc(sizeof(float) * T * n_in));
+    TRY(dy.alloc(sizeof(float) * T * n_out));
+    TRY(da.make(T + 8, n_in));
+    TRY(cudaMemcpy(dx.p, x, sizeof(float) * T * n_in, cudaMemcpyHostToDevice));
+    const bool quant = type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K;
+    if (quant) TRY(fbk_quantize_rows(dx.as<float>(), n_in, T, n_in, &da.a, type == T_Q8_0, type != T_Q8_0, nullptr));
+    for (int t0 = 0; t0 < T; t0 += 8) {
+        GemvArgs g{};
+        g.nseg = 1;
+        g.K = n_in;
+        g.T = T - t0 < 8 ? T - t0 : 8;
+        g.act = da.a;
+        g.act.q32 = da.a.q32 + (size_t)t0 * da.a.ld;
+        g.act.qk = da.a.qk + (size_t)t0 * da.a.ld;
+        g.act.d32 = da.a.d32 + (size_t)t0 * (n_in / 32);
+        g.act.s32 = da.a.s32 + (size_t)t0 * (n_in / 32);
+        g.act.dk = da.a.dk + (size_t)t0 * (n_in / 256);
+        g.act.bsk = da.a.bsk + (size_t)t0 * (n_in / 32);
+        g.xf = dx.as<float>() + (size_t)t0 * n_in;
+        g.ldxf = n_in;
+        g.seg[0].type = type;
+        g.seg[0].w = dw.as<uint8_t>();
+        g.seg[0].row_stride = stride;
+        g.seg[0].rows = n_out;
+        g.seg[0].y = dy.as<float>() + (size_t)t0 * n_out;
+        g.seg[0].ldy = n_out;
+        g.seg[0].epi = EPI_STORE;
+        TRY(fbk_gemv(&g, nullptr));
+    }
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(y, dy.p, sizeof(float) * T * n_out, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int fbx_block_sums(int type, const void* w, int n_in, int n_out, const void* acts, int32_t* sumi, int32_t* mins) {
+    if (!w || !acts || !sumi || n_in <= 0 || n_out <= 0) return -1;
+    if (type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K) return -1;
+    const bool k = type != T_Q8_0;
+    if (n_in % (k ? 256 : 32)) return -1;
+    TRY(check_device());
+    DevBuf dw, ds, dm;
+    DevAct da;
+    size_t stride = 0;
+    TRY(upload_rows(type, w, n_in, n_out, dw, &stride));
+    TRY(da.make(1, n_in));
+    // unpack the reference records into the device planes
+    const uint8_t* a = static_cast<const uint8_t*>(acts);
+    std::vector<int8_t> q(da.a.ld, 0);
+    if (k) {
+        std::vector<float> d(n_in / 256);
+        std::vector<int16_t> bs(n_in / 32);
+        for (int b = 0; b < n_in / 256; ++b) {
+            std::memcpy(&d[b], a + 276 * b, 4);
+            std::memcpy(&bs[8 * b], a + 276 * b + 4, 16);
+            std::memcpy(&q[256 * b], a + 276 * b + 20, 256);
+        }
+        TRY(cudaMemcpy(da.a.qk, q.data(), q.size(), cudaMemcpyHostToDevice));
+        TRY(cudaMemcpy(da.a.dk, d.data(), d.size() * 4, cudaMemcpyHostToDevice));
+        TRY(cudaMemcpy(da.a.bsk, bs.data(), bs.size() * 2, cudaMemcpyHostToDevice));
+    } else {
+        std::vector<float> d(n_in / 32);
+        for (int b = 0; b < n_in / 32; ++b) {
+            std::memcpy(&d[b], a + 40 * b, 4);
+            std::memcpy(&q[32 * b], a + 40 * b + 8, 32);
+        }
+        TRY(cudaMemcpy(da.a.q32, q.data(), q.size(), cudaMemcpyHostToDevice));
+        TRY(cudaMemcpy(da.a.d32, d.data(), d.size() * 4, cudaMemcpyHostToDevice));
+    }
+    const int nb = n_in / (k ? 256 : 32);
+    TRY(ds.alloc(sizeof(int32_t) * (size_t)n_out * nb));
+    TRY(dm.alloc(sizeof(int32_t) * (size_t)n_out * nb));
+    TRY(cudaMemset(dm.p, 0, sizeof(int32_t) * (size_t)n_out * nb));
+    TRY(fbk_block_sums(type, dw.as<uint8_t>(), stride, n_out, n_in, &da.a, ds.as<int32_t>(), dm.as<int32_t>(), nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(sumi, ds.p, sizeof(int32_t) * (size_t)n_out * nb, cudaMemcpyDeviceToHost));
+    if (mins) TRY(cudaMemcpy(mins, dm.p, sizeof(int32_t) * (size_t)n_out * nb, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// A one-layer paged pool whose page i holds positions [16i, 16i+16).
+struct TestPool {
+    DevBuf pool, pt, seq, pos;
+    KvView kv{};
+    int make(int n_pos, int HKV, int D, int f16, int T, int pos0) {
+        const int P = kPageSize, np = (n_pos + P - 1) / P;
+        const size_t head = (size_t)P * D, vofs = (size_t)HKV * head, page = 2 * vofs;
+        const size_t esz = f16 ? 2 : 4;
+        TRY(pool.alloc(page * np * esz));
+        TRY(cudaMemset(pool.p, 0, page * np * esz));
+        std::vector<int32_t> hp(np), hs(T, 0), hq(T);
+        for (int i = 0; i < np; ++i) hp[i] = i;
+        for (int t = 0; t < T; ++t) hq[t] = pos0 + t;
+        TRY(pt.alloc(sizeof(int32_t) * np));
+        TRY(seq.alloc(sizeof(int32_t) * T));
+        TRY(pos.alloc(sizeof(int32_t) * T));
+        TRY(cudaMemcpy(pt.p, hp.data(), sizeof(int32_t) * np, cudaMemcpyHostToDevice));
+        TRY(cudaMemcpy(seq.p, hs.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice));
+        TRY(cudaMemcpy(pos.p, hq.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice));
+        kv.f16 = f16;
+        kv.k = pool.p;
+        kv.v = static_cast<uint8_t*>(pool.p) + vofs * esz;
+        kv.pt = pt.as<int32_t>();
+        kv.pt_stride = np;
+        kv.tok_seq = seq.as<int32_t>();
+        kv.tok_pos = pos.as<int32_t>();
+        kv.page_size = P;
+        kv.page_stride = page;
+        kv.layer_stride = page;
+        kv.head_stride = head;
+        return 0;
+    }
+};
+
+int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0, int T,
+                  int kv_f16, float* out) {
+    if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || D % 32 || D > 128) return -1;
+    TRY(check_device());
+    TestPool tp;
+    TRY(tp.make(n_keys, HKV, D, kv_f16, T, pos0));
+    const int P = kPageSize, np = (n_keys + P - 1) / P;
+    const size_t head = (size_t)P * D, vofs = (size_t)HKV * head, page = 2 * vofs;
+    std::vector<float> hf(page * np, 0.0f);
+    for (int j = 0; j < n_keys; ++j)
+        for (int h = 0; h < HKV; ++h)
+            for (int d = 0; d < D; ++d) {
+                const size_t o = (size_t)(j / P) * page + h * head + (size_t)(j % P) * D + d;
+                hf[o] = k[(size_t)j * HKV * D + h * D + d];
+                hf[o + vofs] = v[(size_t)j * HKV * D + h * D + d];
+            }
+    if (kv_f16) {
+        std::vector<__half> hh(hf.size());
+        for (size_t i = 0; i < hf.size(); ++i) hh[i] = __float2half_rn(hf[i]);
+        TRY(cudaMemcpy(tp.pool.p, hh.data(), hh.size() * 2, cudaMemcpyHostToDevice));
+    } else {
+        TRY(cudaMemcpy(tp.pool.p, hf.data(), hf.size() * 4, cudaMemcpyHostToDevice));
+    }
+    DevBuf dq, dout, scratch;
+    const int n_splits = (pos0 + T + 127) / 128;
+    const size_t sf = (size_t)T * H * n_splits * (D + 2);
+    TRY(dq.alloc(sizeof(float) * T * H * D));
+    TRY(dout.alloc(sizeof(float) * T * H * D));
+    TRY(scratch.alloc(sizeof(float) * sf));
+    TRY(cudaMemcpy(dq.p, q, sizeof(float) * T * H * D, cudaMemcpyHostToDevice));
+    TRY(fbk_attention(dq.as<float>(), H * D, T, H, HKV, D, 1.0f / std::sqrt((float)D), tp.kv, 0, dout.as<float>(), H * D,
+                      scratch.as<float>(), sf, pos0 + T, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(float) * T * H * D, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_dim, int neox, float freq_base, int pos0) {
+    if (!q || !k || T <= 0 || pos0 < 0 || rot_dim <= 0 || rot_dim > D || D % 2) return -1;
+    TRY(check_device());
+    Config c;
+    c.n_ctx = pos0 + T;
+    c.rot_dim = rot_dim;
+    c.head_dim = D;
+    c.freq_base = freq_base;
+    std::vector<float> cs, sn;
+    build_rope_table(c, nullptr, cs, sn);
+    TestPool tp;
+    TRY(tp.make(pos0 + T, HKV, D, 0, T, pos0));
+    DevBuf dq, dk, dv, dc, ds;
+    TRY(dq.alloc(sizeof(float) * T * H * D));
+    TRY(dk.alloc(sizeof(float) * T * HKV * D));
+    TRY(dv.alloc(sizeof(float) * T * HKV * D));
+    TRY(dc.alloc(sizeof(float) * cs.size()));
+    TRY(ds.alloc(sizeof(float) * sn.size()));
+    TRY(cudaMemcpy(dq.p, q, sizeof(float) * T * H * D, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dk.p, k, sizeof(float) * T * HKV * D, cudaMemcpyHostToDevice));
+    TRY(cudaMemset(dv.p, 0, sizeof(float) * T * HKV * D));
+    TRY(cudaMemcpy(dc.p, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(ds.p, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice));
+    TRY(fbk_rope_append(dq.as<float>(), H * D, dk.as<float>(), dv.as<float>(), HKV * D, T, H, HKV, D, rot_dim, neox,
+                        dc.as<float>(), ds.as<float>(), tp.kv, 0, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(q, dq.p, sizeof(float) * T * H * D, cudaMemcpyDeviceToHost));
+    const int P = kPageSize;
+    const size_t head = (size_t)P * D;
+    std::vector<float> pool(tp.kv.page_stride * ((pos0 + T + P - 1) / P));
+    TRY(cudaMemcpy(pool.data(), tp.pool.p, pool.size() * 4, cudaMemcpyDeviceToHost));
+    for (int t = 0; t < T; ++t) {
+        const int j = pos0 + t;
+        for (int h = 0; h < HKV; ++h)
+            for (int d = 0; d < D; ++d)
+                k[(size_t)t * HKV * D + h * D + d] = pool[(size_t)(j / P) * tp.kv.page_stride + h * head + (size_t)(j % P) * D + d];
+    }
+    return 0;
+}
+
+int fbx_argmax(const float* x, int rows, int n, int32_t* out) {
+    if (!x || !out || rows <= 0 || n <= 0) return -1;
+    TRY(check_device());
+    DevBuf dx, dout;
+    TRY(dx.alloc(sizeof(float) * (size_t)rows * n));
+    TRY(dout.alloc(sizeof(int32_t) * rows));
+    TRY(cudaMemcpy(dx.p, x, sizeof(float) * (size_t)rows * n, cudaMemcpyHostToDevice));
+    TRY(fbk_argmax(dx.as<float>(), n, rows, n, dout.as<int32_t>(), nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out) {
+    if (!table || !ids || !out || E <= 0 || n_rows <= 0 || T <= 0) return -1;
+    for (int t = 0; t < T; ++t) if (ids[t] < 0 || ids[t] >= n_rows) return -1;
+    TRY(check_device());
+    DevBuf dw, di, dout;
+    size_t stride = 0;
+    TRY(upload_rows(type, table, E, n_rows, dw, &stride));
+    TRY(di.alloc(sizeof(int32_t) * T));
+    TRY(dout.alloc(sizeof(float) * (size_t)T * E));
+    TRY(cudaMemcpy(di.p, ids, sizeof(int32_t) * T, cudaMemcpyHostToDevice));
+    TRY(fbk_embed(type, dw.as<uint8_t>(), stride, E, di.as<int32_t>(), T, dout.as<float>(), E, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,271 @@
+// attention.cu — RoPE, KV append into the paged cache, causal GQA attention.
+//
+// Reference behaviour: RoPE from the
+// precomputed cos/sin table with pairs (2i, 2i+1) or NeoX (i, i+half)
+// (src/ops.cpp:126-156), K/V rows stored at their position
+// (src/model.cpp:1723-1731), and per (token, head) softmax attention over
+// positions 0..pos with scale 1/sqrt(D) (src/ops.cpp:303-356). The KV cache is
+// paged (P positions per page, every layer of a position range in one page)
+// and fp16 or f32.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fb {
+
+__device__ __forceinline__ size_t kv_off(const KvView& kv, int layer, int head, int t, int pos) {
+    const int page = kv.pt[(size_t)kv.tok_seq[t] * kv.pt_stride + pos / kv.page_size];
+    return (size_t)page * kv.page_stride + (size_t)layer * kv.layer_stride + (size_t)head * kv.head_stride +
+           (size_t)(pos % kv.page_size) * (kv.head_stride / kv.page_size);
+}
+
+__global__ void k_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int H, int HKV, int D,
+                              int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer) {
+    const int t = blockIdx.x;
+    const int pos = kv.tok_pos[t];
+    const int half = rot / 2;
+    const float* c = rcos + (size_t)pos * half;
+    const float* s = rsin + (size_t)pos * half;
+    float* qr = q + (size_t)t * ldq;
+    const float* kr = k + (size_t)t * ldkv;
+    const float* vr = v + (size_t)t * ldkv;
+    // q heads: rotate in place (biases were added by the projection epilogue)
+    for (int idx = threadIdx.x; idx < H * (D / 2); idx += blockDim.x) {
+        const int h = idx / (D / 2), i = idx % (D / 2);
+        float* hv = qr + (size_t)h * D;
+        if (i < half) {
+            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            const float x0 = hv[a], x1 = hv[b];
+            hv[a] = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
+            hv[b] = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+        }
+    }
+    // k heads: rotate and store; v heads: store
+    for (int idx = threadIdx.x; idx < HKV * (D / 2); idx += blockDim.x) {
+        const int h = idx / (D / 2), i = idx % (D / 2);
+        const float* hk = kr + (size_t)h * D;
+        const float* hvv = vr + (size_t)h * D;
+        const size_t base = kv_off(kv, layer, h, t, pos);
+        int a, b;
+        float k0, k1;
+        if (i < half) {
+            a = neox ? i : 2 * i;
+            b = neox ? i + half : 2 * i + 1;
+            const float x0 = hk[a], x1 = hk[b];
+            k0 = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
+            k1 = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+        } else {
+            a = 2 * i;
+            b = 2 * i + 1;
+            k0 = hk[a];
+            k1 = hk[b];
+        }
+        const float v0 = hvv[2 * i], v1 = hvv[2 * i + 1];
+        if (kv.f16) {
+            __half* kp = reinterpret_cast<__half*>(kv.k) + base;
+            __half* vp = reinterpret_cast<__half*>(kv.v) + base;
+            kp[a] = __float2half_rn(k0);
+            kp[b] = __float2half_rn(k1);
+            vp[2 * i] = __float2half_rn(v0);
+            vp[2 * i + 1] = __float2half_rn(v1);
+        } else {
+            float* kp = reinterpret_cast<float*>(kv.k) + base;
+            float* vp = reinterpret_cast<float*>(kv.v) + base;
+            kp[a] = k0;
+            kp[b] = k1;
+            vp[2 * i] = v0;
+            vp[2 * i + 1] = v1;
+        }
+    }
+}
+
+// Split-K attention. CTA = (query token t, kv head hk, key split s); it serves
+// the G = H/HKV query heads of the group so each K/V row is read once per
+// group. Keys are assigned one per lane for the scores (dot over D from
+// shared q), then one D-slice per lane for P.V. Partial (max, sum, o) go to
+// scratch and k_attn_combine merges the splits.
+constexpr int kSplit = 128;      // keys per split
+constexpr int kMaxG = 8;         // query heads per kv head supported
+constexpr int kMaxD = 128;
+
+template <bool F16>
+__global__ void __launch_bounds__(128) k_attn_split(const float* __restrict__ q, int ldq, int H, int HKV, int D,
+                                                    float scale, KvView kv, int layer, float* __restrict__ part,
+                                                    int n_splits) {
+    const int t = blockIdx.z, hk = blockIdx.y, sp = blockIdx.x;
+    const int G = H / HKV;
+    const int pos = kv.tok_pos[t];
+    const int n_keys = pos + 1;
+    const int j0 = sp * kSplit;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float sq[kMaxG][kMaxD];
+    __shared__ float sm[4][kMaxG], sl[4][kMaxG];
+    __shared__ float so[4][kMaxG][kMaxD];
+    float* pm = part + (((size_t)t * H + (size_t)hk * G) * n_splits + sp) * (D + 2);
+    if (j0 >= n_keys) {
+        if (threadIdx.x < G) {
+            float* p = part + (((size_t)t * H + (size_t)hk * G + threadIdx.x) * n_splits + sp) * (D + 2);
+            p[0] = -INFINITY;
+            p[1] = 0.0f;
+        }
+        (void)pm;
+        return;
+    }
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i % D;
+        sq[g][d] = q[(size_t)t * ldq + (size_t)(hk * G + g) * D + d];
+    }
+    __syncthreads();
+    const int j1 = min(n_keys, j0 + kSplit);
+    float m[kMaxG], l[kMaxG], o[kMaxG][4];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
+    }
+    const int dper = D / 32;  // values of D per lane in the P.V step (<= 4)
+    for (int jb = j0 + warp * 32; jb < j1; jb += 4 * 32) {
+        const int j = jb + lane;
+        float sc[kMaxG];
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) sc[g] = -INFINITY;
+        if (j < j1) {
+            const size_t off = kv_off(kv, layer, hk, t, j);
+            float dot[kMaxG];
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g) dot[g] = 0.0f;
+            for (int d = 0; d < D; d += 8) {
+                float kf[8];
+                if (F16) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.k) + off + d);
+                    const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(hp[e]);
+                        kf[2 * e] = f.x;
+                        kf[2 * e + 1] = f.y;
+                    }
+                } else {
+                    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d);
+                    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d + 4);
+                    kf[0] = a.x; kf[1] = a.y; kf[2] = a.z; kf[3] = a.w;
+                    kf[4] = b.x; kf[5] = b.y; kf[6] = b.z; kf[7] = b.w;
+                }
+#pragma unroll
+                for (int g = 0; g < kMaxG; ++g) {
+                    if (g < G) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) dot[g] = fmaf(sq[g][d + e], kf[e], dot[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g) sc[g] = __fmul_rn(dot[g], scale);
+        }
+        // online softmax update for this batch of 32 keys
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+            if (g >= G) break;
+            const float bm = warp_max(sc[g]);
+            const float nm = fmaxf(m[g], bm);
+            const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - nm);
+            const float p = j < j1 ? expf(sc[g] - nm) : 0.0f;
+            l[g] = l[g] * corr + warp_sum(p);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][e] *= corr;
+            m[g] = nm;
+            sc[g] = p;  // reuse as probability
+        }
+        // P.V: lane owns D-slice [lane*dper, +dper)
+        const int nj = min(32, j1 - jb);
+        for (int jj = 0; jj < nj; ++jj) {
+            const size_t off = kv_off(kv, layer, hk, t, jb + jj);
+            float vf[4];
+            if (F16) {
+                const __half* vp = reinterpret_cast<const __half*>(kv.v) + off + lane * dper;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) vf[e] = e < dper ? __half2float(vp[e]) : 0.0f;
+            } else {
+                const float* vp = reinterpret_cast<const float*>(kv.v) + off + lane * dper;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) vf[e] = e < dper ? vp[e] : 0.0f;
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g) {
+                if (g >= G) break;
+                const float p = __shfl_sync(0xffffffffu, sc[g], jj);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+            }
+        }
+    }
+    // merge the 4 warps
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        if (lane == 0) { sm[warp][g] = m[g]; sl[warp][g] = l[g]; }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) if (e < dper) so[warp][g][lane * dper + e] = o[g][e];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i % D;
+        float M = -INFINITY;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w][g]);
+        float L = 0.0f, O = 0.0f;
+        for (int w = 0; w < 4; ++w) {
+            if (sm[w][g] == -INFINITY) continue;
+            const float c = expf(sm[w][g] - M);
+            L += sl[w][g] * c;
+            O += so[w][g][d] * c;
+        }
+        float* p = part + (((size_t)t * H + (size_t)hk * G + g) * n_splits + sp) * (D + 2);
+        if (d == 0) { p[0] = M; p[1] = L; }
+        p[2 + d] = O;
+    }
+}
+
+__global__ void k_attn_combine(const float* __restrict__ part, int H, int D, int n_splits, float* out, int ldo) {
+    const int t = blockIdx.y, h = blockIdx.x;
+    const float* p = part + ((size_t)t * H + h) * n_splits * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, p[(size_t)s * (D + 2)]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float L = 0.0f, O = 0.0f;
+        for (int s = 0; s < n_splits; ++s) {
+            const float ms = p[(size_t)s * (D + 2)];
+            if (ms == -INFINITY) continue;
+            const float c = expf(ms - M);
+            L += p[(size_t)s * (D + 2) + 1] * c;
+            O += p[(size_t)s * (D + 2) + 2 + d] * c;
+        }
+        out[(size_t)t * ldo + (size_t)h * D + d] = L > 0.0f ? O / L : 0.0f;
+    }
+}
+
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" int fbk_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV,
+                               int D, int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer,
+                               cudaStream_t st) {
+    if (T <= 0) return 0;
+    k_rope_append<<<T, 256, 0, st>>>(q, ldq, k, v, ldkv, H, HKV, D, rot, neox, rcos, rsin, kv, layer);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
+                             float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st) {
+    if (T <= 0) return 0;
+    const int G = H / HKV;
+    if (G > kMaxG || D > kMaxD || D % 32 != 0 || D / 32 > 4) return (int)cudaErrorInvalidValue;
+    const int n_splits = (max_ctx + kSplit - 1) / kSplit;
+    if ((size_t)T * H * n_splits * (D + 2) > scratch_floats) return (int)cudaErrorInvalidValue;
+    dim3 grid(n_splits, HKV, T);
+    if (kv.f16) k_attn_split<true><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+    else k_attn_split<false><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+    k_attn_combine<<<dim3(H, T), 128, 0, st>>>(scratch, H, D, n_splits, out, ldo);
+    return (int)cudaGetLastError();
+}

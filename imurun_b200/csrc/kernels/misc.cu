@@ -1,0 +1,220 @@
+// misc.cu — embedding gather, residual add, argmax, MoE routing.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fb {
+
+// Value i of a device-layout row, dequantised exactly like the reference's
+// dequant_row (src/quant.cpp:129-216): same float operations in the same order.
+__device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n, int i) {
+    switch (type) {
+        case T_F32: return reinterpret_cast<const float*>(row)[i];
+        case T_F16: return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
+        case T_Q8_0: {
+            const int nb = n / 32, b = i / 32;
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (size_t)nb * 32 + 2 * b));
+            return __fmul_rn(d, (float)reinterpret_cast<const int8_t*>(row)[i]);
+        }
+        case T_Q4_K: {
+            const int b = i / 256, r = i % 256, g = r / 32, l = r % 32;
+            const uint8_t* blk = row + (size_t)b * 144;
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+            const float dm = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
+            const uint8_t* s = blk + 4;
+            int sc, m;
+            if (g < 4) { sc = s[g] & 63; m = s[g + 4] & 63; }
+            else { sc = (s[g + 4] & 0x0F) | ((s[g - 4] >> 6) << 4); m = (s[g + 4] >> 4) | ((s[g] >> 6) << 4); }
+            const uint8_t qb = blk[16 + 32 * (g >> 1) + l];
+            const int q = (g & 1) ? (qb >> 4) : (qb & 0x0F);
+            return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dm, (float)m));
+        }
+        case T_Q6_K: {
+            const int nb = n / 256, b = i / 256, r = i % 256, h = r / 128, rr = r % 128, quad = rr / 32, l = rr % 32;
+            const uint8_t* blk = row + (size_t)b * 208;
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (size_t)nb * 208 + 2 * b));
+            const uint8_t qlb = blk[64 * h + l + ((quad & 1) ? 32 : 0)];
+            const int lo = quad < 2 ? (qlb & 0x0F) : (qlb >> 4);
+            const int hi = (blk[128 + 32 * h + l] >> (2 * quad)) & 3;
+            const int q = (lo | (hi << 4)) - 32;
+            const int sc = (int)reinterpret_cast<const int8_t*>(blk + 192)[8 * h + 2 * quad + l / 16];
+            return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+        }
+        default: return 0.0f;
+    }
+}
+
+__global__ void k_embed(int type, const uint8_t* __restrict__ w, size_t stride, int E, const int32_t* __restrict__ ids,
+                        float* __restrict__ x, int ldx) {
+    const int t = blockIdx.x;
+    const uint8_t* row = w + (size_t)ids[t] * stride;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) x[(size_t)t * ldx + i] = dequant_at(type, row, E, i);
+}
+
+__global__ void k_add(float* __restrict__ y, const float* __restrict__ x, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] += x[i];
+}
+
+// First index of the maximum (strict '>' scan, src/model.cpp:1939-1946).
+__global__ void k_argmax(const float* __restrict__ x, int n, int ldx, int32_t* out) {
+    const float* r = x + (size_t)blockIdx.x * ldx;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = r[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+// Router: softmax over NE logits (src/ops.cpp:40-55), top-K by probability
+// (ties: lower expert first), renormalised when `norm` (src/model.cpp:1529-1550).
+__global__ void k_moe_route(const float* __restrict__ logits, int T, int NE, int K, int norm, int32_t* sel,
+                            float* wsel) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float p[256];
+    const float* lg = logits + (size_t)t * NE;
+    float m = lg[0];
+    for (int e = 1; e < NE; ++e) if (lg[e] > m) m = lg[e];
+    float sum = 0.0f;
+    for (int e = 0; e < NE; ++e) { p[e] = expf(lg[e] - m); sum += p[e]; }
+    if (sum <= 0.0f) { for (int e = 0; e < NE; ++e) p[e] = 1.0f / NE; }
+    else { const float inv = 1.0f / sum; for (int e = 0; e < NE; ++e) p[e] *= inv; }
+    unsigned long long used[4] = {0, 0, 0, 0};
+    float wsum = 0.0f;
+    for (int k = 0; k < K; ++k) {
+        int best = -1;
+        for (int e = 0; e < NE; ++e) {
+            if ((used[e >> 6] >> (e & 63)) & 1ull) continue;
+            if (best < 0 || p[e] > p[best]) best = e;
+        }
+        used[best >> 6] |= 1ull << (best & 63);
+        sel[(size_t)t * K + k] = best;
+        wsel[(size_t)t * K + k] = p[best];
+        wsum += p[best];
+    }
+    if (norm && wsum > 0.0f)
+        for (int k = 0; k < K; ++k) wsel[(size_t)t * K + k] /= wsum;
+}
+
+// Per-head RMSNorm in place (qk-norm, src/model.cpp:1714-1721 with
+// src/ops.cpp:18-23). One warp per (token, head).
+__global__ void k_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* __restrict__ w, float eps) {
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (gw >= T * n_heads) return;
+    float* r = x + (size_t)(gw / n_heads) * ldx + (size_t)(gw % n_heads) * D;
+    double s = 0.0;
+    for (int i = lane; i < D; i += 32) s += (double)r[i] * (double)r[i];
+    s = warp_sum_d(s);
+    const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / D), eps)));
+    __syncwarp();
+    for (int i = lane; i < D; i += 32) r[i] = __fmul_rn(__fmul_rn(r[i], sc), w[i]);
+}
+
+// Weighted scatter-add of the routed experts' outputs (src/model.cpp:1571-1578):
+// ffn = sum_k w_k * d_k accumulated from zero, then x += ffn.
+__global__ void k_moe_combine(float* x, int ldx, const float* __restrict__ eo, const float* __restrict__ wsel, int T,
+                              int K, int E) {
+    const int t = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < E; i += gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __fmul_rn(wsel[t * K + k], eo[((size_t)t * K + k) * E + i]));
+        x[(size_t)t * ldx + i] = __fadd_rn(x[(size_t)t * ldx + i], acc);
+    }
+}
+
+// ids[0] = argmax(logits); out[*step] = ids[0]; ++*step; ++tok_pos[0].
+__global__ void k_greedy_advance(const float* __restrict__ x, int n, int32_t* ids, int32_t* tok_pos, int32_t* out,
+                                 int32_t* step) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        if (bi == 0x7fffffff) bi = 0;
+        ids[0] = bi;
+        out[*step] = bi;
+        *step += 1;
+        tok_pos[0] += 1;
+    }
+}
+
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st) {
+    const int warps = T * n_heads;
+    if (warps <= 0) return 0;
+    k_head_rmsnorm<<<(warps + 7) / 8, 256, 0, st>>>(x, ldx, T, n_heads, D, w, eps);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_moe_combine(float* x, int ldx, const float* eo, const float* wsel, int T, int K, int E, cudaStream_t st) {
+    if (T <= 0) return 0;
+    k_moe_combine<<<dim3((E + 255) / 256, T), 256, 0, st>>>(x, ldx, eo, wsel, T, K, E);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_greedy_advance(const float* logits, int V, int32_t* ids, int32_t* tok_pos, int32_t* out,
+                                  int32_t* step, cudaStream_t st) {
+    k_greedy_advance<<<1, 1024, 0, st>>>(logits, V, ids, tok_pos, out, step);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_embed(int type, const uint8_t* w, size_t stride, int E, const int32_t* ids, int T, float* x, int ldx,
+                         cudaStream_t st) {
+    if (T <= 0) return 0;
+    k_embed<<<T, 256, 0, st>>>(type, w, stride, E, ids, x, ldx);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_add(float* y, const float* x, size_t n, cudaStream_t st) {
+    if (!n) return 0;
+    const int ctas = (int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+    k_add<<<ctas, 256, 0, st>>>(y, x, n);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k_argmax<<<rows, 1024, 0, st>>>(x, n, ldx, out);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel,
+                             cudaStream_t st) {
+    if (T <= 0) return 0;
+    if (NE > 256 || K > NE) return (int)cudaErrorInvalidValue;
+    k_moe_route<<<(T + 63) / 64, 64, 0, st>>>(logits, T, NE, K, norm, sel, wsel);
+    return (int)cudaGetLastError();
+}

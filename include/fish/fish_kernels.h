@@ -1,0 +1,68 @@
+#pragma once
+/*
+ * Kernel-level entry points of the B200 engine (libfish.so), for parity tests
+ * and for callers that want a single hot-path step without a model.
+ *
+ * Every function takes HOST buffers, runs the same device code the engine's
+ * forward pass runs, and copies the result back. Return 0 on success, a
+ * negative value on bad arguments, or a positive CUDA error code.
+ *
+ * Type ids are ggml's (GGUF specification): 0 F32, 1 F16, 8 Q8_0, 12 Q4_K,
+ * 14 Q6_K. Weight rows are passed in GGUF block order.
+ */
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef FISH_API
+#  define FISH_API __attribute__((visibility("default")))
+#endif
+
+/* Activation quantisers, the reference's records byte for byte:
+ * q8act  = rows x (K/32)  x 40 B  (Q8Act,  reference quant.cpp:400-415)
+ * q8actk = rows x (K/256) x 276 B (Q8ActK, reference quant.cpp:417-434)
+ * Either output may be NULL. Replaces the reference's quantize_acts /
+ * quantize_acts_k (include/fish/quant.h:75-76) and ActBatch::quantize
+ * (include/fish/ops.h:64-81). */
+FISH_API int fbx_quantize_acts(const float* x, int rows, int K, void* q8act, void* q8actk);
+
+/* RMSNorm (reference ops.cpp:18-23) of rows x K, written to out. */
+FISH_API int fbx_rmsnorm(const float* x, const float* w, int rows, int K, float eps, float* out);
+
+/* y[t][r] = W_r . x_t through the int8 (Q8_0/Q4_K/Q6_K) or f32 (F32/F16)
+ * path, activations quantised on the device first. Replaces matmul_batch
+ * (reference include/fish/ops.h:89-91, ops.cpp:177-251). T <= 256. */
+FISH_API int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int T, float* y);
+
+/* Per-(row, block) integer sums of the device integer path on already
+ * quantised activations (q8act for Q8_0, q8actk for K-quants, in the
+ * reference's record layout): Q8_0 s_b, Q4_K sumi_b and mins_b, Q6_K sumi_b
+ * (reference quant_x86.cpp:299-309, 346-382, 431-495). sumi/mins are
+ * n_out x n_blocks; mins may be NULL. */
+FISH_API int fbx_block_sums(int type, const void* w, int n_in, int n_out, const void* acts, int32_t* sumi,
+                            int32_t* mins);
+
+/* Causal GQA attention (reference ops.cpp:303-356) for T queries at
+ * positions pos0.. against K/V caches [n_keys][HKV*D] (n_keys >= pos0+T),
+ * stored into the paged device cache as fp16 (kv_f16=1) or f32. */
+FISH_API int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D,
+                           int pos0, int T, int kv_f16, float* out);
+
+/* RoPE (reference ops.cpp:126-156) on q [T][H*D] and k [T][HKV*D] in place,
+ * token t at position pos0+t, with a table built like rope_build
+ * (ops.cpp:75-124) for freq_base and rot_dim. */
+FISH_API int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_dim, int neox, float freq_base,
+                      int pos0);
+
+/* First index of the maximum per row (reference model.cpp:1939-1946). */
+FISH_API int fbx_argmax(const float* x, int rows, int n, int32_t* out);
+
+/* Embedding row gather + dequantisation (reference dequant_row,
+ * quant.cpp:470-506) for ids[0..T) of a [n_rows][E] table. */
+FISH_API int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out);
+
+#ifdef __cplusplus
+}
+#endif
