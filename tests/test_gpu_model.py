@@ -7,10 +7,12 @@ each test:
   * the reference's engine-vs-engine bar: max |dlogit| <= 2% of max |logit|
     and the same argmax wherever the oracle's top-1/top-2 margin exceeds the
     logit tolerance;
-  * the north-star tolerance |dlogit| <= 1e-2 + 1e-3 |logit| on at least 80%
-    of steps (int8 activation rounding flips, caused by float-order
-    differences of 1 ulp, move a step's logits by up to ~0.02 on these
-    random-init models; the oracle and the reference differ the same way);
+  * the north-star tolerance |dlogit| <= 1e-2 + 1e-3 |logit| for at least 90%
+    of the logits of every step. The bar is per logit, not all-of-them: int8
+    activation rounding flips, set off by 1-ulp float-order differences, move
+    a step's logits by up to ~0.02 on these random-init models. The reference
+    and the C restatement (two CPU engines) show the same floor: 96-99% of
+    logits inside the bar, max ~0.02 (tests/test_oracle_pin.py pins it);
   * integer-exact parts (page tables, greedy ids vs the engine's own
     teacher-forced argmax) must be identical.
 """
@@ -38,14 +40,16 @@ def _margin(logits):
 
 
 def compare_steps(gpu_steps, ref_steps, label):
-    ok_ns = 0
+    """Returns the smallest per-step fraction of logits inside the north-star bar."""
+    worst = 1.0
     for i, (a, b) in enumerate(zip(gpu_steps, ref_steps)):
         d = np.abs(a - b)
         assert d.max() <= 0.02 * np.abs(b).max(), f"{label} step {i}: max diff {d.max():.4f} of {np.abs(b).max():.3f}"
         if _margin(b) > 2 * (1e-2 + 1e-3 * np.abs(b).max()):
             assert int(np.argmax(a)) == int(np.argmax(b)), f"{label} step {i}: argmax differs"
-        ok_ns += int(np.all(d <= 1e-2 + 1e-3 * np.abs(b)))
-    return ok_ns / len(gpu_steps)
+        worst = min(worst, float(np.mean(d <= 1e-2 + 1e-3 * np.abs(b))))
+    print(f"{label}: worst per-step fraction inside 1e-2 abs + 1e-3 rel = {worst:.4f}")
+    return worst
 
 
 def run_teacher_forced(model, ids, n_prompt, n_dec):
@@ -73,7 +77,7 @@ def test_tiny_teacher_forced_vs_oracle(gpu, oracle, tiny_gguf, kv_f32, monkeypat
     om = oracle.load(tiny_gguf, 2048, kv_f16=not kv_f32)
     o = oracle_teacher_forced(om, ids, 128, 24)
     frac = compare_steps(g, o, f"tiny kv_f32={kv_f32}")
-    assert frac >= 0.8, frac
+    assert frac >= 0.9, frac
 
 
 def test_tiny_vs_reference(gpu, reference, tiny_gguf, monkeypatch):
@@ -84,7 +88,7 @@ def test_tiny_vs_reference(gpu, reference, tiny_gguf, monkeypatch):
         g = run_teacher_forced(m, ids, 128, 8)
     rm = reference.load(tiny_gguf, 2048)
     r = [rm.prefill(ids[:128])] + [rm.forward(ids[s:s + 1], s) for s in range(128, 136)]
-    assert compare_steps(g, r, "tiny vs reference") >= 0.8
+    assert compare_steps(g, r, "tiny vs reference") >= 0.9
 
 
 def test_greedy_device_loop_matches_teacher_forced(gpu, tiny_gguf):
@@ -114,7 +118,7 @@ def test_llama8b_shape_two_layers_vs_oracle(gpu, oracle, synth_dir, monkeypatch)
         g = run_teacher_forced(m, ids, 16, 4)
     om = oracle.load(path, 1024)
     o = oracle_teacher_forced(om, ids, 16, 4)
-    assert compare_steps(g, o, "llama8b-2L") >= 0.6
+    assert compare_steps(g, o, "llama8b-2L") >= 0.9
 
 
 def test_qwen_shape_bias_neox_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
@@ -128,7 +132,7 @@ def test_qwen_shape_bias_neox_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
         g = run_teacher_forced(m, ids, 9, 3)
     om = oracle.load(path, 1024)
     o = oracle_teacher_forced(om, ids, 9, 3)
-    assert compare_steps(g, o, "qwen-1L") >= 0.6
+    assert compare_steps(g, o, "qwen-1L") >= 0.9
 
 
 def test_mixtral_shape_moe_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
@@ -142,7 +146,7 @@ def test_mixtral_shape_moe_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
         g = run_teacher_forced(m, ids, 8, 4)
     om = oracle.load(path, 1024)
     o = oracle_teacher_forced(om, ids, 8, 4)
-    assert compare_steps(g, o, "moe-1L") >= 0.6
+    assert compare_steps(g, o, "moe-1L") >= 0.9
 
 
 def test_prefix_cache_hit_through_generate(gpu, tiny_gguf):
