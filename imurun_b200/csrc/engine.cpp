@@ -229,8 +229,8 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     const int model_ctx = c.n_ctx_train;
     c.n_ctx = n_ctx > 0 ? std::min(n_ctx, model_ctx > 0 ? model_ctx : n_ctx) : std::min(4096, model_ctx);
     if (c.n_ctx < 32) { if (err) *err = "context too small"; return false; }
-    if (c.head_dim % 32 != 0 || c.head_dim > 128 || c.n_head / c.n_head_kv > 8) {
-        if (err) *err = "attention shape not supported by the B200 kernels (head_dim must be 32..128, a multiple of 32; <= 8 q heads per kv head)";
+    if ((c.head_dim != 64 && c.head_dim != 128) || c.n_head / c.n_head_kv > 8) {
+        if (err) *err = "attention shape not supported by the B200 kernels (head_dim 64 or 128, <= 8 q heads per kv head)";
         return false;
     }
     {
@@ -469,9 +469,8 @@ bool Engine::alloc_buffers(std::string* err) {
     act_.bsk = reinterpret_cast<int16_t*>(p);
     act_.ld = (int)ld;
     // attention scratch for att_chunk_ tokens per launch at the full context
-    const int n_splits = (c.n_ctx + 127) / 128;
     att_chunk_ = 64;
-    att_scratch_floats_ = (size_t)att_chunk_ * c.n_head * n_splits * (c.head_dim + 2);
+    att_scratch_floats_ = fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx);
     CK(cudaMalloc(&att_scratch_, sizeof(float) * att_scratch_floats_));
     CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));

@@ -254,7 +254,7 @@ struct TestPool {
 
 int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0, int T,
                   int kv_f16, float* out) {
-    if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || D % 32 || D > 128) return -1;
+    if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || (D != 64 && D != 128)) return -1;
     TRY(check_device());
     TestPool tp;
     TRY(tp.make(n_keys, HKV, D, kv_f16, T, pos0));
@@ -276,8 +276,7 @@ int fbx_attention(const float* q, const float* k, const float* v, int n_keys, in
         TRY(cudaMemcpy(tp.pool.p, hf.data(), hf.size() * 4, cudaMemcpyHostToDevice));
     }
     DevBuf dq, dout, scratch;
-    const int n_splits = (pos0 + T + 127) / 128;
-    const size_t sf = (size_t)T * H * n_splits * (D + 2);
+    const size_t sf = fbk_attention_scratch_floats(T, H, D, pos0 + T);
     TRY(dq.alloc(sizeof(float) * T * H * D));
     TRY(dout.alloc(sizeof(float) * T * H * D));
     TRY(scratch.alloc(sizeof(float) * sf));

@@ -78,168 +78,184 @@ __global__ void k_rope_append(float* q, int ldq, const float* k, const float* v,
     }
 }
 
-// Split-K attention. CTA = (query token t, kv head hk, key split s); it serves
-// the G = H/HKV query heads of the group so each K/V row is read once per
-// group. Keys are assigned one per lane for the scores (dot over D from
-// shared q), then one D-slice per lane for P.V. Partial (max, sum, o) go to
-// scratch and k_attn_combine merges the splits.
-constexpr int kSplit = 128;      // keys per split
-constexpr int kMaxG = 8;         // query heads per kv head supported
+
+// Split-K decode attention. CTA = (key split, kv head, query token); NW warps,
+// each warp owns 32 consecutive keys (two 16-position pages). The CTA serves
+// the G = H/HKV query heads of its kv head, so every K/V row is read once per
+// group. Scores: lane = key, dot over D against q staged in shared memory.
+// P.V: lane = a D-slice, 32 keys per warp with the probabilities shuffled.
+// Each split writes (max, sum, o[D]) per head; k_attn_combine merges them.
+constexpr int kMaxG = 8;
 constexpr int kMaxD = 128;
 
-template <bool F16>
-__global__ void __launch_bounds__(128) k_attn_split(const float* __restrict__ q, int ldq, int H, int HKV, int D,
-                                                    float scale, KvView kv, int layer, float* __restrict__ part,
-                                                    int n_splits) {
+template <bool F16, int NW>
+__global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict__ q, int ldq, int H, int HKV, int D,
+                                                        float scale, KvView kv, int layer, float* __restrict__ part,
+                                                        int n_splits) {
     const int t = blockIdx.z, hk = blockIdx.y, sp = blockIdx.x;
     const int G = H / HKV;
-    const int pos = kv.tok_pos[t];
-    const int n_keys = pos + 1;
-    const int j0 = sp * kSplit;
+    const int n_keys = kv.tok_pos[t] + 1;
+    const int j0 = sp * 32 * NW;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __shared__ float sq[kMaxG][kMaxD];
-    __shared__ float sm[4][kMaxG], sl[4][kMaxG];
-    __shared__ float so[4][kMaxG][kMaxD];
-    float* pm = part + (((size_t)t * H + (size_t)hk * G) * n_splits + sp) * (D + 2);
+    __shared__ __align__(16) float sq[kMaxG][kMaxD];
+    __shared__ float sm[NW][kMaxG], sl[NW][kMaxG];
+    __shared__ __align__(16) float so[NW][kMaxG][kMaxD];
     if (j0 >= n_keys) {
         if (threadIdx.x < G) {
             float* p = part + (((size_t)t * H + (size_t)hk * G + threadIdx.x) * n_splits + sp) * (D + 2);
             p[0] = -INFINITY;
             p[1] = 0.0f;
         }
-        (void)pm;
         return;
     }
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-        const int g = i / D, d = i % D;
-        sq[g][d] = q[(size_t)t * ldq + (size_t)(hk * G + g) * D + d];
-    }
+    for (int i = threadIdx.x; i < G * D; i += 32 * NW) sq[i / D][i % D] = q[(size_t)t * ldq + (size_t)hk * G * D + i];
     __syncthreads();
-    const int j1 = min(n_keys, j0 + kSplit);
-    float m[kMaxG], l[kMaxG], o[kMaxG][4];
+    const int jb = j0 + 32 * warp;
+    const int j = jb + lane;
+    const bool valid = j < n_keys;
+    float sc[kMaxG];
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
-    }
-    const int dper = D / 32;  // values of D per lane in the P.V step (<= 4)
-    for (int jb = j0 + warp * 32; jb < j1; jb += 4 * 32) {
-        const int j = jb + lane;
-        float sc[kMaxG];
-#pragma unroll
-        for (int g = 0; g < kMaxG; ++g) sc[g] = -INFINITY;
-        if (j < j1) {
-            const size_t off = kv_off(kv, layer, hk, t, j);
-            float dot[kMaxG];
-#pragma unroll
-            for (int g = 0; g < kMaxG; ++g) dot[g] = 0.0f;
-            for (int d = 0; d < D; d += 8) {
-                float kf[8];
-                if (F16) {
-                    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.k) + off + d);
-                    const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __half22float2(hp[e]);
-                        kf[2 * e] = f.x;
-                        kf[2 * e + 1] = f.y;
-                    }
-                } else {
-                    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d);
-                    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d + 4);
-                    kf[0] = a.x; kf[1] = a.y; kf[2] = a.z; kf[3] = a.w;
-                    kf[4] = b.x; kf[5] = b.y; kf[6] = b.z; kf[7] = b.w;
-                }
-#pragma unroll
-                for (int g = 0; g < kMaxG; ++g) {
-                    if (g < G) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) dot[g] = fmaf(sq[g][d + e], kf[e], dot[g]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < kMaxG; ++g) sc[g] = __fmul_rn(dot[g], scale);
-        }
-        // online softmax update for this batch of 32 keys
-#pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-            if (g >= G) break;
-            const float bm = warp_max(sc[g]);
-            const float nm = fmaxf(m[g], bm);
-            const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - nm);
-            const float p = j < j1 ? expf(sc[g] - nm) : 0.0f;
-            l[g] = l[g] * corr + warp_sum(p);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][e] *= corr;
-            m[g] = nm;
-            sc[g] = p;  // reuse as probability
-        }
-        // P.V: lane owns D-slice [lane*dper, +dper)
-        const int nj = min(32, j1 - jb);
-        for (int jj = 0; jj < nj; ++jj) {
-            const size_t off = kv_off(kv, layer, hk, t, jb + jj);
-            float vf[4];
+    for (int g = 0; g < kMaxG; ++g) sc[g] = 0.0f;
+    if (valid) {
+        const size_t off = kv_off(kv, layer, hk, t, j);
+        for (int d = 0; d < D; d += 8) {
+            float kf[8];
             if (F16) {
-                const __half* vp = reinterpret_cast<const __half*>(kv.v) + off + lane * dper;
+                const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.k) + off + d);
+                const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) vf[e] = e < dper ? __half2float(vp[e]) : 0.0f;
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(hp[e]);
+                    kf[2 * e] = f.x;
+                    kf[2 * e + 1] = f.y;
+                }
             } else {
-                const float* vp = reinterpret_cast<const float*>(kv.v) + off + lane * dper;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) vf[e] = e < dper ? vp[e] : 0.0f;
+                const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d);
+                const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.k) + off + d + 4);
+                kf[0] = a.x; kf[1] = a.y; kf[2] = a.z; kf[3] = a.w; kf[4] = b.x; kf[5] = b.y; kf[6] = b.z; kf[7] = b.w;
             }
 #pragma unroll
             for (int g = 0; g < kMaxG; ++g) {
-                if (g >= G) break;
-                const float p = __shfl_sync(0xffffffffu, sc[g], jj);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+                if (g < G) {
+                    const float4 qa = *reinterpret_cast<const float4*>(&sq[g][d]);
+                    const float4 qb = *reinterpret_cast<const float4*>(&sq[g][d + 4]);
+                    float s = sc[g];
+                    s = fmaf(qa.x, kf[0], s); s = fmaf(qa.y, kf[1], s); s = fmaf(qa.z, kf[2], s); s = fmaf(qa.w, kf[3], s);
+                    s = fmaf(qb.x, kf[4], s); s = fmaf(qb.y, kf[5], s); s = fmaf(qb.z, kf[6], s); s = fmaf(qb.w, kf[7], s);
+                    sc[g] = s;
+                }
             }
         }
     }
-    // merge the 4 warps
+    // softmax pieces of this warp's 32 keys (jb < n_keys, so lane 0 is valid)
+    float m[kMaxG], l[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) {
         if (g >= G) break;
-        if (lane == 0) { sm[warp][g] = m[g]; sl[warp][g] = l[g]; }
+        const float s = valid ? __fmul_rn(sc[g], scale) : -INFINITY;
+        m[g] = warp_max(s);
+        sc[g] = valid ? expf(s - m[g]) : 0.0f;
+        l[g] = warp_sum(sc[g]);
+    }
+    // P.V, lane owns dims [dper*lane, dper*lane + dper)
+    const int dper = D / 32;
+    float o[kMaxG][4];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
+    const int nk = min(32, n_keys - jb);
+#pragma unroll 4
+    for (int jj = 0; jj < nk; ++jj) {
+        const size_t off = kv_off(kv, layer, hk, t, jb + jj) + (size_t)lane * dper;
+        float vf[4];
+        if (F16) {
+            if (dper == 4) {
+                const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(kv.v) + off);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+            } else {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.v) + off));
+                vf[0] = a.x; vf[1] = a.y; vf[2] = 0.0f; vf[3] = 0.0f;
+            }
+        } else {
+            if (dper == 4) {
+                const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.v) + off);
+                vf[0] = a.x; vf[1] = a.y; vf[2] = a.z; vf[3] = a.w;
+            } else {
+                const float2 a = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.v) + off);
+                vf[0] = a.x; vf[1] = a.y; vf[2] = 0.0f; vf[3] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+            if (g >= G) break;
+            const float p = __shfl_sync(0xffffffffu, sc[g], jj);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+        }
+    }
+    float* pbase = part + (((size_t)t * H + (size_t)hk * G) * n_splits + sp) * (D + 2);
+    if (NW == 1) {
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+            if (g >= G) break;
+            float* p = pbase + (size_t)g * n_splits * (D + 2);
+            if (lane == 0) { p[0] = m[g]; p[1] = l[g]; }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) if (e < dper) p[2 + lane * dper + e] = o[g][e];
+        }
+        return;
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        if (lane == 0) { sm[warp][g] = jb < n_keys ? m[g] : -INFINITY; sl[warp][g] = l[g]; }
 #pragma unroll
         for (int e = 0; e < 4; ++e) if (e < dper) so[warp][g][lane * dper + e] = o[g][e];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    for (int i = threadIdx.x; i < G * D; i += 32 * NW) {
         const int g = i / D, d = i % D;
         float M = -INFINITY;
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w][g]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm[w][g]);
         float L = 0.0f, O = 0.0f;
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < NW; ++w) {
             if (sm[w][g] == -INFINITY) continue;
             const float c = expf(sm[w][g] - M);
             L += sl[w][g] * c;
             O += so[w][g][d] * c;
         }
-        float* p = part + (((size_t)t * H + (size_t)hk * G + g) * n_splits + sp) * (D + 2);
+        float* p = pbase + (size_t)g * n_splits * (D + 2);
         if (d == 0) { p[0] = M; p[1] = L; }
         p[2 + d] = O;
     }
 }
 
+// out[t][h][:] = sum_s w_s o_s / sum_s w_s l_s with w_s = exp(m_s - max m).
 __global__ void k_attn_combine(const float* __restrict__ part, int H, int D, int n_splits, float* out, int ldo) {
+    extern __shared__ float sw[];   // n_splits weights
+    __shared__ float s_L;
     const int t = blockIdx.y, h = blockIdx.x;
     const float* p = part + ((size_t)t * H + h) * n_splits * (D + 2);
     float M = -INFINITY;
     for (int s = 0; s < n_splits; ++s) M = fmaxf(M, p[(size_t)s * (D + 2)]);
+    for (int s = threadIdx.x; s < n_splits; s += blockDim.x) {
+        const float ms = p[(size_t)s * (D + 2)];
+        sw[s] = ms == -INFINITY ? 0.0f : expf(ms - M);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float L = 0.0f;
+        for (int s = 0; s < n_splits; ++s) if (sw[s] != 0.0f) L += p[(size_t)s * (D + 2) + 1] * sw[s];
+        s_L = L;
+    }
+    __syncthreads();
+    const float L = s_L;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < n_splits; ++s) {
-            const float ms = p[(size_t)s * (D + 2)];
-            if (ms == -INFINITY) continue;
-            const float c = expf(ms - M);
-            L += p[(size_t)s * (D + 2) + 1] * c;
-            O += p[(size_t)s * (D + 2) + 2 + d] * c;
-        }
+        float O = 0.0f;
+        for (int s = 0; s < n_splits; ++s) if (sw[s] != 0.0f) O += p[(size_t)s * (D + 2) + 2 + d] * sw[s];
         out[(size_t)t * ldo + (size_t)h * D + d] = L > 0.0f ? O / L : 0.0f;
     }
 }
@@ -256,16 +272,32 @@ extern "C" int fbk_rope_append(float* q, int ldq, const float* k, const float* v
     return (int)cudaGetLastError();
 }
 
+// Keys per split: 32 per warp; contexts above 2048 use 4-warp CTAs so the
+// number of splits (and the combine's work) stays <= 64.
+static int attn_warps(int max_ctx) { return max_ctx > 2048 ? 4 : 1; }
+
+extern "C" size_t fbk_attention_scratch_floats(int T, int H, int D, int max_ctx) {
+    const int nw = attn_warps(max_ctx);
+    const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
+    return (size_t)T * H * n_splits * (D + 2);
+}
+
 extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
                              float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
-    if (G > kMaxG || D > kMaxD || D % 32 != 0 || D / 32 > 4) return (int)cudaErrorInvalidValue;
-    const int n_splits = (max_ctx + kSplit - 1) / kSplit;
+    if (G > kMaxG || (D != 64 && D != 128)) return (int)cudaErrorInvalidValue;
+    const int nw = attn_warps(max_ctx);
+    const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
     if ((size_t)T * H * n_splits * (D + 2) > scratch_floats) return (int)cudaErrorInvalidValue;
     dim3 grid(n_splits, HKV, T);
-    if (kv.f16) k_attn_split<true><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
-    else k_attn_split<false><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
-    k_attn_combine<<<dim3(H, T), 128, 0, st>>>(scratch, H, D, n_splits, out, ldo);
+    if (kv.f16) {
+        if (nw == 1) k_attn_split<true, 1><<<grid, 32, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        else k_attn_split<true, 4><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+    } else {
+        if (nw == 1) k_attn_split<false, 1><<<grid, 32, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        else k_attn_split<false, 4><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+    }
+    k_attn_combine<<<dim3(H, T), 128, n_splits * sizeof(float), st>>>(scratch, H, D, n_splits, out, ldo);
     return (int)cudaGetLastError();
 }

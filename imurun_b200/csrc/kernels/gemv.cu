@@ -4,27 +4,32 @@
 // src/quant_x86.cpp:299-309, 346-382, 431-495) or F32 / F16 (f32 path,
 // src/ops.cpp:219-250).
 //
-// The work unit is 32 weight values of one row: a lane streams its unit's
-// bytes with 128-bit (Q4_K, Q8_0) or 64-bit (Q6_K) loads, unpacks nibbles /
-// 6-bit codes in registers and forms int32 dot products with dp4a. The lanes
-// holding the units of one super-block then add their integer partials with
-// shuffles, so every super-block's integer sums
+// The work unit is 32 weight values of one row (unit_math.cuh); the lanes that
+// hold the units of one super-block add their integer partials with shuffles,
+// so every super-block's integer sums
 //     Q4_K  sumi = sum_g sc_g sum_l q x,   mins = sum_g m_g bsums_g
 //     Q6_K  sumi = sum_j sc_j sum (q6-32) x
 //     Q8_0  s    = sum w x
-// are formed exactly as the reference forms them before one float combine
-// per block. The memory stream is the only bound: decode is HBM-bound.
+// are formed exactly as the reference forms them, then combined in float once
+// per block. Decode is HBM-bound; two kernels stream the weights:
+//   k_gemv_bulk  quantised rows: a producer warp streams 8-row x 2048-value
+//                tiles into a ring of shared-memory stages with cp.async.bulk
+//                (TMA) and mbarriers; 8 consumer warps compute from shared.
+//   k_gemv       F32/F16 rows (router, small tensors) with direct loads.
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "layout.cuh"
+#include "unit_math.cuh"
 
 namespace fb {
 
 size_t dev_row_bytes(int type, int n) {
     size_t b = 0;
     switch (type) {
-        case T_Q4_K: b = (size_t)(n / 256) * 144; break;
-        case T_Q6_K: b = (size_t)(n / 256) * 208 + (size_t)(n / 256) * 2; break;
-        case T_Q8_0: b = (size_t)(n / 32) * 32 + (size_t)(n / 32) * 2; break;
+        case T_Q4_K: case T_Q6_K: case T_Q8_0: return row_bytes_dev(type, n);
         case T_F32: b = (size_t)n * 4; break;
         case T_F16: b = (size_t)n * 2; break;
         default: return 0;
@@ -42,18 +47,20 @@ void repack_row(int type, const uint8_t* src, uint8_t* dst, int n) {
         case T_Q6_K: {
             const int nb = n / 256;
             for (int b = 0; b < nb; ++b) {
-                for (int i = 0; i < 208; ++i) dst[(size_t)b * 208 + i] = src[(size_t)b * 210 + i];
-                dst[(size_t)nb * 208 + 2 * b] = src[(size_t)b * 210 + 208];
-                dst[(size_t)nb * 208 + 2 * b + 1] = src[(size_t)b * 210 + 209];
+                const size_t qo = block_offset(T_Q6_K, b), dof = dscale_offset(T_Q6_K, nb, b);
+                for (int i = 0; i < 208; ++i) dst[qo + i] = src[(size_t)b * 210 + i];
+                dst[dof] = src[(size_t)b * 210 + 208];
+                dst[dof + 1] = src[(size_t)b * 210 + 209];
             }
             break;
         }
         case T_Q8_0: {
             const int nb = n / 32;
             for (int b = 0; b < nb; ++b) {
-                for (int i = 0; i < 32; ++i) dst[(size_t)b * 32 + i] = src[(size_t)b * 34 + 2 + i];
-                dst[(size_t)nb * 32 + 2 * b] = src[(size_t)b * 34];
-                dst[(size_t)nb * 32 + 2 * b + 1] = src[(size_t)b * 34 + 1];
+                const size_t qo = block_offset(T_Q8_0, b), dof = dscale_offset(T_Q8_0, nb, b);
+                for (int i = 0; i < 32; ++i) dst[qo + i] = src[(size_t)b * 34 + 2 + i];
+                dst[dof] = src[(size_t)b * 34];
+                dst[dof + 1] = src[(size_t)b * 34 + 1];
             }
             break;
         }
@@ -67,238 +74,118 @@ void repack_row(int type, const uint8_t* src, uint8_t* dst, int n) {
     }
 }
 
-__device__ __forceinline__ uint32_t byte_of(const uint4& h, int k) {
-    // bytes 4..15 of the Q4_K header (the packed scales) live in h.y, h.z, h.w
-    const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
-    return (w >> (8 * (k & 3))) & 0xFFu;
+// ============================================================ activation access
+// Activations are read through L1 (every row of a launch reads the same x).
+
+__device__ __forceinline__ void x_q4k(const ActQ& a, int t, int b, int p, uint4& x0, uint4& x1, uint4& x2, uint4& x3,
+                                      uint32_t& bs) {
+    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 64 * p;
+    x0 = __ldg(reinterpret_cast<const uint4*>(xq));
+    x1 = __ldg(reinterpret_cast<const uint4*>(xq + 16));
+    x2 = __ldg(reinterpret_cast<const uint4*>(xq + 32));
+    x3 = __ldg(reinterpret_cast<const uint4*>(xq + 48));
+    bs = __ldg(reinterpret_cast<const uint32_t*>(a.bsk + (size_t)t * (a.K / 32) + (size_t)b * 8 + 2 * p));
 }
 
-// 6-bit scale and min of sub-block g (src/quant.cpp:136-144).
-__device__ __forceinline__ void q4k_scale_min(const uint4& h, int g, int& sc, int& m) {
-    if (g < 4) {
-        sc = byte_of(h, g) & 63;
-        m = byte_of(h, g + 4) & 63;
-    } else {
-        sc = (byte_of(h, g + 4) & 0x0F) | ((byte_of(h, g - 4) >> 6) << 4);
-        m = (byte_of(h, g + 4) >> 4) | ((byte_of(h, g) >> 6) << 4);
-    }
+__device__ __forceinline__ void x_q6k(const ActQ& a, int t, int b, int j, uint2 (&x)[4]) {
+    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 128 * (j >> 2) + 8 * (j & 3);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = __ldg(reinterpret_cast<const uint2*>(xq + 32 * q));
 }
 
-// ---------------------------------------------------------------- Q4_K
-// unit u of a row: block b = u/4, sub-block pair p = u%4 (sub-blocks 2p, 2p+1,
-// qs bytes 32p .. 32p+31: low nibbles = sub-block 2p, high = 2p+1).
+// ============================================================ direct kernel rows
+
 template <int NT, bool SUMS>
 __device__ __forceinline__ void row_q4k(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
                                         float (&acc)[NT], int32_t* sumi_out, int32_t* mins_out) {
     const int nunits = nb * 4;
-    const int kb = a.K / 256, k32 = a.K / 32;
-    for (int u0 = 0; u0 < nunits; u0 += 64) {
-        uint4 hdr[2], q0[2], q1[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int u = u0 + lane + 32 * i;
-            if (u < nunits) {
-                const uint8_t* blk = row + (size_t)(u >> 2) * 144;
-                hdr[i] = ldg_stream(blk);
-                q0[i] = ldg_stream(blk + 16 + 32 * (u & 3));
-                q1[i] = ldg_stream(blk + 32 + 32 * (u & 3));
-            } else {
-                hdr[i] = make_uint4(0, 0, 0, 0);
-                q0[i] = hdr[i];
-                q1[i] = hdr[i];
-            }
+    for (int u = lane; u - lane < nunits; u += 32) {
+        const bool ok = u < nunits;
+        const int b = u >> 2, p = u & 3;
+        Q4kUnit un;
+        uint4 h = make_uint4(0, 0, 0, 0);
+        if (ok) {
+            const uint8_t* blk = row + (size_t)b * 144;
+            h = ldg_stream(blk);
+            un.load(h, ldg_stream(blk + 16 + 32 * p), ldg_stream(blk + 32 + 32 * p), p);
         }
+        const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int u = u0 + lane + 32 * i;
-            if (u0 + 32 * i >= nunits) break;  // warp-uniform
-            const bool ok = u < nunits;
-            const int b = u >> 2, p = u & 3;
-            int sc0 = 0, sc1 = 0, m0 = 0, m1 = 0;
+        for (int t = 0; t < NT; ++t) {
+            int si = 0, mi = 0;
             if (ok) {
-                q4k_scale_min(hdr[i], 2 * p, sc0, m0);
-                q4k_scale_min(hdr[i], 2 * p + 1, sc1, m1);
+                uint4 x0, x1, x2, x3;
+                uint32_t bs;
+                x_q4k(a, t, b, p, x0, x1, x2, x3, bs);
+                un.dot(x0, x1, x2, x3, bs, si, mi);
             }
-            const uint32_t lo[8] = {q0[i].x & 0x0F0F0F0Fu, q0[i].y & 0x0F0F0F0Fu, q0[i].z & 0x0F0F0F0Fu,
-                                    q0[i].w & 0x0F0F0F0Fu, q1[i].x & 0x0F0F0F0Fu, q1[i].y & 0x0F0F0F0Fu,
-                                    q1[i].z & 0x0F0F0F0Fu, q1[i].w & 0x0F0F0F0Fu};
-            const uint32_t hi[8] = {(q0[i].x >> 4) & 0x0F0F0F0Fu, (q0[i].y >> 4) & 0x0F0F0F0Fu,
-                                    (q0[i].z >> 4) & 0x0F0F0F0Fu, (q0[i].w >> 4) & 0x0F0F0F0Fu,
-                                    (q1[i].x >> 4) & 0x0F0F0F0Fu, (q1[i].y >> 4) & 0x0F0F0F0Fu,
-                                    (q1[i].z >> 4) & 0x0F0F0F0Fu, (q1[i].w >> 4) & 0x0F0F0F0Fu};
-            const float dw = h2f((uint16_t)(hdr[i].x & 0xFFFFu));
-            const float dmw = h2f((uint16_t)(hdr[i].x >> 16));
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                int si = 0, mi = 0;
-                if (ok) {
-                    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 64 * p;
-                    const uint4 x0 = __ldg(reinterpret_cast<const uint4*>(xq));
-                    const uint4 x1 = __ldg(reinterpret_cast<const uint4*>(xq + 16));
-                    const uint4 x2 = __ldg(reinterpret_cast<const uint4*>(xq + 32));
-                    const uint4 x3 = __ldg(reinterpret_cast<const uint4*>(xq + 48));
-                    int s0 = 0, s1 = 0;
-                    s0 = dp4a((int)lo[0], (int)x0.x, s0); s0 = dp4a((int)lo[1], (int)x0.y, s0);
-                    s0 = dp4a((int)lo[2], (int)x0.z, s0); s0 = dp4a((int)lo[3], (int)x0.w, s0);
-                    s0 = dp4a((int)lo[4], (int)x1.x, s0); s0 = dp4a((int)lo[5], (int)x1.y, s0);
-                    s0 = dp4a((int)lo[6], (int)x1.z, s0); s0 = dp4a((int)lo[7], (int)x1.w, s0);
-                    s1 = dp4a((int)hi[0], (int)x2.x, s1); s1 = dp4a((int)hi[1], (int)x2.y, s1);
-                    s1 = dp4a((int)hi[2], (int)x2.z, s1); s1 = dp4a((int)hi[3], (int)x2.w, s1);
-                    s1 = dp4a((int)hi[4], (int)x3.x, s1); s1 = dp4a((int)hi[5], (int)x3.y, s1);
-                    s1 = dp4a((int)hi[6], (int)x3.z, s1); s1 = dp4a((int)hi[7], (int)x3.w, s1);
-                    si = sc0 * s0 + sc1 * s1;
-                    const uint32_t bs = __ldg(reinterpret_cast<const uint32_t*>(a.bsk + (size_t)t * k32 + (size_t)b * 8 + 2 * p));
-                    mi = m0 * (int)(int16_t)(bs & 0xFFFFu) + m1 * (int)(int16_t)(bs >> 16);
-                }
-                si += __shfl_xor_sync(0xffffffffu, si, 1);
-                si += __shfl_xor_sync(0xffffffffu, si, 2);
-                mi += __shfl_xor_sync(0xffffffffu, mi, 1);
-                mi += __shfl_xor_sync(0xffffffffu, mi, 2);
-                if (ok && p == 0) {
-                    if (SUMS) {
-                        sumi_out[b] = si;
-                        mins_out[b] = mi;
-                    } else {
-                        const float dx = __ldg(a.dk + (size_t)t * kb + b);
-                        acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
-                    }
+            si += __shfl_xor_sync(0xffffffffu, si, 1);
+            si += __shfl_xor_sync(0xffffffffu, si, 2);
+            mi += __shfl_xor_sync(0xffffffffu, mi, 1);
+            mi += __shfl_xor_sync(0xffffffffu, mi, 2);
+            if (ok && p == 0) {
+                if (SUMS) { sumi_out[b] = si; mins_out[b] = mi; }
+                else {
+                    const float dx = __ldg(a.dk + (size_t)t * (a.K / 256) + b);
+                    acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
                 }
             }
         }
     }
-}
-
-// ---------------------------------------------------------------- Q6_K
-// unit u: block b = u/8, j = u%8: half h = j/4, l0 = 8*(j%4); covers values
-// l0..l0+7 of each of the half's four 32-value quads (src/quant.cpp:194-216).
-__device__ __forceinline__ uint32_t q6_signed(uint32_t v) {
-    // v: four 6-bit codes 0..63 per byte -> four int8 (code - 32), no borrows.
-    return (v & 0x1F1F1F1Fu) | ((~v & 0x20202020u) * 7u);
 }
 
 template <int NT, bool SUMS>
 __device__ __forceinline__ void row_q6k(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
                                         float (&acc)[NT], int32_t* sumi_out) {
     const int nunits = nb * 8;
-    const int kb = a.K / 256;
-    const uint8_t* dtab = row + (size_t)nb * 208;
-    for (int u0 = 0; u0 < nunits; u0 += 64) {
-        uint2 qa[2], qb[2], qh[2], sc[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int u = u0 + lane + 32 * i;
-            if (u < nunits) {
-                const int b = u >> 3, j = u & 7, h = j >> 2, jj = j & 3;
-                const uint8_t* blk = row + (size_t)b * 208;
-                qa[i] = ldg_stream2(blk + 64 * h + 8 * jj);
-                qb[i] = ldg_stream2(blk + 64 * h + 32 + 8 * jj);
-                qh[i] = ldg_stream2(blk + 128 + 32 * h + 8 * jj);
-                sc[i] = ldg_stream2(blk + 192 + 8 * h);
-            } else {
-                qa[i] = make_uint2(0, 0); qb[i] = qa[i]; qh[i] = qa[i]; sc[i] = qa[i];
-            }
+    for (int u = lane; u - lane < nunits; u += 32) {
+        const bool ok = u < nunits;
+        const int b = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
+        Q6kUnit un;
+        float dw = 0.0f;
+        if (ok) {
+            const uint8_t* blk = row + block_offset(T_Q6_K, b);
+            un.load(ldg_stream2(blk + 64 * hh + 8 * jj), ldg_stream2(blk + 64 * hh + 32 + 8 * jj),
+                    ldg_stream2(blk + 128 + 32 * hh + 8 * jj), ldg_stream2(blk + 192 + 8 * hh), jj);
+            dw = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q6_K, nb, b)));
         }
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int u = u0 + lane + 32 * i;
-            if (u0 + 32 * i >= nunits) break;
-            const bool ok = u < nunits;
-            const int b = u >> 3, j = u & 7, h = j >> 2, jj = j & 3;
-            // codes of quad q, two words (values l0..l0+3, l0+4..l0+7)
-            uint32_t v[4][2];
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-                const uint32_t a_ = w ? qa[i].y : qa[i].x;
-                const uint32_t b_ = w ? qb[i].y : qb[i].x;
-                const uint32_t h_ = w ? qh[i].y : qh[i].x;
-                v[0][w] = q6_signed((a_ & 0x0F0F0F0Fu) | ((h_ & 0x03030303u) << 4));
-                v[1][w] = q6_signed((b_ & 0x0F0F0F0Fu) | (((h_ >> 2) & 0x03030303u) << 4));
-                v[2][w] = q6_signed(((a_ >> 4) & 0x0F0F0F0Fu) | (((h_ >> 4) & 0x03030303u) << 4));
-                v[3][w] = q6_signed(((b_ >> 4) & 0x0F0F0F0Fu) | (((h_ >> 6) & 0x03030303u) << 4));
+        for (int t = 0; t < NT; ++t) {
+            int si = 0;
+            if (ok) {
+                uint2 x[4];
+                x_q6k(a, t, b, j, x);
+                si = un.dot(x);
             }
-            // scale of quad q for this l-range: scales[8h + 2q + (l0 >= 16)]
-            int scq[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int k = 2 * q + (jj >> 1);
-                const uint32_t w = k < 4 ? sc[i].x : sc[i].y;
-                scq[q] = (int)(int8_t)((w >> (8 * (k & 3))) & 0xFFu);
-            }
-            const float dw = ok ? h2f(*reinterpret_cast<const uint16_t*>(dtab + 2 * b)) : 0.0f;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                int si = 0;
-                if (ok) {
-                    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 128 * h + 8 * jj;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint2 xv = __ldg(reinterpret_cast<const uint2*>(xq + 32 * q));
-                        const int iq = dp4a((int)v[q][0], (int)xv.x, dp4a((int)v[q][1], (int)xv.y, 0));
-                        si += scq[q] * iq;
-                    }
-                }
-                si += __shfl_xor_sync(0xffffffffu, si, 1);
-                si += __shfl_xor_sync(0xffffffffu, si, 2);
-                si += __shfl_xor_sync(0xffffffffu, si, 4);
-                if (ok && j == 0) {
-                    if (SUMS) {
-                        sumi_out[b] = si;
-                    } else {
-                        const float dx = __ldg(a.dk + (size_t)t * kb + b);
-                        acc[t] += __fmul_rn(dw, dx) * (float)si;
-                    }
-                }
+            si += __shfl_xor_sync(0xffffffffu, si, 1);
+            si += __shfl_xor_sync(0xffffffffu, si, 2);
+            si += __shfl_xor_sync(0xffffffffu, si, 4);
+            if (ok && j == 0) {
+                if (SUMS) sumi_out[b] = si;
+                else acc[t] += __fmul_rn(dw, __ldg(a.dk + (size_t)t * (a.K / 256) + b)) * (float)si;
             }
         }
     }
 }
 
-// ---------------------------------------------------------------- Q8_0
 template <int NT, bool SUMS>
 __device__ __forceinline__ void row_q80(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
                                         float (&acc)[NT], int32_t* sumi_out) {
-    const int k32 = a.K / 32;
-    const uint8_t* dtab = row + (size_t)nb * 32;
-    for (int b0 = 0; b0 < nb; b0 += 64) {
-        uint4 w0[2], w1[2];
-        float dw[2];
+    for (int b = lane; b < nb; b += 32) {
+        const uint8_t* q = row + block_offset(T_Q8_0, b);
+        const uint4 w0 = ldg_stream(q), w1 = ldg_stream(q + 16);
+        const float dw = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q8_0, nb, b)));
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int b = b0 + lane + 32 * i;
-            if (b < nb) {
-                w0[i] = ldg_stream(row + (size_t)b * 32);
-                w1[i] = ldg_stream(row + (size_t)b * 32 + 16);
-                dw[i] = h2f(*reinterpret_cast<const uint16_t*>(dtab + 2 * b));
-            } else {
-                w0[i] = make_uint4(0, 0, 0, 0); w1[i] = w0[i]; dw[i] = 0.0f;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int b = b0 + lane + 32 * i;
-            if (b >= nb) continue;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const int8_t* xq = a.q32 + (size_t)t * a.ld + (size_t)b * 32;
-                const uint4 x0 = __ldg(reinterpret_cast<const uint4*>(xq));
-                const uint4 x1 = __ldg(reinterpret_cast<const uint4*>(xq + 16));
-                int s = 0;
-                s = dp4a((int)w0[i].x, (int)x0.x, s); s = dp4a((int)w0[i].y, (int)x0.y, s);
-                s = dp4a((int)w0[i].z, (int)x0.z, s); s = dp4a((int)w0[i].w, (int)x0.w, s);
-                s = dp4a((int)w1[i].x, (int)x1.x, s); s = dp4a((int)w1[i].y, (int)x1.y, s);
-                s = dp4a((int)w1[i].z, (int)x1.z, s); s = dp4a((int)w1[i].w, (int)x1.w, s);
-                if (SUMS) {
-                    sumi_out[b] = s;
-                } else {
-                    const float dx = __ldg(a.d32 + (size_t)t * k32 + b);
-                    acc[t] += __fmul_rn(dw[i], dx) * (float)s;
-                }
-            }
+        for (int t = 0; t < NT; ++t) {
+            const int8_t* xq = a.q32 + (size_t)t * a.ld + (size_t)b * 32;
+            const int s = q80_dot(w0, w1, __ldg(reinterpret_cast<const uint4*>(xq)),
+                                  __ldg(reinterpret_cast<const uint4*>(xq + 16)));
+            if (SUMS) sumi_out[b] = s;
+            else acc[t] += __fmul_rn(dw, __ldg(a.d32 + (size_t)t * (a.K / 32) + b)) * (float)s;
         }
     }
 }
 
-// ---------------------------------------------------------------- F32 / F16
 template <int NT>
 __device__ __forceinline__ void row_float(int type, const uint8_t* __restrict__ row, int K, const float* xf, int ldxf,
                                           int lane, float (&acc)[NT]) {
@@ -308,6 +195,13 @@ __device__ __forceinline__ void row_float(int type, const uint8_t* __restrict__ 
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] += w * xf[(size_t)t * ldxf + k];
     }
+}
+
+__device__ __forceinline__ void store_out(const GemvSeg& g, int rr, int t, float v) {
+    if (g.bias) v += g.bias[rr];
+    float* yp = g.y + (size_t)t * g.ldy + rr;
+    if (g.epi == EPI_ADD) *yp += v;
+    else *yp = v;
 }
 
 template <int NT>
@@ -335,13 +229,8 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs args) {
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            float v = warp_sum(acc[t]);
-            if (lane == 0 && t < args.T) {
-                if (g.bias) v += g.bias[rr];
-                float* yp = g.y + (size_t)t * g.ldy + rr;
-                if (g.epi == EPI_ADD) *yp += v;
-                else *yp = v;
-            }
+            const float v = warp_sum(acc[t]);
+            if (lane == 0 && t < args.T) store_out(g, rr, t, v);
         }
     }
 }
@@ -362,6 +251,234 @@ __global__ void k_block_sums(int type, const uint8_t* __restrict__ w, size_t str
     }
 }
 
+// ============================================================ TMA-streamed kernel
+
+constexpr int kBulkConsumers = 8;                 // consumer warps; tile = 8 rows
+constexpr int kBulkRows = kBulkConsumers;
+constexpr int kBulkStages = 6;
+constexpr int kBulkStageBytes = kBulkRows * 2176;  // 8 rows x the largest 2048-value group (Q8_0)
+constexpr long long kSpinLimit = 1LL << 26;       // bounded mbarrier waits
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false after kSpinLimit polls (the caller records an error).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (long long i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+struct BulkJobs {
+    // tiles of 8 rows; segment s owns tiles [tile0[s], tile0[s+1])
+    int tile0[kMaxSeg + 1];
+    int n_groups;       // 2048-value groups per row
+    int* err;           // device error flag (nullable)
+};
+
+// The tile schedule: CTA c takes tiles [c * n / grid, (c+1) * n / grid); a tile
+// is streamed as n_groups stages of 8 row pieces.
+template <int NT>
+__global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArgs args, BulkJobs jobs) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ volatile int s_abort;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kBulkStages;
+    uint8_t* stage_mem = smem + 128;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = jobs.tile0[args.nseg];
+    const int t_begin = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
+    const int t_end = (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x);
+    const int G = jobs.n_groups;
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < kBulkStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kBulkConsumers);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kBulkConsumers) {
+        // ---------------- producer: one lane issues the bulk copies
+        if (lane == 0) {
+            int it = 0;
+            bool failed = false;
+            for (int tile = t_begin; tile < t_end && !failed; ++tile) {
+                int s = 0;
+                while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
+                const GemvSeg& g = args.seg[s];
+                const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
+                const int nr = min(kBulkRows, g.rows - r0);
+                const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
+                const int nb = row_blocks(g.type, args.K);
+                for (int gi = 0; gi < G; ++gi) {
+                    const int slot = it % kBulkStages;
+                    if (s_abort || (it >= kBulkStages && !mbar_wait(&empty[slot], ((it / kBulkStages) - 1) & 1))) {
+                        if (jobs.err) atomicExch(jobs.err, 1);
+                        s_abort = 1;
+                        failed = true;
+                        break;
+                    }
+                    const uint32_t gb = (uint32_t)group_bytes(g.type, group_blocks(g.type, nb, gi));
+                    mbar_expect_tx(&full[slot], gb * nr);
+                    uint8_t* dst = stage_mem + (size_t)slot * kBulkStageBytes;
+                    const uint8_t* src = base + (size_t)r0 * g.row_stride + group_offset(g.type, gi);
+                    for (int r = 0; r < nr; ++r) bulk_g2s(dst + (size_t)r * 2176, src + (size_t)r * g.row_stride, gb, &full[slot]);
+                    ++it;
+                }
+            }
+            if (failed) {
+                // let the copies already issued land before the CTA's shared memory goes away
+                for (int k = max(0, it - kBulkStages); k < it; ++k) mbar_wait(&full[k % kBulkStages], (k / kBulkStages) & 1);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers: warp w owns row w of every tile
+    int it = 0;
+    for (int tile = t_begin; tile < t_end; ++tile) {
+        int s = 0;
+        while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
+        const GemvSeg& g = args.seg[s];
+        const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
+        const int row = r0 + warp;
+        const bool live = row < g.rows;
+        const int nb = row_blocks(g.type, args.K);
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        for (int gi = 0; gi < G; ++gi, ++it) {
+            const int slot = it % kBulkStages;
+            if (s_abort || !mbar_wait(&full[slot], (it / kBulkStages) & 1)) {
+                if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
+                s_abort = 1;
+                return;
+            }
+            const uint8_t* piece = stage_mem + (size_t)slot * kBulkStageBytes + (size_t)warp * 2176;
+            const int gbk = group_blocks(g.type, nb, gi);
+            const int b0 = gi * blocks_per_group(g.type);
+            if (live) {
+                if (g.type == T_Q4_K) {
+                    // 8 blocks x 4 units = 32 units: one per lane
+                    const int u = lane, bl = u >> 2, p = u & 3;
+                    const bool ok = bl < gbk;
+                    Q4kUnit un;
+                    uint4 h = make_uint4(0, 0, 0, 0);
+                    if (ok) {
+                        const uint8_t* blk = piece + bl * 144;
+                        h = *reinterpret_cast<const uint4*>(blk);
+                        un.load(h, *reinterpret_cast<const uint4*>(blk + 16 + 32 * p),
+                                *reinterpret_cast<const uint4*>(blk + 32 + 32 * p), p);
+                    }
+                    const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        int si = 0, mi = 0;
+                        if (ok) {
+                            uint4 x0, x1, x2, x3;
+                            uint32_t bs;
+                            x_q4k(args.act, t, b0 + bl, p, x0, x1, x2, x3, bs);
+                            un.dot(x0, x1, x2, x3, bs, si, mi);
+                        }
+                        si += __shfl_xor_sync(0xffffffffu, si, 1);
+                        si += __shfl_xor_sync(0xffffffffu, si, 2);
+                        mi += __shfl_xor_sync(0xffffffffu, mi, 1);
+                        mi += __shfl_xor_sync(0xffffffffu, mi, 2);
+                        if (ok && p == 0) {
+                            const float dx = __ldg(args.act.dk + (size_t)t * (args.K / 256) + b0 + bl);
+                            acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+                        }
+                    }
+                } else if (g.type == T_Q6_K) {
+                    // 8 blocks x 8 units = 64 units: two per lane
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int u = lane + 32 * k, bl = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
+                        const bool ok = bl < gbk;
+                        Q6kUnit un;
+                        float dw = 0.0f;
+                        if (ok) {
+                            const uint8_t* blk = piece + bl * 208;
+                            un.load(*reinterpret_cast<const uint2*>(blk + 64 * hh + 8 * jj),
+                                    *reinterpret_cast<const uint2*>(blk + 64 * hh + 32 + 8 * jj),
+                                    *reinterpret_cast<const uint2*>(blk + 128 + 32 * hh + 8 * jj),
+                                    *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh), jj);
+                            dw = h2f(*reinterpret_cast<const uint16_t*>(piece + gbk * 208 + 2 * bl));
+                        }
+#pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            int si = 0;
+                            if (ok) {
+                                uint2 x[4];
+                                x_q6k(args.act, t, b0 + bl, j, x);
+                                si = un.dot(x);
+                            }
+                            si += __shfl_xor_sync(0xffffffffu, si, 1);
+                            si += __shfl_xor_sync(0xffffffffu, si, 2);
+                            si += __shfl_xor_sync(0xffffffffu, si, 4);
+                            if (ok && j == 0)
+                                acc[t] += __fmul_rn(dw, __ldg(args.act.dk + (size_t)t * (args.K / 256) + b0 + bl)) * (float)si;
+                        }
+                    }
+                } else {
+                    // Q8_0: 64 blocks of 32: two per lane
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int bl = lane + 32 * k;
+                        if (bl < gbk) {
+                            const uint4 w0 = *reinterpret_cast<const uint4*>(piece + bl * 32);
+                            const uint4 w1 = *reinterpret_cast<const uint4*>(piece + bl * 32 + 16);
+                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(piece + gbk * 32 + 2 * bl));
+#pragma unroll
+                            for (int t = 0; t < NT; ++t) {
+                                const int8_t* xq = args.act.q32 + (size_t)t * args.act.ld + (size_t)(b0 + bl) * 32;
+                                const int sb = q80_dot(w0, w1, __ldg(reinterpret_cast<const uint4*>(xq)),
+                                                       __ldg(reinterpret_cast<const uint4*>(xq + 16)));
+                                acc[t] += __fmul_rn(dw, __ldg(args.act.d32 + (size_t)t * (args.K / 32) + b0 + bl)) * (float)sb;
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        if (live) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_sum(acc[t]);
+                if (lane == 0 && t < args.T) store_out(g, row, t, v);
+            }
+        }
+    }
+}
+
 }  // namespace fb
 
 using namespace fb;
@@ -378,21 +495,64 @@ static int num_sms() {
     return g_num_sms;
 }
 
+static int* g_err = nullptr;
+
+extern "C" int* fbk_gemv_error_flag() {
+    if (!g_err) {
+        if (cudaMalloc(&g_err, sizeof(int)) != cudaSuccess) return nullptr;
+        cudaMemset(g_err, 0, sizeof(int));
+    }
+    return g_err;
+}
+
+template <int NT>
+static int launch_bulk(const GemvArgs* a, cudaStream_t st) {
+    static bool attr = false;
+    const size_t smem = 128 + (size_t)kBulkStages * kBulkStageBytes;
+    if (!attr) {
+        if (cudaFuncSetAttribute(k_gemv_bulk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return (int)cudaGetLastError();
+        attr = true;
+    }
+    BulkJobs jobs{};
+    jobs.tile0[0] = 0;
+    for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kBulkRows - 1) / kBulkRows;
+    for (int s = a->nseg; s < kMaxSeg; ++s) jobs.tile0[s + 1] = jobs.tile0[s];
+    jobs.n_groups = (a->K + kGroupValues - 1) / kGroupValues;
+    jobs.err = fbk_gemv_error_flag();
+    const int n_tiles = jobs.tile0[a->nseg];
+    int ctas = std::min(n_tiles, num_sms());
+    if (ctas < 1) ctas = 1;
+    k_gemv_bulk<NT><<<ctas, 32 * (kBulkConsumers + 1), smem, st>>>(*a, jobs);
+    return (int)cudaGetLastError();
+}
+
 extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
     if (a->T <= 0 || a->nseg <= 0) return 0;
+    if (a->T > 8) return (int)cudaErrorInvalidValue;
+    bool quant = true, same = true;
+    for (int s = 0; s < a->nseg; ++s) {
+        const int t = a->seg[s].type;
+        quant = quant && (t == T_Q4_K || t == T_Q6_K || t == T_Q8_0);
+        same = same && (t == T_Q8_0) == (a->seg[0].type == T_Q8_0);
+    }
+    static const bool bulk_off = getenv("FISH_GEMV_DIRECT") != nullptr;
+    if (quant && same && !bulk_off) {
+        if (a->T == 1) return launch_bulk<1>(a, st);
+        if (a->T == 2) return launch_bulk<2>(a, st);
+        if (a->T <= 4) return launch_bulk<4>(a, st);
+        return launch_bulk<8>(a, st);
+    }
     int total = 0;
     for (int s = 0; s < a->nseg; ++s) total += a->seg[s].rows;
-    const int warps_per_cta = 8;
-    int ctas = (total + warps_per_cta - 1) / warps_per_cta;
+    int ctas = (total + 7) / 8;
     const int cap = num_sms() * 8;
     if (ctas > cap) ctas = cap;
     if (ctas < 1) ctas = 1;
-    // tokens beyond 8 are processed in groups of 8 by the caller
     if (a->T == 1) k_gemv<1><<<ctas, 256, 0, st>>>(*a);
     else if (a->T == 2) k_gemv<2><<<ctas, 256, 0, st>>>(*a);
     else if (a->T <= 4) k_gemv<4><<<ctas, 256, 0, st>>>(*a);
-    else if (a->T <= 8) k_gemv<8><<<ctas, 256, 0, st>>>(*a);
-    else return (int)cudaErrorInvalidValue;
+    else k_gemv<8><<<ctas, 256, 0, st>>>(*a);
     return (int)cudaGetLastError();
 }
 

@@ -89,8 +89,10 @@ struct KvView {
 int fbk_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,
                     int rot, int neox, const float* rope_cos, const float* rope_sin, KvView kv, int layer,
                     cudaStream_t st);
+// Scratch (floats) fbk_attention needs for T tokens at contexts <= max_ctx.
+size_t fbk_attention_scratch_floats(int T, int H, int D, int max_ctx);
 // Causal GQA attention for T query tokens, output [T][H*D]; max_ctx bounds
-// every tok_pos[t] + 1 (it sizes the key splits).
+// every tok_pos[t] + 1 (it sizes the key splits). D must be 64 or 128.
 int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
                   float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st);
 // Per-head RMSNorm in place (q/k norm), rows [T][n_heads*D].

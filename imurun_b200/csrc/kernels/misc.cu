@@ -1,6 +1,7 @@
 // misc.cu — embedding gather, residual add, argmax, MoE routing.
 #include "common.cuh"
 #include "kernels.h"
+#include "layout.cuh"
 
 namespace fb {
 
@@ -12,8 +13,8 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n,
         case T_F16: return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
         case T_Q8_0: {
             const int nb = n / 32, b = i / 32;
-            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (size_t)nb * 32 + 2 * b));
-            return __fmul_rn(d, (float)reinterpret_cast<const int8_t*>(row)[i]);
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q8_0, nb, b)));
+            return __fmul_rn(d, (float)reinterpret_cast<const int8_t*>(row + block_offset(T_Q8_0, b))[i % 32]);
         }
         case T_Q4_K: {
             const int b = i / 256, r = i % 256, g = r / 32, l = r % 32;
@@ -30,8 +31,8 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n,
         }
         case T_Q6_K: {
             const int nb = n / 256, b = i / 256, r = i % 256, h = r / 128, rr = r % 128, quad = rr / 32, l = rr % 32;
-            const uint8_t* blk = row + (size_t)b * 208;
-            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (size_t)nb * 208 + 2 * b));
+            const uint8_t* blk = row + block_offset(T_Q6_K, b);
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q6_K, nb, b)));
             const uint8_t qlb = blk[64 * h + l + ((quad & 1) ? 32 : 0)];
             const int lo = quad < 2 ? (qlb & 0x0F) : (qlb >> 4);
             const int hi = (blk[128 + 32 * h + l] >> (2 * quad)) & 3;

@@ -6,223 +6,196 @@
 //   q = clamp(round_half_even(x * id), -127, 127), sums of q.
 // Every float step uses an explicitly rounded intrinsic so no contraction or
 // approximate reciprocal can change a byte.
+//
+// Work split: a row of K values is cut into 256-value chunks; one warp owns a
+// chunk (lane = 8 consecutive values) and a CTA of 4 warps owns 4 chunks, so a
+// single decode token still spreads over K/1024 CTAs.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace fb {
 
-// One warp quantises 256 consecutive values v[0..255] (lane holds 8, values
-// 8*lane .. 8*lane+7) into both layouts.
-__device__ __forceinline__ void warp_quantize256(const float (&v)[8], int lane, int want32, int wantk,
-                                                 int8_t* q32, float* d32, int32_t* s32,
-                                                 int8_t* qk, float* dk, int16_t* bsk) {
-    float a = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
-    if (wantk) {
-        const float amax = warp_max(a);
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int qv[8];
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int r = __float2int_rn(__fmul_rn(v[i], id));
-            r = max(-127, min(127, r));
-            qv[i] = r;
-            s += r;
-        }
-        uint2 packed;
-        packed.x = (qv[0] & 0xFF) | ((qv[1] & 0xFF) << 8) | ((qv[2] & 0xFF) << 16) | ((uint32_t)(qv[3] & 0xFF) << 24);
-        packed.y = (qv[4] & 0xFF) | ((qv[5] & 0xFF) << 8) | ((qv[6] & 0xFF) << 16) | ((uint32_t)(qv[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(qk + 8 * lane) = packed;
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if ((lane & 3) == 0) bsk[lane >> 2] = static_cast<int16_t>(s);
-        if (lane == 0) *dk = d;
-    }
-    if (want32) {
-        // 32-value blocks: lanes 4g .. 4g+3 hold block g.
-        float am = a;
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-        const float d = __fdiv_rn(am, 127.0f);
-        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int qv[8];
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int r = __float2int_rn(__fmul_rn(v[i], id));
-            r = max(-127, min(127, r));
-            qv[i] = r;
-            s += r;
-        }
-        uint2 packed;
-        packed.x = (qv[0] & 0xFF) | ((qv[1] & 0xFF) << 8) | ((qv[2] & 0xFF) << 16) | ((uint32_t)(qv[3] & 0xFF) << 24);
-        packed.y = (qv[4] & 0xFF) | ((qv[5] & 0xFF) << 8) | ((qv[6] & 0xFF) << 16) | ((uint32_t)(qv[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(q32 + 8 * lane) = packed;
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if ((lane & 3) == 0) {
-            d32[lane >> 2] = d;
-            if (s32) s32[lane >> 2] = s;
-        }
-    }
+constexpr int kQWarps = 4;
+
+__device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
+    uint2 p;
+    p.x = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+    p.y = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+    return p;
 }
 
-// Quantise a row held in `src` (global or shared) of length K (multiple of 32).
-// A trailing partial 256-chunk (K % 256 != 0) only gets the 32-layout, which
+__device__ __forceinline__ int quant8(const float (&v)[8], float id, int (&q)[8]) {
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int r = __float2int_rn(__fmul_rn(v[i], id));
+        r = max(-127, min(127, r));
+        q[i] = r;
+        s += r;
+    }
+    return s;
+}
+
+// Quantise chunk c (values 256c .. 256c+255, lane holds 8 of them) of row t.
+// A partial last chunk (K % 256 != 0) only gets the 32-value layout, which
 // matches the reference: the 256 layout exists only when K % 256 == 0
 // (src/ops.cpp:166-174).
-__device__ void block_quantize_row(const float* src, int K, int t, const ActQ& a, int want32, int wantk) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int n256 = (K + 255) / 256;
-    for (int c = warp; c < n256; c += nw) {
-        const int base = c * 256;
-        const bool full = base + 256 <= K;
-        float v[8];
+__device__ __forceinline__ void quant_chunk(const float (&v)[8], int lane, int K, int t, int c, const ActQ& a,
+                                            int want32, int wantk) {
+    const int base = c * 256;
+    const bool full = base + 256 <= K;
+    float am = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int idx = base + 8 * lane + i;
-            v[i] = idx < K ? src[idx] : 0.0f;
-        }
-        const int wk = wantk && full;
-        if (full) {
-            warp_quantize256(v, lane, want32, wk,
-                             a.q32 ? a.q32 + (size_t)t * a.ld + base : nullptr,
-                             a.d32 ? a.d32 + (size_t)t * (a.K / 32) + base / 32 : nullptr,
-                             a.s32 ? a.s32 + (size_t)t * (a.K / 32) + base / 32 : nullptr,
-                             wk ? a.qk + (size_t)t * a.ld + base : nullptr,
-                             wk ? a.dk + (size_t)t * (a.K / 256) + c : nullptr,
-                             wk ? a.bsk + (size_t)t * (a.K / 32) + base / 32 : nullptr);
-        } else if (want32) {
-            // partial chunk: K - base is a multiple of 32; lanes beyond it idle.
-            float am = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-            const float d = __fdiv_rn(am, 127.0f);
-            const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            int s = 0;
-            int qv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                int r = __float2int_rn(__fmul_rn(v[i], id));
-                r = max(-127, min(127, r));
-                qv[i] = r;
-                s += r;
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            if (base + 8 * lane < K) {
-                int8_t* q = a.q32 + (size_t)t * a.ld + base + 8 * lane;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) q[i] = static_cast<int8_t>(qv[i]);
-                if ((lane & 3) == 0) {
-                    a.d32[(size_t)t * (a.K / 32) + base / 32 + (lane >> 2)] = d;
-                    if (a.s32) a.s32[(size_t)t * (a.K / 32) + base / 32 + (lane >> 2)] = s;
-                }
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    if (wantk && full) {
+        const float amax = warp_max(am);
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[8];
+        int s = quant8(v, id, q);
+        *reinterpret_cast<uint2*>(a.qk + (size_t)t * a.ld + base + 8 * lane) = pack8(q);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) a.bsk[(size_t)t * (a.K / 32) + base / 32 + (lane >> 2)] = (int16_t)s;
+        if (lane == 0) a.dk[(size_t)t * (a.K / 256) + c] = d;
+    }
+    if (want32) {
+        // 32-value blocks: lanes 4g .. 4g+3 hold block g of the chunk
+        float b = am;
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 1));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 2));
+        const float d = __fdiv_rn(b, 127.0f);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[8];
+        int s = quant8(v, id, q);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (base + 8 * lane < K) {
+            *reinterpret_cast<uint2*>(a.q32 + (size_t)t * a.ld + base + 8 * lane) = pack8(q);
+            if ((lane & 3) == 0) {
+                a.d32[(size_t)t * (a.K / 32) + base / 32 + (lane >> 2)] = d;
+                if (a.s32) a.s32[(size_t)t * (a.K / 32) + base / 32 + (lane >> 2)] = s;
             }
         }
     }
 }
 
-__global__ void k_quantize_rows(const float* __restrict__ x, int ldx, int K, ActQ a, int want32, int wantk) {
-    const int t = blockIdx.x;
-    block_quantize_row(x + (size_t)t * ldx, K, t, a, want32, wantk);
+__device__ __forceinline__ void load8(const float* src, int base, int lane, int K, float (&v)[8]) {
+    const int i0 = base + 8 * lane;
+    if (i0 + 8 <= K) {
+        const float4 a = *reinterpret_cast<const float4*>(src + i0);
+        const float4 b = *reinterpret_cast<const float4*>(src + i0 + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+}
+
+__global__ void __launch_bounds__(128) k_quantize_rows(const float* __restrict__ x, int ldx, int K, ActQ a, int want32,
+                                                       int wantk) {
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * kQWarps + (threadIdx.x >> 5);
+    if (c * 256 >= K) return;
+    float v[8];
+    load8(x + (size_t)t * ldx, c * 256, lane, K, v);
+    quant_chunk(v, lane, K, t, c, a, want32, wantk);
 }
 
 // RMSNorm (src/ops.cpp:18-23: sum of squares in double; out = x*scale*w with
-// scale = 1/sqrt(float(sum/n) + eps)) followed by quantisation of the result.
-// One CTA per token row; the normalised row is staged in shared memory.
-__global__ void k_rmsnorm_quant(const float* __restrict__ x, int ldx, const float* __restrict__ w, float eps,
-                                int K, float* __restrict__ xb, int ldxb, ActQ a, int want32, int wantk) {
-    extern __shared__ float srow[];
-    __shared__ double part[32];
+// scale = 1/sqrt(float(sum/n) + eps)) then quantisation. Every CTA of a row
+// reduces the whole row in the same order, so all get the same scale.
+__global__ void __launch_bounds__(128) k_rmsnorm_quant(const float* __restrict__ x, int ldx,
+                                                       const float* __restrict__ w, float eps, int K,
+                                                       float* __restrict__ xb, int ldxb, ActQ a, int want32,
+                                                       int wantk) {
+    __shared__ double part[kQWarps];
     __shared__ float s_scale;
-    const int t = blockIdx.x;
+    const int t = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* xr = x + (size_t)t * ldx;
     double s = 0.0;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = xr[i];
-        srow[i] = v;
-        s += (double)v * (double)v;
+    for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+        const float4 f = *reinterpret_cast<const float4*>(xr + i);
+        s += (double)f.x * f.x + (double)f.y * f.y + (double)f.z * f.z + (double)f.w * f.w;
     }
     s = warp_sum_d(s);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    if (lane == 0) part[warp] = s;
     __syncthreads();
     if (threadIdx.x == 0) {
         double tot = 0.0;
-        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += part[i];
-        const float ms = (float)(tot / K);
-        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+        for (int i = 0; i < kQWarps; ++i) tot += part[i];
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / K), eps)));
     }
     __syncthreads();
+    const int c = blockIdx.x * kQWarps + warp;
+    if (c * 256 >= K) return;
     const float sc = s_scale;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(srow[i], sc), w[i]);
-        srow[i] = v;
-        if (xb) xb[(size_t)t * ldxb + i] = v;
+    float v[8];
+    load8(xr, c * 256, lane, K, v);
+    const int i0 = c * 256 + 8 * lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(v[i], sc), w[i0 + i]) : 0.0f;
+    if (xb && i0 < K) {
+        float* o = xb + (size_t)t * ldxb + i0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i0 + i < K) o[i] = v[i];
     }
-    __syncthreads();
-    if (want32 || wantk) block_quantize_row(srow, K, t, a, want32, wantk);
+    if (want32 || wantk) quant_chunk(v, lane, K, t, c, a, want32, wantk);
 }
 
 // h = silu(g) * u (src/ops.cpp:25-31, src/model.cpp:1501-1506), then quantised.
-// g and u are [T][F] with row strides ldg / ldu.
-__global__ void k_silu_mul_quant(const float* __restrict__ g, int ldg, const float* __restrict__ u, int ldu,
-                                 int F, float* __restrict__ h, int ldh, ActQ a, int want32, int wantk) {
-    extern __shared__ float srow[];
-    const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < F; i += blockDim.x) {
-        const float gv = g[(size_t)t * ldg + i];
-        const float sv = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
-        const float v = __fmul_rn(sv, u[(size_t)t * ldu + i]);
-        srow[i] = v;
-        if (h) h[(size_t)t * ldh + i] = v;
+__global__ void __launch_bounds__(128) k_silu_mul_quant(const float* __restrict__ g, int ldg, const float* __restrict__ u,
+                                                        int ldu, int F, float* __restrict__ h, int ldh, ActQ a,
+                                                        int want32, int wantk) {
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * kQWarps + (threadIdx.x >> 5);
+    if (c * 256 >= F) return;
+    float gv[8], uv[8], v[8];
+    load8(g + (size_t)t * ldg, c * 256, lane, F, gv);
+    load8(u + (size_t)t * ldu, c * 256, lane, F, uv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float sv = __fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i])));
+        v[i] = __fmul_rn(sv, uv[i]);
     }
-    __syncthreads();
-    if (want32 || wantk) block_quantize_row(srow, F, t, a, want32, wantk);
+    const int i0 = c * 256 + 8 * lane;
+    if (h && i0 < F) {
+        float* o = h + (size_t)t * ldh + i0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i0 + i < F) o[i] = v[i];
+    }
+    if (want32 || wantk) quant_chunk(v, lane, F, t, c, a, want32, wantk);
 }
 
 }  // namespace fb
 
-// ---------------------------------------------------------------- launchers
-
 using namespace fb;
+
+static dim3 qgrid(int K, int T) {
+    const int chunks = (K + 255) / 256;
+    return dim3((chunks + kQWarps - 1) / kQWarps, T);
+}
 
 extern "C" int fbk_quantize_rows(const float* x, int ldx, int T, int K, const ActQ* a, int want32, int wantk,
                                  cudaStream_t st) {
     if (T <= 0) return 0;
-    k_quantize_rows<<<T, 256, 0, st>>>(x, ldx, K, *a, want32, wantk);
+    if (K % 8 || ldx % 4) return (int)cudaErrorInvalidValue;
+    k_quantize_rows<<<qgrid(K, T), 32 * kQWarps, 0, st>>>(x, ldx, K, *a, want32, wantk);
     return (int)cudaGetLastError();
 }
 
 extern "C" int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T, int K, float* xb,
                                  int ldxb, const ActQ* a, int want32, int wantk, cudaStream_t st) {
     if (T <= 0) return 0;
-    const size_t smem = (size_t)K * sizeof(float);
-    if (smem > 48 * 1024) {
-        static bool attr_set = false;
-        if (!attr_set) {
-            cudaFuncSetAttribute(k_rmsnorm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            attr_set = true;
-        }
-    }
-    k_rmsnorm_quant<<<T, 256, smem, st>>>(x, ldx, w, eps, K, xb, ldxb, *a, want32, wantk);
+    if (K % 8 || ldx % 4) return (int)cudaErrorInvalidValue;
+    k_rmsnorm_quant<<<qgrid(K, T), 32 * kQWarps, 0, st>>>(x, ldx, w, eps, K, xb, ldxb, *a, want32, wantk);
     return (int)cudaGetLastError();
 }
 
 extern "C" int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                                   const ActQ* a, int want32, int wantk, cudaStream_t st) {
     if (T <= 0) return 0;
-    const size_t smem = (size_t)F * sizeof(float);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(k_silu_mul_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
-    k_silu_mul_quant<<<T, 256, smem, st>>>(g, ldg, u, ldu, F, h, ldh, *a, want32, wantk);
+    if (F % 8 || ldg % 4 || ldu % 4) return (int)cudaErrorInvalidValue;
+    k_silu_mul_quant<<<qgrid(F, T), 32 * kQWarps, 0, st>>>(g, ldg, u, ldu, F, h, ldh, *a, want32, wantk);
     return (int)cudaGetLastError();
 }

@@ -133,6 +133,26 @@ def test_engine_noise_floor_between_cpu_engines(oracle, reference, tiny_gguf):
         assert np.mean(d <= 1e-2 + 1e-3 * np.abs(x)) >= 0.95
 
 
+def test_engine_noise_floor_llama8b_two_layers(oracle, reference, synth_dir):
+    """Same measurement at the Llama-3-8B widths (2 layers, Q4_K_M mixture):
+    the floor is much wider (the residual stream of a random-init model is
+    small, so the final RMSNorm amplifies flips): per step 25-60% of logits
+    inside the bar, max |dlogit| <= 3% of max |logit|, median <= 0.03."""
+    from imurun_b200 import synth
+    path = synth.cached(synth.preset("llama8b", layers=2), synth_dir)
+    ids = np.random.default_rng(8).integers(3, 128256, 20).astype(np.int32)
+    rm, om = reference.load(path, 1024), oracle.load(path, 1024)
+    a = [rm.forward(ids[:16], 0)] + [rm.forward(ids[s:s + 1], s) for s in range(16, 20)]
+    b = [om.forward(ids[:16], 0)] + [om.forward(ids[s:s + 1], s) for s in range(16, 20)]
+    fr = []
+    for x, y in zip(a, b):
+        d = np.abs(x - y)
+        assert d.max() <= 0.03 * np.abs(x).max()
+        assert np.median(d) <= 0.03
+        fr.append(np.mean(d <= 1e-2 + 1e-3 * np.abs(x)))
+    assert 0.25 <= min(fr) and max(fr) <= 0.6
+
+
 @pytest.mark.parametrize("n_tok", [1, 5])
 def test_live_reference_attention(oracle, reference, n_tok):
     rng = np.random.default_rng(n_tok)
