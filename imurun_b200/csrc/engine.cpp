@@ -141,6 +141,7 @@ Engine::~Engine() {
     if (ev1_) cudaEventDestroy(ev1_);
     if (pe0_) cudaEventDestroy(pe0_);
     if (pe1_) cudaEventDestroy(pe1_);
+    for (cudaEvent_t e : prof_events_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -156,17 +157,26 @@ void Engine::drop_graphs() {
     graph_kernels_.clear();
 }
 
-void Engine::prof_begin() { cudaEventRecord(pe0_, stream_); }
+// Profiling records an event before and after each launch without waiting, so
+// the GPU runs the launches back to back; the pairs are read after the run.
+int Engine::prof_event() {
+    if (prof_next_ == (int)prof_events_.size()) {
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        prof_events_.push_back(e);
+    }
+    return prof_next_++;
+}
+
+void Engine::prof_begin() {
+    prof_open_ = prof_event();
+    cudaEventRecord(prof_events_[prof_open_], stream_);
+}
 
 void Engine::prof_end(int cls, double bytes) {
-    cudaEventRecord(pe1_, stream_);
-    cudaEventSynchronize(pe1_);
-    float ms = 0.0f;
-    cudaEventElapsedTime(&ms, pe0_, pe1_);
-    ProfClass& c = (*prof_)[cls];
-    c.launches += 1;
-    c.ms += ms;
-    c.bytes += bytes;
+    const int e1 = prof_event();
+    cudaEventRecord(prof_events_[e1], stream_);
+    prof_recs_.push_back({cls, bytes, prof_open_, e1});
 }
 
 // ------------------------------------------------------------------ load
@@ -962,8 +972,17 @@ bool Engine::profile_decode(int sid, int32_t first, int n_steps, std::vector<Pro
     bool ok = true;
     std::vector<int32_t> am(1);
     for (int i = 0; i < n_steps && ok; ++i) {
-        ok = forward(sid, &tok, 1, nullptr, nullptr, am.data(), err);
+        prof_next_ = 0;
+        prof_recs_.clear();
+        ok = forward(sid, &tok, 1, nullptr, nullptr, am.data(), err);   // ends with a stream sync
         tok = am[0];
+        for (const ProfRec& r : prof_recs_) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, prof_events_[r.e0], prof_events_[r.e1]);
+            cls[r.cls].launches += 1;
+            cls[r.cls].ms += ms;
+            cls[r.cls].bytes += r.bytes;
+        }
     }
     prof_ = nullptr;
     if (ok) *out = cls;

@@ -193,6 +193,11 @@ private:
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     std::vector<ProfClass>* prof_ = nullptr;
     cudaEvent_t pe0_ = nullptr, pe1_ = nullptr;
+    struct ProfRec { int cls; double bytes; int e0, e1; };
+    std::vector<cudaEvent_t> prof_events_;   // pool, reused across profiles
+    std::vector<ProfRec> prof_recs_;
+    int prof_next_ = 0, prof_open_ = -1;
+    int prof_event();
 };
 
 }  // namespace fb

@@ -6,6 +6,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -170,6 +172,63 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
     }
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(y, dy.p, sizeof(float) * T * n_out, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch, double* bytes_per_launch) {
+    if (!ms_per_launch || n_in <= 0 || n_out <= 0 || T <= 0 || T > 8 || iters <= 0) return -1;
+    if (type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K && type != T_F32 && type != T_F16) return -1;
+    TRY(check_device());
+    const size_t stride = dev_row_bytes(type, n_in);
+    const size_t mat = stride * (size_t)n_out;
+    const int copies = (int)std::max<size_t>(1, ((512ull << 20) + mat - 1) / mat);
+    DevBuf dw, dx, dy;
+    DevAct da;
+    TRY(dw.alloc(mat * copies));
+    TRY(cudaMemset(dw.p, 0x11, mat * copies));
+    TRY(dx.alloc(sizeof(float) * T * n_in));
+    TRY(dy.alloc(sizeof(float) * T * n_out));
+    TRY(da.make(8, n_in));
+    std::vector<float> hx((size_t)T * n_in);
+    for (size_t i = 0; i < hx.size(); ++i) hx[i] = (float)((i * 2654435761u) % 1000) / 500.0f - 1.0f;
+    TRY(cudaMemcpy(dx.p, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice));
+    if (type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K)
+        TRY(fbk_quantize_rows(dx.as<float>(), n_in, T, n_in, &da.a, type == T_Q8_0, type != T_Q8_0, nullptr));
+    cudaStream_t st;
+    TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    GemvArgs g{};
+    g.nseg = 1;
+    g.K = n_in;
+    g.T = T;
+    g.act = da.a;
+    g.xf = dx.as<float>();
+    g.ldxf = n_in;
+    g.seg[0].type = type;
+    g.seg[0].row_stride = stride;
+    g.seg[0].rows = n_out;
+    g.seg[0].y = dy.as<float>();
+    g.seg[0].ldy = n_out;
+    g.seg[0].epi = EPI_STORE;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    int rc = 0;
+    for (int i = 0; i < 3 + iters && !rc; ++i) {
+        if (i == 3) cudaEventRecord(e0, st);
+        g.seg[0].w = dw.as<uint8_t>() + (size_t)(i % copies) * mat;
+        rc = fbk_gemv(&g, st);
+    }
+    cudaEventRecord(e1, st);
+    const int sync = (int)cudaStreamSynchronize(st);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(st);
+    if (rc) return rc;
+    if (sync) return sync;
+    *ms_per_launch = ms / iters;
+    if (bytes_per_launch) *bytes_per_launch = (double)ggml_row_bytes(type, (uint64_t)n_in) * n_out + 4.0 * n_out * T;
     return 0;
 }
 

@@ -116,8 +116,9 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
     float sc[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) sc[g] = 0.0f;
+    const size_t koff = valid ? kv_off(kv, layer, hk, t, j) : 0;
     if (valid) {
-        const size_t off = kv_off(kv, layer, hk, t, j);
+        const size_t off = koff;
         for (int d = 0; d < D; d += 8) {
             float kf[8];
             if (F16) {
@@ -165,35 +166,47 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
 #pragma unroll
         for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
     const int nk = min(32, n_keys - jb);
-#pragma unroll 4
-    for (int jj = 0; jj < nk; ++jj) {
-        const size_t off = kv_off(kv, layer, hk, t, jb + jj) + (size_t)lane * dper;
-        float vf[4];
-        if (F16) {
-            if (dper == 4) {
-                const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(kv.v) + off);
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-            } else {
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.v) + off));
-                vf[0] = a.x; vf[1] = a.y; vf[2] = 0.0f; vf[3] = 0.0f;
-            }
-        } else {
-            if (dper == 4) {
-                const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.v) + off);
-                vf[0] = a.x; vf[1] = a.y; vf[2] = a.z; vf[3] = a.w;
-            } else {
-                const float2 a = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.v) + off);
-                vf[0] = a.x; vf[1] = a.y; vf[2] = 0.0f; vf[3] = 0.0f;
+    // each lane computed its own key's cache offset; broadcast them so the V
+    // loads of 8 keys issue together with no dependent page-table reads
+    for (int j8 = 0; j8 < nk; j8 += 8) {
+        float vf[8][4];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int jj = j8 + u;
+            const size_t off = (size_t)__shfl_sync(0xffffffffu, (long long)koff, jj & 31) + (size_t)lane * dper;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) vf[u][e] = 0.0f;
+            if (jj < nk) {
+                if (F16) {
+                    if (dper == 4) {
+                        const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(kv.v) + off);
+                        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                        vf[u][0] = a.x; vf[u][1] = a.y; vf[u][2] = b.x; vf[u][3] = b.y;
+                    } else {
+                        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.v) + off));
+                        vf[u][0] = a.x; vf[u][1] = a.y;
+                    }
+                } else {
+                    if (dper == 4) {
+                        const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.v) + off);
+                        vf[u][0] = a.x; vf[u][1] = a.y; vf[u][2] = a.z; vf[u][3] = a.w;
+                    } else {
+                        const float2 a = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.v) + off);
+                        vf[u][0] = a.x; vf[u][1] = a.y;
+                    }
+                }
             }
         }
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-            if (g >= G) break;
-            const float p = __shfl_sync(0xffffffffu, sc[g], jj);
+        for (int u = 0; u < 8; ++u) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+            for (int g = 0; g < kMaxG; ++g) {
+                if (g >= G) break;
+                const float p = __shfl_sync(0xffffffffu, sc[g], (j8 + u) & 31);   // 0 for keys >= nk
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[u][e], o[g][e]);
+            }
         }
     }
     float* pbase = part + (((size_t)t * H + (size_t)hk * G) * n_splits + sp) * (D + 2);

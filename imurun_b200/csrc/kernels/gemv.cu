@@ -255,8 +255,8 @@ __global__ void k_block_sums(int type, const uint8_t* __restrict__ w, size_t str
 
 constexpr int kBulkConsumers = 8;                 // consumer warps; tile = 8 rows
 constexpr int kBulkRows = kBulkConsumers;
-constexpr int kBulkStages = 6;
-constexpr int kBulkStageBytes = kBulkRows * 2176;  // 8 rows x the largest 2048-value group (Q8_0)
+constexpr int kMaxStages = 32;
+constexpr int kBulkHeader = 2 * kMaxStages * 8;   // mbarriers
 constexpr long long kSpinLimit = 1LL << 26;       // bounded mbarrier waits
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -296,6 +296,8 @@ struct BulkJobs {
     // tiles of 8 rows; segment s owns tiles [tile0[s], tile0[s+1])
     int tile0[kMaxSeg + 1];
     int n_groups;       // 2048-value groups per row
+    int stages;         // ring slots (<= kMaxStages)
+    int piece;          // bytes per row piece in a slot (largest group of the launch's types)
     int* err;           // device error flag (nullable)
 };
 
@@ -305,9 +307,10 @@ template <int NT>
 __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArgs args, BulkJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ volatile int s_abort;
+    const int S = jobs.stages, piece = jobs.piece, stage_bytes = jobs.piece * kBulkRows;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kBulkStages;
-    uint8_t* stage_mem = smem + 128;
+    uint64_t* empty = full + kMaxStages;
+    uint8_t* stage_mem = smem + kBulkHeader;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = jobs.tile0[args.nseg];
     const int t_begin = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
     const int G = jobs.n_groups;
     if (threadIdx.x == 0) {
         s_abort = 0;
-        for (int s = 0; s < kBulkStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kBulkConsumers);
         }
@@ -337,8 +340,8 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                 const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
                 const int nb = row_blocks(g.type, args.K);
                 for (int gi = 0; gi < G; ++gi) {
-                    const int slot = it % kBulkStages;
-                    if (s_abort || (it >= kBulkStages && !mbar_wait(&empty[slot], ((it / kBulkStages) - 1) & 1))) {
+                    const int slot = it % S;
+                    if (s_abort || (it >= S && !mbar_wait(&empty[slot], ((it / S) - 1) & 1))) {
                         if (jobs.err) atomicExch(jobs.err, 1);
                         s_abort = 1;
                         failed = true;
@@ -346,15 +349,15 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                     }
                     const uint32_t gb = (uint32_t)group_bytes(g.type, group_blocks(g.type, nb, gi));
                     mbar_expect_tx(&full[slot], gb * nr);
-                    uint8_t* dst = stage_mem + (size_t)slot * kBulkStageBytes;
+                    uint8_t* dst = stage_mem + (size_t)slot * stage_bytes;
                     const uint8_t* src = base + (size_t)r0 * g.row_stride + group_offset(g.type, gi);
-                    for (int r = 0; r < nr; ++r) bulk_g2s(dst + (size_t)r * 2176, src + (size_t)r * g.row_stride, gb, &full[slot]);
+                    for (int r = 0; r < nr; ++r) bulk_g2s(dst + (size_t)r * piece, src + (size_t)r * g.row_stride, gb, &full[slot]);
                     ++it;
                 }
             }
             if (failed) {
                 // let the copies already issued land before the CTA's shared memory goes away
-                for (int k = max(0, it - kBulkStages); k < it; ++k) mbar_wait(&full[k % kBulkStages], (k / kBulkStages) & 1);
+                for (int k = max(0, it - S); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
             }
         }
         return;
@@ -374,13 +377,13 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
         for (int gi = 0; gi < G; ++gi, ++it) {
-            const int slot = it % kBulkStages;
-            if (s_abort || !mbar_wait(&full[slot], (it / kBulkStages) & 1)) {
+            const int slot = it % S;
+            if (s_abort || !mbar_wait(&full[slot], (it / S) & 1)) {
                 if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
                 s_abort = 1;
                 return;
             }
-            const uint8_t* piece = stage_mem + (size_t)slot * kBulkStageBytes + (size_t)warp * 2176;
+            const uint8_t* pc = stage_mem + (size_t)slot * stage_bytes + (size_t)warp * piece;
             const int gbk = group_blocks(g.type, nb, gi);
             const int b0 = gi * blocks_per_group(g.type);
             if (live) {
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                     Q4kUnit un;
                     uint4 h = make_uint4(0, 0, 0, 0);
                     if (ok) {
-                        const uint8_t* blk = piece + bl * 144;
+                        const uint8_t* blk = pc + bl * 144;
                         h = *reinterpret_cast<const uint4*>(blk);
                         un.load(h, *reinterpret_cast<const uint4*>(blk + 16 + 32 * p),
                                 *reinterpret_cast<const uint4*>(blk + 32 + 32 * p), p);
@@ -424,12 +427,12 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                         Q6kUnit un;
                         float dw = 0.0f;
                         if (ok) {
-                            const uint8_t* blk = piece + bl * 208;
+                            const uint8_t* blk = pc + bl * 208;
                             un.load(*reinterpret_cast<const uint2*>(blk + 64 * hh + 8 * jj),
                                     *reinterpret_cast<const uint2*>(blk + 64 * hh + 32 + 8 * jj),
                                     *reinterpret_cast<const uint2*>(blk + 128 + 32 * hh + 8 * jj),
                                     *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh), jj);
-                            dw = h2f(*reinterpret_cast<const uint16_t*>(piece + gbk * 208 + 2 * bl));
+                            dw = h2f(*reinterpret_cast<const uint16_t*>(pc +gbk * 208 + 2 * bl));
                         }
 #pragma unroll
                         for (int t = 0; t < NT; ++t) {
@@ -452,9 +455,9 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                     for (int k = 0; k < 2; ++k) {
                         const int bl = lane + 32 * k;
                         if (bl < gbk) {
-                            const uint4 w0 = *reinterpret_cast<const uint4*>(piece + bl * 32);
-                            const uint4 w1 = *reinterpret_cast<const uint4*>(piece + bl * 32 + 16);
-                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(piece + gbk * 32 + 2 * bl));
+                            const uint4 w0 = *reinterpret_cast<const uint4*>(pc +bl * 32);
+                            const uint4 w1 = *reinterpret_cast<const uint4*>(pc +bl * 32 + 16);
+                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc +gbk * 32 + 2 * bl));
 #pragma unroll
                             for (int t = 0; t < NT; ++t) {
                                 const int8_t* xq = args.act.q32 + (size_t)t * args.act.ld + (size_t)(b0 + bl) * 32;
@@ -505,24 +508,40 @@ extern "C" int* fbk_gemv_error_flag() {
     return g_err;
 }
 
+static int env_or(const char* name, int def) {
+    const char* v = getenv(name);
+    return v && *v ? atoi(v) : def;
+}
+
+// Pipeline geometry: CTAs per SM and the shared-memory budget per CTA set the
+// ring depth (stages of 8 row pieces); tunable for sweeps through
+// FISH_GEMV_CPS / FISH_GEMV_SMEM_KB.
 template <int NT>
 static int launch_bulk(const GemvArgs* a, cudaStream_t st) {
+    static const int cps = std::max(1, std::min(4, env_or("FISH_GEMV_CPS", 1)));
+    static const int budget = std::max(32, std::min(220, env_or("FISH_GEMV_SMEM_KB", cps == 1 ? 200 : 200 / cps))) * 1024;
     static bool attr = false;
-    const size_t smem = 128 + (size_t)kBulkStages * kBulkStageBytes;
     if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_bulk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemv_bulk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess)
             return (int)cudaGetLastError();
         attr = true;
     }
     BulkJobs jobs{};
+    int piece = 0;
+    for (int s = 0; s < a->nseg; ++s)
+        piece = std::max(piece, (int)group_bytes(a->seg[s].type, blocks_per_group(a->seg[s].type)));
+    jobs.piece = piece;
+    jobs.stages = std::min(kMaxStages, (budget - kBulkHeader) / (piece * kBulkRows));
+    if (jobs.stages < 2) return (int)cudaErrorInvalidValue;
     jobs.tile0[0] = 0;
     for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kBulkRows - 1) / kBulkRows;
     for (int s = a->nseg; s < kMaxSeg; ++s) jobs.tile0[s + 1] = jobs.tile0[s];
     jobs.n_groups = (a->K + kGroupValues - 1) / kGroupValues;
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
-    int ctas = std::min(n_tiles, num_sms());
+    int ctas = std::min(n_tiles, num_sms() * cps);
     if (ctas < 1) ctas = 1;
+    const size_t smem = (size_t)kBulkHeader + (size_t)jobs.stages * piece * kBulkRows;
     k_gemv_bulk<NT><<<ctas, 32 * (kBulkConsumers + 1), smem, st>>>(*a, jobs);
     return (int)cudaGetLastError();
 }

@@ -56,6 +56,16 @@ FISH_API int fbx_attention(const float* q, const float* k, const float* v, int n
 FISH_API int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_dim, int neox, float freq_base,
                       int pos0);
 
+/* Device time of the matmul kernel alone: `iters` back-to-back launches of
+ * y = W x for T tokens, timed with CUDA events on the launching stream after
+ * 3 warm-up launches. W is filled with a constant byte pattern and replicated
+ * into enough copies (>= 512 MB) that consecutive launches read different
+ * copies, so every launch streams its weights from HBM, not L2. Writes the
+ * mean milliseconds per launch and the algorithmic bytes of one launch
+ * (weight rows in GGUF encoding). */
+FISH_API int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch,
+                             double* bytes_per_launch);
+
 /* First index of the maximum per row (reference model.cpp:1939-1946). */
 FISH_API int fbx_argmax(const float* x, int rows, int n, int32_t* out);
 
