@@ -12,10 +12,12 @@
 //     Q8_0  s    = sum w x
 // are formed exactly as the reference forms them, then combined in float once
 // per block. Decode is HBM-bound; two kernels stream the weights:
-//   k_gemv_bulk  quantised rows: a producer warp streams 8-row x 2048-value
-//                tiles into a ring of shared-memory stages with cp.async.bulk
-//                (TMA) and mbarriers; 8 consumer warps compute from shared.
-//   k_gemv       F32/F16 rows (router, small tensors) with direct loads.
+//   k_gemv_stream  quantised rows, T <= 4: a producer warp streams 8-row x
+//                  2048-value pieces into a ring of shared-memory stages with
+//                  cp.async.bulk (TMA) and mbarriers; 8 consumer warps compute
+//                  from shared memory with the activations held in registers.
+//   k_gemv         F32/F16 rows (router, small tensors) and T = 5..8, with
+//                  direct 128-bit loads.
 #include <algorithm>
 #include <cstdlib>
 
@@ -292,29 +294,175 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// Activation chunk of one lane for one 2048-value group, held in registers
+// while every row of the CTA's tiles passes through (the same x serves all
+// rows): Q4_K unit (block lane/4, pair lane%4): 64 int8 + bsums + d;
+// Q6_K units u = lane, lane+32: 2 x 32 int8 + 2 d; Q8_0 blocks lane, lane+32:
+// 2 x 32 int8 + 2 d.
+struct XRegs {
+    uint4 q[4];
+    uint32_t a0, a1;   // Q4_K: bsums pair, d bits | Q6_K/Q8_0: d bits of the two units
+};
+
+__device__ __forceinline__ void load_x(int type, const ActQ& a, int t, int gi, int lane, int nb, XRegs& x) {
+    const int8_t* base = (type == T_Q8_0 ? a.q32 : a.qk) + (size_t)t * a.ld;
+    x.q[0] = x.q[1] = x.q[2] = x.q[3] = make_uint4(0, 0, 0, 0);
+    x.a0 = x.a1 = 0;
+    if (type == T_Q4_K) {
+        const int b = gi * 8 + (lane >> 2), p = lane & 3;
+        if (b < nb) {
+            const int8_t* xq = base + (size_t)b * 256 + 64 * p;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x.q[i] = __ldg(reinterpret_cast<const uint4*>(xq + 16 * i));
+            x.a0 = __ldg(reinterpret_cast<const uint32_t*>(a.bsk + (size_t)t * (a.K / 32) + (size_t)b * 8 + 2 * p));
+            x.a1 = __float_as_uint(__ldg(a.dk + (size_t)t * (a.K / 256) + b));
+        }
+    } else if (type == T_Q6_K) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int u = lane + 32 * k, b = gi * 8 + (u >> 3), j = u & 7;
+            if (b < nb) {
+                const int8_t* xq = base + (size_t)b * 256 + 128 * (j >> 2) + 8 * (j & 3);
+                const uint2 v0 = __ldg(reinterpret_cast<const uint2*>(xq));
+                const uint2 v1 = __ldg(reinterpret_cast<const uint2*>(xq + 32));
+                const uint2 v2 = __ldg(reinterpret_cast<const uint2*>(xq + 64));
+                const uint2 v3 = __ldg(reinterpret_cast<const uint2*>(xq + 96));
+                x.q[2 * k] = make_uint4(v0.x, v0.y, v1.x, v1.y);
+                x.q[2 * k + 1] = make_uint4(v2.x, v2.y, v3.x, v3.y);
+                const uint32_t d = __float_as_uint(__ldg(a.dk + (size_t)t * (a.K / 256) + b));
+                if (k == 0) x.a0 = d; else x.a1 = d;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int b = gi * 64 + lane + 32 * k;
+            if (b < nb) {
+                const int8_t* xq = base + (size_t)b * 32;
+                x.q[2 * k] = __ldg(reinterpret_cast<const uint4*>(xq));
+                x.q[2 * k + 1] = __ldg(reinterpret_cast<const uint4*>(xq + 16));
+                const uint32_t d = __float_as_uint(__ldg(a.d32 + (size_t)t * (a.K / 32) + b));
+                if (k == 0) x.a0 = d; else x.a1 = d;
+            }
+        }
+    }
+}
+
+// Float contribution of one lane for one (row, group) piece in shared memory.
+// Integer sums per super-block are reduced across the lanes that share it
+// (Q4_K: 4 lanes, Q6_K: 8 lanes) before the one float combine per block.
+template <int NT>
+__device__ __forceinline__ void piece_dot(int type, const uint8_t* pc, int gbk, int lane, const XRegs (&x)[NT],
+                                          float (&c)[NT]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) c[t] = 0.0f;
+    if (type == T_Q4_K) {
+        const int bl = lane >> 2, p = lane & 3;
+        const bool ok = bl < gbk;
+        Q4kUnit un;
+        uint4 h = make_uint4(0, 0, 0, 0);
+        if (ok) {
+            const uint8_t* blk = pc + bl * 144;
+            h = *reinterpret_cast<const uint4*>(blk);
+            un.load(h, *reinterpret_cast<const uint4*>(blk + 16 + 32 * p), *reinterpret_cast<const uint4*>(blk + 32 + 32 * p), p);
+        }
+        const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            int si = 0, mi = 0;
+            if (ok) un.dot(x[t].q[0], x[t].q[1], x[t].q[2], x[t].q[3], x[t].a0, si, mi);
+            si += __shfl_xor_sync(0xffffffffu, si, 1);
+            si += __shfl_xor_sync(0xffffffffu, si, 2);
+            mi += __shfl_xor_sync(0xffffffffu, mi, 1);
+            mi += __shfl_xor_sync(0xffffffffu, mi, 2);
+            if (ok && p == 0) {
+                const float dx = __uint_as_float(x[t].a1);
+                c[t] = __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+            }
+        }
+    } else if (type == T_Q6_K) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int u = lane + 32 * k, bl = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
+            const bool ok = bl < gbk;
+            Q6kUnit un;
+            float dw = 0.0f;
+            if (ok) {
+                const uint8_t* blk = pc + bl * 208;
+                un.load(*reinterpret_cast<const uint2*>(blk + 64 * hh + 8 * jj),
+                        *reinterpret_cast<const uint2*>(blk + 64 * hh + 32 + 8 * jj),
+                        *reinterpret_cast<const uint2*>(blk + 128 + 32 * hh + 8 * jj),
+                        *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh), jj);
+                dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 208 + 2 * bl));
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                int si = 0;
+                if (ok) {
+                    const uint4 qa = x[t].q[2 * k], qb = x[t].q[2 * k + 1];
+                    const uint2 xv[4] = {make_uint2(qa.x, qa.y), make_uint2(qa.z, qa.w), make_uint2(qb.x, qb.y),
+                                         make_uint2(qb.z, qb.w)};
+                    si = un.dot(xv);
+                }
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                si += __shfl_xor_sync(0xffffffffu, si, 4);
+                if (ok && j == 0) c[t] += __fmul_rn(dw, __uint_as_float(k ? x[t].a1 : x[t].a0)) * (float)si;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int bl = lane + 32 * k;
+            if (bl < gbk) {
+                const uint4 w0 = *reinterpret_cast<const uint4*>(pc + bl * 32);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(pc + bl * 32 + 16);
+                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 32 + 2 * bl));
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    c[t] += __fmul_rn(dw, __uint_as_float(k ? x[t].a1 : x[t].a0)) *
+                            (float)q80_dot(w0, w1, x[t].q[2 * k], x[t].q[2 * k + 1]);
+            }
+        }
+    }
+}
+
 struct BulkJobs {
     // tiles of 8 rows; segment s owns tiles [tile0[s], tile0[s+1])
     int tile0[kMaxSeg + 1];
     int n_groups;       // 2048-value groups per row
     int stages;         // ring slots (<= kMaxStages)
     int piece;          // bytes per row piece in a slot (largest group of the launch's types)
+    int tiles_per_cta;  // <= kMaxTiles
     int* err;           // device error flag (nullable)
 };
 
-// The tile schedule: CTA c takes tiles [c * n / grid, (c+1) * n / grid); a tile
-// is streamed as n_groups stages of 8 row pieces.
+constexpr int kMaxTiles = 16;   // tiles one CTA accumulates in shared memory (x NT <= 16)
+
+__device__ __forceinline__ int seg_of(const GemvArgs& args, const BulkJobs& jobs, int tile) {
+    int s = 0;
+    while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
+    return s;
+}
+
+// CTA c owns tiles [c*tpc, (c+1)*tpc) and walks them group-major: for every
+// 2048-value group gi, all its tiles' 8-row pieces stream through the ring
+// (stage = one tile x one group), so each lane's activation chunk for gi is
+// loaded once into registers. Per-lane float partials accumulate in shared
+// memory across groups; a warp reduction per row happens once at the end.
 template <int NT>
-__global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArgs args, BulkJobs jobs) {
+__global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvArgs args, BulkJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ volatile int s_abort;
     const int S = jobs.stages, piece = jobs.piece, stage_bytes = jobs.piece * kBulkRows;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
-    uint8_t* stage_mem = smem + kBulkHeader;
+    float* accs = reinterpret_cast<float*>(smem + kBulkHeader);   // [consumer warp][tile][lane][NT]
+    uint8_t* stage_mem = smem + kBulkHeader + (size_t)kBulkConsumers * kMaxTiles * 32 * sizeof(float);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = jobs.tile0[args.nseg];
-    const int t_begin = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
-    const int t_end = (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x);
+    const int t_begin = blockIdx.x * jobs.tiles_per_cta;
+    const int t_end = min(n_tiles, t_begin + jobs.tiles_per_cta);
     const int G = jobs.n_groups;
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -327,19 +475,17 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
     __syncthreads();
 
     if (warp == kBulkConsumers) {
-        // ---------------- producer: one lane issues the bulk copies
         if (lane == 0) {
             int it = 0;
             bool failed = false;
-            for (int tile = t_begin; tile < t_end && !failed; ++tile) {
-                int s = 0;
-                while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
-                const GemvSeg& g = args.seg[s];
-                const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
-                const int nr = min(kBulkRows, g.rows - r0);
-                const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
-                const int nb = row_blocks(g.type, args.K);
-                for (int gi = 0; gi < G; ++gi) {
+            for (int gi = 0; gi < G && !failed; ++gi) {
+                for (int tile = t_begin; tile < t_end; ++tile) {
+                    const int s = seg_of(args, jobs, tile);
+                    const GemvSeg& g = args.seg[s];
+                    const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
+                    const int nr = min(kBulkRows, g.rows - r0);
+                    const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
+                    const int nb = row_blocks(g.type, args.K);
                     const int slot = it % S;
                     if (s_abort || (it >= S && !mbar_wait(&empty[slot], ((it / S) - 1) & 1))) {
                         if (jobs.err) atomicExch(jobs.err, 1);
@@ -355,133 +501,61 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_bulk(GemvArg
                     ++it;
                 }
             }
-            if (failed) {
-                // let the copies already issued land before the CTA's shared memory goes away
+            if (failed)
                 for (int k = max(0, it - S); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
-            }
         }
         return;
     }
 
-    // ---------------- consumers: warp w owns row w of every tile
+    float* myacc = accs + (size_t)warp * kMaxTiles * 32;
+    for (int i = lane; i < kMaxTiles * 32; i += 32) myacc[i] = 0.0f;
     int it = 0;
-    for (int tile = t_begin; tile < t_end; ++tile) {
-        int s = 0;
-        while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
-        const GemvSeg& g = args.seg[s];
-        const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
-        const int row = r0 + warp;
-        const bool live = row < g.rows;
-        const int nb = row_blocks(g.type, args.K);
-        float acc[NT];
+    int cur_type = -1, cur_gi = -1;
+    XRegs x[NT];
+    for (int gi = 0; gi < G; ++gi) {
+        for (int tile = t_begin; tile < t_end; ++tile) {
+            const int s = seg_of(args, jobs, tile);
+            const GemvSeg& g = args.seg[s];
+            const int nb = row_blocks(g.type, args.K);
+            if (g.type != cur_type || gi != cur_gi) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        for (int gi = 0; gi < G; ++gi, ++it) {
+                for (int t = 0; t < NT; ++t) load_x(g.type, args.act, t, gi, lane, nb, x[t]);
+                cur_type = g.type;
+                cur_gi = gi;
+            }
             const int slot = it % S;
             if (s_abort || !mbar_wait(&full[slot], (it / S) & 1)) {
                 if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
                 s_abort = 1;
                 return;
             }
-            const uint8_t* pc = stage_mem + (size_t)slot * stage_bytes + (size_t)warp * piece;
-            const int gbk = group_blocks(g.type, nb, gi);
-            const int b0 = gi * blocks_per_group(g.type);
-            if (live) {
-                if (g.type == T_Q4_K) {
-                    // 8 blocks x 4 units = 32 units: one per lane
-                    const int u = lane, bl = u >> 2, p = u & 3;
-                    const bool ok = bl < gbk;
-                    Q4kUnit un;
-                    uint4 h = make_uint4(0, 0, 0, 0);
-                    if (ok) {
-                        const uint8_t* blk = pc + bl * 144;
-                        h = *reinterpret_cast<const uint4*>(blk);
-                        un.load(h, *reinterpret_cast<const uint4*>(blk + 16 + 32 * p),
-                                *reinterpret_cast<const uint4*>(blk + 32 + 32 * p), p);
-                    }
-                    const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
+            const int row = (tile - jobs.tile0[s]) * kBulkRows + warp;
+            if (row < g.rows) {
+                float c[NT];
+                piece_dot<NT>(g.type, stage_mem + (size_t)slot * stage_bytes + (size_t)warp * piece,
+                              group_blocks(g.type, nb, gi), lane, x, c);
+                // per-lane partial of (local tile, token): slot (tile - t_begin) * NT + t
+                float* a = myacc + (size_t)(tile - t_begin) * NT * 32 + lane;
 #pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        int si = 0, mi = 0;
-                        if (ok) {
-                            uint4 x0, x1, x2, x3;
-                            uint32_t bs;
-                            x_q4k(args.act, t, b0 + bl, p, x0, x1, x2, x3, bs);
-                            un.dot(x0, x1, x2, x3, bs, si, mi);
-                        }
-                        si += __shfl_xor_sync(0xffffffffu, si, 1);
-                        si += __shfl_xor_sync(0xffffffffu, si, 2);
-                        mi += __shfl_xor_sync(0xffffffffu, mi, 1);
-                        mi += __shfl_xor_sync(0xffffffffu, mi, 2);
-                        if (ok && p == 0) {
-                            const float dx = __ldg(args.act.dk + (size_t)t * (args.K / 256) + b0 + bl);
-                            acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
-                        }
-                    }
-                } else if (g.type == T_Q6_K) {
-                    // 8 blocks x 8 units = 64 units: two per lane
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const int u = lane + 32 * k, bl = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
-                        const bool ok = bl < gbk;
-                        Q6kUnit un;
-                        float dw = 0.0f;
-                        if (ok) {
-                            const uint8_t* blk = pc + bl * 208;
-                            un.load(*reinterpret_cast<const uint2*>(blk + 64 * hh + 8 * jj),
-                                    *reinterpret_cast<const uint2*>(blk + 64 * hh + 32 + 8 * jj),
-                                    *reinterpret_cast<const uint2*>(blk + 128 + 32 * hh + 8 * jj),
-                                    *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh), jj);
-                            dw = h2f(*reinterpret_cast<const uint16_t*>(pc +gbk * 208 + 2 * bl));
-                        }
-#pragma unroll
-                        for (int t = 0; t < NT; ++t) {
-                            int si = 0;
-                            if (ok) {
-                                uint2 x[4];
-                                x_q6k(args.act, t, b0 + bl, j, x);
-                                si = un.dot(x);
-                            }
-                            si += __shfl_xor_sync(0xffffffffu, si, 1);
-                            si += __shfl_xor_sync(0xffffffffu, si, 2);
-                            si += __shfl_xor_sync(0xffffffffu, si, 4);
-                            if (ok && j == 0)
-                                acc[t] += __fmul_rn(dw, __ldg(args.act.dk + (size_t)t * (args.K / 256) + b0 + bl)) * (float)si;
-                        }
-                    }
-                } else {
-                    // Q8_0: 64 blocks of 32: two per lane
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        const int bl = lane + 32 * k;
-                        if (bl < gbk) {
-                            const uint4 w0 = *reinterpret_cast<const uint4*>(pc +bl * 32);
-                            const uint4 w1 = *reinterpret_cast<const uint4*>(pc +bl * 32 + 16);
-                            const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc +gbk * 32 + 2 * bl));
-#pragma unroll
-                            for (int t = 0; t < NT; ++t) {
-                                const int8_t* xq = args.act.q32 + (size_t)t * args.act.ld + (size_t)(b0 + bl) * 32;
-                                const int sb = q80_dot(w0, w1, __ldg(reinterpret_cast<const uint4*>(xq)),
-                                                       __ldg(reinterpret_cast<const uint4*>(xq + 16)));
-                                acc[t] += __fmul_rn(dw, __ldg(args.act.d32 + (size_t)t * (args.K / 32) + b0 + bl)) * (float)sb;
-                            }
-                        }
-                    }
-                }
+                for (int t = 0; t < NT; ++t) a[t * 32] += c[t];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            ++it;
         }
-        if (live) {
+    }
+    for (int tile = t_begin; tile < t_end; ++tile) {
+        const int s = seg_of(args, jobs, tile);
+        const GemvSeg& g = args.seg[s];
+        const int row = (tile - jobs.tile0[s]) * kBulkRows + warp;
+        const float* a = myacc + (size_t)(tile - t_begin) * NT * 32 + lane;
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const float v = warp_sum(acc[t]);
-                if (lane == 0 && t < args.T) store_out(g, row, t, v);
-            }
+        for (int t = 0; t < NT; ++t) {
+            const float v = warp_sum(a[t * 32]);
+            if (row < g.rows && lane == 0 && t < args.T) store_out(g, row, t, v);
         }
     }
 }
-
 }  // namespace fb
 
 using namespace fb;
@@ -513,16 +587,17 @@ static int env_or(const char* name, int def) {
     return v && *v ? atoi(v) : def;
 }
 
-// Pipeline geometry: CTAs per SM and the shared-memory budget per CTA set the
-// ring depth (stages of 8 row pieces); tunable for sweeps through
-// FISH_GEMV_CPS / FISH_GEMV_SMEM_KB.
+// Pipeline geometry: the shared-memory budget per CTA (default 100 KB, two
+// CTAs per SM) sets the ring depth; each CTA owns up to 16/NT tiles, and the
+// grid aims at >= 2 CTAs per SM. Tunable for sweeps via FISH_GEMV_SMEM_KB and
+// FISH_GEMV_CTA_PER_SM.
 template <int NT>
-static int launch_bulk(const GemvArgs* a, cudaStream_t st) {
-    static const int cps = std::max(1, std::min(4, env_or("FISH_GEMV_CPS", 1)));
-    static const int budget = std::max(32, std::min(220, env_or("FISH_GEMV_SMEM_KB", cps == 1 ? 200 : 200 / cps))) * 1024;
+static int launch_stream(const GemvArgs* a, cudaStream_t st) {
+    static const int budget = std::max(48, std::min(220, env_or("FISH_GEMV_SMEM_KB", 100))) * 1024;
+    static const int want_cps = std::max(1, std::min(8, env_or("FISH_GEMV_CTA_PER_SM", 2)));
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_bulk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemv_stream<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess)
             return (int)cudaGetLastError();
         attr = true;
     }
@@ -530,8 +605,9 @@ static int launch_bulk(const GemvArgs* a, cudaStream_t st) {
     int piece = 0;
     for (int s = 0; s < a->nseg; ++s)
         piece = std::max(piece, (int)group_bytes(a->seg[s].type, blocks_per_group(a->seg[s].type)));
+    const int acc_bytes = kBulkConsumers * kMaxTiles * 32 * (int)sizeof(float);
     jobs.piece = piece;
-    jobs.stages = std::min(kMaxStages, (budget - kBulkHeader) / (piece * kBulkRows));
+    jobs.stages = std::min(kMaxStages, (budget - kBulkHeader - acc_bytes) / (piece * kBulkRows));
     if (jobs.stages < 2) return (int)cudaErrorInvalidValue;
     jobs.tile0[0] = 0;
     for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kBulkRows - 1) / kBulkRows;
@@ -539,28 +615,27 @@ static int launch_bulk(const GemvArgs* a, cudaStream_t st) {
     jobs.n_groups = (a->K + kGroupValues - 1) / kGroupValues;
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
-    int ctas = std::min(n_tiles, num_sms() * cps);
-    if (ctas < 1) ctas = 1;
-    const size_t smem = (size_t)kBulkHeader + (size_t)jobs.stages * piece * kBulkRows;
-    k_gemv_bulk<NT><<<ctas, 32 * (kBulkConsumers + 1), smem, st>>>(*a, jobs);
+    const int target = num_sms() * want_cps;
+    jobs.tiles_per_cta = std::max(1, std::min(kMaxTiles / NT, (n_tiles + target - 1) / target));
+    const int ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
+    const size_t smem = (size_t)kBulkHeader + acc_bytes + (size_t)jobs.stages * piece * kBulkRows;
+    k_gemv_stream<NT><<<ctas, 32 * (kBulkConsumers + 1), smem, st>>>(*a, jobs);
     return (int)cudaGetLastError();
 }
 
 extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
     if (a->T <= 0 || a->nseg <= 0) return 0;
     if (a->T > 8) return (int)cudaErrorInvalidValue;
-    bool quant = true, same = true;
+    bool quant = true;
     for (int s = 0; s < a->nseg; ++s) {
         const int t = a->seg[s].type;
         quant = quant && (t == T_Q4_K || t == T_Q6_K || t == T_Q8_0);
-        same = same && (t == T_Q8_0) == (a->seg[0].type == T_Q8_0);
     }
-    static const bool bulk_off = getenv("FISH_GEMV_DIRECT") != nullptr;
-    if (quant && same && !bulk_off) {
-        if (a->T == 1) return launch_bulk<1>(a, st);
-        if (a->T == 2) return launch_bulk<2>(a, st);
-        if (a->T <= 4) return launch_bulk<4>(a, st);
-        return launch_bulk<8>(a, st);
+    static const bool stream_off = getenv("FISH_GEMV_DIRECT") != nullptr;
+    if (quant && !stream_off && a->T <= 4) {
+        if (a->T == 1) return launch_stream<1>(a, st);
+        if (a->T == 2) return launch_stream<2>(a, st);
+        return launch_stream<4>(a, st);
     }
     int total = 0;
     for (int s = 0; s < a->nseg; ++s) total += a->seg[s].rows;
