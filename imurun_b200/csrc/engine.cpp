@@ -876,6 +876,9 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
     std::vector<int> sids(T, sid), pos(T);
     for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
     if (!upload_tokens(ids, sids.data(), pos.data(), T, err)) return false;
+    // profiling: hold the stream for 5 ms so every launch of the step is queued
+    // before the first one runs and the event pairs time the kernels alone
+    if (prof_) CK(fbk_delay(5000000ull, stream_));
     const bool all = logits_all != nullptr || argmax != nullptr;
     const int nrows = all ? T : 1;
     if (T == 1 && use_graphs_ && !prof_) {

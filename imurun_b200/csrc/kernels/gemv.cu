@@ -157,7 +157,8 @@ __device__ __forceinline__ void row_q6k(const uint8_t* __restrict__ row, int nb,
             if (ok) {
                 uint2 x[4];
                 x_q6k(a, t, b, j, x);
-                si = un.dot(x);
+                const int xs[4] = {sum8(x[0]), sum8(x[1]), sum8(x[2]), sum8(x[3])};
+                si = un.dot(x, xs);
             }
             si += __shfl_xor_sync(0xffffffffu, si, 1);
             si += __shfl_xor_sync(0xffffffffu, si, 2);
@@ -302,12 +303,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 struct XRegs {
     uint4 q[4];
     uint32_t a0, a1;   // Q4_K: bsums pair, d bits | Q6_K/Q8_0: d bits of the two units
+    int xs[8];         // Q6_K: sums of the 8-value pieces (unit k, quad q at 4k + q)
 };
 
 __device__ __forceinline__ void load_x(int type, const ActQ& a, int t, int gi, int lane, int nb, XRegs& x) {
     const int8_t* base = (type == T_Q8_0 ? a.q32 : a.qk) + (size_t)t * a.ld;
     x.q[0] = x.q[1] = x.q[2] = x.q[3] = make_uint4(0, 0, 0, 0);
     x.a0 = x.a1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x.xs[i] = 0;
     if (type == T_Q4_K) {
         const int b = gi * 8 + (lane >> 2), p = lane & 3;
         if (b < nb) {
@@ -329,6 +333,10 @@ __device__ __forceinline__ void load_x(int type, const ActQ& a, int t, int gi, i
                 const uint2 v3 = __ldg(reinterpret_cast<const uint2*>(xq + 96));
                 x.q[2 * k] = make_uint4(v0.x, v0.y, v1.x, v1.y);
                 x.q[2 * k + 1] = make_uint4(v2.x, v2.y, v3.x, v3.y);
+                x.xs[4 * k + 0] = sum8(v0);
+                x.xs[4 * k + 1] = sum8(v1);
+                x.xs[4 * k + 2] = sum8(v2);
+                x.xs[4 * k + 3] = sum8(v3);
                 const uint32_t d = __float_as_uint(__ldg(a.dk + (size_t)t * (a.K / 256) + b));
                 if (k == 0) x.a0 = d; else x.a1 = d;
             }
@@ -402,7 +410,8 @@ __device__ __forceinline__ void piece_dot(int type, const uint8_t* pc, int gbk, 
                     const uint4 qa = x[t].q[2 * k], qb = x[t].q[2 * k + 1];
                     const uint2 xv[4] = {make_uint2(qa.x, qa.y), make_uint2(qa.z, qa.w), make_uint2(qb.x, qb.y),
                                          make_uint2(qb.z, qb.w)};
-                    si = un.dot(xv);
+                    const int xs[4] = {x[t].xs[4 * k], x[t].xs[4 * k + 1], x[t].xs[4 * k + 2], x[t].xs[4 * k + 3]};
+                    si = un.dot(xv, xs);
                 }
                 si += __shfl_xor_sync(0xffffffffu, si, 1);
                 si += __shfl_xor_sync(0xffffffffu, si, 2);
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
 
     if (warp == kBulkConsumers) {
         if (lane == 0) {
-            int it = 0;
+            int it = 0, slot = 0, round = 0;
             bool failed = false;
             for (int gi = 0; gi < G && !failed; ++gi) {
                 for (int tile = t_begin; tile < t_end; ++tile) {
@@ -486,8 +495,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
                     const int nr = min(kBulkRows, g.rows - r0);
                     const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
                     const int nb = row_blocks(g.type, args.K);
-                    const int slot = it % S;
-                    if (s_abort || (it >= S && !mbar_wait(&empty[slot], ((it / S) - 1) & 1))) {
+                    if (s_abort || (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1))) {
                         if (jobs.err) atomicExch(jobs.err, 1);
                         s_abort = 1;
                         failed = true;
@@ -499,6 +507,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
                     const uint8_t* src = base + (size_t)r0 * g.row_stride + group_offset(g.type, gi);
                     for (int r = 0; r < nr; ++r) bulk_g2s(dst + (size_t)r * piece, src + (size_t)r * g.row_stride, gb, &full[slot]);
                     ++it;
+                    if (++slot == S) { slot = 0; ++round; }
                 }
             }
             if (failed)
@@ -509,7 +518,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
 
     float* myacc = accs + (size_t)warp * kMaxTiles * 32;
     for (int i = lane; i < kMaxTiles * 32; i += 32) myacc[i] = 0.0f;
-    int it = 0;
+    int slot = 0, round = 0;
     int cur_type = -1, cur_gi = -1;
     XRegs x[NT];
     for (int gi = 0; gi < G; ++gi) {
@@ -523,8 +532,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
                 cur_type = g.type;
                 cur_gi = gi;
             }
-            const int slot = it % S;
-            if (s_abort || !mbar_wait(&full[slot], (it / S) & 1)) {
+            if (s_abort || !mbar_wait(&full[slot], round & 1)) {
                 if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
                 s_abort = 1;
                 return;
@@ -541,7 +549,7 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvA
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            ++it;
+            if (++slot == S) { slot = 0; ++round; }
         }
     }
     for (int tile = t_begin; tile < t_end; ++tile) {

@@ -104,6 +104,8 @@ int fbk_moe_combine(float* x, int ldx, const float* eo, const float* wsel, int T
 int fbk_greedy_advance(const float* logits, int V, int32_t* ids, int32_t* tok_pos, int32_t* out, int32_t* step,
                        cudaStream_t st);
 int fbk_add(float* y, const float* x, size_t n, cudaStream_t st);
+// Device-side wait of ns nanoseconds (profiling aid).
+int fbk_delay(unsigned long long ns, cudaStream_t st);
 int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st);
 int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel, cudaStream_t st);
 }

@@ -169,9 +169,27 @@ __global__ void k_greedy_advance(const float* __restrict__ x, int n, int32_t* id
     }
 }
 
+// Busy-wait for `ns` nanoseconds of device time (globaltimer), so a profiler
+// can enqueue a whole step behind it; the loop ends once the time has passed
+// and is additionally capped in iterations.
+__global__ void k_delay(unsigned long long ns) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (long long i = 0; i < (1LL << 30); ++i) {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 >= ns) break;
+        __nanosleep(1000);
+    }
+}
+
 }  // namespace fb
 
 using namespace fb;
+
+extern "C" int fbk_delay(unsigned long long ns, cudaStream_t st) {
+    k_delay<<<1, 1, 0, st>>>(ns);
+    return (int)cudaGetLastError();
+}
 
 extern "C" int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st) {
     const int warps = T * n_heads;
