@@ -66,6 +66,28 @@ FISH_API int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_
 FISH_API int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch,
                              double* bytes_per_launch);
 
+/* Causal GQA attention like fbx_attention, on DEVICE buffers, allocating
+ * nothing. No counterpart in the reference: it serves callers that cannot
+ * allocate device memory on the call path (a serving loop that gave all free
+ * HBM to its KV page pool, code under a caching allocator that must not be
+ * re-entered, a step that must not pay for cudaMalloc/cudaFree, which can
+ * synchronise the device).
+ *   q [T][H*D] f32, out [T][H*D] f32, k and v [n_keys][HKV*D] as fp16
+ *   (kv_f16=1) or f32; every pointer 16-byte aligned; the call is queued on
+ *   `stream` (a cudaStream_t, NULL = default stream) and returns without
+ *   waiting for it.
+ * Its scratch (split partials, positions, an identity page table) is one
+ * fixed __device__ array per device, 8 MiB of partials: pos0+T <= 8192,
+ * T <= 256 and T*H*n_splits*(D+2) <= 2^21 floats, n_splits = ceil((pos0+T)/32)
+ * up to 2048 keys and ceil((pos0+T)/128) above; larger calls return -1.
+ * The first call on a device resolves that array's address and initialises
+ * it (a kernel on `stream`, then a wait for that stream); make it before any
+ * stream capture. Partials need no clearing; every split writes its own. Every call on
+ * a device shares the array, so calls that overlap on the GPU (different
+ * streams, no ordering between them) race and corrupt each other's output. */
+FISH_API int fbx_attention_static(const float* q, const void* k, const void* v, int kv_f16, int n_keys, int H,
+                                  int HKV, int D, int pos0, int T, float* out, void* stream);
+
 /* First index of the maximum per row (reference model.cpp:1939-1946). */
 FISH_API int fbx_argmax(const float* x, int rows, int n, int32_t* out);
 
