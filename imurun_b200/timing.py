@@ -1,0 +1,48 @@
+"""Device timing of single hot-path kernels through the C ABI.
+
+    python -m imurun_b200.timing matmul --type 12 --n-in 4096 --n-out 14336 [--tokens 1] [--iters 20]
+
+Runs fbx_time_matmul: 3 warm-up launches, then `iters` launches timed with
+CUDA events, each launch reading a different copy of the weights (>= 512 MB
+of copies, so every launch streams from HBM). Prints one JSON line with the
+mean launch time, the algorithmic bytes of a launch and their ratio. Also
+the command used for profiler captures of one GEMV launch (`-s 3 -c 1`).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+from . import native
+
+
+def time_matmul(lib, type_id: int, n_in: int, n_out: int, tokens: int = 1, iters: int = 20) -> dict:
+    ms = np.zeros(1, np.float32)
+    nbytes = np.zeros(1, np.float64)
+    rc = lib.fbx_time_matmul(type_id, n_in, n_out, tokens, iters, ms.ctypes.data, nbytes.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"fbx_time_matmul failed: {rc}")
+    us = float(ms[0]) * 1e3
+    return {"type": type_id, "n_in": n_in, "n_out": n_out, "tokens": tokens, "iters": iters,
+            "us_per_launch": round(us, 3), "bytes_per_launch": float(nbytes[0]),
+            "gb_s": round(float(nbytes[0]) / (us * 1e-6) / 1e9, 1)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    mm = sub.add_parser("matmul")
+    mm.add_argument("--type", type=int, required=True, help="ggml type id: 8 Q8_0, 12 Q4_K, 14 Q6_K, 0 F32, 1 F16")
+    mm.add_argument("--n-in", type=int, required=True)
+    mm.add_argument("--n-out", type=int, required=True)
+    mm.add_argument("--tokens", type=int, default=1)
+    mm.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    lib = native.load_library()
+    print(json.dumps(time_matmul(lib, a.type, a.n_in, a.n_out, a.tokens, a.iters)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
