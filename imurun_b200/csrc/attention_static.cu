@@ -104,6 +104,8 @@ extern "C" FISH_API int fbx_attention_static(const float* q, const void* k, cons
     kv.layer_stride = 0;
     kv.head_stride = (size_t)D;
     kv.f16 = kv_f16 ? 1 : 0;
+    kv.n_pages = kStaticMaxKeys;
+    kv.err = nullptr;
     return fbk_attention(q, H * D, T, H, HKV, D, 1.0f / sqrtf((float)D), kv, 0, out, H * D, s->partials,
                          kStaticPartialFloats, max_ctx, st);
 }

@@ -663,10 +663,10 @@ const char* fish_engine_json(fish_ctx* ctx) {
     std::snprintf(b, sizeof(b),
                   "{\"device\":\"%s\",\"kv_page_size\":%d,\"kv_free_pages\":%d,\"kv_bytes\":%llu,"
                   "\"weights_device_bytes\":%llu,\"greedy_graph_kernels\":%d,\"step_graph_kernels\":%d,"
-                  "\"last_decode_device_ms\":%.6f}",
+                  "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d}",
                   e.device_name().c_str(), e.page_size(), e.free_pages(), (unsigned long long)e.kv_bytes(),
                   (unsigned long long)e.device_weight_bytes(), e.graph_kernels(0), e.graph_kernels(1),
-                  (double)e.last_greedy_ms());
+                  (double)e.last_greedy_ms(), fbk_take_error_flag());
     buf = b;
     return buf.c_str();
 }

@@ -194,6 +194,8 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     CK(cudaEventCreate(&pe0_));
     CK(cudaEventCreate(&pe1_));
     use_graphs_ = env_int("FISH_NO_GRAPHS", 0) == 0;
+    no_fuse_ = env_int("FISH_NO_FUSE", 0) != 0;
+    fbk_set_pdl(env_int("FISH_NO_PDL", 0) == 0 ? 1 : 0);
     gguf_ = Gguf::open(path, err);
     if (!gguf_) return false;
     const Gguf& g = *gguf_;
@@ -271,7 +273,7 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         w.n_out = t->ne.size() > 1 ? (int)t->ne[1] : 1;
         w.n_exp = t->ne.size() > 2 ? (int)t->ne[2] : 1;
         w.stride = dev_row_bytes(t->type, w.n_in);
-        w.expert_bytes = w.stride * (size_t)w.n_out;
+        w.expert_bytes = dev_matrix_bytes(t->type, w.n_in, w.n_out);
         if (t->type == T_Q4_K || t->type == T_Q6_K) {
             if (w.n_in % 256) { if (err) *err = "K-quant row not a multiple of 256: " + name; return false; }
         }
@@ -379,7 +381,7 @@ bool Engine::upload_weights(std::string* err) {
         const Tensor* t = g.find(name);
         if (!t) return;
         jobs.push_back({t, w, total});
-        total = align_up(total + w->stride * (size_t)w->n_out * (size_t)w->n_exp, 256);
+        total = align_up(total + w->expert_bytes * (size_t)w->n_exp, 256);
     };
     add("token_embd.weight", &embd_);
     if (!cfg_.tied_output) add("output.weight", &out_w_);
@@ -409,29 +411,39 @@ bool Engine::upload_weights(std::string* err) {
     const int nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     int cur = 0;
     bool ok = true;
+    // chunks of whole 8-row tiles within one expert slice; each host thread
+    // repacks a run of tiles
     for (const Job& j : jobs) {
         const DevW& w = *j.w;
-        const uint64_t rows = (uint64_t)w.n_out * (uint64_t)w.n_exp;
         const size_t src_rb = ggml_row_bytes(j.t->type, (uint64_t)w.n_in);
-        const uint64_t rows_per = std::max<uint64_t>(1, stage / w.stride);
-        for (uint64_t r0 = 0; r0 < rows && ok; r0 += rows_per) {
-            const uint64_t nr = std::min(rows_per, rows - r0);
-            if (cudaEventSynchronize(done[cur]) != cudaSuccess) { ok = false; break; }
-            uint8_t* dst = pin[cur];
-            auto work = [&](int tid) {
-                for (uint64_t r = tid; r < nr; r += nth)
-                    repack_row(j.t->type, j.t->data + (r0 + r) * src_rb, dst + r * w.stride, w.n_in);
-            };
-            std::vector<std::thread> th;
-            for (int i = 1; i < nth; ++i) th.emplace_back(work, i);
-            work(0);
-            for (auto& t : th) t.join();
-            if (cudaMemcpyAsync(w.d + r0 * w.stride, dst, nr * w.stride, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
-                cudaEventRecord(done[cur], stream_) != cudaSuccess) {
-                ok = false;
-                break;
+        const size_t tile_bytes = dev_matrix_bytes(w.type, w.n_in, 8);
+        const int rows_per = (int)std::max<size_t>(8, stage / tile_bytes * 8);
+        for (int e = 0; e < w.n_exp && ok; ++e) {
+            for (int r0 = 0; r0 < w.n_out && ok; r0 += rows_per) {
+                const int nr = std::min(rows_per, w.n_out - r0);
+                const size_t nbytes = dev_matrix_bytes(w.type, w.n_in, nr);
+                if (cudaEventSynchronize(done[cur]) != cudaSuccess) { ok = false; break; }
+                uint8_t* dst = pin[cur];
+                const uint8_t* src = j.t->data + ((size_t)e * w.n_out + r0) * src_rb;
+                const int n_tiles = (nr + 7) / 8;
+                auto work = [&](int tid) {
+                    const int a = (int)((long long)n_tiles * tid / nth), b = (int)((long long)n_tiles * (tid + 1) / nth);
+                    if (a >= b) return;
+                    const int ra = 8 * a, rb = std::min(nr, 8 * b);
+                    repack_rows(w.type, src + (size_t)ra * src_rb, rb - ra, w.n_in, dst + (size_t)a * tile_bytes);
+                };
+                std::vector<std::thread> th;
+                for (int i = 1; i < nth; ++i) th.emplace_back(work, i);
+                work(0);
+                for (auto& t : th) t.join();
+                uint8_t* dev = w.d + (size_t)e * w.expert_bytes + (size_t)(r0 / 8) * tile_bytes;
+                if (cudaMemcpyAsync(dev, dst, nbytes, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+                    cudaEventRecord(done[cur], stream_) != cudaSuccess) {
+                    ok = false;
+                    break;
+                }
+                cur ^= 1;
             }
-            cur ^= 1;
         }
     }
     cudaStreamSynchronize(stream_);
@@ -530,6 +542,8 @@ KvView Engine::kv_view() const {
     kv.page_stride = page_elems_;
     kv.layer_stride = 2 * vofs;
     kv.head_stride = head;
+    kv.n_pages = n_pages_;
+    kv.err = fbk_gemv_error_flag();
     return kv;
 }
 
@@ -666,8 +680,23 @@ static void set_act_rows(GemvArgs& g, const ActQ& a, int t0, int K) {
     if (a.bsk) g.act.bsk = a.bsk + (size_t)t0 * (K / 32);
 }
 
+bool Engine::fusable(const DevW* const* ws, int n, int T) const {
+    if (no_fuse_) return false;
+    GemvArgs g{};
+    g.nseg = n;
+    g.K = ws[0]->n_in;
+    g.T = T;
+    g.pro.mode = PRO_NORM;
+    for (int i = 0; i < n; ++i) {
+        if (ws[i]->n_in != g.K) return false;
+        g.seg[i].type = ws[i]->type;
+        g.seg[i].rows = ws[i]->n_out;
+    }
+    return fbk_gemv_streamable(&g) != 0;
+}
+
 bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
-                        const ActQ& a, int T, int epi, std::string* err) {
+                        const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro) {
     for (int t0 = 0; t0 < T; t0 += 8) {
         const int nt = std::min(8, T - t0);
         GemvArgs g{};
@@ -675,12 +704,14 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
         g.K = ws[0]->n_in;
         g.T = nt;
         set_act_rows(g, a, t0, g.K);
+        if (pro) g.pro = *pro;
         double bytes = 0.0;
         for (int i = 0; i < n; ++i) {
             GemvSeg& s = g.seg[i];
             s.type = ws[i]->type;
             s.w = ws[i]->d;
             s.row_stride = ws[i]->stride;
+            s.w_bytes = ws[i]->expert_bytes * (size_t)ws[i]->n_exp;
             s.rows = ws[i]->n_out;
             s.y = ys[i] + (size_t)t0 * ldys[i];
             s.ldy = ldys[i];
@@ -694,7 +725,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
 }
 
 bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi, const float* xf,
-                  int ldxf, const int32_t* expert, std::string* err) {
+                  int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro) {
     for (int t0 = 0; t0 < T; t0 += 8) {
         const int nt = std::min(8, T - t0);
         GemvArgs g{};
@@ -702,12 +733,14 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         g.K = w.n_in;
         g.T = nt;
         set_act_rows(g, a, t0, g.K);
+        if (pro) g.pro = *pro;
         g.xf = xf ? xf + (size_t)t0 * ldxf : nullptr;
         g.ldxf = ldxf;
         GemvSeg& s = g.seg[0];
         s.type = w.type;
         s.w = w.d;
         s.row_stride = w.stride;
+        s.w_bytes = w.expert_bytes * (size_t)w.n_exp;
         s.rows = w.n_out;
         s.y = y + (size_t)t0 * ldy;
         s.ldy = ldy;
@@ -743,13 +776,18 @@ bool Engine::run_layers(int T, int max_ctx, std::string* err) {
     for (int li = 0; li < c.n_layers; ++li) {
         const DevLayer& L = layers_[li];
         a.K = E;
-        CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.attn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
         {
             const DevW* ws[3] = {&L.wq, &L.wk, &L.wv};
             float* ys[3] = {q_, k_, v_};
             const int lds[3] = {Q, KV, KV};
             const float* bs[3] = {L.bq, L.bk, L.bv};
-            if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err)) return false;
+            if (fusable(ws, 3, T)) {
+                const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.attn_norm, c.eps};
+                if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err, &pro)) return false;
+            } else {
+                CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.attn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+                if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err)) return false;
+            }
         }
         if (L.q_norm && L.k_norm) {
             CKP(PC_OTHER, 0, fbk_head_rmsnorm(q_, Q, T, H, D, L.q_norm, c.eps, stream_));
@@ -766,10 +804,21 @@ bool Engine::run_layers(int T, int max_ctx, std::string* err) {
                                           att_scratch_, att_scratch_floats_, max_ctx, stream_));
         }
         a.K = Q;
-        CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
-        if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+        {
+            const DevW* wo[1] = {&L.wo};
+            if (fusable(wo, 1, T)) {
+                const GemvPro pro{PRO_QUANT, attn_, Q, nullptr, 0, nullptr, 0.0f};
+                if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+            } else {
+                CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
+                if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+            }
+        }
         a.K = E;
-        CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.ffn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+        const DevW* wgu[2] = {&L.wg, &L.wu};
+        const bool fuse_ffn = c.n_experts == 0 && fusable(wgu, 2, T);
+        if (!fuse_ffn)
+            CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.ffn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
         if (c.n_experts > 0) {
             const int NE = c.n_experts, K = c.n_experts_per_tok, F = c.n_ff_exp;
             if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
@@ -794,14 +843,24 @@ bool Engine::run_layers(int T, int max_ctx, std::string* err) {
         } else {
             const int F = c.n_ff;
             {
-                const DevW* ws[2] = {&L.wg, &L.wu};
                 float* ys[2] = {g_, u_};
                 const int lds[2] = {F, F};
-                if (!gemv_group(ws, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
+                if (fuse_ffn) {
+                    const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.ffn_norm, c.eps};
+                    if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro)) return false;
+                } else {
+                    if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
+                }
             }
             a.K = F;
-            CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
-            if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+            const DevW* wd[1] = {&L.wd};
+            if (fusable(wd, 1, T)) {
+                const GemvPro pro{PRO_SILU, g_, F, u_, F, nullptr, 0.0f};
+                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+            } else {
+                CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
+                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+            }
         }
     }
     return true;
@@ -813,6 +872,11 @@ bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err) {
     const int E = c.n_embd;
     ActQ a = act_;
     a.K = E;
+    const DevW* wo[1] = {&out_w_};
+    if (fusable(wo, 1, n)) {
+        const GemvPro pro{PRO_NORM, x_ + (size_t)row0 * E, E, nullptr, 0, out_norm_, c.eps};
+        return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, nullptr, 0, nullptr, err, &pro);
+    }
     CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_ + (size_t)row0 * E, E, out_norm_, c.eps, n, E, xb_, E, &a, want32_e_, wantk_e_,
                                        stream_));
     return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, xb_, E, nullptr, err);
@@ -838,7 +902,7 @@ bool Engine::capture_graph(int key, std::string* err) {
     cudaGraph_t graph = nullptr;
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     std::string e2;
-    bool ok = fbk_embed(embd_.type, embd_.d, embd_.stride, cfg_.n_embd, ids_, T, x_, cfg_.n_embd, stream_) == 0;
+    bool ok = fbk_embed(embd_.type, embd_.d, cfg_.n_embd, embd_.n_out, ids_, T, x_, cfg_.n_embd, fbk_gemv_error_flag(), stream_) == 0;
     ok = ok && run_layers(T, cfg_.n_ctx, &e2);
     ok = ok && run_head(0, T, logits_, &e2);
     if (key == 0)
@@ -885,7 +949,7 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
         if (!graphs_.count(1) && !capture_graph(1, err)) return false;
         CK(cudaGraphLaunch(graphs_[1], stream_));
     } else {
-        CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, embd_.stride, c.n_embd, ids_, T, x_, c.n_embd, stream_));
+        CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, T, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
         if (!run_layers(T, pos0 + T, err)) return false;
         const int row0 = all ? 0 : T - 1;
         if (!run_head(row0, nrows, logits_, err)) return false;
@@ -920,7 +984,7 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
     } else {
         int max_ctx = 0;
         for (int i = 0; i < n; ++i) max_ctx = std::max(max_ctx, pos[i] + 1);
-        CK(fbk_embed(embd_.type, embd_.d, embd_.stride, c.n_embd, ids_, n, x_, c.n_embd, stream_));
+        CK(fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, n, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
         if (!run_layers(n, max_ctx, err)) return false;
         if (!run_head(0, n, logits_, err)) return false;
         CK(fbk_argmax(logits_, c.vocab, n, c.vocab, argmax_, stream_));

@@ -128,9 +128,12 @@ private:
     bool run_layers(int T, int max_ctx, std::string* err);
     bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err);
     bool gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi,
-              const float* xf, int ldxf, const int32_t* expert, std::string* err);
+              const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr);
     bool gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
-                    const ActQ& a, int T, int epi, std::string* err);
+                    const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro = nullptr);
+    // true when a T-token GEMV over these matrices can build its own int8
+    // activations (streamed kernel with a prologue)
+    bool fusable(const DevW* const* ws, int n, int T) const;
     KvView kv_view() const;
     // Step graphs are sequence-agnostic (token -> sequence slot and position
     // come from device arrays): key T = T-token step with logits + argmax,
@@ -189,6 +192,7 @@ private:
     std::map<int, cudaGraphExec_t> graphs_;
     std::map<int, int> graph_kernels_;
     bool use_graphs_ = true;
+    bool no_fuse_ = false;     // FISH_NO_FUSE: separate norm/quant kernels before every GEMV
     float last_greedy_ms_ = 0.0f;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     std::vector<ProfClass>* prof_ = nullptr;

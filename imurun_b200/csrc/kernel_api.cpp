@@ -122,10 +122,8 @@ int fbx_rmsnorm(const float* x, const float* w, int rows, int K, float eps, floa
 static int upload_rows(int type, const void* w, int n_in, int n_out, DevBuf& dw, size_t* stride) {
     const size_t st = dev_row_bytes(type, n_in);
     if (!st) return -1;
-    const size_t src_rb = ggml_row_bytes(type, (uint64_t)n_in);
-    std::vector<uint8_t> h(st * (size_t)n_out);
-    for (int r = 0; r < n_out; ++r)
-        repack_row(type, static_cast<const uint8_t*>(w) + (size_t)r * src_rb, h.data() + (size_t)r * st, n_in);
+    std::vector<uint8_t> h(dev_matrix_bytes(type, n_in, n_out));
+    repack_rows(type, static_cast<const uint8_t*>(w), n_out, n_in, h.data());
     TRY(dw.alloc(h.size()));
     TRY(cudaMemcpy(dw.p, h.data(), h.size(), cudaMemcpyHostToDevice));
     *stride = st;
@@ -164,6 +162,7 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
         g.seg[0].type = type;
         g.seg[0].w = dw.as<uint8_t>();
         g.seg[0].row_stride = stride;
+        g.seg[0].w_bytes = dev_matrix_bytes(type, n_in, n_out);
         g.seg[0].rows = n_out;
         g.seg[0].y = dy.as<float>() + (size_t)t0 * n_out;
         g.seg[0].ldy = n_out;
@@ -180,7 +179,7 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     if (type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K && type != T_F32 && type != T_F16) return -1;
     TRY(check_device());
     const size_t stride = dev_row_bytes(type, n_in);
-    const size_t mat = stride * (size_t)n_out;
+    const size_t mat = (dev_matrix_bytes(type, n_in, n_out) + 255) / 256 * 256;
     const int copies = (int)std::max<size_t>(1, ((512ull << 20) + mat - 1) / mat);
     DevBuf dw, dx, dy;
     DevAct da;
@@ -205,6 +204,7 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     g.ldxf = n_in;
     g.seg[0].type = type;
     g.seg[0].row_stride = stride;
+    g.seg[0].w_bytes = mat;
     g.seg[0].rows = n_out;
     g.seg[0].y = dy.as<float>();
     g.seg[0].ldy = n_out;
@@ -270,7 +270,7 @@ int fbx_block_sums(int type, const void* w, int n_in, int n_out, const void* act
     TRY(ds.alloc(sizeof(int32_t) * (size_t)n_out * nb));
     TRY(dm.alloc(sizeof(int32_t) * (size_t)n_out * nb));
     TRY(cudaMemset(dm.p, 0, sizeof(int32_t) * (size_t)n_out * nb));
-    TRY(fbk_block_sums(type, dw.as<uint8_t>(), stride, n_out, n_in, &da.a, ds.as<int32_t>(), dm.as<int32_t>(), nullptr));
+    TRY(fbk_block_sums(type, dw.as<uint8_t>(), n_out, n_in, &da.a, ds.as<int32_t>(), dm.as<int32_t>(), nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(sumi, ds.p, sizeof(int32_t) * (size_t)n_out * nb, cudaMemcpyDeviceToHost));
     if (mins) TRY(cudaMemcpy(mins, dm.p, sizeof(int32_t) * (size_t)n_out * nb, cudaMemcpyDeviceToHost));
@@ -297,6 +297,8 @@ struct TestPool {
         TRY(cudaMemcpy(seq.p, hs.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice));
         TRY(cudaMemcpy(pos.p, hq.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice));
         kv.f16 = f16;
+        kv.n_pages = np;
+        kv.err = fbk_gemv_error_flag();
         kv.k = pool.p;
         kv.v = static_cast<uint8_t*>(pool.p) + vofs * esz;
         kv.pt = pt.as<int32_t>();
@@ -410,7 +412,8 @@ int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids
     TRY(di.alloc(sizeof(int32_t) * T));
     TRY(dout.alloc(sizeof(float) * (size_t)T * E));
     TRY(cudaMemcpy(di.p, ids, sizeof(int32_t) * T, cudaMemcpyHostToDevice));
-    TRY(fbk_embed(type, dw.as<uint8_t>(), stride, E, di.as<int32_t>(), T, dout.as<float>(), E, nullptr));
+    TRY(fbk_embed(type, dw.as<uint8_t>(), E, n_rows, di.as<int32_t>(), T, dout.as<float>(), E, fbk_gemv_error_flag(),
+                  nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(out, dout.p, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToHost));
     return 0;

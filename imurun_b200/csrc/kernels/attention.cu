@@ -9,17 +9,24 @@
 // and fp16 or f32.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace fb {
 
 __device__ __forceinline__ size_t kv_off(const KvView& kv, int layer, int head, int t, int pos) {
-    const int page = kv.pt[(size_t)kv.tok_seq[t] * kv.pt_stride + pos / kv.page_size];
+    int page = kv.pt[(size_t)kv.tok_seq[t] * kv.pt_stride + pos / kv.page_size];
+    if (page < 0 || page >= kv.n_pages) {
+        if (kv.err) atomicExch(kv.err, 5);
+        page = 0;
+    }
     return (size_t)page * kv.page_stride + (size_t)layer * kv.layer_stride + (size_t)head * kv.head_stride +
            (size_t)(pos % kv.page_size) * (kv.head_stride / kv.page_size);
 }
 
 __global__ void k_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int H, int HKV, int D,
                               int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x;
     const int pos = kv.tok_pos[t];
     const int half = rot / 2;
@@ -92,6 +99,8 @@ template <bool F16, int NW>
 __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict__ q, int ldq, int H, int HKV, int D,
                                                         float scale, KvView kv, int layer, float* __restrict__ part,
                                                         int n_splits) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.z, hk = blockIdx.y, sp = blockIdx.x;
     const int G = H / HKV;
     const int n_keys = kv.tok_pos[t] + 1;
@@ -248,6 +257,8 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
 
 // out[t][h][:] = sum_s w_s o_s / sum_s w_s l_s with w_s = exp(m_s - max m).
 __global__ void k_attn_combine(const float* __restrict__ part, int H, int D, int n_splits, float* out, int ldo) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float sw[];   // n_splits weights
     __shared__ float s_L;
     const int t = blockIdx.y, h = blockIdx.x;
@@ -281,8 +292,8 @@ extern "C" int fbk_rope_append(float* q, int ldq, const float* k, const float* v
                                int D, int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer,
                                cudaStream_t st) {
     if (T <= 0) return 0;
-    k_rope_append<<<T, 256, 0, st>>>(q, ldq, k, v, ldkv, H, HKV, D, rot, neox, rcos, rsin, kv, layer);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_rope_append, dim3(T), dim3(256), 0, st, q, ldq, k, v, ldkv, H, HKV, D, rot, neox, rcos, rsin, kv,
+                           layer);
 }
 
 // Keys per split: 32 per warp; contexts above 2048 use 4-warp CTAs so the
@@ -304,13 +315,15 @@ extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int
     const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
     if ((size_t)T * H * n_splits * (D + 2) > scratch_floats) return (int)cudaErrorInvalidValue;
     dim3 grid(n_splits, HKV, T);
+    cudaError_t e;
     if (kv.f16) {
-        if (nw == 1) k_attn_split<true, 1><<<grid, 32, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
-        else k_attn_split<true, 4><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        if (nw == 1) e = fbk_launch(k_attn_split<true, 1>, grid, dim3(32), 0, st, q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        else e = fbk_launch(k_attn_split<true, 4>, grid, dim3(128), 0, st, q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
     } else {
-        if (nw == 1) k_attn_split<false, 1><<<grid, 32, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
-        else k_attn_split<false, 4><<<grid, 128, 0, st>>>(q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        if (nw == 1) e = fbk_launch(k_attn_split<false, 1>, grid, dim3(32), 0, st, q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
+        else e = fbk_launch(k_attn_split<false, 4>, grid, dim3(128), 0, st, q, ldq, H, HKV, D, scale, kv, layer, scratch, n_splits);
     }
-    k_attn_combine<<<dim3(H, T), 128, n_splits * sizeof(float), st>>>(scratch, H, D, n_splits, out, ldo);
-    return (int)cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    return (int)fbk_launch(k_attn_combine, dim3(H, T), dim3(128), n_splits * sizeof(float), st, scratch, H, D, n_splits, out,
+                           ldo);
 }

@@ -37,6 +37,12 @@ __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// Programmatic dependent launch (no-ops for launches without the attribute):
+// wait until the previous kernel on the stream has completed and its writes
+// are visible / let the next kernel be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Streaming 128-bit load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 r;

@@ -4,29 +4,38 @@
 // src/quant_x86.cpp:299-309, 346-382, 431-495) or F32 / F16 (f32 path,
 // src/ops.cpp:219-250).
 //
-// The work unit is 32 weight values of one row (unit_math.cuh); the lanes that
-// hold the units of one super-block add their integer partials with shuffles,
-// so every super-block's integer sums
-//     Q4_K  sumi = sum_g sc_g sum_l q x,   mins = sum_g m_g bsums_g
-//     Q6_K  sumi = sum_j sc_j sum (q6-32) x
-//     Q8_0  s    = sum w x
-// are formed exactly as the reference forms them, then combined in float once
-// per block. Decode is HBM-bound; two kernels stream the weights:
-//   k_gemv_stream  quantised rows, T <= 4: a producer warp streams 8-row x
-//                  2048-value pieces into a ring of shared-memory stages with
-//                  cp.async.bulk (TMA) and mbarriers; 8 consumer warps compute
-//                  from shared memory with the activations held in registers.
-//   k_gemv         F32/F16 rows (router, small tensors) and T = 5..8, with
-//                  direct 128-bit loads.
+// Every integer the reference forms per block (Q4_K sumi and mins, Q6_K sumi,
+// Q8_0 s) is formed whole by one thread (unit_math.cuh) and converted to float
+// once. Two kernels:
+//   k_gemv_stream  quantised rows, T <= 4 (decode). A producer warp streams
+//                  (8-row tile x 2048-value group) stages — one contiguous
+//                  bulk copy each, thanks to the tile-major layout — into a
+//                  ring of shared-memory slots guarded by mbarriers. Eight
+//                  consumer warps first build the activation image in shared
+//                  memory (copied from quantised planes, or computed from f32
+//                  rows: RMSNorm, SwiGLU or plain, then quantised), then each
+//                  takes half a stage (4 rows x 8 blocks, one block per
+//                  lane). Per-stage row partials go to shared memory and are
+//                  summed over groups at the end in a fixed order.
+//   k_gemv_direct  T = 5..8 (prefill chunks) and F32/F16 rows, plain loads.
+// Launches carry the programmatic-dependent-launch attribute when the caller
+// asks for it: the producer streams weights before the previous kernel has
+// finished (weights never change); everything that reads activations or
+// writes outputs waits for it first.
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "layout.cuh"
 #include "unit_math.cuh"
 
 namespace fb {
+
+// ============================================================ host layouts
 
 size_t dev_row_bytes(int type, int n) {
     size_t b = 0;
@@ -39,166 +48,50 @@ size_t dev_row_bytes(int type, int n) {
     return (b + 15) / 16 * 16;
 }
 
-void repack_row(int type, const uint8_t* src, uint8_t* dst, int n) {
-    const size_t db = dev_row_bytes(type, n);
-    for (size_t i = 0; i < db; ++i) dst[i] = 0;
-    switch (type) {
-        case T_Q4_K:
-            for (size_t i = 0; i < (size_t)(n / 256) * 144; ++i) dst[i] = src[i];
-            break;
-        case T_Q6_K: {
-            const int nb = n / 256;
-            for (int b = 0; b < nb; ++b) {
-                const size_t qo = block_offset(T_Q6_K, b), dof = dscale_offset(T_Q6_K, nb, b);
-                for (int i = 0; i < 208; ++i) dst[qo + i] = src[(size_t)b * 210 + i];
-                dst[dof] = src[(size_t)b * 210 + 208];
-                dst[dof + 1] = src[(size_t)b * 210 + 209];
-            }
-            break;
-        }
-        case T_Q8_0: {
-            const int nb = n / 32;
-            for (int b = 0; b < nb; ++b) {
-                const size_t qo = block_offset(T_Q8_0, b), dof = dscale_offset(T_Q8_0, nb, b);
-                for (int i = 0; i < 32; ++i) dst[qo + i] = src[(size_t)b * 34 + 2 + i];
-                dst[dof] = src[(size_t)b * 34];
-                dst[dof + 1] = src[(size_t)b * 34 + 1];
-            }
-            break;
-        }
-        case T_F32:
-            for (size_t i = 0; i < (size_t)n * 4; ++i) dst[i] = src[i];
-            break;
-        case T_F16:
-            for (size_t i = 0; i < (size_t)n * 2; ++i) dst[i] = src[i];
-            break;
-        default: break;
+size_t dev_matrix_bytes(int type, int n, int rows) {
+    if (is_tiled(type)) return tiled_matrix_bytes(type, n, rows);
+    return dev_row_bytes(type, n) * (size_t)rows;
+}
+
+static size_t ggml_block_bytes(int type) { return type == T_Q8_0 ? 34 : (type == T_Q4_K ? 144 : 210); }
+
+void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst) {
+    const size_t total = dev_matrix_bytes(type, n, rows);
+    std::memset(dst, 0, total);
+    if (!is_tiled(type)) {
+        const size_t sb = type == T_F32 ? (size_t)n * 4 : (size_t)n * 2, db = dev_row_bytes(type, n);
+        for (int r = 0; r < rows; ++r) std::memcpy(dst + (size_t)r * db, src + (size_t)r * sb, sb);
+        return;
     }
-}
-
-// ============================================================ activation access
-// Activations are read through L1 (every row of a launch reads the same x).
-
-__device__ __forceinline__ void x_q4k(const ActQ& a, int t, int b, int p, uint4& x0, uint4& x1, uint4& x2, uint4& x3,
-                                      uint32_t& bs) {
-    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 64 * p;
-    x0 = __ldg(reinterpret_cast<const uint4*>(xq));
-    x1 = __ldg(reinterpret_cast<const uint4*>(xq + 16));
-    x2 = __ldg(reinterpret_cast<const uint4*>(xq + 32));
-    x3 = __ldg(reinterpret_cast<const uint4*>(xq + 48));
-    bs = __ldg(reinterpret_cast<const uint32_t*>(a.bsk + (size_t)t * (a.K / 32) + (size_t)b * 8 + 2 * p));
-}
-
-__device__ __forceinline__ void x_q6k(const ActQ& a, int t, int b, int j, uint2 (&x)[4]) {
-    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)b * 256 + 128 * (j >> 2) + 8 * (j & 3);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) x[q] = __ldg(reinterpret_cast<const uint2*>(xq + 32 * q));
-}
-
-// ============================================================ direct kernel rows
-
-template <int NT, bool SUMS>
-__device__ __forceinline__ void row_q4k(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
-                                        float (&acc)[NT], int32_t* sumi_out, int32_t* mins_out) {
-    const int nunits = nb * 4;
-    for (int u = lane; u - lane < nunits; u += 32) {
-        const bool ok = u < nunits;
-        const int b = u >> 2, p = u & 3;
-        Q4kUnit un;
-        uint4 h = make_uint4(0, 0, 0, 0);
-        if (ok) {
-            const uint8_t* blk = row + (size_t)b * 144;
-            h = ldg_stream(blk);
-            un.load(h, ldg_stream(blk + 16 + 32 * p), ldg_stream(blk + 32 + 32 * p), p);
-        }
-        const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            int si = 0, mi = 0;
-            if (ok) {
-                uint4 x0, x1, x2, x3;
-                uint32_t bs;
-                x_q4k(a, t, b, p, x0, x1, x2, x3, bs);
-                un.dot(x0, x1, x2, x3, bs, si, mi);
-            }
-            si += __shfl_xor_sync(0xffffffffu, si, 1);
-            si += __shfl_xor_sync(0xffffffffu, si, 2);
-            mi += __shfl_xor_sync(0xffffffffu, mi, 1);
-            mi += __shfl_xor_sync(0xffffffffu, mi, 2);
-            if (ok && p == 0) {
-                if (SUMS) { sumi_out[b] = si; mins_out[b] = mi; }
-                else {
-                    const float dx = __ldg(a.dk + (size_t)t * (a.K / 256) + b);
-                    acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+    const int nb = row_blocks(type, n);
+    const size_t srb = (size_t)nb * ggml_block_bytes(type);
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* s = src + (size_t)r * srb;
+        for (int b = 0; b < nb; ++b) {
+            const uint8_t* sb = s + (size_t)b * ggml_block_bytes(type);
+            uint8_t* q = dst + block_offset_tm(type, n, r, b);
+            switch (type) {
+                case T_Q4_K: std::memcpy(q, sb, 144); break;
+                case T_Q6_K: {
+                    std::memcpy(q, sb, 208);
+                    uint8_t* d = dst + dscale_offset_tm(type, n, r, b);
+                    d[0] = sb[208];
+                    d[1] = sb[209];
+                    break;
+                }
+                default: {   // Q8_0: fp16 d then qs[32]
+                    std::memcpy(q, sb + 2, 32);
+                    uint8_t* d = dst + dscale_offset_tm(type, n, r, b);
+                    d[0] = sb[0];
+                    d[1] = sb[1];
+                    break;
                 }
             }
         }
     }
 }
 
-template <int NT, bool SUMS>
-__device__ __forceinline__ void row_q6k(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
-                                        float (&acc)[NT], int32_t* sumi_out) {
-    const int nunits = nb * 8;
-    for (int u = lane; u - lane < nunits; u += 32) {
-        const bool ok = u < nunits;
-        const int b = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
-        Q6kUnit un;
-        float dw = 0.0f;
-        if (ok) {
-            const uint8_t* blk = row + block_offset(T_Q6_K, b);
-            un.load(ldg_stream2(blk + 64 * hh + 8 * jj), ldg_stream2(blk + 64 * hh + 32 + 8 * jj),
-                    ldg_stream2(blk + 128 + 32 * hh + 8 * jj), ldg_stream2(blk + 192 + 8 * hh), jj);
-            dw = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q6_K, nb, b)));
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            int si = 0;
-            if (ok) {
-                uint2 x[4];
-                x_q6k(a, t, b, j, x);
-                const int xs[4] = {sum8(x[0]), sum8(x[1]), sum8(x[2]), sum8(x[3])};
-                si = un.dot(x, xs);
-            }
-            si += __shfl_xor_sync(0xffffffffu, si, 1);
-            si += __shfl_xor_sync(0xffffffffu, si, 2);
-            si += __shfl_xor_sync(0xffffffffu, si, 4);
-            if (ok && j == 0) {
-                if (SUMS) sumi_out[b] = si;
-                else acc[t] += __fmul_rn(dw, __ldg(a.dk + (size_t)t * (a.K / 256) + b)) * (float)si;
-            }
-        }
-    }
-}
-
-template <int NT, bool SUMS>
-__device__ __forceinline__ void row_q80(const uint8_t* __restrict__ row, int nb, const ActQ& a, int lane,
-                                        float (&acc)[NT], int32_t* sumi_out) {
-    for (int b = lane; b < nb; b += 32) {
-        const uint8_t* q = row + block_offset(T_Q8_0, b);
-        const uint4 w0 = ldg_stream(q), w1 = ldg_stream(q + 16);
-        const float dw = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q8_0, nb, b)));
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            const int8_t* xq = a.q32 + (size_t)t * a.ld + (size_t)b * 32;
-            const int s = q80_dot(w0, w1, __ldg(reinterpret_cast<const uint4*>(xq)),
-                                  __ldg(reinterpret_cast<const uint4*>(xq + 16)));
-            if (SUMS) sumi_out[b] = s;
-            else acc[t] += __fmul_rn(dw, __ldg(a.d32 + (size_t)t * (a.K / 32) + b)) * (float)s;
-        }
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void row_float(int type, const uint8_t* __restrict__ row, int K, const float* xf, int ldxf,
-                                          int lane, float (&acc)[NT]) {
-    for (int k = lane; k < K; k += 32) {
-        const float w = type == T_F32 ? reinterpret_cast<const float*>(row)[k]
-                                      : h2f(reinterpret_cast<const uint16_t*>(row)[k]);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] += w * xf[(size_t)t * ldxf + k];
-    }
-}
+// ============================================================ common pieces
 
 __device__ __forceinline__ void store_out(const GemvSeg& g, int rr, int t, float v) {
     if (g.bias) v += g.bias[rr];
@@ -207,63 +100,191 @@ __device__ __forceinline__ void store_out(const GemvSeg& g, int rr, int t, float
     else *yp = v;
 }
 
+// ============================================================ direct kernel
+
+// One lane per (row, block) of 4 rows: weights streamed from global memory,
+// activations from the quantised planes through the read-only cache.
+// true when [p, p + n) lies inside [lo, hi); otherwise the error flag is raised
+__device__ __forceinline__ bool in_range(const uint8_t* p, size_t n, const uint8_t* lo, const uint8_t* hi, int* err) {
+    if (p >= lo && p + n <= hi) return true;
+    if (err) atomicExch(err, 3);
+    return false;
+}
+
 template <int NT>
-__global__ void __launch_bounds__(256) k_gemv(GemvArgs args) {
+__device__ __forceinline__ void direct_rows_q(const GemvSeg& g, const uint8_t* base, int K, const ActQ& a, int T,
+                                              int row, int bl, float (&acc)[NT], int* err) {
+    const int nb = row_blocks(g.type, K);
+    const uint8_t* wend = g.w + g.w_bytes;
+    if (g.type == T_Q4_K) {
+        for (int kb = bl; kb < nb; kb += 8) {
+            uint4 w[9];
+            const uint8_t* p = base + block_offset_tm(T_Q4_K, K, row, kb);
+            if (!in_range(p, 144, g.w, wend, err)) continue;
+#pragma unroll
+            for (int i = 0; i < 9; ++i) w[i] = ldg_stream(p + 16 * i);
+            const float dw = h2f((uint16_t)(w[0].x & 0xFFFFu)), dmw = h2f((uint16_t)(w[0].x >> 16));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t >= T) break;
+                int si, mi;
+                const uint4 bs = __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)t * (K / 32) + (size_t)kb * 8));
+                q4k_block<LdGlobal>(w, a.qk + (size_t)t * a.ld + (size_t)kb * 256, bs, si, mi);
+                const float dx = __ldg(a.dk + (size_t)t * (K / 256) + kb);
+                acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+            }
+        }
+    } else if (g.type == T_Q6_K) {
+        for (int kb = bl; kb < nb; kb += 8) {
+            uint4 w[13];
+            const uint8_t* p = base + block_offset_tm(T_Q6_K, K, row, kb);
+            const uint8_t* pd = base + dscale_offset_tm(T_Q6_K, K, row, kb);
+            if (!in_range(p, 208, g.w, wend, err) || !in_range(pd, 2, g.w, wend, err)) continue;
+#pragma unroll
+            for (int i = 0; i < 13; ++i) w[i] = ldg_stream(p + 16 * i);
+            const float dw = h2f(*reinterpret_cast<const uint16_t*>(pd));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t >= T) break;
+                const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)kb * 256;
+                int16_t xs[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) xs[j] = (int16_t)sum16(__ldg(reinterpret_cast<const uint4*>(xq + 16 * j)));
+                const int si = q6k_block<LdGlobal>(w, xq, xs);
+                acc[t] += __fmul_rn(dw, __ldg(a.dk + (size_t)t * (K / 256) + kb)) * (float)si;
+            }
+        }
+    } else {   // Q8_0: lane takes chunks of 8 blocks
+        const int nch = (nb + 7) / 8;
+        for (int kc = bl; kc < nch; kc += 8) {
+            for (int i = 0; i < 8; ++i) {
+                const int b = 8 * kc + i;
+                if (b >= nb) break;
+                const uint8_t* p = base + block_offset_tm(T_Q8_0, K, row, b);
+                const uint8_t* pd = base + dscale_offset_tm(T_Q8_0, K, row, b);
+                if (!in_range(p, 32, g.w, wend, err) || !in_range(pd, 2, g.w, wend, err)) continue;
+                const uint4 w0 = ldg_stream(p), w1 = ldg_stream(p + 16);
+                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pd));
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    const int s = q80_block<LdGlobal>(w0, w1, a.q32 + (size_t)t * a.ld + (size_t)b * 32);
+                    acc[t] += __fmul_rn(dw, __ldg(a.d32 + (size_t)t * (K / 32) + b)) * (float)s;
+                }
+            }
+        }
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void row_float(int type, const uint8_t* __restrict__ row, int K, const float* xf, int ldxf,
+                                          int T, int lane, float (&acc)[NT]) {
+    for (int k = lane; k < K; k += 32) {
+        const float w = type == T_F32 ? reinterpret_cast<const float*>(row)[k]
+                                      : h2f(reinterpret_cast<const uint16_t*>(row)[k]);
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if (t < T) acc[t] += w * xf[(size_t)t * ldxf + k];
+    }
+}
+
+// Quantised segments: a warp owns 4 rows (lane = row * 8 + block slot);
+// float segments: a warp owns one row.
+template <int NT>
+__global__ void __launch_bounds__(256) k_gemv_direct(GemvArgs args) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
-    int total = 0;
+    int items[kMaxSeg + 1];
+    items[0] = 0;
 #pragma unroll
-    for (int s = 0; s < kMaxSeg; ++s) if (s < args.nseg) total += args.seg[s].rows;
-    for (int r = gw; r < total; r += nw) {
-        int s = 0, rr = r;
-        while (s < args.nseg - 1 && rr >= args.seg[s].rows) { rr -= args.seg[s].rows; ++s; }
+    for (int s = 0; s < kMaxSeg; ++s) {
+        const int r = s < args.nseg ? args.seg[s].rows : 0;
+        const int n = s < args.nseg ? (is_tiled(args.seg[s].type) ? (r + 3) / 4 : r) : 0;
+        items[s + 1] = items[s] + n;
+    }
+    for (int it = gw; it < items[args.nseg]; it += nw) {
+        int s = 0;
+        while (s < args.nseg - 1 && it >= items[s + 1]) ++s;
         const GemvSeg& g = args.seg[s];
         const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
-        const uint8_t* row = base + (size_t)rr * g.row_stride;
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        switch (g.type) {
-            case T_Q4_K: row_q4k<NT, false>(row, args.K / 256, args.act, lane, acc, nullptr, nullptr); break;
-            case T_Q6_K: row_q6k<NT, false>(row, args.K / 256, args.act, lane, acc, nullptr); break;
-            case T_Q8_0: row_q80<NT, false>(row, args.K / 32, args.act, lane, acc, nullptr); break;
-            default: row_float<NT>(g.type, row, args.K, args.xf, args.ldxf, lane, acc); break;
-        }
+        if (is_tiled(g.type)) {
+            const int row = (it - items[s]) * 4 + (lane >> 3), bl = lane & 7;
+            if (row < g.rows) direct_rows_q<NT>(g, base, args.K, args.act, args.T, row, bl, acc, args.err);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            const float v = warp_sum(acc[t]);
-            if (lane == 0 && t < args.T) store_out(g, rr, t, v);
+            for (int t = 0; t < NT; ++t) {
+                float v = acc[t];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                v += __shfl_xor_sync(0xffffffffu, v, 4);
+                if (bl == 0 && row < g.rows && t < args.T) store_out(g, row, t, v);
+            }
+        } else {
+            const int row = it - items[s];
+            if (in_range(base + (size_t)row * g.row_stride, g.row_stride, g.w, g.w + g.w_bytes, lane == 0 ? args.err : nullptr))
+                row_float<NT>(g.type, base + (size_t)row * g.row_stride, args.K, args.xf, args.ldxf, args.T, lane, acc);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_sum(acc[t]);
+                if (lane == 0 && t < args.T) store_out(g, row, t, v);
+            }
         }
     }
 }
 
-__global__ void k_block_sums(int type, const uint8_t* __restrict__ w, size_t stride, int rows, int K, ActQ a,
-                             int32_t* sumi, int32_t* mins) {
-    const int lane = threadIdx.x & 31;
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (r >= rows) return;
-    float acc[1] = {0.0f};
-    const int nb = type == T_Q8_0 ? K / 32 : K / 256;
-    const uint8_t* row = w + (size_t)r * stride;
-    switch (type) {
-        case T_Q4_K: row_q4k<1, true>(row, nb, a, lane, acc, sumi + (size_t)r * nb, mins + (size_t)r * nb); break;
-        case T_Q6_K: row_q6k<1, true>(row, nb, a, lane, acc, sumi + (size_t)r * nb); break;
-        case T_Q8_0: row_q80<1, true>(row, nb, a, lane, acc, sumi + (size_t)r * nb); break;
-        default: break;
+// Debug: the per-(row, block) integer sums, one thread per block, with the
+// same block functions the GEMV kernels use.
+__global__ void k_block_sums(int type, const uint8_t* __restrict__ w, int rows, int K, ActQ a, int32_t* sumi,
+                             int32_t* mins) {
+    const int nb = row_blocks(type, K);
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * nb) return;
+    const int row = (int)(i / nb), b = (int)(i % nb);
+    if (type == T_Q4_K) {
+        uint4 wr[9];
+        const uint8_t* p = w + block_offset_tm(T_Q4_K, K, row, b);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wr[k] = ldg_stream(p + 16 * k);
+        int si, mi;
+        q4k_block<LdGlobal>(wr, a.qk + (size_t)b * 256, __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)b * 8)),
+                            si, mi);
+        sumi[i] = si;
+        if (mins) mins[i] = mi;
+    } else if (type == T_Q6_K) {
+        uint4 wr[13];
+        const uint8_t* p = w + block_offset_tm(T_Q6_K, K, row, b);
+#pragma unroll
+        for (int k = 0; k < 13; ++k) wr[k] = ldg_stream(p + 16 * k);
+        const int8_t* xq = a.qk + (size_t)b * 256;
+        int16_t xs[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xs[j] = (int16_t)sum16(__ldg(reinterpret_cast<const uint4*>(xq + 16 * j)));
+        sumi[i] = q6k_block<LdGlobal>(wr, xq, xs);
+    } else if (type == T_Q8_0) {
+        const uint8_t* p = w + block_offset_tm(T_Q8_0, K, row, b);
+        sumi[i] = q80_block<LdGlobal>(ldg_stream(p), ldg_stream(p + 16), a.q32 + (size_t)b * 32);
     }
 }
 
-// ============================================================ TMA-streamed kernel
+// ============================================================ streamed kernel
 
-constexpr int kBulkConsumers = 8;                 // consumer warps; tile = 8 rows
-constexpr int kBulkRows = kBulkConsumers;
+constexpr int kConsumers = 8;                       // consumer warps (2 per stage)
 constexpr int kMaxStages = 32;
-constexpr int kBulkHeader = 2 * kMaxStages * 8;   // mbarriers
-constexpr long long kSpinLimit = 1LL << 26;       // bounded mbarrier waits
+constexpr int kHdrBytes = 2 * kMaxStages * 8 + 64;  // mbarriers, abort flag, norm scales
+constexpr int kXChunk = 272;                        // bytes per 256 activation int8 (16 B pad: no bank conflicts)
+constexpr long long kWaitNs = 2000000000LL;         // bounded waits: 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -282,11 +303,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: false after kSpinLimit polls (the caller records an error).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (long long i = 0; i < kSpinLimit; ++i)
+// Bounded wait: false after kWaitNs or once another thread raised *abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    for (unsigned i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-    return false;
+        if ((i & 63) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) return false;
+    }
+}
+// Bounded wait that ignores the abort flag (used while draining).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    const unsigned long long t0 = gtimer();
+    for (unsigned i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 63 && (long long)(gtimer() - t0) > kWaitNs) return false;
+    }
 }
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -294,273 +326,374 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
-// Activation chunk of one lane for one 2048-value group, held in registers
-// while every row of the CTA's tiles passes through (the same x serves all
-// rows): Q4_K unit (block lane/4, pair lane%4): 64 int8 + bsums + d;
-// Q6_K units u = lane, lane+32: 2 x 32 int8 + 2 d; Q8_0 blocks lane, lane+32:
-// 2 x 32 int8 + 2 d.
-struct XRegs {
-    uint4 q[4];
-    uint32_t a0, a1;   // Q4_K: bsums pair, d bits | Q6_K/Q8_0: d bits of the two units
-    int xs[8];         // Q6_K: sums of the 8-value pieces (unit k, quad q at 4k + q)
+struct StreamJobs {
+    int tile0[kMaxSeg + 1];  // 8-row tiles: segment s owns tiles [tile0[s], tile0[s+1])
+    int n_groups;            // 2048-value groups per row
+    int stages;              // ring slots
+    int slot_bytes;          // bytes per slot (8 x the largest piece)
+    int tiles_per_cta;
+    int xk_bytes, x32_bytes; // per-token bytes of the two activation images (0 = not built)
+    int* err;                // device error flag
+    int wait_first;          // producer waits for the previous kernel (expert indices)
 };
 
-__device__ __forceinline__ void load_x(int type, const ActQ& a, int t, int gi, int lane, int nb, XRegs& x) {
-    const int8_t* base = (type == T_Q8_0 ? a.q32 : a.qk) + (size_t)t * a.ld;
-    x.q[0] = x.q[1] = x.q[2] = x.q[3] = make_uint4(0, 0, 0, 0);
-    x.a0 = x.a1 = 0;
+// Segment of a tile (segments are copied to shared memory at kernel start,
+// so no parameter array is indexed dynamically).
+__device__ __forceinline__ int seg_index(const int* tile0, int nseg, int tile) {
+    int sg = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) x.xs[i] = 0;
-    if (type == T_Q4_K) {
-        const int b = gi * 8 + (lane >> 2), p = lane & 3;
-        if (b < nb) {
-            const int8_t* xq = base + (size_t)b * 256 + 64 * p;
+    for (int i = 1; i < kMaxSeg; ++i)
+        if (i < nseg && tile >= tile0[i]) sg = i;
+    return sg;
+}
+
+// Activation image in shared memory, per token:
+//   K layout (256-value blocks): q [n256][272], bsums [n256][8] i16,
+//                                sum16 [n256][16] i16, d [n256] f32
+//   32 layout:                   q [n256][272], d [n256][8] f32
+struct XImage {
+    uint8_t* base;
+    int n256, xk, x32, T;
+    __device__ int8_t* qk(int t, int c) const { return (int8_t*)(base + (size_t)t * xk + (size_t)c * kXChunk); }
+    __device__ int16_t* bsk(int t, int c) const {
+        return (int16_t*)(base + (size_t)t * xk + (size_t)n256 * kXChunk + 16 * c);
+    }
+    __device__ int16_t* s16(int t, int c) const {
+        return (int16_t*)(base + (size_t)t * xk + (size_t)n256 * (kXChunk + 16) + 32 * c);
+    }
+    __device__ float* dk(int t, int c) const {
+        return (float*)(base + (size_t)t * xk + (size_t)n256 * (kXChunk + 48) + 4 * c);
+    }
+    __device__ int8_t* q32(int t, int c) const {
+        return (int8_t*)(base + (size_t)T * xk + (size_t)t * x32 + (size_t)c * kXChunk);
+    }
+    __device__ float* d32(int t, int c) const {
+        return (float*)(base + (size_t)T * xk + (size_t)t * x32 + (size_t)n256 * kXChunk + 32 * c);
+    }
+};
+
+static inline int ximg_k_bytes(int K) { return (((K + 255) / 256) * (kXChunk + 16 + 32 + 4) + 15) / 16 * 16; }
+static inline int ximg_32_bytes(int K) { return (((K + 255) / 256) * (kXChunk + 32) + 15) / 16 * 16; }
+
+__device__ __forceinline__ uint2 pack8q(const int (&q)[8]) {
+    uint2 p;
+    p.x = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+    p.y = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+    return p;
+}
+
+// Quantise one 256-value chunk (8 values per lane) into the image, both
+// layouts as requested, with the reference's arithmetic (the same steps as
+// quant_act.cu: d = amax/127, id = 1/d, round half to even, clamp).
+__device__ __forceinline__ void ximg_quant_chunk(const float (&v)[8], int lane, int K, int t, int c,
+                                                 const XImage& xi, bool wantk, bool want32) {
+    const bool full = c * 256 + 256 <= K;
+    float am = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) x.q[i] = __ldg(reinterpret_cast<const uint4*>(xq + 16 * i));
-            x.a0 = __ldg(reinterpret_cast<const uint32_t*>(a.bsk + (size_t)t * (a.K / 32) + (size_t)b * 8 + 2 * p));
-            x.a1 = __float_as_uint(__ldg(a.dk + (size_t)t * (a.K / 256) + b));
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    if (wantk && full) {
+        const float amax = warp_max(am);
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[8], s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], id))));
+            s += q[i];
         }
-    } else if (type == T_Q6_K) {
+        *reinterpret_cast<uint2*>(xi.qk(t, c) + 8 * lane) = pack8q(q);
+        const int s16v = s + __shfl_xor_sync(0xffffffffu, s, 1);
+        const int s32v = s16v + __shfl_xor_sync(0xffffffffu, s16v, 2);
+        if ((lane & 1) == 0) xi.s16(t, c)[lane >> 1] = (int16_t)s16v;
+        if ((lane & 3) == 0) xi.bsk(t, c)[lane >> 2] = (int16_t)s32v;
+        if (lane == 0) *xi.dk(t, c) = d;
+    }
+    if (want32) {
+        float b = am;
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 1));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 2));
+        const float d = __fdiv_rn(b, 127.0f);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[8];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int u = lane + 32 * k, b = gi * 8 + (u >> 3), j = u & 7;
-            if (b < nb) {
-                const int8_t* xq = base + (size_t)b * 256 + 128 * (j >> 2) + 8 * (j & 3);
-                const uint2 v0 = __ldg(reinterpret_cast<const uint2*>(xq));
-                const uint2 v1 = __ldg(reinterpret_cast<const uint2*>(xq + 32));
-                const uint2 v2 = __ldg(reinterpret_cast<const uint2*>(xq + 64));
-                const uint2 v3 = __ldg(reinterpret_cast<const uint2*>(xq + 96));
-                x.q[2 * k] = make_uint4(v0.x, v0.y, v1.x, v1.y);
-                x.q[2 * k + 1] = make_uint4(v2.x, v2.y, v3.x, v3.y);
-                x.xs[4 * k + 0] = sum8(v0);
-                x.xs[4 * k + 1] = sum8(v1);
-                x.xs[4 * k + 2] = sum8(v2);
-                x.xs[4 * k + 3] = sum8(v3);
-                const uint32_t d = __float_as_uint(__ldg(a.dk + (size_t)t * (a.K / 256) + b));
-                if (k == 0) x.a0 = d; else x.a1 = d;
-            }
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int b = gi * 64 + lane + 32 * k;
-            if (b < nb) {
-                const int8_t* xq = base + (size_t)b * 32;
-                x.q[2 * k] = __ldg(reinterpret_cast<const uint4*>(xq));
-                x.q[2 * k + 1] = __ldg(reinterpret_cast<const uint4*>(xq + 16));
-                const uint32_t d = __float_as_uint(__ldg(a.d32 + (size_t)t * (a.K / 32) + b));
-                if (k == 0) x.a0 = d; else x.a1 = d;
-            }
-        }
+        for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], id))));
+        *reinterpret_cast<uint2*>(xi.q32(t, c) + 8 * lane) = pack8q(q);
+        if ((lane & 3) == 0) xi.d32(t, c)[lane >> 2] = d;
     }
 }
 
-// Float contribution of one lane for one (row, group) piece in shared memory.
-// Integer sums per super-block are reduced across the lanes that share it
-// (Q4_K: 4 lanes, Q6_K: 8 lanes) before the one float combine per block.
-template <int NT>
-__device__ __forceinline__ void piece_dot(int type, const uint8_t* pc, int gbk, int lane, const XRegs (&x)[NT],
-                                          float (&c)[NT]) {
+__device__ __forceinline__ void ld8(const float* p, int i0, int K, float (&v)[8]) {
+    if (i0 + 8 <= K) {
+        const float4 a = *reinterpret_cast<const float4*>(p + i0);
+        const float4 b = *reinterpret_cast<const float4*>(p + i0 + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
 #pragma unroll
-    for (int t = 0; t < NT; ++t) c[t] = 0.0f;
-    if (type == T_Q4_K) {
-        const int bl = lane >> 2, p = lane & 3;
-        const bool ok = bl < gbk;
-        Q4kUnit un;
-        uint4 h = make_uint4(0, 0, 0, 0);
-        if (ok) {
-            const uint8_t* blk = pc + bl * 144;
-            h = *reinterpret_cast<const uint4*>(blk);
-            un.load(h, *reinterpret_cast<const uint4*>(blk + 16 + 32 * p), *reinterpret_cast<const uint4*>(blk + 32 + 32 * p), p);
-        }
-        const float dw = h2f((uint16_t)(h.x & 0xFFFFu)), dmw = h2f((uint16_t)(h.x >> 16));
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            int si = 0, mi = 0;
-            if (ok) un.dot(x[t].q[0], x[t].q[1], x[t].q[2], x[t].q[3], x[t].a0, si, mi);
-            si += __shfl_xor_sync(0xffffffffu, si, 1);
-            si += __shfl_xor_sync(0xffffffffu, si, 2);
-            mi += __shfl_xor_sync(0xffffffffu, mi, 1);
-            mi += __shfl_xor_sync(0xffffffffu, mi, 2);
-            if (ok && p == 0) {
-                const float dx = __uint_as_float(x[t].a1);
-                c[t] = __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
-            }
-        }
-    } else if (type == T_Q6_K) {
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int u = lane + 32 * k, bl = u >> 3, j = u & 7, hh = j >> 2, jj = j & 3;
-            const bool ok = bl < gbk;
-            Q6kUnit un;
-            float dw = 0.0f;
-            if (ok) {
-                const uint8_t* blk = pc + bl * 208;
-                un.load(*reinterpret_cast<const uint2*>(blk + 64 * hh + 8 * jj),
-                        *reinterpret_cast<const uint2*>(blk + 64 * hh + 32 + 8 * jj),
-                        *reinterpret_cast<const uint2*>(blk + 128 + 32 * hh + 8 * jj),
-                        *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh), jj);
-                dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 208 + 2 * bl));
-            }
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                int si = 0;
-                if (ok) {
-                    const uint4 qa = x[t].q[2 * k], qb = x[t].q[2 * k + 1];
-                    const uint2 xv[4] = {make_uint2(qa.x, qa.y), make_uint2(qa.z, qa.w), make_uint2(qb.x, qb.y),
-                                         make_uint2(qb.z, qb.w)};
-                    const int xs[4] = {x[t].xs[4 * k], x[t].xs[4 * k + 1], x[t].xs[4 * k + 2], x[t].xs[4 * k + 3]};
-                    si = un.dot(xv, xs);
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+}
+
+// Consumer prologue: build the activation image for T tokens.
+__device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32, float* s_scale,
+                             double* s_part) {
+    const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31;
+    const int K = args.K, T = args.T, n256 = xi.n256;
+    const GemvPro& pro = args.pro;
+    if (pro.mode == PRO_ACT) {
+        const ActQ& a = args.act;
+        for (int t = 0; t < T; ++t) {
+            if (wantk) {
+                for (int i = ct; i < n256 * 16; i += kConsumers * 32) {
+                    const int c = i >> 4, j = i & 15;
+                    const uint4 v =
+                        __ldg(reinterpret_cast<const uint4*>(a.qk + (size_t)t * a.ld + (size_t)c * 256 + 16 * j));
+                    *reinterpret_cast<uint4*>(xi.qk(t, c) + 16 * j) = v;
+                    xi.s16(t, c)[j] = (int16_t)sum16(v);
                 }
-                si += __shfl_xor_sync(0xffffffffu, si, 1);
-                si += __shfl_xor_sync(0xffffffffu, si, 2);
-                si += __shfl_xor_sync(0xffffffffu, si, 4);
-                if (ok && j == 0) c[t] += __fmul_rn(dw, __uint_as_float(k ? x[t].a1 : x[t].a0)) * (float)si;
+                for (int c = ct; c < n256; c += kConsumers * 32) {
+                    *reinterpret_cast<uint4*>(xi.bsk(t, c)) =
+                        __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)t * (K / 32) + (size_t)c * 8));
+                    *xi.dk(t, c) = __ldg(a.dk + (size_t)t * (K / 256) + c);
+                }
+            }
+            if (want32) {
+                for (int i = ct; i < K / 16; i += kConsumers * 32) {
+                    const int c = i >> 4, j = i & 15;
+                    *reinterpret_cast<uint4*>(xi.q32(t, c) + 16 * j) =
+                        __ldg(reinterpret_cast<const uint4*>(a.q32 + (size_t)t * a.ld + 16 * (size_t)i));
+                }
+                for (int b = ct; b < K / 32; b += kConsumers * 32)
+                    xi.d32(t, b >> 3)[b & 7] = __ldg(a.d32 + (size_t)t * (K / 32) + b);
             }
         }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int bl = lane + 32 * k;
-            if (bl < gbk) {
-                const uint4 w0 = *reinterpret_cast<const uint4*>(pc + bl * 32);
-                const uint4 w1 = *reinterpret_cast<const uint4*>(pc + bl * 32 + 16);
-                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 32 + 2 * bl));
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    c[t] += __fmul_rn(dw, __uint_as_float(k ? x[t].a1 : x[t].a0)) *
-                            (float)q80_dot(w0, w1, x[t].q[2 * k], x[t].q[2 * k + 1]);
+        return;
+    }
+    if (pro.mode == PRO_NORM) {
+        // the reference's double sum (src/ops.cpp:18-23) in the exact order of
+        // k_rmsnorm_quant: 128 threads, float4 strides, warp trees, 4 partials
+        const int grp = ct >> 7, gt = ct & 127;
+        for (int t0 = 0; t0 < T; t0 += 2) {
+            const int t = t0 + grp;
+            if (t < T) {
+                const float* xr = pro.src + (size_t)t * pro.ld;
+                double s = 0.0;
+                for (int i = gt * 4; i < K; i += 128 * 4) {
+                    const float4 f = *reinterpret_cast<const float4*>(xr + i);
+                    s += (double)f.x * f.x + (double)f.y * f.y + (double)f.z * f.z + (double)f.w * f.w;
+                }
+                s = warp_sum_d(s);
+                if (lane == 0) s_part[grp * 4 + (gt >> 5)] = s;
             }
+            consumers_sync();
+            if (t < T && gt == 0) {
+                double tot = 0.0;
+                for (int i = 0; i < 4; ++i) tot += s_part[grp * 4 + i];
+                s_scale[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / K), pro.eps)));
+            }
+            consumers_sync();
+        }
+    }
+    const int n_chunks = (K + 255) / 256;
+    for (int t = 0; t < T; ++t) {
+        for (int c = warp; c < n_chunks; c += kConsumers) {
+            const int i0 = c * 256 + 8 * lane;
+            float v[8];
+            if (pro.mode == PRO_NORM) {
+                ld8(pro.src + (size_t)t * pro.ld, i0, K, v);
+                const float sc = s_scale[t];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(v[i], sc), pro.w[i0 + i]) : 0.0f;
+            } else if (pro.mode == PRO_SILU) {
+                float gv[8], uv[8];
+                ld8(pro.src + (size_t)t * pro.ld, i0, K, gv);
+                ld8(pro.src2 + (size_t)t * pro.ld2, i0, K, uv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i]))), uv[i]);
+            } else {
+                ld8(pro.src + (size_t)t * pro.ld, i0, K, v);
+            }
+            ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
         }
     }
 }
 
-struct BulkJobs {
-    // tiles of 8 rows; segment s owns tiles [tile0[s], tile0[s+1])
-    int tile0[kMaxSeg + 1];
-    int n_groups;       // 2048-value groups per row
-    int stages;         // ring slots (<= kMaxStages)
-    int piece;          // bytes per row piece in a slot (largest group of the launch's types)
-    int tiles_per_cta;  // <= kMaxTiles
-    int* err;           // device error flag (nullable)
-};
-
-constexpr int kMaxTiles = 16;   // tiles one CTA accumulates in shared memory (x NT <= 16)
-
-__device__ __forceinline__ int seg_of(const GemvArgs& args, const BulkJobs& jobs, int tile) {
-    int s = 0;
-    while (s < args.nseg - 1 && tile >= jobs.tile0[s + 1]) ++s;
-    return s;
-}
-
-// CTA c owns tiles [c*tpc, (c+1)*tpc) and walks them group-major: for every
-// 2048-value group gi, all its tiles' 8-row pieces stream through the ring
-// (stage = one tile x one group), so each lane's activation chunk for gi is
-// loaded once into registers. Per-lane float partials accumulate in shared
-// memory across groups; a warp reduction per row happens once at the end.
 template <int NT>
-__global__ void __launch_bounds__(32 * (kBulkConsumers + 1)) k_gemv_stream(GemvArgs args, BulkJobs jobs) {
+__global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ volatile int s_abort;
-    const int S = jobs.stages, piece = jobs.piece, stage_bytes = jobs.piece * kBulkRows;
+    pdl_trigger();
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
-    float* accs = reinterpret_cast<float*>(smem + kBulkHeader);   // [consumer warp][tile][lane][NT]
-    uint8_t* stage_mem = smem + kBulkHeader + (size_t)kBulkConsumers * kMaxTiles * 32 * sizeof(float);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tiles = jobs.tile0[args.nseg];
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8);
+    float* s_scale = reinterpret_cast<float*>(smem + 2 * kMaxStages * 8 + 16);   // [4]
+    __shared__ double s_part[8];
+    __shared__ GemvSeg s_seg[kMaxSeg];
+    __shared__ int s_tile0[kMaxSeg + 1];
+    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages;
+    int n_tiles = jobs.tile0[0];
+#pragma unroll
+    for (int i = 1; i <= kMaxSeg; ++i)
+        if (i == args.nseg) n_tiles = jobs.tile0[i];
     const int t_begin = blockIdx.x * jobs.tiles_per_cta;
     const int t_end = min(n_tiles, t_begin + jobs.tiles_per_cta);
-    const int G = jobs.n_groups;
+    const int n_stages = (t_end - t_begin) * G;
+    XImage xi;
+    xi.base = smem + kHdrBytes;
+    xi.n256 = (K + 255) / 256;
+    xi.xk = jobs.xk_bytes;
+    xi.x32 = jobs.x32_bytes;
+    xi.T = T;
+    float* part = reinterpret_cast<float*>(xi.base + (size_t)T * (jobs.xk_bytes + jobs.x32_bytes));
+    uint8_t* ring = reinterpret_cast<uint8_t*>(part) +
+                    (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < kMaxSeg; ++i)
+        if (threadIdx.x == i) s_seg[i] = args.seg[i];
+#pragma unroll
+    for (int i = 0; i <= kMaxSeg; ++i)
+        if (threadIdx.x == i) s_tile0[i] = jobs.tile0[i];
     if (threadIdx.x == 0) {
-        s_abort = 0;
+        *s_abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kBulkConsumers);
+            mbar_init(&empty[s], 2);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
-    if (warp == kBulkConsumers) {
+    if (warp == kConsumers) {   // producer
         if (lane == 0) {
-            int it = 0, slot = 0, round = 0;
-            bool failed = false;
-            for (int gi = 0; gi < G && !failed; ++gi) {
-                for (int tile = t_begin; tile < t_end; ++tile) {
-                    const int s = seg_of(args, jobs, tile);
-                    const GemvSeg& g = args.seg[s];
-                    const int r0 = (tile - jobs.tile0[s]) * kBulkRows;
-                    const int nr = min(kBulkRows, g.rows - r0);
-                    const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
-                    const int nb = row_blocks(g.type, args.K);
-                    if (s_abort || (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1))) {
-                        if (jobs.err) atomicExch(jobs.err, 1);
-                        s_abort = 1;
-                        failed = true;
-                        break;
-                    }
-                    const uint32_t gb = (uint32_t)group_bytes(g.type, group_blocks(g.type, nb, gi));
-                    mbar_expect_tx(&full[slot], gb * nr);
-                    uint8_t* dst = stage_mem + (size_t)slot * stage_bytes;
-                    const uint8_t* src = base + (size_t)r0 * g.row_stride + group_offset(g.type, gi);
-                    for (int r = 0; r < nr; ++r) bulk_g2s(dst + (size_t)r * piece, src + (size_t)r * g.row_stride, gb, &full[slot]);
-                    ++it;
-                    if (++slot == S) { slot = 0; ++round; }
+            if (jobs.wait_first) pdl_wait();
+            int issued = 0;
+            bool ok = true;
+            for (int s = 0; s < n_stages; ++s) {
+                const int tile = t_begin + s / G, gi = s % G;
+                const int sg = seg_index(s_tile0, args.nseg, tile);
+                const GemvSeg& g = s_seg[sg];
+                const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
+                const int nb = row_blocks(g.type, K);
+                const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
+                const int slot = s % S;
+                if (s >= S && !mbar_wait(&empty[slot], (uint32_t)((s / S - 1) & 1), s_abort)) { ok = false; break; }
+                const uint8_t* src = base + (size_t)(tile - s_tile0[sg]) * kTileRows * g.row_stride +
+                                     (size_t)kTileRows * group_offset(g.type, gi);
+                if (bytes <= (uint32_t)jobs.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, jobs.err)) {
+                    mbar_expect_tx(&full[slot], bytes);
+                    bulk_g2s(ring + (size_t)slot * jobs.slot_bytes, src, bytes, &full[slot]);
+                } else {
+                    mbar_arrive(&full[slot]);   // keep the ring moving; the stage holds stale bytes
                 }
+                ++issued;
             }
-            if (failed)
-                for (int k = max(0, it - S); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
+            if (!ok) {
+                if (jobs.err) atomicExch(jobs.err, 1);
+                *s_abort = 1;
+                // let the copies in flight land before the CTA can exit
+                for (int k = max(0, issued - S); k < issued; ++k) mbar_wait_bounded(&full[k % S], (uint32_t)((k / S) & 1));
+            }
         }
         return;
     }
 
-    float* myacc = accs + (size_t)warp * kMaxTiles * 32;
-    for (int i = lane; i < kMaxTiles * 32; i += 32) myacc[i] = 0.0f;
-    int slot = 0, round = 0;
-    int cur_type = -1, cur_gi = -1;
-    XRegs x[NT];
-    for (int gi = 0; gi < G; ++gi) {
-        for (int tile = t_begin; tile < t_end; ++tile) {
-            const int s = seg_of(args, jobs, tile);
-            const GemvSeg& g = args.seg[s];
-            const int nb = row_blocks(g.type, args.K);
-            if (g.type != cur_type || gi != cur_gi) {
+    // consumers
+    pdl_wait();
+    const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
+    build_ximage(args, xi, wantk, want32, s_scale, s_part);
+    consumers_sync();
+    const int half = warp & 1, quarter = warp >> 1;
+    const int r8 = 4 * half + (lane >> 3), bl = lane & 7;
+    bool ok = true;
+    for (int s = quarter; s < n_stages; s += kConsumers / 2) {
+        const int tile = t_begin + s / G, gi = s % G;
+        const int type = s_seg[seg_index(s_tile0, args.nseg, tile)].type;
+        const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
+        const int piece = (int)group_bytes(type, gbk);
+        const int slot = s % S;
+        if (!mbar_wait(&full[slot], (uint32_t)((s / S) & 1), s_abort)) { ok = false; break; }
+        const uint8_t* pc = ring + (size_t)slot * jobs.slot_bytes + (size_t)r8 * piece;
+        float c[NT];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) load_x(g.type, args.act, t, gi, lane, nb, x[t]);
-                cur_type = g.type;
-                cur_gi = gi;
-            }
-            if (s_abort || !mbar_wait(&full[slot], round & 1)) {
-                if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
-                s_abort = 1;
-                return;
-            }
-            const int row = (tile - jobs.tile0[s]) * kBulkRows + warp;
-            if (row < g.rows) {
-                float c[NT];
-                piece_dot<NT>(g.type, stage_mem + (size_t)slot * stage_bytes + (size_t)warp * piece,
-                              group_blocks(g.type, nb, gi), lane, x, c);
-                // per-lane partial of (local tile, token): slot (tile - t_begin) * NT + t
-                float* a = myacc + (size_t)(tile - t_begin) * NT * 32 + lane;
+        for (int t = 0; t < NT; ++t) c[t] = 0.0f;
+        if (type == T_Q4_K) {
+            if (bl < gbk) {
+                uint4 w[9];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) a[t * 32] += c[t];
+                for (int i = 0; i < 9; ++i) w[i] = *reinterpret_cast<const uint4*>(pc + bl * 144 + 16 * i);
+                const float dw = h2f((uint16_t)(w[0].x & 0xFFFFu)), dmw = h2f((uint16_t)(w[0].x >> 16));
+                const int kb = gi * 8 + bl;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    int si, mi;
+                    q4k_block<LdShared>(w, xi.qk(t, kb), *reinterpret_cast<const uint4*>(xi.bsk(t, kb)), si, mi);
+                    const float dx = *xi.dk(t, kb);
+                    c[t] = __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (++slot == S) { slot = 0; ++round; }
+        } else if (type == T_Q6_K) {
+            if (bl < gbk) {
+                uint4 w[13];
+#pragma unroll
+                for (int i = 0; i < 13; ++i) w[i] = *reinterpret_cast<const uint4*>(pc + bl * 208 + 16 * i);
+                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 208 + 2 * bl));
+                const int kb = gi * 8 + bl;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    const int si = q6k_block<LdShared>(w, xi.qk(t, kb), xi.s16(t, kb));
+                    c[t] = __fmul_rn(dw, *xi.dk(t, kb)) * (float)si;
+                }
+            }
+        } else {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group
+            const int kc = gi * 8 + bl;
+            for (int i = 0; i < 8; ++i) {
+                const int b = 8 * bl + i;
+                if (b >= gbk) break;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(pc + 32 * b);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(pc + 32 * b + 16);
+                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 32 + 2 * b));
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    const int sv = q80_block<LdShared>(w0, w1, xi.q32(t, kc) + 32 * i);
+                    c[t] += __fmul_rn(dw, xi.d32(t, kc)[i]) * (float)sv;
+                }
+            }
         }
-    }
-    for (int tile = t_begin; tile < t_end; ++tile) {
-        const int s = seg_of(args, jobs, tile);
-        const GemvSeg& g = args.seg[s];
-        const int row = (tile - jobs.tile0[s]) * kBulkRows + warp;
-        const float* a = myacc + (size_t)(tile - t_begin) * NT * 32 + lane;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            const float v = warp_sum(a[t * 32]);
-            if (row < g.rows && lane == 0 && t < args.T) store_out(g, row, t, v);
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 1);
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 2);
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 4);
+        }
+        if (bl == 0) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) part[((size_t)s * kTileRows + r8) * NT + t] = c[t];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (!ok) {
+        if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
+        *s_abort = 1;
+    }
+    consumers_sync();
+    if (*s_abort) return;
+    // rows of this CTA: sum the group partials in group order
+    const int n_rows = (t_end - t_begin) * kTileRows;
+    for (int idx = threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
+        const int tl = idx / kTileRows, rr = idx % kTileRows, tile = t_begin + tl;
+        const int sg = seg_index(s_tile0, args.nseg, tile);
+        const GemvSeg& g = s_seg[sg];
+        const int row = (tile - s_tile0[sg]) * kTileRows + rr;
+        if (row >= g.rows) continue;
+        for (int t = 0; t < T; ++t) {
+            float v = 0.0f;
+            for (int gi = 0; gi < G; ++gi) v += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
+            store_out(g, row, t, v);
         }
     }
 }
@@ -590,77 +723,118 @@ extern "C" int* fbk_gemv_error_flag() {
     return g_err;
 }
 
+extern "C" int fbk_take_error_flag() {
+    if (!g_err) return 0;
+    int v = 0;
+    if (cudaMemcpy(&v, g_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v) cudaMemset(g_err, 0, sizeof(int));
+    return v;
+}
+
 static int env_or(const char* name, int def) {
     const char* v = getenv(name);
     return v && *v ? atoi(v) : def;
 }
 
-// Pipeline geometry: the shared-memory budget per CTA (default 100 KB, two
-// CTAs per SM) sets the ring depth; each CTA owns up to 16/NT tiles, and the
-// grid aims at >= 2 CTAs per SM. Tunable for sweeps via FISH_GEMV_SMEM_KB and
-// FISH_GEMV_CTA_PER_SM.
+// Pipeline geometry: CTAs per SM (default 2) split the SM's shared memory;
+// after the activation image and the row partials, the rest is ring slots.
 template <int NT>
 static int launch_stream(const GemvArgs* a, cudaStream_t st) {
-    static const int budget = std::max(48, std::min(220, env_or("FISH_GEMV_SMEM_KB", 100))) * 1024;
-    static const int want_cps = std::max(1, std::min(8, env_or("FISH_GEMV_CTA_PER_SM", 2)));
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_stream<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess)
+    static const int want_cps = std::max(1, std::min(4, env_or("FISH_GEMV_CTA_PER_SM", 2)));
+    static int max_smem = 0;   // dynamic shared memory one CTA may take
+    if (!max_smem) {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, k_gemv_stream<NT>) != cudaSuccess) return (int)cudaGetLastError();
+        const int dyn = optin - (int)fa.sharedSizeBytes;
+        if (dyn <= 0) return (int)cudaErrorInvalidValue;
+        if (cudaFuncSetAttribute(k_gemv_stream<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
             return (int)cudaGetLastError();
-        attr = true;
+        max_smem = dyn;
     }
-    BulkJobs jobs{};
-    int piece = 0;
-    for (int s = 0; s < a->nseg; ++s)
-        piece = std::max(piece, (int)group_bytes(a->seg[s].type, blocks_per_group(a->seg[s].type)));
-    const int acc_bytes = kBulkConsumers * kMaxTiles * 32 * (int)sizeof(float);
-    jobs.piece = piece;
-    jobs.stages = std::min(kMaxStages, (budget - kBulkHeader - acc_bytes) / (piece * kBulkRows));
-    if (jobs.stages < 2) return (int)cudaErrorInvalidValue;
+    StreamJobs jobs{};
+    bool wantk = false, want32 = false;
+    int slot = 0;
+    for (int s = 0; s < a->nseg; ++s) {
+        const int t = a->seg[s].type;
+        slot = std::max(slot, kTileRows * (int)group_bytes(t, blocks_per_group(t)));
+        if (t == T_Q8_0) want32 = true; else wantk = true;
+        if (a->seg[s].expert) jobs.wait_first = 1;
+    }
+    jobs.slot_bytes = slot;
+    jobs.xk_bytes = wantk ? ximg_k_bytes(a->K) : 0;
+    jobs.x32_bytes = want32 ? ximg_32_bytes(a->K) : 0;
     jobs.tile0[0] = 0;
-    for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kBulkRows - 1) / kBulkRows;
+    for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kTileRows - 1) / kTileRows;
     for (int s = a->nseg; s < kMaxSeg; ++s) jobs.tile0[s + 1] = jobs.tile0[s];
-    jobs.n_groups = (a->K + kGroupValues - 1) / kGroupValues;
+    jobs.n_groups = row_groups(a->seg[0].type, a->K);
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
-    const int target = num_sms() * want_cps;
-    jobs.tiles_per_cta = std::max(1, std::min(kMaxTiles / NT, (n_tiles + target - 1) / target));
-    const int ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
-    const size_t smem = (size_t)kBulkHeader + acc_bytes + (size_t)jobs.stages * piece * kBulkRows;
-    k_gemv_stream<NT><<<ctas, 32 * (kBulkConsumers + 1), smem, st>>>(*a, jobs);
-    return (int)cudaGetLastError();
+    const size_t xbytes = (size_t)a->T * (jobs.xk_bytes + jobs.x32_bytes);
+    int ctas = 0, stages = 0;
+    size_t smem = 0;
+    for (int cps = NT == 1 ? want_cps : 1;; --cps) {
+        const int budget = max_smem / cps - 2048;
+        ctas = std::min(n_tiles, num_sms() * cps);
+        jobs.tiles_per_cta = (n_tiles + ctas - 1) / ctas;
+        ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
+        const size_t part = ((size_t)jobs.tiles_per_cta * jobs.n_groups * kTileRows * NT * 4 + 127) / 128 * 128;
+        const long long left = (long long)budget - kHdrBytes - (long long)xbytes - (long long)part;
+        stages = (int)std::min<long long>(kMaxStages, left > 0 ? left / slot : 0);
+        smem = kHdrBytes + xbytes + part + (size_t)stages * slot;
+        if (stages >= 3 || cps == 1) break;
+    }
+    if (stages < 2) return (int)cudaErrorInvalidValue;
+    jobs.stages = stages;
+    return (int)fbk_launch(k_gemv_stream<NT>, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
+}
+
+extern "C" int fbk_gemv_streamable(const GemvArgs* a) {
+    if (a->T <= 0 || a->T > 4 || a->nseg <= 0) return 0;
+    const int g0 = row_groups(a->seg[0].type, a->K);
+    for (int s = 0; s < a->nseg; ++s) {
+        const int t = a->seg[s].type;
+        if (!is_tiled(t)) return 0;
+        if (row_groups(t, a->K) != g0) return 0;
+        if ((t == T_Q4_K || t == T_Q6_K) && a->K % 256) return 0;
+    }
+    if (a->K % 8) return 0;
+    static const bool stream_off = getenv("FISH_GEMV_DIRECT") != nullptr;
+    return stream_off && a->pro.mode == PRO_ACT ? 0 : 1;
 }
 
 extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
     if (a->T <= 0 || a->nseg <= 0) return 0;
     if (a->T > 8) return (int)cudaErrorInvalidValue;
-    bool quant = true;
-    for (int s = 0; s < a->nseg; ++s) {
-        const int t = a->seg[s].type;
-        quant = quant && (t == T_Q4_K || t == T_Q6_K || t == T_Q8_0);
-    }
-    static const bool stream_off = getenv("FISH_GEMV_DIRECT") != nullptr;
-    if (quant && !stream_off && a->T <= 4) {
+    if (fbk_gemv_streamable(a)) {
         if (a->T == 1) return launch_stream<1>(a, st);
         if (a->T == 2) return launch_stream<2>(a, st);
         return launch_stream<4>(a, st);
     }
-    int total = 0;
-    for (int s = 0; s < a->nseg; ++s) total += a->seg[s].rows;
-    int ctas = (total + 7) / 8;
+    if (a->pro.mode != PRO_ACT) return (int)cudaErrorInvalidValue;
+    GemvArgs ad = *a;
+    if (!ad.err) ad.err = fbk_gemv_error_flag();
+    a = &ad;
+    int items = 0;
+    for (int s = 0; s < a->nseg; ++s) items += is_tiled(a->seg[s].type) ? (a->seg[s].rows + 3) / 4 : a->seg[s].rows;
+    int ctas = (items + 7) / 8;
     const int cap = num_sms() * 8;
     if (ctas > cap) ctas = cap;
     if (ctas < 1) ctas = 1;
-    if (a->T == 1) k_gemv<1><<<ctas, 256, 0, st>>>(*a);
-    else if (a->T == 2) k_gemv<2><<<ctas, 256, 0, st>>>(*a);
-    else if (a->T <= 4) k_gemv<4><<<ctas, 256, 0, st>>>(*a);
-    else k_gemv<8><<<ctas, 256, 0, st>>>(*a);
-    return (int)cudaGetLastError();
+    cudaError_t e;
+    if (a->T == 1) e = fbk_launch(k_gemv_direct<1>, dim3(ctas), dim3(256), 0, st, *a);
+    else if (a->T == 2) e = fbk_launch(k_gemv_direct<2>, dim3(ctas), dim3(256), 0, st, *a);
+    else if (a->T <= 4) e = fbk_launch(k_gemv_direct<4>, dim3(ctas), dim3(256), 0, st, *a);
+    else e = fbk_launch(k_gemv_direct<8>, dim3(ctas), dim3(256), 0, st, *a);
+    return (int)e;
 }
 
-extern "C" int fbk_block_sums(int type, const uint8_t* w, size_t stride, int rows, int K, const ActQ* a,
-                              int32_t* sumi, int32_t* mins, cudaStream_t st) {
-    const int ctas = (rows + 7) / 8;
-    k_block_sums<<<ctas, 256, 0, st>>>(type, w, stride, rows, K, *a, sumi, mins);
+extern "C" int fbk_block_sums(int type, const uint8_t* w, int rows, int K, const ActQ* a, int32_t* sumi, int32_t* mins,
+                              cudaStream_t st) {
+    const long long n = (long long)rows * row_blocks(type, K);
+    const int ctas = (int)((n + 255) / 256);
+    k_block_sums<<<ctas, 256, 0, st>>>(type, w, rows, K, *a, sumi, mins);
     return (int)cudaGetLastError();
 }

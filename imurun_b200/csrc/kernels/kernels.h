@@ -10,23 +10,21 @@
 
 namespace fb {
 
-// Device weight layouts (a bijective repack of the GGUF blocks so that every
-// row starts 16-byte aligned and every load is 8 or 16 bytes):
-//   Q4_K  row = nb x 144 B blocks, unchanged (144 = 9 x 16)
-//   Q6_K  row = nb x 208 B (ql 128 | qh 64 | scales 16) then nb x fp16 d,
-//         padded to 16 B
-//   Q8_0  row = nb x 32 B qs then nb x fp16 d, padded to 16 B
-//   F32 / F16  row = n_in values, padded to 16 B
+// Device weight layouts (layout.cuh): quantised matrices are tile-major
+// (8-row tiles, inside a tile group pieces ordered group first), F32/F16
+// matrices row-major with rows padded to 16 bytes.
 size_t dev_row_bytes(int type, int n_in);
-// Repack one GGUF row (src) into the device layout (dst, dev_row_bytes wide).
-void repack_row(int type, const uint8_t* src, uint8_t* dst, int n_in);
+size_t dev_matrix_bytes(int type, int n_in, int rows);
+// Repack `rows` consecutive GGUF rows (the first one starting a tile) into
+// the device layout at dst (dev_matrix_bytes(type, n_in, rows) bytes).
+void repack_rows(int type, const uint8_t* src, int rows, int n_in, uint8_t* dst);
 
 // Epilogue of a GEMV segment.
 enum : int { EPI_STORE = 0, EPI_ADD = 1 };
 
 struct GemvSeg {
     int type;
-    const uint8_t* w;       // device rows (dev_row_bytes stride)
+    const uint8_t* w;       // device matrix (tile-major for quantised types)
     size_t row_stride;
     int rows;               // output rows in this segment
     float* y;               // output [T][ldy]
@@ -35,9 +33,26 @@ struct GemvSeg {
     int epi;                // EPI_STORE / EPI_ADD
     const int32_t* expert;  // optional: rows start at w + (*expert) * expert_bytes
     size_t expert_bytes;
+    size_t w_bytes;         // bytes readable from w (every expert); reads outside are skipped and flagged
 };
 
 constexpr int kMaxSeg = 4;
+
+// Prologue of the streamed GEMV: where its int8 activations come from.
+//   PRO_ACT    quantised planes already in global memory (GemvArgs::act)
+//   PRO_NORM   RMSNorm of f32 rows src (weights w, eps), then quantised
+//   PRO_QUANT  f32 rows src, quantised
+//   PRO_SILU   silu(src) * src2, quantised
+enum : int { PRO_ACT = 0, PRO_NORM = 1, PRO_QUANT = 2, PRO_SILU = 3 };
+struct GemvPro {
+    int mode;
+    const float* src;
+    int ld;
+    const float* src2;
+    int ld2;
+    const float* w;
+    float eps;
+};
 
 struct GemvArgs {
     GemvSeg seg[kMaxSeg];
@@ -47,6 +62,8 @@ struct GemvArgs {
     ActQ act;               // quantised activations (per type layout)
     const float* xf;        // f32 activations [T][ldxf] for F32/F16 weights
     int ldxf;
+    GemvPro pro;            // streamed kernel only (T <= 4, quantised segments)
+    int* err;               // device error flag (nullable): 3 = weight read out of range
 };
 
 }  // namespace fb
@@ -58,14 +75,24 @@ int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T,
 int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                        const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);
-// Debug: per-(row, block) integer sums of one quantised row set (bit-exact
+// 1 if fbk_gemv runs this call on the streamed kernel (the only one that
+// takes a prologue other than PRO_ACT).
+int fbk_gemv_streamable(const fb::GemvArgs* args);
+// Debug: per-(row, block) integer sums of one quantised matrix (bit-exact
 // check of the GEMV's integer arithmetic). sumi/mins: [rows][nblocks].
-int fbk_block_sums(int type, const uint8_t* w, size_t row_stride, int rows, int K, const fb::ActQ* a,
-                   int32_t* sumi, int32_t* mins, cudaStream_t st);
+int fbk_block_sums(int type, const uint8_t* w, int rows, int K, const fb::ActQ* a, int32_t* sumi, int32_t* mins,
+                   cudaStream_t st);
+// Programmatic dependent launch for every kernel launched after this call
+// (in-order streams and graphs captured from them).
+void fbk_set_pdl(int on);
+int fbk_pdl_enabled(void);
 
 // Embedding row gather + dequantisation: x[t][0..E) = dequant(embd row ids[t]).
-int fbk_embed(int type, const uint8_t* w, size_t row_stride, int E, const int32_t* ids, int T, float* x, int ldx,
+int fbk_embed(int type, const uint8_t* w, int E, int n_rows, const int32_t* ids, int T, float* x, int ldx, int* err,
               cudaStream_t st);
+// Shared device error flag of the kernels (0 = none); read-and-clear.
+int* fbk_gemv_error_flag();
+int fbk_take_error_flag();
 
 // Paged KV cache as the kernels see it. A page holds `page_size` positions of
 // every layer: per layer a K block [HKV][page_size][D] then a V block of the
@@ -84,6 +111,8 @@ struct KvView {
     size_t layer_stride;     // elements per layer inside a page (2*HKV*P*D)
     size_t head_stride;      // elements per kv head block (P*D)
     int f16;
+    int n_pages;             // pages in the pool (page indices outside are clamped and flagged)
+    int* err;                // device error flag (nullable): 5 = page index out of range
 };
 // RoPE on q (in place) and k, then K/V stored at each token's position.
 int fbk_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,

@@ -1,24 +1,26 @@
 // misc.cu — embedding gather, residual add, argmax, MoE routing.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "layout.cuh"
 
 namespace fb {
 
-// Value i of a device-layout row, dequantised exactly like the reference's
-// dequant_row (src/quant.cpp:129-216): same float operations in the same order.
-__device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n, int i) {
+// Value i of row `row` of a device-layout matrix, dequantised exactly like the
+// reference's dequant_row (src/quant.cpp:129-216): same float operations in
+// the same order.
+__device__ __forceinline__ float dequant_at(int type, const uint8_t* w, int n, int row, int i) {
     switch (type) {
-        case T_F32: return reinterpret_cast<const float*>(row)[i];
-        case T_F16: return h2f(reinterpret_cast<const uint16_t*>(row)[i]);
+        case T_F32: return reinterpret_cast<const float*>(w + (size_t)row * (((size_t)n * 4 + 15) / 16 * 16))[i];
+        case T_F16: return h2f(reinterpret_cast<const uint16_t*>(w + (size_t)row * (((size_t)n * 2 + 15) / 16 * 16))[i]);
         case T_Q8_0: {
-            const int nb = n / 32, b = i / 32;
-            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q8_0, nb, b)));
-            return __fmul_rn(d, (float)reinterpret_cast<const int8_t*>(row + block_offset(T_Q8_0, b))[i % 32]);
+            const int b = i / 32;
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(w + dscale_offset_tm(T_Q8_0, n, row, b)));
+            return __fmul_rn(d, (float)reinterpret_cast<const int8_t*>(w + block_offset_tm(T_Q8_0, n, row, b))[i % 32]);
         }
         case T_Q4_K: {
             const int b = i / 256, r = i % 256, g = r / 32, l = r % 32;
-            const uint8_t* blk = row + (size_t)b * 144;
+            const uint8_t* blk = w + block_offset_tm(T_Q4_K, n, row, b);
             const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
             const float dm = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
             const uint8_t* s = blk + 4;
@@ -30,9 +32,9 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n,
             return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dm, (float)m));
         }
         case T_Q6_K: {
-            const int nb = n / 256, b = i / 256, r = i % 256, h = r / 128, rr = r % 128, quad = rr / 32, l = rr % 32;
-            const uint8_t* blk = row + block_offset(T_Q6_K, b);
-            const float d = h2f(*reinterpret_cast<const uint16_t*>(row + dscale_offset(T_Q6_K, nb, b)));
+            const int b = i / 256, r = i % 256, h = r / 128, rr = r % 128, quad = rr / 32, l = rr % 32;
+            const uint8_t* blk = w + block_offset_tm(T_Q6_K, n, row, b);
+            const float d = h2f(*reinterpret_cast<const uint16_t*>(w + dscale_offset_tm(T_Q6_K, n, row, b)));
             const uint8_t qlb = blk[64 * h + l + ((quad & 1) ? 32 : 0)];
             const int lo = quad < 2 ? (qlb & 0x0F) : (qlb >> 4);
             const int hi = (blk[128 + 32 * h + l] >> (2 * quad)) & 3;
@@ -44,20 +46,30 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* row, int n,
     }
 }
 
-__global__ void k_embed(int type, const uint8_t* __restrict__ w, size_t stride, int E, const int32_t* __restrict__ ids,
-                        float* __restrict__ x, int ldx) {
+__global__ void k_embed(int type, const uint8_t* __restrict__ w, int E, int n_rows, const int32_t* __restrict__ ids,
+                        float* __restrict__ x, int ldx, int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x;
-    const uint8_t* row = w + (size_t)ids[t] * stride;
-    for (int i = threadIdx.x; i < E; i += blockDim.x) x[(size_t)t * ldx + i] = dequant_at(type, row, E, i);
+    int row = ids[t];
+    if (row < 0 || row >= n_rows) {
+        if (err && threadIdx.x == 0) atomicExch(err, 4);
+        row = 0;
+    }
+    for (int i = threadIdx.x; i < E; i += blockDim.x) x[(size_t)t * ldx + i] = dequant_at(type, w, E, row, i);
 }
 
 __global__ void k_add(float* __restrict__ y, const float* __restrict__ x, size_t n) {
+    pdl_trigger();
+    pdl_wait();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         y[i] += x[i];
 }
 
 // First index of the maximum (strict '>' scan, src/model.cpp:1939-1946).
 __global__ void k_argmax(const float* __restrict__ x, int n, int ldx, int32_t* out) {
+    pdl_trigger();
+    pdl_wait();
     const float* r = x + (size_t)blockIdx.x * ldx;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -86,6 +98,8 @@ __global__ void k_argmax(const float* __restrict__ x, int n, int ldx, int32_t* o
 // (ties: lower expert first), renormalised when `norm` (src/model.cpp:1529-1550).
 __global__ void k_moe_route(const float* __restrict__ logits, int T, int NE, int K, int norm, int32_t* sel,
                             float* wsel) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     float p[256];
@@ -116,6 +130,8 @@ __global__ void k_moe_route(const float* __restrict__ logits, int T, int NE, int
 // Per-head RMSNorm in place (qk-norm, src/model.cpp:1714-1721 with
 // src/ops.cpp:18-23). One warp per (token, head).
 __global__ void k_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* __restrict__ w, float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (gw >= T * n_heads) return;
     float* r = x + (size_t)(gw / n_heads) * ldx + (size_t)(gw % n_heads) * D;
@@ -131,6 +147,8 @@ __global__ void k_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, con
 // ffn = sum_k w_k * d_k accumulated from zero, then x += ffn.
 __global__ void k_moe_combine(float* x, int ldx, const float* __restrict__ eo, const float* __restrict__ wsel, int T,
                               int K, int E) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < E; i += gridDim.x * blockDim.x) {
         float acc = 0.0f;
@@ -142,6 +160,8 @@ __global__ void k_moe_combine(float* x, int ldx, const float* __restrict__ eo, c
 // ids[0] = argmax(logits); out[*step] = ids[0]; ++*step; ++tok_pos[0].
 __global__ void k_greedy_advance(const float* __restrict__ x, int n, int32_t* ids, int32_t* tok_pos, int32_t* out,
                                  int32_t* step) {
+    pdl_trigger();
+    pdl_wait();
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -186,6 +206,10 @@ __global__ void k_delay(unsigned long long ns) {
 
 using namespace fb;
 
+static bool g_pdl = false;
+extern "C" void fbk_set_pdl(int on) { g_pdl = on != 0; }
+extern "C" int fbk_pdl_enabled(void) { return g_pdl ? 1 : 0; }
+
 extern "C" int fbk_delay(unsigned long long ns, cudaStream_t st) {
     k_delay<<<1, 1, 0, st>>>(ns);
     return (int)cudaGetLastError();
@@ -194,46 +218,39 @@ extern "C" int fbk_delay(unsigned long long ns, cudaStream_t st) {
 extern "C" int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st) {
     const int warps = T * n_heads;
     if (warps <= 0) return 0;
-    k_head_rmsnorm<<<(warps + 7) / 8, 256, 0, st>>>(x, ldx, T, n_heads, D, w, eps);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_head_rmsnorm, dim3((warps + 7) / 8), dim3(256), 0, st, x, ldx, T, n_heads, D, w, eps);
 }
 
 extern "C" int fbk_moe_combine(float* x, int ldx, const float* eo, const float* wsel, int T, int K, int E, cudaStream_t st) {
     if (T <= 0) return 0;
-    k_moe_combine<<<dim3((E + 255) / 256, T), 256, 0, st>>>(x, ldx, eo, wsel, T, K, E);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_moe_combine, dim3((E + 255) / 256, T), dim3(256), 0, st, x, ldx, eo, wsel, T, K, E);
 }
 
 extern "C" int fbk_greedy_advance(const float* logits, int V, int32_t* ids, int32_t* tok_pos, int32_t* out,
                                   int32_t* step, cudaStream_t st) {
-    k_greedy_advance<<<1, 1024, 0, st>>>(logits, V, ids, tok_pos, out, step);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_greedy_advance, dim3(1), dim3(1024), 0, st, logits, V, ids, tok_pos, out, step);
 }
 
-extern "C" int fbk_embed(int type, const uint8_t* w, size_t stride, int E, const int32_t* ids, int T, float* x, int ldx,
-                         cudaStream_t st) {
+extern "C" int fbk_embed(int type, const uint8_t* w, int E, int n_rows, const int32_t* ids, int T, float* x, int ldx,
+                         int* err, cudaStream_t st) {
     if (T <= 0) return 0;
-    k_embed<<<T, 256, 0, st>>>(type, w, stride, E, ids, x, ldx);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_embed, dim3(T), dim3(256), 0, st, type, w, E, n_rows, ids, x, ldx, err);
 }
 
 extern "C" int fbk_add(float* y, const float* x, size_t n, cudaStream_t st) {
     if (!n) return 0;
     const int ctas = (int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
-    k_add<<<ctas, 256, 0, st>>>(y, x, n);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_add, dim3(ctas), dim3(256), 0, st, y, x, n);
 }
 
 extern "C" int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st) {
     if (rows <= 0) return 0;
-    k_argmax<<<rows, 1024, 0, st>>>(x, n, ldx, out);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_argmax, dim3(rows), dim3(1024), 0, st, x, n, ldx, out);
 }
 
 extern "C" int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel,
                              cudaStream_t st) {
     if (T <= 0) return 0;
     if (NE > 256 || K > NE) return (int)cudaErrorInvalidValue;
-    k_moe_route<<<(T + 63) / 64, 64, 0, st>>>(logits, T, NE, K, norm, sel, wsel);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_moe_route, dim3((T + 63) / 64), dim3(64), 0, st, logits, T, NE, K, norm, sel, wsel);
 }

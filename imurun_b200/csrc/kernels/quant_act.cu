@@ -12,6 +12,7 @@
 // single decode token still spreads over K/1024 CTAs.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace fb {
 
@@ -94,6 +95,8 @@ __device__ __forceinline__ void load8(const float* src, int base, int lane, int 
 
 __global__ void __launch_bounds__(128) k_quantize_rows(const float* __restrict__ x, int ldx, int K, ActQ a, int want32,
                                                        int wantk) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y, lane = threadIdx.x & 31;
     const int c = blockIdx.x * kQWarps + (threadIdx.x >> 5);
     if (c * 256 >= K) return;
@@ -109,6 +112,8 @@ __global__ void __launch_bounds__(128) k_rmsnorm_quant(const float* __restrict__
                                                        const float* __restrict__ w, float eps, int K,
                                                        float* __restrict__ xb, int ldxb, ActQ a, int want32,
                                                        int wantk) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double part[kQWarps];
     __shared__ float s_scale;
     const int t = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -147,6 +152,8 @@ __global__ void __launch_bounds__(128) k_rmsnorm_quant(const float* __restrict__
 __global__ void __launch_bounds__(128) k_silu_mul_quant(const float* __restrict__ g, int ldg, const float* __restrict__ u,
                                                         int ldu, int F, float* __restrict__ h, int ldh, ActQ a,
                                                         int want32, int wantk) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y, lane = threadIdx.x & 31;
     const int c = blockIdx.x * kQWarps + (threadIdx.x >> 5);
     if (c * 256 >= F) return;
@@ -180,22 +187,21 @@ extern "C" int fbk_quantize_rows(const float* x, int ldx, int T, int K, const Ac
                                  cudaStream_t st) {
     if (T <= 0) return 0;
     if (K % 8 || ldx % 4) return (int)cudaErrorInvalidValue;
-    k_quantize_rows<<<qgrid(K, T), 32 * kQWarps, 0, st>>>(x, ldx, K, *a, want32, wantk);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_quantize_rows, qgrid(K, T), dim3(32 * kQWarps), 0, st, x, ldx, K, *a, want32, wantk);
 }
 
 extern "C" int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T, int K, float* xb,
                                  int ldxb, const ActQ* a, int want32, int wantk, cudaStream_t st) {
     if (T <= 0) return 0;
     if (K % 8 || ldx % 4) return (int)cudaErrorInvalidValue;
-    k_rmsnorm_quant<<<qgrid(K, T), 32 * kQWarps, 0, st>>>(x, ldx, w, eps, K, xb, ldxb, *a, want32, wantk);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_rmsnorm_quant, qgrid(K, T), dim3(32 * kQWarps), 0, st, x, ldx, w, eps, K, xb, ldxb, *a, want32,
+                           wantk);
 }
 
 extern "C" int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                                   const ActQ* a, int want32, int wantk, cudaStream_t st) {
     if (T <= 0) return 0;
     if (F % 8 || ldg % 4 || ldu % 4) return (int)cudaErrorInvalidValue;
-    k_silu_mul_quant<<<qgrid(F, T), 32 * kQWarps, 0, st>>>(g, ldg, u, ldu, F, h, ldh, *a, want32, wantk);
-    return (int)cudaGetLastError();
+    return (int)fbk_launch(k_silu_mul_quant, qgrid(F, T), dim3(32 * kQWarps), 0, st, g, ldg, u, ldu, F, h, ldh, *a, want32,
+                           wantk);
 }

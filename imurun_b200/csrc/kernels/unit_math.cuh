@@ -1,124 +1,147 @@
-// unit_math.cuh — integer arithmetic of one 32-value work unit, shared by every
-// GEMV variant so they all form exactly the reference's integer sums
-// (src/quant_x86.cpp:299-309, 346-382, 431-495).
+// unit_math.cuh — integer arithmetic of one weight block against one int8
+// activation block, shared by every GEMV variant and by the block-sum check so
+// they all form exactly the reference's integer sums
+// (src/quant_x86.cpp:299-309, 346-382, 431-495):
+//   Q4_K  sumi = sum_g sc_g sum_l q x      mins = sum_g m_g bsums_g
+//   Q6_K  sumi = sum_j sc_j sum_l (q6 - 32) x
+//   Q8_0  s    = sum_l w x
+// One thread owns a whole block, so each integer is complete in one register
+// and is converted to float once, as the reference does.
 #pragma once
 
 #include "common.cuh"
 
 namespace fb {
 
-__device__ __forceinline__ uint32_t q4k_byte(const uint4& h, int k) {
-    // bytes 4..15 of a Q4_K block (the packed 6-bit scales / mins) are h.y, h.z, h.w
-    const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
-    return (w >> (8 * (k & 3))) & 0xFFu;
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// 6-bit scale and min of sub-block g (src/quant.cpp:136-144).
-__device__ __forceinline__ void q4k_scale_min(const uint4& h, int g, int& sc, int& m) {
-    if (g < 4) {
-        sc = q4k_byte(h, g) & 63;
-        m = q4k_byte(h, g + 4) & 63;
-    } else {
-        sc = (q4k_byte(h, g + 4) & 0x0F) | ((q4k_byte(h, g - 4) >> 6) << 4);
-        m = (q4k_byte(h, g + 4) >> 4) | ((q4k_byte(h, g) >> 6) << 4);
-    }
-}
+__device__ __forceinline__ int byte_of(uint32_t v, int k) { return (int)((v >> (8 * k)) & 0xFFu); }
+// component k (a compile-time constant after unrolling) of a uint4
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
 
-// Scales and mins of sub-blocks 2p and 2p+1 at once (the same bit layout as
-// q4k_scale_min, src/quant.cpp:136-144), as byte pairs: low byte = sub-block
-// 2p, high byte = 2p+1. Branch-free so lanes with different p stay converged.
-__device__ __forceinline__ void q4k_scale_pair(const uint4& h, int p, int& sc0, int& sc1, int& m0, int& m1) {
-    const int sh = 16 * (p & 1);
-    const uint32_t ys = h.y >> sh, zs = h.z >> sh, ws = h.w >> sh;
-    const uint32_t sc_lo = ys & 0x3F3Fu, m_lo = zs & 0x3F3Fu;                                 // p < 2
-    const uint32_t sc_hi = (ws & 0x0F0Fu) | ((ys >> 2) & 0x3030u);                              // p >= 2
-    const uint32_t m_hi = ((ws >> 4) & 0x0F0Fu) | ((zs >> 2) & 0x3030u);
-    const uint32_t scp = p < 2 ? sc_lo : sc_hi, mp = p < 2 ? m_lo : m_hi;
-    sc0 = (int)(scp & 0xFFu);
-    sc1 = (int)((scp >> 8) & 0xFFu);
-    m0 = (int)(mp & 0xFFu);
-    m1 = (int)((mp >> 8) & 0xFFu);
-}
-
-// Q4_K unit = sub-block pair p of a block: header h (d, dmin, scales),
-// q0/q1 = qs bytes 32p .. 32p+31 (low nibbles sub-block 2p, high 2p+1),
-// x = the 64 activation int8 of sub-blocks 2p, 2p+1, bs = their two bsums.
-// si = sc_2p * sum q.x + sc_2p+1 * sum q.x;  mi = m_2p bs_2p + m_2p+1 bs_2p+1.
-struct Q4kUnit {
-    uint32_t lo[8], hi[8];
-    int sc0, sc1, m0, m1;
-    __device__ __forceinline__ void load(const uint4& h, const uint4& q0, const uint4& q1, int p) {
-        q4k_scale_pair(h, p, sc0, sc1, m0, m1);
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+// Q4_K block (144 B as 9 uint4: h = d | dmin | 12 scale bytes, then qs[128])
+// against activation block x (256 int8 as 16 uint4, through LD) and its eight
+// 32-value sums bs. Sub-block g's 6-bit scale and min follow
+// src/quant.cpp:136-144; qs[32p + l] holds sub-block 2p (low nibble) and
+// 2p+1 (high nibble) value l. The high nibbles enter dp4a unshifted (16 q),
+// and the sixteenfold sum is divided exactly once per block.
+template <class LD>
+__device__ __forceinline__ void q4k_block(const uint4 (&w)[9], const int8_t* x, uint4 bs, int& sumi, int& mins) {
+    const uint4 h = w[0];
+    const uint32_t sc_lo = h.y & 0x3F3F3F3Fu;                                  // sub-blocks 0..3
+    const uint32_t m_lo = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);   // sub-blocks 4..7
+    const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    int even = 0, odd16 = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            lo[i] = w[i] & 0x0F0F0F0Fu;
-            hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
-        }
-    }
-    __device__ __forceinline__ void dot(const uint4& x0, const uint4& x1, const uint4& x2, const uint4& x3, uint32_t bs,
-                                        int& si, int& mi) const {
+    for (int p = 0; p < 4; ++p) {
+        const uint4 qa = w[1 + 2 * p], qb = w[2 + 2 * p];
+        const uint4 x0 = LD::ld(x + 64 * p), x1 = LD::ld(x + 64 * p + 16);
+        const uint4 x2 = LD::ld(x + 64 * p + 32), x3 = LD::ld(x + 64 * p + 48);
         int s0 = 0, s1 = 0;
-        s0 = dp4a((int)lo[0], (int)x0.x, s0); s0 = dp4a((int)lo[1], (int)x0.y, s0);
-        s0 = dp4a((int)lo[2], (int)x0.z, s0); s0 = dp4a((int)lo[3], (int)x0.w, s0);
-        s0 = dp4a((int)lo[4], (int)x1.x, s0); s0 = dp4a((int)lo[5], (int)x1.y, s0);
-        s0 = dp4a((int)lo[6], (int)x1.z, s0); s0 = dp4a((int)lo[7], (int)x1.w, s0);
-        s1 = dp4a((int)hi[0], (int)x2.x, s1); s1 = dp4a((int)hi[1], (int)x2.y, s1);
-        s1 = dp4a((int)hi[2], (int)x2.z, s1); s1 = dp4a((int)hi[3], (int)x2.w, s1);
-        s1 = dp4a((int)hi[4], (int)x3.x, s1); s1 = dp4a((int)hi[5], (int)x3.y, s1);
-        s1 = dp4a((int)hi[6], (int)x3.z, s1); s1 = dp4a((int)hi[7], (int)x3.w, s1);
-        si = sc0 * s0 + sc1 * s1;
-        mi = m0 * (int)(int16_t)(bs & 0xFFFFu) + m1 * (int)(int16_t)(bs >> 16);
+        s0 = dp4a_us(qa.x & 0x0F0F0F0Fu, x0.x, s0); s0 = dp4a_us(qa.y & 0x0F0F0F0Fu, x0.y, s0);
+        s0 = dp4a_us(qa.z & 0x0F0F0F0Fu, x0.z, s0); s0 = dp4a_us(qa.w & 0x0F0F0F0Fu, x0.w, s0);
+        s0 = dp4a_us(qb.x & 0x0F0F0F0Fu, x1.x, s0); s0 = dp4a_us(qb.y & 0x0F0F0F0Fu, x1.y, s0);
+        s0 = dp4a_us(qb.z & 0x0F0F0F0Fu, x1.z, s0); s0 = dp4a_us(qb.w & 0x0F0F0F0Fu, x1.w, s0);
+        s1 = dp4a_us(qa.x & 0xF0F0F0F0u, x2.x, s1); s1 = dp4a_us(qa.y & 0xF0F0F0F0u, x2.y, s1);
+        s1 = dp4a_us(qa.z & 0xF0F0F0F0u, x2.z, s1); s1 = dp4a_us(qa.w & 0xF0F0F0F0u, x2.w, s1);
+        s1 = dp4a_us(qb.x & 0xF0F0F0F0u, x3.x, s1); s1 = dp4a_us(qb.y & 0xF0F0F0F0u, x3.y, s1);
+        s1 = dp4a_us(qb.z & 0xF0F0F0F0u, x3.z, s1); s1 = dp4a_us(qb.w & 0xF0F0F0F0u, x3.w, s1);
+        const uint32_t scv = p < 2 ? sc_lo : sc_hi;
+        const int k0 = (2 * p) & 3, k1 = (2 * p + 1) & 3;
+        even += byte_of(scv, k0) * s0;
+        odd16 += byte_of(scv, k1) * s1;
     }
-};
+    sumi = even + (odd16 >> 4);   // odd16 is an exact multiple of 16
+    const int b0 = (int)(int16_t)(bs.x & 0xFFFFu), b1 = (int)(int16_t)(bs.x >> 16);
+    const int b2 = (int)(int16_t)(bs.y & 0xFFFFu), b3 = (int)(int16_t)(bs.y >> 16);
+    const int b4 = (int)(int16_t)(bs.z & 0xFFFFu), b5 = (int)(int16_t)(bs.z >> 16);
+    const int b6 = (int)(int16_t)(bs.w & 0xFFFFu), b7 = (int)(int16_t)(bs.w >> 16);
+    mins = byte_of(m_lo, 0) * b0 + byte_of(m_lo, 1) * b1 + byte_of(m_lo, 2) * b2 + byte_of(m_lo, 3) * b3 +
+           byte_of(m_hi, 0) * b4 + byte_of(m_hi, 1) * b5 + byte_of(m_hi, 2) * b6 + byte_of(m_hi, 3) * b7;
+}
 
-// Q6_K unit j (0..7) of a block: half hh = j/4, values l0 = 8*(j%4) .. l0+7 of
-// each of the half's four 32-value quads (src/quant.cpp:194-216).
-// qa = ql[64hh + l0 ..+8] (quads 0, 2), qb = ql[64hh + 32 + l0 ..+8] (quads 1, 3),
-// qh = qh[32hh + l0 ..+8], sc = scales[8hh .. 8hh+8].
-// si = sum_q sc_q * sum (q6 - 32) x over the unit's four 8-value pieces,
-// formed as sum_q sc_q * (sum q6 x - 32 sum x): the same integer, with the
-// unsigned 6-bit codes fed to dp4a directly (they are < 128) and sum x, which
-// depends on the activations only, computed once per activation chunk.
-struct Q6kUnit {
-    uint32_t v[4][2];
-    int scq[4];
-    __device__ __forceinline__ void load(const uint2& qa, const uint2& qb, const uint2& qh, const uint2& sc, int jj) {
+// Q6_K block (208 B as 13 uint4: ql[128], qh[64], int8 scales[16]; the fp16 d
+// lives in the group's scale table) against x (256 int8) and xs16[j] = sum of
+// x over values 16j .. 16j+15. Value l (0..31) of quad q (0..3) of half hh:
+// ql nibble (ql[64hh + l + 32(q&1)], low for q < 2) | 2 bits of qh[32hh + l]
+// at 2q, scale sc[8hh + 2q + l/16] (src/quant.cpp:194-216). The unsigned
+// 6-bit codes go to dp4a as they are; sum (q6 - 32) x = sum q6 x - 32 sum x.
+template <class LD>
+__device__ __forceinline__ int q6k_block(const uint4 (&w)[13], const int8_t* x, const int16_t* xs16) {
+    const uint4 scw = w[12];
+    int sumi = 0, corr = 0;
 #pragma unroll
-        for (int w = 0; w < 2; ++w) {
-            const uint32_t a = w ? qa.y : qa.x, b = w ? qb.y : qb.x, h = w ? qh.y : qh.x;
-            v[0][w] = (a & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);
-            v[1][w] = (b & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);
-            v[2][w] = ((a >> 4) & 0x0F0F0F0Fu) | (h & 0x30303030u);
-            v[3][w] = ((b >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u);
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int hl = 0; hl < 2; ++hl) {   // values l in [16 hl, 16 hl + 16)
+            int s[4] = {0, 0, 0, 0};
+            const uint4 xa = LD::ld(x + 128 * hh + 16 * hl);        // quad 0
+            const uint4 xb = LD::ld(x + 128 * hh + 32 + 16 * hl);   // quad 1
+            const uint4 xc = LD::ld(x + 128 * hh + 64 + 16 * hl);   // quad 2
+            const uint4 xd = LD::ld(x + 128 * hh + 96 + 16 * hl);   // quad 3
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int wi = 4 * hl + i;
+                const uint32_t a = word_of(w[(16 * hh + wi) >> 2], wi & 3);
+                const uint32_t b = word_of(w[(16 * hh + 8 + wi) >> 2], wi & 3);
+                const uint32_t hb = word_of(w[8 + ((8 * hh + wi) >> 2)], wi & 3);
+                const uint32_t v0 = (a & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u);
+                const uint32_t v1 = (b & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u);
+                const uint32_t v2 = ((a >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u);
+                const uint32_t v3 = ((b >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u);
+                s[0] = dp4a_us(v0, word_of(xa, i), s[0]);
+                s[1] = dp4a_us(v1, word_of(xb, i), s[1]);
+                s[2] = dp4a_us(v2, word_of(xc, i), s[2]);
+                s[3] = dp4a_us(v3, word_of(xd, i), s[3]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int j = 8 * hh + 2 * q + hl;
+                const int sc = (int)(int8_t)byte_of(word_of(scw, j >> 2), j & 3);
+                sumi += sc * s[q];
+                corr += sc * (int)xs16[j];
+            }
         }
-        const uint32_t s = (jj >> 1) ? 8u : 0u;   // byte 2q + (l0 >= 16) of the half's 8 scales
-        scq[0] = (int)(int8_t)((sc.x >> s) & 0xFFu);
-        scq[1] = (int)(int8_t)((sc.x >> (16 + s)) & 0xFFu);
-        scq[2] = (int)(int8_t)((sc.y >> s) & 0xFFu);
-        scq[3] = (int)(int8_t)((sc.y >> (16 + s)) & 0xFFu);
     }
-    // x[q] = the 8 activation int8 of quad q, xs[q] = their sum
-    __device__ __forceinline__ int dot(const uint2 (&x)[4], const int (&xs)[4]) const {
-        int si = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            si += scq[q] * (dp4a((int)v[q][0], (int)x[q].x, dp4a((int)v[q][1], (int)x[q].y, 0)) - 32 * xs[q]);
-        return si;
-    }
-};
+    return sumi - 32 * corr;
+}
 
-// sum of the 8 int8 in x
-__device__ __forceinline__ int sum8(const uint2& x) { return dp4a((int)x.x, 0x01010101, dp4a((int)x.y, 0x01010101, 0)); }
-
-// Q8_0 unit = one block: s = sum w.x over 32 values.
-__device__ __forceinline__ int q80_dot(const uint4& w0, const uint4& w1, const uint4& x0, const uint4& x1) {
+// Q8_0 block (qs[32] as 2 uint4) against x (32 int8): s = sum w x.
+template <class LD>
+__device__ __forceinline__ int q80_block(uint4 w0, uint4 w1, const int8_t* x) {
+    const uint4 x0 = LD::ld(x), x1 = LD::ld(x + 16);
     int s = 0;
-    s = dp4a((int)w0.x, (int)x0.x, s); s = dp4a((int)w0.y, (int)x0.y, s);
-    s = dp4a((int)w0.z, (int)x0.z, s); s = dp4a((int)w0.w, (int)x0.w, s);
-    s = dp4a((int)w1.x, (int)x1.x, s); s = dp4a((int)w1.y, (int)x1.y, s);
-    s = dp4a((int)w1.z, (int)x1.z, s); s = dp4a((int)w1.w, (int)x1.w, s);
+    s = __dp4a((int)w0.x, (int)x0.x, s); s = __dp4a((int)w0.y, (int)x0.y, s);
+    s = __dp4a((int)w0.z, (int)x0.z, s); s = __dp4a((int)w0.w, (int)x0.w, s);
+    s = __dp4a((int)w1.x, (int)x1.x, s); s = __dp4a((int)w1.y, (int)x1.y, s);
+    s = __dp4a((int)w1.z, (int)x1.z, s); s = __dp4a((int)w1.w, (int)x1.w, s);
     return s;
 }
+
+// sum of the 16 int8 in x
+__device__ __forceinline__ int sum16(uint4 x) {
+    int s = __dp4a((int)x.x, 0x01010101, 0);
+    s = __dp4a((int)x.y, 0x01010101, s);
+    s = __dp4a((int)x.z, 0x01010101, s);
+    return __dp4a((int)x.w, 0x01010101, s);
+}
+
+// loaders: shared memory (plain), global weights (streaming, no L1
+// allocation), global activations (read-only cache)
+struct LdShared {
+    static __device__ __forceinline__ uint4 ld(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+};
+struct LdStream {
+    static __device__ __forceinline__ uint4 ld(const void* p) { return ldg_stream(p); }
+};
+struct LdGlobal {
+    static __device__ __forceinline__ uint4 ld(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+};
 
 }  // namespace fb
