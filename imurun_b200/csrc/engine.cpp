@@ -132,7 +132,7 @@ Engine::~Engine() {
     cudaFree(warena_);
     cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
     cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
-    cudaFree(act_mem_); cudaFree(att_scratch_);
+    cudaFree(act_mem_); cudaFree(att_scratch_); cudaFree(att_counters_);
     cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
@@ -492,8 +492,11 @@ bool Engine::alloc_buffers(std::string* err) {
     act_.ld = (int)ld;
     // attention scratch for att_chunk_ tokens per launch at the full context
     att_chunk_ = 64;
-    att_scratch_floats_ = fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx);
+    att_scratch_floats_ = std::max(fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx),
+                                   fbk_attention_decode_scratch_floats(kMaxBatch, c.n_head, c.head_dim, c.n_ctx, 0));
     CK(cudaMalloc(&att_scratch_, sizeof(float) * att_scratch_floats_));
+    CK(cudaMalloc(&att_counters_, sizeof(int) * kMaxBatch * c.n_head_kv));
+    CK(cudaMemset(att_counters_, 0, sizeof(int) * kMaxBatch * c.n_head_kv));
     CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
@@ -767,7 +770,7 @@ static ActQ act_row(const ActQ& a, int row, int K) {
 
 // ------------------------------------------------------------------ forward
 
-bool Engine::run_layers(int T, int max_ctx, std::string* err) {
+bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
     const Config& c = cfg_;
     const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim(), H = c.n_head, HKV = c.n_head_kv, D = c.head_dim;
     const float scale = 1.0f / std::sqrt((float)D);
@@ -793,6 +796,11 @@ bool Engine::run_layers(int T, int max_ctx, std::string* err) {
             CKP(PC_OTHER, 0, fbk_head_rmsnorm(q_, Q, T, H, D, L.q_norm, c.eps, stream_));
             CKP(PC_OTHER, 0, fbk_head_rmsnorm(k_, KV, T, HKV, D, L.k_norm, c.eps, stream_));
         }
+        if (distinct && !no_fuse_) {
+            CKP(PC_ATTN, 0, fbk_attention_decode(q_, Q, k_, v_, KV, T, H, HKV, D, scale, c.rot_dim, c.neox ? 1 : 0,
+                                                 rope_cos_, rope_sin_, kv, li, attn_, Q, att_scratch_,
+                                                 att_scratch_floats_, att_counters_, max_ctx, stream_));
+        } else {
         CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
                                         rope_sin_, kv, li, stream_));
         for (int t0 = 0; t0 < T; t0 += att_chunk_) {
@@ -802,6 +810,7 @@ bool Engine::run_layers(int T, int max_ctx, std::string* err) {
             kvc.tok_pos = tok_pos_ + t0;
             CKP(PC_ATTN, 0, fbk_attention(q_ + (size_t)t0 * Q, Q, nt, H, HKV, D, scale, kvc, li, attn_ + (size_t)t0 * Q, Q,
                                           att_scratch_, att_scratch_floats_, max_ctx, stream_));
+        }
         }
         a.K = Q;
         {
@@ -903,7 +912,7 @@ bool Engine::capture_graph(int key, std::string* err) {
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     std::string e2;
     bool ok = fbk_embed(embd_.type, embd_.d, cfg_.n_embd, embd_.n_out, ids_, T, x_, cfg_.n_embd, fbk_gemv_error_flag(), stream_) == 0;
-    ok = ok && run_layers(T, cfg_.n_ctx, &e2);
+    ok = ok && run_layers(T, cfg_.n_ctx, true, &e2);
     ok = ok && run_head(0, T, logits_, &e2);
     if (key == 0)
         ok = ok && fbk_greedy_advance(logits_, cfg_.vocab, ids_, tok_pos_, greedy_out_, greedy_step_, stream_) == 0;
@@ -950,7 +959,7 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
         CK(cudaGraphLaunch(graphs_[1], stream_));
     } else {
         CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, T, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
-        if (!run_layers(T, pos0 + T, err)) return false;
+        if (!run_layers(T, pos0 + T, T == 1, err)) return false;
         const int row0 = all ? 0 : T - 1;
         if (!run_head(row0, nrows, logits_, err)) return false;
         if (argmax) CKP(PC_OTHER, 0, fbk_argmax(logits_, c.vocab, nrows, c.vocab, argmax_, stream_));
@@ -985,7 +994,7 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
         int max_ctx = 0;
         for (int i = 0; i < n; ++i) max_ctx = std::max(max_ctx, pos[i] + 1);
         CK(fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, n, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
-        if (!run_layers(n, max_ctx, err)) return false;
+        if (!run_layers(n, max_ctx, true, err)) return false;
         if (!run_head(0, n, logits_, err)) return false;
         CK(fbk_argmax(logits_, c.vocab, n, c.vocab, argmax_, stream_));
     }

@@ -125,7 +125,9 @@ private:
     bool upload_weights(std::string* err);
     bool ensure_pages(int sid, int new_len, std::string* err);
     void write_page_table(int sid);
-    bool run_layers(int T, int max_ctx, std::string* err);
+    // distinct: the T tokens belong to T different sequences (decode steps),
+    // so attention can append each token's K/V inside the fused kernel
+    bool run_layers(int T, int max_ctx, bool distinct, std::string* err);
     bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err);
     bool gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi,
               const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr);
@@ -170,6 +172,7 @@ private:
     ActQ act_{};
     int8_t* act_mem_ = nullptr;
     float* att_scratch_ = nullptr;
+    int* att_counters_ = nullptr;   // [kMaxBatch][n_head_kv] split counters of the fused decode attention
     size_t att_scratch_floats_ = 0;
     int att_chunk_ = 32;
     int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;

@@ -10,6 +10,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "tma.cuh"
 
 namespace fb {
 
@@ -284,6 +285,318 @@ __global__ void k_attn_combine(const float* __restrict__ part, int H, int D, int
     }
 }
 
+
+// ================================================================ fused decode
+// Decode attention for T tokens of T distinct sequences, one kernel per layer:
+// RoPE of q and of the new k, the append of the new K/V row into the cache,
+// split-K attention over the cached keys and the merge of the splits.
+// CTA = (key split of KPS keys, kv head, token), 4 warps. The split's K and V
+// page blocks (16 positions x D each, contiguous in the paged layout) land in
+// shared memory by bulk copies; the CTA holding the token's own position
+// rotates and stores the new k/v and patches its shared copy. Warps take 32
+// keys each (lane = key for q.k, lane = a D-slice for p.V); the CTA merges
+// its warps and writes (max, sum, o[D]) per head; the last CTA of a
+// (token, kv head) to finish — an atomic counter, reset by that CTA — merges
+// the splits into the output. Arithmetic follows k_rope_append, k_attn_split
+// and k_attn_combine (src/ops.cpp:126-156, 303-356).
+constexpr int kDecWarps = 4;
+
+template <class E>
+__device__ __forceinline__ void ld_chunk(const E* p, float (&f)[8]);
+template <>
+__device__ __forceinline__ void ld_chunk<__half>(const __half* p, float (&f)[8]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 v = __half22float2(h[e]);
+        f[2 * e] = v.x;
+        f[2 * e + 1] = v.y;
+    }
+}
+template <>
+__device__ __forceinline__ void ld_chunk<float>(const float* p, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+__device__ __forceinline__ float to_store(float x, __half*) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float to_store(float x, float*) { return x; }
+__device__ __forceinline__ void put(__half* p, float x) { *p = __float2half_rn(x); }
+__device__ __forceinline__ void put(float* p, float x) { *p = x; }
+
+template <class E>
+__host__ __device__ constexpr int dec_kps() { return sizeof(E) == 2 ? 128 : 64; }
+
+// dynamic shared memory of k_attn_decode<E>
+template <class E>
+__host__ __device__ constexpr size_t dec_smem_bytes() {
+    return 16 + 2 * (size_t)dec_kps<E>() * kMaxD * sizeof(E) +
+           sizeof(float) * ((size_t)kMaxG * kMaxD + 2 * kDecWarps * kMaxG + (size_t)kDecWarps * kMaxG * kMaxD + 2 * kMaxD);
+}
+
+template <class E>
+__global__ void __launch_bounds__(32 * kDecWarps) k_attn_decode(
+    const float* __restrict__ q, int ldq, const float* __restrict__ knew, const float* __restrict__ vnew, int ldkv,
+    int H, int HKV, int D, float scale, int rot, int neox, const float* __restrict__ rcos,
+    const float* __restrict__ rsin, KvView kv, int layer, float* __restrict__ part, int n_splits,
+    int* __restrict__ counters, float* __restrict__ out, int ldo) {
+    constexpr int KPS = dec_kps<E>();
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_last;
+    __shared__ volatile int s_abort;
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.z, hk = blockIdx.y, sp = blockIdx.x, G = H / HKV;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos = kv.tok_pos[t], n_keys = pos + 1, j0 = sp * KPS;
+    if (j0 >= n_keys) return;
+    const int n_active = (n_keys + KPS - 1) / KPS, nk = min(KPS, n_keys - j0);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    E* sk = reinterpret_cast<E*>(smem + 16);
+    E* sv = sk + (size_t)KPS * kMaxD;
+    float* sq = reinterpret_cast<float*>(sv + (size_t)KPS * kMaxD);   // [G][D]
+    float* swm = sq + kMaxG * kMaxD;                                    // [warp][G]
+    float* swl = swm + kDecWarps * kMaxG;                               // [warp][G]
+    float* swo = swl + kDecWarps * kMaxG;                               // [warp][G][D]
+    float* snew = swo + kDecWarps * kMaxG * kMaxD;                     // [2][D]
+    const int seq = kv.tok_seq[t];
+    const int np = (nk + 15) / 16;
+    const size_t blk = (size_t)16 * D;   // elements of one page's block of this head
+    if (tid == 0) {
+        s_abort = 0;
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        mbar_expect_tx(bar, (uint32_t)(2 * np * blk * sizeof(E)));
+        for (int i = 0; i < np; ++i) {
+            int page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + i];
+            if (page < 0 || page >= kv.n_pages) {
+                if (kv.err) atomicExch(kv.err, 5);
+                page = 0;
+            }
+            const size_t off = (size_t)page * kv.page_stride + (size_t)layer * kv.layer_stride + (size_t)hk * kv.head_stride;
+            bulk_g2s(sk + i * blk, reinterpret_cast<const E*>(kv.k) + off, (uint32_t)(blk * sizeof(E)), bar);
+            bulk_g2s(sv + i * blk, reinterpret_cast<const E*>(kv.v) + off, (uint32_t)(blk * sizeof(E)), bar);
+        }
+    }
+    // q heads of this kv head, rotated (biases and q-norm were applied upstream)
+    const int half = rot / 2;
+    const float* c = rcos + (size_t)pos * half;
+    const float* s = rsin + (size_t)pos * half;
+    const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
+    for (int idx = tid; idx < G * (D / 2); idx += 32 * kDecWarps) {
+        const int g = idx / (D / 2), i = idx % (D / 2);
+        const float* hv = qr + (size_t)g * D;
+        if (i < half) {
+            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            const float x0 = hv[a], x1 = hv[b];
+            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
+            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+        } else {
+            sq[g * kMaxD + 2 * i] = hv[2 * i];
+            sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
+        }
+    }
+    // the token's own position: rotate k, store k and v, keep their stored values
+    const bool own = pos >= j0 && pos < j0 + KPS;
+    if (own) {
+        const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
+        const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
+        const size_t base = kv_off(kv, layer, hk, t, pos);
+        E* kp = reinterpret_cast<E*>(kv.k) + base;
+        E* vp = reinterpret_cast<E*>(kv.v) + base;
+        for (int i = tid; i < D / 2; i += 32 * kDecWarps) {
+            int a, b;
+            float k0, k1;
+            if (i < half) {
+                a = neox ? i : 2 * i;
+                b = neox ? i + half : 2 * i + 1;
+                const float x0 = kr[a], x1 = kr[b];
+                k0 = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
+                k1 = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+            } else {
+                a = 2 * i;
+                b = 2 * i + 1;
+                k0 = kr[a];
+                k1 = kr[b];
+            }
+            put(kp + a, k0);
+            put(kp + b, k1);
+            put(vp + 2 * i, vr[2 * i]);
+            put(vp + 2 * i + 1, vr[2 * i + 1]);
+            snew[a] = to_store(k0, (E*)nullptr);
+            snew[b] = to_store(k1, (E*)nullptr);
+            snew[kMaxD + 2 * i] = to_store(vr[2 * i], (E*)nullptr);
+            snew[kMaxD + 2 * i + 1] = to_store(vr[2 * i + 1], (E*)nullptr);
+        }
+    }
+    const bool ok = mbar_wait(bar, 0, &s_abort);
+    if (!ok) {
+        s_abort = 1;
+        if (kv.err) atomicExch(kv.err, 6);
+    }
+    __syncthreads();
+    if (s_abort) {
+        if (tid == 0) mbar_wait_bounded(bar, 0);   // let the copies land before the CTA exits
+        return;
+    }
+    if (own) {
+        const int r = pos - j0;
+        for (int d = tid; d < D; d += 32 * kDecWarps) {
+            put(sk + (size_t)r * D + d, snew[d]);
+            put(sv + (size_t)r * D + d, snew[kMaxD + d]);
+        }
+    }
+    __syncthreads();
+
+    // scores: lane = key, 16-byte chunks visited in a lane-rotated order
+    const int jw = 32 * warp;                    // this warp's first key in the split
+    const int j = jw + lane;
+    const bool valid = j < nk;
+    const int nch = D / 8;                       // 8-element chunks per row
+    float sc[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) sc[g] = 0.0f;
+    if (valid) {
+        const E* krow = sk + (size_t)j * D;
+        for (int cc = 0; cc < nch; ++cc) {
+            const int ch = (cc + lane) % nch;
+            float kf[8];
+            ld_chunk<E>(krow + 8 * ch, kf);
+#pragma unroll
+            for (int g = 0; g < kMaxG; ++g) {
+                if (g < G) {
+                    const float4 qa = *reinterpret_cast<const float4*>(&sq[g * kMaxD + 8 * ch]);
+                    const float4 qb = *reinterpret_cast<const float4*>(&sq[g * kMaxD + 8 * ch + 4]);
+                    float v = sc[g];
+                    v = fmaf(qa.x, kf[0], v); v = fmaf(qa.y, kf[1], v); v = fmaf(qa.z, kf[2], v); v = fmaf(qa.w, kf[3], v);
+                    v = fmaf(qb.x, kf[4], v); v = fmaf(qb.y, kf[5], v); v = fmaf(qb.z, kf[6], v); v = fmaf(qb.w, kf[7], v);
+                    sc[g] = v;
+                }
+            }
+        }
+    }
+    const int nkw = max(0, min(32, nk - jw));    // keys of this warp
+    float m[kMaxG], l[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        const float sv_ = valid ? __fmul_rn(sc[g], scale) : -INFINITY;
+        m[g] = warp_max(sv_);
+        sc[g] = valid ? expf(sv_ - m[g]) : 0.0f;
+        l[g] = warp_sum(sc[g]);
+    }
+    // p.V: lane owns dims [dper*lane, dper*lane + dper)
+    const int dper = D / 32;
+    float o[kMaxG][4];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
+    for (int u = 0; u < nkw; ++u) {
+        const E* vrow = sv + (size_t)(jw + u) * D + lane * dper;
+        float vf[4];
+        if (dper == 4) {
+            if (sizeof(E) == 2) {
+                const uint2 raw = *reinterpret_cast<const uint2*>(vrow);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+            } else {
+                const float4 a = *reinterpret_cast<const float4*>(vrow);
+                vf[0] = a.x; vf[1] = a.y; vf[2] = a.z; vf[3] = a.w;
+            }
+        } else {
+            if (sizeof(E) == 2) {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(vrow));
+                vf[0] = a.x; vf[1] = a.y;
+            } else {
+                const float2 a = *reinterpret_cast<const float2*>(vrow);
+                vf[0] = a.x; vf[1] = a.y;
+            }
+            vf[2] = vf[3] = 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+            if (g >= G) break;
+            const float p = __shfl_sync(0xffffffffu, sc[g], u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        if (lane == 0) {
+            swm[warp * kMaxG + g] = nkw > 0 ? m[g] : -INFINITY;
+            swl[warp * kMaxG + g] = nkw > 0 ? l[g] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (e < dper) swo[((size_t)warp * kMaxG + g) * kMaxD + lane * dper + e] = o[g][e];
+    }
+    __syncthreads();
+    // merge the warps into this split's (max, sum, o[D]) per head
+    for (int idx = tid; idx < G * D; idx += 32 * kDecWarps) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, swm[w * kMaxG + g]);
+        float L = 0.0f, O = 0.0f;
+        for (int w = 0; w < kDecWarps; ++w) {
+            const float mw = swm[w * kMaxG + g];
+            if (mw == -INFINITY) continue;
+            const float cw = expf(mw - M);
+            L += swl[w * kMaxG + g] * cw;
+            O += swo[((size_t)w * kMaxG + g) * kMaxD + d] * cw;
+        }
+        float* pp = part + (((size_t)t * H + (size_t)hk * G + g) * n_splits + sp) * (D + 2);
+        if (d == 0) { pp[0] = M; pp[1] = L; }
+        pp[2 + d] = O;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int prev = atomicAdd(&counters[t * HKV + hk], 1);
+        s_last = prev == n_active - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // last split of this (token, kv head): merge the splits (k_attn_combine)
+    float* sw = swo;                      // [G][n_active] weights
+    float* sL = swm;                      // [G]
+    if (tid < G) {
+        const int g = tid;
+        const float* pg = part + ((size_t)t * H + (size_t)hk * G + g) * n_splits * (D + 2);
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < n_active; ++s2) M = fmaxf(M, __ldcg(pg + (size_t)s2 * (D + 2)));
+        float L = 0.0f;
+        for (int s2 = 0; s2 < n_active; ++s2) {
+            const float ms = __ldcg(pg + (size_t)s2 * (D + 2));
+            const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
+            sw[g * n_active + s2] = w;
+            if (w != 0.0f) L += __ldcg(pg + (size_t)s2 * (D + 2) + 1) * w;
+        }
+        sL[g] = L;
+    }
+    if (tid == 0) counters[t * HKV + hk] = 0;
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += 32 * kDecWarps) {
+        const int g = idx / D, d = idx % D;
+        const float* pg = part + ((size_t)t * H + (size_t)hk * G + g) * n_splits * (D + 2);
+        float O = 0.0f;
+        for (int s2 = 0; s2 < n_active; ++s2) {
+            const float w = sw[g * n_active + s2];
+            if (w != 0.0f) O += __ldcg(pg + (size_t)s2 * (D + 2) + 2 + d) * w;
+        }
+        const float L = sL[g];
+        out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = L > 0.0f ? O / L : 0.0f;
+    }
+}
+
 }  // namespace fb
 
 using namespace fb;
@@ -326,4 +639,49 @@ extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int
     if (e != cudaSuccess) return (int)e;
     return (int)fbk_launch(k_attn_combine, dim3(H, T), dim3(128), n_splits * sizeof(float), st, scratch, H, D, n_splits, out,
                            ldo);
+}
+
+extern "C" size_t fbk_attention_decode_scratch_floats(int T, int H, int D, int max_ctx, int kv_f16) {
+    const int kps = kv_f16 ? dec_kps<__half>() : dec_kps<float>();
+    return (size_t)T * H * ((max_ctx + kps - 1) / kps) * (D + 2);
+}
+
+extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H,
+                                    int HKV, int D, float scale, int rot, int neox, const float* rcos, const float* rsin,
+                                    KvView kv, int layer, float* out, int ldo, float* scratch, size_t scratch_floats,
+                                    int* counters, int max_ctx, cudaStream_t st) {
+    if (T <= 0) return 0;
+    const int G = H / HKV;
+    if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16 || !counters) return (int)cudaErrorInvalidValue;
+    if (fbk_attention_decode_scratch_floats(T, H, D, max_ctx, kv.f16) > scratch_floats) return (int)cudaErrorInvalidValue;
+    // the last split's merge keeps G x n_splits weights in the warp-output buffer
+    const int kps = kv.f16 ? dec_kps<__half>() : dec_kps<float>();
+    if ((size_t)G * ((max_ctx + kps - 1) / kps) > (size_t)kDecWarps * kMaxG * kMaxD) return (int)cudaErrorInvalidValue;
+    cudaError_t e;
+    if (kv.f16) {
+        static bool attr = false;
+        if (!attr) {
+            e = cudaFuncSetAttribute(k_attn_decode<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)dec_smem_bytes<__half>());
+            if (e != cudaSuccess) return (int)e;
+            attr = true;
+        }
+        const int n_splits = (max_ctx + dec_kps<__half>() - 1) / dec_kps<__half>();
+        e = fbk_launch(k_attn_decode<__half>, dim3(n_splits, HKV, T), dim3(32 * kDecWarps), dec_smem_bytes<__half>(), st,
+                       q, ldq, k, v, ldkv, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, scratch, n_splits,
+                       counters, out, ldo);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            e = cudaFuncSetAttribute(k_attn_decode<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)dec_smem_bytes<float>());
+            if (e != cudaSuccess) return (int)e;
+            attr = true;
+        }
+        const int n_splits = (max_ctx + dec_kps<float>() - 1) / dec_kps<float>();
+        e = fbk_launch(k_attn_decode<float>, dim3(n_splits, HKV, T), dim3(32 * kDecWarps), dec_smem_bytes<float>(), st,
+                       q, ldq, k, v, ldkv, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, scratch, n_splits,
+                       counters, out, ldo);
+    }
+    return (int)e;
 }
