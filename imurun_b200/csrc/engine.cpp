@@ -132,7 +132,7 @@ Engine::~Engine() {
     cudaFree(warena_);
     cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
     cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
-    cudaFree(act_mem_); cudaFree(att_scratch_); cudaFree(att_counters_);
+    cudaFree(act_mem_); cudaFree(att_scratch_);
     cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
@@ -492,11 +492,8 @@ bool Engine::alloc_buffers(std::string* err) {
     act_.ld = (int)ld;
     // attention scratch for att_chunk_ tokens per launch at the full context
     att_chunk_ = 64;
-    att_scratch_floats_ = std::max(fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx),
-                                   fbk_attention_decode_scratch_floats(kMaxBatch, c.n_head, c.head_dim, c.n_ctx, 0));
+    att_scratch_floats_ = fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx);
     CK(cudaMalloc(&att_scratch_, sizeof(float) * att_scratch_floats_));
-    CK(cudaMalloc(&att_counters_, sizeof(int) * kMaxBatch * c.n_head_kv));
-    CK(cudaMemset(att_counters_, 0, sizeof(int) * kMaxBatch * c.n_head_kv));
     CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
@@ -798,8 +795,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
         }
         if (distinct && !no_fuse_) {
             CKP(PC_ATTN, 0, fbk_attention_decode(q_, Q, k_, v_, KV, T, H, HKV, D, scale, c.rot_dim, c.neox ? 1 : 0,
-                                                 rope_cos_, rope_sin_, kv, li, attn_, Q, att_scratch_,
-                                                 att_scratch_floats_, att_counters_, max_ctx, stream_));
+                                                 rope_cos_, rope_sin_, kv, li, attn_, Q, stream_));
         } else {
         CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
                                         rope_sin_, kv, li, stream_));

@@ -172,7 +172,6 @@ private:
     ActQ act_{};
     int8_t* act_mem_ = nullptr;
     float* att_scratch_ = nullptr;
-    int* att_counters_ = nullptr;   // [kMaxBatch][n_head_kv] split counters of the fused decode attention
     size_t att_scratch_floats_ = 0;
     int att_chunk_ = 32;
     int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;

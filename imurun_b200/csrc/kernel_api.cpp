@@ -349,6 +349,79 @@ int fbx_attention(const float* q, const float* k, const float* v, int n_keys, in
     return 0;
 }
 
+int fbx_attention_decode(const float* q, const float* k_cache, const float* v_cache, const float* k_new,
+                         const float* v_new, int pos, int H, int HKV, int D, int rot_dim, int neox, float freq_base,
+                         int kv_f16, float* out, float* k_stored, float* v_stored) {
+    if (!q || !k_new || !v_new || !out || pos < 0 || (pos > 0 && (!k_cache || !v_cache)) || H % HKV ||
+        (D != 64 && D != 128) || rot_dim <= 0 || rot_dim > D || rot_dim % 2)
+        return -1;
+    TRY(check_device());
+    const int n_keys = pos + 1;
+    TestPool tp;
+    TRY(tp.make(n_keys, HKV, D, kv_f16, 1, pos));
+    const int P = kPageSize, np = (n_keys + P - 1) / P;
+    const size_t head = (size_t)P * D, vofs = (size_t)HKV * head, page = 2 * vofs;
+    std::vector<float> hf(page * np, 0.0f);
+    for (int j = 0; j < pos; ++j)
+        for (int h = 0; h < HKV; ++h)
+            for (int d = 0; d < D; ++d) {
+                const size_t o = (size_t)(j / P) * page + h * head + (size_t)(j % P) * D + d;
+                hf[o] = k_cache[(size_t)j * HKV * D + h * D + d];
+                hf[o + vofs] = v_cache[(size_t)j * HKV * D + h * D + d];
+            }
+    if (kv_f16) {
+        std::vector<__half> hh(hf.size());
+        for (size_t i = 0; i < hf.size(); ++i) hh[i] = __float2half_rn(hf[i]);
+        TRY(cudaMemcpy(tp.pool.p, hh.data(), hh.size() * 2, cudaMemcpyHostToDevice));
+    } else {
+        TRY(cudaMemcpy(tp.pool.p, hf.data(), hf.size() * 4, cudaMemcpyHostToDevice));
+    }
+    Config c;
+    c.n_ctx = n_keys;
+    c.rot_dim = rot_dim;
+    c.head_dim = D;
+    c.freq_base = freq_base;
+    std::vector<float> cs, sn;
+    build_rope_table(c, nullptr, cs, sn);
+    DevBuf dq, dk, dv, dout, dc, ds;
+    TRY(dq.alloc(sizeof(float) * H * D));
+    TRY(dk.alloc(sizeof(float) * HKV * D));
+    TRY(dv.alloc(sizeof(float) * HKV * D));
+    TRY(dout.alloc(sizeof(float) * H * D));
+    TRY(dc.alloc(sizeof(float) * cs.size()));
+    TRY(ds.alloc(sizeof(float) * sn.size()));
+    TRY(cudaMemcpy(dq.p, q, sizeof(float) * H * D, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dk.p, k_new, sizeof(float) * HKV * D, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dv.p, v_new, sizeof(float) * HKV * D, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dc.p, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(ds.p, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice));
+    TRY(fbk_attention_decode(dq.as<float>(), H * D, dk.as<float>(), dv.as<float>(), HKV * D, 1, H, HKV, D,
+                             1.0f / std::sqrt((float)D), rot_dim, neox, dc.as<float>(), ds.as<float>(), tp.kv, 0,
+                             dout.as<float>(), H * D, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(float) * H * D, cudaMemcpyDeviceToHost));
+    if (k_stored || v_stored) {
+        const size_t esz = kv_f16 ? 2 : 4;
+        std::vector<uint8_t> raw(page * np * esz);
+        TRY(cudaMemcpy(raw.data(), tp.pool.p, raw.size(), cudaMemcpyDeviceToHost));
+        for (int h = 0; h < HKV; ++h)
+            for (int d = 0; d < D; ++d) {
+                const size_t o = (size_t)(pos / P) * page + h * head + (size_t)(pos % P) * D + d;
+                float kx, vx;
+                if (kv_f16) {
+                    kx = __half2float(reinterpret_cast<const __half*>(raw.data())[o]);
+                    vx = __half2float(reinterpret_cast<const __half*>(raw.data())[o + vofs]);
+                } else {
+                    kx = reinterpret_cast<const float*>(raw.data())[o];
+                    vx = reinterpret_cast<const float*>(raw.data())[o + vofs];
+                }
+                if (k_stored) k_stored[h * D + d] = kx;
+                if (v_stored) v_stored[h * D + d] = vx;
+            }
+    }
+    return 0;
+}
+
 int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_dim, int neox, float freq_base, int pos0) {
     if (!q || !k || T <= 0 || pos0 < 0 || rot_dim <= 0 || rot_dim > D || D % 2) return -1;
     TRY(check_device());

@@ -7,6 +7,8 @@
 // positions 0..pos with scale 1/sqrt(D) (src/ops.cpp:303-356). The KV cache is
 // paged (P positions per page, every layer of a position range in one page)
 // and fp16 or f32.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -289,134 +291,160 @@ __global__ void k_attn_combine(const float* __restrict__ part, int H, int D, int
 // ================================================================ fused decode
 // Decode attention for T tokens of T distinct sequences, one kernel per layer:
 // RoPE of q and of the new k, the append of the new K/V row into the cache,
-// split-K attention over the cached keys and the merge of the splits.
-// CTA = (key split of KPS keys, kv head, token), 4 warps. The split's K and V
-// page blocks (16 positions x D each, contiguous in the paged layout) land in
-// shared memory by bulk copies; the CTA holding the token's own position
-// rotates and stores the new k/v and patches its shared copy. Warps take 32
-// keys each (lane = key for q.k, lane = a D-slice for p.V); the CTA merges
-// its warps and writes (max, sum, o[D]) per head; the last CTA of a
-// (token, kv head) to finish — an atomic counter, reset by that CTA — merges
-// the splits into the output. Arithmetic follows k_rope_append, k_attn_split
-// and k_attn_combine (src/ops.cpp:126-156, 303-356).
-constexpr int kDecWarps = 4;
+// attention over the cached keys, and the merge of the partial results.
+// A thread-block cluster of C CTAs serves one (token, kv head); CTA r takes
+// the 64-key blocks r, r + C, ... of the context. A block's K and V page
+// pieces (16 positions x D, contiguous in the paged layout) arrive by bulk
+// copies into a two-slot ring while the previous block is computed. Scores:
+// 8 lanes per key (D/8 dims each) reduced by shuffles; softmax is kept online
+// per CTA (running max, sum and unnormalised output in shared memory); the C
+// partials are merged through distributed shared memory. The CTA holding the
+// token's own position rotates and stores the new k/v and patches its shared
+// copy. Arithmetic follows k_rope_append, k_attn_split and k_attn_combine
+// (src/ops.cpp:126-156, 303-356).
+constexpr int kDecThreads = 128;
+constexpr int kDecKeys = 64;
 
-template <class E>
-__device__ __forceinline__ void ld_chunk(const E* p, float (&f)[8]);
-template <>
-__device__ __forceinline__ void ld_chunk<__half>(const __half* p, float (&f)[8]) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
-    const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const float2 v = __half22float2(h[e]);
-        f[2 * e] = v.x;
-        f[2 * e + 1] = v.y;
-    }
-}
-template <>
-__device__ __forceinline__ void ld_chunk<float>(const float* p, float (&f)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
-__device__ __forceinline__ float to_store(float x, __half*) { return __half2float(__float2half_rn(x)); }
-__device__ __forceinline__ float to_store(float x, float*) { return x; }
+__device__ __forceinline__ float to_store(float x, const __half*) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float to_store(float x, const float*) { return x; }
 __device__ __forceinline__ void put(__half* p, float x) { *p = __float2half_rn(x); }
 __device__ __forceinline__ void put(float* p, float x) { *p = x; }
+__device__ __forceinline__ float get(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ float get(const float* p) { return *p; }
 
-template <class E>
-__host__ __device__ constexpr int dec_kps() { return sizeof(E) == 2 ? 128 : 64; }
-
-// dynamic shared memory of k_attn_decode<E>
-template <class E>
-__host__ __device__ constexpr size_t dec_smem_bytes() {
-    return 16 + 2 * (size_t)dec_kps<E>() * kMaxD * sizeof(E) +
-           sizeof(float) * ((size_t)kMaxG * kMaxD + 2 * kDecWarps * kMaxG + (size_t)kDecWarps * kMaxG * kMaxD + 2 * kMaxD);
+// n consecutive values (n = 8 or 16) of row p, as floats
+template <int N>
+__device__ __forceinline__ void ld_vals(const __half* p, float (&f)[16]) {
+#pragma unroll
+    for (int c = 0; c < N / 8; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p + 8 * c);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 v = __half22float2(h[e]);
+            f[8 * c + 2 * e] = v.x;
+            f[8 * c + 2 * e + 1] = v.y;
+        }
+    }
+}
+template <int N>
+__device__ __forceinline__ void ld_vals(const float* p, float (&f)[16]) {
+#pragma unroll
+    for (int c = 0; c < N / 4; ++c) {
+        const float4 a = *reinterpret_cast<const float4*>(p + 4 * c);
+        f[4 * c] = a.x; f[4 * c + 1] = a.y; f[4 * c + 2] = a.z; f[4 * c + 3] = a.w;
+    }
 }
 
 template <class E>
-__global__ void __launch_bounds__(32 * kDecWarps) k_attn_decode(
+struct DecSmem {
+    static constexpr size_t kv_elems = (size_t)kDecKeys * kMaxD;
+    static constexpr size_t off_k = 64;                                     // after 2 mbarriers + flags
+    static constexpr size_t off_v = off_k + 2 * kv_elems * sizeof(E);
+    static constexpr size_t off_q = off_v + 2 * kv_elems * sizeof(E);        // [G][D] f32
+    static constexpr size_t off_s = off_q + sizeof(float) * kMaxG * kMaxD;   // [G][64] scores / probabilities
+    static constexpr size_t off_o = off_s + sizeof(float) * kMaxG * kDecKeys;  // [G][D] output accumulator
+    static constexpr size_t off_m = off_o + sizeof(float) * kMaxG * kMaxD;   // [G] running max
+    static constexpr size_t off_l = off_m + sizeof(float) * kMaxG;           // [G] running sum
+    static constexpr size_t off_c = off_l + sizeof(float) * kMaxG;           // [G] rescale of this block
+    static constexpr size_t off_n = off_c + sizeof(float) * kMaxG;           // [2][D] new k, v (stored values)
+    static constexpr size_t bytes = off_n + sizeof(float) * 2 * kMaxD;
+};
+
+template <class E>
+__global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     const float* __restrict__ q, int ldq, const float* __restrict__ knew, const float* __restrict__ vnew, int ldkv,
     int H, int HKV, int D, float scale, int rot, int neox, const float* __restrict__ rcos,
-    const float* __restrict__ rsin, KvView kv, int layer, float* __restrict__ part, int n_splits,
-    int* __restrict__ counters, float* __restrict__ out, int ldo) {
-    constexpr int KPS = dec_kps<E>();
+    const float* __restrict__ rsin, KvView kv, int layer, float* __restrict__ out, int ldo) {
+    using L = DecSmem<E>;
+    namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_last;
-    __shared__ volatile int s_abort;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.z, hk = blockIdx.y, sp = blockIdx.x, G = H / HKV;
+    const int t = blockIdx.z, hk = blockIdx.y, G = H / HKV;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pos = kv.tok_pos[t], n_keys = pos + 1, j0 = sp * KPS;
-    if (j0 >= n_keys) return;
-    const int n_active = (n_keys + KPS - 1) / KPS, nk = min(KPS, n_keys - j0);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-    E* sk = reinterpret_cast<E*>(smem + 16);
-    E* sv = sk + (size_t)KPS * kMaxD;
-    float* sq = reinterpret_cast<float*>(sv + (size_t)KPS * kMaxD);   // [G][D]
-    float* swm = sq + kMaxG * kMaxD;                                    // [warp][G]
-    float* swl = swm + kDecWarps * kMaxG;                               // [warp][G]
-    float* swo = swl + kDecWarps * kMaxG;                               // [warp][G][D]
-    float* snew = swo + kDecWarps * kMaxG * kMaxD;                     // [2][D]
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 16);
+    E* sk = reinterpret_cast<E*>(smem + L::off_k);
+    E* sv = reinterpret_cast<E*>(smem + L::off_v);
+    float* sq = reinterpret_cast<float*>(smem + L::off_q);
+    float* ss = reinterpret_cast<float*>(smem + L::off_s);
+    float* so = reinterpret_cast<float*>(smem + L::off_o);
+    float* sm = reinterpret_cast<float*>(smem + L::off_m);
+    float* sl = reinterpret_cast<float*>(smem + L::off_l);
+    float* sc = reinterpret_cast<float*>(smem + L::off_c);
+    float* snew = reinterpret_cast<float*>(smem + L::off_n);
+    const int pos = kv.tok_pos[t], n_keys = pos + 1;
+    const int n_blocks = (n_keys + kDecKeys - 1) / kDecKeys;
+    const int nb_mine = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
     const int seq = kv.tok_seq[t];
-    const int np = (nk + 15) / 16;
-    const size_t blk = (size_t)16 * D;   // elements of one page's block of this head
-    if (tid == 0) {
-        s_abort = 0;
-        mbar_init(bar, 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        mbar_expect_tx(bar, (uint32_t)(2 * np * blk * sizeof(E)));
-        for (int i = 0; i < np; ++i) {
-            int page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + i];
+    const size_t pblk = (size_t)16 * D;   // elements of one page's piece of this head
+    const int b_own = pos / kDecKeys;
+
+    auto issue = [&](int i) {   // bulk copies of my i-th block into slot i & 1
+        const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0), np = (kb + 15) / 16;
+        uint64_t* br = &bar[i & 1];
+        mbar_expect_tx(br, (uint32_t)(2 * np * pblk * sizeof(E)));
+        for (int pp = 0; pp < np; ++pp) {
+            int page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + pp];
             if (page < 0 || page >= kv.n_pages) {
                 if (kv.err) atomicExch(kv.err, 5);
                 page = 0;
             }
             const size_t off = (size_t)page * kv.page_stride + (size_t)layer * kv.layer_stride + (size_t)hk * kv.head_stride;
-            bulk_g2s(sk + i * blk, reinterpret_cast<const E*>(kv.k) + off, (uint32_t)(blk * sizeof(E)), bar);
-            bulk_g2s(sv + i * blk, reinterpret_cast<const E*>(kv.v) + off, (uint32_t)(blk * sizeof(E)), bar);
+            bulk_g2s(sk + (size_t)(i & 1) * L::kv_elems + pp * pblk, reinterpret_cast<const E*>(kv.k) + off,
+                     (uint32_t)(pblk * sizeof(E)), br);
+            bulk_g2s(sv + (size_t)(i & 1) * L::kv_elems + pp * pblk, reinterpret_cast<const E*>(kv.v) + off,
+                     (uint32_t)(pblk * sizeof(E)), br);
         }
+    };
+    if (tid == 0) {
+        *s_abort = 0;
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        if (nb_mine > 0) issue(0);
+        if (nb_mine > 1) issue(1);
     }
     // q heads of this kv head, rotated (biases and q-norm were applied upstream)
     const int half = rot / 2;
-    const float* c = rcos + (size_t)pos * half;
-    const float* s = rsin + (size_t)pos * half;
+    const float* cs = rcos + (size_t)pos * half;
+    const float* sn = rsin + (size_t)pos * half;
     const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
-    for (int idx = tid; idx < G * (D / 2); idx += 32 * kDecWarps) {
+    for (int idx = tid; idx < G * (D / 2); idx += kDecThreads) {
         const int g = idx / (D / 2), i = idx % (D / 2);
         const float* hv = qr + (size_t)g * D;
         if (i < half) {
             const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
             const float x0 = hv[a], x1 = hv[b];
-            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
-            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
         } else {
             sq[g * kMaxD + 2 * i] = hv[2 * i];
             sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
         }
     }
-    // the token's own position: rotate k, store k and v, keep their stored values
-    const bool own = pos >= j0 && pos < j0 + KPS;
-    if (own) {
+    // the token's own position: rotate k, store k and v, keep the stored values
+    if (b_own % C == r) {
         const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
         const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
         const size_t base = kv_off(kv, layer, hk, t, pos);
         E* kp = reinterpret_cast<E*>(kv.k) + base;
         E* vp = reinterpret_cast<E*>(kv.v) + base;
-        for (int i = tid; i < D / 2; i += 32 * kDecWarps) {
+        for (int i = tid; i < D / 2; i += kDecThreads) {
             int a, b;
             float k0, k1;
             if (i < half) {
                 a = neox ? i : 2 * i;
                 b = neox ? i + half : 2 * i + 1;
                 const float x0 = kr[a], x1 = kr[b];
-                k0 = __fsub_rn(__fmul_rn(x0, c[i]), __fmul_rn(x1, s[i]));
-                k1 = __fadd_rn(__fmul_rn(x0, s[i]), __fmul_rn(x1, c[i]));
+                k0 = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+                k1 = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
             } else {
                 a = 2 * i;
                 b = 2 * i + 1;
@@ -427,174 +455,138 @@ __global__ void __launch_bounds__(32 * kDecWarps) k_attn_decode(
             put(kp + b, k1);
             put(vp + 2 * i, vr[2 * i]);
             put(vp + 2 * i + 1, vr[2 * i + 1]);
-            snew[a] = to_store(k0, (E*)nullptr);
-            snew[b] = to_store(k1, (E*)nullptr);
-            snew[kMaxD + 2 * i] = to_store(vr[2 * i], (E*)nullptr);
-            snew[kMaxD + 2 * i + 1] = to_store(vr[2 * i + 1], (E*)nullptr);
+            snew[a] = to_store(k0, kp);
+            snew[b] = to_store(k1, kp);
+            snew[kMaxD + 2 * i] = to_store(vr[2 * i], vp);
+            snew[kMaxD + 2 * i + 1] = to_store(vr[2 * i + 1], vp);
         }
     }
-    const bool ok = mbar_wait(bar, 0, &s_abort);
-    if (!ok) {
-        s_abort = 1;
-        if (kv.err) atomicExch(kv.err, 6);
-    }
-    __syncthreads();
-    if (s_abort) {
-        if (tid == 0) mbar_wait_bounded(bar, 0);   // let the copies land before the CTA exits
-        return;
-    }
-    if (own) {
-        const int r = pos - j0;
-        for (int d = tid; d < D; d += 32 * kDecWarps) {
-            put(sk + (size_t)r * D + d, snew[d]);
-            put(sv + (size_t)r * D + d, snew[kMaxD + d]);
-        }
+    for (int i = tid; i < G * kMaxD; i += kDecThreads) so[i] = 0.0f;
+    if (tid < G) {
+        sm[tid] = -INFINITY;
+        sl[tid] = 0.0f;
     }
     __syncthreads();
 
-    // scores: lane = key, 16-byte chunks visited in a lane-rotated order
-    const int jw = 32 * warp;                    // this warp's first key in the split
-    const int j = jw + lane;
-    const bool valid = j < nk;
-    const int nch = D / 8;                       // 8-element chunks per row
-    float sc[kMaxG];
+    const int dpp = D / 8;                     // dims per lane in a key's dot
+    const int part = lane & 7;
+    int failed_at = -1;
+    for (int i = 0; i < nb_mine; ++i) {
+        const bool ok = mbar_wait(&bar[i & 1], (uint32_t)((i >> 1) & 1), s_abort);
+        if (__syncthreads_or(!ok)) {
+            failed_at = i;
+            break;
+        }
+        const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0);
+        E* K = sk + (size_t)(i & 1) * L::kv_elems;
+        E* V = sv + (size_t)(i & 1) * L::kv_elems;
+        if (b == b_own) {
+            const int rr = pos - j0;
+            for (int d = tid; d < D; d += kDecThreads) {
+                put(K + (size_t)rr * D + d, snew[d]);
+                put(V + (size_t)rr * D + d, snew[kMaxD + d]);
+            }
+            __syncthreads();
+        }
+        // scores: warp w holds keys 16w .. 16w+15, four per pass, 8 lanes per key
+#pragma unroll 1
+        for (int ps = 0; ps < 4; ++ps) {
+            const int key = 16 * warp + 4 * ps + (lane >> 3);
+            const bool valid = key < kb;
+            float acc[kMaxG];
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) sc[g] = 0.0f;
-    if (valid) {
-        const E* krow = sk + (size_t)j * D;
-        for (int cc = 0; cc < nch; ++cc) {
-            const int ch = (cc + lane) % nch;
-            float kf[8];
-            ld_chunk<E>(krow + 8 * ch, kf);
+            for (int g = 0; g < kMaxG; ++g) acc[g] = 0.0f;
+            if (valid) {
+                float kf[16];
+                if (dpp == 16) ld_vals<16>(K + (size_t)key * D + 16 * part, kf);
+                else ld_vals<8>(K + (size_t)key * D + 8 * part, kf);
+#pragma unroll
+                for (int g = 0; g < kMaxG; ++g) {
+                    if (g < G) {
+                        const float* qq = sq + g * kMaxD + dpp * part;
+                        float a = 0.0f;
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            if (4 * e4 < dpp) {
+                                const float4 qv = *reinterpret_cast<const float4*>(qq + 4 * e4);
+                                a = fmaf(qv.x, kf[4 * e4], a);
+                                a = fmaf(qv.y, kf[4 * e4 + 1], a);
+                                a = fmaf(qv.z, kf[4 * e4 + 2], a);
+                                a = fmaf(qv.w, kf[4 * e4 + 3], a);
+                            }
+                        }
+                        acc[g] = a;
+                    }
+                }
+            }
 #pragma unroll
             for (int g = 0; g < kMaxG; ++g) {
                 if (g < G) {
-                    const float4 qa = *reinterpret_cast<const float4*>(&sq[g * kMaxD + 8 * ch]);
-                    const float4 qb = *reinterpret_cast<const float4*>(&sq[g * kMaxD + 8 * ch + 4]);
-                    float v = sc[g];
-                    v = fmaf(qa.x, kf[0], v); v = fmaf(qa.y, kf[1], v); v = fmaf(qa.z, kf[2], v); v = fmaf(qa.w, kf[3], v);
-                    v = fmaf(qb.x, kf[4], v); v = fmaf(qb.y, kf[5], v); v = fmaf(qb.z, kf[6], v); v = fmaf(qb.w, kf[7], v);
-                    sc[g] = v;
+                    float a = acc[g];
+                    a += __shfl_xor_sync(0xffffffffu, a, 1);
+                    a += __shfl_xor_sync(0xffffffffu, a, 2);
+                    a += __shfl_xor_sync(0xffffffffu, a, 4);
+                    if (part == 0 && valid) ss[g * kDecKeys + key] = __fmul_rn(a, scale);
                 }
             }
         }
-    }
-    const int nkw = max(0, min(32, nk - jw));    // keys of this warp
-    float m[kMaxG], l[kMaxG];
-#pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-        if (g >= G) break;
-        const float sv_ = valid ? __fmul_rn(sc[g], scale) : -INFINITY;
-        m[g] = warp_max(sv_);
-        sc[g] = valid ? expf(sv_ - m[g]) : 0.0f;
-        l[g] = warp_sum(sc[g]);
-    }
-    // p.V: lane owns dims [dper*lane, dper*lane + dper)
-    const int dper = D / 32;
-    float o[kMaxG][4];
-#pragma unroll
-    for (int g = 0; g < kMaxG; ++g)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[g][e] = 0.0f;
-    for (int u = 0; u < nkw; ++u) {
-        const E* vrow = sv + (size_t)(jw + u) * D + lane * dper;
-        float vf[4];
-        if (dper == 4) {
-            if (sizeof(E) == 2) {
-                const uint2 raw = *reinterpret_cast<const uint2*>(vrow);
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-            } else {
-                const float4 a = *reinterpret_cast<const float4*>(vrow);
-                vf[0] = a.x; vf[1] = a.y; vf[2] = a.z; vf[3] = a.w;
+        __syncthreads();
+        // online softmax per head (warp g, g + 4)
+        for (int g = warp; g < G; g += kDecThreads / 32) {
+            const float s0 = lane < kb ? ss[g * kDecKeys + lane] : -INFINITY;
+            const float s1 = lane + 32 < kb ? ss[g * kDecKeys + lane + 32] : -INFINITY;
+            const float mb = warp_max(fmaxf(s0, s1));
+            const float mo = sm[g], mn = fmaxf(mo, mb);
+            const float p0 = lane < kb ? expf(s0 - mn) : 0.0f;
+            const float p1 = lane + 32 < kb ? expf(s1 - mn) : 0.0f;
+            const float sum = warp_sum(p0 + p1);
+            ss[g * kDecKeys + lane] = p0;
+            ss[g * kDecKeys + lane + 32] = p1;
+            if (lane == 0) {
+                const float corr = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                sl[g] = sl[g] * corr + sum;
+                sm[g] = mn;
+                sc[g] = corr;
             }
-        } else {
-            if (sizeof(E) == 2) {
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(vrow));
-                vf[0] = a.x; vf[1] = a.y;
-            } else {
-                const float2 a = *reinterpret_cast<const float2*>(vrow);
-                vf[0] = a.x; vf[1] = a.y;
-            }
-            vf[2] = vf[3] = 0.0f;
         }
-#pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-            if (g >= G) break;
-            const float p = __shfl_sync(0xffffffffu, sc[g], u);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(p, vf[e], o[g][e]);
+        __syncthreads();
+        // p.V: thread = one dim of one head (heads tid / D, tid / D + 128 / D, ...)
+        for (int g = tid / D; g < G; g += kDecThreads / D) {
+            const int d = tid % D;
+            float o = so[g * kMaxD + d] * sc[g];
+            const float* pg = ss + g * kDecKeys;
+            for (int j = 0; j < kb; ++j) o = fmaf(pg[j], get(V + (size_t)j * D + d), o);
+            so[g * kMaxD + d] = o;
         }
+        __syncthreads();
+        if (tid == 0 && i + 2 < nb_mine) issue(i + 2);
     }
-#pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-        if (g >= G) break;
-        if (lane == 0) {
-            swm[warp * kMaxG + g] = nkw > 0 ? m[g] : -INFINITY;
-            swl[warp * kMaxG + g] = nkw > 0 ? l[g] : 0.0f;
+    if (failed_at >= 0) {
+        // let the copies still in flight (blocks failed_at, failed_at + 1) land before the CTA can exit
+        if (tid == 0) {
+            if (kv.err) atomicExch(kv.err, 6);
+            for (int i = failed_at; i < nb_mine && i < failed_at + 2; ++i)
+                mbar_wait_bounded(&bar[i & 1], (uint32_t)((i >> 1) & 1));
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            if (e < dper) swo[((size_t)warp * kMaxG + g) * kMaxD + lane * dper + e] = o[g][e];
+        if (tid < G) { sm[tid] = -INFINITY; sl[tid] = 0.0f; }
     }
-    __syncthreads();
-    // merge the warps into this split's (max, sum, o[D]) per head
-    for (int idx = tid; idx < G * D; idx += 32 * kDecWarps) {
+    cluster.sync();
+    // merge the C partials (distributed shared memory); CTA r takes outputs r*128 + tid, step C*128
+    for (int idx = r * kDecThreads + tid; idx < G * D; idx += C * kDecThreads) {
         const int g = idx / D, d = idx % D;
         float M = -INFINITY;
-        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, swm[w * kMaxG + g]);
-        float L = 0.0f, O = 0.0f;
-        for (int w = 0; w < kDecWarps; ++w) {
-            const float mw = swm[w * kMaxG + g];
-            if (mw == -INFINITY) continue;
-            const float cw = expf(mw - M);
-            L += swl[w * kMaxG + g] * cw;
-            O += swo[((size_t)w * kMaxG + g) * kMaxD + d] * cw;
+        for (int rr = 0; rr < C; ++rr) M = fmaxf(M, *cluster.map_shared_rank(sm + g, rr));
+        float Ls = 0.0f, O = 0.0f;
+        for (int rr = 0; rr < C; ++rr) {
+            const float mr = *cluster.map_shared_rank(sm + g, rr);
+            if (mr == -INFINITY) continue;
+            const float w = expf(mr - M);
+            Ls += *cluster.map_shared_rank(sl + g, rr) * w;
+            O += *cluster.map_shared_rank(so + g * kMaxD + d, rr) * w;
         }
-        float* pp = part + (((size_t)t * H + (size_t)hk * G + g) * n_splits + sp) * (D + 2);
-        if (d == 0) { pp[0] = M; pp[1] = L; }
-        pp[2 + d] = O;
+        out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(&counters[t * HKV + hk], 1);
-        s_last = prev == n_active - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // last split of this (token, kv head): merge the splits (k_attn_combine)
-    float* sw = swo;                      // [G][n_active] weights
-    float* sL = swm;                      // [G]
-    if (tid < G) {
-        const int g = tid;
-        const float* pg = part + ((size_t)t * H + (size_t)hk * G + g) * n_splits * (D + 2);
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < n_active; ++s2) M = fmaxf(M, __ldcg(pg + (size_t)s2 * (D + 2)));
-        float L = 0.0f;
-        for (int s2 = 0; s2 < n_active; ++s2) {
-            const float ms = __ldcg(pg + (size_t)s2 * (D + 2));
-            const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
-            sw[g * n_active + s2] = w;
-            if (w != 0.0f) L += __ldcg(pg + (size_t)s2 * (D + 2) + 1) * w;
-        }
-        sL[g] = L;
-    }
-    if (tid == 0) counters[t * HKV + hk] = 0;
-    __syncthreads();
-    for (int idx = tid; idx < G * D; idx += 32 * kDecWarps) {
-        const int g = idx / D, d = idx % D;
-        const float* pg = part + ((size_t)t * H + (size_t)hk * G + g) * n_splits * (D + 2);
-        float O = 0.0f;
-        for (int s2 = 0; s2 < n_active; ++s2) {
-            const float w = sw[g * n_active + s2];
-            if (w != 0.0f) O += __ldcg(pg + (size_t)s2 * (D + 2) + 2 + d) * w;
-        }
-        const float L = sL[g];
-        out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = L > 0.0f ? O / L : 0.0f;
-    }
+    cluster.sync();   // keep this CTA's shared memory alive until every remote read is done
 }
 
 }  // namespace fb
@@ -641,47 +633,70 @@ extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int
                            ldo);
 }
 
-extern "C" size_t fbk_attention_decode_scratch_floats(int T, int H, int D, int max_ctx, int kv_f16) {
-    const int kps = kv_f16 ? dec_kps<__half>() : dec_kps<float>();
-    return (size_t)T * H * ((max_ctx + kps - 1) / kps) * (D + 2);
+// Cluster size of the decode attention: 16 CTAs when the device can host such
+// clusters with this kernel's shared memory, else 8.
+template <class E>
+static int dec_cluster_size() {
+    int c = 16;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(16, 1, 1);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = DecSmem<E>::bytes;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 16;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_attn_decode<E>, &cfg) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        c = 8;
+    }
+    return c;
+}
+
+template <class E>
+static int launch_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV,
+                         int D, float scale, int rot, int neox, const float* rcos, const float* rsin, KvView kv,
+                         int layer, float* out, int ldo, cudaStream_t st) {
+    static int cluster = 0;
+    if (!cluster) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)DecSmem<E>::bytes);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_decode<E>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return (int)e;
+        cluster = dec_cluster_size<E>();
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(cluster, HKV, T);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = DecSmem<E>::bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    int na = 1;
+    if (fbk_pdl_enabled()) {
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        na = 2;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return (int)cudaLaunchKernelEx(&cfg, k_attn_decode<E>, q, ldq, k, v, ldkv, H, HKV, D, scale, rot, neox, rcos, rsin, kv,
+                                   layer, out, ldo);
 }
 
 extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H,
                                     int HKV, int D, float scale, int rot, int neox, const float* rcos, const float* rsin,
-                                    KvView kv, int layer, float* out, int ldo, float* scratch, size_t scratch_floats,
-                                    int* counters, int max_ctx, cudaStream_t st) {
+                                    KvView kv, int layer, float* out, int ldo, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
-    if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16 || !counters) return (int)cudaErrorInvalidValue;
-    if (fbk_attention_decode_scratch_floats(T, H, D, max_ctx, kv.f16) > scratch_floats) return (int)cudaErrorInvalidValue;
-    // the last split's merge keeps G x n_splits weights in the warp-output buffer
-    const int kps = kv.f16 ? dec_kps<__half>() : dec_kps<float>();
-    if ((size_t)G * ((max_ctx + kps - 1) / kps) > (size_t)kDecWarps * kMaxG * kMaxD) return (int)cudaErrorInvalidValue;
-    cudaError_t e;
-    if (kv.f16) {
-        static bool attr = false;
-        if (!attr) {
-            e = cudaFuncSetAttribute(k_attn_decode<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)dec_smem_bytes<__half>());
-            if (e != cudaSuccess) return (int)e;
-            attr = true;
-        }
-        const int n_splits = (max_ctx + dec_kps<__half>() - 1) / dec_kps<__half>();
-        e = fbk_launch(k_attn_decode<__half>, dim3(n_splits, HKV, T), dim3(32 * kDecWarps), dec_smem_bytes<__half>(), st,
-                       q, ldq, k, v, ldkv, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, scratch, n_splits,
-                       counters, out, ldo);
-    } else {
-        static bool attr = false;
-        if (!attr) {
-            e = cudaFuncSetAttribute(k_attn_decode<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)dec_smem_bytes<float>());
-            if (e != cudaSuccess) return (int)e;
-            attr = true;
-        }
-        const int n_splits = (max_ctx + dec_kps<float>() - 1) / dec_kps<float>();
-        e = fbk_launch(k_attn_decode<float>, dim3(n_splits, HKV, T), dim3(32 * kDecWarps), dec_smem_bytes<float>(), st,
-                       q, ldq, k, v, ldkv, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, scratch, n_splits,
-                       counters, out, ldo);
-    }
-    return (int)e;
+    if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
+    if (kv.f16) return launch_decode<__half>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
+    return launch_decode<float>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
 }

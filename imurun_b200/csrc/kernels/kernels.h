@@ -126,13 +126,11 @@ int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float s
                   float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st);
 // Decode attention for T tokens of T distinct sequences, RoPE and the K/V
 // append fused: q and k/v are the raw projections [T][...]; the new rows are
-// stored at each token's position; out [T][H*D]. counters: [T][HKV] ints,
-// zero before the first call (each call leaves them zero). Page size 16.
-size_t fbk_attention_decode_scratch_floats(int T, int H, int D, int max_ctx, int kv_f16);
+// stored at each token's position; out [T][H*D]. Page size 16. One cluster
+// of CTAs per (token, kv head); no scratch.
 int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,
                          float scale, int rot, int neox, const float* rope_cos, const float* rope_sin, KvView kv,
-                         int layer, float* out, int ldo, float* scratch, size_t scratch_floats, int* counters,
-                         int max_ctx, cudaStream_t st);
+                         int layer, float* out, int ldo, cudaStream_t st);
 // Per-head RMSNorm in place (q/k norm), rows [T][n_heads*D].
 int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st);
 // MoE: x[t] += sum_k wsel[t][k] * eo[t][k][:]

@@ -50,6 +50,19 @@ FISH_API int fbx_block_sums(int type, const void* w, int n_in, int n_out, const 
 FISH_API int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D,
                            int pos0, int T, int kv_f16, float* out);
 
+/* One decode step of one sequence with the fused kernel the engine uses for
+ * single-token steps: q [H*D] and the new k/v [HKV*D] are the raw
+ * projections of the token at position pos; RoPE (reference ops.cpp:126-156,
+ * table like rope_build ops.cpp:75-124) rotates q and k, the new K/V row is
+ * stored in the paged cache at pos (reference model.cpp:1723-1731) after
+ * caches k_cache/v_cache [pos][HKV*D] (already rotated, positions 0..pos-1),
+ * and causal attention over positions 0..pos (reference ops.cpp:303-356)
+ * writes out [H*D]. k_stored/v_stored (nullable) receive the row read back
+ * from the cache at pos. */
+FISH_API int fbx_attention_decode(const float* q, const float* k_cache, const float* v_cache, const float* k_new,
+                                  const float* v_new, int pos, int H, int HKV, int D, int rot_dim, int neox,
+                                  float freq_base, int kv_f16, float* out, float* k_stored, float* v_stored);
+
 /* RoPE (reference ops.cpp:126-156) on q [T][H*D] and k [T][HKV*D] in place,
  * token t at position pos0+t, with a table built like rope_build
  * (ops.cpp:75-124) for freq_base and rot_dim. */

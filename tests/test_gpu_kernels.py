@@ -199,6 +199,37 @@ def test_attention_vs_oracle(lib, oracle, f16, T, pos0, H, HKV, D):
     assert np.max(np.abs(out - want)) <= 2e-5 * max(1.0, np.max(np.abs(want)))
 
 
+@pytest.mark.parametrize("f16", [0, 1])
+@pytest.mark.parametrize("pos,H,HKV,D,rot,neox", [(0, 8, 4, 64, 64, 0), (37, 32, 8, 128, 128, 0),
+                                                  (200, 28, 4, 128, 128, 1), (1000, 64, 8, 128, 128, 0),
+                                                  (3000, 8, 8, 64, 32, 1), (70, 16, 2, 128, 64, 0)])
+def test_fused_decode_attention(lib, oracle, f16, pos, H, HKV, D, rot, neox):
+    """RoPE + KV append + attention in one kernel vs the unfused pieces:
+    RoPE on the GPU (bit-exact with the oracle, test_rope_bit_exact) then the
+    oracle's attention; the appended row is bit-exact."""
+    rng = np.random.default_rng(pos + H + D + f16)
+    base = 500000.0
+    q = rng.standard_normal(H * D).astype(np.float32)
+    kc = rng.standard_normal((max(pos, 1), HKV * D)).astype(np.float32)
+    vc = rng.standard_normal((max(pos, 1), HKV * D)).astype(np.float32)
+    kn = rng.standard_normal(HKV * D).astype(np.float32)
+    vn = rng.standard_normal(HKV * D).astype(np.float32)
+    out = np.zeros(H * D, np.float32)
+    ks = np.zeros(HKV * D, np.float32)
+    vs = np.zeros(HKV * D, np.float32)
+    assert lib.fbx_attention_decode(_p(q), _p(kc), _p(vc), _p(kn), _p(vn), pos, H, HKV, D, rot, neox, base, f16,
+                                    _p(out), _p(ks), _p(vs)) == 0
+    qr, kr = q.copy(), kn.copy()
+    assert lib.fbx_rope(_p(qr), _p(kr), 1, H, HKV, D, rot, neox, base, pos) == 0
+    rnd = oracle.fp16_round if f16 else (lambda a: a)
+    assert np.array_equal(ks, rnd(kr)) and np.array_equal(vs, rnd(vn))
+    keys = rnd(np.concatenate([kc[:pos], kr[None, :]]))
+    vals = rnd(np.concatenate([vc[:pos], vn[None, :]]))
+    want = oracle.attention(qr[None, :], keys, vals, H, HKV, D, pos, 1, 1.0 / np.sqrt(D))[0]
+    # online softmax over blocks and a cluster merge vs the two-pass softmax
+    assert np.max(np.abs(out - want)) <= 2e-5 * max(1.0, np.max(np.abs(want)))
+
+
 def test_argmax_first_index(lib):
     x = np.zeros((3, 100000), np.float32)
     x[0, 5] = 1.0
