@@ -383,11 +383,15 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     const size_t pblk = (size_t)16 * D;   // elements of one page's piece of this head
     const int b_own = pos / kDecKeys;
 
-    auto issue = [&](int i) {   // bulk copies of my i-th block into slot i & 1
+    // bulk copies of my i-th block into slot i & 1: lane 0 sets the expected
+    // bytes, lane pp (< 4) reads its page-table entry and copies that page
+    auto issue = [&](int i) {   // called by all lanes of warp 0
         const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0), np = (kb + 15) / 16;
         uint64_t* br = &bar[i & 1];
-        mbar_expect_tx(br, (uint32_t)(2 * np * pblk * sizeof(E)));
-        for (int pp = 0; pp < np; ++pp) {
+        if (lane == 0) mbar_expect_tx(br, (uint32_t)(2 * np * pblk * sizeof(E)));
+        __syncwarp();
+        if (lane < np) {
+            const int pp = lane;
             int page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + pp];
             if (page < 0 || page >= kv.n_pages) {
                 if (kv.err) atomicExch(kv.err, 5);
@@ -407,7 +411,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         mbar_fence_init();
     }
     __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {
         if (nb_mine > 0) issue(0);
         if (nb_mine > 1) issue(1);
     }
@@ -559,7 +563,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             so[g * kMaxD + d] = o;
         }
         __syncthreads();
-        if (tid == 0 && i + 2 < nb_mine) issue(i + 2);
+        if (warp == 0 && i + 2 < nb_mine) issue(i + 2);
     }
     if (failed_at >= 0) {
         // let the copies still in flight (blocks failed_at, failed_at + 1) land before the CTA can exit
@@ -571,18 +575,32 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         if (tid < G) { sm[tid] = -INFINITY; sl[tid] = 0.0f; }
     }
     cluster.sync();
-    // merge the C partials (distributed shared memory); CTA r takes outputs r*128 + tid, step C*128
+    // merge the C partials through distributed shared memory: CTA r takes
+    // outputs r*128 + tid (step C*128); every remote value is requested before
+    // any is used
     for (int idx = r * kDecThreads + tid; idx < G * D; idx += C * kDecThreads) {
         const int g = idx / D, d = idx % D;
+        float mv[16], lv[16], ov[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C) {
+                mv[rr] = *cluster.map_shared_rank(sm + g, rr);
+                lv[rr] = *cluster.map_shared_rank(sl + g, rr);
+                ov[rr] = *cluster.map_shared_rank(so + g * kMaxD + d, rr);
+            }
+        }
         float M = -INFINITY;
-        for (int rr = 0; rr < C; ++rr) M = fmaxf(M, *cluster.map_shared_rank(sm + g, rr));
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr)
+            if (rr < C) M = fmaxf(M, mv[rr]);
         float Ls = 0.0f, O = 0.0f;
-        for (int rr = 0; rr < C; ++rr) {
-            const float mr = *cluster.map_shared_rank(sm + g, rr);
-            if (mr == -INFINITY) continue;
-            const float w = expf(mr - M);
-            Ls += *cluster.map_shared_rank(sl + g, rr) * w;
-            O += *cluster.map_shared_rank(so + g * kMaxD + d, rr) * w;
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C && mv[rr] != -INFINITY) {
+                const float w = expf(mv[rr] - M);
+                Ls += lv[rr] * w;
+                O += ov[rr] * w;
+            }
         }
         out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
     }
