@@ -659,15 +659,26 @@ const char* fish_engine_json(fish_ctx* ctx) {
     std::lock_guard<std::mutex> lock(ctx->mu);
     if (!ctx->eng) return "{}";
     fb::Engine& e = *ctx->eng;
-    char b[512];
+    long long wr[128] = {0};
+    const int kerr = fbk_take_error_flag();
+    const int nwr = fbk_take_wait_record(wr);
+    std::string recs = "[";
+    for (int i = 0; i < std::min(nwr, 8); ++i) {
+        if (i) recs += ",";
+        recs += "[";
+        for (int j = 0; j < 16; ++j) recs += (j ? "," : "") + std::to_string(wr[i * 16 + j]);
+        recs += "]";
+    }
+    recs += "]";
+    char b[1024];
     std::snprintf(b, sizeof(b),
                   "{\"device\":\"%s\",\"kv_page_size\":%d,\"kv_free_pages\":%d,\"kv_bytes\":%llu,"
                   "\"weights_device_bytes\":%llu,\"greedy_graph_kernels\":%d,\"step_graph_kernels\":%d,"
-                  "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d}",
+                  "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d,\"wait_failures\":%d,\"wait_records\":",
                   e.device_name().c_str(), e.page_size(), e.free_pages(), (unsigned long long)e.kv_bytes(),
                   (unsigned long long)e.device_weight_bytes(), e.graph_kernels(0), e.graph_kernels(1),
-                  (double)e.last_greedy_ms(), fbk_take_error_flag());
-    buf = b;
+                  (double)e.last_greedy_ms(), kerr, nwr);
+    buf = std::string(b) + recs + "}";
     return buf.c_str();
 }
 

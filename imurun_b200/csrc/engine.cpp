@@ -133,7 +133,7 @@ Engine::~Engine() {
     cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
     cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
     cudaFree(act_mem_); cudaFree(att_scratch_);
-    cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_);
+    cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_); cudaFree(amax_keys_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
     if (h_pinned_) cudaFreeHost(h_pinned_);
@@ -498,6 +498,8 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&argmax_, sizeof(int32_t) * kMaxBatch));
+    CK(cudaMalloc(&amax_keys_, sizeof(unsigned long long) * kMaxBatch));
+    CK(cudaMemset(amax_keys_, 0, sizeof(unsigned long long) * kMaxBatch));
     CK(cudaMalloc(&greedy_out_, sizeof(int32_t) * greedy_cap_));
     CK(cudaMalloc(&greedy_step_, sizeof(int32_t)));
     CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * 3 * kMaxBatch));
@@ -725,7 +727,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
 }
 
 bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi, const float* xf,
-                  int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro) {
+                  int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro, unsigned long long* keys) {
     for (int t0 = 0; t0 < T; t0 += 8) {
         const int nt = std::min(8, T - t0);
         GemvArgs g{};
@@ -748,6 +750,7 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         s.epi = epi;
         s.expert = expert;
         s.expert_bytes = w.expert_bytes;
+        s.amax = keys ? keys + t0 : nullptr;
         CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
     }
     return true;
@@ -872,7 +875,8 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
 }
 
 // Final norm + output projection for x rows [row0, row0+n) into logits rows 0..n-1.
-bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err) {
+bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err, unsigned long long* keys, bool* keyed) {
+    if (keyed) *keyed = false;
     const Config& c = cfg_;
     const int E = c.n_embd;
     ActQ a = act_;
@@ -880,7 +884,8 @@ bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err) {
     const DevW* wo[1] = {&out_w_};
     if (fusable(wo, 1, n)) {
         const GemvPro pro{PRO_NORM, x_ + (size_t)row0 * E, E, nullptr, 0, out_norm_, c.eps};
-        return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, nullptr, 0, nullptr, err, &pro);
+        if (keyed) *keyed = keys != nullptr;
+        return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, nullptr, 0, nullptr, err, &pro, keys);
     }
     CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_ + (size_t)row0 * E, E, out_norm_, c.eps, n, E, xb_, E, &a, want32_e_, wantk_e_,
                                        stream_));
@@ -909,11 +914,14 @@ bool Engine::capture_graph(int key, std::string* err) {
     std::string e2;
     bool ok = fbk_embed(embd_.type, embd_.d, cfg_.n_embd, embd_.n_out, ids_, T, x_, cfg_.n_embd, fbk_gemv_error_flag(), stream_) == 0;
     ok = ok && run_layers(T, cfg_.n_ctx, true, &e2);
-    ok = ok && run_head(0, T, logits_, &e2);
+    bool keyed = false;
+    ok = ok && run_head(0, T, logits_, &e2, amax_keys_, &keyed);
     if (key == 0)
-        ok = ok && fbk_greedy_advance(logits_, cfg_.vocab, ids_, tok_pos_, greedy_out_, greedy_step_, stream_) == 0;
+        ok = ok && (keyed ? fbk_greedy_from_keys(amax_keys_, ids_, tok_pos_, greedy_out_, greedy_step_, stream_)
+                          : fbk_greedy_advance(logits_, cfg_.vocab, ids_, tok_pos_, greedy_out_, greedy_step_, stream_)) == 0;
     else
-        ok = ok && fbk_argmax(logits_, cfg_.vocab, T, cfg_.vocab, argmax_, stream_) == 0;
+        ok = ok && (keyed ? fbk_argmax_from_keys(amax_keys_, T, argmax_, stream_)
+                          : fbk_argmax(logits_, cfg_.vocab, T, cfg_.vocab, argmax_, stream_)) == 0;
     const cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
     if (!ok || ce != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);

@@ -128,9 +128,13 @@ private:
     // distinct: the T tokens belong to T different sequences (decode steps),
     // so attention can append each token's K/V inside the fused kernel
     bool run_layers(int T, int max_ctx, bool distinct, std::string* err);
-    bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err);
+    // keys (nullable): argmax keys per row accumulated by the output GEMV;
+    // returns in *keyed whether they were (streamed kernel only)
+    bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err,
+                  unsigned long long* keys = nullptr, bool* keyed = nullptr);
     bool gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi,
-              const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr);
+              const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr,
+              unsigned long long* keys = nullptr);
     bool gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
                     const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro = nullptr);
     // true when a T-token GEMV over these matrices can build its own int8
@@ -176,6 +180,7 @@ private:
     int att_chunk_ = 32;
     int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;
     int32_t *greedy_out_ = nullptr, *greedy_step_ = nullptr;
+    unsigned long long* amax_keys_ = nullptr;   // [kMaxBatch] argmax keys, zero between steps
     int greedy_cap_ = 1 << 16;
     int32_t* h_pinned_ = nullptr;   // pinned staging for ids / tok_seq / tok_pos
 

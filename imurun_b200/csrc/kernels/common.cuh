@@ -37,6 +37,20 @@ __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// Argmax key of logit v at index i: ordered float bits above, inverted index
+// below, so an unsigned max picks the largest value and, among equal values,
+// the first index — the reference's strict '>' scan from -inf
+// (src/model.cpp:1939-1946). NaN and -inf never win (key 0 decodes to 0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    if (!(v > -INFINITY)) return 0ull;
+    uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+}
+__device__ __forceinline__ int argmax_index(unsigned long long key) {
+    return key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+}
+
 // Programmatic dependent launch (no-ops for launches without the attribute):
 // wait until the previous kernel on the stream has completed and its writes
 // are visible / let the next kernel be scheduled.

@@ -94,11 +94,12 @@ void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst) {
 
 // ============================================================ common pieces
 
-__device__ __forceinline__ void store_out(const GemvSeg& g, int rr, int t, float v) {
+__device__ __forceinline__ float store_out(const GemvSeg& g, int rr, int t, float v) {
     if (g.bias) v += g.bias[rr];
     float* yp = g.y + (size_t)t * g.ldy + rr;
-    if (g.epi == EPI_ADD) *yp += v;
-    else *yp = v;
+    if (g.epi == EPI_ADD) v += *yp;
+    *yp = v;
+    return v;
 }
 
 // ============================================================ direct kernel
@@ -281,10 +282,43 @@ constexpr int kXChunk = 272;                        // bytes per 256 activation 
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
+// Records of bounded waits that gave up (read with fbk_take_wait_record),
+// up to kWaitRecs, 16 values each:
+// [0] kind (1 producer/empty, 2 consumer/full), [1] CTA, [2] stage, [3] slot,
+// [4] parity, [5] stages of the CTA, [6] ring slots, [7] stages the producer
+// has issued, [8] ns spent waiting, [9] ns since the kernel started, [10] warp,
+// [11] stage the producer is waiting to reuse (-1 none), [12] raw word of
+// full[slot], [13] raw word of empty[slot], [14] SM id, [15] smem bytes
+constexpr int kWaitRecs = 8;
+__device__ long long g_wait_rec[kWaitRecs][16];
+__device__ int g_wait_rec_n;
+
+__device__ __noinline__ void record_wait_fail(int kind, int s, int slot, int parity, int n_stages, int S, int issued,
+                                              unsigned long long t_start, unsigned long long t_kernel, int prod_wait,
+                                              const uint64_t* full, const uint64_t* empty, int smem_bytes) {
+    const int k = atomicAdd(&g_wait_rec_n, 1);
+    if (k >= kWaitRecs) return;
+    const unsigned long long now = gtimer();
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    long long* r = g_wait_rec[k];
+    r[0] = kind; r[1] = blockIdx.x; r[2] = s; r[3] = slot; r[4] = parity; r[5] = n_stages; r[6] = S; r[7] = issued;
+    r[8] = (long long)(now - t_start); r[9] = (long long)(now - t_kernel); r[10] = threadIdx.x >> 5;
+    r[11] = prod_wait; r[12] = (long long)full[slot]; r[13] = (long long)empty[slot]; r[14] = smid; r[15] = smem_bytes;
+    __threadfence();
+}
+
+// Ring slots: consumer pair q (= stage & 3) owns slots [q*Sq, q*Sq + Sq), and
+// its j-th stage (j = stage >> 2) uses slot q*Sq + j % Sq in phase j / Sq. A
+// pair therefore waits on each of its slots phase after phase and never for a
+// phase two ahead of the barrier, which a parity wait could not tell apart.
+__device__ __forceinline__ int ring_slot(int s, int Sq) { return (s & 3) * Sq + (s >> 2) % Sq; }
+__device__ __forceinline__ int ring_phase(int s, int Sq) { return (s >> 2) / Sq; }
+
 struct StreamJobs {
     int tile0[kMaxSeg + 1];  // 8-row tiles: segment s owns tiles [tile0[s], tile0[s+1])
     int n_groups;            // 2048-value groups per row
-    int stages;              // ring slots
+    int stages;              // ring slots (4 x slots per consumer pair)
     int slot_bytes;          // bytes per slot (8 x the largest piece)
     int tiles_per_cta;
     int xk_bytes, x32_bytes; // per-token bytes of the two activation images (0 = not built)
@@ -476,14 +510,19 @@ template <int NT>
 __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
+    const unsigned long long t_kernel = gtimer();
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8);
     float* s_scale = reinterpret_cast<float*>(smem + 2 * kMaxStages * 8 + 16);   // [4]
+    volatile int* s_issued = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8 + 4);
+    volatile int* s_prod_wait = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8 + 8);
+    unsigned dyn_smem;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
     __shared__ double s_part[8];
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
-    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages;
+    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages, Sq = S / 4;
     int n_tiles = jobs.tile0[0];
 #pragma unroll
     for (int i = 1; i <= kMaxSeg; ++i)
@@ -509,6 +548,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
         if (threadIdx.x == i) s_tile0[i] = jobs.tile0[i];
     if (threadIdx.x == 0) {
         *s_abort = 0;
+        *s_issued = 0;
+        *s_prod_wait = -1;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 2);
@@ -529,13 +570,24 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
                 const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
                 const int nb = row_blocks(g.type, K);
                 const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
-                const int slot = s % S;
-                if (s >= S && !mbar_wait(&empty[slot], (uint32_t)((s / S - 1) & 1), s_abort)) { ok = false; break; }
+                const int slot = ring_slot(s, Sq), phase = ring_phase(s, Sq);
+                if (phase > 0) {
+                    const unsigned long long tw = gtimer();
+                    *s_prod_wait = s - 4 * Sq;
+                    if (!mbar_wait(&empty[slot], (uint32_t)((phase - 1) & 1), s_abort)) {
+                        record_wait_fail(1, s, slot, (phase - 1) & 1, n_stages, S, issued, tw, t_kernel, s - 4 * Sq, full,
+                                         empty, (int)dyn_smem);
+                        ok = false;
+                        break;
+                    }
+                    *s_prod_wait = -1;
+                }
                 const uint8_t* src = base + (size_t)(tile - s_tile0[sg]) * kTileRows * g.row_stride +
                                      (size_t)kTileRows * group_offset(g.type, gi);
                 if (bytes <= (uint32_t)jobs.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, jobs.err)) {
                     mbar_expect_tx(&full[slot], bytes);
                     bulk_g2s(ring + (size_t)slot * jobs.slot_bytes, src, bytes, &full[slot]);
+                    *s_issued = s + 1;
                 } else {
                     mbar_arrive(&full[slot]);   // keep the ring moving; the stage holds stale bytes
                 }
@@ -545,7 +597,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
                 if (jobs.err) atomicExch(jobs.err, 1);
                 *s_abort = 1;
                 // let the copies in flight land before the CTA can exit
-                for (int k = max(0, issued - S); k < issued; ++k) mbar_wait_bounded(&full[k % S], (uint32_t)((k / S) & 1));
+                for (int k = max(0, issued - S); k < issued; ++k)
+                    mbar_wait_bounded(&full[ring_slot(k, Sq)], (uint32_t)(ring_phase(k, Sq) & 1));
             }
         }
         return;
@@ -564,8 +617,17 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
         const int type = s_seg[seg_index(s_tile0, args.nseg, tile)].type;
         const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
         const int piece = (int)group_bytes(type, gbk);
-        const int slot = s % S;
-        if (!mbar_wait(&full[slot], (uint32_t)((s / S) & 1), s_abort)) { ok = false; break; }
+        const int slot = ring_slot(s, Sq), phase = ring_phase(s, Sq);
+        {
+            const unsigned long long tw = gtimer();
+            if (!mbar_wait(&full[slot], (uint32_t)(phase & 1), s_abort)) {
+                if (!*s_abort)
+                    record_wait_fail(2, s, slot, phase & 1, n_stages, S, *s_issued, tw, t_kernel, *s_prod_wait, full,
+                                     empty, (int)dyn_smem);
+                ok = false;
+                break;
+            }
+        }
         const uint8_t* pc = ring + (size_t)slot * jobs.slot_bytes + (size_t)r8 * piece;
         float c[NT];
 #pragma unroll
@@ -636,6 +698,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
     consumers_sync();
     if (*s_abort) return;
     // rows of this CTA: sum the group partials in group order
+    unsigned long long best[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) best[t] = 0ull;
     const int n_rows = (t_end - t_begin) * kTileRows;
     for (int idx = threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
         const int tl = idx / kTileRows, rr = idx % kTileRows, tile = t_begin + tl;
@@ -643,10 +708,35 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs 
         const GemvSeg& g = s_seg[sg];
         const int row = (tile - s_tile0[sg]) * kTileRows + rr;
         if (row >= g.rows) continue;
-        for (int t = 0; t < T; ++t) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t >= T) break;
             float v = 0.0f;
             for (int gi = 0; gi < G; ++gi) v += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
-            store_out(g, row, t, v);
+            v = store_out(g, row, t, v);
+            if (g.amax) {
+                const unsigned long long key = argmax_key(v, row);
+                best[t] = key > best[t] ? key : best[t];
+            }
+        }
+    }
+    if (s_seg[0].amax) {   // one segment (the output projection): merge the CTA's keys, one atomic per token
+        __shared__ unsigned long long s_best[kConsumers][4];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            unsigned long long k = best[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+                k = ok > k ? ok : k;
+            }
+            if (lane == 0) s_best[warp][t] = k;
+        }
+        consumers_sync();
+        if (threadIdx.x < T) {
+            unsigned long long k = 0ull;
+            for (int w = 0; w < kConsumers; ++w) k = s_best[w][threadIdx.x] > k ? s_best[w][threadIdx.x] : k;
+            if (k) atomicMax(&s_seg[0].amax[threadIdx.x], k);
         }
     }
 }
@@ -674,6 +764,19 @@ extern "C" int* fbk_gemv_error_flag() {
         cudaMemset(g_err, 0, sizeof(int));
     }
     return g_err;
+}
+
+extern "C" int fbk_take_wait_record(long long* rec) {
+    long long h[kWaitRecs][16] = {};
+    int n = 0;
+    if (cudaMemcpyFromSymbol(&n, g_wait_rec_n, sizeof(int)) != cudaSuccess) return -1;
+    if (n) {
+        if (cudaMemcpyFromSymbol(h, g_wait_rec, sizeof(h)) != cudaSuccess) return -1;
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_wait_rec_n, &zero, sizeof(int));
+    }
+    for (int i = 0; i < kWaitRecs * 16; ++i) rec[i] = (&h[0][0])[i];
+    return n;
 }
 
 extern "C" int fbk_take_error_flag() {
@@ -735,11 +838,11 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
         ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
         const size_t part = ((size_t)jobs.tiles_per_cta * jobs.n_groups * kTileRows * NT * 4 + 127) / 128 * 128;
         const long long left = (long long)budget - kHdrBytes - (long long)xbytes - (long long)part;
-        stages = (int)std::min<long long>(kMaxStages, left > 0 ? left / slot : 0);
+        stages = 4 * (int)std::min<long long>(kMaxStages / 4, left > 0 ? left / (4LL * slot) : 0);
         smem = kHdrBytes + xbytes + part + (size_t)stages * slot;
-        if (stages >= 3 || cps == 1) break;
+        if (stages >= 4 || cps == 1) break;
     }
-    if (stages < 2) return (int)cudaErrorInvalidValue;
+    if (stages < 4) return (int)cudaErrorInvalidValue;
     jobs.stages = stages;
     return (int)fbk_launch(k_gemv_stream<NT>, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
 }
@@ -755,7 +858,7 @@ extern "C" int fbk_gemv_streamable(const GemvArgs* a) {
     }
     if (a->K % 8) return 0;
     static const bool stream_off = getenv("FISH_GEMV_DIRECT") != nullptr;
-    return stream_off && a->pro.mode == PRO_ACT ? 0 : 1;
+    return stream_off ? 0 : 1;
 }
 
 extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {

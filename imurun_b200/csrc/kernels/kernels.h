@@ -34,6 +34,7 @@ struct GemvSeg {
     const int32_t* expert;  // optional: rows start at w + (*expert) * expert_bytes
     size_t expert_bytes;
     size_t w_bytes;         // bytes readable from w (every expert); reads outside are skipped and flagged
+    unsigned long long* amax;  // optional [T]: running argmax key per token (streamed kernel, EPI_STORE)
 };
 
 constexpr int kMaxSeg = 4;
@@ -93,6 +94,10 @@ int fbk_embed(int type, const uint8_t* w, int E, int n_rows, const int32_t* ids,
 // Shared device error flag of the kernels (0 = none); read-and-clear.
 int* fbk_gemv_error_flag();
 int fbk_take_error_flag();
+// Bounded waits of the streamed GEMV that gave up since the last call: up to
+// 8 records of 16 values (see gemv.cu) into rec[128]; returns how many
+// occurred (may exceed 8).
+int fbk_take_wait_record(long long* rec);
 
 // Paged KV cache as the kernels see it. A page holds `page_size` positions of
 // every layer: per layer a K block [HKV][page_size][D] then a V block of the
@@ -143,5 +148,11 @@ int fbk_add(float* y, const float* x, size_t n, cudaStream_t st);
 // Device-side wait of ns nanoseconds (profiling aid).
 int fbk_delay(unsigned long long ns, cudaStream_t st);
 int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st);
+// Argmax keys (value, first index) accumulated by a GEMV's epilogue
+// (GemvSeg::amax): decode them into out[t] / advance a greedy loop like
+// fbk_greedy_advance, and reset the keys for the next step.
+int fbk_argmax_from_keys(unsigned long long* keys, int T, int32_t* out, cudaStream_t st);
+int fbk_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out, int32_t* step,
+                         cudaStream_t st);
 int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel, cudaStream_t st);
 }

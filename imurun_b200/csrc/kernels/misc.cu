@@ -46,17 +46,40 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* w, int n, i
     }
 }
 
+// grid (ceil(E / 256), T): one value per thread
 __global__ void k_embed(int type, const uint8_t* __restrict__ w, int E, int n_rows, const int32_t* __restrict__ ids,
                         float* __restrict__ x, int ldx, int* err) {
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x;
+    const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
     int row = ids[t];
     if (row < 0 || row >= n_rows) {
-        if (err && threadIdx.x == 0) atomicExch(err, 4);
+        if (err && i == 0) atomicExch(err, 4);
         row = 0;
     }
-    for (int i = threadIdx.x; i < E; i += blockDim.x) x[(size_t)t * ldx + i] = dequant_at(type, w, E, row, i);
+    if (i < E) x[(size_t)t * ldx + i] = dequant_at(type, w, E, row, i);
+}
+
+__global__ void k_argmax_from_keys(unsigned long long* keys, int T, int32_t* out) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = threadIdx.x;
+    if (t < T) {
+        out[t] = argmax_index(keys[t]);
+        keys[t] = 0ull;
+    }
+}
+
+__global__ void k_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out,
+                                   int32_t* step) {
+    pdl_trigger();
+    pdl_wait();
+    const int bi = argmax_index(keys[0]);
+    keys[0] = 0ull;
+    ids[0] = bi;
+    out[*step] = bi;
+    *step += 1;
+    tok_pos[0] += 1;
 }
 
 __global__ void k_add(float* __restrict__ y, const float* __restrict__ x, size_t n) {
@@ -234,7 +257,18 @@ extern "C" int fbk_greedy_advance(const float* logits, int V, int32_t* ids, int3
 extern "C" int fbk_embed(int type, const uint8_t* w, int E, int n_rows, const int32_t* ids, int T, float* x, int ldx,
                          int* err, cudaStream_t st) {
     if (T <= 0) return 0;
-    return (int)fbk_launch(k_embed, dim3(T), dim3(256), 0, st, type, w, E, n_rows, ids, x, ldx, err);
+    return (int)fbk_launch(k_embed, dim3((E + 255) / 256, T), dim3(256), 0, st, type, w, E, n_rows, ids, x, ldx, err);
+}
+
+extern "C" int fbk_argmax_from_keys(unsigned long long* keys, int T, int32_t* out, cudaStream_t st) {
+    if (T <= 0) return 0;
+    if (T > 1024) return (int)cudaErrorInvalidValue;
+    return (int)fbk_launch(k_argmax_from_keys, dim3(1), dim3(T), 0, st, keys, T, out);
+}
+
+extern "C" int fbk_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out,
+                                    int32_t* step, cudaStream_t st) {
+    return (int)fbk_launch(k_greedy_from_keys, dim3(1), dim3(1), 0, st, keys, ids, tok_pos, out, step);
 }
 
 extern "C" int fbk_add(float* y, const float* x, size_t n, cudaStream_t st) {
