@@ -459,16 +459,24 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
     }
     if (pro.mode == PRO_NORM) {
         // the reference's double sum (src/ops.cpp:18-23) in the exact order of
-        // k_rmsnorm_quant: 128 threads, float4 strides, warp trees, 4 partials
+        // k_rmsnorm_quant: 128 threads, float4 strides, warp trees, 4 partials;
+        // a thread's loads are all issued before the first is used
         const int grp = ct >> 7, gt = ct & 127;
         for (int t0 = 0; t0 < T; t0 += 2) {
             const int t = t0 + grp;
             if (t < T) {
                 const float* xr = pro.src + (size_t)t * pro.ld;
                 double s = 0.0;
-                for (int i = gt * 4; i < K; i += 128 * 4) {
-                    const float4 f = *reinterpret_cast<const float4*>(xr + i);
-                    s += (double)f.x * f.x + (double)f.y * f.y + (double)f.z * f.z + (double)f.w * f.w;
+                for (int i0 = gt * 4; i0 < K; i0 += 8 * 512) {
+                    float4 f[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (i0 + 512 * k < K) f[k] = *reinterpret_cast<const float4*>(xr + i0 + 512 * k);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (i0 + 512 * k < K)
+                            s += (double)f[k].x * f[k].x + (double)f[k].y * f[k].y + (double)f[k].z * f[k].z +
+                                 (double)f[k].w * f[k].w;
                 }
                 s = warp_sum_d(s);
                 if (lane == 0) s_part[grp * 4 + (gt >> 5)] = s;
@@ -482,32 +490,52 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
             consumers_sync();
         }
     }
+    // quantisation: warp w takes chunks w, w + 8, ...; each batch of up to 4
+    // chunks loads everything it needs before computing
     const int n_chunks = (K + 255) / 256;
+    constexpr int kB = 2;
     for (int t = 0; t < T; ++t) {
-        for (int c = warp; c < n_chunks; c += kConsumers) {
-            const int i0 = c * 256 + 8 * lane;
-            float v[8];
-            if (pro.mode == PRO_NORM) {
-                ld8(pro.src + (size_t)t * pro.ld, i0, K, v);
-                const float sc = s_scale[t];
+        const float* xr = pro.src + (size_t)t * pro.ld;
+        const float* ur = pro.mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
+        for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kB) {
+            float va[kB][8], ua[kB][8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(v[i], sc), pro.w[i0 + i]) : 0.0f;
-            } else if (pro.mode == PRO_SILU) {
-                float gv[8], uv[8];
-                ld8(pro.src + (size_t)t * pro.ld, i0, K, gv);
-                ld8(pro.src2 + (size_t)t * pro.ld2, i0, K, uv);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i]))), uv[i]);
-            } else {
-                ld8(pro.src + (size_t)t * pro.ld, i0, K, v);
+            for (int k = 0; k < kB; ++k) {
+                const int c = c0 + kConsumers * k;
+                if (c < n_chunks) {
+                    const int i0 = c * 256 + 8 * lane;
+                    ld8(xr, i0, K, va[k]);
+                    if (pro.mode == PRO_NORM) ld8(pro.w, i0, K, ua[k]);
+                    else if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
+                }
             }
-            ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
+#pragma unroll
+            for (int k = 0; k < kB; ++k) {
+                const int c = c0 + kConsumers * k;
+                if (c < n_chunks) {
+                    const int i0 = c * 256 + 8 * lane;
+                    float v[8];
+                    if (pro.mode == PRO_NORM) {
+                        const float sc = s_scale[t];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(va[k][i], sc), ua[k][i]) : 0.0f;
+                    } else if (pro.mode == PRO_SILU) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            v[i] = __fmul_rn(__fdiv_rn(va[k][i], __fadd_rn(1.0f, expf(-va[k][i]))), ua[k][i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[i] = va[k][i];
+                    }
+                    ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
+                }
+            }
         }
     }
 }
 
 template <int NT>
-__global__ void __launch_bounds__(32 * (kConsumers + 1)) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
+__global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
     const unsigned long long t_kernel = gtimer();
