@@ -563,6 +563,22 @@ int fish_decode_greedy(fish_ctx* ctx, int32_t first, int n_steps, int32_t* out_i
     return n;
 }
 
+int fish_trace_decode(fish_ctx* ctx, int32_t first, int n_steps, uint64_t* out, int cap) {
+    if (!ctx || !out || cap <= 0 || n_steps <= 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    if (fbk_trace_enable(cap)) { ctx->err = "trace buffer"; return -2; }
+    std::vector<int32_t> ids(n_steps);
+    std::string err;
+    const int n = ctx->eng->decode_greedy(0, first, n_steps, ids.data(), &err);
+    const int got = fbk_trace_dump(reinterpret_cast<unsigned long long*>(out), cap);
+    fbk_trace_enable(0);
+    if (n < 0) { ctx->err = err; return -2; }
+    ctx->cache_ids.push_back(first);
+    for (int i = 0; i + 1 < n; ++i) ctx->cache_ids.push_back(ids[i]);
+    return got;
+}
+
 int fish_kv_len(fish_ctx* ctx) {
     if (!ctx) return -1;
     std::lock_guard<std::mutex> lock(ctx->mu);

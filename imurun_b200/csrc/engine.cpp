@@ -698,7 +698,7 @@ bool Engine::fusable(const DevW* const* ws, int n, int T) const {
 }
 
 bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
-                        const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro) {
+                        const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro, bool swiglu) {
     for (int t0 = 0; t0 < T; t0 += 8) {
         const int nt = std::min(8, T - t0);
         GemvArgs g{};
@@ -707,6 +707,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
         g.T = nt;
         set_act_rows(g, a, t0, g.K);
         if (pro) g.pro = *pro;
+        g.swiglu = swiglu ? 1 : 0;
         double bytes = 0.0;
         for (int i = 0; i < n; ++i) {
             GemvSeg& s = g.seg[i];
@@ -855,14 +856,17 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
                 const int lds[2] = {F, F};
                 if (fuse_ffn) {
                     const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.ffn_norm, c.eps};
-                    if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro)) return false;
+                    if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro, true)) return false;
                 } else {
                     if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
                 }
             }
             a.K = F;
             const DevW* wd[1] = {&L.wd};
-            if (fusable(wd, 1, T)) {
+            if (fuse_ffn && fusable(wd, 1, T)) {   // h = silu(g) * u already in g_
+                const GemvPro pro{PRO_QUANT, g_, F, nullptr, 0, nullptr, 0.0f};
+                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+            } else if (fusable(wd, 1, T)) {
                 const GemvPro pro{PRO_SILU, g_, F, u_, F, nullptr, 0.0f};
                 if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
             } else {

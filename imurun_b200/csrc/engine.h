@@ -136,7 +136,8 @@ private:
               const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr,
               unsigned long long* keys = nullptr);
     bool gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
-                    const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro = nullptr);
+                    const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro = nullptr,
+                    bool swiglu = false);
     // true when a T-token GEMV over these matrices can build its own int8
     // activations (streamed kernel with a prologue)
     bool fusable(const DevW* const* ws, int n, int T) const;

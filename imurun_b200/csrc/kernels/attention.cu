@@ -13,6 +13,7 @@
 #include "kernels.h"
 #include "launch.cuh"
 #include "tma.cuh"
+#include "trace.cuh"
 
 namespace fb {
 
@@ -362,7 +363,14 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     cg::cluster_group cluster = cg::this_cluster();
     const int C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
     pdl_trigger();
+    const bool tr = tracing() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    __shared__ int s_tseq;
+    if (tr && threadIdx.x == 0) {
+        s_tseq = trace_launch(TR_ATTN);
+        trace_ev(TR_ATTN, EV_START, s_tseq);
+    }
     pdl_wait();
+    if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
     const int t = blockIdx.z, hk = blockIdx.y, G = H / HKV;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
@@ -471,6 +479,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         sl[tid] = 0.0f;
     }
     __syncthreads();
+    if (tr && tid == 0) trace_ev(TR_ATTN, 4, s_tseq);   // q rotated, own row stored
 
     const int dpp = D / 8;                     // dims per lane in a key's dot
     const int part = lane & 7;
@@ -481,6 +490,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             failed_at = i;
             break;
         }
+        if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 5, s_tseq);   // first block landed
         const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0);
         E* K = sk + (size_t)(i & 1) * L::kv_elems;
         E* V = sv + (size_t)(i & 1) * L::kv_elems;
@@ -535,6 +545,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             }
         }
         __syncthreads();
+        if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 8, s_tseq);   // scores done
         // online softmax per head (warp g, g + 4)
         for (int g = warp; g < G; g += kDecThreads / 32) {
             const float s0 = lane < kb ? ss[g * kDecKeys + lane] : -INFINITY;
@@ -554,6 +565,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             }
         }
         __syncthreads();
+        if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 9, s_tseq);   // softmax done
         // p.V: thread = one dim of one head (heads tid / D, tid / D + 128 / D, ...)
         for (int g = tid / D; g < G; g += kDecThreads / D) {
             const int d = tid % D;
@@ -563,6 +575,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             so[g * kMaxD + d] = o;
         }
         __syncthreads();
+        if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 10, s_tseq);   // p.V done
         if (warp == 0 && i + 2 < nb_mine) issue(i + 2);
     }
     if (failed_at >= 0) {
@@ -574,7 +587,9 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         }
         if (tid < G) { sm[tid] = -INFINITY; sl[tid] = 0.0f; }
     }
+    if (tr && tid == 0) trace_ev(TR_ATTN, 6, s_tseq);   // blocks done
     cluster.sync();
+    if (tr && tid == 0) trace_ev(TR_ATTN, 7, s_tseq);   // cluster barrier passed
     // merge the C partials through distributed shared memory: CTA r takes
     // outputs r*128 + tid (step C*128); every remote value is requested before
     // any is used
@@ -605,6 +620,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
     }
     cluster.sync();   // keep this CTA's shared memory alive until every remote read is done
+    if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_END, s_tseq);
 }
 
 }  // namespace fb
@@ -718,3 +734,5 @@ extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, con
     if (kv.f16) return launch_decode<__half>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
     return launch_decode<float>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
 }
+
+extern "C" int fbk_trace_set_attn(const fb::TraceState* s) { return (int)fb::trace_set(*s); }

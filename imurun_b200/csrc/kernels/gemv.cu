@@ -32,6 +32,7 @@
 #include "launch.cuh"
 #include "layout.cuh"
 #include "tma.cuh"
+#include "trace.cuh"
 #include "unit_math.cuh"
 
 namespace fb {
@@ -324,6 +325,7 @@ struct StreamJobs {
     int xk_bytes, x32_bytes; // per-token bytes of the two activation images (0 = not built)
     int* err;                // device error flag
     int wait_first;          // producer waits for the previous kernel (expert indices)
+    int pair;                // tiles alternate between segments 0 and 1 (SwiGLU epilogue)
 };
 
 // Segment of a tile (segments are copied to shared memory at kernel start,
@@ -334,6 +336,17 @@ __device__ __forceinline__ int seg_index(const int* tile0, int nseg, int tile) {
     for (int i = 1; i < kMaxSeg; ++i)
         if (i < nseg && tile >= tile0[i]) sg = i;
     return sg;
+}
+// Segment and segment-local tile of a tile: in pair mode tiles alternate
+// (gate tile j, up tile j) so one CTA holds both halves of its output rows.
+__device__ __forceinline__ void tile_seg(const int* tile0, int nseg, int pair, int tile, int& sg, int& lt) {
+    if (pair) {
+        sg = tile & 1;
+        lt = tile >> 1;
+    } else {
+        sg = seg_index(tile0, nseg, tile);
+        lt = tile - tile0[sg];
+    }
 }
 
 // Activation image in shared memory, per token:
@@ -548,6 +561,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     unsigned dyn_smem;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
     __shared__ double s_part[8];
+    __shared__ int s_tseq;
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
     const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages, Sq = S / 4;
@@ -574,6 +588,11 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
 #pragma unroll
     for (int i = 0; i <= kMaxSeg; ++i)
         if (threadIdx.x == i) s_tile0[i] = jobs.tile0[i];
+    const bool tr = tracing() && blockIdx.x == 0;
+    if (tr && threadIdx.x == 0) {
+        s_tseq = trace_launch(TR_GEMV);
+        trace_ev(TR_GEMV, EV_START, s_tseq);
+    }
     if (threadIdx.x == 0) {
         *s_abort = 0;
         *s_issued = 0;
@@ -593,7 +612,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
             bool ok = true;
             for (int s = 0; s < n_stages; ++s) {
                 const int tile = t_begin + s / G, gi = s % G;
-                const int sg = seg_index(s_tile0, args.nseg, tile);
+                int sg, lt;
+                tile_seg(s_tile0, args.nseg, jobs.pair, tile, sg, lt);
                 const GemvSeg& g = s_seg[sg];
                 const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
                 const int nb = row_blocks(g.type, K);
@@ -610,7 +630,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                     }
                     *s_prod_wait = -1;
                 }
-                const uint8_t* src = base + (size_t)(tile - s_tile0[sg]) * kTileRows * g.row_stride +
+                const uint8_t* src = base + (size_t)lt * kTileRows * g.row_stride +
                                      (size_t)kTileRows * group_offset(g.type, gi);
                 if (bytes <= (uint32_t)jobs.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, jobs.err)) {
                     mbar_expect_tx(&full[slot], bytes);
@@ -634,15 +654,19 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
 
     // consumers
     pdl_wait();
+    if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_WAITED, s_tseq);
     const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
     build_ximage(args, xi, wantk, want32, s_scale, s_part);
     consumers_sync();
+    if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
     const int half = warp & 1, quarter = warp >> 1;
     const int r8 = 4 * half + (lane >> 3), bl = lane & 7;
     bool ok = true;
     for (int s = quarter; s < n_stages; s += kConsumers / 2) {
         const int tile = t_begin + s / G, gi = s % G;
-        const int type = s_seg[seg_index(s_tile0, args.nseg, tile)].type;
+        int sgc, ltc;
+        tile_seg(s_tile0, args.nseg, jobs.pair, tile, sgc, ltc);
+        const int type = s_seg[sgc].type;
         const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
         const int piece = (int)group_bytes(type, gbk);
         const int slot = ring_slot(s, Sq), phase = ring_phase(s, Sq);
@@ -730,7 +754,26 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
 #pragma unroll
     for (int t = 0; t < NT; ++t) best[t] = 0ull;
     const int n_rows = (t_end - t_begin) * kTileRows;
-    for (int idx = threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
+    if (jobs.pair) {
+        // tiles (2j, 2j+1) are (gate, up) tile j: h = silu(g) * u into segment 0's y
+        const GemvSeg& g0 = s_seg[0];
+        for (int idx = threadIdx.x; idx < n_rows / 2; idx += kConsumers * 32) {
+            const int tp = idx / kTileRows, rr = idx % kTileRows;
+            const int tl = 2 * tp, row = ((t_begin + tl) >> 1) * kTileRows + rr;
+            if (row >= g0.rows) continue;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t >= T) break;
+                float gv = 0.0f, uv = 0.0f;
+                for (int gi = 0; gi < G; ++gi) {
+                    gv += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
+                    uv += part[((size_t)((tl + 1) * G + gi) * kTileRows + rr) * NT + t];
+                }
+                g0.y[(size_t)t * g0.ldy + row] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+            }
+        }
+    }
+    for (int idx = jobs.pair ? n_rows : threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
         const int tl = idx / kTileRows, rr = idx % kTileRows, tile = t_begin + tl;
         const int sg = seg_index(s_tile0, args.nseg, tile);
         const GemvSeg& g = s_seg[sg];
@@ -747,6 +790,10 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 best[t] = key > best[t] ? key : best[t];
             }
         }
+    }
+    if (tr) {
+        consumers_sync();
+        if (threadIdx.x == 0) trace_ev(TR_GEMV, EV_END, s_tseq);
     }
     if (s_seg[0].amax) {   // one segment (the output projection): merge the CTA's keys, one atomic per token
         __shared__ unsigned long long s_best[kConsumers][4];
@@ -793,6 +840,8 @@ extern "C" int* fbk_gemv_error_flag() {
     }
     return g_err;
 }
+
+extern "C" int fbk_trace_set_gemv(const TraceState* s) { return (int)trace_set(*s); }
 
 extern "C" int fbk_take_wait_record(long long* rec) {
     long long h[kWaitRecs][16] = {};
@@ -853,6 +902,9 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     jobs.tile0[0] = 0;
     for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kTileRows - 1) / kTileRows;
     for (int s = a->nseg; s < kMaxSeg; ++s) jobs.tile0[s + 1] = jobs.tile0[s];
+    jobs.pair = a->swiglu ? 1 : 0;
+    if (jobs.pair && (a->nseg != 2 || a->seg[0].rows != a->seg[1].rows || a->seg[0].epi != EPI_STORE))
+        return (int)cudaErrorInvalidValue;
     jobs.n_groups = row_groups(a->seg[0].type, a->K);
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
@@ -863,6 +915,7 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
         const int budget = max_smem / cps - 2048;
         ctas = std::min(n_tiles, num_sms() * cps);
         jobs.tiles_per_cta = (n_tiles + ctas - 1) / ctas;
+        if (jobs.pair) jobs.tiles_per_cta += jobs.tiles_per_cta & 1;   // whole (gate, up) pairs per CTA
         ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
         const size_t part = ((size_t)jobs.tiles_per_cta * jobs.n_groups * kTileRows * NT * 4 + 127) / 128 * 128;
         const long long left = (long long)budget - kHdrBytes - (long long)xbytes - (long long)part;
@@ -897,7 +950,7 @@ extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
         if (a->T == 2) return launch_stream<2>(a, st);
         return launch_stream<4>(a, st);
     }
-    if (a->pro.mode != PRO_ACT) return (int)cudaErrorInvalidValue;
+    if (a->pro.mode != PRO_ACT || a->swiglu) return (int)cudaErrorInvalidValue;
     GemvArgs ad = *a;
     if (!ad.err) ad.err = fbk_gemv_error_flag();
     a = &ad;

@@ -64,6 +64,8 @@ struct GemvArgs {
     const float* xf;        // f32 activations [T][ldxf] for F32/F16 weights
     int ldxf;
     GemvPro pro;            // streamed kernel only (T <= 4, quantised segments)
+    int swiglu;             // streamed kernel, 2 segments of equal rows (gate, up): the output
+                            // is h = silu(gate) * up into segment 0's y (src/model.cpp:1501-1506)
     int* err;               // device error flag (nullable): 3 = weight read out of range
 };
 
@@ -86,6 +88,10 @@ int fbk_block_sums(int type, const uint8_t* w, int rows, int K, const fb::ActQ* 
 // Programmatic dependent launch for every kernel launched after this call
 // (in-order streams and graphs captured from them).
 void fbk_set_pdl(int on);
+// Device-time trace of kernel phases (diagnostics): enable with a record
+// capacity (0 = off); dump returns the records (ns, tag, event, launch).
+int fbk_trace_enable(int cap);
+int fbk_trace_dump(unsigned long long* out, int cap);
 int fbk_pdl_enabled(void);
 
 // Embedding row gather + dequantisation: x[t][0..E) = dequant(embd row ids[t]).

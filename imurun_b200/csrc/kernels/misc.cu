@@ -3,6 +3,7 @@
 #include "kernels.h"
 #include "launch.cuh"
 #include "layout.cuh"
+#include "trace.cuh"
 
 namespace fb {
 
@@ -50,7 +51,11 @@ __device__ __forceinline__ float dequant_at(int type, const uint8_t* w, int n, i
 __global__ void k_embed(int type, const uint8_t* __restrict__ w, int E, int n_rows, const int32_t* __restrict__ ids,
                         float* __restrict__ x, int ldx, int* err) {
     pdl_trigger();
+    const bool tr = tracing() && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0;
+    const int tseq = tr ? trace_launch(TR_EMBED) : 0;
+    if (tr) trace_ev(TR_EMBED, EV_START, tseq);
     pdl_wait();
+    if (tr) trace_ev(TR_EMBED, EV_END, tseq);
     const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
     int row = ids[t];
     if (row < 0 || row >= n_rows) {
@@ -73,7 +78,10 @@ __global__ void k_argmax_from_keys(unsigned long long* keys, int T, int32_t* out
 __global__ void k_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out,
                                    int32_t* step) {
     pdl_trigger();
+    const int tseq = tracing() ? trace_launch(TR_KEYS) : 0;
+    if (tracing()) trace_ev(TR_KEYS, EV_START, tseq);
     pdl_wait();
+    if (tracing()) trace_ev(TR_KEYS, EV_END, tseq);
     const int bi = argmax_index(keys[0]);
     keys[0] = 0ull;
     ids[0] = bi;
@@ -287,4 +295,46 @@ extern "C" int fbk_moe_route(const float* logits, int T, int NE, int K, int norm
     if (T <= 0) return 0;
     if (NE > 256 || K > NE) return (int)cudaErrorInvalidValue;
     return (int)fbk_launch(k_moe_route, dim3((T + 63) / 64), dim3(64), 0, st, logits, T, NE, K, norm, sel, wsel);
+}
+
+extern "C" int fbk_trace_set_misc(const fb::TraceState* s) { return (int)fb::trace_set(*s); }
+
+// Tracing for every kernel that records: a shared buffer of `cap` records,
+// or off (cap <= 0). fbk_trace_dump copies the records out (4 values each:
+// globaltimer ns, tag, event, launch number) and returns how many.
+static unsigned long long* g_tbuf = nullptr;
+static int* g_tcnt = nullptr;
+static int g_tcap = 0;
+extern "C" int fbk_trace_set_gemv(const fb::TraceState* s);
+extern "C" int fbk_trace_set_attn(const fb::TraceState* s);
+extern "C" int fbk_trace_enable(int cap) {
+    fb::TraceState s{};
+    if (cap > 0) {
+        if (g_tcap < cap) {
+            if (g_tbuf) cudaFree(g_tbuf);
+            if (g_tcnt) cudaFree(g_tcnt);
+            if (cudaMalloc(&g_tbuf, sizeof(unsigned long long) * 4 * (size_t)cap) != cudaSuccess) return -1;
+            if (cudaMalloc(&g_tcnt, sizeof(int) * 9) != cudaSuccess) return -1;
+            g_tcap = cap;
+        }
+        cudaMemset(g_tcnt, 0, sizeof(int) * 9);
+        s.buf = g_tbuf;
+        s.cap = cap;
+        s.n = g_tcnt;
+        s.seq = g_tcnt + 1;
+    }
+    int rc = fbk_trace_set_gemv(&s);
+    if (!rc) rc = fbk_trace_set_attn(&s);
+    if (!rc) rc = fbk_trace_set_misc(&s);
+    return rc;
+}
+extern "C" int fbk_trace_dump(unsigned long long* out, int cap) {
+    if (!g_tbuf) return 0;
+    int n = 0;
+    if (cudaMemcpy(&n, g_tcnt, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    n = n < g_tcap ? n : g_tcap;
+    n = n < cap ? n : cap;
+    if (n > 0 && cudaMemcpy(out, g_tbuf, sizeof(unsigned long long) * 4 * (size_t)n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    return n;
 }

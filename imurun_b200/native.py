@@ -67,6 +67,7 @@ ABI5_FUNCTIONS = [
     "fish_prefill_ids", "fish_decode_ids", "fish_decode_greedy", "fish_kv_len", "fish_set_kv_len",
     "fish_session_open", "fish_session_fork", "fish_session_close", "fish_session_len", "fish_session_prefill",
     "fish_decode_batch", "fish_session_pages", "fish_kv_page_size", "fish_engine_json", "fish_profile_decode_json",
+    "fish_trace_decode",
 ]
 KERNEL_FUNCTIONS = [
     "fbx_quantize_acts", "fbx_rmsnorm", "fbx_matmul", "fbx_block_sums", "fbx_attention", "fbx_rope",
@@ -103,6 +104,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "fish_session_prefill": ([P, I, P, I, P], I), "fish_decode_batch": ([P, P, P, I, P, P], I),
         "fish_session_pages": ([P, I, P, I], I), "fish_kv_page_size": ([P], I),
         "fish_engine_json": ([P], CP), "fish_profile_decode_json": ([P, ctypes.c_int32, I], CP),
+        "fish_trace_decode": ([P, ctypes.c_int32, I, P, I], I),
         "fbx_quantize_acts": ([P, I, I, P, P], I), "fbx_rmsnorm": ([P, P, I, I, F, P], I),
         "fbx_matmul": ([I, P, I, I, P, I, P], I), "fbx_block_sums": ([I, P, I, I, P, P, P], I),
         "fbx_attention": ([P, P, P, I, I, I, I, I, I, I, P], I),

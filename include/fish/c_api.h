@@ -209,6 +209,14 @@ FISH_API const char* fish_engine_json(fish_ctx* ctx);
  * context's sequence by n_steps. NULL on error. */
 FISH_API const char* fish_profile_decode_json(fish_ctx* ctx, int32_t first, int n_steps);
 
+/* Device-time trace of n_steps graph-replayed greedy decode steps (like
+ * fish_decode_greedy, which it performs): the first CTA of each traced kernel
+ * records (globaltimer ns, kernel tag, event, launch number) into out
+ * (4 values per record, at most cap records). Tags: 1 GEMV, 2 attention,
+ * 3 embedding, 4 argmax/greedy. Events: 0 start, 1 dependency wait passed,
+ * 2 operands ready, 3 end. Returns the number of records, or < 0. */
+FISH_API int fish_trace_decode(fish_ctx* ctx, int32_t first, int n_steps, uint64_t* out, int cap);
+
 #ifdef __cplusplus
 }
 #endif
