@@ -8,6 +8,7 @@
 // paged (P positions per page, every layer of a position range in one page)
 // and fp16 or f32.
 #include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -623,6 +624,399 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_END, s_tseq);
 }
 
+
+// ================================================================ fused decode, tensor cores (fp16 KV)
+// Same structure as k_attn_decode, with both products on the tensor cores
+// (mma.sync m16n8k16, f16 inputs, f32 accumulation): per warp and 64-key
+// block, S^T[16 keys][8 heads] = K[16][D] . Q^T[D][8] and
+// O^T[D][8 heads] += V^T[D][16 keys] . P^T[16][8]. q and p are split into
+// f16 high and low parts (x = hi + lo to about 2^-22 relative) and both
+// parts are multiplied, so the products keep f32 accuracy; K and V are the
+// cache's f16 values. Every warp keeps its own online softmax state for its
+// 16 keys of each block (the score and output fragments put the same two
+// heads in each lane); the warps, then the cluster's CTAs, are merged at the
+// end. K and V rows land in shared memory by one bulk copy per row, at a
+// padded stride (D + 8 halves) so that ldmatrix reads are free of bank
+// conflicts.
+constexpr int kTcKeys = 64;
+constexpr int kTcWarps = 4;
+constexpr int kTcRs = kMaxD + 8;   // padded row stride (halves) for D = 128; D = 64 uses 72
+
+struct TcSmem {
+    static constexpr size_t ring = (size_t)kTcKeys * kTcRs;                  // halves per slot
+    static constexpr size_t off_k = 64;
+    static constexpr size_t off_v = off_k + 2 * ring * 2;
+    static constexpr size_t off_q = off_v + 2 * ring * 2;                     // [G][D] f32
+    static constexpr size_t off_p = off_q + sizeof(float) * kMaxG * kMaxD;   // [warp][2][8 heads][16 keys] f16
+    static constexpr size_t off_n = off_p + 2 * kTcWarps * 2 * 8 * 16;       // [2][D] f32 new k, v
+    static constexpr size_t bytes = off_n + sizeof(float) * 2 * kMaxD;
+    // after the last block the K ring holds the warps' partials and the V
+    // ring the CTA's partial
+    static constexpr size_t off_wm = off_k;                                   // [warp][8] f32
+    static constexpr size_t off_wl = off_wm + sizeof(float) * kTcWarps * 8;
+    static constexpr size_t off_wo = off_wl + sizeof(float) * kTcWarps * 8;  // [warp][8][D] f32
+    static constexpr size_t off_cm = off_v;                                   // [8] f32
+    static constexpr size_t off_cl = off_cm + sizeof(float) * 8;
+    static constexpr size_t off_co = off_cl + sizeof(float) * 8;              // [8][D] f32
+};
+static_assert(TcSmem::off_wo + sizeof(float) * kTcWarps * 8 * kMaxD <= TcSmem::off_v, "warp partials fit the K ring");
+static_assert(TcSmem::off_co + sizeof(float) * 8 * kMaxD <= TcSmem::off_q, "CTA partial fits the V ring");
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// x = hi + lo with hi, lo in f16
+__device__ __forceinline__ void split_h(float x, float& hi, float& lo) {
+    hi = __half2float(__float2half_rn(x));
+    lo = x - hi;
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int D>
+__global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
+    const float* __restrict__ q, int ldq, const float* __restrict__ knew, const float* __restrict__ vnew, int ldkv,
+    int H, int HKV, float scale, int rot, int neox, const float* __restrict__ rcos, const float* __restrict__ rsin,
+    KvView kv, int layer, float* __restrict__ out, int ldo) {
+    using L = TcSmem;
+    constexpr int RS = D + 8;        // padded row stride (halves)
+    constexpr int KS = D / 16;       // k-steps of q.k, m-tiles of p.V
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
+    pdl_trigger();
+    const bool tr = tracing() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    __shared__ int s_tseq;
+    if (tr && threadIdx.x == 0) {
+        s_tseq = trace_launch(TR_ATTN);
+        trace_ev(TR_ATTN, EV_START, s_tseq);
+    }
+    pdl_wait();
+    if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
+    const int t = blockIdx.z, hk = blockIdx.y, G = H / HKV;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 16);
+    __half* sk = reinterpret_cast<__half*>(smem + L::off_k);
+    __half* sv = reinterpret_cast<__half*>(smem + L::off_v);
+    float* sq = reinterpret_cast<float*>(smem + L::off_q);
+    __half* sp = reinterpret_cast<__half*>(smem + L::off_p);
+    float* snew = reinterpret_cast<float*>(smem + L::off_n);
+    const int pos = kv.tok_pos[t], n_keys = pos + 1;
+    const int n_blocks = (n_keys + kTcKeys - 1) / kTcKeys;
+    const int nb_mine = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
+    const int seq = kv.tok_seq[t];
+    const int b_own = pos / kTcKeys;
+
+    // warp 0: one bulk copy per K row and per V row of my i-th block (slot i & 1)
+    auto issue = [&](int i) {
+        const int b = r + C * i, j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0), np = (kb + 15) / 16;
+        uint64_t* br = &bar[i & 1];
+        int page = 0;
+        if (lane < np) {
+            page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + lane];
+            if (page < 0 || page >= kv.n_pages) {
+                if (kv.err) atomicExch(kv.err, 5);
+                page = 0;
+            }
+        }
+        if (lane == 0) mbar_expect_tx(br, (uint32_t)(2 * 16 * np * D * 2));
+        __syncwarp();
+        for (int k = 0; k < 2; ++k) {
+            const int rr = lane + 32 * k;
+            const int pg = __shfl_sync(0xffffffffu, page, (rr >> 4) & 3);
+            if (rr < 16 * np) {
+                const size_t off = (size_t)pg * kv.page_stride + (size_t)layer * kv.layer_stride +
+                                   (size_t)hk * kv.head_stride + (size_t)(rr & 15) * D;
+                bulk_g2s(sk + (size_t)(i & 1) * L::ring + (size_t)rr * RS, reinterpret_cast<const __half*>(kv.k) + off,
+                         (uint32_t)(D * 2), br);
+                bulk_g2s(sv + (size_t)(i & 1) * L::ring + (size_t)rr * RS, reinterpret_cast<const __half*>(kv.v) + off,
+                         (uint32_t)(D * 2), br);
+            }
+        }
+    };
+    if (tid == 0) {
+        *s_abort = 0;
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp == 0) {
+        if (nb_mine > 0) issue(0);
+        if (nb_mine > 1) issue(1);
+    }
+    // q heads of this kv head, rotated
+    const int half = rot / 2;
+    const float* cs = rcos + (size_t)pos * half;
+    const float* sn = rsin + (size_t)pos * half;
+    const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
+    for (int idx = tid; idx < G * (D / 2); idx += 32 * kTcWarps) {
+        const int g = idx / (D / 2), i = idx % (D / 2);
+        const float* hv = qr + (size_t)g * D;
+        if (i < half) {
+            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            const float x0 = hv[a], x1 = hv[b];
+            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
+        } else {
+            sq[g * kMaxD + 2 * i] = hv[2 * i];
+            sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
+        }
+    }
+    if (b_own % C == r) {
+        const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
+        const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
+        const size_t base = kv_off(kv, layer, hk, t, pos);
+        __half* kp = reinterpret_cast<__half*>(kv.k) + base;
+        __half* vp = reinterpret_cast<__half*>(kv.v) + base;
+        for (int i = tid; i < D / 2; i += 32 * kTcWarps) {
+            int a, b;
+            float k0, k1;
+            if (i < half) {
+                a = neox ? i : 2 * i;
+                b = neox ? i + half : 2 * i + 1;
+                const float x0 = kr[a], x1 = kr[b];
+                k0 = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+                k1 = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
+            } else {
+                a = 2 * i;
+                b = 2 * i + 1;
+                k0 = kr[a];
+                k1 = kr[b];
+            }
+            kp[a] = __float2half_rn(k0);
+            kp[b] = __float2half_rn(k1);
+            vp[2 * i] = __float2half_rn(vr[2 * i]);
+            vp[2 * i + 1] = __float2half_rn(vr[2 * i + 1]);
+            snew[a] = __half2float(__float2half_rn(k0));
+            snew[b] = __half2float(__float2half_rn(k1));
+            snew[kMaxD + 2 * i] = __half2float(__float2half_rn(vr[2 * i]));
+            snew[kMaxD + 2 * i + 1] = __half2float(__float2half_rn(vr[2 * i + 1]));
+        }
+    }
+    __syncthreads();
+    if (tr && tid == 0) trace_ev(TR_ATTN, 4, s_tseq);
+
+    // q as the B operand (k = dims, n = heads): lane holds head lane/4, dims
+    // 2(lane%4) + {0, 1, 8, 9} of each 16-dim step, as hi and lo halves
+    const int gq = lane >> 2, k0 = 2 * (lane & 3);
+    uint32_t qh[KS][2], ql[KS][2];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int d = 16 * ks + k0 + 8 * e;
+            const float x0 = gq < G ? sq[gq * kMaxD + d] : 0.0f, x1 = gq < G ? sq[gq * kMaxD + d + 1] : 0.0f;
+            float h0, l0, h1, l1;
+            split_h(x0, h0, l0);
+            split_h(x1, h1, l1);
+            qh[ks][e] = pack_h2(h0, h1);
+            ql[ks][e] = pack_h2(l0, l1);
+        }
+    }
+    // this lane's two heads in the score and output fragments
+    const int h0 = 2 * (lane & 3);
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+    float acc[KS][4];
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+    __half* pw = sp + (size_t)warp * 2 * 8 * 16;   // [hi/lo][8 heads][16 keys]
+    const int r_in = (lane & 7) + ((lane >> 3) & 1) * 8, c_in = (lane >> 4) * 8;       // ldmatrix (K rows)
+    const int key_in = (lane & 7) + ((lane >> 4) & 1) * 8, dim_in = ((lane >> 3) & 1) * 8;  // ldmatrix.trans (V)
+    int failed_at = -1;
+    for (int i = 0; i < nb_mine; ++i) {
+        const bool ok = mbar_wait(&bar[i & 1], (uint32_t)((i >> 1) & 1), s_abort);
+        if (__syncthreads_or(!ok)) {
+            failed_at = i;
+            break;
+        }
+        const int b = r + C * i, j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0);
+        __half* K = sk + (size_t)(i & 1) * L::ring;
+        __half* V = sv + (size_t)(i & 1) * L::ring;
+        if (b == b_own) {
+            const int rr = pos - j0;
+            for (int d = tid; d < D; d += 32 * kTcWarps) {
+                K[(size_t)rr * RS + d] = __float2half_rn(snew[d]);
+                V[(size_t)rr * RS + d] = __float2half_rn(snew[kMaxD + d]);
+            }
+            __syncthreads();
+        }
+        const int kw = 16 * warp;   // this warp's first key in the block
+        if (kw < kb) {
+            // scores S^T[16 keys][8 heads]
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t a[4];
+                ldsm_x4(a, K + (size_t)(kw + r_in) * RS + 16 * ks + c_in);
+                mma16816(c, a, qh[ks][0], qh[ks][1]);
+                mma16816(c, a, ql[ks][0], ql[ks][1]);
+            }
+            // c0: (key lane/4, head h0), c1: (lane/4, h0+1), c2: (lane/4+8, h0), c3: (lane/4+8, h0+1)
+            const int ka = kw + (lane >> 2), kb2 = ka + 8;
+            float s[4];
+            s[0] = ka < kb ? __fmul_rn(c[0], scale) : -INFINITY;
+            s[1] = ka < kb ? __fmul_rn(c[1], scale) : -INFINITY;
+            s[2] = kb2 < kb ? __fmul_rn(c[2], scale) : -INFINITY;
+            s[3] = kb2 < kb ? __fmul_rn(c[3], scale) : -INFINITY;
+            float corr[2], p[4];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float mx = fmaxf(s[e], s[e + 2]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m_r[e], mx);
+                corr[e] = m_r[e] == -INFINITY ? 0.0f : expf(m_r[e] - mn);
+                p[e] = s[e] == -INFINITY ? 0.0f : expf(s[e] - mn);
+                p[e + 2] = s[e + 2] == -INFINITY ? 0.0f : expf(s[e + 2] - mn);
+                float sum = p[e] + p[e + 2];
+                sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+                l_r[e] = l_r[e] * corr[e] + sum;
+                m_r[e] = mn;
+            }
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                acc[mt][0] *= corr[0];
+                acc[mt][1] *= corr[1];
+                acc[mt][2] *= corr[0];
+                acc[mt][3] *= corr[1];
+            }
+            // P^T as the B operand of p.V (k = keys, n = heads): transpose through shared memory
+            {
+                const int kr = lane >> 2;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int hh = h0 + (e & 1), kk = kr + 8 * (e >> 1);
+                    float ph, pl;
+                    split_h(p[e], ph, pl);
+                    pw[(0 * 8 + hh) * 16 + kk] = __float2half_rn(ph);
+                    pw[(1 * 8 + hh) * 16 + kk] = __float2half_rn(pl);
+                }
+            }
+            __syncwarp();
+            const uint32_t pbh0 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0);
+            const uint32_t pbh1 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0 + 8);
+            const uint32_t pbl0 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0);
+            const uint32_t pbl1 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0 + 8);
+            __syncwarp();
+            // O^T[D][8 heads] += V^T[D][16 keys] . P^T[16 keys][8 heads]
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                uint32_t a[4];
+                ldsm_x4_t(a, V + (size_t)(kw + key_in) * RS + 16 * mt + dim_in);
+                mma16816(acc[mt], a, pbh0, pbh1);
+                mma16816(acc[mt], a, pbl0, pbl1);
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && i + 2 < nb_mine) issue(i + 2);
+    }
+    if (tr && tid == 0) trace_ev(TR_ATTN, 6, s_tseq);
+    float* wm = reinterpret_cast<float*>(smem + L::off_wm);
+    float* wl = reinterpret_cast<float*>(smem + L::off_wl);
+    float* wo = reinterpret_cast<float*>(smem + L::off_wo);
+    float* cm = reinterpret_cast<float*>(smem + L::off_cm);
+    float* cl = reinterpret_cast<float*>(smem + L::off_cl);
+    float* co = reinterpret_cast<float*>(smem + L::off_co);
+    if (failed_at >= 0) {
+        if (tid == 0) {
+            if (kv.err) atomicExch(kv.err, 6);
+            for (int i = failed_at; i < nb_mine && i < failed_at + 2; ++i)
+                mbar_wait_bounded(&bar[i & 1], (uint32_t)((i >> 1) & 1));
+        }
+        __syncthreads();
+        if (tid < 8) { cm[tid] = -INFINITY; cl[tid] = 0.0f; }
+    } else {
+        // the warps' partials (max, sum, unnormalised O) -> the CTA's
+        if (lane < 4) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                wm[warp * 8 + h0 + e] = m_r[e];
+                wl[warp * 8 + h0 + e] = l_r[e];
+            }
+        }
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            const int d = 16 * mt + (lane >> 2);
+            wo[((size_t)warp * 8 + h0) * kMaxD + d] = acc[mt][0];
+            wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d] = acc[mt][1];
+            wo[((size_t)warp * 8 + h0) * kMaxD + d + 8] = acc[mt][2];
+            wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d + 8] = acc[mt][3];
+        }
+        __syncthreads();
+        for (int idx = tid; idx < G * D; idx += 32 * kTcWarps) {
+            const int g = idx / D, d = idx % D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, wm[w * 8 + g]);
+            float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kTcWarps; ++w) {
+                const float mw = wm[w * 8 + g];
+                if (mw == -INFINITY) continue;
+                const float cw = expf(mw - M);
+                Ls += wl[w * 8 + g] * cw;
+                O += wo[((size_t)w * 8 + g) * kMaxD + d] * cw;
+            }
+            co[g * kMaxD + d] = O;
+            if (d == 0) { cm[g] = M; cl[g] = Ls; }
+        }
+    }
+    cluster.sync();
+    if (tr && tid == 0) trace_ev(TR_ATTN, 7, s_tseq);
+    // merge the C partials through distributed shared memory
+    for (int idx = r * 32 * kTcWarps + tid; idx < G * D; idx += C * 32 * kTcWarps) {
+        const int g = idx / D, d = idx % D;
+        float mv[16], lv[16], ov[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C) {
+                mv[rr] = *cluster.map_shared_rank(cm + g, rr);
+                lv[rr] = *cluster.map_shared_rank(cl + g, rr);
+                ov[rr] = *cluster.map_shared_rank(co + g * kMaxD + d, rr);
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr)
+            if (rr < C) M = fmaxf(M, mv[rr]);
+        float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C && mv[rr] != -INFINITY) {
+                const float w = expf(mv[rr] - M);
+                Ls += lv[rr] * w;
+                O += ov[rr] * w;
+            }
+        }
+        out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+    }
+    cluster.sync();
+    if (tr && tid == 0) trace_ev(TR_ATTN, EV_END, s_tseq);
+}
+
 }  // namespace fb
 
 using namespace fb;
@@ -725,12 +1119,68 @@ static int launch_decode(const float* q, int ldq, const float* k, const float* v
                                    layer, out, ldo);
 }
 
+// Tensor-core decode attention for fp16 caches; cluster size as for the f32 kernel.
+template <int D>
+static int launch_decode_tc(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV,
+                            float scale, int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer,
+                            float* out, int ldo, cudaStream_t st) {
+    static int cluster = 0;
+    if (!cluster) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)TcSmem::bytes);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_decode_tc<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return (int)e;
+        cluster = 16;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(16, 1, 1);
+        cfg.blockDim = dim3(32 * kTcWarps);
+        cfg.dynamicSmemBytes = TcSmem::bytes;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 16;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_attn_decode_tc<D>, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            cluster = 8;
+        }
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(cluster, HKV, T);
+    cfg.blockDim = dim3(32 * kTcWarps);
+    cfg.dynamicSmemBytes = TcSmem::bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    int na = 1;
+    if (fbk_pdl_enabled()) {
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        na = 2;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return (int)cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox, rcos, rsin, kv,
+                                   layer, out, ldo);
+}
+
 extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H,
                                     int HKV, int D, float scale, int rot, int neox, const float* rcos, const float* rsin,
                                     KvView kv, int layer, float* out, int ldo, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
     if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
+    static const bool tc_off = getenv("FISH_ATTN_SIMT") != nullptr;
+    if (kv.f16 && !tc_off) {
+        if (D == 128) return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
+        return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
+    }
     if (kv.f16) return launch_decode<__half>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
     return launch_decode<float>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
 }
