@@ -707,8 +707,9 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
         s_tseq = trace_launch(TR_ATTN);
         trace_ev(TR_ATTN, EV_START, s_tseq);
     }
-    pdl_wait();
-    if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
+    // Before the dependency wait: everything written before this graph step
+    // began (token positions, page tables, the KV cache of earlier positions,
+    // the RoPE table). After it: q and the new k/v rows of the QKV projection.
     const int t = blockIdx.z, hk = blockIdx.y, G = H / HKV;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
@@ -758,16 +759,27 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
         mbar_fence_init();
     }
     __syncthreads();
-    if (warp == 0) {
+    // the last warp issues the copies; the others rotate q and store the new row
+    constexpr int kIssuer = kTcWarps - 1;
+    if (warp == kIssuer) {
         if (nb_mine > 0) issue(0);
         if (nb_mine > 1) issue(1);
     }
-    // q heads of this kv head, rotated
+    // this position's rotation table, staged in shared memory
     const int half = rot / 2;
-    const float* cs = rcos + (size_t)pos * half;
-    const float* sn = rsin + (size_t)pos * half;
+    __shared__ float s_rot[2][kMaxD / 2];
+    if (tid < half) {
+        s_rot[0][tid] = rcos[(size_t)pos * half + tid];
+        s_rot[1][tid] = rsin[(size_t)pos * half + tid];
+    }
+    __syncthreads();
+    const float* cs = s_rot[0];
+    const float* sn = s_rot[1];
+    pdl_wait();
+    if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
     const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
-    for (int idx = tid; idx < G * (D / 2); idx += 32 * kTcWarps) {
+    const int wt = 32 * kIssuer;   // threads doing the rotation
+    for (int idx = tid; warp < kIssuer && idx < G * (D / 2); idx += wt) {
         const int g = idx / (D / 2), i = idx % (D / 2);
         const float* hv = qr + (size_t)g * D;
         if (i < half) {
@@ -780,13 +792,13 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
             sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
         }
     }
-    if (b_own % C == r) {
+    if (b_own % C == r && warp < kIssuer) {
         const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
         const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
         const size_t base = kv_off(kv, layer, hk, t, pos);
         __half* kp = reinterpret_cast<__half*>(kv.k) + base;
         __half* vp = reinterpret_cast<__half*>(kv.v) + base;
-        for (int i = tid; i < D / 2; i += 32 * kTcWarps) {
+        for (int i = tid; i < D / 2; i += wt) {
             int a, b;
             float k0, k1;
             if (i < half) {
@@ -931,7 +943,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
             }
         }
         __syncthreads();
-        if (warp == 0 && i + 2 < nb_mine) issue(i + 2);
+        if (warp == kIssuer && i + 2 < nb_mine) issue(i + 2);
     }
     if (tr && tid == 0) trace_ev(TR_ATTN, 6, s_tseq);
     float* wm = reinterpret_cast<float*>(smem + L::off_wm);

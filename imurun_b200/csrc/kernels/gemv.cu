@@ -326,6 +326,7 @@ struct StreamJobs {
     int* err;                // device error flag
     int wait_first;          // producer waits for the previous kernel (expert indices)
     int pair;                // tiles alternate between segments 0 and 1 (SwiGLU epilogue)
+    int stage_bytes;         // PRO_NORM, T = 1: shared copies of x and of the norm weights (0 = none)
 };
 
 // Segment of a tile (segments are copied to shared memory at kernel start,
@@ -437,7 +438,7 @@ __device__ __forceinline__ void ld8(const float* p, int i0, int K, float (&v)[8]
 
 // Consumer prologue: build the activation image for T tokens.
 __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32, float* s_scale,
-                             double* s_part) {
+                             double* s_part, float* xs, const float* ws) {
     const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31;
     const int K = args.K, T = args.T, n256 = xi.n256;
     const GemvPro& pro = args.pro;
@@ -485,6 +486,11 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
                         if (i0 + 512 * k < K) f[k] = *reinterpret_cast<const float4*>(xr + i0 + 512 * k);
+                    if (xs) {
+#pragma unroll
+                        for (int k = 0; k < 8; ++k)
+                            if (i0 + 512 * k < K) *reinterpret_cast<float4*>(xs + i0 + 512 * k) = f[k];
+                    }
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
                         if (i0 + 512 * k < K)
@@ -507,8 +513,29 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
     // chunks loads everything it needs before computing
     const int n_chunks = (K + 255) / 256;
     constexpr int kB = 2;
+    if (pro.mode == PRO_QUANT) {   // one source: four chunks per batch
+        constexpr int kQ = 4;
+        for (int t = 0; t < T; ++t) {
+            const float* xr = pro.src + (size_t)t * pro.ld;
+            for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kQ) {
+                float va[kQ][8];
+#pragma unroll
+                for (int k = 0; k < kQ; ++k) {
+                    const int c = c0 + kConsumers * k;
+                    if (c < n_chunks) ld8(xr, c * 256 + 8 * lane, K, va[k]);
+                }
+#pragma unroll
+                for (int k = 0; k < kQ; ++k) {
+                    const int c = c0 + kConsumers * k;
+                    if (c < n_chunks) ximg_quant_chunk(va[k], lane, K, t, c, xi, wantk, want32);
+                }
+            }
+        }
+        return;
+    }
     for (int t = 0; t < T; ++t) {
-        const float* xr = pro.src + (size_t)t * pro.ld;
+        const float* xr = xs ? xs : pro.src + (size_t)t * pro.ld;
+        const float* wr = ws ? ws : pro.w;
         const float* ur = pro.mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
         for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kB) {
             float va[kB][8], ua[kB][8];
@@ -518,7 +545,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
                 if (c < n_chunks) {
                     const int i0 = c * 256 + 8 * lane;
                     ld8(xr, i0, K, va[k]);
-                    if (pro.mode == PRO_NORM) ld8(pro.w, i0, K, ua[k]);
+                    if (pro.mode == PRO_NORM) ld8(wr, i0, K, ua[k]);
                     else if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
                 }
             }
@@ -579,8 +606,9 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     xi.x32 = jobs.x32_bytes;
     xi.T = T;
     float* part = reinterpret_cast<float*>(xi.base + (size_t)T * (jobs.xk_bytes + jobs.x32_bytes));
-    uint8_t* ring = reinterpret_cast<uint8_t*>(part) +
-                    (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128);
+    float* xstage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(part) +
+                                             (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128));
+    uint8_t* ring = reinterpret_cast<uint8_t*>(xstage) + jobs.stage_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < kMaxSeg; ++i)
@@ -652,11 +680,20 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
         return;
     }
 
-    // consumers
+    // consumers: the norm weights are constant, so their shared copy is made
+    // before waiting for the previous kernel
+    float* xs = nullptr;
+    float* ws = nullptr;
+    if (jobs.stage_bytes) {
+        xs = xstage;
+        ws = xstage + K;
+        for (int i = threadIdx.x; i < K / 4; i += kConsumers * 32)
+            reinterpret_cast<float4*>(ws)[i] = __ldg(reinterpret_cast<const float4*>(args.pro.w) + i);
+    }
     pdl_wait();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_WAITED, s_tseq);
     const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
-    build_ximage(args, xi, wantk, want32, s_scale, s_part);
+    build_ximage(args, xi, wantk, want32, s_scale, s_part, xs, ws);
     consumers_sync();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
     const int half = warp & 1, quarter = warp >> 1;
@@ -908,7 +945,8 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     jobs.n_groups = row_groups(a->seg[0].type, a->K);
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
-    const size_t xbytes = (size_t)a->T * (jobs.xk_bytes + jobs.x32_bytes);
+    jobs.stage_bytes = (a->pro.mode == PRO_NORM && a->T == 1 && a->K % 512 == 0 && a->K <= 5120) ? 2 * a->K * 4 : 0;
+    const size_t xbytes = (size_t)a->T * (jobs.xk_bytes + jobs.x32_bytes) + jobs.stage_bytes;
     int ctas = 0, stages = 0;
     size_t smem = 0;
     for (int cps = NT == 1 ? want_cps : 1;; --cps) {
