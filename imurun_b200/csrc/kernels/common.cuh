@@ -33,6 +33,28 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// RMSNorm sum of squares (src/ops.cpp:18-23 sums x*x in double). Every kernel
+// that normalises a row sums in this one order, so fused and unfused paths
+// give the same scale bit for bit: 8 warps, warp w takes the 256-value chunks
+// w, w+8, ... in ascending order, lane l values 8l .. 8l+7 of a chunk
+// (sumsq8, left to right); each lane adds its chunk sums in order, the warp
+// reduces with warp_sum_d, and the 8 warp sums are added in warp order
+// (norm_total). Products of two floats are exact in double, so no
+// contraction choice can change a partial.
+constexpr int kNormWarps = 8;
+__device__ __forceinline__ double sumsq8(const float (&v)[8]) {
+    double s = __dmul_rn((double)v[0], (double)v[0]);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) s = __dadd_rn(s, __dmul_rn((double)v[i], (double)v[i]));
+    return s;
+}
+__device__ __forceinline__ float norm_total(const double* part, int K, float eps) {
+    double tot = 0.0;
+#pragma unroll
+    for (int i = 0; i < kNormWarps; ++i) tot = __dadd_rn(tot, part[i]);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)__ddiv_rn(tot, (double)K), eps)));
+}
+
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }

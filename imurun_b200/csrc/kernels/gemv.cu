@@ -14,9 +14,10 @@
 //                  consumer warps first build the activation image in shared
 //                  memory (copied from quantised planes, or computed from f32
 //                  rows: RMSNorm, SwiGLU or plain, then quantised), then each
-//                  takes half a stage (4 rows x 8 blocks, one block per
-//                  lane). Per-stage row partials go to shared memory and are
-//                  summed over groups at the end in a fixed order.
+//                  pair of them takes every fourth stage (4 rows x 8 blocks
+//                  a warp, one block per lane). Per-stage row partials go to
+//                  shared memory and are summed over groups at the end in a
+//                  fixed order.
 //   k_gemv_direct  T = 5..8 (prefill chunks) and F32/F16 rows, plain loads.
 // Launches carry the programmatic-dependent-launch attribute when the caller
 // asks for it: the producer streams weights before the previous kernel has
@@ -114,55 +115,72 @@ __device__ __forceinline__ bool in_range(const uint8_t* p, size_t n, const uint8
     return false;
 }
 
+// Float steps of one block, shared by both kernels (explicit roundings, so no
+// multiply-add contraction can make the two kernels differ):
+//   Q4_K  (dw dx) si - (dmin dx) mins      Q6_K, Q8_0  (dw dx) s
+__device__ __forceinline__ float q4k_term(float dw, float dmw, float dx, int si, int mi) {
+    return __fsub_rn(__fmul_rn(__fmul_rn(dw, dx), (float)si), __fmul_rn(__fmul_rn(dmw, dx), (float)mi));
+}
+__device__ __forceinline__ float scaled_term(float dw, float dx, int s) { return __fmul_rn(__fmul_rn(dw, dx), (float)s); }
+
+// One row, 8 lanes (bl = lane & 7). Summation order shared with
+// k_gemv_stream, so a row's result does not depend on which kernel (which
+// batch size) computed it: per 2048-value group, lane bl's term (the block
+// gi*8 + bl for K-quants; for Q8_0 the sum, in block order, of blocks
+// gi*64 + 8 bl .. + 7), then the tree over bl (xor 1, 2, 4), then the group
+// sums added in group order. Every lane of the 8 runs every group (valid =
+// row exists), so the shuffles never diverge.
 template <int NT>
 __device__ __forceinline__ void direct_rows_q(const GemvSeg& g, const uint8_t* base, int K, const ActQ& a, int T,
-                                              int row, int bl, float (&acc)[NT], int* err) {
+                                              int row, bool valid, int bl, float (&acc)[NT], int* err) {
     const int nb = row_blocks(g.type, K);
+    const int G = row_groups(g.type, K);
     const uint8_t* wend = g.w + g.w_bytes;
-    if (g.type == T_Q4_K) {
-        for (int kb = bl; kb < nb; kb += 8) {
-            uint4 w[9];
+    for (int gi = 0; gi < G; ++gi) {
+        float c[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) c[t] = 0.0f;
+        if (g.type == T_Q4_K) {
+            const int kb = gi * 8 + bl;
             const uint8_t* p = base + block_offset_tm(T_Q4_K, K, row, kb);
-            if (!in_range(p, 144, g.w, wend, err)) continue;
+            if (valid && kb < nb && in_range(p, 144, g.w, wend, err)) {
+                uint4 w[9];
 #pragma unroll
-            for (int i = 0; i < 9; ++i) w[i] = ldg_stream(p + 16 * i);
-            const float dw = h2f((uint16_t)(w[0].x & 0xFFFFu)), dmw = h2f((uint16_t)(w[0].x >> 16));
+                for (int i = 0; i < 9; ++i) w[i] = ldg_stream(p + 16 * i);
+                const float dw = h2f((uint16_t)(w[0].x & 0xFFFFu)), dmw = h2f((uint16_t)(w[0].x >> 16));
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t >= T) break;
-                int si, mi;
-                const uint4 bs = __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)t * (K / 32) + (size_t)kb * 8));
-                q4k_block<LdGlobal>(w, a.qk + (size_t)t * a.ld + (size_t)kb * 256, bs, si, mi);
-                const float dx = __ldg(a.dk + (size_t)t * (K / 256) + kb);
-                acc[t] += __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    int si, mi;
+                    const uint4 bs = __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)t * (K / 32) + (size_t)kb * 8));
+                    q4k_block<LdGlobal>(w, a.qk + (size_t)t * a.ld + (size_t)kb * 256, bs, si, mi);
+                    c[t] = q4k_term(dw, dmw, __ldg(a.dk + (size_t)t * (K / 256) + kb), si, mi);
+                }
             }
-        }
-    } else if (g.type == T_Q6_K) {
-        for (int kb = bl; kb < nb; kb += 8) {
-            uint4 w[13];
+        } else if (g.type == T_Q6_K) {
+            const int kb = gi * 8 + bl;
             const uint8_t* p = base + block_offset_tm(T_Q6_K, K, row, kb);
             const uint8_t* pd = base + dscale_offset_tm(T_Q6_K, K, row, kb);
-            if (!in_range(p, 208, g.w, wend, err) || !in_range(pd, 2, g.w, wend, err)) continue;
+            if (valid && kb < nb && in_range(p, 208, g.w, wend, err) && in_range(pd, 2, g.w, wend, err)) {
+                uint4 w[13];
 #pragma unroll
-            for (int i = 0; i < 13; ++i) w[i] = ldg_stream(p + 16 * i);
-            const float dw = h2f(*reinterpret_cast<const uint16_t*>(pd));
+                for (int i = 0; i < 13; ++i) w[i] = ldg_stream(p + 16 * i);
+                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pd));
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t >= T) break;
-                const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)kb * 256;
-                int16_t xs[16];
+                for (int t = 0; t < NT; ++t) {
+                    if (t >= T) break;
+                    const int8_t* xq = a.qk + (size_t)t * a.ld + (size_t)kb * 256;
+                    int16_t xs[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) xs[j] = (int16_t)sum16(__ldg(reinterpret_cast<const uint4*>(xq + 16 * j)));
-                const int si = q6k_block<LdGlobal>(w, xq, xs);
-                acc[t] += __fmul_rn(dw, __ldg(a.dk + (size_t)t * (K / 256) + kb)) * (float)si;
+                    for (int j = 0; j < 16; ++j) xs[j] = (int16_t)sum16(__ldg(reinterpret_cast<const uint4*>(xq + 16 * j)));
+                    const int si = q6k_block<LdGlobal>(w, xq, xs);
+                    c[t] = scaled_term(dw, __ldg(a.dk + (size_t)t * (K / 256) + kb), si);
+                }
             }
-        }
-    } else {   // Q8_0: lane takes chunks of 8 blocks
-        const int nch = (nb + 7) / 8;
-        for (int kc = bl; kc < nch; kc += 8) {
+        } else {   // Q8_0: blocks gi*64 + 8 bl + i, i = 0..7, summed in block order
             for (int i = 0; i < 8; ++i) {
-                const int b = 8 * kc + i;
-                if (b >= nb) break;
+                const int b = gi * 64 + 8 * bl + i;
+                if (!valid || b >= nb) break;
                 const uint8_t* p = base + block_offset_tm(T_Q8_0, K, row, b);
                 const uint8_t* pd = base + dscale_offset_tm(T_Q8_0, K, row, b);
                 if (!in_range(p, 32, g.w, wend, err) || !in_range(pd, 2, g.w, wend, err)) continue;
@@ -172,9 +190,16 @@ __device__ __forceinline__ void direct_rows_q(const GemvSeg& g, const uint8_t* b
                 for (int t = 0; t < NT; ++t) {
                     if (t >= T) break;
                     const int s = q80_block<LdGlobal>(w0, w1, a.q32 + (size_t)t * a.ld + (size_t)b * 32);
-                    acc[t] += __fmul_rn(dw, __ldg(a.d32 + (size_t)t * (K / 32) + b)) * (float)s;
+                    c[t] = __fadd_rn(c[t], scaled_term(dw, __ldg(a.d32 + (size_t)t * (K / 32) + b), s));
                 }
             }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 1);
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 2);
+            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 4);
+            acc[t] += c[t];
         }
     }
 }
@@ -218,15 +243,10 @@ __global__ void __launch_bounds__(256) k_gemv_direct(GemvArgs args) {
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
         if (is_tiled(g.type)) {
             const int row = (it - items[s]) * 4 + (lane >> 3), bl = lane & 7;
-            if (row < g.rows) direct_rows_q<NT>(g, base, args.K, args.act, args.T, row, bl, acc, args.err);
+            direct_rows_q<NT>(g, base, args.K, args.act, args.T, row, row < g.rows, bl, acc, args.err);
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                float v = acc[t];
-                v += __shfl_xor_sync(0xffffffffu, v, 1);
-                v += __shfl_xor_sync(0xffffffffu, v, 2);
-                v += __shfl_xor_sync(0xffffffffu, v, 4);
-                if (bl == 0 && row < g.rows && t < args.T) store_out(g, row, t, v);
-            }
+            for (int t = 0; t < NT; ++t)
+                if (bl == 0 && row < g.rows && t < args.T) store_out(g, row, t, acc[t]);
         } else {
             const int row = it - items[s];
             if (in_range(base + (size_t)row * g.row_stride, g.row_stride, g.w, g.w + g.w_bytes, lane == 0 ? args.err : nullptr))
@@ -276,7 +296,7 @@ __global__ void k_block_sums(int type, const uint8_t* __restrict__ w, int rows, 
 
 // ============================================================ streamed kernel
 
-constexpr int kConsumers = 8;                       // consumer warps (2 per stage)
+constexpr int kConsumers = 8;                       // consumer warps: 4 pairs, a pair per stage
 constexpr int kMaxStages = 32;
 constexpr int kHdrBytes = 2 * kMaxStages * 8 + 64;  // mbarriers, abort flag, norm scales
 constexpr int kXChunk = 272;                        // bytes per 256 activation int8 (16 B pad: no bank conflicts)
@@ -309,24 +329,27 @@ __device__ __noinline__ void record_wait_fail(int kind, int s, int slot, int par
     __threadfence();
 }
 
-// Ring slots: consumer pair q (= stage & 3) owns slots [q*Sq, q*Sq + Sq), and
-// its j-th stage (j = stage >> 2) uses slot q*Sq + j % Sq in phase j / Sq. A
-// pair therefore waits on each of its slots phase after phase and never for a
-// phase two ahead of the barrier, which a parity wait could not tell apart.
-__device__ __forceinline__ int ring_slot(int s, int Sq) { return (s & 3) * Sq + (s >> 2) % Sq; }
-__device__ __forceinline__ int ring_phase(int s, int Sq) { return (s >> 2) / Sq; }
+// Ring slots: a FIFO, stage s in slot s % S, phase s / S, with S a multiple
+// of the 4 consumer pairs. Pair q takes stages q, q + 4, ..., so every slot it
+// touches is only ever its own (slot = s % S keeps s's residue mod 4), and it
+// waits on each of them phase after phase: never for a phase two ahead of the
+// barrier, which a parity wait could not tell apart.
+constexpr int kPairs = kConsumers / 2;
+__device__ __forceinline__ int ring_slot(int s, int S) { return s % S; }
+__device__ __forceinline__ int ring_phase(int s, int S) { return s / S; }
 
 struct StreamJobs {
     int tile0[kMaxSeg + 1];  // 8-row tiles: segment s owns tiles [tile0[s], tile0[s+1])
     int n_groups;            // 2048-value groups per row
-    int stages;              // ring slots (4 x slots per consumer pair)
+    int stages;              // ring slots
     int slot_bytes;          // bytes per slot (8 x the largest piece)
-    int tiles_per_cta;
+    int tiles_per_cta;       // most tiles any CTA gets (sizes the partials)
+    int n_units;             // work units (a tile, or a (gate, up) tile pair): CTA b takes
+                             // units [b n_units / grid, (b+1) n_units / grid)
     int xk_bytes, x32_bytes; // per-token bytes of the two activation images (0 = not built)
     int* err;                // device error flag
     int wait_first;          // producer waits for the previous kernel (expert indices)
     int pair;                // tiles alternate between segments 0 and 1 (SwiGLU epilogue)
-    int stage_bytes;         // PRO_NORM, T = 1: shared copies of x and of the norm weights (0 = none)
 };
 
 // Segment of a tile (segments are copied to shared memory at kernel start,
@@ -436,9 +459,14 @@ __device__ __forceinline__ void ld8(const float* p, int i0, int K, float (&v)[8]
     }
 }
 
+// Norm weights a consumer lane keeps in registers: chunks warp + 8k, k < 2
+// (all of them up to K = 4096), loaded before the wait for the previous kernel.
+constexpr int kNormRegs = 2;
+static_assert(kConsumers == kNormWarps, "the fused norm sums in the shared order of k_rmsnorm_quant");
+
 // Consumer prologue: build the activation image for T tokens.
-__device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32, float* s_scale,
-                             double* s_part, float* xs, const float* ws) {
+__device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32,
+                                             double* s_part, const float (&wv)[kNormRegs][8], int tseq) {
     const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31;
     const int K = args.K, T = args.T, n256 = xi.n256;
     const GemvPro& pro = args.pro;
@@ -471,47 +499,59 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
         }
         return;
     }
+    const int n_chunks = (K + 255) / 256;
     if (pro.mode == PRO_NORM) {
-        // the reference's double sum (src/ops.cpp:18-23) in the exact order of
-        // k_rmsnorm_quant: 128 threads, float4 strides, warp trees, 4 partials;
-        // a thread's loads are all issued before the first is used
-        const int grp = ct >> 7, gt = ct & 127;
-        for (int t0 = 0; t0 < T; t0 += 2) {
-            const int t = t0 + grp;
-            if (t < T) {
-                const float* xr = pro.src + (size_t)t * pro.ld;
-                double s = 0.0;
-                for (int i0 = gt * 4; i0 < K; i0 += 8 * 512) {
-                    float4 f[8];
+        // the reference's double sum (src/ops.cpp:18-23) in the order every
+        // norm kernel shares (common.cuh); chunks that fit stay in registers
+        // between the sum and the quantisation
+        for (int t = 0; t < T; ++t) {
+            const float* xr = pro.src + (size_t)t * pro.ld;
+            float va[kNormRegs][8];
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (i0 + 512 * k < K) f[k] = *reinterpret_cast<const float4*>(xr + i0 + 512 * k);
-                    if (xs) {
+            for (int k = 0; k < kNormRegs; ++k) {
+                const int c = warp + kConsumers * k;
+                if (c < n_chunks) ld8(xr, c * 256 + 8 * lane, K, va[k]);
+            }
+            double s = 0.0;
 #pragma unroll
-                        for (int k = 0; k < 8; ++k)
-                            if (i0 + 512 * k < K) *reinterpret_cast<float4*>(xs + i0 + 512 * k) = f[k];
-                    }
+            for (int k = 0; k < kNormRegs; ++k)
+                if (warp + kConsumers * k < n_chunks) s = __dadd_rn(s, sumsq8(va[k]));
+            for (int c = warp + kConsumers * kNormRegs; c < n_chunks; c += kConsumers) {
+                float v[8];
+                ld8(xr, c * 256 + 8 * lane, K, v);
+                s = __dadd_rn(s, sumsq8(v));
+            }
+            s = warp_sum_d(s);
+            if (lane == 0) s_part[warp] = s;
+            consumers_sync();
+            const float sc = norm_total(s_part, K, pro.eps);
+            if (t == 0 && tseq >= 0 && ct == 0) trace_ev(TR_GEMV, EV_SCALE, tseq);
+            consumers_sync();   // s_part is reused by the next token
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (i0 + 512 * k < K)
-                            s += (double)f[k].x * f[k].x + (double)f[k].y * f[k].y + (double)f[k].z * f[k].z +
-                                 (double)f[k].w * f[k].w;
+            for (int k = 0; k < kNormRegs; ++k) {
+                const int c = warp + kConsumers * k;
+                if (c < n_chunks) {
+                    const int i0 = c * 256 + 8 * lane;
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(va[k][i], sc), wv[k][i]) : 0.0f;
+                    ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
                 }
-                s = warp_sum_d(s);
-                if (lane == 0) s_part[grp * 4 + (gt >> 5)] = s;
             }
-            consumers_sync();
-            if (t < T && gt == 0) {
-                double tot = 0.0;
-                for (int i = 0; i < 4; ++i) tot += s_part[grp * 4 + i];
-                s_scale[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / K), pro.eps)));
+            for (int c = warp + kConsumers * kNormRegs; c < n_chunks; c += kConsumers) {
+                const int i0 = c * 256 + 8 * lane;
+                float xv[8], w8[8], v[8];
+                ld8(xr, i0, K, xv);
+                ld8(pro.w, i0, K, w8);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(xv[i], sc), w8[i]) : 0.0f;
+                ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
             }
-            consumers_sync();
         }
+        return;
     }
     // quantisation: warp w takes chunks w, w + 8, ...; each batch of up to 4
     // chunks loads everything it needs before computing
-    const int n_chunks = (K + 255) / 256;
     constexpr int kB = 2;
     if (pro.mode == PRO_QUANT) {   // one source: four chunks per batch
         constexpr int kQ = 4;
@@ -534,8 +574,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
         return;
     }
     for (int t = 0; t < T; ++t) {
-        const float* xr = xs ? xs : pro.src + (size_t)t * pro.ld;
-        const float* wr = ws ? ws : pro.w;
+        const float* xr = pro.src + (size_t)t * pro.ld;
         const float* ur = pro.mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
         for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kB) {
             float va[kB][8], ua[kB][8];
@@ -545,8 +584,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
                 if (c < n_chunks) {
                     const int i0 = c * 256 + 8 * lane;
                     ld8(xr, i0, K, va[k]);
-                    if (pro.mode == PRO_NORM) ld8(wr, i0, K, ua[k]);
-                    else if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
+                    if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
                 }
             }
 #pragma unroll
@@ -555,11 +593,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
                 if (c < n_chunks) {
                     const int i0 = c * 256 + 8 * lane;
                     float v[8];
-                    if (pro.mode == PRO_NORM) {
-                        const float sc = s_scale[t];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(va[k][i], sc), ua[k][i]) : 0.0f;
-                    } else if (pro.mode == PRO_SILU) {
+                    if (pro.mode == PRO_SILU) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
                             v[i] = __fmul_rn(__fdiv_rn(va[k][i], __fadd_rn(1.0f, expf(-va[k][i]))), ua[k][i]);
@@ -582,23 +616,24 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8);
-    float* s_scale = reinterpret_cast<float*>(smem + 2 * kMaxStages * 8 + 16);   // [4]
     volatile int* s_issued = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8 + 4);
     volatile int* s_prod_wait = reinterpret_cast<volatile int*>(smem + 2 * kMaxStages * 8 + 8);
     unsigned dyn_smem;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
-    __shared__ double s_part[8];
+    __shared__ double s_part[kNormWarps];
     __shared__ int s_tseq;
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
-    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages, Sq = S / 4;
+    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages;
     int n_tiles = jobs.tile0[0];
 #pragma unroll
     for (int i = 1; i <= kMaxSeg; ++i)
         if (i == args.nseg) n_tiles = jobs.tile0[i];
-    const int t_begin = blockIdx.x * jobs.tiles_per_cta;
-    const int t_end = min(n_tiles, t_begin + jobs.tiles_per_cta);
-    const int n_stages = (t_end - t_begin) * G;
+    // balanced split: units of one tile, or of a (gate, up) tile pair
+    const int unit = jobs.pair ? 2 : 1;
+    const int t_begin = (int)((long long)blockIdx.x * jobs.n_units / gridDim.x) * unit;
+    const int t_end = min(n_tiles, (int)((long long)(blockIdx.x + 1) * jobs.n_units / gridDim.x) * unit);
+    const int n_stages = max(0, t_end - t_begin) * G;
     XImage xi;
     xi.base = smem + kHdrBytes;
     xi.n256 = (K + 255) / 256;
@@ -606,9 +641,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     xi.x32 = jobs.x32_bytes;
     xi.T = T;
     float* part = reinterpret_cast<float*>(xi.base + (size_t)T * (jobs.xk_bytes + jobs.x32_bytes));
-    float* xstage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(part) +
-                                             (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128));
-    uint8_t* ring = reinterpret_cast<uint8_t*>(xstage) + jobs.stage_bytes;
+    uint8_t* ring = reinterpret_cast<uint8_t*>(part) +
+                    (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < kMaxSeg; ++i)
@@ -646,12 +680,12 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
                 const int nb = row_blocks(g.type, K);
                 const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
-                const int slot = ring_slot(s, Sq), phase = ring_phase(s, Sq);
+                const int slot = ring_slot(s, S), phase = ring_phase(s, S);
                 if (phase > 0) {
-                    const unsigned long long tw = gtimer();
-                    *s_prod_wait = s - 4 * Sq;
-                    if (!mbar_wait(&empty[slot], (uint32_t)((phase - 1) & 1), s_abort)) {
-                        record_wait_fail(1, s, slot, (phase - 1) & 1, n_stages, S, issued, tw, t_kernel, s - 4 * Sq, full,
+                    unsigned long long tw = 0;
+                    *s_prod_wait = s - S;
+                    if (!mbar_wait(&empty[slot], (uint32_t)((phase - 1) & 1), s_abort, &tw)) {
+                        record_wait_fail(1, s, slot, (phase - 1) & 1, n_stages, S, issued, tw, t_kernel, s - S, full,
                                          empty, (int)dyn_smem);
                         ok = false;
                         break;
@@ -674,42 +708,45 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 *s_abort = 1;
                 // let the copies in flight land before the CTA can exit
                 for (int k = max(0, issued - S); k < issued; ++k)
-                    mbar_wait_bounded(&full[ring_slot(k, Sq)], (uint32_t)(ring_phase(k, Sq) & 1));
+                    mbar_wait_bounded(&full[ring_slot(k, S)], (uint32_t)(ring_phase(k, S) & 1));
             }
         }
         return;
     }
 
-    // consumers: the norm weights are constant, so their shared copy is made
-    // before waiting for the previous kernel
-    float* xs = nullptr;
-    float* ws = nullptr;
-    if (jobs.stage_bytes) {
-        xs = xstage;
-        ws = xstage + K;
-        for (int i = threadIdx.x; i < K / 4; i += kConsumers * 32)
-            reinterpret_cast<float4*>(ws)[i] = __ldg(reinterpret_cast<const float4*>(args.pro.w) + i);
+    // consumers: the norm weights are constant, so they are loaded before
+    // waiting for the previous kernel
+    float wv[kNormRegs][8];
+    if (args.pro.mode == PRO_NORM) {
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int c = warp + kConsumers * k;
+            if (c * 256 < K) ld8(args.pro.w, c * 256 + 8 * lane, K, wv[k]);
+        }
     }
     pdl_wait();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_WAITED, s_tseq);
     const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
-    build_ximage(args, xi, wantk, want32, s_scale, s_part, xs, ws);
+    build_ximage(args, xi, wantk, want32, s_part, wv, tr ? s_tseq : -1);
     consumers_sync();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
-    const int half = warp & 1, quarter = warp >> 1;
+    // pair q = warp / 2 takes stages q, q + 4, ...; warp half h of the pair
+    // rows 4h .. 4h+3 of the tile, lane = row * 8 + block
+    const int half = warp & 1, pq = warp >> 1;
     const int r8 = 4 * half + (lane >> 3), bl = lane & 7;
     bool ok = true;
-    for (int s = quarter; s < n_stages; s += kConsumers / 2) {
-        const int tile = t_begin + s / G, gi = s % G;
+    int tile = t_begin + pq / G, gi = pq % G;   // stage pq; advanced incrementally below
+    int slot = pq % S, phase = pq / S;
+    for (int s = pq; s < n_stages; s += kPairs) {
         int sgc, ltc;
         tile_seg(s_tile0, args.nseg, jobs.pair, tile, sgc, ltc);
         const int type = s_seg[sgc].type;
         const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
         const int piece = (int)group_bytes(type, gbk);
-        const int slot = ring_slot(s, Sq), phase = ring_phase(s, Sq);
+        const uint8_t* pc = ring + (size_t)slot * jobs.slot_bytes + (size_t)r8 * piece;
         {
-            const unsigned long long tw = gtimer();
-            if (!mbar_wait(&full[slot], (uint32_t)(phase & 1), s_abort)) {
+            unsigned long long tw = 0;
+            if (!mbar_wait(&full[slot], (uint32_t)(phase & 1), s_abort, &tw)) {
                 if (!*s_abort)
                     record_wait_fail(2, s, slot, phase & 1, n_stages, S, *s_issued, tw, t_kernel, *s_prod_wait, full,
                                      empty, (int)dyn_smem);
@@ -717,7 +754,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 break;
             }
         }
-        const uint8_t* pc = ring + (size_t)slot * jobs.slot_bytes + (size_t)r8 * piece;
+        if (tr && s == 0 && threadIdx.x == 0) trace_ev(TR_GEMV, EV_FIRST, s_tseq);
         float c[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) c[t] = 0.0f;
@@ -733,8 +770,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                     if (t >= T) break;
                     int si, mi;
                     q4k_block<LdShared>(w, xi.qk(t, kb), *reinterpret_cast<const uint4*>(xi.bsk(t, kb)), si, mi);
-                    const float dx = *xi.dk(t, kb);
-                    c[t] = __fmul_rn(dw, dx) * (float)si - __fmul_rn(dmw, dx) * (float)mi;
+                    c[t] = q4k_term(dw, dmw, *xi.dk(t, kb), si, mi);
                 }
             }
         } else if (type == T_Q6_K) {
@@ -748,10 +784,10 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 for (int t = 0; t < NT; ++t) {
                     if (t >= T) break;
                     const int si = q6k_block<LdShared>(w, xi.qk(t, kb), xi.s16(t, kb));
-                    c[t] = __fmul_rn(dw, *xi.dk(t, kb)) * (float)si;
+                    c[t] = scaled_term(dw, *xi.dk(t, kb), si);
                 }
             }
-        } else {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group
+        } else {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group, in block order
             const int kc = gi * 8 + bl;
             for (int i = 0; i < 8; ++i) {
                 const int b = 8 * bl + i;
@@ -763,7 +799,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
                 for (int t = 0; t < NT; ++t) {
                     if (t >= T) break;
                     const int sv = q80_block<LdShared>(w0, w1, xi.q32(t, kc) + 32 * i);
-                    c[t] += __fmul_rn(dw, xi.d32(t, kc)[i]) * (float)sv;
+                    c[t] = __fadd_rn(c[t], scaled_term(dw, xi.d32(t, kc)[i], sv));
                 }
             }
         }
@@ -779,7 +815,19 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        // next stage of this pair: s + 4
+        gi += kPairs;
+        while (gi >= G) {
+            gi -= G;
+            ++tile;
+        }
+        slot += kPairs;
+        if (slot >= S) {
+            slot -= S;
+            ++phase;
+        }
     }
+    if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_LOOP, s_tseq);
     if (!ok) {
         if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
         *s_abort = 1;
@@ -945,23 +993,22 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     jobs.n_groups = row_groups(a->seg[0].type, a->K);
     jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
-    jobs.stage_bytes = (a->pro.mode == PRO_NORM && a->T == 1 && a->K % 512 == 0 && a->K <= 5120) ? 2 * a->K * 4 : 0;
-    const size_t xbytes = (size_t)a->T * (jobs.xk_bytes + jobs.x32_bytes) + jobs.stage_bytes;
+    const int unit = jobs.pair ? 2 : 1;
+    jobs.n_units = (n_tiles + unit - 1) / unit;
+    const size_t xbytes = (size_t)a->T * (jobs.xk_bytes + jobs.x32_bytes);
     int ctas = 0, stages = 0;
     size_t smem = 0;
     for (int cps = NT == 1 ? want_cps : 1;; --cps) {
         const int budget = max_smem / cps - 2048;
-        ctas = std::min(n_tiles, num_sms() * cps);
-        jobs.tiles_per_cta = (n_tiles + ctas - 1) / ctas;
-        if (jobs.pair) jobs.tiles_per_cta += jobs.tiles_per_cta & 1;   // whole (gate, up) pairs per CTA
-        ctas = (n_tiles + jobs.tiles_per_cta - 1) / jobs.tiles_per_cta;
+        ctas = std::min(jobs.n_units, num_sms() * cps);
+        jobs.tiles_per_cta = (jobs.n_units + ctas - 1) / ctas * unit;
         const size_t part = ((size_t)jobs.tiles_per_cta * jobs.n_groups * kTileRows * NT * 4 + 127) / 128 * 128;
         const long long left = (long long)budget - kHdrBytes - (long long)xbytes - (long long)part;
-        stages = 4 * (int)std::min<long long>(kMaxStages / 4, left > 0 ? left / (4LL * slot) : 0);
+        stages = kPairs * (int)std::min<long long>(kMaxStages / kPairs, left > 0 ? left / (kPairs * (long long)slot) : 0);
         smem = kHdrBytes + xbytes + part + (size_t)stages * slot;
-        if (stages >= 4 || cps == 1) break;
+        if (stages >= kPairs || cps == 1) break;
     }
-    if (stages < 4) return (int)cudaErrorInvalidValue;
+    if (stages < kPairs) return (int)cudaErrorInvalidValue;
     jobs.stages = stages;
     return (int)fbk_launch(k_gemv_stream<NT>, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
 }

@@ -106,35 +106,32 @@ __global__ void __launch_bounds__(128) k_quantize_rows(const float* __restrict__
 }
 
 // RMSNorm (src/ops.cpp:18-23: sum of squares in double; out = x*scale*w with
-// scale = 1/sqrt(float(sum/n) + eps)) then quantisation. Every CTA of a row
-// reduces the whole row in the same order, so all get the same scale.
-__global__ void __launch_bounds__(128) k_rmsnorm_quant(const float* __restrict__ x, int ldx,
-                                                       const float* __restrict__ w, float eps, int K,
-                                                       float* __restrict__ xb, int ldxb, ActQ a, int want32,
-                                                       int wantk) {
+// scale = 1/sqrt(float(sum/n) + eps)) then quantisation. A CTA has the
+// kNormWarps warps of the shared summation order (common.cuh) and quantises
+// chunks 8*blockIdx.x + warp; every CTA of a row reduces the whole row in that
+// order, so all of them, and the fused GEMV prologue, get the same scale.
+__global__ void __launch_bounds__(32 * kNormWarps) k_rmsnorm_quant(const float* __restrict__ x, int ldx,
+                                                                  const float* __restrict__ w, float eps, int K,
+                                                                  float* __restrict__ xb, int ldxb, ActQ a, int want32,
+                                                                  int wantk) {
     pdl_trigger();
     pdl_wait();
-    __shared__ double part[kQWarps];
-    __shared__ float s_scale;
+    __shared__ double part[kNormWarps];
     const int t = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_chunks = (K + 255) / 256;
     const float* xr = x + (size_t)t * ldx;
     double s = 0.0;
-    for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
-        const float4 f = *reinterpret_cast<const float4*>(xr + i);
-        s += (double)f.x * f.x + (double)f.y * f.y + (double)f.z * f.z + (double)f.w * f.w;
+    for (int c = warp; c < n_chunks; c += kNormWarps) {
+        float v[8];
+        load8(xr, c * 256, lane, K, v);
+        s = __dadd_rn(s, sumsq8(v));
     }
     s = warp_sum_d(s);
     if (lane == 0) part[warp] = s;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        double tot = 0.0;
-        for (int i = 0; i < kQWarps; ++i) tot += part[i];
-        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tot / K), eps)));
-    }
-    __syncthreads();
-    const int c = blockIdx.x * kQWarps + warp;
-    if (c * 256 >= K) return;
-    const float sc = s_scale;
+    const float sc = norm_total(part, K, eps);
+    const int c = blockIdx.x * kNormWarps + warp;
+    if (c >= n_chunks) return;
     float v[8];
     load8(xr, c * 256, lane, K, v);
     const int i0 = c * 256 + 8 * lane;
@@ -194,7 +191,8 @@ extern "C" int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float 
                                  int ldxb, const ActQ* a, int want32, int wantk, cudaStream_t st) {
     if (T <= 0) return 0;
     if (K % 8 || ldx % 4) return (int)cudaErrorInvalidValue;
-    return (int)fbk_launch(k_rmsnorm_quant, qgrid(K, T), dim3(32 * kQWarps), 0, st, x, ldx, w, eps, K, xb, ldxb, *a, want32,
+    const dim3 grid(((K + 255) / 256 + kNormWarps - 1) / kNormWarps, T);
+    return (int)fbk_launch(k_rmsnorm_quant, grid, dim3(32 * kNormWarps), 0, st, x, ldx, w, eps, K, xb, ldxb, *a, want32,
                            wantk);
 }
 

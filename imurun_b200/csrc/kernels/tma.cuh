@@ -37,12 +37,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait: false after kWaitNs or once another thread raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// The clock is read only once the first try has failed; t_start (optional)
+// receives that time when the wait gives up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned long long* t_start = nullptr) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
     for (unsigned i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) return false;
+        if ((i & 63) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) {
+            if (t_start) *t_start = t0;
+            return false;
+        }
     }
 }
 // Bounded wait that ignores the abort flag (used while draining).

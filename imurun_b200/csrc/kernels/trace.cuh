@@ -13,6 +13,9 @@ namespace fb {
 
 enum : int { TR_GEMV = 1, TR_ATTN = 2, TR_EMBED = 3, TR_KEYS = 4 };
 enum : int { EV_START = 0, EV_WAITED = 1, EV_READY = 2, EV_END = 3 };
+// finer GEMV events: norm scale known, first stage's weights in shared
+// memory, last stage consumed (before the final reduction)
+enum : int { EV_SCALE = 8, EV_FIRST = 9, EV_LOOP = 10 };
 
 struct TraceState {
     unsigned long long* buf;   // [cap][4]

@@ -112,6 +112,60 @@ __device__ __forceinline__ int q6k_block(const uint4 (&w)[13], const int8_t* x, 
     return sumi - 32 * corr;
 }
 
+// Quarter p (0..3) of a Q4_K block, for four lanes that share one block: qs
+// bytes 32p .. 32p+31 (qa, qb), i.e. sub-blocks 2p (low nibbles, x0 x1) and
+// 2p+1 (high nibbles, x2 x3), and bsw = the two 32-value sums of those
+// sub-blocks (int16 pair). acc16 = 16 * (low part) + (unshifted high part);
+// the four lanes' acc16 and mins add up, as integers, to 16 * sumi and to the
+// mins of q4k_block, so sumi = (sum acc16) >> 4 exactly.
+__device__ __forceinline__ void q4k_quarter(uint4 h, uint4 qa, uint4 qb, uint4 x0, uint4 x1, uint4 x2, uint4 x3,
+                                            uint32_t bsw, int p, int& acc16, int& mins) {
+    const uint32_t sc = p < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+    const uint32_t mn = p < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+    const int k0 = (2 * p) & 3;
+    int s0 = 0, s1 = 0;
+    s0 = dp4a_us(qa.x & 0x0F0F0F0Fu, x0.x, s0); s0 = dp4a_us(qa.y & 0x0F0F0F0Fu, x0.y, s0);
+    s0 = dp4a_us(qa.z & 0x0F0F0F0Fu, x0.z, s0); s0 = dp4a_us(qa.w & 0x0F0F0F0Fu, x0.w, s0);
+    s0 = dp4a_us(qb.x & 0x0F0F0F0Fu, x1.x, s0); s0 = dp4a_us(qb.y & 0x0F0F0F0Fu, x1.y, s0);
+    s0 = dp4a_us(qb.z & 0x0F0F0F0Fu, x1.z, s0); s0 = dp4a_us(qb.w & 0x0F0F0F0Fu, x1.w, s0);
+    s1 = dp4a_us(qa.x & 0xF0F0F0F0u, x2.x, s1); s1 = dp4a_us(qa.y & 0xF0F0F0F0u, x2.y, s1);
+    s1 = dp4a_us(qa.z & 0xF0F0F0F0u, x2.z, s1); s1 = dp4a_us(qa.w & 0xF0F0F0F0u, x2.w, s1);
+    s1 = dp4a_us(qb.x & 0xF0F0F0F0u, x3.x, s1); s1 = dp4a_us(qb.y & 0xF0F0F0F0u, x3.y, s1);
+    s1 = dp4a_us(qb.z & 0xF0F0F0F0u, x3.z, s1); s1 = dp4a_us(qb.w & 0xF0F0F0F0u, x3.w, s1);
+    acc16 = 16 * byte_of(sc, k0) * s0 + byte_of(sc, k0 + 1) * s1;
+    mins = byte_of(mn, k0) * (int)(int16_t)(bsw & 0xFFFFu) + byte_of(mn, k0 + 1) * (int)(int16_t)(bsw >> 16);
+}
+
+// Quarter (hh, hl) of a Q6_K block: values l in [16 hl, 16 hl + 16) of half hh
+// of all four quads (the iteration (hh, hl) of q6k_block). a, b = ql bytes
+// 64hh + 16hl and 64hh + 32 + 16hl, hb = qh bytes 32hh + 16hl, sc = the
+// block's 16 scales, xa..xd = x at 128hh + 16hl + 32q, xs16 = sums of x over
+// the same four 16-value runs. Returns sum (q6 - 32) x over those values; the
+// four quarters add up to q6k_block's result.
+__device__ __forceinline__ int q6k_quarter(uint4 a4, uint4 b4, uint4 h4, uint4 sc, uint4 xa, uint4 xb, uint4 xc,
+                                           uint4 xd, const int (&xs16)[4], int hh, int hl) {
+    int s[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t a = word_of(a4, i), b = word_of(b4, i), hb = word_of(h4, i);
+        const uint32_t v0 = (a & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u);
+        const uint32_t v1 = (b & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u);
+        const uint32_t v2 = ((a >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u);
+        const uint32_t v3 = ((b >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u);
+        s[0] = dp4a_us(v0, word_of(xa, i), s[0]);
+        s[1] = dp4a_us(v1, word_of(xb, i), s[1]);
+        s[2] = dp4a_us(v2, word_of(xc, i), s[2]);
+        s[3] = dp4a_us(v3, word_of(xd, i), s[3]);
+    }
+    // scales j = 8hh + 2q + hl: bytes hl and 2 + hl of the halves of word 2hh (q < 2) and 2hh + 1 (q >= 2)
+    const uint32_t w0 = hh ? sc.z : sc.x, w1 = hh ? sc.w : sc.y;
+    const int c0 = (int)(int8_t)byte_of(w0, hl), c1 = (int)(int8_t)byte_of(w0, 2 + hl);
+    const int c2 = (int)(int8_t)byte_of(w1, hl), c3 = (int)(int8_t)byte_of(w1, 2 + hl);
+    const int sumi = c0 * s[0] + c1 * s[1] + c2 * s[2] + c3 * s[3];
+    const int corr = c0 * xs16[0] + c1 * xs16[1] + c2 * xs16[2] + c3 * xs16[3];
+    return sumi - 32 * corr;
+}
+
 // Q8_0 block (qs[32] as 2 uint4) against x (32 int8): s = sum w x.
 template <class LD>
 __device__ __forceinline__ int q80_block(uint4 w0, uint4 w1, const int8_t* x) {

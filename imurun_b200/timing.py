@@ -1,12 +1,16 @@
 """Device timing of single hot-path kernels through the C ABI.
 
     python -m imurun_b200.timing matmul --type 12 --n-in 4096 --n-out 14336 [--tokens 1] [--iters 20]
+    python -m imurun_b200.timing attention --pos 575 [--heads 32 --kv-heads 8 --dim 128 --calls 3]
 
 Runs fbx_time_matmul: 3 warm-up launches, then `iters` launches timed with
 CUDA events, each launch reading a different copy of the weights (>= 512 MB
 of copies, so every launch streams from HBM). Prints one JSON line with the
 mean launch time, the algorithmic bytes of a launch and their ratio. Also
 the command used for profiler captures of one GEMV launch (`-s 3 -c 1`).
+`attention` runs the fused decode-attention kernel (fp16 cache, one
+token at position pos) `calls` times through fbx_attention_decode — the small
+case for profiler captures of that kernel.
 """
 from __future__ import annotations
 
@@ -30,6 +34,23 @@ def time_matmul(lib, type_id: int, n_in: int, n_out: int, tokens: int = 1, iters
             "gb_s": round(float(nbytes[0]) / (us * 1e-6) / 1e9, 1)}
 
 
+def attention(lib, pos: int, heads: int, kv_heads: int, dim: int, calls: int) -> dict:
+    rng = np.random.default_rng(pos)
+    q = rng.standard_normal(heads * dim).astype(np.float32)
+    kc = rng.standard_normal((max(pos, 1), kv_heads * dim)).astype(np.float32)
+    vc = rng.standard_normal((max(pos, 1), kv_heads * dim)).astype(np.float32)
+    kn = rng.standard_normal(kv_heads * dim).astype(np.float32)
+    vn = rng.standard_normal(kv_heads * dim).astype(np.float32)
+    out = np.zeros(heads * dim, np.float32)
+    for _ in range(calls):
+        rc = lib.fbx_attention_decode(q.ctypes.data, kc.ctypes.data, vc.ctypes.data, kn.ctypes.data, vn.ctypes.data, pos,
+                                      heads, kv_heads, dim, dim, 0, 500000.0, 1, out.ctypes.data, None, None)
+        if rc != 0:
+            raise RuntimeError(f"fbx_attention_decode failed: {rc}")
+    return {"pos": pos, "heads": heads, "kv_heads": kv_heads, "dim": dim, "calls": calls,
+            "out_absmax": float(np.abs(out).max())}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -39,9 +60,18 @@ def main() -> None:
     mm.add_argument("--n-out", type=int, required=True)
     mm.add_argument("--tokens", type=int, default=1)
     mm.add_argument("--iters", type=int, default=20)
+    at = sub.add_parser("attention")
+    at.add_argument("--pos", type=int, required=True)
+    at.add_argument("--heads", type=int, default=32)
+    at.add_argument("--kv-heads", type=int, default=8)
+    at.add_argument("--dim", type=int, default=128)
+    at.add_argument("--calls", type=int, default=3)
     a = ap.parse_args()
     lib = native.load_library()
-    print(json.dumps(time_matmul(lib, a.type, a.n_in, a.n_out, a.tokens, a.iters)), flush=True)
+    if a.cmd == "matmul":
+        print(json.dumps(time_matmul(lib, a.type, a.n_in, a.n_out, a.tokens, a.iters)), flush=True)
+    else:
+        print(json.dumps(attention(lib, a.pos, a.heads, a.kv_heads, a.dim, a.calls)), flush=True)
 
 
 if __name__ == "__main__":
