@@ -85,15 +85,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_from_profiles():
-    f = ROOT / "profiles" / "gemv_llama8b_decode.txt"
+def traffic_ratio_from_profiles():
+    """DRAM bytes per algorithmic byte of the GEMV, from the committed ncu
+    summary (one captured launch of the same kernel on an 8B-shaped matrix)."""
+    f = ROOT / "profiles" / "gemv_stream_q4k_4096x14336.md"
     if not f.exists():
         return None
     for ln in f.read_text().splitlines():
-        if ln.startswith("traffic_bytes_per_launch:"):
+        if "dram_bytes_per_algorithmic_byte:" in ln:
             try:
-                return float(ln.split(":", 1)[1].split()[0])
-            except ValueError:
+                return float(ln.split("dram_bytes_per_algorithmic_byte:", 1)[1].split()[0])
+            except (ValueError, IndexError):
                 return None
     return None
 
@@ -257,6 +259,8 @@ def run_ours(args):
     g = cls["gemv"]
     peak, peak_kind = peaks()
     achieved = (g["bytes"] / g["launches"]) / ((g["ms"] / g["launches"]) / 1e3) / 1e9
+    ratio = traffic_ratio_from_profiles()
+    traffic = round(ratio * g["bytes"] / g["launches"]) if ratio else None
     total_ms = sum(c["ms"] for c in prof["classes"])
     # whole decode step against HBM: weights (GGUF bytes, embedding row only) + KV read
     info = m.info
@@ -291,8 +295,10 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches_per_step * K * WORLD),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
-                         "kernel": "k_gemv<1> (Q4_K/Q6_K decode GEMV)", "peak_kind": peak_kind},
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "k_gemv_stream<1> (Q4_K/Q6_K decode GEMV)", "peak_kind": peak_kind,
+                         "traffic_note": "bytes per launch = ncu DRAM/algorithmic ratio of one captured launch "
+                                         "(profiles/gemv_stream_q4k_4096x14336.md) x this run's algorithmic bytes per launch"},
             "cpu_baseline": cpu,
             "clocks": clk,
         }
