@@ -567,12 +567,37 @@ int fish_trace_decode(fish_ctx* ctx, int32_t first, int n_steps, uint64_t* out, 
     if (!ctx || !out || cap <= 0 || n_steps <= 0) return -1;
     std::lock_guard<std::mutex> lock(ctx->mu);
     if (!need_model(ctx)) return -1;
-    if (fbk_trace_enable(cap)) { ctx->err = "trace buffer"; return -2; }
     std::vector<int32_t> ids(n_steps);
     std::string err;
-    const int n = ctx->eng->decode_greedy(0, first, n_steps, ids.data(), &err);
-    const int got = fbk_trace_dump(reinterpret_cast<unsigned long long*>(out), cap);
-    fbk_trace_enable(0);
+    int n = 0, got = 0;
+    if (ctx->eng->step_ready()) {
+        // persistent step kernel: phase boundaries of the first and the last
+        // CTA, as records (ns, tag 5, event, step * 2 + which CTA)
+        const size_t vals = (size_t)n_steps * fb::kStepTraceEvents * 2;
+        unsigned long long* dev = nullptr;
+        if (cudaMalloc(&dev, vals * sizeof(unsigned long long)) != cudaSuccess) { ctx->err = "trace buffer"; return -2; }
+        cudaMemset(dev, 0, vals * sizeof(unsigned long long));
+        ctx->eng->set_step_trace(dev);
+        n = ctx->eng->decode_greedy(0, first, n_steps, ids.data(), &err);
+        ctx->eng->set_step_trace(nullptr);
+        std::vector<unsigned long long> h(vals);
+        cudaMemcpy(h.data(), dev, vals * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        cudaFree(dev);
+        for (size_t i = 0; i < vals && got < cap; ++i) {
+            if (!h[i]) continue;
+            const size_t step = i / (2 * fb::kStepTraceEvents), ev = (i / 2) % fb::kStepTraceEvents, which = i % 2;
+            uint64_t* r = out + 4 * (size_t)got++;
+            r[0] = h[i];
+            r[1] = 5;
+            r[2] = ev;
+            r[3] = step * 2 + which;
+        }
+    } else {
+        if (fbk_trace_enable(cap)) { ctx->err = "trace buffer"; return -2; }
+        n = ctx->eng->decode_greedy(0, first, n_steps, ids.data(), &err);
+        got = fbk_trace_dump(reinterpret_cast<unsigned long long*>(out), cap);
+        fbk_trace_enable(0);
+    }
     if (n < 0) { ctx->err = err; return -2; }
     ctx->cache_ids.push_back(first);
     for (int i = 0; i + 1 < n; ++i) ctx->cache_ids.push_back(ids[i]);
@@ -690,11 +715,14 @@ const char* fish_engine_json(fish_ctx* ctx) {
     std::snprintf(b, sizeof(b),
                   "{\"device\":\"%s\",\"kv_page_size\":%d,\"kv_free_pages\":%d,\"kv_bytes\":%llu,"
                   "\"weights_device_bytes\":%llu,\"greedy_graph_kernels\":%d,\"step_graph_kernels\":%d,"
-                  "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d,\"wait_failures\":%d,\"wait_records\":",
+                  "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d,\"wait_failures\":%d,"
+                  "\"step_kernel\":%d,\"step_grid\":%d,\"step_ring_slots\":%d,\"step_slot_bytes\":%d,"
+                  "\"step_weight_bytes\":%.0f,\"last_step_ms\":%.6f,\"wait_records\":",
                   e.device_name().c_str(), e.page_size(), e.free_pages(), (unsigned long long)e.kv_bytes(),
                   (unsigned long long)e.device_weight_bytes(), e.graph_kernels(0), e.graph_kernels(1),
-                  (double)e.last_greedy_ms(), kerr, nwr);
-    buf = std::string(b) + recs + "}";
+                  (double)e.last_greedy_ms(), kerr, nwr, e.step_ready() ? 1 : 0, e.step_grid(), e.step_stages(),
+                  e.step_slot_bytes(), e.step_weight_bytes(), (double)e.last_step_ms());
+    buf = std::string(b) + recs + ",\"step_unavailable\":\"" + e.step_why() + "\"}";
     return buf.c_str();
 }
 

@@ -1,5 +1,7 @@
 // engine.cpp — see engine.h.
 #include "engine.h"
+#include "kernels/layout.cuh"
+#include "kernels/stream_common.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -136,6 +138,7 @@ Engine::~Engine() {
     cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_); cudaFree(amax_keys_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
+    cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
@@ -769,6 +772,227 @@ static ActQ act_row(const ActQ& a, int row, int K) {
     return r;
 }
 
+// ------------------------------------------------------------------ persistent step
+
+// One streamed-GEMV job of the step program: the same segments, prologue and
+// epilogue as the graph path's launch for one token.
+static bool step_job(const DevW* const* ws, float* const* ys, const int* lds, const float* const* bs, const int* epis,
+                     int n, const GemvPro& pro, bool swiglu, int grid, StepPhase* out, int* slot_max, int* union_need,
+                     double* wbytes) {
+    StepPhase ph{};
+    GemvArgs& g = ph.a;
+    g.nseg = n;
+    g.K = ws[0]->n_in;
+    g.T = 1;
+    g.pro = pro;
+    g.swiglu = swiglu ? 1 : 0;
+    bool wantk = false, want32 = false;
+    const int G = row_groups(ws[0]->type, g.K);
+    ph.tile0[0] = 0;
+    for (int i = 0; i < n; ++i) {
+        const DevW& w = *ws[i];
+        if (!is_tiled(w.type) || w.n_in != g.K || row_groups(w.type, g.K) != G) return false;
+        if ((w.type == T_Q4_K || w.type == T_Q6_K) && g.K % 256) return false;
+        GemvSeg& sg = g.seg[i];
+        sg.type = w.type;
+        sg.w = w.d;
+        sg.row_stride = w.stride;
+        sg.w_bytes = w.expert_bytes * (size_t)w.n_exp;
+        sg.rows = w.n_out;
+        sg.y = ys[i];
+        sg.ldy = lds[i];
+        sg.bias = bs ? bs[i] : nullptr;
+        sg.epi = epis[i];
+        ph.tile0[i + 1] = ph.tile0[i] + (w.n_out + kTileRows - 1) / kTileRows;
+        *slot_max = std::max(*slot_max, kTileRows * (int)group_bytes(w.type, blocks_per_group(w.type)));
+        if (w.type == T_Q8_0) want32 = true; else wantk = true;
+        *wbytes += (double)ggml_row_bytes(w.type, (uint64_t)w.n_in) * w.n_out;
+    }
+    for (int i = n; i < kMaxSeg; ++i) ph.tile0[i + 1] = ph.tile0[i];
+    if (g.K % 8) return false;
+    const int unit = swiglu ? 2 : 1;
+    if (swiglu && (n != 2 || ws[0]->n_out != ws[1]->n_out)) return false;
+    ph.n_units = (ph.tile0[n] + unit - 1) / unit;
+    ph.G = G;
+    ph.xk_bytes = wantk ? ximg_k_bytes(g.K) : 0;
+    ph.x32_bytes = want32 ? ximg_32_bytes(g.K) : 0;
+    ph.attn_layer = -1;
+    const int tiles_max = (ph.n_units + grid - 1) / grid * unit;
+    const int part = ((tiles_max * G * kTileRows * 4) + 127) / 128 * 128;
+    *union_need = std::max(*union_need, ph.xk_bytes + ph.x32_bytes + part);
+    *out = ph;
+    return true;
+}
+
+bool Engine::step_ready() {
+    if (step_state_) return step_state_ > 0;
+    step_state_ = -1;
+    const Config& c = cfg_;
+    if (!env_int("FISH_PERSIST", 0)) { step_why_ = "off (FISH_PERSIST=1 enables it)"; return false; }
+    if (c.n_experts > 0) { step_why_ = "mixture of experts"; return false; }
+    if (c.qk_norm) { step_why_ = "q/k norm"; return false; }
+    const int G = c.n_head_kv > 0 ? c.n_head / c.n_head_kv : 0;
+    if (c.head_dim != 128 || c.n_head % c.n_head_kv || !(G == 1 || G == 2 || G == 4 || G == 8) || c.rot_dim > 128 ||
+        c.rot_dim % 2) {
+        step_why_ = "attention shape";
+        return false;
+    }
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = sms;   // one CTA per SM
+    const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim(), F = c.n_ff, D = c.head_dim;
+    std::vector<StepPhase> phs;
+    int slot = 0, uni = 0;
+    double wb = 0.0;
+    for (int li = 0; li < c.n_layers; ++li) {
+        const DevLayer& L = layers_[li];
+        StepPhase ph{};
+        {
+            const DevW* ws[3] = {&L.wq, &L.wk, &L.wv};
+            float* ys[3] = {q_, k_, v_};
+            const int lds[3] = {Q, KV, KV};
+            const float* bs[3] = {L.bq, L.bk, L.bv};
+            const int ep[3] = {EPI_STORE, EPI_STORE, EPI_STORE};
+            const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.attn_norm, c.eps};
+            if (!step_job(ws, ys, lds, bs, ep, 3, pro, false, grid, &ph, &slot, &uni, &wb)) { step_why_ = "qkv weights"; return false; }
+            phs.push_back(ph);
+        }
+        {
+            const DevW* ws[1] = {&L.wo};
+            float* ys[1] = {x_};
+            const int lds[1] = {E};
+            const int ep[1] = {EPI_ADD};
+            const GemvPro pro{PRO_MERGE, att_part_, 0, nullptr, D, nullptr, 0.0f};   // src patched below
+            if (!step_job(ws, ys, lds, nullptr, ep, 1, pro, false, grid, &ph, &slot, &uni, &wb)) { step_why_ = "o weights"; return false; }
+            ph.attn_layer = li;
+            phs.push_back(ph);
+        }
+        {
+            const DevW* ws[2] = {&L.wg, &L.wu};
+            float* ys[2] = {g_, u_};
+            const int lds[2] = {F, F};
+            const int ep[2] = {EPI_STORE, EPI_STORE};
+            const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.ffn_norm, c.eps};
+            if (!step_job(ws, ys, lds, nullptr, ep, 2, pro, true, grid, &ph, &slot, &uni, &wb)) { step_why_ = "ffn weights"; return false; }
+            phs.push_back(ph);
+        }
+        {
+            const DevW* ws[1] = {&L.wd};
+            float* ys[1] = {x_};
+            const int lds[1] = {E};
+            const int ep[1] = {EPI_ADD};
+            const GemvPro pro{PRO_QUANT, g_, F, nullptr, 0, nullptr, 0.0f};
+            if (!step_job(ws, ys, lds, nullptr, ep, 1, pro, false, grid, &ph, &slot, &uni, &wb)) { step_why_ = "down weights"; return false; }
+            phs.push_back(ph);
+        }
+    }
+    {
+        StepPhase ph{};
+        const DevW* ws[1] = {&out_w_};
+        float* ys[1] = {logits_};
+        const int lds[1] = {c.vocab};
+        const int ep[1] = {EPI_STORE};
+        const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, out_norm_, c.eps};
+        if (!step_job(ws, ys, lds, nullptr, ep, 1, pro, false, grid, &ph, &slot, &uni, &wb)) { step_why_ = "output weights"; return false; }
+        ph.a.seg[0].amax = reinterpret_cast<unsigned long long*>(1);   // patched per step on the device
+        phs.push_back(ph);
+    }
+    // attention scratch in the same union area: q [G][D+4], own k/v [2][D], warp partials [8][G][D+2]
+    // (+ page bases of a chunk: 80 x 8 bytes)
+    uni = std::max(uni, (int)(sizeof(float) * (G * (D + 4) + 2 * D + 8 * G * (D + 2)) + 80 * sizeof(size_t)));
+    uni = (uni + 127) / 128 * 128;   // the ring after it starts 128-byte aligned
+    int g2 = 0, S = 0;
+    size_t smem = 0;
+    const int rc = fbk_step_plan(G, kv_f16_ ? 1 : 0, slot, uni, &g2, &S, &smem);
+    if (rc != 0 || g2 != grid) { step_why_ = "step kernel does not fit (plan " + std::to_string(rc) + ")"; cudaGetLastError(); return false; }
+    // key chunks per kv head: at most 8 (the o projection's prologue merges
+    // them), more only when a chunk would exceed ~1024 keys
+    att_max_chunks_ = std::min(grid / c.n_head_kv, std::max(8, (c.n_ctx + 1023) / 1024));
+    const size_t part_floats = (size_t)att_max_chunks_ * c.n_head * (D + 2);
+    if (cudaMalloc(&att_part_, part_floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&step_ctl_, sizeof(StepCtl)) != cudaSuccess ||
+        cudaMalloc(&step_keys_, 2 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMalloc(&step_ph_, phs.size() * sizeof(StepPhase)) != cudaSuccess) {
+        step_why_ = "allocation";
+        cudaGetLastError();
+        return false;
+    }
+    for (StepPhase& ph : phs)
+        if (ph.a.pro.mode == PRO_MERGE) ph.a.pro.src = att_part_;
+    if (cudaMemcpy(step_ph_, phs.data(), phs.size() * sizeof(StepPhase), cudaMemcpyHostToDevice) != cudaSuccess) {
+        step_why_ = "upload";
+        return false;
+    }
+    (void)Q;
+    step_nph_ = (int)phs.size();
+    step_grid_ = grid;
+    step_S_ = S;
+    step_slot_ = slot;
+    step_union_ = uni;
+    step_smem_ = smem;
+    step_wbytes_ = wb;
+    step_state_ = 1;
+    step_why_.clear();
+    return true;
+}
+
+// n_steps greedy steps of sequence sid from ids_[0] at tok_pos_[0] (already
+// uploaded); argmax of step i -> out_dev[i]; logits of the last step in logits_.
+bool Engine::run_step(int sid, int n_steps, int32_t* out_dev, std::string* err) {
+    const Config& c = cfg_;
+    StepArgs A{};
+    A.ph = step_ph_;
+    A.n_ph = step_nph_;
+    A.q = q_;
+    A.k = k_;
+    A.v = v_;
+    A.att_part = att_part_;
+    A.rcos = rope_cos_;
+    A.rsin = rope_sin_;
+    A.H = c.n_head;
+    A.HKV = c.n_head_kv;
+    A.D = c.head_dim;
+    A.rot = c.rot_dim;
+    A.neox = c.neox ? 1 : 0;
+    A.scale = 1.0f / std::sqrt((float)c.head_dim);
+    A.max_chunks = att_max_chunks_;
+    A.kv = kv_view();
+    A.sid = sid;
+    A.emb_type = embd_.type;
+    A.emb = embd_.d;
+    A.E = c.n_embd;
+    A.emb_rows = embd_.n_out;
+    A.x = x_;
+    A.ids = ids_;
+    A.tok_pos = tok_pos_;
+    A.out = out_dev;
+    A.n_steps = n_steps;
+    A.keys = step_keys_;
+    A.ctl = step_ctl_;
+    A.S = step_S_;
+    A.slot_bytes = step_slot_;
+    A.union_bytes = step_union_;
+    A.trace = step_trace_;
+    CK(cudaMemsetAsync(step_ctl_, 0, sizeof(StepCtl), stream_));
+    CK(cudaMemsetAsync(step_keys_, 0, 2 * sizeof(unsigned long long), stream_));
+    cudaEventRecord(pe0_, stream_);
+    CK(fbk_step_decode(&A, step_grid_, step_smem_, stream_));
+    cudaEventRecord(pe1_, stream_);
+    StepCtl h{};
+    CK(cudaMemcpyAsync(&h, step_ctl_, sizeof(StepCtl), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    cudaEventElapsedTime(&last_step_ms_, pe0_, pe1_);
+    if (h.err) {
+        if (err)
+            *err = "step kernel failed: code " + std::to_string(h.err) + " (CTA " + std::to_string(h.info[0]) + ", step " +
+                   std::to_string(h.info[1]) + ", phase " + std::to_string(h.info[2]) + ", stage " +
+                   std::to_string(h.info[3]) + ", slot " + std::to_string(h.info[4]) + ")";
+        return false;
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ forward
 
 bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
@@ -962,7 +1186,9 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
     if (prof_) CK(fbk_delay(5000000ull, stream_));
     const bool all = logits_all != nullptr || argmax != nullptr;
     const int nrows = all ? T : 1;
-    if (T == 1 && use_graphs_ && !prof_) {
+    if (T == 1 && !prof_ && step_ready()) {
+        if (!run_step(sid, 1, argmax_, err)) return false;
+    } else if (T == 1 && use_graphs_ && !prof_) {
         if (!graphs_.count(1) && !capture_graph(1, err)) return false;
         CK(cudaGraphLaunch(graphs_[1], stream_));
     } else {
@@ -1023,6 +1249,16 @@ int Engine::decode_greedy(int sid, int32_t first, int n_steps, int32_t* out, std
     const int pos = s.len;
     if (!upload_tokens(&first, &sid, &pos, 1, err)) return -1;
     if (cudaMemsetAsync(greedy_step_, 0, sizeof(int32_t), stream_) != cudaSuccess) { if (err) *err = "memset failed"; return -1; }
+    if (step_ready()) {
+        if (!run_step(sid, n_steps, greedy_out_, err)) return -1;
+        last_greedy_ms_ = last_step_ms_;
+        if (cudaMemcpy(out, greedy_out_, sizeof(int32_t) * n_steps, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            if (err) *err = "copy failed";
+            return -1;
+        }
+        s.len += n_steps;
+        return n_steps;
+    }
     if (!graphs_.count(0) && !capture_graph(0, err)) return -1;
     cudaGraphExec_t exec = graphs_[0];
     cudaEventRecord(ev0_, stream_);

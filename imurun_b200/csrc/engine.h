@@ -120,6 +120,21 @@ public:
     // ---- kernel-level access for the parity entry points
     cudaStream_t stream() const { return stream_; }
 
+    // Persistent decode step (k_step): used for single-sequence decode of
+    // dense models it supports when FISH_PERSIST=1 is set. step_ready()
+    // builds its phase program on first use; step_why() says why not.
+    bool step_ready();
+    const std::string& step_why() const { return step_why_; }
+    int step_grid() const { return step_grid_; }
+    int step_stages() const { return step_S_; }
+    int step_slot_bytes() const { return step_slot_; }
+    double step_weight_bytes() const { return step_wbytes_; }   // GGUF bytes streamed per step
+    // Device time of the last step-kernel launch (CUDA events around it).
+    float last_step_ms() const { return last_step_ms_; }
+    // Phase trace of the step kernel (device buffer of kStepTraceEvents * 2
+    // values per step, or null = off).
+    void set_step_trace(unsigned long long* dev) { step_trace_ = dev; }
+
 private:
     bool alloc_buffers(std::string* err);
     bool upload_weights(std::string* err);
@@ -201,6 +216,20 @@ private:
     std::map<int, int> graph_kernels_;
     bool use_graphs_ = true;
     bool no_fuse_ = false;     // FISH_NO_FUSE: separate norm/quant kernels before every GEMV
+    // persistent step
+    bool run_step(int sid, int n_steps, int32_t* out_dev, std::string* err);
+    int step_state_ = 0;       // 0 not built, 1 ready, -1 unavailable
+    std::string step_why_;
+    StepPhase* step_ph_ = nullptr;
+    int step_nph_ = 0;
+    StepCtl* step_ctl_ = nullptr;
+    unsigned long long* step_keys_ = nullptr;
+    float* att_part_ = nullptr;
+    int step_grid_ = 0, step_S_ = 0, step_slot_ = 0, step_union_ = 0, att_max_chunks_ = 0;
+    size_t step_smem_ = 0;
+    double step_wbytes_ = 0.0;
+    float last_step_ms_ = 0.0f;
+    unsigned long long* step_trace_ = nullptr;
     float last_greedy_ms_ = 0.0f;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     std::vector<ProfClass>* prof_ = nullptr;

@@ -32,6 +32,7 @@
 #include "kernels.h"
 #include "launch.cuh"
 #include "layout.cuh"
+#include "stream_common.cuh"
 #include "tma.cuh"
 #include "trace.cuh"
 #include "unit_math.cuh"
@@ -94,36 +95,10 @@ void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst) {
     }
 }
 
-// ============================================================ common pieces
-
-__device__ __forceinline__ float store_out(const GemvSeg& g, int rr, int t, float v) {
-    if (g.bias) v += g.bias[rr];
-    float* yp = g.y + (size_t)t * g.ldy + rr;
-    if (g.epi == EPI_ADD) v += *yp;
-    *yp = v;
-    return v;
-}
-
 // ============================================================ direct kernel
 
-// One lane per (row, block) of 4 rows: weights streamed from global memory,
-// activations from the quantised planes through the read-only cache.
-// true when [p, p + n) lies inside [lo, hi); otherwise the error flag is raised
-__device__ __forceinline__ bool in_range(const uint8_t* p, size_t n, const uint8_t* lo, const uint8_t* hi, int* err) {
-    if (p >= lo && p + n <= hi) return true;
-    if (err) atomicExch(err, 3);
-    return false;
-}
-
-// Float steps of one block, shared by both kernels (explicit roundings, so no
-// multiply-add contraction can make the two kernels differ):
-//   Q4_K  (dw dx) si - (dmin dx) mins      Q6_K, Q8_0  (dw dx) s
-__device__ __forceinline__ float q4k_term(float dw, float dmw, float dx, int si, int mi) {
-    return __fsub_rn(__fmul_rn(__fmul_rn(dw, dx), (float)si), __fmul_rn(__fmul_rn(dmw, dx), (float)mi));
-}
-__device__ __forceinline__ float scaled_term(float dw, float dx, int s) { return __fmul_rn(__fmul_rn(dw, dx), (float)s); }
-
-// One row, 8 lanes (bl = lane & 7). Summation order shared with
+// Weights streamed from global memory, activations from the quantised planes
+// through the read-only cache. One row, 8 lanes (bl = lane & 7). Summation order shared with
 // k_gemv_stream, so a row's result does not depend on which kernel (which
 // batch size) computed it: per 2048-value group, lane bl's term (the block
 // gi*8 + bl for K-quants; for Q8_0 the sum, in block order, of blocks
@@ -296,12 +271,8 @@ __global__ void k_block_sums(int type, const uint8_t* __restrict__ w, int rows, 
 
 // ============================================================ streamed kernel
 
-constexpr int kConsumers = 8;                       // consumer warps: 4 pairs, a pair per stage
-constexpr int kMaxStages = 32;
 constexpr int kHdrBytes = 2 * kMaxStages * 8 + 64;  // mbarriers, abort flag, norm scales
-constexpr int kXChunk = 272;                        // bytes per 256 activation int8 (16 B pad: no bank conflicts)
 
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
 // Records of bounded waits that gave up (read with fbk_take_wait_record),
 // up to kWaitRecs, 16 values each:
@@ -334,7 +305,6 @@ __device__ __noinline__ void record_wait_fail(int kind, int s, int slot, int par
 // touches is only ever its own (slot = s % S keeps s's residue mod 4), and it
 // waits on each of them phase after phase: never for a phase two ahead of the
 // barrier, which a parity wait could not tell apart.
-constexpr int kPairs = kConsumers / 2;
 __device__ __forceinline__ int ring_slot(int s, int S) { return s % S; }
 __device__ __forceinline__ int ring_phase(int s, int S) { return s / S; }
 
@@ -352,262 +322,6 @@ struct StreamJobs {
     int pair;                // tiles alternate between segments 0 and 1 (SwiGLU epilogue)
 };
 
-// Segment of a tile (segments are copied to shared memory at kernel start,
-// so no parameter array is indexed dynamically).
-__device__ __forceinline__ int seg_index(const int* tile0, int nseg, int tile) {
-    int sg = 0;
-#pragma unroll
-    for (int i = 1; i < kMaxSeg; ++i)
-        if (i < nseg && tile >= tile0[i]) sg = i;
-    return sg;
-}
-// Segment and segment-local tile of a tile: in pair mode tiles alternate
-// (gate tile j, up tile j) so one CTA holds both halves of its output rows.
-__device__ __forceinline__ void tile_seg(const int* tile0, int nseg, int pair, int tile, int& sg, int& lt) {
-    if (pair) {
-        sg = tile & 1;
-        lt = tile >> 1;
-    } else {
-        sg = seg_index(tile0, nseg, tile);
-        lt = tile - tile0[sg];
-    }
-}
-
-// Activation image in shared memory, per token:
-//   K layout (256-value blocks): q [n256][272], bsums [n256][8] i16,
-//                                sum16 [n256][16] i16, d [n256] f32
-//   32 layout:                   q [n256][272], d [n256][8] f32
-struct XImage {
-    uint8_t* base;
-    int n256, xk, x32, T;
-    __device__ int8_t* qk(int t, int c) const { return (int8_t*)(base + (size_t)t * xk + (size_t)c * kXChunk); }
-    __device__ int16_t* bsk(int t, int c) const {
-        return (int16_t*)(base + (size_t)t * xk + (size_t)n256 * kXChunk + 16 * c);
-    }
-    __device__ int16_t* s16(int t, int c) const {
-        return (int16_t*)(base + (size_t)t * xk + (size_t)n256 * (kXChunk + 16) + 32 * c);
-    }
-    __device__ float* dk(int t, int c) const {
-        return (float*)(base + (size_t)t * xk + (size_t)n256 * (kXChunk + 48) + 4 * c);
-    }
-    __device__ int8_t* q32(int t, int c) const {
-        return (int8_t*)(base + (size_t)T * xk + (size_t)t * x32 + (size_t)c * kXChunk);
-    }
-    __device__ float* d32(int t, int c) const {
-        return (float*)(base + (size_t)T * xk + (size_t)t * x32 + (size_t)n256 * kXChunk + 32 * c);
-    }
-};
-
-static inline int ximg_k_bytes(int K) { return (((K + 255) / 256) * (kXChunk + 16 + 32 + 4) + 15) / 16 * 16; }
-static inline int ximg_32_bytes(int K) { return (((K + 255) / 256) * (kXChunk + 32) + 15) / 16 * 16; }
-
-__device__ __forceinline__ uint2 pack8q(const int (&q)[8]) {
-    uint2 p;
-    p.x = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
-    p.y = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-    return p;
-}
-
-// Quantise one 256-value chunk (8 values per lane) into the image, both
-// layouts as requested, with the reference's arithmetic (the same steps as
-// quant_act.cu: d = amax/127, id = 1/d, round half to even, clamp).
-__device__ __forceinline__ void ximg_quant_chunk(const float (&v)[8], int lane, int K, int t, int c,
-                                                 const XImage& xi, bool wantk, bool want32) {
-    const bool full = c * 256 + 256 <= K;
-    float am = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
-    if (wantk && full) {
-        const float amax = warp_max(am);
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int q[8], s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], id))));
-            s += q[i];
-        }
-        *reinterpret_cast<uint2*>(xi.qk(t, c) + 8 * lane) = pack8q(q);
-        const int s16v = s + __shfl_xor_sync(0xffffffffu, s, 1);
-        const int s32v = s16v + __shfl_xor_sync(0xffffffffu, s16v, 2);
-        if ((lane & 1) == 0) xi.s16(t, c)[lane >> 1] = (int16_t)s16v;
-        if ((lane & 3) == 0) xi.bsk(t, c)[lane >> 2] = (int16_t)s32v;
-        if (lane == 0) *xi.dk(t, c) = d;
-    }
-    if (want32) {
-        float b = am;
-        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 1));
-        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 2));
-        const float d = __fdiv_rn(b, 127.0f);
-        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int q[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] = max(-127, min(127, __float2int_rn(__fmul_rn(v[i], id))));
-        *reinterpret_cast<uint2*>(xi.q32(t, c) + 8 * lane) = pack8q(q);
-        if ((lane & 3) == 0) xi.d32(t, c)[lane >> 2] = d;
-    }
-}
-
-__device__ __forceinline__ void ld8(const float* p, int i0, int K, float (&v)[8]) {
-    if (i0 + 8 <= K) {
-        const float4 a = *reinterpret_cast<const float4*>(p + i0);
-        const float4 b = *reinterpret_cast<const float4*>(p + i0 + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-    }
-}
-
-// Norm weights a consumer lane keeps in registers: chunks warp + 8k, k < 2
-// (all of them up to K = 4096), loaded before the wait for the previous kernel.
-constexpr int kNormRegs = 2;
-static_assert(kConsumers == kNormWarps, "the fused norm sums in the shared order of k_rmsnorm_quant");
-
-// Consumer prologue: build the activation image for T tokens.
-__device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32,
-                                             double* s_part, const float (&wv)[kNormRegs][8], int tseq) {
-    const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31;
-    const int K = args.K, T = args.T, n256 = xi.n256;
-    const GemvPro& pro = args.pro;
-    if (pro.mode == PRO_ACT) {
-        const ActQ& a = args.act;
-        for (int t = 0; t < T; ++t) {
-            if (wantk) {
-                for (int i = ct; i < n256 * 16; i += kConsumers * 32) {
-                    const int c = i >> 4, j = i & 15;
-                    const uint4 v =
-                        __ldg(reinterpret_cast<const uint4*>(a.qk + (size_t)t * a.ld + (size_t)c * 256 + 16 * j));
-                    *reinterpret_cast<uint4*>(xi.qk(t, c) + 16 * j) = v;
-                    xi.s16(t, c)[j] = (int16_t)sum16(v);
-                }
-                for (int c = ct; c < n256; c += kConsumers * 32) {
-                    *reinterpret_cast<uint4*>(xi.bsk(t, c)) =
-                        __ldg(reinterpret_cast<const uint4*>(a.bsk + (size_t)t * (K / 32) + (size_t)c * 8));
-                    *xi.dk(t, c) = __ldg(a.dk + (size_t)t * (K / 256) + c);
-                }
-            }
-            if (want32) {
-                for (int i = ct; i < K / 16; i += kConsumers * 32) {
-                    const int c = i >> 4, j = i & 15;
-                    *reinterpret_cast<uint4*>(xi.q32(t, c) + 16 * j) =
-                        __ldg(reinterpret_cast<const uint4*>(a.q32 + (size_t)t * a.ld + 16 * (size_t)i));
-                }
-                for (int b = ct; b < K / 32; b += kConsumers * 32)
-                    xi.d32(t, b >> 3)[b & 7] = __ldg(a.d32 + (size_t)t * (K / 32) + b);
-            }
-        }
-        return;
-    }
-    const int n_chunks = (K + 255) / 256;
-    if (pro.mode == PRO_NORM) {
-        // the reference's double sum (src/ops.cpp:18-23) in the order every
-        // norm kernel shares (common.cuh); chunks that fit stay in registers
-        // between the sum and the quantisation
-        for (int t = 0; t < T; ++t) {
-            const float* xr = pro.src + (size_t)t * pro.ld;
-            float va[kNormRegs][8];
-#pragma unroll
-            for (int k = 0; k < kNormRegs; ++k) {
-                const int c = warp + kConsumers * k;
-                if (c < n_chunks) ld8(xr, c * 256 + 8 * lane, K, va[k]);
-            }
-            double s = 0.0;
-#pragma unroll
-            for (int k = 0; k < kNormRegs; ++k)
-                if (warp + kConsumers * k < n_chunks) s = __dadd_rn(s, sumsq8(va[k]));
-            for (int c = warp + kConsumers * kNormRegs; c < n_chunks; c += kConsumers) {
-                float v[8];
-                ld8(xr, c * 256 + 8 * lane, K, v);
-                s = __dadd_rn(s, sumsq8(v));
-            }
-            s = warp_sum_d(s);
-            if (lane == 0) s_part[warp] = s;
-            consumers_sync();
-            const float sc = norm_total(s_part, K, pro.eps);
-            if (t == 0 && tseq >= 0 && ct == 0) trace_ev(TR_GEMV, EV_SCALE, tseq);
-            consumers_sync();   // s_part is reused by the next token
-#pragma unroll
-            for (int k = 0; k < kNormRegs; ++k) {
-                const int c = warp + kConsumers * k;
-                if (c < n_chunks) {
-                    const int i0 = c * 256 + 8 * lane;
-                    float v[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(va[k][i], sc), wv[k][i]) : 0.0f;
-                    ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
-                }
-            }
-            for (int c = warp + kConsumers * kNormRegs; c < n_chunks; c += kConsumers) {
-                const int i0 = c * 256 + 8 * lane;
-                float xv[8], w8[8], v[8];
-                ld8(xr, i0, K, xv);
-                ld8(pro.w, i0, K, w8);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = i0 + i < K ? __fmul_rn(__fmul_rn(xv[i], sc), w8[i]) : 0.0f;
-                ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
-            }
-        }
-        return;
-    }
-    // quantisation: warp w takes chunks w, w + 8, ...; each batch of up to 4
-    // chunks loads everything it needs before computing
-    constexpr int kB = 2;
-    if (pro.mode == PRO_QUANT) {   // one source: four chunks per batch
-        constexpr int kQ = 4;
-        for (int t = 0; t < T; ++t) {
-            const float* xr = pro.src + (size_t)t * pro.ld;
-            for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kQ) {
-                float va[kQ][8];
-#pragma unroll
-                for (int k = 0; k < kQ; ++k) {
-                    const int c = c0 + kConsumers * k;
-                    if (c < n_chunks) ld8(xr, c * 256 + 8 * lane, K, va[k]);
-                }
-#pragma unroll
-                for (int k = 0; k < kQ; ++k) {
-                    const int c = c0 + kConsumers * k;
-                    if (c < n_chunks) ximg_quant_chunk(va[k], lane, K, t, c, xi, wantk, want32);
-                }
-            }
-        }
-        return;
-    }
-    for (int t = 0; t < T; ++t) {
-        const float* xr = pro.src + (size_t)t * pro.ld;
-        const float* ur = pro.mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
-        for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kB) {
-            float va[kB][8], ua[kB][8];
-#pragma unroll
-            for (int k = 0; k < kB; ++k) {
-                const int c = c0 + kConsumers * k;
-                if (c < n_chunks) {
-                    const int i0 = c * 256 + 8 * lane;
-                    ld8(xr, i0, K, va[k]);
-                    if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kB; ++k) {
-                const int c = c0 + kConsumers * k;
-                if (c < n_chunks) {
-                    const int i0 = c * 256 + 8 * lane;
-                    float v[8];
-                    if (pro.mode == PRO_SILU) {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            v[i] = __fmul_rn(__fdiv_rn(va[k][i], __fadd_rn(1.0f, expf(-va[k][i]))), ua[k][i]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) v[i] = va[k][i];
-                    }
-                    ximg_quant_chunk(v, lane, K, t, c, xi, wantk, want32);
-                }
-            }
-        }
-    }
-}
-
 template <int NT>
 __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -624,25 +338,43 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     __shared__ int s_tseq;
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
-    const int T = args.T, K = args.K, G = jobs.n_groups, S = jobs.stages;
+    __shared__ unsigned long long s_best[kConsumers][4];
+    const int K = args.K, G = jobs.n_groups, S = jobs.stages;
     int n_tiles = jobs.tile0[0];
 #pragma unroll
     for (int i = 1; i <= kMaxSeg; ++i)
         if (i == args.nseg) n_tiles = jobs.tile0[i];
     // balanced split: units of one tile, or of a (gate, up) tile pair
     const int unit = jobs.pair ? 2 : 1;
-    const int t_begin = (int)((long long)blockIdx.x * jobs.n_units / gridDim.x) * unit;
-    const int t_end = min(n_tiles, (int)((long long)(blockIdx.x + 1) * jobs.n_units / gridDim.x) * unit);
-    const int n_stages = max(0, t_end - t_begin) * G;
+    JobView jv;
+    jv.seg = s_seg;
+    jv.tile0 = s_tile0;
+    jv.nseg = args.nseg;
+    jv.pair = jobs.pair;
+    jv.G = G;
+    jv.K = K;
+    jv.T = args.T;
+    jv.t_begin = (int)((long long)blockIdx.x * jobs.n_units / gridDim.x) * unit;
+    jv.t_end = min(n_tiles, (int)((long long)(blockIdx.x + 1) * jobs.n_units / gridDim.x) * unit);
+    const int n_stages = job_stages(jv);
     XImage xi;
     xi.base = smem + kHdrBytes;
     xi.n256 = (K + 255) / 256;
     xi.xk = jobs.xk_bytes;
     xi.x32 = jobs.x32_bytes;
-    xi.T = T;
-    float* part = reinterpret_cast<float*>(xi.base + (size_t)T * (jobs.xk_bytes + jobs.x32_bytes));
-    uint8_t* ring = reinterpret_cast<uint8_t*>(part) +
-                    (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128);
+    xi.T = args.T;
+    float* part = reinterpret_cast<float*>(xi.base + (size_t)args.T * (jobs.xk_bytes + jobs.x32_bytes));
+    RingView rg;
+    rg.base = reinterpret_cast<uint8_t*>(part) + (((size_t)jobs.tiles_per_cta * G * kTileRows * NT * 4 + 127) / 128 * 128);
+    rg.full = full;
+    rg.empty = empty;
+    rg.S = S;
+    rg.slot_bytes = jobs.slot_bytes;
+    rg.issued = s_issued;
+    rg.abort = s_abort;
+    rg.guard = 0;   // S is a multiple of the pairs and the job starts at ring stage 0
+    rg.pwait = nullptr;
+    rg.cwait = nullptr;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < kMaxSeg; ++i)
@@ -670,40 +402,11 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     if (warp == kConsumers) {   // producer
         if (lane == 0) {
             if (jobs.wait_first) pdl_wait();
-            int issued = 0;
-            bool ok = true;
-            for (int s = 0; s < n_stages; ++s) {
-                const int tile = t_begin + s / G, gi = s % G;
-                int sg, lt;
-                tile_seg(s_tile0, args.nseg, jobs.pair, tile, sg, lt);
-                const GemvSeg& g = s_seg[sg];
-                const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
-                const int nb = row_blocks(g.type, K);
-                const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
-                const int slot = ring_slot(s, S), phase = ring_phase(s, S);
-                if (phase > 0) {
-                    unsigned long long tw = 0;
-                    *s_prod_wait = s - S;
-                    if (!mbar_wait(&empty[slot], (uint32_t)((phase - 1) & 1), s_abort, &tw)) {
-                        record_wait_fail(1, s, slot, (phase - 1) & 1, n_stages, S, issued, tw, t_kernel, s - S, full,
-                                         empty, (int)dyn_smem);
-                        ok = false;
-                        break;
-                    }
-                    *s_prod_wait = -1;
-                }
-                const uint8_t* src = base + (size_t)lt * kTileRows * g.row_stride +
-                                     (size_t)kTileRows * group_offset(g.type, gi);
-                if (bytes <= (uint32_t)jobs.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, jobs.err)) {
-                    mbar_expect_tx(&full[slot], bytes);
-                    bulk_g2s(ring + (size_t)slot * jobs.slot_bytes, src, bytes, &full[slot]);
-                    *s_issued = s + 1;
-                } else {
-                    mbar_arrive(&full[slot]);   // keep the ring moving; the stage holds stale bytes
-                }
-                ++issued;
-            }
-            if (!ok) {
+            WaitFail wf{};
+            if (!produce_stages(rg, jv, 0, jobs.err, &wf)) {
+                const int issued = wf.stage;   // stages issued before the one that waited
+                record_wait_fail(1, wf.stage, wf.slot, wf.parity, n_stages, S, issued, wf.t0, t_kernel, wf.stage - S, full,
+                                 empty, (int)dyn_smem);
                 if (jobs.err) atomicExch(jobs.err, 1);
                 *s_abort = 1;
                 // let the copies in flight land before the CTA can exit
@@ -730,174 +433,22 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     build_ximage(args, xi, wantk, want32, s_part, wv, tr ? s_tseq : -1);
     consumers_sync();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
-    // pair q = warp / 2 takes stages q, q + 4, ...; warp half h of the pair
-    // rows 4h .. 4h+3 of the tile, lane = row * 8 + block
-    const int half = warp & 1, pq = warp >> 1;
-    const int r8 = 4 * half + (lane >> 3), bl = lane & 7;
-    bool ok = true;
-    int tile = t_begin + pq / G, gi = pq % G;   // stage pq; advanced incrementally below
-    int slot = pq % S, phase = pq / S;
-    for (int s = pq; s < n_stages; s += kPairs) {
-        int sgc, ltc;
-        tile_seg(s_tile0, args.nseg, jobs.pair, tile, sgc, ltc);
-        const int type = s_seg[sgc].type;
-        const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
-        const int piece = (int)group_bytes(type, gbk);
-        const uint8_t* pc = ring + (size_t)slot * jobs.slot_bytes + (size_t)r8 * piece;
-        {
-            unsigned long long tw = 0;
-            if (!mbar_wait(&full[slot], (uint32_t)(phase & 1), s_abort, &tw)) {
-                if (!*s_abort)
-                    record_wait_fail(2, s, slot, phase & 1, n_stages, S, *s_issued, tw, t_kernel, *s_prod_wait, full,
-                                     empty, (int)dyn_smem);
-                ok = false;
-                break;
-            }
-        }
-        if (tr && s == 0 && threadIdx.x == 0) trace_ev(TR_GEMV, EV_FIRST, s_tseq);
-        float c[NT];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) c[t] = 0.0f;
-        if (type == T_Q4_K) {
-            if (bl < gbk) {
-                uint4 w[9];
-#pragma unroll
-                for (int i = 0; i < 9; ++i) w[i] = *reinterpret_cast<const uint4*>(pc + bl * 144 + 16 * i);
-                const float dw = h2f((uint16_t)(w[0].x & 0xFFFFu)), dmw = h2f((uint16_t)(w[0].x >> 16));
-                const int kb = gi * 8 + bl;
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (t >= T) break;
-                    int si, mi;
-                    q4k_block<LdShared>(w, xi.qk(t, kb), *reinterpret_cast<const uint4*>(xi.bsk(t, kb)), si, mi);
-                    c[t] = q4k_term(dw, dmw, *xi.dk(t, kb), si, mi);
-                }
-            }
-        } else if (type == T_Q6_K) {
-            if (bl < gbk) {
-                uint4 w[13];
-#pragma unroll
-                for (int i = 0; i < 13; ++i) w[i] = *reinterpret_cast<const uint4*>(pc + bl * 208 + 16 * i);
-                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 208 + 2 * bl));
-                const int kb = gi * 8 + bl;
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (t >= T) break;
-                    const int si = q6k_block<LdShared>(w, xi.qk(t, kb), xi.s16(t, kb));
-                    c[t] = scaled_term(dw, *xi.dk(t, kb), si);
-                }
-            }
-        } else {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group, in block order
-            const int kc = gi * 8 + bl;
-            for (int i = 0; i < 8; ++i) {
-                const int b = 8 * bl + i;
-                if (b >= gbk) break;
-                const uint4 w0 = *reinterpret_cast<const uint4*>(pc + 32 * b);
-                const uint4 w1 = *reinterpret_cast<const uint4*>(pc + 32 * b + 16);
-                const float dw = h2f(*reinterpret_cast<const uint16_t*>(pc + gbk * 32 + 2 * b));
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (t >= T) break;
-                    const int sv = q80_block<LdShared>(w0, w1, xi.q32(t, kc) + 32 * i);
-                    c[t] = __fadd_rn(c[t], scaled_term(dw, xi.d32(t, kc)[i], sv));
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 1);
-            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 2);
-            c[t] += __shfl_xor_sync(0xffffffffu, c[t], 4);
-        }
-        if (bl == 0) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t) part[((size_t)s * kTileRows + r8) * NT + t] = c[t];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        // next stage of this pair: s + 4
-        gi += kPairs;
-        while (gi >= G) {
-            gi -= G;
-            ++tile;
-        }
-        slot += kPairs;
-        if (slot >= S) {
-            slot -= S;
-            ++phase;
-        }
-    }
-    if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_LOOP, s_tseq);
+    WaitFail wf{};
+    const bool ok = consume_stages<NT>(rg, jv, 0, xi, part, &wf, tr ? s_tseq : -1);
     if (!ok) {
+        if (!*s_abort)
+            record_wait_fail(2, wf.stage, wf.slot, wf.parity, n_stages, S, *s_issued, wf.t0, t_kernel, *s_prod_wait, full,
+                             empty, (int)dyn_smem);
         if (jobs.err && lane == 0) atomicExch(jobs.err, 2);
         *s_abort = 1;
     }
+    if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_LOOP, s_tseq);
     consumers_sync();
     if (*s_abort) return;
-    // rows of this CTA: sum the group partials in group order
-    unsigned long long best[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) best[t] = 0ull;
-    const int n_rows = (t_end - t_begin) * kTileRows;
-    if (jobs.pair) {
-        // tiles (2j, 2j+1) are (gate, up) tile j: h = silu(g) * u into segment 0's y
-        const GemvSeg& g0 = s_seg[0];
-        for (int idx = threadIdx.x; idx < n_rows / 2; idx += kConsumers * 32) {
-            const int tp = idx / kTileRows, rr = idx % kTileRows;
-            const int tl = 2 * tp, row = ((t_begin + tl) >> 1) * kTileRows + rr;
-            if (row >= g0.rows) continue;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t >= T) break;
-                float gv = 0.0f, uv = 0.0f;
-                for (int gi = 0; gi < G; ++gi) {
-                    gv += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
-                    uv += part[((size_t)((tl + 1) * G + gi) * kTileRows + rr) * NT + t];
-                }
-                g0.y[(size_t)t * g0.ldy + row] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
-            }
-        }
-    }
-    for (int idx = jobs.pair ? n_rows : threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
-        const int tl = idx / kTileRows, rr = idx % kTileRows, tile = t_begin + tl;
-        const int sg = seg_index(s_tile0, args.nseg, tile);
-        const GemvSeg& g = s_seg[sg];
-        const int row = (tile - s_tile0[sg]) * kTileRows + rr;
-        if (row >= g.rows) continue;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t >= T) break;
-            float v = 0.0f;
-            for (int gi = 0; gi < G; ++gi) v += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
-            v = store_out(g, row, t, v);
-            if (g.amax) {
-                const unsigned long long key = argmax_key(v, row);
-                best[t] = key > best[t] ? key : best[t];
-            }
-        }
-    }
+    reduce_rows<NT>(jv, part, s_best);
     if (tr) {
         consumers_sync();
         if (threadIdx.x == 0) trace_ev(TR_GEMV, EV_END, s_tseq);
-    }
-    if (s_seg[0].amax) {   // one segment (the output projection): merge the CTA's keys, one atomic per token
-        __shared__ unsigned long long s_best[kConsumers][4];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            unsigned long long k = best[t];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
-                k = ok > k ? ok : k;
-            }
-            if (lane == 0) s_best[warp][t] = k;
-        }
-        consumers_sync();
-        if (threadIdx.x < T) {
-            unsigned long long k = 0ull;
-            for (int w = 0; w < kConsumers; ++w) k = s_best[w][threadIdx.x] > k ? s_best[w][threadIdx.x] : k;
-            if (k) atomicMax(&s_seg[0].amax[threadIdx.x], k);
-        }
     }
 }
 }  // namespace fb

@@ -44,7 +44,10 @@ constexpr int kMaxSeg = 4;
 //   PRO_NORM   RMSNorm of f32 rows src (weights w, eps), then quantised
 //   PRO_QUANT  f32 rows src, quantised
 //   PRO_SILU   silu(src) * src2, quantised
-enum : int { PRO_ACT = 0, PRO_NORM = 1, PRO_QUANT = 2, PRO_SILU = 3 };
+//   PRO_MERGE  one token's decode-attention partials of ld key chunks (head
+//              dim ld2; acc [C][H][D] then (m, l) [C][H][2] at src), merged
+//              and quantised (persistent decode step)
+enum : int { PRO_ACT = 0, PRO_NORM = 1, PRO_QUANT = 2, PRO_SILU = 3, PRO_MERGE = 4 };
 struct GemvPro {
     int mode;
     const float* src;
@@ -161,4 +164,67 @@ int fbk_argmax_from_keys(unsigned long long* keys, int T, int32_t* out, cudaStre
 int fbk_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out, int32_t* step,
                          cudaStream_t st);
 int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel, cudaStream_t st);
+}
+
+// ---------------------------------------------------------------- persistent decode step (step.cu)
+namespace fb {
+// One GEMV phase of the step program: the same job the streamed GEMV kernel
+// runs (segments, prologue, epilogue; T = 1), with its tile split.
+struct StepPhase {
+    GemvArgs a;
+    int tile0[kMaxSeg + 1];   // 8-row tiles per segment (prefix sums; pair mode interleaves)
+    int n_units;              // tiles, or (gate, up) tile pairs
+    int G;                    // 2048-value groups per row
+    int xk_bytes, x32_bytes;  // activation image layouts the segments need
+    int attn_layer;           // >= 0: that layer's attention runs before this phase
+};
+// Control block in device memory (zeroed before each launch).
+struct StepCtl {
+    unsigned int bar;         // grid-barrier arrivals, monotonic
+    int abort;                // set by the first CTA that gives up
+    int err;                  // first error: 1 ring wait, 2 grid barrier, 3 weight range, 4 token id, 5 page index
+    int info[5];              // CTA, step, phase, stage, slot of the first failure
+};
+struct StepArgs {
+    const StepPhase* ph;      // [n_ph]: per layer qkv, o, gate+up, down; then the output projection
+    int n_ph;
+    // attention
+    const float *q, *k, *v;   // raw projections of the token (written by the qkv phase)
+    float* att_part;          // partials: acc [C][H][D], then (m, l) [C][H][2]
+    const float *rcos, *rsin; // RoPE table [n_ctx][rot/2]
+    int H, HKV, D, rot, neox;
+    float scale;
+    int max_chunks;           // key chunks per kv head at most (HKV * max_chunks <= grid)
+    KvView kv;
+    int sid;                  // sequence slot (page-table row)
+    // embedding and residual stream
+    int emb_type;
+    const uint8_t* emb;
+    int E, emb_rows;
+    float* x;
+    // token state
+    const int32_t* ids;       // ids[0]: first token
+    const int32_t* tok_pos;   // tok_pos[0]: its position
+    int32_t* out;             // [n_steps] greedy tokens (argmax of each step)
+    int n_steps;
+    unsigned long long* keys; // [2] argmax keys of even / odd steps (zeroed before launch)
+    StepCtl* ctl;
+    int S, slot_bytes, union_bytes;
+    // optional phase trace (nullable): thread 0 of the first and the last CTA
+    // store %globaltimer at each phase boundary into
+    // trace[(step * kStepTraceEvents + event) * 2 + (last CTA ? 1 : 0)]
+    unsigned long long* trace;
+};
+constexpr int kStepTraceEvents = 1024;
+}  // namespace fb
+
+extern "C" {
+// Launch shape of the step kernel (G = q heads per kv head, f16 = fp16 KV
+// cache) for a ring slot size and a union area
+// (activation image + partials, or attention scratch): CTAs (1 per SM), ring
+// slots, dynamic shared memory. Returns 0, or a CUDA error / -1 when it does
+// not fit.
+int fbk_step_plan(int G, int f16, int slot_bytes, int union_bytes, int* grid, int* stages, size_t* smem);
+// Cooperative launch of n_steps greedy decode steps.
+int fbk_step_decode(const fb::StepArgs* a, int grid, size_t smem, cudaStream_t st);
 }

@@ -39,12 +39,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: false after kWaitNs or once another thread raised *abort.
 // The clock is read only once the first try has failed; t_start (optional)
 // receives that time when the wait gives up.
+// waited (optional) accumulates the ns spent when the first try failed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          unsigned long long* t_start = nullptr) {
+                                          unsigned long long* t_start = nullptr, unsigned long long* waited = nullptr) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
     for (unsigned i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity)) {
+            if (waited) *waited += gtimer() - t0;
+            return true;
+        }
         if ((i & 63) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) {
             if (t_start) *t_start = t0;
             return false;

@@ -214,7 +214,10 @@ FISH_API const char* fish_profile_decode_json(fish_ctx* ctx, int32_t first, int 
  * records (globaltimer ns, kernel tag, event, launch number) into out
  * (4 values per record, at most cap records). Tags: 1 GEMV, 2 attention,
  * 3 embedding, 4 argmax/greedy. Events: 0 start, 1 dependency wait passed,
- * 2 operands ready, 3 end. Returns the number of records, or < 0. */
+ * 2 operands ready, 3 end. When the persistent step kernel runs the decode,
+ * records are (ns, tag 5, phase-boundary index, step * 2 + c) for thread 0 of
+ * the first (c = 0) and the last (c = 1) CTA. Returns the number of records,
+ * or < 0. */
 FISH_API int fish_trace_decode(fish_ctx* ctx, int32_t first, int n_steps, uint64_t* out, int cap);
 
 #ifdef __cplusplus

@@ -275,3 +275,59 @@ def test_decode_batch_equals_single_decodes(gpu, tiny_gguf):
             assert np.array_equal(lg1[0], lg[i])
             assert am1[0] == am[i]
             m.session_close(t)
+
+
+@pytest.mark.parametrize("kv_f32", [0, 1])
+def test_persistent_step_matches_graph_path(gpu, synth_dir, monkeypatch, kv_f32):
+    """The persistent decode kernel (k_step) against the graph path on one
+    8B-shaped model (2 layers). Both run the same GEMV jobs (identical rows,
+    one RMSNorm summation order); attention is split and merged differently
+    (key chunks merged by the o projection's prologue), and on this model a
+    1-ulp difference in the attention output re-quantises to a different
+    int8 activation now and then, which the random-init residual stream
+    amplifies (two CPU engines differ by up to 2.2% of max |logit| here, see
+    test_llama8b_shape_two_layers_vs_oracle). Bar: max |dlogit| <= 3% of max
+    |logit|, median <= 0.03, argmax equal where the margin clears the bar.
+    Exact: greedy ids of one launch running 8 steps equal those of 8
+    single-token launches of the same kernel (device-side token feedback and
+    K/V appends). The 300-id prompt puts positions past one 64-key chunk, so
+    the partial merge runs."""
+    import json
+    from imurun_b200 import synth
+    from imurun_b200.native import Model
+    path = synth.cached(synth.preset("llama8b", layers=2), synth_dir)
+    if kv_f32:
+        monkeypatch.setenv("FISH_KV_F32", "1")
+    ids = np.random.default_rng(31).integers(3, 128256, 306).astype(np.int32)
+    res = {}
+    for persist in (1, 0):
+        if persist:
+            monkeypatch.setenv("FISH_PERSIST", "1")
+        else:
+            monkeypatch.delenv("FISH_PERSIST", raising=False)
+        with Model(path, 1024) as m:
+            m.prefill(ids[:300], 0)
+            steps = [m.decode(ids[s:s + 1], s)[0][0].copy() for s in range(300, 306)]
+            info = json.loads(m.lib.fish_engine_json(m.ctx).decode())
+            extra = None
+            if persist:
+                m.set_kv_len(303)
+                greedy = m.greedy(int(ids[303]), 8)          # one launch, 8 steps
+                m.set_kv_len(303)
+                tok, one_by_one = int(ids[303]), []
+                for s in range(8):                           # 8 launches, 1 step each
+                    _, am = m.decode(np.array([tok], np.int32), 303 + s)
+                    tok = int(am[0])
+                    one_by_one.append(tok)
+                extra = (greedy, np.array(one_by_one, np.int32))
+        res[persist] = (steps, info, extra)
+    assert res[1][1]["step_kernel"] == 1, res[1][1].get("step_unavailable")
+    assert res[0][1]["step_kernel"] == 0
+    for i, (a, b) in enumerate(zip(res[1][0], res[0][0])):
+        d = np.abs(a - b)
+        assert d.max() <= 0.03 * np.abs(b).max(), (i, float(d.max()), float(np.abs(b).max()))
+        assert np.median(d) <= 0.03, (i, float(np.median(d)))
+        if _margin(b) > 2 * (1e-2 + 1e-3 * np.abs(b).max()):
+            assert int(np.argmax(a)) == int(np.argmax(b)), i
+    greedy, one_by_one = res[1][2]
+    assert np.array_equal(greedy, one_by_one)
