@@ -28,7 +28,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hi
           f"-I{ROOT / 'include'}", f"-I{CSRC}"]
 
 SOURCES = [
-    "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu",
+    "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu", "kernels/gemm.cu",
     "gguf.cpp", "tokenizer.cpp", "sampler.cpp", "engine.cpp", "c_api.cpp", "kernel_api.cpp",
     "attention_static.cu",
 ]

@@ -702,8 +702,23 @@ bool Engine::fusable(const DevW* const* ws, int n, int T) const {
 
 bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
                         const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro, bool swiglu) {
-    for (int t0 = 0; t0 < T; t0 += 8) {
-        const int nt = std::min(8, T - t0);
+    // T >= 16 tokens with quantised planes: one tensor-core launch per
+    // segment; otherwise GEMV launches of up to 8 tokens
+    int chunk = 8;
+    if (T >= 16 && !pro && !swiglu) {
+        GemvArgs p{};
+        p.nseg = n;
+        p.K = ws[0]->n_in;
+        p.T = T;
+        p.act = a;
+        for (int i = 0; i < n; ++i) {
+            p.seg[i].type = ws[i]->type;
+            p.seg[i].rows = ws[i]->n_out;
+        }
+        if (fbk_gemm_eligible(&p)) chunk = T;
+    }
+    for (int t0 = 0; t0 < T; t0 += chunk) {
+        const int nt = std::min(chunk, T - t0);
         GemvArgs g{};
         g.nseg = n;
         g.K = ws[0]->n_in;
@@ -725,15 +740,27 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
             s.epi = epi;
             bytes += gemv_bytes(*ws[i], nt);
         }
-        CKP(PC_GEMV, bytes, fbk_gemv(&g, stream_));
+        if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, bytes, fbk_gemm(&g, stream_));
+        else CKP(PC_GEMV, bytes, fbk_gemv(&g, stream_));
     }
     return true;
 }
 
 bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi, const float* xf,
                   int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro, unsigned long long* keys) {
-    for (int t0 = 0; t0 < T; t0 += 8) {
-        const int nt = std::min(8, T - t0);
+    int chunk = 8;
+    if (T >= 16 && !pro && !expert && !keys) {
+        GemvArgs p{};
+        p.nseg = 1;
+        p.K = w.n_in;
+        p.T = T;
+        p.act = a;
+        p.seg[0].type = w.type;
+        p.seg[0].rows = w.n_out;
+        if (fbk_gemm_eligible(&p)) chunk = T;
+    }
+    for (int t0 = 0; t0 < T; t0 += chunk) {
+        const int nt = std::min(chunk, T - t0);
         GemvArgs g{};
         g.nseg = 1;
         g.K = w.n_in;
@@ -755,7 +782,8 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         s.expert = expert;
         s.expert_bytes = w.expert_bytes;
         s.amax = keys ? keys + t0 : nullptr;
-        CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
+        if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemm(&g, stream_));
+        else CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
     }
     return true;
 }

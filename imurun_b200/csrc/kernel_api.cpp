@@ -145,11 +145,24 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
     TRY(cudaMemcpy(dx.p, x, sizeof(float) * T * n_in, cudaMemcpyHostToDevice));
     const bool quant = type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K;
     if (quant) TRY(fbk_quantize_rows(dx.as<float>(), n_in, T, n_in, &da.a, type == T_Q8_0, type != T_Q8_0, nullptr));
-    for (int t0 = 0; t0 < T; t0 += 8) {
+    // T >= 16 quantised rows go to the tensor-core kernel in one launch,
+    // otherwise GEMV launches of up to 8 tokens
+    int step = 8;
+    {
+        GemvArgs probe{};
+        probe.nseg = 1;
+        probe.K = n_in;
+        probe.T = T;
+        probe.act = da.a;
+        probe.seg[0].type = type;
+        probe.seg[0].rows = n_out;
+        if (fbk_gemm_eligible(&probe)) step = T;
+    }
+    for (int t0 = 0; t0 < T; t0 += step) {
         GemvArgs g{};
         g.nseg = 1;
         g.K = n_in;
-        g.T = T - t0 < 8 ? T - t0 : 8;
+        g.T = T - t0 < step ? T - t0 : step;
         g.act = da.a;
         g.act.q32 = da.a.q32 + (size_t)t0 * da.a.ld;
         g.act.qk = da.a.qk + (size_t)t0 * da.a.ld;
@@ -167,7 +180,8 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
         g.seg[0].y = dy.as<float>() + (size_t)t0 * n_out;
         g.seg[0].ldy = n_out;
         g.seg[0].epi = EPI_STORE;
-        TRY(fbk_gemv(&g, nullptr));
+        if (fbk_gemm_eligible(&g)) TRY(fbk_gemm(&g, nullptr));
+        else TRY(fbk_gemv(&g, nullptr));
     }
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(y, dy.p, sizeof(float) * T * n_out, cudaMemcpyDeviceToHost));

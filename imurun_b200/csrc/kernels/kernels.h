@@ -81,6 +81,12 @@ int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T,
 int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                        const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);
+// Batched products on the int8 tensor cores (gemm.cu): T >= 16 tokens,
+// quantised planes already built (PRO_ACT), Q4_K / Q6_K / Q8_0 segments,
+// K % 256 == 0. fbk_gemm_eligible says whether a job qualifies
+// (FISH_NO_GEMM turns the path off).
+int fbk_gemm_eligible(const fb::GemvArgs* args);
+int fbk_gemm(const fb::GemvArgs* args, cudaStream_t st);
 // 1 if fbk_gemv runs this call on the streamed kernel (the only one that
 // takes a prologue other than PRO_ACT).
 int fbk_gemv_streamable(const fb::GemvArgs* args);

@@ -84,6 +84,7 @@ __device__ __forceinline__ bool grid_sync(const StepArgs& A, unsigned& target, v
             unsigned v;
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&A.ctl->bar) : "memory");
             if ((int)(v - target) >= 0) break;
+            __nanosleep(32);
             if ((i & 255) == 0) {
                 if (*reinterpret_cast<volatile int*>(&A.ctl->abort)) {
                     *s_abort = 1;

@@ -476,6 +476,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
         if (rg.guard && ld_acquire_smem(rg.issued) <= gbase + l) {
             const unsigned long long t0 = gtimer();
             for (unsigned i = 1; ld_acquire_smem(rg.issued) <= gbase + l; ++i) {
+                __nanosleep(64);
                 if ((i & 63) == 0 && (*rg.abort || (long long)(gtimer() - t0) > kWaitNs)) {
                     wf->stage = gbase + l;
                     wf->slot = slot;
@@ -601,6 +602,7 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
         if (rg.guard && ld_acquire_smem(rg.issued) <= gbase + l) {
             const unsigned long long t0 = gtimer();
             for (unsigned i = 1; ld_acquire_smem(rg.issued) <= gbase + l; ++i) {
+                __nanosleep(64);
                 if ((i & 63) == 0 && (*rg.abort || (long long)(gtimer() - t0) > kWaitNs)) {
                     wf->stage = gbase + l;
                     wf->slot = slot;

@@ -36,6 +36,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread is parked (not spinning, so it
+// takes no issue slots from the warps that do work) until the phase completes
+// or about kSuspendNs pass.
+constexpr uint32_t kSuspendNs = 2000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait: false after kWaitNs or once another thread raised *abort.
 // The clock is read only once the first try has failed; t_start (optional)
 // receives that time when the wait gives up.
@@ -45,11 +58,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
     for (unsigned i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) {
+        if (mbar_try_wait_sleep(bar, parity)) {
             if (waited) *waited += gtimer() - t0;
             return true;
         }
-        if ((i & 63) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) {
+        if ((i & 7) == 0 && (*abort || (long long)(gtimer() - t0) > kWaitNs)) {
             if (t_start) *t_start = t0;
             return false;
         }
@@ -59,8 +72,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     const unsigned long long t0 = gtimer();
     for (unsigned i = 0;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 63 && (long long)(gtimer() - t0) > kWaitNs) return false;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if ((i & 7) == 7 && (long long)(gtimer() - t0) > kWaitNs) return false;
     }
 }
 // One bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0),
