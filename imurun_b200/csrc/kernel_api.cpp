@@ -189,7 +189,7 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
 }
 
 int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch, double* bytes_per_launch) {
-    if (!ms_per_launch || n_in <= 0 || n_out <= 0 || T <= 0 || T > 8 || iters <= 0) return -1;
+    if (!ms_per_launch || n_in <= 0 || n_out <= 0 || T <= 0 || T > kMaxBatch || iters <= 0) return -1;
     if (type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K && type != T_F32 && type != T_F16) return -1;
     TRY(check_device());
     const size_t stride = dev_row_bytes(type, n_in);
@@ -201,7 +201,7 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     TRY(cudaMemset(dw.p, 0x11, mat * copies));
     TRY(dx.alloc(sizeof(float) * T * n_in));
     TRY(dy.alloc(sizeof(float) * T * n_out));
-    TRY(da.make(8, n_in));
+    TRY(da.make(T, n_in));   // planes for all T rows (the quantiser writes T rows)
     std::vector<float> hx((size_t)T * n_in);
     for (size_t i = 0; i < hx.size(); ++i) hx[i] = (float)((i * 2654435761u) % 1000) / 500.0f - 1.0f;
     TRY(cudaMemcpy(dx.p, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice));
@@ -230,7 +230,7 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     for (int i = 0; i < 3 + iters && !rc; ++i) {
         if (i == 3) cudaEventRecord(e0, st);
         g.seg[0].w = dw.as<uint8_t>() + (size_t)(i % copies) * mat;
-        rc = fbk_gemv(&g, st);
+        rc = fbk_gemm_eligible(&g) ? fbk_gemm(&g, st) : fbk_gemv(&g, st);
     }
     cudaEventRecord(e1, st);
     const int sync = (int)cudaStreamSynchronize(st);

@@ -2,13 +2,17 @@
 
     python -m imurun_b200.timing matmul --type 12 --n-in 4096 --n-out 14336 [--tokens 1] [--iters 20]
     python -m imurun_b200.timing attention --pos 575 [--heads 32 --kv-heads 8 --dim 128 --calls 3]
+    python -m imurun_b200.timing prefill --tokens 512 [--layers 32]
 
 Runs fbx_time_matmul: 3 warm-up launches, then `iters` launches timed with
 CUDA events, each launch reading a different copy of the weights (>= 512 MB
 of copies, so every launch streams from HBM). Prints one JSON line with the
 mean launch time, the algorithmic bytes of a launch and their ratio. Also
 the command used for profiler captures of one GEMV launch (`-s 3 -c 1`).
-`attention` runs the fused decode-attention kernel (fp16 cache, one
+`prefill` prefills `tokens` random ids into the seeded Llama-3-8B-shaped
+Q4_K_M GGUF (synthesised and cached under $FISH_SYNTH_DIR, default
+/tmp/fish_synth; `--layers` truncates it) after a 64-token warm-up, and prints
+the wall time and tok/s. `attention` runs the fused decode-attention kernel (fp16 cache, one
 token at position pos) `calls` times through fbx_attention_decode — the small
 case for profiler captures of that kernel.
 """
@@ -31,7 +35,8 @@ def time_matmul(lib, type_id: int, n_in: int, n_out: int, tokens: int = 1, iters
     us = float(ms[0]) * 1e3
     return {"type": type_id, "n_in": n_in, "n_out": n_out, "tokens": tokens, "iters": iters,
             "us_per_launch": round(us, 3), "bytes_per_launch": float(nbytes[0]),
-            "gb_s": round(float(nbytes[0]) / (us * 1e-6) / 1e9, 1)}
+            "gb_s": round(float(nbytes[0]) / (us * 1e-6) / 1e9, 1),
+            "tops": round(2.0 * n_in * n_out * tokens / (us * 1e-6) / 1e12, 2)}
 
 
 def attention(lib, pos: int, heads: int, kv_heads: int, dim: int, calls: int) -> dict:
@@ -51,6 +56,22 @@ def attention(lib, pos: int, heads: int, kv_heads: int, dim: int, calls: int) ->
             "out_absmax": float(np.abs(out).max())}
 
 
+def prefill(tokens: int, layers: int) -> dict:
+    import os
+    import time
+    from . import synth
+    from .native import Model
+    cfg = synth.preset("llama8b") if layers == 32 else synth.preset("llama8b", layers=layers)
+    path = synth.cached(cfg, os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    ids = np.random.default_rng(1).integers(3, 128256, tokens).astype(np.int32)
+    with Model(path, max(1024, tokens + 64)) as m:
+        m.prefill(ids[:64], 0)
+        t0 = time.perf_counter()
+        m.prefill(ids, 0)
+        dt = time.perf_counter() - t0
+    return {"tokens": tokens, "layers": layers, "seconds": round(dt, 5), "tok_s": round(tokens / dt, 1)}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -66,7 +87,13 @@ def main() -> None:
     at.add_argument("--kv-heads", type=int, default=8)
     at.add_argument("--dim", type=int, default=128)
     at.add_argument("--calls", type=int, default=3)
+    pf = sub.add_parser("prefill")
+    pf.add_argument("--tokens", type=int, default=512)
+    pf.add_argument("--layers", type=int, default=32)
     a = ap.parse_args()
+    if a.cmd == "prefill":
+        print(json.dumps(prefill(a.tokens, a.layers)), flush=True)
+        return
     lib = native.load_library()
     if a.cmd == "matmul":
         print(json.dumps(time_matmul(lib, a.type, a.n_in, a.n_out, a.tokens, a.iters)), flush=True)

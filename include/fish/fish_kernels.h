@@ -70,7 +70,9 @@ FISH_API int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_
                       int pos0);
 
 /* Device time of the matmul kernel alone: `iters` back-to-back launches of
- * y = W x for T tokens, timed with CUDA events on the launching stream after
+ * y = W x for T <= 256 tokens (the GEMV kernels up to 15 tokens, the int8
+ * tensor-core kernel from 16 for quantised rows), timed with CUDA events on
+ * the launching stream after
  * 3 warm-up launches. W is filled with a constant byte pattern and replicated
  * into enough copies (>= 512 MB) that consecutive launches read different
  * copies, so every launch streams its weights from HBM, not L2. Writes the
