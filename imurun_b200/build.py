@@ -67,7 +67,7 @@ def build_fish(jobs: int = 8, verbose: bool = False) -> Path:
     objs = [str(_obj(s)) for s in SOURCES]
     newest = max(Path(o).stat().st_mtime for o in objs)
     if not out.exists() or out.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(out), *objs, "-lpthread"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(out), *objs, "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -41,6 +41,8 @@ struct fish_ctx {
     std::string model_path;
     int n_ctx_req = 0;
     std::vector<float> logits;
+    int tp_rank = 0, tp_world = 1;       // set by fish_tp_init for the next fish_load
+    unsigned char tp_id[128] = {};
 };
 
 namespace {
@@ -126,6 +128,12 @@ int load_locked(fish_ctx* ctx, const char* path, int n_ctx) {
     ctx->tok.reset();
     auto eng = std::make_unique<fb::Engine>();
     std::string err;
+    if (ctx->tp_world > 1) {   // the group id is used once: a reload needs a new fish_tp_init
+        const bool ok = eng->set_tp(ctx->tp_rank, ctx->tp_world, ctx->tp_id, &err);
+        ctx->tp_world = 1;
+        ctx->tp_rank = 0;
+        if (!ok) { ctx->err = err; return -2; }
+    }
     if (!eng->load(path, n_ctx > 0 ? n_ctx : 4096, &err)) { ctx->err = err; return -2; }
     auto tok = fb::Tokenizer::create(eng->gguf(), &err);
     if (!tok) { ctx->err = err; return -3; }
@@ -315,9 +323,9 @@ int fish_model_info_of(fish_ctx* ctx, fish_model_info* out) {
     std::snprintf(out->arch, sizeof(out->arch), "%s", c.arch.c_str());
     out->n_layers = c.n_layers;
     out->n_embd = c.n_embd;
-    out->n_ff = c.n_ff;
-    out->n_head = c.n_head;
-    out->n_head_kv = c.n_head_kv;
+    out->n_ff = c.n_ff_model;   // the model's own shape, also under tensor parallelism
+    out->n_head = c.n_head_model;
+    out->n_head_kv = c.n_head_kv_model;
     out->head_dim = c.head_dim;
     out->n_ctx = c.n_ctx;
     out->vocab = c.vocab;
@@ -548,6 +556,25 @@ int fish_decode_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0, float* l
     std::string err;
     if (!e.forward(0, ids, n, ctx->logits.data(), logits_all, argmax_out, &err)) { ctx->err = err; return -2; }
     ctx->cache_ids.insert(ctx->cache_ids.end(), ids, ids + n);
+    return 0;
+}
+
+int fish_tp_unique_id(void* out, int cap) {
+    if (!out || cap < (int)sizeof(ncclUniqueId)) return (int)sizeof(ncclUniqueId);
+    const fb::NcclApi* nc = fb::nccl_api(nullptr);
+    ncclUniqueId id;
+    if (!nc || nc->get_unique_id(&id) != ncclSuccess) return -1;
+    std::memcpy(out, &id, sizeof(id));
+    return (int)sizeof(id);
+}
+
+int fish_tp_init(fish_ctx* ctx, int rank, int world, const void* id, int id_bytes) {
+    if (!ctx || world < 1 || rank < 0 || rank >= world) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (world > 1 && (!id || id_bytes != (int)sizeof(ncclUniqueId))) { ctx->err = "tensor parallelism: bad group id"; return -1; }
+    ctx->tp_rank = rank;
+    ctx->tp_world = world;
+    if (world > 1) std::memcpy(ctx->tp_id, id, sizeof(ncclUniqueId));
     return 0;
 }
 

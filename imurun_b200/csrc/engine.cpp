@@ -1,5 +1,9 @@
 // engine.cpp — see engine.h.
 #include "engine.h"
+
+#include <dlfcn.h>
+#include <mutex>
+#include <nccl.h>
 #include "kernels/layout.cuh"
 #include "kernels/stream_common.cuh"
 
@@ -139,6 +143,8 @@ Engine::~Engine() {
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
     cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
+    cudaFree(tp_tmp_); cudaFree(tp_logits_);
+    if (nccl_) nccl_api(nullptr)->comm_destroy((ncclComm_t)nccl_);   // after the graphs that hold its calls
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
@@ -248,6 +254,27 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         if (err) *err = "attention shape not supported by the B200 kernels (head_dim 64 or 128, <= 8 q heads per kv head)";
         return false;
     }
+    c.n_head_model = c.n_head;
+    c.n_head_kv_model = c.n_head_kv;
+    c.n_ff_model = c.n_ff;
+    c.out_rows = c.vocab;
+    c.out_row0 = 0;
+    if (tp_world_ > 1) {   // this rank's heads, FFN rows and vocab rows
+        const int N = tp_world_;
+        if (c.n_experts > 0) {
+            if (err) *err = "tensor parallelism: dense models only (experts are not split across ranks yet)";
+            return false;
+        }
+        if (c.n_head_kv % N || c.n_ff % N || c.vocab % N || (c.vocab / N) % 8) {
+            if (err) *err = "tensor parallelism: kv heads, FFN rows and vocab rows must split evenly over the ranks";
+            return false;
+        }
+        c.n_head /= N;
+        c.n_head_kv /= N;
+        c.n_ff /= N;
+        c.out_rows = c.vocab / N;
+        c.out_row0 = tp_rank_ * c.out_rows;
+    }
     {
         const std::string type = g.str(key("rope.scaling.type"), "none");
         const float factor = (float)g.f64(key("rope.scaling.factor"), 1.0);
@@ -275,6 +302,8 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         w.n_in = (int)t->ne[0];
         w.n_out = t->ne.size() > 1 ? (int)t->ne[1] : 1;
         w.n_exp = t->ne.size() > 2 ? (int)t->ne[2] : 1;
+        w.n_in_src = w.n_in;
+        w.n_out_src = w.n_out;
         w.stride = dev_row_bytes(t->type, w.n_in);
         w.expert_bytes = dev_matrix_bytes(t->type, w.n_in, w.n_out);
         if (t->type == T_Q4_K || t->type == T_Q6_K) {
@@ -282,9 +311,29 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         }
         return true;
     };
+    // tensor-parallel shards: a row range, or a range of input values (whole
+    // blocks, so a shard's block integers are the unsharded ones)
+    auto shard_rows = [&](DevW& w, int n, int row0) {
+        w.n_out = n;
+        w.row0 = row0;
+        w.expert_bytes = dev_matrix_bytes(w.type, w.n_in, w.n_out);
+    };
+    auto shard_k = [&](DevW& w, int n, int k0, const std::string& name) -> bool {
+        const int blk = w.type == T_Q8_0 ? 32 : (w.type == T_Q4_K || w.type == T_Q6_K ? 256 : 8);
+        if (k0 % blk || n % blk) {
+            if (err) *err = "tensor parallelism: input slice of " + name + " is not block-aligned";
+            return false;
+        }
+        w.n_in = n;
+        w.k0 = k0;
+        w.stride = dev_row_bytes(w.type, w.n_in);
+        w.expert_bytes = dev_matrix_bytes(w.type, w.n_in, w.n_out);
+        return true;
+    };
     if (!bind("token_embd.weight", embd_, true)) return false;
     if (!bind("output.weight", out_w_, false)) return false;
     if (out_w_.type < 0) { out_w_ = embd_; c.tied_output = true; }
+    else if (tp_world_ > 1) shard_rows(out_w_, c.out_rows, c.out_row0);
     layers_.resize(c.n_layers);
     for (int i = 0; i < c.n_layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
@@ -292,6 +341,13 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         if (!bind(p + "attn_q.weight", L.wq, true) || !bind(p + "attn_k.weight", L.wk, true) ||
             !bind(p + "attn_v.weight", L.wv, true) || !bind(p + "attn_output.weight", L.wo, true))
             return false;
+        if (tp_world_ > 1) {
+            const int Q = c.q_dim(), KV = c.kv_dim(), r = tp_rank_;
+            shard_rows(L.wq, Q, r * Q);
+            shard_rows(L.wk, KV, r * KV);
+            shard_rows(L.wv, KV, r * KV);
+            if (!shard_k(L.wo, Q, r * Q, p + "attn_output.weight")) return false;
+        }
         if (c.n_experts > 0) {
             if (!bind(p + "ffn_gate_inp.weight", L.gate_inp, true) || !bind(p + "ffn_gate_exps.weight", L.gate_exps, true) ||
                 !bind(p + "ffn_up_exps.weight", L.up_exps, true) || !bind(p + "ffn_down_exps.weight", L.down_exps, true))
@@ -301,6 +357,12 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
             if (!bind(p + "ffn_gate.weight", L.wg, true) || !bind(p + "ffn_up.weight", L.wu, true) ||
                 !bind(p + "ffn_down.weight", L.wd, true))
                 return false;
+            if (tp_world_ > 1) {
+                const int F = c.n_ff, r = tp_rank_;
+                shard_rows(L.wg, F, r * F);
+                shard_rows(L.wu, F, r * F);
+                if (!shard_k(L.wd, F, r * F, p + "ffn_down.weight")) return false;
+            }
         }
     }
     // activation layouts each consumer needs
@@ -326,7 +388,8 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     load_seconds_upload = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 
     // small vectors
-    auto dev_vec = [&](const std::string& name, float** out, bool required) -> bool {
+    // row0 / n: this rank's slice of the vector (biases of sharded rows)
+    auto dev_vec = [&](const std::string& name, float** out, bool required, int row0 = 0, int n = -1) -> bool {
         const Tensor* t = g.find(name);
         if (!t) {
             if (required && err) *err = "missing tensor " + name;
@@ -334,6 +397,10 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         }
         std::vector<float> v;
         if (!host_vec(t, v)) { if (err) *err = "bad vector " + name; return false; }
+        if (n >= 0) {
+            if (row0 + n > (int)v.size()) { if (err) *err = "bad vector slice " + name; return false; }
+            v = std::vector<float>(v.begin() + row0, v.begin() + row0 + n);
+        }
         float* d = nullptr;
         CK(cudaMalloc(&d, v.size() * sizeof(float)));
         CK(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -344,9 +411,12 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     for (int i = 0; i < c.n_layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
         DevLayer& L = layers_[i];
+        const int sq = tp_world_ > 1 ? c.q_dim() : -1, skv = tp_world_ > 1 ? c.kv_dim() : -1;
         if (!dev_vec(p + "attn_norm.weight", &L.attn_norm, true) || !dev_vec(p + "ffn_norm.weight", &L.ffn_norm, true) ||
-            !dev_vec(p + "attn_q.bias", &L.bq, false) || !dev_vec(p + "attn_k.bias", &L.bk, false) ||
-            !dev_vec(p + "attn_v.bias", &L.bv, false) || !dev_vec(p + "attn_q_norm.weight", &L.q_norm, false) ||
+            !dev_vec(p + "attn_q.bias", &L.bq, false, tp_rank_ * c.q_dim(), sq) ||
+            !dev_vec(p + "attn_k.bias", &L.bk, false, tp_rank_ * c.kv_dim(), skv) ||
+            !dev_vec(p + "attn_v.bias", &L.bv, false, tp_rank_ * c.kv_dim(), skv) ||
+            !dev_vec(p + "attn_q_norm.weight", &L.q_norm, false) ||
             !dev_vec(p + "attn_k_norm.weight", &L.k_norm, false))
             return false;
         if (L.q_norm && L.k_norm) c.qk_norm = true;
@@ -400,7 +470,15 @@ bool Engine::upload_weights(std::string* err) {
     weights_dev_bytes_ = total;
     CK(cudaMalloc(&warena_, total + 256));
     for (Job& j : jobs) j.w->d = warena_ + j.off;
-    if (cfg_.tied_output) out_w_ = embd_;
+    if (cfg_.tied_output) {
+        out_w_ = embd_;
+        if (tp_world_ > 1) {   // this rank's vocab rows of the shared table: whole 8-row tiles
+            out_w_.n_out = cfg_.out_rows;
+            out_w_.row0 = cfg_.out_row0;
+            out_w_.d = embd_.d + (size_t)(cfg_.out_row0 / 8) * dev_matrix_bytes(embd_.type, embd_.n_in, 8);
+            out_w_.expert_bytes = dev_matrix_bytes(embd_.type, embd_.n_in, cfg_.out_rows);
+        }
+    }
 
     // staged, repacked upload: rows repacked by host threads into pinned
     // buffers, copied while the next buffer fills.
@@ -418,7 +496,8 @@ bool Engine::upload_weights(std::string* err) {
     // repacks a run of tiles
     for (const Job& j : jobs) {
         const DevW& w = *j.w;
-        const size_t src_rb = ggml_row_bytes(j.t->type, (uint64_t)w.n_in);
+        const size_t src_rb = ggml_row_bytes(j.t->type, (uint64_t)w.n_in_src);   // a whole source row
+        const size_t k_off = ggml_row_bytes(j.t->type, (uint64_t)w.k0);          // the shard's first value
         const size_t tile_bytes = dev_matrix_bytes(w.type, w.n_in, 8);
         const int rows_per = (int)std::max<size_t>(8, stage / tile_bytes * 8);
         for (int e = 0; e < w.n_exp && ok; ++e) {
@@ -427,13 +506,13 @@ bool Engine::upload_weights(std::string* err) {
                 const size_t nbytes = dev_matrix_bytes(w.type, w.n_in, nr);
                 if (cudaEventSynchronize(done[cur]) != cudaSuccess) { ok = false; break; }
                 uint8_t* dst = pin[cur];
-                const uint8_t* src = j.t->data + ((size_t)e * w.n_out + r0) * src_rb;
+                const uint8_t* src = j.t->data + ((size_t)e * w.n_out_src + w.row0 + r0) * src_rb + k_off;
                 const int n_tiles = (nr + 7) / 8;
                 auto work = [&](int tid) {
                     const int a = (int)((long long)n_tiles * tid / nth), b = (int)((long long)n_tiles * (tid + 1) / nth);
                     if (a >= b) return;
                     const int ra = 8 * a, rb = std::min(nr, 8 * b);
-                    repack_rows(w.type, src + (size_t)ra * src_rb, rb - ra, w.n_in, dst + (size_t)a * tile_bytes);
+                    repack_rows(w.type, src + (size_t)ra * src_rb, rb - ra, w.n_in, dst + (size_t)a * tile_bytes, src_rb);
                 };
                 std::vector<std::thread> th;
                 for (int i = 1; i < nth; ++i) th.emplace_back(work, i);
@@ -475,6 +554,10 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMalloc(&g_, sizeof(float) * (size_t)R * F));
     CK(cudaMalloc(&u_, sizeof(float) * (size_t)R * F));
     CK(cudaMalloc(&logits_, sizeof(float) * (size_t)kMaxBatch * c.vocab));
+    if (tp_world_ > 1) {
+        CK(cudaMalloc(&tp_tmp_, sizeof(float) * (size_t)kMaxBatch * E));
+        CK(cudaMalloc(&tp_logits_, sizeof(float) * (size_t)tp_world_ * kMaxBatch * c.out_rows));
+    }
     if (c.n_experts > 0) {
         CK(cudaMalloc(&router_, sizeof(float) * kMaxBatch * c.n_experts));
         CK(cudaMalloc(&eo_, sizeof(float) * (size_t)R * E));
@@ -782,6 +865,7 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         s.expert = expert;
         s.expert_bytes = w.expert_bytes;
         s.amax = keys ? keys + t0 : nullptr;
+        s.key_row0 = keys ? cfg_.out_row0 : 0;   // argmax keys carry global vocab rows
         if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemm(&g, stream_));
         else CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
     }
@@ -858,6 +942,7 @@ bool Engine::step_ready() {
     const Config& c = cfg_;
     if (!env_int("FISH_PERSIST", 0)) { step_why_ = "off (FISH_PERSIST=1 enables it)"; return false; }
     if (c.n_experts > 0) { step_why_ = "mixture of experts"; return false; }
+    if (tp_world_ > 1) { step_why_ = "tensor parallel"; return false; }
     if (c.qk_norm) { step_why_ = "q/k norm"; return false; }
     const int G = c.n_head_kv > 0 ? c.n_head / c.n_head_kv : 0;
     if (c.head_dim != 128 || c.n_head % c.n_head_kv || !(G == 1 || G == 2 || G == 4 || G == 8) || c.rot_dim > 128 ||
@@ -1066,14 +1151,20 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
         }
         a.K = Q;
         {
+            // tensor parallelism: this rank's heads give a partial sum of o,
+            // all-reduced before the residual add
+            const bool tp = tp_world_ > 1;
+            float* oy = tp ? tp_tmp_ : x_;
+            const int oepi = tp ? EPI_STORE : EPI_ADD;
             const DevW* wo[1] = {&L.wo};
             if (fusable(wo, 1, T)) {
                 const GemvPro pro{PRO_QUANT, attn_, Q, nullptr, 0, nullptr, 0.0f};
-                if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+                if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err, &pro)) return false;
             } else {
                 CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
-                if (!gemv(L.wo, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+                if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err)) return false;
             }
+            if (tp && !tp_reduce_add(T, err)) return false;
         }
         a.K = E;
         const DevW* wgu[2] = {&L.wg, &L.wu};
@@ -1114,38 +1205,137 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
                 }
             }
             a.K = F;
+            const bool tp = tp_world_ > 1;
+            float* dy = tp ? tp_tmp_ : x_;
+            const int depi = tp ? EPI_STORE : EPI_ADD;
             const DevW* wd[1] = {&L.wd};
             if (fuse_ffn && fusable(wd, 1, T)) {   // h = silu(g) * u already in g_
                 const GemvPro pro{PRO_QUANT, g_, F, nullptr, 0, nullptr, 0.0f};
-                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro)) return false;
             } else if (fusable(wd, 1, T)) {
                 const GemvPro pro{PRO_SILU, g_, F, u_, F, nullptr, 0.0f};
-                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err, &pro)) return false;
+                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro)) return false;
             } else {
                 CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
-                if (!gemv(L.wd, a, T, x_, E, nullptr, EPI_ADD, nullptr, 0, nullptr, err)) return false;
+                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err)) return false;
             }
+            if (tp && !tp_reduce_add(T, err)) return false;
         }
     }
     return true;
 }
 
 // Final norm + output projection for x rows [row0, row0+n) into logits rows 0..n-1.
-bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err, unsigned long long* keys, bool* keyed) {
+bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err, unsigned long long* keys, bool* keyed,
+                      bool need_logits) {
     if (keyed) *keyed = false;
     const Config& c = cfg_;
     const int E = c.n_embd;
     ActQ a = act_;
     a.K = E;
     const DevW* wo[1] = {&out_w_};
+    // tensor parallelism: this rank's vocab rows into its slice of
+    // tp_logits_; argmax keys (global row ids) reduced by max over the ranks;
+    // logits gathered when the caller needs them
+    const bool tp = tp_world_ > 1;
+    float* ydst = tp ? tp_logits_ + (size_t)tp_rank_ * n * c.out_rows : logits_dev;
+    const int ldy = tp ? c.out_rows : c.vocab;
+    bool k = false;
     if (fusable(wo, 1, n)) {
         const GemvPro pro{PRO_NORM, x_ + (size_t)row0 * E, E, nullptr, 0, out_norm_, c.eps};
-        if (keyed) *keyed = keys != nullptr;
-        return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, nullptr, 0, nullptr, err, &pro, keys);
+        k = keys != nullptr;
+        if (!gemv(out_w_, a, n, ydst, ldy, nullptr, EPI_STORE, nullptr, 0, nullptr, err, &pro, keys)) return false;
+    } else {
+        CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_ + (size_t)row0 * E, E, out_norm_, c.eps, n, E, xb_, E, &a, want32_e_,
+                                           wantk_e_, stream_));
+        if (!gemv(out_w_, a, n, ydst, ldy, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
     }
-    CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_ + (size_t)row0 * E, E, out_norm_, c.eps, n, E, xb_, E, &a, want32_e_, wantk_e_,
-                                       stream_));
-    return gemv(out_w_, a, n, logits_dev, c.vocab, nullptr, EPI_STORE, xb_, E, nullptr, err);
+    if (keyed) *keyed = k;
+    if (tp) {
+        if (k && nccl_api(err)->all_reduce(keys, keys, (size_t)n, ncclUint64, ncclMax, (ncclComm_t)nccl_, stream_) !=
+                     ncclSuccess) {
+            if (err) *err = "NCCL all-reduce of argmax keys failed";
+            return false;
+        }
+        if ((need_logits || !k) && !tp_gather_logits(n, logits_dev, err)) return false;
+    }
+    return true;
+}
+
+bool Engine::tp_reduce_add(int T, std::string* err) {
+    const size_t n = (size_t)T * cfg_.n_embd;
+    if (nccl_api(err)->all_reduce(tp_tmp_, tp_tmp_, n, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_) != ncclSuccess) {
+        if (err) *err = "NCCL all-reduce failed";
+        return false;
+    }
+    CKP(PC_OTHER, 0, fbk_add(x_, tp_tmp_, n, stream_));
+    return true;
+}
+
+// tp_logits_ holds [world][rows][out_rows] after the gather; logits rows are
+// [rows][vocab] with rank r's slice at columns r * out_rows.
+bool Engine::tp_gather_logits(int rows, float* logits_dev, std::string* err) {
+    const int R = cfg_.out_rows;
+    const size_t cnt = (size_t)rows * R;
+    if (nccl_api(err)->all_gather(tp_logits_ + (size_t)tp_rank_ * cnt, tp_logits_, cnt, ncclFloat, (ncclComm_t)nccl_,
+                                  stream_) != ncclSuccess) {
+        if (err) *err = "NCCL all-gather of logits failed";
+        return false;
+    }
+    for (int r = 0; r < tp_world_; ++r)
+        CK(cudaMemcpy2DAsync(logits_dev + (size_t)r * R, sizeof(float) * cfg_.vocab, tp_logits_ + (size_t)r * cnt,
+                             sizeof(float) * R, sizeof(float) * R, rows, cudaMemcpyDeviceToDevice, stream_));
+    return true;
+}
+
+// NCCL, loaded when tensor parallelism is first asked for (no link-time
+// dependency: a process that also loads another NCCL build, e.g. a Python
+// framework's, keeps whichever was loaded first). An NCCL already in the
+// process is used as is.
+const NcclApi* nccl_api(std::string* err) {
+    static NcclApi api;
+    static bool tried = false;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (tried) {
+        if (!api.ok && err) *err = "NCCL is not available";
+        return api.ok ? &api : nullptr;
+    }
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW);
+    if (!h) { if (err) *err = "NCCL (libnccl.so.2) not found"; return nullptr; }
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce && api.all_gather &&
+             api.error_string;
+    if (!api.ok && err) *err = "NCCL library lacks an expected function";
+    return api.ok ? &api : nullptr;
+}
+
+bool Engine::set_tp(int rank, int world, const void* id, std::string* err) {
+    if (gguf_) { if (err) *err = "tensor parallelism must be set up before the model is loaded"; return false; }
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) { if (err) *err = "bad tensor-parallel rank/world"; return false; }
+    if (world == 1) return true;
+    const NcclApi* nc = nccl_api(err);
+    if (!nc) return false;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = nc->comm_init_rank(&comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        if (err) *err = std::string("ncclCommInitRank: ") + nc->error_string(r);
+        return false;
+    }
+    nccl_ = comm;
+    tp_rank_ = rank;
+    tp_world_ = world;
+    return true;
 }
 
 bool Engine::upload_tokens(const int32_t* ids, const int* sids, const int* pos, int T, std::string* err) {
@@ -1171,7 +1361,7 @@ bool Engine::capture_graph(int key, std::string* err) {
     bool ok = fbk_embed(embd_.type, embd_.d, cfg_.n_embd, embd_.n_out, ids_, T, x_, cfg_.n_embd, fbk_gemv_error_flag(), stream_) == 0;
     ok = ok && run_layers(T, cfg_.n_ctx, true, &e2);
     bool keyed = false;
-    ok = ok && run_head(0, T, logits_, &e2, amax_keys_, &keyed);
+    ok = ok && run_head(0, T, logits_, &e2, amax_keys_, &keyed, key != 0);
     if (key == 0)
         ok = ok && (keyed ? fbk_greedy_from_keys(amax_keys_, ids_, tok_pos_, greedy_out_, greedy_step_, stream_)
                           : fbk_greedy_advance(logits_, cfg_.vocab, ids_, tok_pos_, greedy_out_, greedy_step_, stream_)) == 0;

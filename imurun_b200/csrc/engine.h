@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nccl.h>   // types only: the library is loaded at run time (nccl_api)
 
 #include <cstdint>
 #include <map>
@@ -32,6 +33,10 @@ struct Config {
     int bos = 1, eos = 2;
     bool tied_output = false, neox = false, qk_norm = false;
     int n_experts = 0, n_experts_per_tok = 0, n_ff_exp = 0;
+    // tensor parallelism: the head counts and n_ff above are this rank's
+    // shares; the model's own values are kept here (equal without it)
+    int n_head_model = 0, n_head_kv_model = 0, n_ff_model = 0;
+    int out_rows = 0, out_row0 = 0;   // output-projection rows of this rank (vocab slice)
     bool expert_weights_norm = true;
     // RoPE scaling (src/model.cpp:508-537)
     float freq_scale = 1.0f, mscale = 1.0f;
@@ -47,7 +52,10 @@ void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, 
 
 struct DevW {
     int type = -1;
-    int n_in = 0, n_out = 0, n_exp = 1;
+    int n_in = 0, n_out = 0, n_exp = 1;   // this rank's shard (the whole tensor without tensor parallelism)
+    // shard of the GGUF tensor: rows [row0, row0 + n_out) of its n_out_src,
+    // values [k0, k0 + n_in) of its rows of n_in_src values (k0 a block edge)
+    int row0 = 0, k0 = 0, n_in_src = 0, n_out_src = 0;
     size_t stride = 0;           // device row stride
     size_t expert_bytes = 0;     // bytes per expert slice (3-D tensors)
     uint8_t* d = nullptr;
@@ -66,12 +74,34 @@ struct Seq {
     std::vector<int> pages;      // page ids in position order
 };
 
+// NCCL entry points, resolved at run time (nccl_api() in engine.cpp); the
+// types come from nccl.h.
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+const NcclApi* nccl_api(std::string* err);
+
 class Engine {
 public:
     Engine() = default;
     ~Engine();
     Engine(const Engine&) = delete;
     Engine& operator=(const Engine&) = delete;
+
+    // Tensor parallelism over `world` ranks (one process per GPU), before
+    // load: q/k/v and gate/up rows split by heads / FFN rows, o and down split
+    // along their inputs (256-aligned K slices) with an NCCL all-reduce after
+    // each, the output projection split by vocab rows (argmax keys reduced by
+    // max, logits gathered). id: the 128-byte NCCL unique id of the group.
+    bool set_tp(int rank, int world, const void* id, std::string* err);
+    int tp_rank() const { return tp_rank_; }
+    int tp_world() const { return tp_world_; }
 
     bool load(const std::string& path, int n_ctx, std::string* err);
     const Config& cfg() const { return cfg_; }
@@ -145,8 +175,10 @@ private:
     bool run_layers(int T, int max_ctx, bool distinct, std::string* err);
     // keys (nullable): argmax keys per row accumulated by the output GEMV;
     // returns in *keyed whether they were (streamed kernel only)
+    // need_logits = false: with argmax keys and tensor parallelism, the
+    // logits are not gathered (greedy steps)
     bool run_head(int rows_from, int n_rows, float* logits_dev, std::string* err,
-                  unsigned long long* keys = nullptr, bool* keyed = nullptr);
+                  unsigned long long* keys = nullptr, bool* keyed = nullptr, bool need_logits = true);
     bool gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi,
               const float* xf, int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro = nullptr,
               unsigned long long* keys = nullptr);
@@ -214,6 +246,13 @@ private:
 
     std::map<int, cudaGraphExec_t> graphs_;
     std::map<int, int> graph_kernels_;
+    // tensor parallelism
+    int tp_rank_ = 0, tp_world_ = 1;
+    void* nccl_ = nullptr;            // ncclComm_t
+    float* tp_tmp_ = nullptr;         // [kMaxBatch][E] partial sums of o / down
+    float* tp_logits_ = nullptr;      // [world][kMaxBatch][out_rows] gathered vocab slices
+    bool tp_reduce_add(int T, std::string* err);   // x += all-reduce(tp_tmp_)
+    bool tp_gather_logits(int rows, float* logits_dev, std::string* err);
     bool use_graphs_ = true;
     bool no_fuse_ = false;     // FISH_NO_FUSE: separate norm/quant kernels before every GEMV
     // persistent step

@@ -59,16 +59,17 @@ size_t dev_matrix_bytes(int type, int n, int rows) {
 
 static size_t ggml_block_bytes(int type) { return type == T_Q8_0 ? 34 : (type == T_Q4_K ? 144 : 210); }
 
-void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst) {
+void repack_rows(int type, const uint8_t* src, int rows, int n, uint8_t* dst, size_t src_stride) {
     const size_t total = dev_matrix_bytes(type, n, rows);
     std::memset(dst, 0, total);
     if (!is_tiled(type)) {
         const size_t sb = type == T_F32 ? (size_t)n * 4 : (size_t)n * 2, db = dev_row_bytes(type, n);
-        for (int r = 0; r < rows; ++r) std::memcpy(dst + (size_t)r * db, src + (size_t)r * sb, sb);
+        const size_t ss = src_stride ? src_stride : sb;
+        for (int r = 0; r < rows; ++r) std::memcpy(dst + (size_t)r * db, src + (size_t)r * ss, sb);
         return;
     }
     const int nb = row_blocks(type, n);
-    const size_t srb = (size_t)nb * ggml_block_bytes(type);
+    const size_t srb = src_stride ? src_stride : (size_t)nb * ggml_block_bytes(type);
     for (int r = 0; r < rows; ++r) {
         const uint8_t* s = src + (size_t)r * srb;
         for (int b = 0; b < nb; ++b) {

@@ -17,7 +17,10 @@ size_t dev_row_bytes(int type, int n_in);
 size_t dev_matrix_bytes(int type, int n_in, int rows);
 // Repack `rows` consecutive GGUF rows (the first one starting a tile) into
 // the device layout at dst (dev_matrix_bytes(type, n_in, rows) bytes).
-void repack_rows(int type, const uint8_t* src, int rows, int n_in, uint8_t* dst);
+// Repack `rows` GGUF rows of n_in values into the device layout at dst (whole
+// 8-row tiles). src_stride: bytes from one source row to the next (0 = the
+// rows are contiguous; larger for a slice of K-blocks of wider rows).
+void repack_rows(int type, const uint8_t* src, int rows, int n_in, uint8_t* dst, size_t src_stride = 0);
 
 // Epilogue of a GEMV segment.
 enum : int { EPI_STORE = 0, EPI_ADD = 1 };
@@ -35,6 +38,7 @@ struct GemvSeg {
     size_t expert_bytes;
     size_t w_bytes;         // bytes readable from w (every expert); reads outside are skipped and flagged
     unsigned long long* amax;  // optional [T]: running argmax key per token (streamed kernel, EPI_STORE)
+    int key_row0;           // added to the row index in argmax keys (a vocab slice's first global row)
 };
 
 constexpr int kMaxSeg = 4;

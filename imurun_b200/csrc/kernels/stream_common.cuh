@@ -789,7 +789,7 @@ __device__ __forceinline__ void reduce_rows(const JobView& j, const float* part,
             for (int gi = 0; gi < G; ++gi) v += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
             v = store_out(g, row, t, v);
             if (g.amax) {
-                const unsigned long long key = argmax_key(v, row);
+                const unsigned long long key = argmax_key(v, row + g.key_row0);
                 best[t] = key > best[t] ? key : best[t];
             }
         }

@@ -67,7 +67,7 @@ ABI5_FUNCTIONS = [
     "fish_prefill_ids", "fish_decode_ids", "fish_decode_greedy", "fish_kv_len", "fish_set_kv_len",
     "fish_session_open", "fish_session_fork", "fish_session_close", "fish_session_len", "fish_session_prefill",
     "fish_decode_batch", "fish_session_pages", "fish_kv_page_size", "fish_engine_json", "fish_profile_decode_json",
-    "fish_trace_decode",
+    "fish_trace_decode", "fish_tp_unique_id", "fish_tp_init",
 ]
 KERNEL_FUNCTIONS = [
     "fbx_quantize_acts", "fbx_rmsnorm", "fbx_matmul", "fbx_block_sums", "fbx_attention", "fbx_rope",
@@ -105,6 +105,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "fish_session_pages": ([P, I, P, I], I), "fish_kv_page_size": ([P], I),
         "fish_engine_json": ([P], CP), "fish_profile_decode_json": ([P, ctypes.c_int32, I], CP),
         "fish_trace_decode": ([P, ctypes.c_int32, I, P, I], I),
+        "fish_tp_unique_id": ([P, I], I), "fish_tp_init": ([P, I, I, P, I], I),
         "fbx_quantize_acts": ([P, I, I, P, P], I), "fbx_rmsnorm": ([P, P, I, I, F, P], I),
         "fbx_matmul": ([I, P, I, I, P, I, P], I), "fbx_block_sums": ([I, P, I, I, P, P, P], I),
         "fbx_attention": ([P, P, P, I, I, I, I, I, I, I, P], I),
@@ -125,12 +126,32 @@ class FishError(RuntimeError):
     pass
 
 
+def tp_unique_id(lib: ctypes.CDLL | None = None) -> bytes:
+    """A new tensor-parallel group id (on one rank; share it with the others)."""
+    lib = lib or load_library()
+    buf = ctypes.create_string_buffer(128)
+    n = lib.fish_tp_unique_id(buf, 128)
+    if n <= 0 or n > 128:
+        raise FishError("fish_tp_unique_id failed")
+    return buf.raw[:n]
+
+
 class Model:
     """One fish_ctx with a loaded model; thin id-level convenience wrapper."""
 
-    def __init__(self, path, n_ctx: int = 4096, lib: ctypes.CDLL | None = None):
+    def __init__(self, path, n_ctx: int = 4096, lib: ctypes.CDLL | None = None, tp: tuple | None = None):
+        """tp = (rank, world, group id bytes from tp_unique_id()): tensor
+        parallelism, one process per GPU; every rank makes the same calls."""
         self.lib = lib or load_library()
         self.ctx = self.lib.fish_create()
+        if tp is not None and tp[1] > 1:
+            rank, world, gid = tp
+            buf = ctypes.create_string_buffer(bytes(gid), len(gid))
+            if self.lib.fish_tp_init(self.ctx, int(rank), int(world), buf, len(gid)) != 0:
+                err = self.lib.fish_last_error(self.ctx).decode()
+                self.lib.fish_destroy(self.ctx)
+                self.ctx = None
+                raise FishError(f"fish_tp_init: {err}")
         rc = self.lib.fish_load(self.ctx, str(path).encode(), int(n_ctx))
         if rc != 0:
             err = self.lib.fish_last_error(self.ctx).decode()

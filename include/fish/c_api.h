@@ -172,6 +172,22 @@ FISH_API int fish_decode_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0,
  * Stops early only on error. Returns the number of ids written. */
 FISH_API int fish_decode_greedy(fish_ctx* ctx, int32_t first, int n_steps, int32_t* out_ids);
 
+/* Tensor parallelism (ABI 5 addition; no counterpart in the reference, which
+ * runs one model per process on the CPU): one process per GPU, ranks
+ * 0..world-1. fish_tp_unique_id writes a new 128-byte group id into out (on
+ * one rank; every rank then receives it through the caller's own channel) and
+ * returns its size (or the size needed when cap is too small, < 0 on error).
+ * fish_tp_init records rank, world and id for the next fish_load, which
+ * then joins the NCCL group and loads only this rank's shard: q/k/v and
+ * gate/up rows split by heads and FFN rows, attn_output and ffn_down split
+ * along their inputs (256-aligned), the output projection split by vocab
+ * rows; two all-reduces per layer. Dense llama/qwen2 models whose kv heads,
+ * FFN rows and vocab divide by world. Every rank must make the same calls in
+ * the same order (prefill, decode, greedy); logits and ids returned are the
+ * whole model's. Returns 0, or -1 on bad arguments. */
+FISH_API int fish_tp_unique_id(void* out, int cap);
+FISH_API int fish_tp_init(fish_ctx* ctx, int rank, int world, const void* id, int id_bytes);
+
 FISH_API int  fish_kv_len(fish_ctx* ctx);
 FISH_API int  fish_set_kv_len(fish_ctx* ctx, int n);
 
