@@ -143,7 +143,7 @@ Engine::~Engine() {
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
     cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
-    cudaFree(tp_tmp_); cudaFree(tp_logits_);
+    cudaFree(tp_tmp_); cudaFree(tp_logits_); cudaFree(sel_loc_);
     if (nccl_) nccl_api(nullptr)->comm_destroy((ncclComm_t)nccl_);   // after the graphs that hold its calls
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (ev0_) cudaEventDestroy(ev0_);
@@ -261,17 +261,16 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     c.out_row0 = 0;
     if (tp_world_ > 1) {   // this rank's heads, FFN rows and vocab rows
         const int N = tp_world_;
-        if (c.n_experts > 0) {
-            if (err) *err = "tensor parallelism: dense models only (experts are not split across ranks yet)";
-            return false;
-        }
-        if (c.n_head_kv % N || c.n_ff % N || c.vocab % N || (c.vocab / N) % 8) {
-            if (err) *err = "tensor parallelism: kv heads, FFN rows and vocab rows must split evenly over the ranks";
+        const bool moe = c.n_experts > 0;   // experts are split over the ranks (expert parallelism), not their rows
+        if (c.n_head_kv % N || (!moe && c.n_ff % N) || (moe && c.n_experts % N) || c.vocab % N || (c.vocab / N) % 8) {
+            if (err) *err = "tensor parallelism: kv heads, FFN rows (experts) and vocab rows must split evenly over the ranks";
             return false;
         }
         c.n_head /= N;
         c.n_head_kv /= N;
-        c.n_ff /= N;
+        if (!moe) c.n_ff /= N;
+        ep_n_ = moe ? c.n_experts / N : 0;
+        ep_e0_ = tp_rank_ * ep_n_;
         c.out_rows = c.vocab / N;
         c.out_row0 = tp_rank_ * c.out_rows;
     }
@@ -353,6 +352,13 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
                 !bind(p + "ffn_up_exps.weight", L.up_exps, true) || !bind(p + "ffn_down_exps.weight", L.down_exps, true))
                 return false;
             c.n_ff_exp = L.gate_exps.n_out;
+            if (tp_world_ > 1) {   // this rank's experts
+                for (DevW* w : {&L.gate_exps, &L.up_exps, &L.down_exps}) {
+                    if (w->n_exp != c.n_experts) { if (err) *err = "expert tensor count differs from expert_count"; return false; }
+                    w->n_exp = ep_n_;
+                    w->e0 = ep_e0_;
+                }
+            }
         } else {
             if (!bind(p + "ffn_gate.weight", L.wg, true) || !bind(p + "ffn_up.weight", L.wu, true) ||
                 !bind(p + "ffn_down.weight", L.wd, true))
@@ -506,7 +512,7 @@ bool Engine::upload_weights(std::string* err) {
                 const size_t nbytes = dev_matrix_bytes(w.type, w.n_in, nr);
                 if (cudaEventSynchronize(done[cur]) != cudaSuccess) { ok = false; break; }
                 uint8_t* dst = pin[cur];
-                const uint8_t* src = j.t->data + ((size_t)e * w.n_out_src + w.row0 + r0) * src_rb + k_off;
+                const uint8_t* src = j.t->data + ((size_t)(w.e0 + e) * w.n_out_src + w.row0 + r0) * src_rb + k_off;
                 const int n_tiles = (nr + 7) / 8;
                 auto work = [&](int tid) {
                     const int a = (int)((long long)n_tiles * tid / nth), b = (int)((long long)n_tiles * (tid + 1) / nth);
@@ -562,6 +568,7 @@ bool Engine::alloc_buffers(std::string* err) {
         CK(cudaMalloc(&router_, sizeof(float) * kMaxBatch * c.n_experts));
         CK(cudaMalloc(&eo_, sizeof(float) * (size_t)R * E));
         CK(cudaMalloc(&sel_, sizeof(int32_t) * R));
+        if (tp_world_ > 1) CK(cudaMalloc(&sel_loc_, sizeof(int32_t) * R));
         CK(cudaMalloc(&wsel_, sizeof(float) * R));
     }
     // activation planes: q32 | qk (R x ld each), d32 | s32 | bsk (R x max_k/32), dk (R x max_k/256)
@@ -1175,12 +1182,16 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
             const int NE = c.n_experts, K = c.n_experts_per_tok, F = c.n_ff_exp;
             if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
             CKP(PC_OTHER, 0, fbk_moe_route(router_, T, NE, K, c.expert_weights_norm ? 1 : 0, sel_, wsel_, stream_));
+            // expert parallelism: experts of other ranks map to -1 (zero rows)
+            const bool ep = tp_world_ > 1;
+            const int32_t* esel = ep ? sel_loc_ : sel_;
+            if (ep) CKP(PC_OTHER, 0, fbk_moe_localize(sel_, T * K, ep_e0_, ep_n_, sel_loc_, stream_));
             for (int t = 0; t < T; ++t) {
                 const ActQ ar = act_row(a, t, E);
                 for (int k = 0; k < K; ++k) {
                     const int r = t * K + k;
-                    if (!gemv(L.gate_exps, ar, 1, g_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err) ||
-                        !gemv(L.up_exps, ar, 1, u_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err))
+                    if (!gemv(L.gate_exps, ar, 1, g_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, esel + r, err) ||
+                        !gemv(L.up_exps, ar, 1, u_ + (size_t)r * F, F, nullptr, EPI_STORE, nullptr, 0, esel + r, err))
                         return false;
                 }
             }
@@ -1188,10 +1199,16 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
             CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T * K, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
             for (int r = 0; r < T * K; ++r) {
                 const ActQ ar = act_row(a, r, F);
-                if (!gemv(L.down_exps, ar, 1, eo_ + (size_t)r * E, E, nullptr, EPI_STORE, nullptr, 0, sel_ + r, err))
+                if (!gemv(L.down_exps, ar, 1, eo_ + (size_t)r * E, E, nullptr, EPI_STORE, nullptr, 0, esel + r, err))
                     return false;
             }
-            CKP(PC_OTHER, 0, fbk_moe_combine(x_, E, eo_, wsel_, T, K, E, stream_));
+            if (ep) {   // this rank's weighted experts, summed over the ranks, then the residual add
+                CK(cudaMemsetAsync(tp_tmp_, 0, sizeof(float) * (size_t)T * E, stream_));
+                CKP(PC_OTHER, 0, fbk_moe_combine(tp_tmp_, E, eo_, wsel_, T, K, E, stream_));
+                if (!tp_reduce_add(T, err)) return false;
+            } else {
+                CKP(PC_OTHER, 0, fbk_moe_combine(x_, E, eo_, wsel_, T, K, E, stream_));
+            }
         } else {
             const int F = c.n_ff;
             {

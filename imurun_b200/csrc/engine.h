@@ -56,6 +56,7 @@ struct DevW {
     // shard of the GGUF tensor: rows [row0, row0 + n_out) of its n_out_src,
     // values [k0, k0 + n_in) of its rows of n_in_src values (k0 a block edge)
     int row0 = 0, k0 = 0, n_in_src = 0, n_out_src = 0;
+    int e0 = 0;   // first expert of this rank's slice (expert parallelism)
     size_t stride = 0;           // device row stride
     size_t expert_bytes = 0;     // bytes per expert slice (3-D tensors)
     uint8_t* d = nullptr;
@@ -251,6 +252,8 @@ private:
     void* nccl_ = nullptr;            // ncclComm_t
     float* tp_tmp_ = nullptr;         // [kMaxBatch][E] partial sums of o / down
     float* tp_logits_ = nullptr;      // [world][kMaxBatch][out_rows] gathered vocab slices
+    int32_t* sel_loc_ = nullptr;      // expert parallelism: routed experts as local ids (-1: another rank's)
+    int ep_e0_ = 0, ep_n_ = 0;        // this rank's experts [ep_e0_, ep_e0_ + ep_n_)
     bool tp_reduce_add(int T, std::string* err);   // x += all-reduce(tp_tmp_)
     bool tp_gather_logits(int rows, float* logits_dev, std::string* err);
     bool use_graphs_ = true;

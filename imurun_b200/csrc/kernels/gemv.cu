@@ -18,7 +18,8 @@
 //                  a warp, one block per lane). Per-stage row partials go to
 //                  shared memory and are summed over groups at the end in a
 //                  fixed order.
-//   k_gemv_direct  T = 5..8 (prefill chunks) and F32/F16 rows, plain loads.
+//   k_gemv_direct  T = 5..15 and F32/F16 rows, plain loads (T >= 16 on
+//                  quantised rows: the tensor-core kernel, gemm.cu).
 // Launches carry the programmatic-dependent-launch attribute when the caller
 // asks for it: the producer streams weights before the previous kernel has
 // finished (weights never change); everything that reads activations or
@@ -213,19 +214,21 @@ __global__ void __launch_bounds__(256) k_gemv_direct(GemvArgs args) {
         int s = 0;
         while (s < args.nseg - 1 && it >= items[s + 1]) ++s;
         const GemvSeg& g = args.seg[s];
-        const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
+        const int eidx = g.expert ? __ldg(g.expert) : 0;   // < 0: an expert of another rank (zero rows)
+        const uint8_t* base = g.w + (size_t)max(eidx, 0) * g.expert_bytes;
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
         if (is_tiled(g.type)) {
             const int row = (it - items[s]) * 4 + (lane >> 3), bl = lane & 7;
-            direct_rows_q<NT>(g, base, args.K, args.act, args.T, row, row < g.rows, bl, acc, args.err);
+            direct_rows_q<NT>(g, base, args.K, args.act, args.T, row, row < g.rows && eidx >= 0, bl, acc, args.err);
 #pragma unroll
             for (int t = 0; t < NT; ++t)
                 if (bl == 0 && row < g.rows && t < args.T) store_out(g, row, t, acc[t]);
         } else {
             const int row = it - items[s];
-            if (in_range(base + (size_t)row * g.row_stride, g.row_stride, g.w, g.w + g.w_bytes, lane == 0 ? args.err : nullptr))
+            if (eidx >= 0 &&
+                in_range(base + (size_t)row * g.row_stride, g.row_stride, g.w, g.w + g.w_bytes, lane == 0 ? args.err : nullptr))
                 row_float<NT>(g.type, base + (size_t)row * g.row_stride, args.K, args.xf, args.ldxf, args.T, lane, acc);
 #pragma unroll
             for (int t = 0; t < NT; ++t) {

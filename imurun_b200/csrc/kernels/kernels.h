@@ -174,6 +174,9 @@ int fbk_argmax_from_keys(unsigned long long* keys, int T, int32_t* out, cudaStre
 int fbk_greedy_from_keys(unsigned long long* keys, int32_t* ids, int32_t* tok_pos, int32_t* out, int32_t* step,
                          cudaStream_t st);
 int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel, cudaStream_t st);
+// Expert parallelism: out[i] = sel[i] - e0 when this rank holds that expert
+// (e0 <= sel[i] < e0 + n), else -1 (the expert GEMVs write zero rows for -1).
+int fbk_moe_localize(const int32_t* sel, int n_sel, int e0, int n, int32_t* out, cudaStream_t st);
 }
 
 // ---------------------------------------------------------------- persistent decode step (step.cu)

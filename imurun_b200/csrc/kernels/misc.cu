@@ -213,6 +213,23 @@ extern "C" int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, co
     return (int)fbk_launch(k_head_rmsnorm, dim3((warps + 7) / 8), dim3(256), 0, st, x, ldx, T, n_heads, D, w, eps);
 }
 
+// Expert parallelism: global expert ids -> this rank's local ids (e - e0 for
+// e in [e0, e0 + n), else -1: the expert GEMVs then write zero rows).
+__global__ void k_moe_localize(const int32_t* __restrict__ sel, int n_sel, int e0, int n, int32_t* out) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_sel) {
+        const int e = sel[i];
+        out[i] = (e >= e0 && e < e0 + n) ? e - e0 : -1;
+    }
+}
+
+extern "C" int fbk_moe_localize(const int32_t* sel, int n_sel, int e0, int n, int32_t* out, cudaStream_t st) {
+    if (n_sel <= 0) return 0;
+    return (int)fbk_launch(k_moe_localize, dim3((n_sel + 255) / 256), dim3(256), 0, st, sel, n_sel, e0, n, out);
+}
+
 extern "C" int fbk_moe_combine(float* x, int ldx, const float* eo, const float* wsel, int T, int K, int E, cudaStream_t st) {
     if (T <= 0) return 0;
     return (int)fbk_launch(k_moe_combine, dim3((E + 255) / 256, T), dim3(256), 0, st, x, ldx, eo, wsel, T, K, E);

@@ -419,7 +419,10 @@ __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView
         int sg, lt;
         tile_seg(j.tile0, j.nseg, j.pair, tile, sg, lt);
         const GemvSeg& g = j.seg[sg];
-        const uint8_t* base = g.expert ? g.w + (size_t)__ldg(g.expert) * g.expert_bytes : g.w;
+        // expert index < 0: an expert held by another rank (expert
+        // parallelism): nothing is streamed and the epilogue writes zeros
+        const int eidx = g.expert ? __ldg(g.expert) : 0;
+        const uint8_t* base = g.w + (size_t)max(eidx, 0) * g.expert_bytes;
         const int nb = row_blocks(g.type, j.K);
         const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
         if (ph > 0) {
@@ -433,7 +436,7 @@ __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView
             }
         }
         const uint8_t* src = base + (size_t)lt * kTileRows * g.row_stride + (size_t)kTileRows * group_offset(g.type, gi);
-        if (bytes <= (uint32_t)rg.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, err)) {
+        if (eidx >= 0 && bytes <= (uint32_t)rg.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, err)) {
             mbar_expect_tx(&rg.full[slot], bytes);
             bulk_g2s(rg.base + (size_t)slot * rg.slot_bytes, src, bytes, &rg.full[slot]);
         } else {
@@ -787,6 +790,7 @@ __device__ __forceinline__ void reduce_rows(const JobView& j, const float* part,
             if (t >= T) break;
             float v = 0.0f;
             for (int gi = 0; gi < G; ++gi) v += part[((size_t)(tl * G + gi) * kTileRows + rr) * NT + t];
+            if (g.expert && __ldg(g.expert) < 0) v = 0.0f;   // an expert of another rank
             v = store_out(g, row, t, v);
             if (g.amax) {
                 const unsigned long long key = argmax_key(v, row + g.key_row0);

@@ -32,13 +32,14 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _run_tp(world: int, path: Path, tmp: Path) -> dict:
+def _run_tp(world: int, path: Path, tmp: Path, vocab: int = 128256) -> dict:
     idfile, out = tmp / f"tp{world}.id", tmp / f"tp{world}.npz"
     procs = []
     for r in range(world):
         env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(r), NCCL_NVLS_ENABLE="0")
         procs.append(subprocess.Popen([sys.executable, str(ROOT / "tests" / "tp_worker.py"), str(r), str(world), str(path),
-                                       str(idfile), str(out)], env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
+                                       str(idfile), str(out), str(vocab)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT))
     logs, rcs = [], []
     for p in procs:
         try:
@@ -53,6 +54,28 @@ def _run_tp(world: int, path: Path, tmp: Path) -> dict:
     return dict(np.load(out))
 
 
+def _compare(tp: dict, one: dict):
+    for i, (a, b) in enumerate(zip(tp["logits"], one["logits"])):
+        d = np.abs(a - b)
+        assert d.max() <= 0.03 * np.abs(b).max(), (i, float(d.max()), float(np.abs(b).max()))
+        assert np.median(d) <= 0.03, (i, float(np.median(d)))
+        s = np.sort(b)
+        if s[-1] - s[-2] > 2 * (1e-2 + 1e-3 * np.abs(b).max()):
+            assert int(np.argmax(a)) == int(np.argmax(b)), i
+    assert np.array_equal(tp["greedy"], tp["forced"])
+
+
+def test_expert_parallel_mixtral_shape(synth_dir, tmp_path):
+    """Mixtral-shaped, 1 layer: 8 experts split 4 + 4 over 2 ranks (routing
+    on every rank, other ranks' experts give zero rows, weighted outputs
+    all-reduced), attention split by heads (1 kv head per rank)."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    from imurun_b200 import synth
+    path = synth.cached(synth.preset("mixtral", layers=1, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=2), synth_dir)
+    _compare(_run_tp(2, path, tmp_path, 32000), _run_tp(1, path, tmp_path, 32000))
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_tensor_parallel_matches_one_gpu(synth_dir, tmp_path, world):
     if _gpus() < world:
@@ -63,12 +86,5 @@ def test_tensor_parallel_matches_one_gpu(synth_dir, tmp_path, world):
     path = synth.cached(synth.preset("llama8b", layers=2), synth_dir)
     tp = _run_tp(world, path, tmp_path)
     one = _run_tp(1, path, tmp_path)
-    for i, (a, b) in enumerate(zip(tp["logits"], one["logits"])):
-        d = np.abs(a - b)
-        assert d.max() <= 0.03 * np.abs(b).max(), (i, float(d.max()), float(np.abs(b).max()))
-        assert np.median(d) <= 0.03, (i, float(np.median(d)))
-        s = np.sort(b)
-        if s[-1] - s[-2] > 2 * (1e-2 + 1e-3 * np.abs(b).max()):
-            assert int(np.argmax(a)) == int(np.argmax(b)), i
-    assert np.array_equal(tp["greedy"], tp["forced"])
+    _compare(tp, one)
     assert tp["greedy"].size == tp_worker.N_GREEDY

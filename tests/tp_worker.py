@@ -1,6 +1,6 @@
 """One rank of a tensor-parallel run, for tests/test_gpu_tp.py (not a test file).
 
-    python tests/tp_worker.py RANK WORLD GGUF IDFILE OUT
+    python tests/tp_worker.py RANK WORLD GGUF IDFILE OUT [VOCAB]
 
 Runs on the GPU named by CUDA_VISIBLE_DEVICES. Rank 0 creates the NCCL group
 id and writes it to IDFILE; the other ranks wait for it (bounded). Every rank
@@ -24,6 +24,7 @@ N_PROMPT, N_DEC, N_GREEDY = 40, 4, 8
 
 def main() -> int:
     rank, world, path, idfile, out = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3], sys.argv[4], sys.argv[5]
+    vocab = int(sys.argv[6]) if len(sys.argv) > 6 else 128256
     lib = native.load_library()
     if rank == 0:
         gid = native.tp_unique_id(lib)
@@ -39,7 +40,7 @@ def main() -> int:
                 return 2
             time.sleep(0.05)
         gid = open(idfile, "rb").read()
-    ids = np.random.default_rng(21).integers(3, 128256, N_PROMPT + N_DEC).astype(np.int32)
+    ids = np.random.default_rng(21).integers(3, vocab, N_PROMPT + N_DEC).astype(np.int32)
     with native.Model(path, 1024, lib=lib, tp=(rank, world, gid)) as m:
         steps = [m.prefill(ids[:N_PROMPT], 0)]
         am = []
