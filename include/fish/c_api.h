@@ -181,10 +181,13 @@ FISH_API int fish_decode_greedy(fish_ctx* ctx, int32_t first, int n_steps, int32
  * then joins the NCCL group and loads only this rank's shard: q/k/v and
  * gate/up rows split by heads and FFN rows, attn_output and ffn_down split
  * along their inputs (256-aligned), the output projection split by vocab
- * rows; two all-reduces per layer. Dense llama/qwen2 models whose kv heads,
- * FFN rows and vocab divide by world. Every rank must make the same calls in
- * the same order (prefill, decode, greedy); logits and ids returned are the
- * whole model's. Returns 0, or -1 on bad arguments. */
+ * rows; two all-reduces per layer. MoE models split the experts instead of
+ * the FFN rows (experts/world per rank; routing computed on every rank;
+ * selections of other ranks' experts contribute zero rows) and all-reduce
+ * the weighted expert outputs. Models whose kv heads, FFN rows (or experts)
+ * and vocab divide by world. Every rank must make the same calls in the same
+ * order (prefill, decode, greedy); logits and ids returned are the whole
+ * model's. Returns 0, or -1 on bad arguments. */
 FISH_API int fish_tp_unique_id(void* out, int cap);
 FISH_API int fish_tp_init(fish_ctx* ctx, int rank, int world, const void* id, int id_bytes);
 
