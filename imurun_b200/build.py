@@ -26,6 +26,10 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if Path("/usr/local/cud
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
           f"-I{ROOT / 'include'}", f"-I{CSRC}"]
+# FISH_TRACE_CTA_BUILD=1 compiles the every-CTA trace events (kernels/trace.cuh)
+# into the kernels; off by default, since they cost time on every launch.
+if os.environ.get("FISH_TRACE_CTA_BUILD", "0") not in ("", "0"):
+    COMMON.append("-DFB_TRACE_CTA=1")
 
 SOURCES = [
     "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu", "kernels/gemm.cu",
@@ -40,7 +44,13 @@ def _obj(src: str) -> Path:
 
 def _headers_mtime() -> float:
     hs = list(CSRC.rglob("*.h")) + list(CSRC.rglob("*.cuh")) + list((ROOT / "include").rglob("*.h"))
-    return max((h.stat().st_mtime for h in hs), default=0.0)
+    t = max((h.stat().st_mtime for h in hs), default=0.0)
+    # a change of compiler flags makes every object stale
+    stamp = BUILD / "flags.txt"
+    flags = " ".join(ARCH + COMMON)
+    if not stamp.exists() or stamp.read_text() != flags:
+        stamp.write_text(flags)
+    return max(t, stamp.stat().st_mtime)
 
 
 def _compile(src: str, hdr_mtime: float) -> str:

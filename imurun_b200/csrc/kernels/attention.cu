@@ -701,11 +701,19 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     cg::cluster_group cluster = cg::this_cluster();
     const int C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
     pdl_trigger();
-    const bool tr = tracing() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    const unsigned long long t_kernel = gtimer();
+    const bool tr = tracing() && !tracing_all() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
     __shared__ int s_tseq;
     if (tr && threadIdx.x == 0) {
         s_tseq = trace_launch(TR_ATTN);
         trace_ev(TR_ATTN, EV_START, s_tseq);
+    }
+    const int tcb = trace_cta_begin(3);
+    if (tcb >= 0) {
+        unsigned long long* r = g_trace.buf + 4 * (size_t)tcb;
+        r[0] = t_kernel; r[1] = TR_ATTN; r[2] = EV_C_START;
+        r[3] = (blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z)) |
+               ((unsigned long long)gridDim.x * gridDim.y * gridDim.z << 20);
     }
     // Before the dependency wait: everything written before this graph step
     // began (token positions, page tables, the KV cache of earlier positions,
@@ -776,6 +784,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const float* cs = s_rot[0];
     const float* sn = s_rot[1];
     pdl_wait();
+    trace_cta(tcb, 1, TR_ATTN, EV_C_WAITED);
     if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
     const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
     const int wt = 32 * kIssuer;   // threads doing the rotation
@@ -1027,6 +1036,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     }
     cluster.sync();
     if (tr && tid == 0) trace_ev(TR_ATTN, EV_END, s_tseq);
+    trace_cta(tcb, 2, TR_ATTN, EV_C_END);
 }
 
 }  // namespace fb
@@ -1142,14 +1152,16 @@ static int launch_decode_tc(const float* q, int ldq, const float* k, const float
                                              (int)TcSmem::bytes);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_decode_tc<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return (int)e;
-        cluster = 16;
+        const char* ev = getenv("FISH_ATTN_CLUSTER");
+        const int want = ev ? atoi(ev) : 16;
+        cluster = (want == 1 || want == 2 || want == 4 || want == 8) ? want : 16;
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(16, 1, 1);
+        cfg.gridDim = dim3(cluster, 1, 1);
         cfg.blockDim = dim3(32 * kTcWarps);
         cfg.dynamicSmemBytes = TcSmem::bytes;
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = 16;
+        at[0].val.clusterDim.x = cluster;
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;

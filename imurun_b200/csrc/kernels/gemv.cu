@@ -27,7 +27,9 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -326,7 +328,9 @@ struct StreamJobs {
     int pair;                // tiles alternate between segments 0 and 1 (SwiGLU epilogue)
 };
 
-template <int NT>
+// TM: the weight types the kernel handles (TM_* bits); PM: the prologue mode,
+// or -1 for any (read from the arguments).
+template <int NT, int TM, int PM>
 __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv_stream(GemvArgs args, StreamJobs jobs) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
@@ -343,6 +347,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
     __shared__ unsigned long long s_best[kConsumers][4];
+    __shared__ long long s_pw, s_cw;   // summed wait cycles (all-CTA tracing)
     const int K = args.K, G = jobs.n_groups, S = jobs.stages;
     int n_tiles = jobs.tile0[0];
 #pragma unroll
@@ -379,6 +384,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     rg.guard = 0;   // S is a multiple of the pairs and the job starts at ring stage 0
     rg.pwait = nullptr;
     rg.cwait = nullptr;
+    rg.pclk = tracing_all() ? &s_pw : nullptr;
+    rg.cclk = tracing_all() ? &s_cw : nullptr;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < kMaxSeg; ++i)
@@ -386,7 +393,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
 #pragma unroll
     for (int i = 0; i <= kMaxSeg; ++i)
         if (threadIdx.x == i) s_tile0[i] = jobs.tile0[i];
-    const bool tr = tracing() && blockIdx.x == 0;
+    const bool tr = tracing() && !tracing_all() && blockIdx.x == 0;
     if (tr && threadIdx.x == 0) {
         s_tseq = trace_launch(TR_GEMV);
         trace_ev(TR_GEMV, EV_START, s_tseq);
@@ -395,6 +402,8 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
         *s_abort = 0;
         *s_issued = 0;
         *s_prod_wait = -1;
+        s_pw = 0;
+        s_cw = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 2);
@@ -407,7 +416,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
         if (lane == 0) {
             if (jobs.wait_first) pdl_wait();
             WaitFail wf{};
-            if (!produce_stages(rg, jv, 0, jobs.err, &wf)) {
+            if (!produce_stages<TM>(rg, jv, 0, jobs.err, &wf)) {
                 const int issued = wf.stage;   // stages issued before the one that waited
                 record_wait_fail(1, wf.stage, wf.slot, wf.parity, n_stages, S, issued, wf.t0, t_kernel, wf.stage - S, full,
                                  empty, (int)dyn_smem);
@@ -423,8 +432,14 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
 
     // consumers: the norm weights are constant, so they are loaded before
     // waiting for the previous kernel
+    const int tcb = trace_cta_begin(7);
+    if (tcb >= 0) {
+        unsigned long long* r = g_trace.buf + 4 * (size_t)tcb;
+        r[0] = t_kernel; r[1] = TR_GEMV; r[2] = EV_C_START;
+        r[3] = blockIdx.x | ((unsigned long long)gridDim.x << 20);
+    }
     float wv[kNormRegs][8];
-    if (args.pro.mode == PRO_NORM) {
+    if ((PM >= 0 ? PM : args.pro.mode) == PRO_NORM) {
 #pragma unroll
         for (int k = 0; k < kNormRegs; ++k) {
             const int c = warp + kConsumers * k;
@@ -433,12 +448,14 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     }
     pdl_wait();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_WAITED, s_tseq);
+    trace_cta(tcb, 1, TR_GEMV, EV_C_WAITED);
     const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
-    build_ximage(args, xi, wantk, want32, s_part, wv, tr ? s_tseq : -1);
+    build_ximage<PM>(args, xi, wantk, want32, s_part, wv, tr ? s_tseq : -1);
     consumers_sync();
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
+    trace_cta(tcb, 2, TR_GEMV, EV_C_READY);
     WaitFail wf{};
-    const bool ok = consume_stages<NT>(rg, jv, 0, xi, part, &wf, tr ? s_tseq : -1);
+    const bool ok = consume_stages<NT, TM>(rg, jv, 0, xi, part, &wf, tr ? s_tseq : -1);
     if (!ok) {
         if (!*s_abort)
             record_wait_fail(2, wf.stage, wf.slot, wf.parity, n_stages, S, *s_issued, wf.t0, t_kernel, *s_prod_wait, full,
@@ -447,12 +464,19 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
         *s_abort = 1;
     }
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_LOOP, s_tseq);
+    trace_cta(tcb, 3, TR_GEMV, EV_C_LOOP);
+    trace_cta_val(tcb, 5, TR_GEMV, EV_C_CWAIT, (unsigned long long)s_cw);
     consumers_sync();
     if (*s_abort) return;
     reduce_rows<NT>(jv, part, s_best);
     if (tr) {
         consumers_sync();
         if (threadIdx.x == 0) trace_ev(TR_GEMV, EV_END, s_tseq);
+    }
+    if (tcb >= 0 || (tracing_all() && threadIdx.x < 32)) {
+        __syncwarp();
+        trace_cta(tcb, 4, TR_GEMV, EV_C_END);   // warp 0's rows are written
+        trace_cta_val(tcb, 6, TR_GEMV, EV_C_PWAIT, (unsigned long long)s_pw);
     }
 }
 }  // namespace fb
@@ -511,6 +535,42 @@ static int env_or(const char* name, int def) {
 
 // Pipeline geometry: CTAs per SM (default 2) split the SM's shared memory;
 // after the activation image and the row partials, the rest is ring slots.
+using StreamKernel = void (*)(GemvArgs, StreamJobs);
+
+// Single-token launches get a kernel compiled for their weight-type set and
+// prologue mode: the variant that carries every type's consumer arithmetic
+// and every prologue does not fit the instruction cache (a quarter of its
+// fetches missed in a decode-sized launch). Other launches use that generic
+// variant.
+template <int NT>
+static StreamKernel stream_variant(int tm, int pm) {
+    if (NT == 1) {
+        switch (pm * 8 + tm) {
+#define FB_SV(P, T) \
+    case P * 8 + T: return k_gemv_stream<1, T, P>;
+            FB_SV(PRO_NORM, 1) FB_SV(PRO_NORM, 2) FB_SV(PRO_NORM, 3) FB_SV(PRO_NORM, 4)
+            FB_SV(PRO_QUANT, 1) FB_SV(PRO_QUANT, 2) FB_SV(PRO_QUANT, 3) FB_SV(PRO_QUANT, 4)
+            FB_SV(PRO_SILU, 1) FB_SV(PRO_SILU, 2) FB_SV(PRO_SILU, 4)
+#undef FB_SV
+            default: break;
+        }
+    }
+    return k_gemv_stream<NT, TM_ALL, -1>;
+}
+
+// Dynamic shared memory opt-in, once per kernel variant.
+static int stream_smem_optin(StreamKernel k, int dyn) {
+    static std::mutex mu;
+    static std::vector<StreamKernel> done;
+    std::lock_guard<std::mutex> lock(mu);
+    for (StreamKernel d : done)
+        if (d == k) return 0;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
+        return (int)cudaGetLastError();
+    done.push_back(k);
+    return 0;
+}
+
 template <int NT>
 static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     static const int want_cps = std::max(1, std::min(4, env_or("FISH_GEMV_CTA_PER_SM", 2)));
@@ -520,11 +580,9 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, k_gemv_stream<NT>) != cudaSuccess) return (int)cudaGetLastError();
+        if (cudaFuncGetAttributes(&fa, k_gemv_stream<NT, TM_ALL, -1>) != cudaSuccess) return (int)cudaGetLastError();
         const int dyn = optin - (int)fa.sharedSizeBytes;
         if (dyn <= 0) return (int)cudaErrorInvalidValue;
-        if (cudaFuncSetAttribute(k_gemv_stream<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
-            return (int)cudaGetLastError();
         max_smem = dyn;
     }
     StreamJobs jobs{};
@@ -565,7 +623,11 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     }
     if (stages < kPairs) return (int)cudaErrorInvalidValue;
     jobs.stages = stages;
-    return (int)fbk_launch(k_gemv_stream<NT>, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
+    int tm = 0;
+    for (int s = 0; s < a->nseg; ++s) tm |= type_bit(a->seg[s].type);
+    const StreamKernel kern = stream_variant<NT>(tm, a->pro.mode);
+    if (const int e = stream_smem_optin(kern, max_smem)) return e;
+    return (int)fbk_launch(kern, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
 }
 
 extern "C" int fbk_gemv_streamable(const GemvArgs* a) {

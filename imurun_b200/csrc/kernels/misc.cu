@@ -300,6 +300,8 @@ extern "C" int fbk_trace_enable(int cap) {
         s.cap = cap;
         s.n = g_tcnt;
         s.seq = g_tcnt + 1;
+        const char* all = getenv("FISH_TRACE_ALL");
+        s.all = all && *all && *all != '0';
     }
     int rc = fbk_trace_set_gemv(&s);
     if (!rc) rc = fbk_trace_set_attn(&s);

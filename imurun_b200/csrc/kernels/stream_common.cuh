@@ -157,13 +157,17 @@ __device__ __forceinline__ void ld8(const float* p, int i0, int K, float (&v)[8]
 constexpr int kNormRegs = 2;
 static_assert(kConsumers == kNormWarps, "the fused norm sums in the shared order of k_rmsnorm_quant");
 
-// Consumer prologue: build the activation image for T tokens.
+// Consumer prologue: build the activation image for T tokens. PM >= 0 fixes
+// the prologue mode at compile time (only that mode's code is emitted);
+// PM < 0 reads it from the arguments.
+template <int PM = -1>
 __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage& xi, bool wantk, bool want32,
                                              double* s_part, const float (&wv)[kNormRegs][8], int tseq) {
     const int ct = threadIdx.x, warp = ct >> 5, lane = ct & 31;
     const int K = args.K, T = args.T, n256 = xi.n256;
     const GemvPro& pro = args.pro;
-    if (pro.mode == PRO_ACT) {
+    const int mode = PM >= 0 ? PM : pro.mode;
+    if (mode == PRO_ACT) {
         const ActQ& a = args.act;
         for (int t = 0; t < T; ++t) {
             if (wantk) {
@@ -193,7 +197,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
         return;
     }
     const int n_chunks = (K + 255) / 256;
-    if (pro.mode == PRO_MERGE) {
+    if (mode == PRO_MERGE) {
         // decode-attention partials of C key chunks (one token): acc at
         // src[(c H + h) D ..], (m, l) at src[C H D + 2 (c H + h)]; the head's
         // output is sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c,
@@ -248,7 +252,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
         }
         return;
     }
-    if (pro.mode == PRO_NORM) {
+    if (mode == PRO_NORM) {
         // the reference's double sum (src/ops.cpp:18-23) in the order every
         // norm kernel shares (common.cuh); chunks that fit stay in registers
         // between the sum and the quantisation
@@ -301,7 +305,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
     // quantisation: warp w takes chunks w, w + 8, ...; each batch of up to 4
     // chunks loads everything it needs before computing
     constexpr int kB = 2;
-    if (pro.mode == PRO_QUANT) {   // one source: four chunks per batch
+    if (mode == PRO_QUANT) {   // one source: four chunks per batch
         constexpr int kQ = 4;
         for (int t = 0; t < T; ++t) {
             const float* xr = pro.src + (size_t)t * pro.ld;
@@ -323,7 +327,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
     }
     for (int t = 0; t < T; ++t) {
         const float* xr = pro.src + (size_t)t * pro.ld;
-        const float* ur = pro.mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
+        const float* ur = mode == PRO_SILU ? pro.src2 + (size_t)t * pro.ld2 : nullptr;
         for (int c0 = warp; c0 < n_chunks; c0 += kConsumers * kB) {
             float va[kB][8], ua[kB][8];
 #pragma unroll
@@ -332,7 +336,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
                 if (c < n_chunks) {
                     const int i0 = c * 256 + 8 * lane;
                     ld8(xr, i0, K, va[k]);
-                    if (pro.mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
+                    if (mode == PRO_SILU) ld8(ur, i0, K, ua[k]);
                 }
             }
 #pragma unroll
@@ -340,7 +344,7 @@ __device__ __forceinline__ void build_ximage(const GemvArgs& args, const XImage&
                 const int c = c0 + kConsumers * k;
                 if (c < n_chunks) {
                     float v[8];
-                    if (pro.mode == PRO_SILU) {
+                    if (mode == PRO_SILU) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
                             v[i] = __fmul_rn(__fdiv_rn(va[k][i], __fadd_rn(1.0f, expf(-va[k][i]))), ua[k][i]);
@@ -394,6 +398,8 @@ struct RingView {
     int guard;                // consumers wait for *issued > g first
     unsigned long long* pwait;   // optional: ns the producer waited for free slots
     unsigned long long* cwait;   // optional: ns consumer warp 0 waited for data
+    long long* pclk = nullptr;   // optional: SM cycles in the producer's slot waits
+    long long* cclk = nullptr;   // optional: SM cycles in thread 0's data waits
 };
 
 struct JobView {
@@ -403,6 +409,16 @@ struct JobView {
     int t_begin, t_end;
 };
 
+// Weight-type sets a streamed kernel is compiled for (bit per type); a single
+// type makes the per-stage type arithmetic constant, and the consumer loop
+// carries only the arithmetic of the types in the set.
+constexpr int TM_Q4K = 1, TM_Q6K = 2, TM_Q80 = 4, TM_ALL = 7;
+__host__ __device__ constexpr int type_bit(int t) { return t == T_Q4_K ? TM_Q4K : t == T_Q6_K ? TM_Q6K : t == T_Q8_0 ? TM_Q80 : 0; }
+template <int TM>
+__device__ __forceinline__ int stage_type(int t) {
+    return TM == TM_Q4K ? T_Q4_K : TM == TM_Q6K ? T_Q6_K : TM == TM_Q80 ? T_Q8_0 : t;
+}
+
 struct WaitFail {
     int stage, slot, parity;
     unsigned long long t0;
@@ -411,6 +427,7 @@ struct WaitFail {
 __device__ __forceinline__ int job_stages(const JobView& j) { return max(0, j.t_end - j.t_begin) * j.G; }
 
 // Producer (one thread): the job's stages as ring stages gbase, gbase+1, ...
+template <int TM = TM_ALL>
 __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView& j, int gbase, int* err, WaitFail* wf) {
     const int n = job_stages(j);
     int tile = j.t_begin, gi = 0;
@@ -423,11 +440,15 @@ __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView
         // parallelism): nothing is streamed and the epilogue writes zeros
         const int eidx = g.expert ? __ldg(g.expert) : 0;
         const uint8_t* base = g.w + (size_t)max(eidx, 0) * g.expert_bytes;
-        const int nb = row_blocks(g.type, j.K);
-        const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(g.type, group_blocks(g.type, nb, gi)));
+        const int gt = stage_type<TM>(g.type);
+        const int nb = row_blocks(gt, j.K);
+        const uint32_t bytes = (uint32_t)(kTileRows * group_bytes(gt, group_blocks(gt, nb, gi)));
         if (ph > 0) {
             unsigned long long tw = 0;
-            if (!mbar_wait(&rg.empty[slot], (uint32_t)((ph - 1) & 1), rg.abort, &tw, rg.pwait)) {
+            const long long c0 = rg.pclk ? clock64() : 0;
+            const bool got = mbar_wait(&rg.empty[slot], (uint32_t)((ph - 1) & 1), rg.abort, &tw, rg.pwait);
+            if (rg.pclk) *rg.pclk += clock64() - c0;
+            if (!got) {
                 wf->stage = gbase + l;
                 wf->slot = slot;
                 wf->parity = (ph - 1) & 1;
@@ -435,7 +456,7 @@ __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView
                 return false;
             }
         }
-        const uint8_t* src = base + (size_t)lt * kTileRows * g.row_stride + (size_t)kTileRows * group_offset(g.type, gi);
+        const uint8_t* src = base + (size_t)lt * kTileRows * g.row_stride + (size_t)kTileRows * group_offset(gt, gi);
         if (eidx >= 0 && bytes <= (uint32_t)rg.slot_bytes && in_range(src, bytes, g.w, g.w + g.w_bytes, err)) {
             mbar_expect_tx(&rg.full[slot], bytes);
             bulk_g2s(rg.base + (size_t)slot * rg.slot_bytes, src, bytes, &rg.full[slot]);
@@ -459,7 +480,7 @@ __device__ __forceinline__ bool produce_stages(const RingView& rg, const JobView
 // (gbase + l) % 4 == pq; warp half h of the pair rows 4h .. 4h+3 of the tile,
 // lane = row * 8 + block. Row partials of local stage l go to
 // part[(l * 8 + row) * NT + t]. False when a wait gave up (or the CTA aborted).
-template <int NT>
+template <int NT, int TM = TM_ALL>
 __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView& j, int gbase, const XImage& xi, float* part,
                                                WaitFail* wf, int tseq) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -472,7 +493,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
     for (; l < n; l += kPairs) {
         int sgc, ltc;
         tile_seg(j.tile0, j.nseg, j.pair, tile, sgc, ltc);
-        const int type = j.seg[sgc].type;
+        const int type = stage_type<TM>(j.seg[sgc].type);
         const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
         const int piece = (int)group_bytes(type, gbk);
         const uint8_t* pc = rg.base + (size_t)slot * rg.slot_bytes + (size_t)r8 * piece;
@@ -491,7 +512,10 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
         }
         {
             unsigned long long tw = 0;
-            if (!mbar_wait(&rg.full[slot], (uint32_t)(ph & 1), rg.abort, &tw, threadIdx.x == 0 ? rg.cwait : nullptr)) {
+            const long long c0 = rg.cclk && threadIdx.x == 0 ? clock64() : 0;
+            const bool got = mbar_wait(&rg.full[slot], (uint32_t)(ph & 1), rg.abort, &tw, threadIdx.x == 0 ? rg.cwait : nullptr);
+            if (rg.cclk && threadIdx.x == 0) *rg.cclk += clock64() - c0;
+            if (!got) {
                 wf->stage = gbase + l;
                 wf->slot = slot;
                 wf->parity = ph & 1;
@@ -505,7 +529,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
         for (int t = 0; t < NT; ++t) c[t] = 0.0f;
         // (the slot is released after the arithmetic: holding a whole block
         // in registers across an early release spills at the 96-register cap)
-        if (type == T_Q4_K) {
+        if ((TM & TM_Q4K) && type == T_Q4_K) {
             if (bl < gbk) {
                 uint4 w[9];
 #pragma unroll
@@ -520,7 +544,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
                     c[t] = q4k_term(dw, dmw, *xi.dk(t, kb), si, mi);
                 }
             }
-        } else if (type == T_Q6_K) {
+        } else if ((TM & TM_Q6K) && type == T_Q6_K) {
             if (bl < gbk) {
                 uint4 w[13];
 #pragma unroll
@@ -534,7 +558,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
                     c[t] = scaled_term(dw, *xi.dk(t, kb), si);
                 }
             }
-        } else {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group, in block order
+        } else if (TM & TM_Q80) {   // Q8_0: lane takes blocks 8 bl .. 8 bl + 7 of the group, in block order
             const int kc = gi * 8 + bl;
             for (int i = 0; i < 8; ++i) {
                 const int b = 8 * bl + i;
