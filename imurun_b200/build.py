@@ -30,6 +30,8 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hi
 # into the kernels; off by default, since they cost time on every launch.
 if os.environ.get("FISH_TRACE_CTA_BUILD", "0") not in ("", "0"):
     COMMON.append("-DFB_TRACE_CTA=1")
+# extra preprocessor definitions for experiment builds, e.g. "-DFOO=1 -DBAR=2"
+COMMON += [d for d in os.environ.get("FISH_NVCC_DEFINES", "").split() if d.startswith("-D")]
 
 SOURCES = [
     "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu", "kernels/gemm.cu",

@@ -793,9 +793,9 @@ bool Engine::fusable(const DevW* const* ws, int n, int T) const {
 bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
                         const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro, bool swiglu) {
     // T >= 16 tokens with quantised planes: one tensor-core launch per
-    // segment; otherwise GEMV launches of up to 8 tokens
+    // segment; otherwise GEMV launches of up to 4 (streamed) or 8 tokens
     int chunk = 8;
-    if (T >= 16 && !pro && !swiglu) {
+    {
         GemvArgs p{};
         p.nseg = n;
         p.K = ws[0]->n_in;
@@ -805,7 +805,8 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
             p.seg[i].type = ws[i]->type;
             p.seg[i].rows = ws[i]->n_out;
         }
-        if (fbk_gemm_eligible(&p)) chunk = T;
+        chunk = fbk_gemv_chunk(&p);
+        if (T >= 16 && !pro && !swiglu && fbk_gemm_eligible(&p)) chunk = T;
     }
     for (int t0 = 0; t0 < T; t0 += chunk) {
         const int nt = std::min(chunk, T - t0);
@@ -839,7 +840,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
 bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const float* bias, int epi, const float* xf,
                   int ldxf, const int32_t* expert, std::string* err, const GemvPro* pro, unsigned long long* keys) {
     int chunk = 8;
-    if (T >= 16 && !pro && !expert && !keys) {
+    {
         GemvArgs p{};
         p.nseg = 1;
         p.K = w.n_in;
@@ -847,7 +848,8 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         p.act = a;
         p.seg[0].type = w.type;
         p.seg[0].rows = w.n_out;
-        if (fbk_gemm_eligible(&p)) chunk = T;
+        chunk = fbk_gemv_chunk(&p);
+        if (T >= 16 && !pro && !expert && !keys && fbk_gemm_eligible(&p)) chunk = T;
     }
     for (int t0 = 0; t0 < T; t0 += chunk) {
         const int nt = std::min(chunk, T - t0);

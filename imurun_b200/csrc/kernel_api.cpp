@@ -146,7 +146,7 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
     const bool quant = type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K;
     if (quant) TRY(fbk_quantize_rows(dx.as<float>(), n_in, T, n_in, &da.a, type == T_Q8_0, type != T_Q8_0, nullptr));
     // T >= 16 quantised rows go to the tensor-core kernel in one launch,
-    // otherwise GEMV launches of up to 8 tokens
+    // otherwise GEMV launches of up to 4 (streamed) or 8 tokens
     int step = 8;
     {
         GemvArgs probe{};
@@ -156,6 +156,7 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
         probe.act = da.a;
         probe.seg[0].type = type;
         probe.seg[0].rows = n_out;
+        step = fbk_gemv_chunk(&probe);
         if (fbk_gemm_eligible(&probe)) step = T;
     }
     for (int t0 = 0; t0 < T; t0 += step) {
@@ -227,10 +228,24 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     int rc = 0;
+    const bool gemm = fbk_gemm_eligible(&g) != 0;
+    const int chunk = gemm ? T : fbk_gemv_chunk(&g);   // as the engine splits a call
     for (int i = 0; i < 3 + iters && !rc; ++i) {
         if (i == 3) cudaEventRecord(e0, st);
         g.seg[0].w = dw.as<uint8_t>() + (size_t)(i % copies) * mat;
-        rc = fbk_gemm_eligible(&g) ? fbk_gemm(&g, st) : fbk_gemv(&g, st);
+        for (int t0 = 0; t0 < T && !rc; t0 += chunk) {
+            GemvArgs c = g;
+            c.T = std::min(chunk, T - t0);
+            if (da.a.q32) c.act.q32 = da.a.q32 + (size_t)t0 * da.a.ld;
+            if (da.a.qk) c.act.qk = da.a.qk + (size_t)t0 * da.a.ld;
+            if (da.a.d32) c.act.d32 = da.a.d32 + (size_t)t0 * (n_in / 32);
+            if (da.a.s32) c.act.s32 = da.a.s32 + (size_t)t0 * (n_in / 32);
+            if (da.a.dk) c.act.dk = da.a.dk + (size_t)t0 * (n_in / 256);
+            if (da.a.bsk) c.act.bsk = da.a.bsk + (size_t)t0 * (n_in / 32);
+            c.xf = dx.as<float>() + (size_t)t0 * n_in;
+            c.seg[0].y = dy.as<float>() + (size_t)t0 * n_out;
+            rc = gemm ? fbk_gemm(&c, st) : fbk_gemv(&c, st);
+        }
     }
     cudaEventRecord(e1, st);
     const int sync = (int)cudaStreamSynchronize(st);

@@ -644,6 +644,12 @@ extern "C" int fbk_gemv_streamable(const GemvArgs* a) {
     return stream_off ? 0 : 1;
 }
 
+extern "C" int fbk_gemv_chunk(const GemvArgs* a) {
+    GemvArgs p = *a;
+    p.T = 4;
+    return fbk_gemv_streamable(&p) ? 4 : 8;
+}
+
 extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
     if (a->T <= 0 || a->nseg <= 0) return 0;
     if (a->T > 8) return (int)cudaErrorInvalidValue;

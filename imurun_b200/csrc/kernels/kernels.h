@@ -85,6 +85,10 @@ int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T,
 int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                        const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);
+// Tokens per GEMV launch when a call has more than fit one: 4 where the
+// streamed kernel takes the segments (two 4-token launches outrun the direct
+// kernel's 8-token launch several times over), else 8.
+int fbk_gemv_chunk(const fb::GemvArgs* args);
 // Batched products on the int8 tensor cores (gemm.cu): T >= 16 tokens,
 // quantised planes already built (PRO_ACT), Q4_K / Q6_K / Q8_0 segments,
 // K % 256 == 0. fbk_gemm_eligible says whether a job qualifies

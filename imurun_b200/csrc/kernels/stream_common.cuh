@@ -609,7 +609,7 @@ __device__ __forceinline__ bool consume_stages(const RingView& rg, const JobView
 // over blocks are those of consume_stages, so a row's value is the same.
 // Empty barriers count 1 (the consuming warp); rg.guard must be set unless S
 // is a multiple of 8 and the job starts at ring stage 0.
-template <int NT>
+template <int NT, int TM = TM_ALL>
 __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobView& j, int gbase, const XImage& xi,
                                                  float* part, WaitFail* wf) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -621,7 +621,7 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
     for (; l < n; l += kConsumers) {
         int sgc, ltc;
         tile_seg(j.tile0, j.nseg, j.pair, tile, sgc, ltc);
-        const int type = j.seg[sgc].type;
+        const int type = stage_type<TM>(j.seg[sgc].type);
         const int nb = row_blocks(type, K), gbk = group_blocks(type, nb, gi);
         const int piece = (int)group_bytes(type, gbk);
         const uint8_t* p0 = rg.base + (size_t)slot * rg.slot_bytes + (size_t)r0 * piece;
@@ -656,7 +656,7 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
             c1[t] = 0.0f;
         }
         const int kb = gi * 8 + bl;
-        if (type == T_Q4_K) {
+        if ((TM & TM_Q4K) && type == T_Q4_K) {
             if (bl < gbk) {
                 const uint8_t* b0 = p0 + bl * 144;
                 const uint8_t* b1 = p1 + bl * 144;
@@ -689,7 +689,7 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
                     c1[t] = q4k_term(h2f((uint16_t)(h1.x & 0xFFFFu)), h2f((uint16_t)(h1.x >> 16)), dx, a1 >> 4, m1);
                 }
             }
-        } else if (type == T_Q6_K) {
+        } else if ((TM & TM_Q6K) && type == T_Q6_K) {
             if (bl < gbk) {
                 const uint8_t* b0 = p0 + bl * 208;
                 const uint8_t* b1 = p1 + bl * 208;
@@ -721,7 +721,7 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
                     c1[t] = scaled_term(dw1, dx, si1);
                 }
             }
-        } else {   // Q8_0: blocks 8 bl .. 8 bl + 7 of the group, in block order
+        } else if (TM & TM_Q80) {   // Q8_0: blocks 8 bl .. 8 bl + 7 of the group, in block order
             for (int i = 0; i < 8; ++i) {
                 const int b = 8 * bl + i;
                 if (b >= gbk) break;
