@@ -17,13 +17,14 @@
 // groups in order; Q8_0: each eighth of a group summed in block order first),
 // so a row's value does not depend on the number of tokens in the call.
 //
-// CTA tile 64 rows x 64 tokens, 8 warps (2 x 4 of 32 rows x 16 tokens). Each
-// K step is
-// one 256-value block (8 Q8_0 blocks): the CTA's 64 weight rows of that block
-// and the 64 tokens' 256 int8 activations are copied to shared memory with
-// cp.async, double-buffered. Nibbles / 6-bit codes are unpacked into A
-// fragments in registers (Q4_K low nibbles of qs words are already four
-// int8 in fragment order).
+// CTA tile 64 rows x BN tokens, 8 warps of 16 FT rows x 8 JT tokens; BN = 64
+// (warps of 32 x 16) for long prompts (compute-bound), 16 or 32 (warps of
+// 16 x 8, 16 x 16) for batched decode and short prompts, which the weight
+// stream bounds: narrower token tiles and a deeper pipeline. Each K step is one 256-value block (8 Q8_0 blocks): the CTA's
+// 64 weight rows of that block and the BN tokens' 256 int8 activations are
+// copied to shared memory with cp.async into an NS-stage ring. Nibbles /
+// 6-bit codes are unpacked into A fragments in registers (Q4_K low nibbles of
+// qs words are already four int8 in fragment order).
 #include <cstdint>
 #include <cstdlib>
 
@@ -36,7 +37,7 @@
 
 namespace fb {
 
-constexpr int kBM = 64, kBN = 64, kGemmThreads = 256;   // 8 warps: 2 x 4 of 32 rows x 16 tokens
+constexpr int kBM = 64;   // rows per CTA
 constexpr int kXStride = 272;   // bytes per token row of activations in shared memory (256 + pad)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -84,28 +85,31 @@ struct Step<T_Q8_0> {
 
 
 // Shared-memory stage of one K step: weights [64][WB], activations
-// [64][272], per-token scales (dx, or 8 d32 for Q8_0) [64][8] f32, Q4_K
-// 32-value activation sums [64][8] i16.
-template <int W>
+// [BN][272], per-token scales (dx, or 8 d32 for Q8_0) [BN][8] f32, Q4_K
+// 32-value activation sums [BN][8] i16.
+template <int W, int BN>
 struct StageLayout {
     static constexpr int WB = Step<W>::wbytes;
     static constexpr int w_off = 0;
     static constexpr int x_off = kBM * WB;
-    static constexpr int d_off = x_off + kBN * kXStride;
-    static constexpr int b_off = d_off + kBN * 8 * 4;
-    static constexpr int bytes = b_off + kBN * 16;
+    static constexpr int d_off = x_off + BN * kXStride;
+    static constexpr int b_off = d_off + BN * 8 * 4;
+    static constexpr int bytes = b_off + BN * 16;
 };
 
-template <int W>
-__global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err) {
-    using L = StageLayout<W>;
+template <int W, int BN, int NS, int FT, int JT>
+__global__ void __launch_bounds__(256) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err) {
+    using L = StageLayout<W, BN>;
     constexpr int WB = L::WB;
+    // 8 warps, each 16 FT rows x 8 JT tokens: 64 / (16 FT) along rows
+    constexpr int kBN = BN, kGemmThreads = 256, WRN = 4 / FT;
+    static_assert(WRN * (BN / (8 * JT)) == 8, "8 warps cover the 64 x BN tile");
     extern __shared__ __align__(128) uint8_t sm[];
     pdl_trigger();
     pdl_wait();
     const int row0 = blockIdx.x * kBM, t0 = blockIdx.y * kBN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
-    const int wr = warp & 1, wc = warp >> 1;   // rows 32 wr .., tokens 16 wc ..
+    const int wr = warp % WRN, wc = warp / WRN;   // rows 16 FT wr .., tokens 8 JT wc ..
     const int nsteps = K / 256;
     const uint8_t* wend = g.w + g.w_bytes;
 
@@ -166,11 +170,11 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
 
     // Per output: the running row value and the pending nodes of the
     // current group's tree (block bi of the group: see tree_push).
-    float acc[2][2][4], pa[2][2][4], pb[2][2][4], pc[2][2][4];
+    float acc[FT][JT][4], pa[FT][JT][4], pb[FT][JT][4], pc[FT][JT][4];
 #pragma unroll
-    for (int f = 0; f < 2; ++f)
+    for (int f = 0; f < FT; ++f)
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+        for (int j = 0; j < JT; ++j)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 acc[f][j][c] = 0.0f;
@@ -197,28 +201,34 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
     // group is short; the GEMV adds +0 for its missing blocks)
     auto tree_close = [&](int bi) {
 #pragma unroll
-        for (int f = 0; f < 2; ++f)
+        for (int f = 0; f < FT; ++f)
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < JT; ++j)
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
                     for (int z = bi + 1; z < 8; ++z) tree_push(f, j, c, 0.0f, z);
     };
 
-    {
-        const float dx0 = issue(0, sm);
-        if (W != T_Q8_0 && tid < kBN) reinterpret_cast<float*>(sm + L::d_off)[tid] = dx0;
+    // steps 0 .. NS-2 in flight before the loop; every iteration commits one
+    // group (the step NS-1 ahead, or an empty group past the end), so the
+    // wait for all but the NS-1 newest groups always completes step s
+#pragma unroll
+    for (int p = 0; p < NS - 1; ++p) {
+        if (p < nsteps) {
+            const float dx0 = issue(p, sm + (size_t)p * L::bytes);
+            if (W != T_Q8_0 && tid < kBN) reinterpret_cast<float*>(sm + (size_t)p * L::bytes + L::d_off)[tid] = dx0;
+        } else {
+            cp_async_commit();
+        }
     }
     for (int s = 0; s < nsteps; ++s) {
-        uint8_t* cur = sm + (size_t)(s & 1) * L::bytes;
-        uint8_t* nxt = sm + (size_t)((s + 1) & 1) * L::bytes;
+        uint8_t* cur = sm + (size_t)(s % NS) * L::bytes;
+        const int sn = s + NS - 1;   // the step issued now, into the stage step s - 1 used
+        uint8_t* nxt = sm + (size_t)(sn % NS) * L::bytes;
         float dx_next = 0.0f;
-        if (s + 1 < nsteps) {
-            dx_next = issue(s + 1, nxt);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        if (sn < nsteps) dx_next = issue(sn, nxt);
+        else cp_async_commit();
+        cp_async_wait<NS - 1>();
         __syncthreads();
         const uint8_t* sW = cur + L::w_off;
         const uint8_t* sX = cur + L::x_off;
@@ -228,13 +238,13 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
         // tokens (local): fragment j, columns 2 tig, 2 tig + 1
         if (W == T_Q4_K) {
             // per row: fp16 d, dmin; 6-bit scales and mins of the 8 sub-blocks
-            float dw[2][2], dmw[2][2];
-            uint32_t sclo[2][2], schi[2][2], mlo[2][2], mhi[2][2];
+            float dw[FT][2], dmw[FT][2];
+            uint32_t sclo[FT][2], schi[FT][2], mlo[FT][2], mhi[FT][2];
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint4 hd = *reinterpret_cast<const uint4*>(sW + (32 * wr + 16 * f + 8 * h + gid) * WB);
+                    const uint4 hd = *reinterpret_cast<const uint4*>(sW + (16 * FT * wr + 16 * f + 8 * h + gid) * WB);
                     dw[f][h] = h2f((uint16_t)(hd.x & 0xFFFFu));
                     dmw[f][h] = h2f((uint16_t)(hd.x >> 16));
                     sclo[f][h] = hd.y & 0x3F3F3F3Fu;
@@ -242,20 +252,20 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                     schi[f][h] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
                     mhi[f][h] = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
                 }
-            int sumi[2][2][4];
+            int sumi[FT][JT][4];
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < JT; ++j)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) sumi[f][j][c] = 0;
 #pragma unroll
             for (int gq = 0; gq < 8; ++gq) {
                 const int qoff = 16 + 32 * (gq >> 1), sh = (gq & 1) ? 4 : 0;
-                uint32_t A[2][4];
+                uint32_t A[FT][4];
 #pragma unroll
-                for (int f = 0; f < 2; ++f) {
-                    const uint8_t* r0p = sW + (32 * wr + 16 * f + gid) * WB + qoff + 4 * tig;
+                for (int f = 0; f < FT; ++f) {
+                    const uint8_t* r0p = sW + (16 * FT * wr + 16 * f + gid) * WB + qoff + 4 * tig;
                     const uint8_t* r1p = r0p + 8 * WB;
                     A[f][0] = (lds32(r0p) >> sh) & 0x0F0F0F0Fu;
                     A[f][1] = (lds32(r1p) >> sh) & 0x0F0F0F0Fu;
@@ -263,11 +273,11 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                     A[f][3] = (lds32(r1p + 16) >> sh) & 0x0F0F0F0Fu;
                 }
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const uint8_t* xp = sX + (16 * wc + 8 * j + gid) * kXStride + 32 * gq + 4 * tig;
+                for (int j = 0; j < JT; ++j) {
+                    const uint8_t* xp = sX + (8 * JT * wc + 8 * j + gid) * kXStride + 32 * gq + 4 * tig;
                     const uint32_t B[2] = {lds32(xp), lds32(xp + 16)};
 #pragma unroll
-                    for (int f = 0; f < 2; ++f) {
+                    for (int f = 0; f < FT; ++f) {
                         int c[4] = {0, 0, 0, 0};
                         mma_k32(c, A[f], B);
                         const int s0 = byte_of(gq < 4 ? sclo[f][0] : schi[f][0], gq & 3);
@@ -281,14 +291,14 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
             }
             // mins = sum_g m_g bsums_g, then the block's float term
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
+            for (int j = 0; j < JT; ++j) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int n = 16 * wc + 8 * j + 2 * tig + e;
+                    const int n = 8 * JT * wc + 8 * j + 2 * tig + e;
                     const uint4 bw = *reinterpret_cast<const uint4*>(cur + L::b_off + 16 * n);
                     const float dx = sD[n];
 #pragma unroll
-                    for (int f = 0; f < 2; ++f)
+                    for (int f = 0; f < FT; ++f)
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             int mins = 0;
@@ -303,17 +313,17 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                 }
             }
         } else if (W == T_Q6_K) {
-            float dw[2][2];
+            float dw[FT][2];
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
-                    dw[f][h] = h2f(*reinterpret_cast<const uint16_t*>(sW + (32 * wr + 16 * f + 8 * h + gid) * WB + 208 + 2 * bi));
-            int sumi[2][2][4];
+                    dw[f][h] = h2f(*reinterpret_cast<const uint16_t*>(sW + (16 * FT * wr + 16 * f + 8 * h + gid) * WB + 208 + 2 * bi));
+            int sumi[FT][JT][4];
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < JT; ++j)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) sumi[f][j][c] = 0;
 #pragma unroll 4
@@ -322,22 +332,22 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                 const int qlo = 64 * hh + 32 * (quad & 1) + 16 * part + 4 * tig;
                 const int qho = 128 + 32 * hh + 16 * part + 4 * tig;
                 const int nsh = quad < 2 ? 0 : 4, hsh = 2 * quad;
-                uint32_t A[2][2];
-                int sc[2][2];
+                uint32_t A[FT][2];
+                int sc[FT][2];
 #pragma unroll
-                for (int f = 0; f < 2; ++f)
+                for (int f = 0; f < FT; ++f)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint8_t* rp = sW + (32 * wr + 16 * f + 8 * h + gid) * WB;
+                        const uint8_t* rp = sW + (16 * FT * wr + 16 * f + 8 * h + gid) * WB;
                         const uint32_t v6 = ((lds32(rp + qlo) >> nsh) & 0x0F0F0F0Fu) | (((lds32(rp + qho) >> hsh) & 0x03030303u) << 4);
                         A[f][h] = __vsub4(v6, 0x20202020u);   // q6 - 32, per byte
                         sc[f][h] = (int)reinterpret_cast<const int8_t*>(rp + 192)[jg];
                     }
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const uint32_t B = lds32(sX + (16 * wc + 8 * j + gid) * kXStride + 16 * jg + 4 * tig);
+                for (int j = 0; j < JT; ++j) {
+                    const uint32_t B = lds32(sX + (8 * JT * wc + 8 * j + gid) * kXStride + 16 * jg + 4 * tig);
 #pragma unroll
-                    for (int f = 0; f < 2; ++f) {
+                    for (int f = 0; f < FT; ++f) {
                         int c[4] = {0, 0, 0, 0};
                         mma_k16(c, A[f], B);
                         sumi[f][j][0] += sc[f][0] * c[0];
@@ -348,31 +358,31 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < JT; ++j)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const float dx = sD[16 * wc + 8 * j + 2 * tig + e];
+                    const float dx = sD[8 * JT * wc + 8 * j + 2 * tig + e];
 #pragma unroll
-                    for (int f = 0; f < 2; ++f)
+                    for (int f = 0; f < FT; ++f)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
                             tree_push(f, j, 2 * h + e, scaled_term(dw[f][h], dx, sumi[f][j][2 * h + e]), bi);
                 }
         } else {   // Q8_0: eight 32-value blocks per step, summed in block order (a GEMV lane's share)
-            float cs[2][2][4];
+            float cs[FT][JT][4];
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < JT; ++j)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) cs[f][j][c] = 0.0f;
 #pragma unroll 2
             for (int ib = 0; ib < 8; ++ib) {
-                uint32_t A[2][4];
-                float dw[2][2];
+                uint32_t A[FT][4];
+                float dw[FT][2];
 #pragma unroll
-                for (int f = 0; f < 2; ++f) {
-                    const uint8_t* r0p = sW + (32 * wr + 16 * f + gid) * WB;
+                for (int f = 0; f < FT; ++f) {
+                    const uint8_t* r0p = sW + (16 * FT * wr + 16 * f + gid) * WB;
                     const uint8_t* r1p = r0p + 8 * WB;
                     A[f][0] = lds32(r0p + 32 * ib + 4 * tig);
                     A[f][1] = lds32(r1p + 32 * ib + 4 * tig);
@@ -382,13 +392,13 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                     dw[f][1] = h2f(*reinterpret_cast<const uint16_t*>(r1p + 256 + 2 * ib));
                 }
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const uint8_t* xp = sX + (16 * wc + 8 * j + gid) * kXStride + 32 * ib + 4 * tig;
+                for (int j = 0; j < JT; ++j) {
+                    const uint8_t* xp = sX + (8 * JT * wc + 8 * j + gid) * kXStride + 32 * ib + 4 * tig;
                     const uint32_t B[2] = {lds32(xp), lds32(xp + 16)};
-                    const float dx0 = sD[(16 * wc + 8 * j + 2 * tig) * 8 + ib];
-                    const float dx1 = sD[(16 * wc + 8 * j + 2 * tig + 1) * 8 + ib];
+                    const float dx0 = sD[(8 * JT * wc + 8 * j + 2 * tig) * 8 + ib];
+                    const float dx1 = sD[(8 * JT * wc + 8 * j + 2 * tig + 1) * 8 + ib];
 #pragma unroll
-                    for (int f = 0; f < 2; ++f) {
+                    for (int f = 0; f < FT; ++f) {
                         int c[4] = {0, 0, 0, 0};
                         mma_k32(c, A[f], B);
                         cs[f][j][0] = __fadd_rn(cs[f][j][0], scaled_term(dw[f][0], dx0, c[0]));
@@ -399,28 +409,28 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
                 }
             }
 #pragma unroll
-            for (int f = 0; f < 2; ++f)
+            for (int f = 0; f < FT; ++f)
 #pragma unroll
-                for (int j = 0; j < 2; ++j)
+                for (int j = 0; j < JT; ++j)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) tree_push(f, j, c, cs[f][j][c], bi);
         }
         if (bi != 7 && s + 1 == nsteps) tree_close(bi);   // the row's short last group
-        if (W != T_Q8_0 && s + 1 < nsteps && tid < kBN) reinterpret_cast<float*>(nxt + L::d_off)[tid] = dx_next;
+        if (W != T_Q8_0 && sn < nsteps && tid < kBN) reinterpret_cast<float*>(nxt + L::d_off)[tid] = dx_next;
         __syncthreads();   // the stage is read; the next issue may overwrite it
     }
     // epilogue: bias, residual add (store_out)
 #pragma unroll
-    for (int f = 0; f < 2; ++f)
+    for (int f = 0; f < FT; ++f)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int row = row0 + 32 * wr + 16 * f + 8 * h + gid;
+            const int row = row0 + 16 * FT * wr + 16 * f + 8 * h + gid;
             if (row >= g.rows) continue;
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < JT; ++j)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int t = t0 + 16 * wc + 8 * j + 2 * tig + e;
+                    const int t = t0 + 8 * JT * wc + 8 * j + 2 * tig + e;
                     if (t < T) store_out(g, row, t, acc[f][j][2 * h + e]);
                 }
         }
@@ -430,13 +440,30 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm_q(GemvSeg g, ActQ a, int 
 
 using namespace fb;
 
+template <int W, int BN, int NS, int FT, int JT>
+static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int T, int* err, cudaStream_t st) {
+    constexpr size_t smem = NS * (size_t)StageLayout<W, BN>::bytes;
+    static cudaError_t attr =
+        cudaFuncSetAttribute(k_gemm_q<W, BN, NS, FT, JT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    const dim3 grid((g.rows + kBM - 1) / kBM, (T + BN - 1) / BN);
+    return fbk_launch(k_gemm_q<W, BN, NS, FT, JT>, grid, dim3(256), smem, st, g, a, K, T, err);
+}
+
+// Token tile by call size: up to 32 tokens (batched decode, short prompts)
+// the weight stream bounds the time, so the tile is as narrow as the call and
+// four stages are in flight; longer prompts use 64-token tiles (each weight
+// step serves more tokens) double-buffered.
 template <int W>
 static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, int* err, cudaStream_t st) {
-    constexpr size_t smem = 2 * (size_t)StageLayout<W>::bytes;
-    static cudaError_t attr = cudaFuncSetAttribute(k_gemm_q<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (attr != cudaSuccess) return attr;
-    const dim3 grid((g.rows + kBM - 1) / kBM, (T + kBN - 1) / kBN);
-    return fbk_launch(k_gemm_q<W>, grid, dim3(kGemmThreads), smem, st, g, a, K, T, err);
+    static const int bn_env = [] {
+        const char* e = getenv("FISH_GEMM_BN");
+        return e ? atoi(e) : 0;
+    }();
+    const int bn = bn_env == 16 || bn_env == 32 || bn_env == 64 ? bn_env : (T <= 16 ? 16 : T <= 32 ? 32 : 64);
+    if (bn == 16) return launch_gemm_tile<W, 16, 4, 1, 1>(g, a, K, T, err, st);   // warps of 16 rows x 8 tokens
+    if (bn == 32) return launch_gemm_tile<W, 32, 4, 1, 2>(g, a, K, T, err, st);   // 16 rows x 16 tokens
+    return launch_gemm_tile<W, 64, 2, 2, 2>(g, a, K, T, err, st);                 // 32 rows x 16 tokens
 }
 
 extern "C" int fbk_gemm_eligible(const GemvArgs* a) {

@@ -122,10 +122,11 @@ def test_block_sums_golden_rows(lib, golden, oracle):
 
 
 @pytest.mark.parametrize("t", [8, 12, 14, 0, 1])
-@pytest.mark.parametrize("T", [1, 3, 8, 16, 37, 130])
+@pytest.mark.parametrize("T", [1, 3, 8, 16, 29, 37, 130])
 def test_matmul_vs_oracle(lib, oracle, t, T):
     """T < 16: GEMV kernels; T >= 16: the int8 tensor-core kernel for the
-    quantised types (partial 64-row / 64-token tiles at 300 rows, T = 37, 130)."""
+    quantised types, in its 16-, 32- and 64-token tiles (partial 64-row tiles
+    at 300 rows, partial token tiles at T = 29, 37, 130)."""
     rng = np.random.default_rng(100 * t + T)
     n_in = 512 if t in (0, 1, 8) else 4096
     n_out = 300
@@ -142,20 +143,22 @@ def test_matmul_vs_oracle(lib, oracle, t, T):
 
 @pytest.mark.parametrize("t", [8, 12, 14])
 @pytest.mark.parametrize("n_in", [4096, 3584])
-def test_matmul_rows_batch_invariant(lib, t, n_in):
+@pytest.mark.parametrize("T", [16, 29, 37])
+def test_matmul_rows_batch_invariant(lib, t, n_in, T):
     """A token's outputs are the same bits whatever the number of tokens in
-    the call: the tensor-core kernel (T = 37) adds each block's float term in
-    the GEMV kernels' order (pairwise over a group's blocks, groups in order,
-    +0 for a short last group: 3584 = 1 full + 1 partial group), so it matches
-    the streamed GEMV (T = 1) exactly. This is what makes a prefix-cache hit
-    reproduce a fresh prefill bit for bit."""
+    the call: the tensor-core kernel (T = 16, 29, 37: its 16-, 32- and
+    64-token tiles) adds each block's float term in the GEMV kernels' order
+    (pairwise over a group's blocks, groups in order, +0 for a short last
+    group: 3584 = 1 full + 1 partial group), so it matches the streamed GEMV
+    (T = 1) exactly. This is what makes a prefix-cache hit reproduce a fresh
+    prefill bit for bit."""
     rng = np.random.default_rng(7 * t + n_in)
-    n_out, T = 200, 37
+    n_out = 200
     w = rand_rows(t, n_in, n_out, rng)
     x = rng.standard_normal((T, n_in)).astype(np.float32)
     y = np.zeros((T, n_out), np.float32)
     assert lib.fbx_matmul(t, _p(w), n_in, n_out, _p(x), T, _p(y)) == 0
-    for i in (0, 5, 17, 36):
+    for i in (0, 5, T // 2, T - 1):
         y1 = np.zeros((1, n_out), np.float32)
         xi = np.ascontiguousarray(x[i:i + 1])
         assert lib.fbx_matmul(t, _p(w), n_in, n_out, _p(xi), 1, _p(y1)) == 0
