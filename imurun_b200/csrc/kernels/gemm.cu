@@ -17,7 +17,8 @@
 // groups in order; Q8_0: each eighth of a group summed in block order first),
 // so a row's value does not depend on the number of tokens in the call.
 //
-// CTA tile 64 rows x BN tokens, 8 warps of 16 FT rows x 8 JT tokens; BN = 64
+// CTA tile BM (64, or 32 for small matrices) rows x BN tokens, warps of 16 FT
+// rows x 8 JT tokens; BN = 64
 // (warps of 32 x 16) for long prompts (compute-bound), 16 or 32 (warps of
 // 16 x 8, 16 x 16) for batched decode and short prompts, which the weight
 // stream bounds: narrower token tiles and a deeper pipeline. Each K step is one 256-value block (8 Q8_0 blocks): the CTA's
@@ -37,7 +38,6 @@
 
 namespace fb {
 
-constexpr int kBM = 64;   // rows per CTA
 constexpr int kXStride = 272;   // bytes per token row of activations in shared memory (256 + pad)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -84,26 +84,26 @@ struct Step<T_Q8_0> {
 };
 
 
-// Shared-memory stage of one K step: weights [64][WB], activations
+// Shared-memory stage of one K step: weights [BM][WB], activations
 // [BN][272], per-token scales (dx, or 8 d32 for Q8_0) [BN][8] f32, Q4_K
 // 32-value activation sums [BN][8] i16.
-template <int W, int BN>
+template <int W, int BM, int BN>
 struct StageLayout {
     static constexpr int WB = Step<W>::wbytes;
     static constexpr int w_off = 0;
-    static constexpr int x_off = kBM * WB;
+    static constexpr int x_off = BM * WB;
     static constexpr int d_off = x_off + BN * kXStride;
     static constexpr int b_off = d_off + BN * 8 * 4;
     static constexpr int bytes = b_off + BN * 16;
 };
 
-template <int W, int BN, int NS, int FT, int JT>
-__global__ void __launch_bounds__(256) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err) {
-    using L = StageLayout<W, BN>;
+template <int W, int BM, int BN, int NS, int FT, int JT>
+__global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err) {
+    using L = StageLayout<W, BM, BN>;
     constexpr int WB = L::WB;
-    // 8 warps, each 16 FT rows x 8 JT tokens: 64 / (16 FT) along rows
-    constexpr int kBN = BN, kGemmThreads = 256, WRN = 4 / FT;
-    static_assert(WRN * (BN / (8 * JT)) == 8, "8 warps cover the 64 x BN tile");
+    // warps of 16 FT rows x 8 JT tokens: BM / (16 FT) along rows, BN / (8 JT) along tokens
+    constexpr int kBM = BM, kBN = BN, WRN = BM / (16 * FT), kGemmThreads = 32 * WRN * (BN / (8 * JT));
+    static_assert(WRN * 16 * FT == BM && (BN / (8 * JT)) * 8 * JT == BN, "warps tile the BM x BN tile");
     extern __shared__ __align__(128) uint8_t sm[];
     pdl_trigger();
     pdl_wait();
@@ -440,14 +440,22 @@ __global__ void __launch_bounds__(256) k_gemm_q(GemvSeg g, ActQ a, int K, int T,
 
 using namespace fb;
 
-template <int W, int BN, int NS, int FT, int JT>
+static int gemm_num_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 1;
+}
+
+template <int W, int BM, int BN, int NS, int FT, int JT>
 static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int T, int* err, cudaStream_t st) {
-    constexpr size_t smem = NS * (size_t)StageLayout<W, BN>::bytes;
-    static cudaError_t attr =
-        cudaFuncSetAttribute(k_gemm_q<W, BN, NS, FT, JT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    constexpr size_t smem = NS * (size_t)StageLayout<W, BM, BN>::bytes;
+    constexpr int threads = BM * BN / (4 * FT * JT);   // 32 x warps
+    static cudaError_t attr = cudaFuncSetAttribute(k_gemm_q<W, BM, BN, NS, FT, JT>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (attr != cudaSuccess) return attr;
-    const dim3 grid((g.rows + kBM - 1) / kBM, (T + BN - 1) / BN);
-    return fbk_launch(k_gemm_q<W, BN, NS, FT, JT>, grid, dim3(256), smem, st, g, a, K, T, err);
+    const dim3 grid((g.rows + BM - 1) / BM, (T + BN - 1) / BN);
+    return fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT>, grid, dim3(threads), smem, st, g, a, K, T, err);
 }
 
 // Token tile by call size: up to 32 tokens (batched decode, short prompts)
@@ -461,9 +469,15 @@ static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, in
         return e ? atoi(e) : 0;
     }();
     const int bn = bn_env == 16 || bn_env == 32 || bn_env == 64 ? bn_env : (T <= 16 ? 16 : T <= 32 ? 32 : 64);
-    if (bn == 16) return launch_gemm_tile<W, 16, 4, 1, 1>(g, a, K, T, err, st);   // warps of 16 rows x 8 tokens
-    if (bn == 32) return launch_gemm_tile<W, 32, 4, 1, 2>(g, a, K, T, err, st);   // 16 rows x 16 tokens
-    return launch_gemm_tile<W, 64, 2, 2, 2>(g, a, K, T, err, st);                 // 32 rows x 16 tokens
+    // narrow token tiles on matrices with fewer 64-row tiles than SMs:
+    // 32-row tiles, so twice the CTAs share the long K loop
+    static const int sms = gemm_num_sms();
+    const bool rows32 = bn < 64 && (g.rows + 63) / 64 < sms;
+    if (bn == 16) return rows32 ? launch_gemm_tile<W, 32, 16, 4, 1, 1>(g, a, K, T, err, st)    // 4 warps of 16 x 8
+                                : launch_gemm_tile<W, 64, 16, 4, 1, 1>(g, a, K, T, err, st);   // 8 warps of 16 x 8
+    if (bn == 32) return rows32 ? launch_gemm_tile<W, 32, 32, 4, 1, 2>(g, a, K, T, err, st)    // 4 warps of 16 x 16
+                                : launch_gemm_tile<W, 64, 32, 4, 1, 2>(g, a, K, T, err, st);   // 8 warps of 16 x 16
+    return launch_gemm_tile<W, 64, 64, 2, 2, 2>(g, a, K, T, err, st);                           // 8 warps of 32 x 16
 }
 
 extern "C" int fbk_gemm_eligible(const GemvArgs* a) {

@@ -142,6 +142,24 @@ def test_matmul_vs_oracle(lib, oracle, t, T):
 
 
 @pytest.mark.parametrize("t", [8, 12, 14])
+@pytest.mark.parametrize("T", [16, 29])
+def test_matmul_tall_small_batch(lib, oracle, t, T):
+    """A matrix with more 64-row tiles than SMs (9500 rows): the tensor-core
+    kernel's 64-row tiles with 16- and 32-token widths (smaller matrices take
+    32-row tiles), against the oracle."""
+    rng = np.random.default_rng(31 * t + T)
+    n_in, n_out = 256, 9500
+    w = rand_rows(t, n_in, n_out, rng)
+    x = rng.standard_normal((T, n_in)).astype(np.float32)
+    y = np.zeros((T, n_out), np.float32)
+    assert lib.fbx_matmul(t, _p(w), n_in, n_out, _p(x), T, _p(y)) == 0
+    want = oracle.matmul(t, w, x, n_in, n_out)
+    wd = np.stack([oracle.dequant(t, w[r], n_in) for r in range(n_out)])
+    mass = np.abs(x) @ np.abs(wd).T + 1e-9
+    assert np.all(np.abs(y - want) <= 1e-5 * mass), float(np.max(np.abs(y - want) / mass))
+
+
+@pytest.mark.parametrize("t", [8, 12, 14])
 @pytest.mark.parametrize("n_in", [4096, 3584])
 @pytest.mark.parametrize("T", [16, 29, 37])
 def test_matmul_rows_batch_invariant(lib, t, n_in, T):
