@@ -596,6 +596,12 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMalloc(&greedy_out_, sizeof(int32_t) * greedy_cap_));
     CK(cudaMalloc(&greedy_step_, sizeof(int32_t)));
     CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * 3 * kMaxBatch));
+    // the kernels' shared error flag is allocated on first use; make that use
+    // now, so a context's first launches may be inside a graph capture
+    if (!fbk_gemv_error_flag()) {
+        if (err) *err = "error flag allocation failed";
+        return false;
+    }
 
     // KV pool
     kv_f16_ = env_int("FISH_KV_F32", 0) == 0;

@@ -72,6 +72,23 @@ def prefill(tokens: int, layers: int) -> dict:
     return {"tokens": tokens, "layers": layers, "seconds": round(dt, 5), "tok_s": round(tokens / dt, 1)}
 
 
+def greedy(layers: int, steps: int) -> dict:
+    """Greedy decode from an empty context on a Llama-3-8B-shaped model of
+    `layers` layers: with no prefill, the first streamed-GEMV launches are
+    layer 0's qkv, o, gate/up and down (a small case for ncu captures)."""
+    import os
+    import time
+    from . import synth
+    from .native import Model
+    cfg = synth.preset("llama8b") if layers == 32 else synth.preset("llama8b", layers=layers)
+    path = synth.cached(cfg, os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    with Model(path, 1024) as m:
+        t0 = time.perf_counter()
+        out = m.greedy(5, steps)
+        dt = time.perf_counter() - t0
+    return {"layers": layers, "steps": steps, "ids": [int(v) for v in out], "seconds": round(dt, 5)}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -90,9 +107,15 @@ def main() -> None:
     pf = sub.add_parser("prefill")
     pf.add_argument("--tokens", type=int, default=512)
     pf.add_argument("--layers", type=int, default=32)
+    gr = sub.add_parser("greedy")
+    gr.add_argument("--layers", type=int, default=2)
+    gr.add_argument("--steps", type=int, default=3)
     a = ap.parse_args()
     if a.cmd == "prefill":
         print(json.dumps(prefill(a.tokens, a.layers)), flush=True)
+        return
+    if a.cmd == "greedy":
+        print(json.dumps(greedy(a.layers, a.steps)), flush=True)
         return
     lib = native.load_library()
     if a.cmd == "matmul":

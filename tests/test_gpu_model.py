@@ -19,9 +19,12 @@ each test:
 from __future__ import annotations
 
 import os
+from pathlib import Path
 
 import numpy as np
 import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
 
 pytestmark = pytest.mark.gpu
 
@@ -108,6 +111,26 @@ def test_greedy_device_loop_matches_teacher_forced(gpu, tiny_gguf):
         _, am = m.decode(np.array(chain, np.int32), 64, logits=False)
         # batched teacher-forced argmax equals the device greedy chain
         assert np.array_equal(am, out)
+
+
+def test_greedy_on_a_fresh_process_and_context(gpu, tiny_gguf):
+    """The first kernel launches of a process may be inside the greedy loop's
+    graph capture (no prefill before it): nothing may allocate there. Run in
+    a child process, so no earlier test has made the first launches."""
+    import subprocess
+    import sys
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path.insert(0, {str(ROOT)!r})\n"
+        "from imurun_b200.native import Model\n"
+        f"with Model({str(tiny_gguf)!r}, 256) as m:\n"
+        "    out = m.greedy(5, 8)\n"
+        "    m.set_kv_len(0)\n"
+        "    _, am = m.decode(np.array([5] + list(out[:-1]), np.int32), 0, logits=False)\n"
+        "    assert np.array_equal(am, out), (list(am), list(out))\n"
+        "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 def test_llama8b_shape_two_layers_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
