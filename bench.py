@@ -320,6 +320,103 @@ def run_ours(args):
     return 0
 
 
+# Sharded workloads (one model over the ranks): preset, decode batch, prompt.
+SHARDED = {
+    "llama70b-tp": ("llama70b", 32, 4096, "Llama-3-70B-shaped Q4_K_M (80 L, d 8192, 64/8 heads, FFN 28672, "
+                    "vocab 128256), tensor-parallel over heads / FFN rows / vocab rows"),
+    "mixtral-ep": ("mixtral", 16, 1024, "Mixtral-8x7B-shaped Q4_K_M (32 L, d 4096, 32/8 heads, 8 experts top-2, "
+                   "expert FFN 14336, vocab 32000), experts split over the ranks, attention by heads"),
+}
+
+
+def run_sharded(args):
+    """One model sharded over WORLD GPUs (tensor or expert parallelism; one
+    process per GPU, NCCL group id from rank 0 over the gloo group): B
+    sessions fork one shared random prompt (its KV pages referenced, not
+    copied), then batched greedy decode steps. Every rank makes the same
+    calls; each step's device time is the batch graph's CUDA-event time on the
+    engine stream, max over ranks. value = B tokens per step / step time."""
+    from imurun_b200 import native, synth
+    from imurun_b200.native import Model
+    preset, B, prompt, desc = SHARDED[args.workload]
+    B = args.batch or B
+    prompt = args.prompt or prompt
+    dist = dist_init()
+    cfg = synth.preset(preset, layers=args.layers) if args.layers else synth.preset(preset)
+    if args.layers:
+        desc += f"; TRUNCATED to {args.layers} layers (plumbing check, not the config)"
+    d = os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")
+    if RANK == 0:
+        t0 = time.time()
+        p = synth.cached(cfg, d)
+        log(f"[bench] model {p} ({p.stat().st_size / 1e9:.2f} GB, {time.time() - t0:.1f} s)")
+    barrier(dist)
+    path = synth.cached(cfg, d)
+    lib = native.load_library()
+    gid = None
+    if WORLD > 1:
+        obj = [native.tp_unique_id(lib) if RANK == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        gid = obj[0]
+    K, W = args.steps, args.warmup
+    n_ctx = (prompt + W + K + 2 + 255) // 256 * 256
+    t0 = time.time()
+    m = Model(path, n_ctx, lib=lib, tp=(RANK, WORLD, gid) if WORLD > 1 else None)
+    load_s = time.time() - t0
+    ids = np.random.default_rng(4321).integers(3, m.vocab, prompt).astype(np.int32)   # same on every rank
+    barrier(dist)
+    t0 = time.perf_counter()
+    lg = m.prefill(ids, 0)
+    prefill_s = max_over_ranks(dist, time.perf_counter() - t0)
+    sids = [0] + [m.session_fork(0, prompt) for _ in range(B - 1)]
+    tok = np.full(B, int(np.argmax(lg)), np.int32)
+    for _ in range(W):
+        tok = m.decode_batch(sids, tok)[0]
+    barrier(dist)
+    clocks = Clocks()
+    clocks.start()
+    dev_ms = 0.0
+    t0 = time.perf_counter()
+    for _ in range(K):
+        tok = m.decode_batch(sids, tok)[0]
+        dev_ms += float(json.loads(m.lib.fish_engine_json(m.ctx).decode())["last_batch_device_ms"])
+    wall_s = time.perf_counter() - t0
+    clk = clocks.stop()
+    barrier(dist)
+    dev_ms_max = max_over_ranks(dist, dev_ms)
+    wall_s = max_over_ranks(dist, wall_s)
+    eng = json.loads(m.lib.fish_engine_json(m.ctx).decode())
+    wbytes = float(eng["weights_device_bytes"])
+    m.close()
+    peak, peak_kind = peaks()
+    step_s = dev_ms_max / K / 1e3
+    if RANK == 0:
+        line = {
+            "metric": BASELINE["metric"], "value": round(B / step_s, 3), "unit": "tok/s", "n_gpus": WORLD,
+            "steps": K, "warmup": W, "ms_per_step": round(step_s * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {
+                "workload": f"{desc}; batch {B} sessions forked from one {prompt}-token random prompt, {K} batched "
+                            "greedy decode steps",
+                "global_batch": B, "seq_len": prompt + W + K,
+                "parallelism": f"{'tp' if args.workload.endswith('tp') else 'ep'}{WORLD}",
+                "prefill_tok_s": round(prompt / prefill_s, 1), "load_s": round(load_s, 1),
+                "weights_bytes_per_gpu": wbytes,
+                "weights_gbs_per_gpu": round(wbytes / step_s / 1e9, 1),
+                "hbm_frac_per_gpu": round(wbytes / step_s / 1e9 / peak, 4),
+                "l2": "inputs larger than L2 (the rank's weights are streamed every step)",
+            },
+            "e2e": {"value": round(B * K / wall_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+                    "d2h_bytes_per_step": 4 * B},
+            "peak_kind": peak_kind,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -327,11 +424,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="llama8b", choices=["llama8b"] + sorted(SHARDED),
+                    help="llama8b: the headline config (replicas at N > 1); the others shard one model over N GPUs")
+    ap.add_argument("--batch", type=int, default=0, help="sharded workloads: decode batch (default: the config's)")
+    ap.add_argument("--prompt", type=int, default=0, help="sharded workloads: prompt tokens (default: the config's)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="sharded workloads: truncate the model (a plumbing check; the line says so)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "llama8b":
+        return run_sharded(args)
     return run_ours(args)
 
 

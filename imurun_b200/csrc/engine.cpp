@@ -1466,7 +1466,9 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
     if (!upload_tokens(ids, sids, pos.data(), n, err)) return false;
     if (use_graphs_) {
         if (!graphs_.count(n) && !capture_graph(n, err)) return false;
+        CK(cudaEventRecord(ev0_, stream_));
         CK(cudaGraphLaunch(graphs_[n], stream_));
+        CK(cudaEventRecord(ev1_, stream_));
     } else {
         int max_ctx = 0;
         for (int i = 0; i < n; ++i) max_ctx = std::max(max_ctx, pos[i] + 1);
@@ -1478,6 +1480,7 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
     if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, stream_));
     if (logits) CK(cudaMemcpyAsync(logits, logits_, sizeof(float) * (size_t)n * c.vocab, cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    if (use_graphs_) cudaEventElapsedTime(&last_batch_ms_, ev0_, ev1_);
     for (int i = 0; i < n; ++i) seqs_[sids[i]].len += 1;
     return true;
 }

@@ -136,6 +136,7 @@ public:
     int decode_greedy(int sid, int32_t first, int n_steps, int32_t* out, std::string* err);
     // Device time (CUDA events on the engine stream) of the last greedy run.
     float last_greedy_ms() const { return last_greedy_ms_; }
+    float last_batch_ms() const { return last_batch_ms_; }   // device time of the last batched decode step
     // Kernel nodes of the captured step graph for T tokens (0 if none yet).
     int graph_kernels(int T) const {
         auto it = graph_kernels_.find(T);
@@ -273,6 +274,7 @@ private:
     float last_step_ms_ = 0.0f;
     unsigned long long* step_trace_ = nullptr;
     float last_greedy_ms_ = 0.0f;
+    float last_batch_ms_ = 0.0f;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     std::vector<ProfClass>* prof_ = nullptr;
     cudaEvent_t pe0_ = nullptr, pe1_ = nullptr;

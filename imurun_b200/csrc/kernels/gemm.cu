@@ -85,16 +85,14 @@ struct Step<T_Q8_0> {
 
 
 // Shared-memory stage of one K step: weights [BM][WB], activations
-// [BN][272], per-token scales (dx, or 8 d32 for Q8_0) [BN][8] f32, Q4_K
-// 32-value activation sums [BN][8] i16.
+// [BN][272], per-token scales (dx, or 8 d32 for Q8_0) [BN][8] f32.
 template <int W, int BM, int BN>
 struct StageLayout {
     static constexpr int WB = Step<W>::wbytes;
     static constexpr int w_off = 0;
     static constexpr int x_off = BM * WB;
     static constexpr int d_off = x_off + BN * kXStride;
-    static constexpr int b_off = d_off + BN * 8 * 4;
-    static constexpr int bytes = b_off + BN * 16;
+    static constexpr int bytes = d_off + BN * 8 * 4;
 };
 
 template <int W, int BM, int BN, int NS, int FT, int JT>
@@ -154,14 +152,6 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                 cp_async16(b + L::d_off + n * 32 + 16 * c, src, ok);
             }
         } else {
-            if (W == T_Q4_K) {
-                for (int i = tid; i < kBN; i += kGemmThreads) {
-                    const int t = t0 + i;
-                    const bool ok = t < T;
-                    const void* src = ok ? (const void*)(a.bsk + (size_t)t * (K / 32) + 8 * s) : (const void*)a.bsk;
-                    cp_async16(b + L::b_off + 16 * i, src, ok);
-                }
-            }
             if (tid < kBN && t0 + tid < T) dxv = __ldg(a.dk + (size_t)(t0 + tid) * (K / 256) + s);
         }
         cp_async_commit();
@@ -252,16 +242,25 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     schi[f][h] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
                     mhi[f][h] = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
                 }
-            int sumi[FT][JT][4];
+            // mins = sum_g m_g bsums_g = sum_l m_g(l) x_l: one more MMA per
+            // sub-block with m_g in every byte of its A fragment, accumulated
+            // in the MMA (exact integers, as sumi)
+            int sumi[FT][JT][4], mn[FT][JT][4];
 #pragma unroll
             for (int f = 0; f < FT; ++f)
 #pragma unroll
                 for (int j = 0; j < JT; ++j)
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) sumi[f][j][c] = 0;
+                    for (int c = 0; c < 4; ++c) sumi[f][j][c] = mn[f][j][c] = 0;
 #pragma unroll
             for (int gq = 0; gq < 8; ++gq) {
                 const int qoff = 16 + 32 * (gq >> 1), sh = (gq & 1) ? 4 : 0;
+                uint32_t Am[FT][4];
+#pragma unroll
+                for (int f = 0; f < FT; ++f) {
+                    Am[f][0] = Am[f][2] = (uint32_t)byte_of(gq < 4 ? mlo[f][0] : mhi[f][0], gq & 3) * 0x01010101u;
+                    Am[f][1] = Am[f][3] = (uint32_t)byte_of(gq < 4 ? mlo[f][1] : mhi[f][1], gq & 3) * 0x01010101u;
+                }
                 uint32_t A[FT][4];
 #pragma unroll
                 for (int f = 0; f < FT; ++f) {
@@ -286,30 +285,22 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                         sumi[f][j][1] += s0 * c[1];
                         sumi[f][j][2] += s1 * c[2];
                         sumi[f][j][3] += s1 * c[3];
+                        mma_k32(mn[f][j], Am[f], B);
                     }
                 }
             }
-            // mins = sum_g m_g bsums_g, then the block's float term
+            // the block's float term
 #pragma unroll
             for (int j = 0; j < JT; ++j) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int n = 8 * JT * wc + 8 * j + 2 * tig + e;
-                    const uint4 bw = *reinterpret_cast<const uint4*>(cur + L::b_off + 16 * n);
-                    const float dx = sD[n];
+                    const float dx = sD[8 * JT * wc + 8 * j + 2 * tig + e];
 #pragma unroll
                     for (int f = 0; f < FT; ++f)
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            int mins = 0;
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const uint32_t wq = word_of(bw, q);
-                                mins += byte_of(q < 2 ? mlo[f][h] : mhi[f][h], (2 * q) & 3) * (int)(int16_t)(wq & 0xFFFFu);
-                                mins += byte_of(q < 2 ? mlo[f][h] : mhi[f][h], (2 * q + 1) & 3) * (int)(int16_t)(wq >> 16);
-                            }
-                            tree_push(f, j, 2 * h + e, q4k_term(dw[f][h], dmw[f][h], dx, sumi[f][j][2 * h + e], mins), bi);
-                        }
+                        for (int h = 0; h < 2; ++h)
+                            tree_push(f, j, 2 * h + e,
+                                      q4k_term(dw[f][h], dmw[f][h], dx, sumi[f][j][2 * h + e], mn[f][j][2 * h + e]), bi);
                 }
             }
         } else if (W == T_Q6_K) {
