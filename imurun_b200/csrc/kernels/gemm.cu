@@ -171,8 +171,28 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                 pa[f][j][c] = pb[f][j][c] = pc[f][j][c] = 0.0f;
             }
     // The GEMV order for the 8 terms t0..t7 of a group:
-    //   ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7)), then acc += group
-    auto tree_push = [&](int f, int j, int c, float t, int bi) {
+    //   ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7)), then acc += group.
+    // Block bi of the group is the same for the whole CTA: one branch per
+    // block, every output inside it.
+    auto tree_push = [&](const float (&t)[FT][JT][4], int bi) {
+#define FB_EACH for (int f = 0; f < FT; ++f) for (int j = 0; j < JT; ++j) for (int c = 0; c < 4; ++c)
+        switch (bi) {
+            case 0: _Pragma("unroll") FB_EACH pa[f][j][c] = t[f][j][c]; break;
+            case 1: _Pragma("unroll") FB_EACH pa[f][j][c] = __fadd_rn(pa[f][j][c], t[f][j][c]); break;
+            case 2: _Pragma("unroll") FB_EACH pc[f][j][c] = t[f][j][c]; break;
+            case 3: _Pragma("unroll") FB_EACH pa[f][j][c] = __fadd_rn(pa[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c])); break;
+            case 4: _Pragma("unroll") FB_EACH pb[f][j][c] = t[f][j][c]; break;
+            case 5: _Pragma("unroll") FB_EACH pb[f][j][c] = __fadd_rn(pb[f][j][c], t[f][j][c]); break;
+            case 6: _Pragma("unroll") FB_EACH pc[f][j][c] = t[f][j][c]; break;
+            default:
+                _Pragma("unroll") FB_EACH acc[f][j][c] = __fadd_rn(
+                    acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c]))));
+        }
+#undef FB_EACH
+    };
+    // the same steps for one output (the Q6_K path: its 16 scale groups
+    // leave fewer registers for a whole tile of terms)
+    auto tree_push1 = [&](int f, int j, int c, float t, int bi) {
         switch (bi) {
             case 0: pa[f][j][c] = t; break;
             case 1: pa[f][j][c] = __fadd_rn(pa[f][j][c], t); break;
@@ -181,22 +201,21 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
             case 4: pb[f][j][c] = t; break;
             case 5: pb[f][j][c] = __fadd_rn(pb[f][j][c], t); break;
             case 6: pc[f][j][c] = t; break;
-            default: {
-                const float grp = __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t)));
-                acc[f][j][c] = __fadd_rn(acc[f][j][c], grp);
-            }
+            default:
+                acc[f][j][c] = __fadd_rn(acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t))));
         }
     };
     // after block bi of a group that ends there (bi < 7: the row's last
     // group is short; the GEMV adds +0 for its missing blocks)
     auto tree_close = [&](int bi) {
+        float zero[FT][JT][4];
 #pragma unroll
         for (int f = 0; f < FT; ++f)
 #pragma unroll
             for (int j = 0; j < JT; ++j)
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    for (int z = bi + 1; z < 8; ++z) tree_push(f, j, c, 0.0f, z);
+                for (int c = 0; c < 4; ++c) zero[f][j][c] = 0.0f;
+        for (int z = bi + 1; z < 8; ++z) tree_push(zero, z);
     };
 
     // steps 0 .. NS-2 in flight before the loop; every iteration commits one
@@ -289,7 +308,8 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     }
                 }
             }
-            // the block's float term
+            // the block's float terms
+            float tt[FT][JT][4];
 #pragma unroll
             for (int j = 0; j < JT; ++j) {
 #pragma unroll
@@ -299,10 +319,10 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     for (int f = 0; f < FT; ++f)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
-                            tree_push(f, j, 2 * h + e,
-                                      q4k_term(dw[f][h], dmw[f][h], dx, sumi[f][j][2 * h + e], mn[f][j][2 * h + e]), bi);
+                            tt[f][j][2 * h + e] = q4k_term(dw[f][h], dmw[f][h], dx, sumi[f][j][2 * h + e], mn[f][j][2 * h + e]);
                 }
             }
+            tree_push(tt, bi);
         } else if (W == T_Q6_K) {
             float dw[FT][2];
 #pragma unroll
@@ -357,7 +377,7 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     for (int f = 0; f < FT; ++f)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
-                            tree_push(f, j, 2 * h + e, scaled_term(dw[f][h], dx, sumi[f][j][2 * h + e]), bi);
+                            tree_push1(f, j, 2 * h + e, scaled_term(dw[f][h], dx, sumi[f][j][2 * h + e]), bi);
                 }
         } else {   // Q8_0: eight 32-value blocks per step, summed in block order (a GEMV lane's share)
             float cs[FT][JT][4];
@@ -399,12 +419,7 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     }
                 }
             }
-#pragma unroll
-            for (int f = 0; f < FT; ++f)
-#pragma unroll
-                for (int j = 0; j < JT; ++j)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tree_push(f, j, c, cs[f][j][c], bi);
+            tree_push(cs, bi);
         }
         if (bi != 7 && s + 1 == nsteps) tree_close(bi);   // the row's short last group
         if (W != T_Q8_0 && sn < nsteps && tid < kBN) reinterpret_cast<float*>(nxt + L::d_off)[tid] = dx_next;
