@@ -9,7 +9,9 @@ the cross-rank sums differs from one GPU, and on this random-init model a
 1-ulp difference re-quantises to a different int8 activation now and then
 (the CPU-vs-CPU floor of test_llama8b_shape_two_layers_vs_oracle): the bar is
 max |dlogit| <= 3% of max |logit|, median <= 0.03, argmax equal where the
-margin clears the bar. Exact: the device-side greedy loop (max-reduced keys)
+margin clears the bar; the logits compared are the prefill's, the
+teacher-forced decode steps' and two batched steps of three sessions forked
+from the prompt. Exact: the device-side greedy loop (max-reduced keys)
 reproduces the same run's teacher-forced argmax ids.
 """
 from __future__ import annotations

@@ -5,7 +5,8 @@
 Runs on the GPU named by CUDA_VISIBLE_DEVICES. Rank 0 creates the NCCL group
 id and writes it to IDFILE; the other ranks wait for it (bounded). Every rank
 makes the same calls in the same order: prefill, teacher-forced decode steps,
-a greedy loop. Rank 0 writes the logits and ids to OUT (.npz).
+a greedy loop, batched decode of sessions forked from the prompt. Rank 0
+writes the logits and ids to OUT (.npz).
 """
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from imurun_b200 import native  # noqa: E402
 
-N_PROMPT, N_DEC, N_GREEDY = 40, 4, 8
+N_PROMPT, N_DEC, N_GREEDY = 40, 6, 8
 
 
 def main() -> int:
@@ -58,6 +59,13 @@ def main() -> int:
             _, a = m.decode(np.array([tok], np.int32), N_PROMPT + N_DEC + s)
             tok = int(a[0])
             forced.append(tok)
+        # batched decode: three sessions forked from the prompt, fed the same
+        # ids on every run (not their argmax, which may differ where the
+        # margin is below the bar)
+        sids = [m.session_fork(0, N_PROMPT) for _ in range(3)]
+        for k in range(2):
+            _, blg = m.decode_batch(sids, ids[N_PROMPT + 3 * k:N_PROMPT + 3 * k + 3], logits=True)
+            steps.extend(blg.copy())
     if rank == 0:
         np.savez(out, logits=np.stack(steps), argmax=np.array(am, np.int32), greedy=np.asarray(greedy, np.int32),
                  forced=np.array(forced, np.int32), ids=ids)
