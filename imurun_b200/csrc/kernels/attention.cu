@@ -8,6 +8,7 @@
 // paged (P positions per page, every layer of a position range in one page)
 // and fp16 or f32.
 #include <cooperative_groups.h>
+#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -1055,9 +1056,15 @@ extern "C" int fbk_rope_append(float* q, int ldq, const float* k, const float* v
 // number of splits (and the combine's work) stays <= 64.
 static int attn_warps(int max_ctx) { return max_ctx > 2048 ? 4 : 1; }
 
+// Scratch for calls of up to T tokens at any context up to max_ctx: a
+// context of at most 2048 keys splits them 32 a CTA, a longer one 128 a CTA,
+// so the most splits are at min(max_ctx, 2048) or at max_ctx.
 extern "C" size_t fbk_attention_scratch_floats(int T, int H, int D, int max_ctx) {
-    const int nw = attn_warps(max_ctx);
-    const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
+    int n_splits = 0;
+    for (const int ctx : {std::min(max_ctx, 2048), max_ctx}) {
+        const int nw = attn_warps(ctx);
+        n_splits = std::max(n_splits, (ctx + 32 * nw - 1) / (32 * nw));
+    }
     return (size_t)T * H * n_splits * (D + 2);
 }
 

@@ -113,6 +113,21 @@ def test_greedy_device_loop_matches_teacher_forced(gpu, tiny_gguf):
         assert np.array_equal(am, out)
 
 
+def test_prefill_below_2048_keys_in_a_longer_context(gpu, tiny_gguf):
+    """A context longer than 2048 positions with a prompt between a quarter of
+    it and 2048 tokens: prefill attention then splits the keys 32 a CTA, more
+    splits than the longest context needs, and its scratch must hold them.
+    The result equals the same prefill in a 2048-position context (same
+    splits, same bits)."""
+    from imurun_b200.native import Model
+    ids = np.random.default_rng(11).integers(3, 32000, 1500).astype(np.int32)
+    with Model(tiny_gguf, 4096) as m:
+        long_ctx = m.prefill(ids, 0)
+    with Model(tiny_gguf, 2048) as m:
+        short_ctx = m.prefill(ids, 0)
+    assert np.array_equal(long_ctx, short_ctx)
+
+
 def test_greedy_on_a_fresh_process_and_context(gpu, tiny_gguf):
     """The first kernel launches of a process may be inside the greedy loop's
     graph capture (no prefill before it): nothing may allocate there. Run in
