@@ -27,8 +27,11 @@ ROOT = Path(__file__).resolve().parent
 LOCAL_RANK = int(os.environ.get("LOCAL_RANK", "0"))
 RANK = int(os.environ.get("RANK", "0"))
 WORLD = int(os.environ.get("WORLD_SIZE", "1"))
-if WORLD > 1 and "CUDA_VISIBLE_DEVICES" not in os.environ:
-    os.environ["CUDA_VISIBLE_DEVICES"] = str(LOCAL_RANK)
+if WORLD > 1:
+    # one GPU per rank: the LOCAL_RANK-th of the visible devices (all of
+    # them when the variable is unset), set before any CUDA call
+    _vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    os.environ["CUDA_VISIBLE_DEVICES"] = _vis[LOCAL_RANK % len(_vis)] if _vis else str(LOCAL_RANK)
 sys.path.insert(0, str(ROOT))
 
 import numpy as np  # noqa: E402
