@@ -69,6 +69,16 @@ def barrier(dist):
         dist.barrier()
 
 
+def share_group_id(dist, make):
+    """Rank 0 makes the NCCL group id (make()); every rank receives it over
+    the gloo group. None without a process group."""
+    if dist is None:
+        return None
+    obj = [make() if RANK == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def model_path(dist):
     from imurun_b200 import synth
     cfg = synth.preset("llama8b")
@@ -356,11 +366,7 @@ def run_sharded(args):
     barrier(dist)
     path = synth.cached(cfg, d)
     lib = native.load_library()
-    gid = None
-    if WORLD > 1:
-        obj = [native.tp_unique_id(lib) if RANK == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        gid = obj[0]
+    gid = share_group_id(dist, lambda: native.tp_unique_id(lib))
     K, W = args.steps, args.warmup
     n_ctx = (prompt + W + K + 2 + 255) // 256 * 256
     t0 = time.time()
