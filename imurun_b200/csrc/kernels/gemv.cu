@@ -17,9 +17,12 @@
 //                  pair of them takes every fourth stage (4 rows x 8 blocks
 //                  a warp, one block per lane). Per-stage row partials go to
 //                  shared memory and are summed over groups at the end in a
-//                  fixed order.
-//   k_gemv_direct  T = 5..15 and F32/F16 rows, plain loads (T >= 16 on
-//                  quantised rows: the tensor-core kernel, gemm.cu).
+//                  fixed order. Single-token launches use a variant compiled
+//                  for their weight-type set and prologue mode.
+//   k_gemv_direct  F32/F16 rows (up to 8 tokens), plain loads. Quantised
+//                  calls of 5-15 tokens run as 4-token streamed launches
+//                  (fbk_gemv_chunk); 16 or more go to the tensor-core
+//                  kernel (gemm.cu).
 // Launches carry the programmatic-dependent-launch attribute when the caller
 // asks for it: the producer streams weights before the previous kernel has
 // finished (weights never change); everything that reads activations or
