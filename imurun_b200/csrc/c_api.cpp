@@ -554,7 +554,9 @@ int fish_decode_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0, float* l
     e.seq_truncate(0, pos0);
     ctx->cache_ids.resize(std::min(ctx->cache_ids.size(), (size_t)pos0));
     std::string err;
-    if (!e.forward(0, ids, n, ctx->logits.data(), logits_all, argmax_out, &err)) { ctx->err = err; return -2; }
+    // only what the caller asked for crosses back (the last row of logits is
+    // 513 KB for a 128k vocabulary; no later call reads it from the context)
+    if (!e.forward(0, ids, n, nullptr, logits_all, argmax_out, &err)) { ctx->err = err; return -2; }
     ctx->cache_ids.insert(ctx->cache_ids.end(), ids, ids + n);
     return 0;
 }
