@@ -216,9 +216,12 @@ FISH_API int  fish_session_pages(fish_ctx* ctx, int session, int32_t* out, int c
 FISH_API int  fish_kv_page_size(fish_ctx* ctx);
 
 /* Engine state as one JSON object: device, KV pool pages (total / free),
- * kernels per captured step graph, and the device time (CUDA events on the
- * engine's stream) of the last fish_decode_greedy call. The pointer is valid
- * until the next call on the same thread. */
+ * weight bytes on the device, kernels per captured step graph, the device
+ * times (CUDA events on the engine's stream) of the last fish_decode_greedy
+ * call (last_decode_device_ms) and of the last graph-launched
+ * fish_decode_batch step (last_batch_device_ms), kernel error and wait
+ * failure records, the persistent step kernel's state, and tp_world. The
+ * pointer is valid until the next call on the same thread. */
 FISH_API const char* fish_engine_json(fish_ctx* ctx);
 
 /* Per-kernel-class device timing of n_steps single-token decode steps run
