@@ -8,6 +8,7 @@
 // identical prompt -> n-1), prefill in chunks of <= 256, sampled decode with
 // UTF-8-complete streaming callbacks, cancel between forwards, stats.
 #include <fish/c_api.h>
+#include <fish/fish_kernels.h>
 
 #include <sys/resource.h>
 
@@ -389,6 +390,43 @@ const char* fish_chat_format(fish_ctx* ctx) {
     std::lock_guard<std::mutex> lock(ctx->mu);
     if (!ctx->tok) return "none";
     return fb::chat_format_name(ctx->tok->format());
+}
+
+// ------------------------------------------------ tokenizer without a model
+// The tokenizer fish_load would build for the GGUF at `path`, from its
+// metadata alone (no weights read, no device touched).
+static std::unique_ptr<fb::Tokenizer> tokenizer_of(const char* path, std::unique_ptr<fb::Gguf>* g) {
+    if (!path) return nullptr;
+    std::string err;
+    *g = fb::Gguf::open(path, &err);
+    if (!*g) return nullptr;
+    return fb::Tokenizer::create(**g, &err);
+}
+
+int fbx_tokenize_gguf(const char* gguf_path, const char* text, int add_bos, int32_t* out, int cap) {
+    std::unique_ptr<fb::Gguf> g;
+    auto tok = tokenizer_of(gguf_path, &g);
+    if (!tok || !text) return -1;
+    const auto ids = tok->encode(text, add_bos != 0, true);
+    if (!out || cap <= 0) return (int)ids.size();
+    const int n = std::min((int)ids.size(), cap);
+    std::memcpy(out, ids.data(), sizeof(int32_t) * (size_t)n);
+    return n;
+}
+
+int fbx_detokenize_gguf(const char* gguf_path, const int32_t* ids, int n, char* out, int cap) {
+    std::unique_ptr<fb::Gguf> g;
+    auto tok = tokenizer_of(gguf_path, &g);
+    if (!tok || !ids || n < 0) return -1;
+    return write_string(tok->decode(std::vector<int32_t>(ids, ids + n)), out, cap);
+}
+
+int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const char* const* contents, int n,
+                         char* out, int cap) {
+    std::unique_ptr<fb::Gguf> g;
+    auto tok = tokenizer_of(gguf_path, &g);
+    if (!tok || n < 0) return -1;
+    return write_string(tok->apply_chat(to_messages(roles, contents, n), tok->format()), out, cap);
 }
 
 int fish_generate(fish_ctx* ctx, const char* prompt, int add_bos, int max_tokens, float temperature, int top_k,

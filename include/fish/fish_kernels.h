@@ -110,6 +110,19 @@ FISH_API int fbx_argmax(const float* x, int rows, int n, int32_t* out);
  * quant.cpp:470-506) for ids[0..T) of a [n_rows][E] table. */
 FISH_API int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out);
 
+/* Tokenizer of a GGUF file without loading its model: host code only, no
+ * device needed. It is the tokenizer fish_load sets up for the same file
+ * (vocabulary, merges or scores, special tokens, chat template), built from
+ * the GGUF metadata on every call, for tokenizer parity tests and for tools
+ * that only tokenize. Return values as fish_tokenize, fish_detokenize and
+ * fish_chat_prompt (c_api.h), which replace the reference's
+ * (model/fish/include/fish/c_api.h:108-121); -1 when the file or its
+ * tokenizer cannot be read. */
+FISH_API int fbx_tokenize_gguf(const char* gguf_path, const char* text, int add_bos, int32_t* out, int cap);
+FISH_API int fbx_detokenize_gguf(const char* gguf_path, const int32_t* ids, int n, char* out, int cap);
+FISH_API int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const char* const* contents,
+                                  int n, char* out, int cap);
+
 #ifdef __cplusplus
 }
 #endif
