@@ -429,6 +429,26 @@ int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const 
     return write_string(tok->apply_chat(to_messages(roles, contents, n), tok->format()), out, cap);
 }
 
+int fbx_sample(const float* logits, int n_vocab, float temperature, int top_k, float top_p, float repeat_penalty,
+               int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed, int n_draws, int32_t* out) {
+    if (!logits || n_vocab <= 0 || n_draws < 0 || (n_draws > 0 && !out) || n_recent < 0 || (n_recent > 0 && !recent))
+        return -1;
+    fb::SampleParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.repeat_penalty = repeat_penalty;
+    p.repeat_last_n = repeat_last_n;
+    fb::Sampler s(seed);
+    const std::vector<int32_t> rec(recent, recent + n_recent);
+    std::vector<float> work((size_t)n_vocab);
+    for (int i = 0; i < n_draws; ++i) {
+        std::memcpy(work.data(), logits, sizeof(float) * (size_t)n_vocab);
+        out[i] = s.sample(work.data(), n_vocab, p, rec);
+    }
+    return 0;
+}
+
 int fish_generate(fish_ctx* ctx, const char* prompt, int add_bos, int max_tokens, float temperature, int top_k,
                   float top_p, float repeat_penalty, fish_token_cb cb, void* user) {
     if (!ctx || !prompt) return -1;

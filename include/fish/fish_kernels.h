@@ -123,6 +123,17 @@ FISH_API int fbx_detokenize_gguf(const char* gguf_path, const int32_t* ids, int 
 FISH_API int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const char* const* contents,
                                   int n, char* out, int cap);
 
+/* The sampler of fish_generate on host logits (host code only): repetition
+ * penalty over the last repeat_last_n of `recent`, temperature, top-k,
+ * top-p, then a draw from a std::mt19937_64 seeded with `seed` (0: from the
+ * clock), n_draws times with one generator, each draw on a fresh copy of the
+ * logits. Replaces the reference's Sampler::sample
+ * (model/fish/include/fish/sampler.h:26-33). Returns 0, or -1 on bad
+ * arguments. */
+FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int top_k, float top_p,
+                        float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
+                        int n_draws, int32_t* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,10 +12,12 @@
 #include <fish/quant.h>
 #include <fish/ops.h>
 #include <fish/threadpool.h>
+#include <fish/sampler.h>
 
 #include <cstring>
 #include <memory>
 #include <string>
+#include <vector>
 
 using namespace fish;
 
@@ -106,6 +108,28 @@ __attribute__((visibility("default"))) void ref_model_set_kv_len(void* h, int n)
 __attribute__((visibility("default"))) void ref_model_reset(void* h) { static_cast<RefModel*>(h)->m->reset_kv(); }
 __attribute__((visibility("default"))) unsigned long long ref_model_weights_bytes(void* h) {
     return static_cast<RefModel*>(h)->m->weights_bytes();
+}
+/* Sampler::sample (include/fish/sampler.h:26-33) n_draws times with one
+ * Sampler seeded with `seed`, each draw on a fresh copy of the logits (the
+ * call modifies them in place); the ids go to out. */
+__attribute__((visibility("default"))) void ref_sample(const float* logits, int n_vocab, float temperature, int top_k,
+                                                       float top_p, float repeat_penalty, int repeat_last_n,
+                                                       const int32_t* recent, int n_recent, unsigned long long seed,
+                                                       int n_draws, int32_t* out) {
+    SampleParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.repeat_penalty = repeat_penalty;
+    p.repeat_last_n = repeat_last_n;
+    p.seed = seed;
+    Sampler s(seed);
+    std::vector<int32_t> rec(recent, recent + n_recent);
+    std::vector<float> work(static_cast<size_t>(n_vocab));
+    for (int i = 0; i < n_draws; ++i) {
+        std::memcpy(work.data(), logits, sizeof(float) * static_cast<size_t>(n_vocab));
+        out[i] = s.sample(work.data(), n_vocab, p, rec);
+    }
 }
 
 }  // extern "C"
