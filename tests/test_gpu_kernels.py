@@ -161,11 +161,12 @@ def test_matmul_tall_small_batch(lib, oracle, t, T):
 
 @pytest.mark.parametrize("t", [8, 12, 14])
 @pytest.mark.parametrize("n_in", [4096, 3584])
-@pytest.mark.parametrize("T", [16, 29, 37])
+@pytest.mark.parametrize("T", [16, 29, 37, 70])
 def test_matmul_rows_batch_invariant(lib, t, n_in, T):
     """A token's outputs are the same bits whatever the number of tokens in
-    the call: the tensor-core kernel (T = 16, 29, 37: its 16-, 32- and
-    64-token tiles) adds each block's float term in the GEMV kernels' order
+    the call: the tensor-core kernel (T = 16: a 16-token tile; 29, 37: one and
+    two 32-token tiles; 70: 64-token tiles) adds each block's float term in
+    the GEMV kernels' order
     (pairwise over a group's blocks, groups in order, +0 for a short last
     group: 3584 = 1 full + 1 partial group), so it matches the streamed GEMV
     (T = 1) exactly. This is what makes a prefix-cache hit reproduce a fresh
