@@ -429,6 +429,53 @@ int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const 
     return write_string(tok->apply_chat(to_messages(roles, contents, n), tok->format()), out, cap);
 }
 
+// FNV-1a over bytes, for the digest of metadata arrays
+static uint64_t fnv1a(uint64_t h, const void* p, size_t n) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return h;
+}
+
+int fbx_gguf_digest(const char* gguf_path, const char* const* keys, int n_keys, char* out, int cap) {
+    if (!gguf_path || n_keys < 0 || (n_keys > 0 && !keys)) return -1;
+    std::string err;
+    auto g = fb::Gguf::open(gguf_path, &err);
+    if (!g) return -1;
+    std::string d;
+    char line[256];
+    for (const fb::Tensor& t : g->tensors()) {
+        d += "T " + t.name + " " + std::to_string(t.type) + " ";
+        for (size_t i = 0; i < t.ne.size(); ++i) d += (i ? "," : "") + std::to_string(t.ne[i]);
+        std::snprintf(line, sizeof(line), " %llu %llu\n", (unsigned long long)(t.data - g->map_base()),
+                      (unsigned long long)t.nbytes);
+        d += line;
+    }
+    for (int k = 0; k < n_keys; ++k) {
+        const fb::MetaValue* m = keys[k] ? g->meta(keys[k]) : nullptr;
+        d += std::string("K ") + (keys[k] ? keys[k] : "") + " ";
+        if (!m) { d += "missing\n"; continue; }
+        d += std::to_string((int)m->kind) + " ";
+        switch (m->kind) {
+            case fb::MetaValue::UINT: d += std::to_string(m->u); break;
+            case fb::MetaValue::INT: d += std::to_string(m->i); break;
+            case fb::MetaValue::FLOAT: std::snprintf(line, sizeof(line), "%.17g", m->f); d += line; break;
+            case fb::MetaValue::BOOL: d += m->b ? "1" : "0"; break;
+            case fb::MetaValue::STRING: d += m->s; break;
+            default: {
+                uint64_t h = 1469598103934665603ull;
+                for (const std::string& s : m->sarr) h = fnv1a(h, s.c_str(), s.size() + 1);
+                h = fnv1a(h, m->iarr.data(), m->iarr.size() * sizeof(int32_t));
+                h = fnv1a(h, m->farr.data(), m->farr.size() * sizeof(float));
+                std::snprintf(line, sizeof(line), "n=%llu s=%zu i=%zu f=%zu h=%016llx", (unsigned long long)m->count,
+                              m->sarr.size(), m->iarr.size(), m->farr.size(), (unsigned long long)h);
+                d += line;
+            }
+        }
+        d += "\n";
+    }
+    return write_string(d, out, cap);
+}
+
 int fbx_sample(const float* logits, int n_vocab, float temperature, int top_k, float top_p, float repeat_penalty,
                int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed, int n_draws, int32_t* out) {
     if (!logits || n_vocab <= 0 || n_draws < 0 || (n_draws > 0 && !out) || n_recent < 0 || (n_recent > 0 && !recent))

@@ -61,6 +61,7 @@ public:
     const std::vector<Tensor>& tensors() const { return tensors_; }
     const std::string& path() const { return path_; }
     size_t file_size() const { return size_; }
+    const uint8_t* map_base() const { return map_; }   // the file's first byte in the mapping
 
 private:
     Gguf() = default;

@@ -134,6 +134,18 @@ FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int
                         float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
                         int n_draws, int32_t* out);
 
+/* Digest of how this library reads a GGUF file (host code only): one line
+ * per tensor in directory order, "T name type ne0,ne1,.. file_offset nbytes"
+ * (the absolute offset of its data in the file), then one line per key in
+ * `keys`, "K key kind value" (kind as in the GGUF metadata value kinds:
+ * 0 uint, 1 int, 2 float, 3 bool, 4 string, 5 array; arrays as their length,
+ * element counts per storage and an FNV-1a digest of the contents) or
+ * "K key missing". For parity tests of the container reader against the
+ * reference's GgufFile (model/fish/include/fish/gguf.h:77-116). Returns the
+ * digest length, written as fish_detokenize writes strings; -1 when the file
+ * cannot be read. */
+FISH_API int fbx_gguf_digest(const char* gguf_path, const char* const* keys, int n_keys, char* out, int cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,8 @@
 #include <fish/ops.h>
 #include <fish/threadpool.h>
 #include <fish/sampler.h>
+#include <fish/gguf.h>
+#include <cstdio>
 
 #include <cstring>
 #include <memory>
@@ -130,6 +132,60 @@ __attribute__((visibility("default"))) void ref_sample(const float* logits, int 
         std::memcpy(work.data(), logits, sizeof(float) * static_cast<size_t>(n_vocab));
         out[i] = s.sample(work.data(), n_vocab, p, rec);
     }
+}
+/* The same digest as the library's fbx_gguf_digest, from the reference's own
+ * GgufFile reader (include/fish/gguf.h:77-116): tensor directory and the
+ * requested metadata keys, arrays reduced to counts and an FNV-1a digest. */
+static unsigned long long ref_fnv1a(unsigned long long h, const void* p, size_t n) {
+    const unsigned char* b = static_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return h;
+}
+__attribute__((visibility("default"))) int ref_gguf_digest(const char* path, const char* const* keys, int n_keys,
+                                                           char* out, int cap) {
+    std::string err;
+    auto g = GgufFile::open(path, &err);
+    if (!g) return -1;
+    std::string d;
+    char line[256];
+    for (const TensorInfo& t : g->tensors()) {
+        d += "T " + t.name + " " + std::to_string(static_cast<unsigned>(t.type)) + " ";
+        for (size_t i = 0; i < t.ne.size(); ++i) d += (i ? "," : "") + std::to_string(t.ne[i]);
+        const unsigned long long off = static_cast<unsigned long long>(t.data - g->data_base()) + g->data_offset();
+        std::snprintf(line, sizeof(line), " %llu %llu\n", off, static_cast<unsigned long long>(t.nbytes));
+        d += line;
+    }
+    for (int k = 0; k < n_keys; ++k) {
+        const MetaValue* m = g->meta(keys[k]);
+        d += std::string("K ") + keys[k] + " ";
+        if (!m) { d += "missing\n"; continue; }
+        d += std::to_string(static_cast<int>(m->kind)) + " ";
+        switch (m->kind) {
+            case MetaValue::UINT: d += std::to_string(m->u); break;
+            case MetaValue::INT: d += std::to_string(m->i); break;
+            case MetaValue::FLOAT: std::snprintf(line, sizeof(line), "%.17g", m->f); d += line; break;
+            case MetaValue::BOOL: d += m->b ? "1" : "0"; break;
+            case MetaValue::STRING: d += m->s; break;
+            default: {
+                unsigned long long h = 1469598103934665603ull;
+                for (const std::string& s : m->sarr) h = ref_fnv1a(h, s.c_str(), s.size() + 1);
+                h = ref_fnv1a(h, m->iarr.data(), m->iarr.size() * sizeof(int32_t));
+                h = ref_fnv1a(h, m->farr.data(), m->farr.size() * sizeof(float));
+                const size_t n = m->sarr.size() + m->iarr.size() + m->farr.size() + m->arr.size();
+                std::snprintf(line, sizeof(line), "n=%zu s=%zu i=%zu f=%zu h=%016llx", n, m->sarr.size(),
+                              m->iarr.size(), m->farr.size(), h);
+                d += line;
+            }
+        }
+        d += "\n";
+    }
+    const int need = static_cast<int>(d.size());
+    if (out && cap > 0) {
+        const int n = need < cap - 1 ? need : cap - 1;
+        std::memcpy(out, d.data(), static_cast<size_t>(n));
+        out[n] = '\0';
+    }
+    return need;
 }
 
 }  // extern "C"

@@ -1,0 +1,75 @@
+"""GGUF container parity with the reference FISH engine, on the CPU. Both
+readers open the same synthetic GGUF: the reference's GgufFile
+(model/fish/include/fish/gguf.h:77-116, compiled here from its own sources
+into oracle/_ref with the ref_gguf_digest probe) and this library's reader
+(fbx_gguf_digest). Each returns one line per tensor (name, type, dimensions,
+absolute file offset of the data, byte count) and one line per requested
+metadata key (kind and value, arrays as counts plus an FNV-1a digest of the
+contents); the two texts must be equal. The keys are the ones the model
+loaders read (hyperparameters, tokenizer tables, MoE counts) and one that no
+file has."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from imurun_b200 import native
+
+P, I, CP = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
+SUFFIXES = ["block_count", "context_length", "embedding_length", "feed_forward_length",
+            "attention.head_count", "attention.head_count_kv", "attention.layer_norm_rms_epsilon",
+            "rope.freq_base", "rope.dimension_count", "expert_count", "expert_used_count", "vocab_size"]
+GENERAL = ["general.architecture", "general.name", "general.alignment", "tokenizer.ggml.model",
+           "tokenizer.ggml.tokens", "tokenizer.ggml.scores", "tokenizer.ggml.token_type",
+           "tokenizer.ggml.bos_token_id", "tokenizer.ggml.eos_token_id", "tokenizer.ggml.add_bos_token",
+           "tokenizer.chat_template", "no.such.key"]
+
+
+@pytest.fixture(scope="module")
+def ref_lib():
+    from oracle.binding import REF_SO
+    if not REF_SO.exists():
+        pytest.skip("reference build (oracle/_ref) not present")
+    L = ctypes.CDLL(str(REF_SO))
+    L.ref_gguf_digest.argtypes = [CP, P, I, ctypes.c_char_p, I]
+    L.ref_gguf_digest.restype = I
+    return L
+
+
+@pytest.fixture(scope="module")
+def ours():
+    L = native.load_library()
+    L.fbx_gguf_digest.argtypes = [CP, P, I, ctypes.c_char_p, I]
+    L.fbx_gguf_digest.restype = I
+    return L
+
+
+def _digest(fn, path, keys):
+    arr = (ctypes.c_char_p * max(len(keys), 1))(*[k.encode() for k in keys])
+    n = fn(str(path).encode(), ctypes.cast(arr, P), len(keys), None, 0)
+    assert n >= 0
+    buf = ctypes.create_string_buffer(n + 1)
+    assert fn(str(path).encode(), ctypes.cast(arr, P), len(keys), buf, n + 1) == n
+    return buf.raw[:n].decode()
+
+
+@pytest.mark.parametrize("name", ["tiny", "qwen7b", "mixtral"])
+def test_gguf_digest_matches_reference(ref_lib, ours, synth_dir, name):
+    from imurun_b200 import synth
+    cfg = {"tiny": lambda: synth.preset("tiny"),
+           "qwen7b": lambda: synth.preset("qwen7b", layers=1),
+           "mixtral": lambda: synth.preset("mixtral", layers=1, n_embd=512, n_ff=1024, n_head=8,
+                                                 n_head_kv=2)}[name]()
+    path = synth.cached(cfg, synth_dir)
+    arch_line = _digest(ours.fbx_gguf_digest, path, ["general.architecture"]).splitlines()[-1]
+    arch = arch_line.split(" ", 3)[3]
+    keys = GENERAL + [f"{arch}.{s}" for s in SUFFIXES]
+    got = _digest(ours.fbx_gguf_digest, path, keys)
+    want = _digest(ref_lib.ref_gguf_digest, path, keys)
+    assert got.count("\nT ") + got.startswith("T ") > 0
+    assert got.splitlines() == want.splitlines()
+
+
+def test_unreadable_file(ours):
+    assert ours.fbx_gguf_digest(b"/nonexistent.gguf", None, 0, None, 0) == -1
