@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "prompt_fit.h"
 #include "sampler.h"
 #include "tokenizer.h"
 
@@ -35,8 +36,7 @@ struct fish_ctx {
     std::atomic<bool> cancel{false};
     fish_stats stats{};
     std::vector<int32_t> cache_ids;
-    int trunc_head = 0, trunc_drop_end = 0;
-    std::vector<int32_t> trunc_head_ids;
+    fb::PromptCut cut;
     std::string adapter_path;
     float adapter_scale = 1.0f;
     std::string model_path;
@@ -177,41 +177,9 @@ int generate_ids_locked(fish_ctx* ctx, std::vector<int32_t> ids, int max_tokens,
     fb::Engine& e = *ctx->eng;
     const fb::Config& c = e.cfg();
     if (max_tokens <= 0) max_tokens = c.n_ctx;
-    ctx->stats.truncated = 0;
-    {
-        const int reserve = std::max(64, std::min(max_tokens, c.n_ctx / 4));
-        const int budget = std::max(32, c.n_ctx - reserve);
-        const int n = (int)ids.size();
-        if (n > budget) {
-            int head = ctx->trunc_head, drop_end = ctx->trunc_drop_end;
-            const bool reuse = head > 0 && drop_end > head && drop_end < n && n - (drop_end - head) <= budget &&
-                               (int)ctx->trunc_head_ids.size() == head &&
-                               std::equal(ctx->trunc_head_ids.begin(), ctx->trunc_head_ids.end(), ids.begin());
-            if (!reuse) {
-                head = budget / 4;
-                const int tail = std::max(1, budget - head - budget / 4);
-                drop_end = n - tail;
-                ctx->trunc_head = head;
-                ctx->trunc_drop_end = drop_end;
-                ctx->trunc_head_ids.assign(ids.begin(), ids.begin() + head);
-            }
-            std::vector<int32_t> kept(ids.begin(), ids.begin() + head);
-            kept.insert(kept.end(), ids.begin() + drop_end, ids.end());
-            ids.swap(kept);
-            ctx->stats.truncated = 1;
-        } else {
-            ctx->trunc_head = ctx->trunc_drop_end = 0;
-            ctx->trunc_head_ids.clear();
-        }
-    }
+    ctx->stats.truncated = fb::fit_prompt(ids, c.n_ctx, max_tokens, ctx->cut) ? 1 : 0;
     ctx->cancel = false;
-    int prefix = 0;
-    {
-        const int lim = (int)std::min(ids.size(), ctx->cache_ids.size());
-        while (prefix < lim && ids[prefix] == ctx->cache_ids[prefix]) ++prefix;
-        if (prefix >= (int)ids.size()) prefix = (int)ids.size() - 1;
-        if (prefix < 8) prefix = 0;
-    }
+    const int prefix = fb::cached_prefix(ids, ctx->cache_ids);
     ctx->stats.cached_tokens = prefix;
     const double t0 = now_s();
     e.seq_truncate(0, prefix);
@@ -434,6 +402,32 @@ static uint64_t fnv1a(uint64_t h, const void* p, size_t n) {
     const uint8_t* b = static_cast<const uint8_t*>(p);
     for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
     return h;
+}
+
+struct fbx_prompt_state {
+    fb::PromptCut cut;
+    std::vector<int32_t> cache_ids;
+};
+
+fbx_prompt_state* fbx_prompt_state_create(void) { return new (std::nothrow) fbx_prompt_state(); }
+void fbx_prompt_state_destroy(fbx_prompt_state* s) { delete s; }
+
+int fbx_prompt_plan(fbx_prompt_state* s, const int32_t* ids, int n, int n_ctx, int max_tokens, int32_t* kept, int cap,
+                    int* cached, int* truncated) {
+    if (!s || !ids || n <= 0 || n_ctx <= 0 || !kept || !cached || !truncated) return -1;
+    if (max_tokens <= 0) max_tokens = n_ctx;
+    std::vector<int32_t> v(ids, ids + n);
+    *truncated = fb::fit_prompt(v, n_ctx, max_tokens, s->cut) ? 1 : 0;
+    *cached = fb::cached_prefix(v, s->cache_ids);
+    if ((int)v.size() > cap) return -1;
+    std::copy(v.begin(), v.end(), kept);
+    return (int)v.size();
+}
+
+int fbx_prompt_commit(fbx_prompt_state* s, const int32_t* ids, int n) {
+    if (!s || n < 0 || (n > 0 && !ids)) return -1;
+    s->cache_ids.assign(ids, ids + n);
+    return 0;
 }
 
 int fbx_gguf_digest(const char* gguf_path, const char* const* keys, int n_keys, char* out, int cap) {

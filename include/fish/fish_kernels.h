@@ -134,6 +134,23 @@ FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int
                         float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
                         int n_draws, int32_t* out);
 
+/* The prompt decisions fish_generate makes before its first forward (host
+ * code only, the same functions the generation loop calls): a state holding
+ * the last head+tail cut and the ids whose KV the one-slot prefix cache holds
+ * (model/fish/src/c_api.cpp:40-44, 516-567). fbx_prompt_plan fits `ids` into
+ * n_ctx for `max_tokens` (<= 0: n_ctx) as fish_generate does, writes the kept
+ * ids to `kept` and returns their count (fish_stats.prompt_tokens), with
+ * *truncated (fish_stats.truncated) and *cached, the tokens the cache would
+ * serve (fish_stats.cached_tokens); -1 on a bad argument or cap < the kept
+ * count. fbx_prompt_commit sets the cached ids, as a finished turn leaves
+ * them: the kept prompt followed by every generated token fed back. */
+typedef struct fbx_prompt_state fbx_prompt_state;
+FISH_API fbx_prompt_state* fbx_prompt_state_create(void);
+FISH_API void fbx_prompt_state_destroy(fbx_prompt_state* s);
+FISH_API int fbx_prompt_plan(fbx_prompt_state* s, const int32_t* ids, int n, int n_ctx, int max_tokens,
+                             int32_t* kept, int cap, int* cached, int* truncated);
+FISH_API int fbx_prompt_commit(fbx_prompt_state* s, const int32_t* ids, int n);
+
 /* Digest of how this library reads a GGUF file (host code only): one line
  * per tensor in directory order, "T name type ne0,ne1,.. file_offset nbytes"
  * (the absolute offset of its data in the file), then one line per key in
