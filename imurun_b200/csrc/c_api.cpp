@@ -78,6 +78,14 @@ void emit_utf8(fish_token_cb cb, void* user, const std::string& bytes, int id, s
     if (cb) cb(ready.c_str(), id, user);
 }
 
+// Send what is still pending when generation ends (c_api.cpp:774-779).
+void flush_utf8(fish_token_cb cb, void* user, std::string& pending, std::string& sink) {
+    if (pending.empty()) return;
+    sink += pending;
+    if (cb) cb(pending.c_str(), -1, user);
+    pending.clear();
+}
+
 int write_string(const std::string& s, char* out, int cap) {
     const int need = (int)s.size();
     if (out && cap > 0) {
@@ -226,10 +234,7 @@ int generate_ids_locked(fish_ctx* ctx, std::vector<int32_t> ids, int max_tokens,
         ++pos;
         next = ctx->sampler.sample(ctx->logits.data(), c.vocab, sp, recent);
     }
-    if (!pending.empty()) {
-        sink += pending;
-        if (cb) cb(pending.c_str(), -1, user);
-    }
+    flush_utf8(cb, user, pending, sink);
     const double t2 = now_s();
     ctx->stats.prefill_seconds = t1 - t0;
     ctx->stats.decode_seconds = t2 - t1;
@@ -395,6 +400,19 @@ int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const 
     auto tok = tokenizer_of(gguf_path, &g);
     if (!tok || n < 0) return -1;
     return write_string(tok->apply_chat(to_messages(roles, contents, n), tok->format()), out, cap);
+}
+
+int fbx_stream_gguf(const char* gguf_path, const int32_t* ids, int n, char* out, int cap) {
+    std::unique_ptr<fb::Gguf> g;
+    auto tok = tokenizer_of(gguf_path, &g);
+    if (!tok || n < 0 || (n > 0 && !ids)) return -1;
+    std::string rec, pending, sink;
+    const fish_token_cb cb = [](const char* text, int id, void* user) {
+        *static_cast<std::string*>(user) += std::to_string(id) + " " + std::to_string(std::strlen(text)) + "\n" + text;
+    };
+    for (int i = 0; i < n; ++i) emit_utf8(cb, &rec, tok->token_text(ids[i]), ids[i], pending, sink);
+    flush_utf8(cb, &rec, pending, sink);
+    return write_string(rec, out, cap);
 }
 
 // FNV-1a over bytes, for the digest of metadata arrays

@@ -134,6 +134,14 @@ FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int
                         float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
                         int n_draws, int32_t* out);
 
+/* The token callback stream fish_generate produces for the generated ids
+ * `ids` (host code only; the generation loop's own UTF-8 emitter and final
+ * flush over the GGUF tokenizer's token texts, model/fish/src/c_api.cpp:81-101,
+ * 774-779): every callback as "<token_id> <strlen(text)>\n<text>", in order.
+ * Returns the record length, written as fish_detokenize writes strings; -1
+ * when the file cannot be read. */
+FISH_API int fbx_stream_gguf(const char* gguf_path, const int32_t* ids, int n, char* out, int cap);
+
 /* The prompt decisions fish_generate makes before its first forward (host
  * code only, the same functions the generation loop calls): a state holding
  * the last head+tail cut and the ids whose KV the one-slot prefix cache holds
