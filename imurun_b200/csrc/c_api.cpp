@@ -402,6 +402,15 @@ int fbx_chat_prompt_gguf(const char* gguf_path, const char* const* roles, const 
     return write_string(tok->apply_chat(to_messages(roles, contents, n), tok->format()), out, cap);
 }
 
+int fbx_chat_info_gguf(const char* gguf_path, const char* const* roles, const char* const* contents, int n,
+                       char* format, int cap) {
+    std::unique_ptr<fb::Gguf> g;
+    auto tok = tokenizer_of(gguf_path, &g);
+    if (!tok || n < 0) return -1;
+    write_string(fb::chat_format_name(tok->format()), format, cap);
+    return (int)tok->encode_chat(to_messages(roles, contents, n)).size();
+}
+
 int fbx_stream_gguf(const char* gguf_path, const int32_t* ids, int n, char* out, int cap) {
     std::unique_ptr<fb::Gguf> g;
     auto tok = tokenizer_of(gguf_path, &g);

@@ -234,6 +234,7 @@ typedef struct fish_synth_config {
     unsigned long long seed;
     float wstd;                  // weight std (0.02)
     float router_std;            // MoE router std (1/64 variance -> 0.125)
+    const char* chat_template;   // tokenizer.chat_template; nullptr or "" writes none
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -342,6 +343,7 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     w.kv_u32("tokenizer.ggml.eos_token_id", 2); ++n_kv;
     w.kv_u32("tokenizer.ggml.unknown_token_id", 0); ++n_kv;
     w.kv_bool("tokenizer.ggml.add_bos_token", true); ++n_kv;
+    if (c->chat_template && c->chat_template[0]) { w.kv_str("tokenizer.chat_template", c->chat_template); ++n_kv; }
     std::memcpy(w.buf.data() + n_kv_pos, &n_kv, 8);
 
     for (const auto& t : ts) {

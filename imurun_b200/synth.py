@@ -47,6 +47,7 @@ class SynthConfig:
     seed: int = 1234
     wstd: float = 0.02
     router_std: float = 0.125
+    chat_template: str = ""   # written as tokenizer.chat_template when not empty
 
 
 PRESETS = {
@@ -74,6 +75,7 @@ class _CConfig(ctypes.Structure):
         ("n_experts", ctypes.c_int), ("n_experts_per_tok", ctypes.c_int),
         ("qkv_bias", ctypes.c_int), ("wtype", ctypes.c_int),
         ("seed", ctypes.c_ulonglong), ("wstd", ctypes.c_float), ("router_std", ctypes.c_float),
+        ("chat_template", ctypes.c_char_p),
     ]
 
 
@@ -94,7 +96,8 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
     fn.restype = ctypes.c_int
     c = _CConfig(cfg.arch.encode(), cfg.n_layers, cfg.n_embd, cfg.n_ff, cfg.n_head, cfg.n_head_kv,
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
-                 cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std)
+                 cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
+                 cfg.chat_template.encode())
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

@@ -134,6 +134,14 @@ FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int
                         float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
                         int n_draws, int32_t* out);
 
+/* fish_count_chat_tokens and fish_chat_format for the GGUF at gguf_path with
+ * no model loaded (host code only, model/fish/src/c_api.cpp:384-397): returns
+ * the token count of the formatted chat, and writes the chat format's name
+ * to `format` as fish_detokenize writes strings; -1 when the file cannot be
+ * read. */
+FISH_API int fbx_chat_info_gguf(const char* gguf_path, const char* const* roles, const char* const* contents, int n,
+                                char* format, int cap);
+
 /* The token callback stream fish_generate produces for the generated ids
  * `ids` (host code only; the generation loop's own UTF-8 emitter and final
  * flush over the GGUF tokenizer's token texts, model/fish/src/c_api.cpp:81-101,

@@ -40,6 +40,10 @@ def ref_lib():
     L.fish_detokenize.restype = I
     L.fish_chat_prompt.argtypes = [P, P, P, I, ctypes.c_char_p, I]
     L.fish_chat_prompt.restype = I
+    L.fish_count_chat_tokens.argtypes = [P, P, P, I]
+    L.fish_count_chat_tokens.restype = I
+    L.fish_chat_format.argtypes = [P]
+    L.fish_chat_format.restype = ctypes.c_char_p
     return L
 
 
@@ -52,6 +56,8 @@ def ours():
     L.fbx_detokenize_gguf.restype = I
     L.fbx_chat_prompt_gguf.argtypes = [CP, P, P, I, ctypes.c_char_p, I]
     L.fbx_chat_prompt_gguf.restype = I
+    L.fbx_chat_info_gguf.argtypes = [CP, P, P, I, ctypes.c_char_p, I]
+    L.fbx_chat_info_gguf.restype = I
     return L
 
 
@@ -109,6 +115,47 @@ def test_tokenize_matches_reference(ref_lib, ours, ref_ctx, gguf, text, bos):
 def test_chat_prompt_matches_reference(ref_lib, ours, ref_ctx, gguf, k):
     args = _chat_args(CHATS[k])
     assert _str(ours.fbx_chat_prompt_gguf, str(gguf).encode(), *args) == _str(ref_lib.fish_chat_prompt, ref_ctx, *args)
+
+
+@pytest.mark.parametrize("k", range(len(CHATS)))
+def test_chat_count_and_format_match_reference(ref_lib, ours, ref_ctx, gguf, k):
+    args = _chat_args(CHATS[k])
+    fmt = ctypes.create_string_buffer(64)
+    n = ours.fbx_chat_info_gguf(str(gguf).encode(), *args, fmt, 64)
+    assert n == ref_lib.fish_count_chat_tokens(ref_ctx, *args) > 0
+    assert fmt.value == ref_lib.fish_chat_format(ref_ctx)
+
+
+# Minimal templates carrying the marker each chat format is detected by
+# (model/fish/src/tokenizer.cpp:274-288); "" writes no template.
+TEMPLATES = {
+    "plain": "",
+    "llama3": "{{ '<|start_header_id|>' + role + '<|end_header_id|>' + content }}",
+    "chatml": "{{ '<|im_start|>' + role + content }}",
+    "gemma": "{{ '<start_of_turn>' + role + content }}",
+    "phi3": "{{ '<|user|>' + content + '<|end|>' }}",
+    "deepseek": "{{ '<\uff5cUser\uff5c>' + content }}",
+    "mistral": "{{ '[INST] ' + content + ' [/INST]' }}",
+}
+
+
+@pytest.mark.parametrize("name", list(TEMPLATES))
+def test_chat_formats_match_reference(ref_lib, ours, synth_dir, name):
+    from imurun_b200 import synth
+    path = synth.cached(synth.preset("tiny", layers=1, chat_template=TEMPLATES[name]), synth_dir)
+    ctx = ref_lib.fish_create()
+    try:
+        assert ref_lib.fish_load(ctx, str(path).encode(), 256) == 0
+        assert ref_lib.fish_chat_format(ctx) == name.encode()
+        fmt = ctypes.create_string_buffer(64)
+        for msgs in CHATS:
+            args = _chat_args(msgs)
+            assert _str(ours.fbx_chat_prompt_gguf, str(path).encode(), *args) == _str(ref_lib.fish_chat_prompt, ctx, *args)
+            assert ours.fbx_chat_info_gguf(str(path).encode(), *args, fmt, 64) == \
+                ref_lib.fish_count_chat_tokens(ctx, *args)
+            assert fmt.value == name.encode()
+    finally:
+        ref_lib.fish_destroy(ctx)
 
 
 def test_unreadable_file(ours):
