@@ -7,7 +7,9 @@ the GGUF's metadata through the host-only fbx_*_gguf entry points, which
 build the tokenizer fish_load builds. The synthetic vocabulary is
 SentencePiece-style (<unk> <s> </s>, 256 byte tokens, then "▁t<i>" pieces),
 so the cases exercise byte fallback, the space prefix, BOS, special-token
-text, the pieces that do match, and the chat format chosen per architecture."""
+text and the pieces that do match. The chat cases cover every format the
+reference detects, from files carrying a template with that format's
+marker."""
 from __future__ import annotations
 
 import ctypes
