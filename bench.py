@@ -98,6 +98,26 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def gemv_share_from_profiles():
+    """The streamed GEMV's share of one decode step's launch time, from the
+    committed ncu launch list of the same build."""
+    import re
+    f = ROOT / "profiles" / "decode_step_llama8b_launches.md"
+    if not f.exists():
+        return None
+    m = re.search(r"dominant kernel \((\d+) launches, ([\d.]+) %", f.read_text())
+    return float(m.group(2)) / 100.0 if m else None
+
+
+def int8_peak():
+    """Dense int8 tensor peak for the prefill roofline: twice the measured
+    bf16 GEMM burst (B200's dense int8 rate is twice its bf16 rate)."""
+    if PEAKS_PATH.exists():
+        p = json.loads(PEAKS_PATH.read_text())
+        return round(2.0 * float(p["bf16_tflops"]), 1), "2x measured bf16 burst (MEASURED_PEAKS.json)"
+    return 4500.0, "nominal dense int8"
+
+
 def traffic_ratio_from_profiles():
     """DRAM bytes per algorithmic byte of the GEMV, from the committed ncu
     summary (one captured launch of the same kernel on an 8B-shaped matrix)."""
@@ -159,6 +179,38 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def cpu_info() -> dict:
+    """Host CPU model, physical cores (distinct (package, core) pairs) and
+    logical CPUs, from /proc/cpuinfo."""
+    model, cores, cur = None, set(), {}
+    try:
+        lines = Path("/proc/cpuinfo").read_text().splitlines() + [""]
+    except OSError:
+        lines = []
+    for ln in lines:
+        if ":" not in ln:
+            if "core id" in cur:
+                cores.add((cur.get("physical id", "0"), cur["core id"]))
+            cur = {}
+            continue
+        k, v = (x.strip() for x in ln.split(":", 1))
+        if k == "model name" and model is None:
+            model = v
+        if k in ("physical id", "core id"):
+            cur[k] = v
+    return {"cpu_model": model, "physical_cores": len(cores) or None, "logical_cpus": os.cpu_count()}
+
+
+def synth_in_child(preset: str) -> Path:
+    """Write (or find) a preset's synthetic GGUF in a separate process, so the
+    process that times the reference maps only the reference's library."""
+    code = ("import sys; sys.path.insert(0, %r); from imurun_b200 import synth; "
+            "print(synth.cached(synth.preset(%r), %r))" % (str(ROOT), preset,
+                                                           os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+    return Path(r.stdout.strip().splitlines()[-1])
+
+
 def cpu_reference_decode(path, n_prompt: int, n_decode: int):
     """Reference FISH CPU engine (oracle/_ref) with all host threads:
     prefill n_prompt ids, then time n_decode greedy decode steps."""
@@ -177,7 +229,7 @@ def cpu_reference_decode(path, n_prompt: int, n_decode: int):
             tok = int(np.argmax(lg))
         dt = time.perf_counter() - t0
         m.close()
-        return n_decode / dt, "reference", ref.threads(), dt
+        return n_decode / dt, "reference", ref.threads(), dt, ref.kernel_name()
     o = Oracle()
     m = o.load(path, N_CTX)
     lg = m.forward(ids, 0)
@@ -187,18 +239,17 @@ def cpu_reference_decode(path, n_prompt: int, n_decode: int):
         lg = m.forward(np.array([tok], np.int32), n_prompt + s)
         tok = int(np.argmax(lg))
     dt = time.perf_counter() - t0
-    return n_decode / dt, "port", 1, dt
+    return n_decode / dt, "port", 1, dt, "scalar C restatement"
 
 
 def run_reference(args):
     if RANK != 0:
         return 0
-    from imurun_b200 import synth
-    path = synth.cached(synth.preset("llama8b"), os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    path = synth_in_child("llama8b")
     n_prompt = 32
     k = min(args.steps, 32)
     w = min(args.warmup, 4)
-    value, kind, cores, dt = cpu_reference_decode(path, n_prompt, k + w)
+    value, kind, cores, dt, kname = cpu_reference_decode(path, n_prompt, k + w)
     sample = (f"Llama-3-8B-shaped Q4_K_M, prompt {n_prompt} random ids, {k + w} greedy decode steps "
               f"(steps capped at 32 + 4 for the CPU), batch 1")
     line = {
@@ -207,7 +258,8 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": "llama8b-shaped Q4_K_M decode, batch 1 (reference FISH CPU engine)",
                    "global_batch": 1, "seq_len": n_prompt + k + w, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample,
+                         "kernel_name": kname, **cpu_info()},
         "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -265,42 +317,82 @@ def run_ours(args):
     e2e_s = max_over_ranks(dist, e2e_s)
     e2e_value = WORLD * K / e2e_s
 
-    # roofline of the dominant kernel (the quantised GEMV): per-launch events
-    m.set_kv_len(pos_start)
+    # e2e through the generation loop a user's chat turn runs (fish_generate_to,
+    # greedy: penalty and argmax on the device, only the id crosses back);
+    # decode tok/s from fish_stats, the reference's own semantics
+    from imurun_b200.native import FishStats
+    import ctypes
+    text = " ".join(f"t{int(i)}" for i in ids[:64]).encode()
+    gbuf = ctypes.create_string_buffer(1 << 16)
+    m.lib.fish_reset(m.ctx)
+    barrier(dist)
+    ng = m.lib.fish_generate_to(m.ctx, text, 1, K, 0.0, 1, 1.0, 1.0, gbuf, 1 << 16)
+    st = FishStats()
+    m.lib.fish_get_stats(m.ctx, ctypes.byref(st))
+    gen_tps = -max_over_ranks(dist, -float(st.tokens_per_second)) * WORLD   # slowest rank x ranks
+    if ng <= 0:
+        gen_tps = None
+
+    # per-launch events of the eager path (context for the class split), from
+    # the same 512-id prompt
+    m.set_kv_len(0)
+    m.prefill(ids, 0)
     prof = json.loads(m.lib.fish_profile_decode_json(m.ctx, nxt, 16).decode())
     cls = {c["name"]: c for c in prof["classes"]}
     g = cls["gemv"]
     peak, peak_kind = peaks()
-    achieved = (g["bytes"] / g["launches"]) / ((g["ms"] / g["launches"]) / 1e3) / 1e9
-    ratio = traffic_ratio_from_profiles()
-    traffic = round(ratio * g["bytes"] / g["launches"]) if ratio else None
     total_ms = sum(c["ms"] for c in prof["classes"])
-    # whole decode step against HBM: weights (GGUF bytes, embedding row only) + KV read
+    # the timed decode step against HBM: algorithmic bytes = weights in their
+    # GGUF encoding (embedding: one row) + the K/V rows every step reads
     info = m.info
     kv_row = 2 * info.n_layers * info.n_head_kv * info.head_dim * 2
     avg_pos = pos_start + K / 2
     step_bytes = g["bytes"] / prof["steps"] + kv_row * avg_pos
-    step_gbs = step_bytes / (dev_ms / K / 1e3) / 1e9
+    step_ms = dev_ms / K
+    step_gbs = step_bytes / (step_ms / 1e3) / 1e9
+    ratio = traffic_ratio_from_profiles()
+    share = gemv_share_from_profiles()
     persistent = bool(eng.get("step_kernel"))
     if persistent:
-        # one cooperative launch of k_step ran all K steps: the dominant (only)
-        # kernel; its algorithmic bytes are the weights (GGUF encoding) and the
-        # K/V rows every step reads, over the launch's event-timed duration
+        # one cooperative launch of k_step ran all K steps; its algorithmic
+        # bytes are the weights (GGUF encoding) and the K/V rows every step
+        # reads, over the launch's event-timed duration
         step_alg = eng["step_weight_bytes"] + kv_row * avg_pos
         achieved = step_alg * K / (float(eng["last_step_ms"]) / 1e3) / 1e9
         traffic = None
         kernel = "k_step (persistent decode step: all GEMV phases, attention, argmax)"
         timed_launches = 1
     else:
-        kernel = "k_gemv_stream<1> (Q4_K/Q6_K decode GEMV)"
+        achieved = step_gbs
+        traffic = round(ratio * step_bytes) if ratio else None
+        kernel = ("decode step: one CUDA graph per token (streamed GEMV x129, decode attention x32, embedding, "
+                  "argmax), the K replays timed with CUDA events on the engine stream")
         timed_launches = eng["greedy_graph_kernels"] * K
+    gemv = None
+    if share and not persistent:
+        gemv_ms = share * step_ms
+        gemv_bytes = g["bytes"] / prof["steps"]
+        gemv = {"kernel": "k_gemv_stream<1, TM, PM> (Q4_K/Q6_K decode GEMV)", "share_of_step": share,
+                "ms_per_step_est": round(gemv_ms, 4),
+                "achieved_gbs_est": round(gemv_bytes / (gemv_ms / 1e3) / 1e9, 1),
+                "frac_est": round(gemv_bytes / (gemv_ms / 1e3) / 1e9 / peak, 4),
+                "note": "share of the step's launch time from the committed ncu launch list "
+                        "(profiles/decode_step_llama8b_launches.md) times the timed step"}
+    # prefill against the int8 tensor roofline: 2 x int8 MACs of the layers
+    # for every prompt token + the output projection of the last one
+    E, F, V, L = info.n_embd, info.n_ff, info.vocab, info.n_layers
+    Qd, KVd = info.n_head * info.head_dim, info.n_head_kv * info.head_dim
+    macs = PROMPT * L * (E * (Qd + 2 * KVd) + Qd * E + 3 * E * F) + V * E
+    i8_peak, i8_kind = int8_peak()
+    prefill_tops = 2.0 * macs / prefill_s / 1e12
     m.close()
 
     cpu = None
     if RANK == 0 and WORLD == 1 and not args.no_cpu:
-        v, kind, cores, dt = cpu_reference_decode(path, 16, 8)
+        v, kind, cores, dt, kname = cpu_reference_decode(path, 16, 8)
         cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": kind,
-               "sample": f"same GGUF, prompt 16 random ids, 8 greedy decode steps, {dt:.1f} s of CPU decode"}
+               "sample": f"same GGUF, prompt 16 random ids, 8 greedy decode steps, {dt:.1f} s of CPU decode",
+               "kernel_name": kname, **cpu_info()}
     if RANK == 0:
         line = {
             "metric": BASELINE["metric"], "value": round(value, 3), "unit": "tok/s", "n_gpus": WORLD,
@@ -312,6 +404,10 @@ def run_ours(args):
                 "global_batch": WORLD, "seq_len": PROMPT + W + K, "parallelism": f"replicas x{WORLD}",
                 "l2": "inputs larger than L2 (4.6 GB of weights streamed per step)",
                 "prefill_tok_s": round(PROMPT / prefill_s, 1),
+                "prefill_roofline": {"bound": "tensor", "achieved": round(prefill_tops, 2), "peak": i8_peak,
+                                     "unit": "TOP/s (int8)", "frac": round(prefill_tops / i8_peak, 4),
+                                     "peak_kind": i8_kind,
+                                     "work": f"{2.0 * macs / 1e12:.3f} T int8 ops for {PROMPT} tokens"},
                 "decode_step_gbs": round(step_gbs, 1),
                 "decode_step_hbm_frac": round(step_gbs / peak, 4),
                 "profile_ms_per_step": {k: round(v["ms"] / prof["steps"], 4) for k, v in cls.items()},
@@ -319,11 +415,14 @@ def run_ours(args):
                 "decode_kernel": "k_step (one cooperative launch per greedy call)" if persistent else "graph of per-op kernels",
                 "profile_total_ms_per_step": round(total_ms / prof["steps"], 4),
             },
-            "e2e": {"value": round(e2e_value, 3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
+            "e2e": {"value": round(e2e_value, 3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4,
+                    "generate_tok_s": round(gen_tps, 3) if gen_tps else None,
+                    "generate_note": "fish_generate_to, greedy, 64-token text prompt, fish_stats decode tok/s"},
             "gpu_launches": int(timed_launches * WORLD),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": kernel, "peak_kind": peak_kind},
+                         "kernel": kernel, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step": round(step_bytes), "gemv": gemv},
             "cpu_baseline": cpu,
             "clocks": clk,
         }

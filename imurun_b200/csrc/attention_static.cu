@@ -11,6 +11,8 @@
 // The scratch this entry point needs (the per-split softmax partials, the
 // per-token positions and an identity page table) lives in one file-scope
 // __device__ array of fixed size, shared by every call on a device.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "fish/fish_kernels.h"
@@ -18,8 +20,9 @@
 
 namespace {
 
-// Limits of one call. The partials of a call take T*H*n_splits*(D+2) floats,
-// with n_splits = ceil(n_keys/32) for n_keys <= 2048 and ceil(n_keys/128) above.
+// Limits of one call. The partials of a call take T*H*n_splits*(D+2) floats
+// (fbk_attention_call_floats: n_splits = ceil((pos0+T)/32) up to 2048 keys,
+// ceil((pos0+T)/128) above).
 constexpr int kStaticMaxKeys = 8192;
 constexpr int kStaticMaxTokens = 256;
 constexpr size_t kStaticPartialFloats = size_t(2) << 20;   // 8 MiB
@@ -33,9 +36,44 @@ struct StaticScratch {
 
 static __device__ __align__(256) StaticScratch g_attn_scratch;
 
+// One cached address per device, tagged with the id of the context it was
+// resolved in: after cudaDeviceReset the device gets a new primary context,
+// the module is loaded again (the array may move and is zeroed), and the
+// id no longer matches, so the set-up runs again.
 constexpr int kMaxDevices = 64;
+struct Resolved {
+    unsigned long long ctx_id = 0;
+    StaticScratch* ptr = nullptr;
+};
 std::mutex g_setup_mu;
-StaticScratch* g_scratch_ptr[kMaxDevices] = {};
+Resolved g_resolved[kMaxDevices];
+
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the current context (driver entry points looked up through the
+// runtime, so the library links no libcuda soname); 0 when unavailable.
+unsigned long long current_ctx_id() {
+    static PfnCtxGetCurrent get_current = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PfnCtxGetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PfnCtxGetId>(f);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 
 __global__ void k_static_setup(StaticScratch* s) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kStaticMaxKeys; i += gridDim.x * blockDim.x) {
@@ -49,26 +87,35 @@ __global__ void k_static_positions(StaticScratch* s, int pos0, int T) {
     if (t < T) s->tok_pos[t] = pos0 + t;
 }
 
-// Address of this device's scratch; the first call on a device resolves the
-// symbol and fills the identity page table and the zero sequence slots.
+// Address of this device's scratch. The first call on a device (and the
+// first after a cudaDeviceReset) resolves the symbol with the device current
+// and fills the identity page table and the zero sequence slots.
 int scratch_for_current_device(cudaStream_t st, StaticScratch** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(g_setup_mu);
-    if (!g_scratch_ptr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_attn_scratch);
-        if (e != cudaSuccess) return (int)e;
-        if (!p) return (int)cudaErrorInvalidSymbol;
+    Resolved& r = g_resolved[dev];
+    unsigned long long id = current_ctx_id();   // 0: no context current on this thread yet
+    if (r.ptr && id != 0 && r.ctx_id == id) {
+        *out = r.ptr;
+        return 0;
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);   // makes the device's context current if needed
+    if (e != cudaSuccess) return (int)e;
+    if (!p) return (int)cudaErrorInvalidSymbol;
+    id = current_ctx_id();
+    if (p != r.ptr || id == 0 || id != r.ctx_id) {
         k_static_setup<<<(kStaticMaxKeys + 255) / 256, 256, 0, st>>>(static_cast<StaticScratch*>(p));
         e = cudaGetLastError();
         if (e == cudaSuccess) e = cudaStreamSynchronize(st);   // later calls may come on other streams
         if (e != cudaSuccess) return (int)e;
-        g_scratch_ptr[dev] = static_cast<StaticScratch*>(p);
+        r.ptr = static_cast<StaticScratch*>(p);
+        r.ctx_id = id;
     }
-    *out = g_scratch_ptr[dev];
+    *out = r.ptr;
     return 0;
 }
 
@@ -82,9 +129,8 @@ extern "C" FISH_API int fbx_attention_static(const float* q, const void* k, cons
         return -1;
     if (n_keys < pos0 + T || pos0 + T > kStaticMaxKeys || T > kStaticMaxTokens) return -1;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return -1;
-    const int max_ctx = pos0 + T;
-    const size_t need = fbk_attention_scratch_floats(T, H, D, max_ctx);
-    if (need > kStaticPartialFloats) return -1;
+    const int max_ctx = pos0 + T;   // causal: only keys [0, pos0+T) are read
+    if (fbk_attention_call_floats(T, H, D, max_ctx) > kStaticPartialFloats) return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     StaticScratch* s = nullptr;
     int rc = scratch_for_current_device(st, &s);

@@ -225,6 +225,23 @@ int generate_ids_locked(fish_ctx* ctx, std::vector<int32_t> ids, int max_tokens,
         if (recent.size() > recent_cap) recent.erase(recent.begin());
         ++generated;
         std::string err;
+        if (sp.temperature <= 0.0f) {
+            // greedy: penalty and argmax on the device, only the id comes back
+            // (the sampler's window: the last repeat_last_n ids of `recent`)
+            const int window = sp.repeat_last_n > 0 ? sp.repeat_last_n : 64;
+            const size_t start = recent.size() > (size_t)window ? recent.size() - window : 0;
+            int32_t am = 0;
+            if (!e.decode_argmax(0, next, recent.data() + start, (int)(recent.size() - start), sp.repeat_penalty, &am,
+                                 &err)) {
+                ctx->err = "decode failed: " + err;
+                ctx->cache_ids.clear();
+                break;
+            }
+            ctx->cache_ids.push_back(next);
+            ++pos;
+            next = am;
+            continue;
+        }
         if (!e.forward(0, &next, 1, ctx->logits.data(), nullptr, nullptr, &err)) {
             ctx->err = "decode failed: " + err;
             ctx->cache_ids.clear();

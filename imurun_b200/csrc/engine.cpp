@@ -145,6 +145,7 @@ Engine::~Engine() {
     cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
     cudaFree(tp_tmp_); cudaFree(tp_logits_); cudaFree(sel_loc_);
     if (nccl_) nccl_api(nullptr)->comm_destroy((ncclComm_t)nccl_);   // after the graphs that hold its calls
+    if (recent_dev_) cudaFree(recent_dev_);
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
@@ -595,7 +596,8 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMemset(amax_keys_, 0, sizeof(unsigned long long) * kMaxBatch));
     CK(cudaMalloc(&greedy_out_, sizeof(int32_t) * greedy_cap_));
     CK(cudaMalloc(&greedy_step_, sizeof(int32_t)));
-    CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * 3 * kMaxBatch));
+    CK(cudaMalloc(&recent_dev_, sizeof(int32_t) * kMaxRecent));
+    CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * (3 * kMaxBatch + kMaxRecent)));
     // the kernels' shared error flag is allocated on first use; make that use
     // now, so a context's first launches may be inside a graph capture
     if (!fbk_gemv_error_flag()) {
@@ -1448,6 +1450,36 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
     if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * T, cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
     s.len = pos0 + T;
+    return true;
+}
+
+bool Engine::decode_argmax(int sid, int32_t id, const int32_t* recent, int n_recent, float penalty, int32_t* out,
+                           std::string* err) {
+    const bool pen = n_recent > 0 && penalty > 0.0f && penalty != 1.0f;
+    if (!pen) return forward(sid, &id, 1, nullptr, nullptr, out, err);
+    if (n_recent > kMaxRecent) { if (err) *err = "penalty window too long"; return false; }
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session"; return false; }
+    const Config& c = cfg_;
+    if (id < 0 || id >= c.vocab) { if (err) *err = "token id out of range"; return false; }
+    Seq& s = seqs_[sid];
+    const int pos0 = s.len;
+    if (!ensure_pages(sid, pos0 + 1, err)) return false;
+    if (!upload_tokens(&id, &sid, &pos0, 1, err)) return false;   // waits for the previous step's copies
+    int32_t* hr = h_pinned_ + 3 * kMaxBatch;
+    std::copy(recent, recent + n_recent, hr);
+    CK(cudaMemcpyAsync(recent_dev_, hr, sizeof(int32_t) * n_recent, cudaMemcpyHostToDevice, stream_));
+    if (use_graphs_) {
+        if (!graphs_.count(1) && !capture_graph(1, err)) return false;
+        CK(cudaGraphLaunch(graphs_[1], stream_));
+    } else {
+        CK(fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, 1, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
+        if (!run_layers(1, pos0 + 1, true, err)) return false;
+        if (!run_head(0, 1, logits_, err)) return false;
+    }
+    CK(fbk_argmax_penalized(logits_, c.vocab, recent_dev_, n_recent, penalty, argmax_, stream_));
+    CK(cudaMemcpyAsync(out, argmax_, sizeof(int32_t), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    s.len = pos0 + 1;
     return true;
 }
 

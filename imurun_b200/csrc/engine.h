@@ -130,6 +130,11 @@ public:
     // are optional. Chunking to kMaxBatch is the caller's job.
     bool forward(int sid, const int32_t* ids, int T, float* logits_last, float* logits_all, int32_t* argmax,
                  std::string* err);
+    // One token onto sid, then the sampler's greedy branch on the device:
+    // the repetition penalty of the n_recent ids (the sampler's window) and
+    // the first index of the maximum; only that id comes back to the host.
+    bool decode_argmax(int sid, int32_t id, const int32_t* recent, int n_recent, float penalty, int32_t* out,
+                       std::string* err);
     // One token for each of n sequences (n <= kMaxBatch).
     bool decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err);
     // Greedy decode of n_steps on the device with a captured CUDA graph.
@@ -232,7 +237,8 @@ private:
     int32_t *greedy_out_ = nullptr, *greedy_step_ = nullptr;
     unsigned long long* amax_keys_ = nullptr;   // [kMaxBatch] argmax keys, zero between steps
     int greedy_cap_ = 1 << 16;
-    int32_t* h_pinned_ = nullptr;   // pinned staging for ids / tok_seq / tok_pos
+    int32_t* h_pinned_ = nullptr;   // pinned staging for ids / tok_seq / tok_pos / the penalty window
+    int32_t* recent_dev_ = nullptr;  // [kMaxRecent] penalty window of decode_argmax
 
     // KV pool
     void* kv_pool_ = nullptr;

@@ -504,6 +504,21 @@ int fbx_argmax(const float* x, int rows, int n, int32_t* out) {
     return 0;
 }
 
+int fbx_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty, int32_t* out) {
+    if (!x || !out || n <= 0 || n_recent < 0 || n_recent > kMaxRecent || (n_recent > 0 && !recent)) return -1;
+    TRY(check_device());
+    DevBuf dx, dr, dout;
+    TRY(dx.alloc(sizeof(float) * (size_t)n));
+    TRY(dr.alloc(sizeof(int32_t) * (size_t)(n_recent > 0 ? n_recent : 1)));
+    TRY(dout.alloc(sizeof(int32_t)));
+    TRY(cudaMemcpy(dx.p, x, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice));
+    if (n_recent > 0) TRY(cudaMemcpy(dr.p, recent, sizeof(int32_t) * (size_t)n_recent, cudaMemcpyHostToDevice));
+    TRY(fbk_argmax_penalized(dx.as<float>(), n, dr.as<int32_t>(), n_recent, penalty, dout.as<int32_t>(), nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    return 0;
+}
+
 int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out) {
     if (!table || !ids || !out || E <= 0 || n_rows <= 0 || T <= 0) return -1;
     for (int t = 0; t < T; ++t) if (ids[t] < 0 || ids[t] >= n_rows) return -1;

@@ -1068,6 +1068,13 @@ extern "C" size_t fbk_attention_scratch_floats(int T, int H, int D, int max_ctx)
     return (size_t)T * H * n_splits * (D + 2);
 }
 
+// Scratch one fbk_attention call of T tokens with this max_ctx uses.
+extern "C" size_t fbk_attention_call_floats(int T, int H, int D, int max_ctx) {
+    const int nw = attn_warps(max_ctx);
+    const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
+    return (size_t)T * H * n_splits * (D + 2);
+}
+
 extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
                              float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st) {
     if (T <= 0) return 0;
@@ -1075,7 +1082,7 @@ extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int
     if (G > kMaxG || (D != 64 && D != 128)) return (int)cudaErrorInvalidValue;
     const int nw = attn_warps(max_ctx);
     const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
-    if ((size_t)T * H * n_splits * (D + 2) > scratch_floats) return (int)cudaErrorInvalidValue;
+    if (fbk_attention_call_floats(T, H, D, max_ctx) > scratch_floats) return (int)cudaErrorInvalidValue;
     dim3 grid(n_splits, HKV, T);
     cudaError_t e;
     if (kv.f16) {

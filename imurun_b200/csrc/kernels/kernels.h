@@ -148,6 +148,8 @@ int fbk_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv,
                     cudaStream_t st);
 // Scratch (floats) fbk_attention needs for T tokens at contexts <= max_ctx.
 size_t fbk_attention_scratch_floats(int T, int H, int D, int max_ctx);
+// scratch one fbk_attention call with exactly this max_ctx needs
+size_t fbk_attention_call_floats(int T, int H, int D, int max_ctx);
 // Causal GQA attention for T query tokens, output [T][H*D]; max_ctx bounds
 // every tok_pos[t] + 1 (it sizes the key splits). D must be 64 or 128.
 int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
@@ -171,6 +173,13 @@ int fbk_add(float* y, const float* x, size_t n, cudaStream_t st);
 // Device-side wait of ns nanoseconds (profiling aid).
 int fbk_delay(unsigned long long ns, cudaStream_t st);
 int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st);
+// Greedy sampling with a repetition penalty on one row of n logits: each of
+// the n_recent ids (device array, the sampler's window, <= kMaxRecent)
+// penalises its logit once per occurrence, then out[0] = first index of the
+// maximum. x is read, not modified.
+constexpr int kMaxRecent = 256;
+int fbk_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty, int32_t* out,
+                         cudaStream_t st);
 // Argmax keys (value, first index) accumulated by a GEMV's epilogue
 // (GemvSeg::amax): decode them into out[t] / advance a greedy loop like
 // fbk_greedy_advance, and reset the keys for the next step.

@@ -86,6 +86,67 @@ __global__ void k_argmax(const float* __restrict__ x, int n, int ldx, int32_t* o
     }
 }
 
+// Repetition penalty, then the first index of the maximum, over one row of
+// logits: the greedy branch of the sampler on the device. Every occurrence of
+// an id in `recent` (the sampler's window, oldest first) applies
+// v = v > 0 ? v / p : v * p once (src/sampler.cpp: penalise, then argmax), so
+// an id seen c times is penalised c times in a row. A bitmap of the window's
+// ids in shared memory keeps the scan at one load per logit.
+__global__ void k_argmax_penalized(const float* __restrict__ x, int n, const int32_t* __restrict__ recent,
+                                   int n_recent, float penalty, int32_t* out) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ uint32_t s_bits[];
+    __shared__ int s_id[kMaxRecent];
+    __shared__ float s_val[kMaxRecent];
+    const int words = (n + 31) >> 5;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) s_bits[i] = 0u;
+    __syncthreads();
+    if (threadIdx.x < n_recent) {
+        const int id = recent[threadIdx.x];
+        int first = 1, count = 0;
+        for (int j = 0; j < n_recent; ++j) {
+            if (recent[j] == id) {
+                if (j < (int)threadIdx.x) first = 0;
+                ++count;
+            }
+        }
+        s_id[threadIdx.x] = (first && id >= 0 && id < n) ? id : -1;
+        if (s_id[threadIdx.x] >= 0) {
+            float v = x[id];
+            for (int c = 0; c < count; ++c) v = v > 0.0f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
+            s_val[threadIdx.x] = v;
+            atomicOr(&s_bits[id >> 5], 1u << (id & 31));
+        }
+    }
+    __syncthreads();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = x[i];
+        if (s_bits[i >> 5] & (1u << (i & 31))) {
+            for (int j = 0; j < n_recent; ++j)
+                if (s_id[j] == i) { v = s_val[j]; break; }
+        }
+        if (v > bv) { bv = v; bi = i; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        out[0] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
 // Router: softmax over NE logits (src/ops.cpp:40-55), top-K by probability
 // (ties: lower expert first), renormalised when `norm` (src/model.cpp:1529-1550).
 __global__ void k_moe_route(const float* __restrict__ logits, int T, int NE, int K, int norm, int32_t* sel,
@@ -266,6 +327,21 @@ extern "C" int fbk_add(float* y, const float* x, size_t n, cudaStream_t st) {
 extern "C" int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStream_t st) {
     if (rows <= 0) return 0;
     return (int)fbk_launch(k_argmax, dim3(rows), dim3(1024), 0, st, x, n, ldx, out);
+}
+
+extern "C" int fbk_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty,
+                                    int32_t* out, cudaStream_t st) {
+    if (n <= 0 || n_recent < 0 || n_recent > kMaxRecent) return (int)cudaErrorInvalidValue;
+    const size_t smem = sizeof(uint32_t) * (size_t)((n + 31) / 32);
+    if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        const cudaError_t e = cudaFuncSetAttribute(k_argmax_penalized, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   200 * 1024);
+        if (e != cudaSuccess) return (int)e;
+        attr = true;
+    }
+    return (int)fbk_launch(k_argmax_penalized, dim3(1), dim3(1024), smem, st, x, n, recent, n_recent, penalty, out);
 }
 
 extern "C" int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel,

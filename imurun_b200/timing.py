@@ -72,19 +72,22 @@ def prefill(tokens: int, layers: int) -> dict:
     return {"tokens": tokens, "layers": layers, "seconds": round(dt, 5), "tok_s": round(tokens / dt, 1)}
 
 
-def greedy(layers: int, steps: int) -> dict:
-    """Greedy decode from an empty context on a Llama-3-8B-shaped model of
-    `layers` layers: with no prefill, the first streamed-GEMV launches are
-    layer 0's qkv, o, gate/up and down (a small case for ncu captures)."""
+def greedy(layers: int, steps: int, prompt: int = 0) -> dict:
+    """Greedy decode on a Llama-3-8B-shaped model of `layers` layers, after a
+    prefill of `prompt` random ids (none by default: the first streamed-GEMV
+    launches are then layer 0's qkv, o, gate/up and down, a small case for
+    ncu captures; with a prompt, the decode steps see a realistic context)."""
     import os
     import time
     from . import synth
     from .native import Model
     cfg = synth.preset("llama8b") if layers == 32 else synth.preset("llama8b", layers=layers)
     path = synth.cached(cfg, os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
-    with Model(path, 1024) as m:
+    ids = np.random.default_rng(1).integers(3, 128256, max(prompt, 1)).astype(np.int32)
+    with Model(path, max(1024, (prompt + steps + 64 + 255) // 256 * 256)) as m:
+        first = int(np.argmax(m.prefill(ids, 0))) if prompt > 0 else 5
         t0 = time.perf_counter()
-        out = m.greedy(5, steps)
+        out = m.greedy(first, steps)
         dt = time.perf_counter() - t0
     return {"layers": layers, "steps": steps, "ids": [int(v) for v in out], "seconds": round(dt, 5)}
 
@@ -110,12 +113,13 @@ def main() -> None:
     gr = sub.add_parser("greedy")
     gr.add_argument("--layers", type=int, default=2)
     gr.add_argument("--steps", type=int, default=3)
+    gr.add_argument("--prompt", type=int, default=0)
     a = ap.parse_args()
     if a.cmd == "prefill":
         print(json.dumps(prefill(a.tokens, a.layers)), flush=True)
         return
     if a.cmd == "greedy":
-        print(json.dumps(greedy(a.layers, a.steps)), flush=True)
+        print(json.dumps(greedy(a.layers, a.steps, a.prompt)), flush=True)
         return
     lib = native.load_library()
     if a.cmd == "matmul":

@@ -90,21 +90,34 @@ FISH_API int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, fl
  *   q [T][H*D] f32, out [T][H*D] f32, k and v [n_keys][HKV*D] as fp16
  *   (kv_f16=1) or f32; every pointer 16-byte aligned; the call is queued on
  *   `stream` (a cudaStream_t, NULL = default stream) and returns without
- *   waiting for it.
+ *   waiting for it. Token t sits at position pos0+t and attends to keys
+ *   [0, pos0+t]; only rows [0, pos0+T) of k and v are read, so n_keys (which
+ *   must be >= pos0+T) is only the caller's bound on those buffers.
  * Its scratch (split partials, positions, an identity page table) is one
  * fixed __device__ array per device, 8 MiB of partials: pos0+T <= 8192,
  * T <= 256 and T*H*n_splits*(D+2) <= 2^21 floats, n_splits = ceil((pos0+T)/32)
  * up to 2048 keys and ceil((pos0+T)/128) above; larger calls return -1.
  * The first call on a device resolves that array's address and initialises
  * it (a kernel on `stream`, then a wait for that stream); make it before any
- * stream capture. Partials need no clearing; every split writes its own. Every call on
- * a device shares the array, so calls that overlap on the GPU (different
- * streams, no ordering between them) race and corrupt each other's output. */
+ * stream capture. After cudaDeviceReset the next call does this again (the
+ * device's new context is detected by its id). Partials need no clearing;
+ * every split writes its own. Every call on a device shares the array, so
+ * calls that overlap on the GPU (different streams, no ordering between
+ * them) race and corrupt each other's output. */
 FISH_API int fbx_attention_static(const float* q, const void* k, const void* v, int kv_f16, int n_keys, int H,
                                   int HKV, int D, int pos0, int T, float* out, void* stream);
 
 /* First index of the maximum per row (reference model.cpp:1939-1946). */
 FISH_API int fbx_argmax(const float* x, int rows, int n, int32_t* out);
+
+/* The sampler's greedy branch on the device: every occurrence of an id in
+ * recent[0..n_recent) (the penalty window, oldest first, n_recent <= 256)
+ * applies the repetition penalty to its logit (v > 0 ? v / p : v * p), then
+ * out[0] = the first index of the maximum of x[0..n). Reference
+ * Sampler::penalise + greedy argmax (model/fish/src/sampler.cpp:42-132);
+ * the generation loop runs it for temperature <= 0. Host buffers. */
+FISH_API int fbx_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty,
+                                  int32_t* out);
 
 /* Embedding row gather + dequantisation (reference dequant_row,
  * quant.cpp:470-506) for ids[0..T) of a [n_rows][E] table. */

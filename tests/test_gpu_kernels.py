@@ -287,6 +287,36 @@ def test_argmax_first_index(lib):
     assert list(out) == [5, 7, 0]
 
 
+@pytest.mark.parametrize("vocab,pen,last_n", [(32000, 1.1, 64), (128256, 1.3, 64), (152064, 0.8, 32),
+                                               (1000, 1.1, 200), (50000, 1.0, 64)])
+def test_argmax_penalized_matches_host_sampler(lib, vocab, pen, last_n):
+    """The generation loop's greedy branch on the device (penalty per
+    occurrence in the window, then the first index of the maximum) equals
+    the host sampler's (fbx_sample at temperature 0, pinned to the
+    reference's Sampler::sample on the CPU), recent ids repeated and the
+    penalised ids among the likely ones."""
+    lib.fbx_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                               ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_ulonglong,
+                               ctypes.c_int, ctypes.c_void_p]
+    lib.fbx_sample.restype = ctypes.c_int
+    rng = np.random.default_rng(vocab + int(pen * 10))
+    for trial in range(20):
+        logits = (rng.standard_normal(vocab) * 2.0).astype(np.float32)
+        recent = rng.integers(0, vocab, 128).astype(np.int32)
+        recent[-10:-5] = recent[-5:]                      # repeats: penalised twice
+        logits[recent[-6:]] = np.abs(logits[recent[-6:]]) + 6.0 + 0.01 * trial
+        logits[recent[-1]] = -logits[recent[-1]]          # a negative penalised logit
+        if trial % 5 == 0:
+            logits[7] = logits.max()                       # ties resolve to the first index
+        want = np.zeros(1, np.int32)
+        assert lib.fbx_sample(_p(logits), vocab, 0.0, 40, 0.9, pen, last_n, _p(recent), recent.size, 1, 1,
+                              _p(want)) == 0
+        window = recent[max(0, recent.size - last_n):].copy()
+        got = np.zeros(1, np.int32)
+        assert lib.fbx_argmax_penalized(_p(logits), vocab, _p(window), window.size, pen, _p(got)) == 0
+        assert int(got[0]) == int(want[0]), (trial, int(got[0]), int(want[0]))
+
+
 @pytest.mark.parametrize("t", [8, 12, 14])
 def test_embed_dequant_bit_exact(lib, oracle, t):
     rng = np.random.default_rng(t)

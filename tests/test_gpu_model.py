@@ -226,6 +226,75 @@ def test_prefix_cache_hit_through_generate(gpu, tiny_gguf):
     lib.fish_destroy(ctx)
 
 
+@pytest.mark.parametrize("penalty", [1.0, 1.3])
+def test_greedy_generate_device_argmax_matches_host_sampler(gpu, tiny_gguf, penalty):
+    """fish_generate at temperature 0 takes the sampler's greedy branch on the
+    device (penalty + first-index argmax, only the id copied back). The same
+    loop replayed step by step with the logits copied to the host and the
+    host sampler (fbx_sample, pinned to the reference's Sampler::sample)
+    must give the same token callbacks (ids and UTF-8 chunks)."""
+    import ctypes
+    from imurun_b200 import native
+    lib = native.load_library()
+    lib.fbx_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                               ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_ulonglong,
+                               ctypes.c_int, ctypes.c_void_p]
+    lib.fbx_sample.restype = ctypes.c_int
+    ctx = lib.fish_create()
+    assert lib.fish_load(ctx, str(tiny_gguf).encode(), 2048) == 0
+    vocab = 32000
+    prompt = b"t17 t99 t4000 the quick brown fox t12 t12 t12 jumps"
+    n_gen = 24
+    chunks = []
+
+    def on_token(text, tid, user):
+        t = ctypes.string_at(text) if text else b""
+        chunks.append(b"%d %d\n" % (tid, len(t)) + t)
+
+    cb = native.FISH_TOKEN_CB(on_token)
+    assert lib.fish_generate(ctx, prompt, 1, n_gen, 0.0, 40, 0.9, penalty, cb, None) >= 0
+    got = b"".join(chunks)
+    # replay: same prompt ids, logits to the host, host sampler
+    lib.fish_reset(ctx)
+    ids = np.zeros(512, np.int32)
+    n = lib.fish_tokenize(ctx, prompt, 1, ids.ctypes.data, 512)
+    assert 0 < n < 512
+    ids = ids[:n].copy()
+    lg = np.zeros((n, vocab), np.float32)
+    am = np.zeros(n, np.int32)
+    assert lib.fish_decode_ids(ctx, ids.ctypes.data, n, 0, lg.ctypes.data, am.ctypes.data) == 0
+    recent = list(ids[-128:])
+    logits = lg[-1].copy()
+    out = []
+    pos = n
+    one = np.zeros(1, np.int32)
+    for _ in range(n_gen):
+        r = np.array(recent, np.int32)
+        nxt = np.zeros(1, np.int32)
+        assert lib.fbx_sample(logits.ctypes.data, vocab, 0.0, 40, 0.9, penalty, 64, r.ctypes.data, r.size, 1, 1,
+                              nxt.ctypes.data) == 0
+        tok = int(nxt[0])
+        if tok == 2:   # end of generation
+            break
+        out.append(tok)
+        recent.append(tok)
+        recent = recent[-128:]
+        one[0] = tok
+        lg1 = np.zeros((1, vocab), np.float32)
+        assert lib.fish_decode_ids(ctx, one.ctypes.data, 1, pos, lg1.ctypes.data, am.ctypes.data) == 0
+        logits = lg1[0].copy()
+        pos += 1
+    # the callbacks the loop's emitter makes for these ids
+    o = np.array(out, np.int32)
+    buf = ctypes.create_string_buffer(1 << 16)
+    lib.fbx_stream_gguf.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+    lib.fbx_stream_gguf.restype = ctypes.c_int
+    need = lib.fbx_stream_gguf(str(tiny_gguf).encode(), o.ctypes.data, o.size, buf, 1 << 16)
+    assert 0 <= need < (1 << 16)
+    assert got == buf.raw[:need], (got[:120], buf.raw[:120])
+    lib.fish_destroy(ctx)
+
+
 class PageModel:
     """CPU model of the engine's page allocator: LIFO free list, refcounts,
     shared full pages on fork, copy-on-write of a shared partial page."""

@@ -1,6 +1,7 @@
 """fbx_attention_static — the attention entry point that allocates nothing —
-against fbx_attention (which allocates its own device buffers) on the same
-inputs, through the C ABI, on two calls in a row.
+against fbx_attention (which allocates its own device buffers) and against
+the CPU oracle's attention on the same inputs, through the C ABI, on two
+calls in a row.
 
 The file name sorts last so it also runs after every other test in one
 process; it must pass alone in a fresh process too. Device buffers for the
@@ -24,6 +25,12 @@ def env():
     return native.load_library(), torch
 
 
+@pytest.fixture(scope="module")
+def oracle():
+    from oracle.binding import Oracle
+    return Oracle()
+
+
 def _p(a):
     return a.ctypes.data
 
@@ -36,13 +43,15 @@ def _host_reference(lib, q, k, v, n_keys, H, HKV, D, pos0, T, f16):
 
 
 # (T, pos0, H, HKV, D): decode at a short and a long context (1 and 4 warps
-# per split), a small prefill chunk, and MHA with D = 64.
-SHAPES = [(1, 300, 32, 8, 128), (1, 3000, 32, 8, 128), (7, 120, 28, 4, 128), (5, 0, 8, 8, 64)]
+# per split), a small prefill chunk, MHA with D = 64, and a 16-token chunk
+# just past 2048 keys (the documented partials limit admits it).
+SHAPES = [(1, 300, 32, 8, 128), (1, 3000, 32, 8, 128), (7, 120, 28, 4, 128), (5, 0, 8, 8, 64),
+          (16, 2984, 32, 8, 128)]
 
 
 @pytest.mark.parametrize("f16", [0, 1])
 @pytest.mark.parametrize("T,pos0,H,HKV,D", SHAPES)
-def test_static_matches_allocating_entry(env, f16, T, pos0, H, HKV, D):
+def test_static_matches_allocating_entry(env, oracle, f16, T, pos0, H, HKV, D):
     lib, torch = env
     dev = torch.device("cuda:0")
     n_keys = pos0 + T
@@ -68,6 +77,12 @@ def test_static_matches_allocating_entry(env, f16, T, pos0, H, HKV, D):
         # tolerance (2e-5 of the output scale) is the bar
         assert np.all(np.isfinite(got))
         assert np.max(np.abs(got - want)) <= 2e-5 * max(1.0, float(np.max(np.abs(want))))
+        # and against the CPU oracle (cache values rounded to fp16 when the
+        # cache is fp16), with the attention tests' bar
+        if f16:
+            k, v = oracle.fp16_round(k), oracle.fp16_round(v)
+        ref = oracle.attention(q, k, v, H, HKV, D, pos0, T, 1.0 / np.sqrt(D))
+        assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref))))
 
 
 def test_static_rejects_oversize(env):
