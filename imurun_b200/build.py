@@ -34,7 +34,7 @@ if os.environ.get("FISH_TRACE_CTA_BUILD", "0") not in ("", "0"):
 COMMON += [d for d in os.environ.get("FISH_NVCC_DEFINES", "").split() if d.startswith("-D")]
 
 SOURCES = [
-    "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu", "kernels/gemm.cu",
+    "kernels/quant_act.cu", "kernels/gemv.cu", "kernels/attention.cu", "kernels/misc.cu", "kernels/step.cu", "kernels/gemm.cu", "kernels/gemm_tc.cu",
     "gguf.cpp", "tokenizer.cpp", "sampler.cpp", "engine.cpp", "c_api.cpp", "kernel_api.cpp",
     "attention_static.cu",
 ]

@@ -704,6 +704,33 @@ int fish_decode_ids(fish_ctx* ctx, const int32_t* ids, int n, int pos0, float* l
     return 0;
 }
 
+int fbx_layer_probe(fish_ctx* ctx, int layer, int pos0, const float* x_in, int n_tok, float* x_out,
+                    fbx_layer_probe_out* out) {
+    if (!ctx || !x_in || !x_out || !out || n_tok <= 0) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (!need_model(ctx)) return -1;
+    fb::Engine& e = *ctx->eng;
+    fb::LayerProbe p;
+    std::string err;
+    if (!e.layer_probe(layer, pos0, x_in, n_tok, x_out, &p, &err)) { ctx->err = err; return -1; }
+    ctx->cache_ids.clear();   // the sequence's KV no longer matches any id list
+    for (int st = 0; st < 4; ++st) {
+        out->rows[st] = p.rows[st];
+        out->K[st] = p.K[st];
+        out->has_k[st] = p.has_k[st] ? 1 : 0;
+        out->has_32[st] = p.has_32[st] ? 1 : 0;
+        if (out->f[st] && !p.f[st].empty()) std::memcpy(out->f[st], p.f[st].data(), sizeof(float) * p.f[st].size());
+        if (out->qk[st] && !p.rk[st].empty()) std::memcpy(out->qk[st], p.rk[st].data(), p.rk[st].size());
+        if (out->q32[st] && !p.r32[st].empty()) std::memcpy(out->q32[st], p.r32[st].data(), p.r32[st].size());
+    }
+    out->silu_in_prologue = p.f[4].empty() ? 0 : 1;
+    if (out->silu_in_prologue) {
+        if (out->gate3) std::memcpy(out->gate3, p.f[4].data(), sizeof(float) * p.f[4].size());
+        if (out->up3) std::memcpy(out->up3, p.f[5].data(), sizeof(float) * p.f[5].size());
+    }
+    return 0;
+}
+
 int fish_tp_unique_id(void* out, int cap) {
     if (!out || cap < (int)sizeof(ncclUniqueId)) return (int)sizeof(ncclUniqueId);
     const fb::NcclApi* nc = fb::nccl_api(nullptr);

@@ -145,6 +145,8 @@ Engine::~Engine() {
     cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
     cudaFree(tp_tmp_); cudaFree(tp_logits_); cudaFree(sel_loc_);
     if (nccl_) nccl_api(nullptr)->comm_destroy((ncclComm_t)nccl_);   // after the graphs that hold its calls
+    if (probe_img_) cudaFree(probe_img_);
+    if (probe_h_) cudaFree(probe_h_);
     if (recent_dev_) cudaFree(recent_dev_);
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (ev0_) cudaEventDestroy(ev0_);
@@ -825,6 +827,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
         set_act_rows(g, a, t0, g.K);
         if (pro) g.pro = *pro;
         g.swiglu = swiglu ? 1 : 0;
+        g.img_dump = dump_img_ ? dump_img_ + (size_t)(t0 / chunk) * kProbeChunkBytes : nullptr;
         double bytes = 0.0;
         for (int i = 0; i < n; ++i) {
             GemvSeg& s = g.seg[i];
@@ -867,6 +870,7 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         g.T = nt;
         set_act_rows(g, a, t0, g.K);
         if (pro) g.pro = *pro;
+        g.img_dump = dump_img_ ? dump_img_ + (size_t)(t0 / chunk) * kProbeChunkBytes : nullptr;
         g.xf = xf ? xf + (size_t)t0 * ldxf : nullptr;
         g.ldxf = ldxf;
         GemvSeg& s = g.seg[0];
@@ -1125,13 +1129,14 @@ bool Engine::run_step(int sid, int n_steps, int32_t* out_dev, std::string* err) 
 
 // ------------------------------------------------------------------ forward
 
-bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
+bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int l0, int l1) {
     const Config& c = cfg_;
     const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim(), H = c.n_head, HKV = c.n_head_kv, D = c.head_dim;
     const float scale = 1.0f / std::sqrt((float)D);
     const KvView kv = kv_view();
     ActQ a = act_;
-    for (int li = 0; li < c.n_layers; ++li) {
+    if (l1 < 0) l1 = c.n_layers;
+    for (int li = l0; li < l1; ++li) {
         const DevLayer& L = layers_[li];
         a.K = E;
         {
@@ -1139,11 +1144,16 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
             float* ys[3] = {q_, k_, v_};
             const int lds[3] = {Q, KV, KV};
             const float* bs[3] = {L.bq, L.bk, L.bv};
+            if (probe_ && !probe_float(0, x_, T, E, err)) return false;
             if (fusable(ws, 3, T)) {
                 const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.attn_norm, c.eps};
-                if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err, &pro)) return false;
+                if (probe_) dump_img_ = probe_img_;
+                const bool ok = gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err, &pro);
+                dump_img_ = nullptr;
+                if (!ok || (probe_ && !probe_image(0, T, E, err))) return false;
             } else {
                 CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.attn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+                if (probe_ && !probe_planes(0, a, T, E, want32_e_, wantk_e_, err)) return false;
                 if (!gemv_group(ws, ys, lds, bs, 3, a, T, EPI_STORE, err)) return false;
             }
         }
@@ -1174,11 +1184,16 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
             float* oy = tp ? tp_tmp_ : x_;
             const int oepi = tp ? EPI_STORE : EPI_ADD;
             const DevW* wo[1] = {&L.wo};
+            if (probe_ && !probe_float(1, attn_, T, Q, err)) return false;
             if (fusable(wo, 1, T)) {
                 const GemvPro pro{PRO_QUANT, attn_, Q, nullptr, 0, nullptr, 0.0f};
-                if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err, &pro)) return false;
+                if (probe_) dump_img_ = probe_img_;
+                const bool ok = gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err, &pro);
+                dump_img_ = nullptr;
+                if (!ok || (probe_ && !probe_image(1, T, Q, err))) return false;
             } else {
                 CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
+                if (probe_ && !probe_planes(1, a, T, Q, want32_q_, wantk_q_, err)) return false;
                 if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err)) return false;
             }
             if (tp && !tp_reduce_add(T, err)) return false;
@@ -1186,8 +1201,11 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
         a.K = E;
         const DevW* wgu[2] = {&L.wg, &L.wu};
         const bool fuse_ffn = c.n_experts == 0 && fusable(wgu, 2, T);
-        if (!fuse_ffn)
+        if (probe_ && !probe_float(2, x_, T, E, err)) return false;
+        if (!fuse_ffn) {
             CKP(PC_NORMQ, 0, fbk_rmsnorm_quant(x_, E, L.ffn_norm, c.eps, T, E, xb_, E, &a, want32_e_, wantk_e_, stream_));
+            if (probe_ && !probe_planes(2, a, T, E, want32_e_, wantk_e_, err)) return false;
+        }
         if (c.n_experts > 0) {
             const int NE = c.n_experts, K = c.n_experts_per_tok, F = c.n_ff_exp;
             if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
@@ -1206,7 +1224,11 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
                 }
             }
             a.K = F;
-            CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T * K, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
+            CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T * K, F, probe_ ? probe_h_ : nullptr, F, &a, want32_f_,
+                                                wantk_f_, stream_));
+            if (probe_ && (!probe_float(3, probe_h_, T * K, F, err) ||
+                           !probe_planes(3, a, T * K, F, want32_f_, wantk_f_, err)))
+                return false;
             for (int r = 0; r < T * K; ++r) {
                 const ActQ ar = act_row(a, r, F);
                 if (!gemv(L.down_exps, ar, 1, eo_ + (size_t)r * E, E, nullptr, EPI_STORE, nullptr, 0, esel + r, err))
@@ -1226,7 +1248,10 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
                 const int lds[2] = {F, F};
                 if (fuse_ffn) {
                     const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.ffn_norm, c.eps};
-                    if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro, true)) return false;
+                    if (probe_) dump_img_ = probe_img_;
+                    const bool ok = gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro, true);
+                    dump_img_ = nullptr;
+                    if (!ok || (probe_ && !probe_image(2, T, E, err))) return false;
                 } else {
                     if (!gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
                 }
@@ -1238,17 +1263,186 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err) {
             const DevW* wd[1] = {&L.wd};
             if (fuse_ffn && fusable(wd, 1, T)) {   // h = silu(g) * u already in g_
                 const GemvPro pro{PRO_QUANT, g_, F, nullptr, 0, nullptr, 0.0f};
-                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro)) return false;
+                if (probe_ && !probe_float(3, g_, T, F, err)) return false;
+                if (probe_) dump_img_ = probe_img_;
+                const bool ok = gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro);
+                dump_img_ = nullptr;
+                if (!ok || (probe_ && !probe_image(3, T, F, err))) return false;
             } else if (fusable(wd, 1, T)) {
                 const GemvPro pro{PRO_SILU, g_, F, u_, F, nullptr, 0.0f};
-                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro)) return false;
+                if (probe_ && (!probe_float(4, g_, T, F, err) || !probe_float(5, u_, T, F, err))) return false;
+                if (probe_) dump_img_ = probe_img_;
+                const bool ok = gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err, &pro);
+                dump_img_ = nullptr;
+                if (!ok || (probe_ && !probe_image(3, T, F, err))) return false;
             } else {
-                CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, nullptr, 0, &a, want32_f_, wantk_f_, stream_));
+                CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, F, u_, F, T, F, probe_ ? probe_h_ : nullptr, F, &a, want32_f_,
+                                                    wantk_f_, stream_));
+                if (probe_ && (!probe_float(3, probe_h_, T, F, err) ||
+                               !probe_planes(3, a, T, F, want32_f_, wantk_f_, err)))
+                    return false;
                 if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err)) return false;
             }
             if (tp && !tp_reduce_add(T, err)) return false;
         }
     }
+    return true;
+}
+
+// ------------------------------------------------------------------ layer probe
+
+static_assert(kXChunkBytes == kXChunk, "probe image parsing follows the streamed GEMV's image layout");
+
+bool Engine::probe_float(int idx, const float* dev, int rows, int K, std::string* err) {
+    LayerProbe& p = *probe_;
+    p.f[idx].resize((size_t)rows * K);
+    p.rows[idx] = rows;
+    p.K[idx] = K;
+    CK(cudaMemcpyAsync(p.f[idx].data(), dev, sizeof(float) * (size_t)rows * K, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    return true;
+}
+
+namespace {
+// Activation records in the reference's byte layout (quant.h:58-70).
+void put_k_record(uint8_t* r, float d, const int16_t* bsums, const int8_t* qs) {
+    std::memcpy(r, &d, 4);
+    std::memcpy(r + 4, bsums, 16);
+    std::memcpy(r + 20, qs, 256);
+}
+void put_32_record(uint8_t* r, float d, const int8_t* qs) {
+    int32_t sum = 0;
+    for (int i = 0; i < 32; ++i) sum += qs[i];
+    std::memcpy(r, &d, 4);
+    std::memcpy(r + 4, &sum, 4);
+    std::memcpy(r + 8, qs, 32);
+}
+}  // namespace
+
+bool Engine::probe_planes(int stage, const ActQ& a, int rows, int K, bool want32, bool wantk, std::string* err) {
+    LayerProbe& p = *probe_;
+    CK(cudaStreamSynchronize(stream_));
+    p.has_k[stage] = wantk && K % 256 == 0;
+    p.has_32[stage] = want32 && K % 32 == 0;
+    p.rows[stage] = rows;
+    p.K[stage] = K;
+    if (p.has_k[stage]) {
+        const int nb = K / 256;
+        std::vector<int8_t> q((size_t)rows * a.ld);
+        std::vector<float> d((size_t)rows * nb);
+        std::vector<int16_t> bs((size_t)rows * (K / 32));
+        CK(cudaMemcpy(q.data(), a.qk, q.size(), cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(d.data(), a.dk, sizeof(float) * d.size(), cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(bs.data(), a.bsk, sizeof(int16_t) * bs.size(), cudaMemcpyDeviceToHost));
+        p.rk[stage].resize((size_t)rows * nb * 276);
+        for (int t = 0; t < rows; ++t)
+            for (int c = 0; c < nb; ++c)
+                put_k_record(&p.rk[stage][((size_t)t * nb + c) * 276], d[(size_t)t * nb + c],
+                             &bs[(size_t)t * (K / 32) + 8 * c], &q[(size_t)t * a.ld + 256 * c]);
+    }
+    if (p.has_32[stage]) {
+        const int nb = K / 32;
+        std::vector<int8_t> q((size_t)rows * a.ld);
+        std::vector<float> d((size_t)rows * nb);
+        CK(cudaMemcpy(q.data(), a.q32, q.size(), cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(d.data(), a.d32, sizeof(float) * d.size(), cudaMemcpyDeviceToHost));
+        p.r32[stage].resize((size_t)rows * nb * 40);
+        for (int t = 0; t < rows; ++t)
+            for (int b = 0; b < nb; ++b)
+                put_32_record(&p.r32[stage][((size_t)t * nb + b) * 40], d[(size_t)t * nb + b], &q[(size_t)t * a.ld + 32 * b]);
+    }
+    return true;
+}
+
+bool Engine::probe_image(int stage, int rows, int K, std::string* err) {
+    LayerProbe& p = *probe_;
+    CK(cudaStreamSynchronize(stream_));
+    p.rows[stage] = rows;
+    p.K[stage] = K;
+    const int nbk = K / 256, nb32 = K / 32;
+    int done = 0;
+    std::vector<uint8_t> buf;
+    for (int ch = 0; done < rows; ++ch) {
+        if ((size_t)(ch + 1) * kProbeChunkBytes > probe_img_bytes_) { if (err) *err = "probe: too many chunks"; return false; }
+        int hdr[4] = {0, 0, 0, 0};
+        const uint8_t* src = probe_img_ + (size_t)ch * kProbeChunkBytes;
+        CK(cudaMemcpy(hdr, src, sizeof(hdr), cudaMemcpyDeviceToHost));
+        const int xk = hdr[0], x32 = hdr[1], tc = hdr[2], n256 = hdr[3];
+        if (tc <= 0 || done + tc > rows || n256 != (K + 255) / 256 ||
+            16 + (size_t)tc * (xk + x32) > kProbeChunkBytes) {
+            if (err) *err = "probe: bad activation image header";
+            return false;
+        }
+        buf.resize((size_t)tc * (xk + x32));
+        CK(cudaMemcpy(buf.data(), src + 16, buf.size(), cudaMemcpyDeviceToHost));
+        p.has_k[stage] = xk > 0 && K % 256 == 0;
+        p.has_32[stage] = x32 > 0 && K % 32 == 0;
+        if (p.has_k[stage]) {
+            p.rk[stage].resize((size_t)rows * nbk * 276);
+            for (int t = 0; t < tc; ++t) {
+                const uint8_t* b = buf.data() + (size_t)t * xk;
+                for (int c = 0; c < nbk; ++c) {
+                    float d;
+                    std::memcpy(&d, b + (size_t)n256 * (kXChunkBytes + 48) + 4 * c, 4);
+                    put_k_record(&p.rk[stage][((size_t)(done + t) * nbk + c) * 276], d,
+                                 reinterpret_cast<const int16_t*>(b + (size_t)n256 * kXChunkBytes + 16 * c),
+                                 reinterpret_cast<const int8_t*>(b + (size_t)c * kXChunkBytes));
+                }
+            }
+        }
+        if (p.has_32[stage]) {
+            p.r32[stage].resize((size_t)rows * nb32 * 40);
+            for (int t = 0; t < tc; ++t) {
+                const uint8_t* b = buf.data() + (size_t)tc * xk + (size_t)t * x32;
+                for (int blk = 0; blk < nb32; ++blk) {
+                    const int c = blk / 8, j = blk % 8;
+                    float d;
+                    std::memcpy(&d, b + (size_t)n256 * kXChunkBytes + 32 * c + 4 * j, 4);
+                    put_32_record(&p.r32[stage][((size_t)(done + t) * nb32 + blk) * 40], d,
+                                  reinterpret_cast<const int8_t*>(b + (size_t)c * kXChunkBytes + 32 * j));
+                }
+            }
+        }
+        done += tc;
+    }
+    return true;
+}
+
+bool Engine::layer_probe(int li, int pos0, const float* x_in, int T, float* x_out, LayerProbe* p, std::string* err) {
+    const Config& c = cfg_;
+    if (li < 0 || li >= c.n_layers || T <= 0 || T > kMaxBatch || pos0 < 0 || !x_in || !x_out || !p) {
+        if (err) *err = "probe: bad argument";
+        return false;
+    }
+    if (tp_world_ > 1) { if (err) *err = "probe: single-GPU engines only"; return false; }
+    Seq& s = seqs_[0];
+    if (pos0 > s.len) { if (err) *err = "probe: pos0 beyond the sequence"; return false; }
+    if (!ensure_pages(0, pos0 + T, err)) return false;
+    const size_t img_need = (size_t)((T + 3) / 4 + 1) * kProbeChunkBytes;
+    if (probe_img_bytes_ < img_need) {
+        if (probe_img_) cudaFree(probe_img_);
+        probe_img_ = nullptr;
+        probe_img_bytes_ = 0;
+        CK(cudaMalloc(&probe_img_, img_need));
+        probe_img_bytes_ = img_need;
+    }
+    const int F = c.n_experts > 0 ? c.n_ff_exp : c.n_ff;
+    const size_t h_need = (size_t)kMaxBatch * std::max(1, c.n_experts_per_tok) * F;
+    if (!probe_h_) CK(cudaMalloc(&probe_h_, sizeof(float) * h_need));
+    std::vector<int32_t> ids(T, 0);
+    std::vector<int> sids(T, 0), pos(T);
+    for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
+    if (!upload_tokens(ids.data(), sids.data(), pos.data(), T, err)) return false;
+    CK(cudaMemcpyAsync(x_, x_in, sizeof(float) * (size_t)T * c.n_embd, cudaMemcpyHostToDevice, stream_));
+    *p = LayerProbe{};
+    probe_ = p;
+    const bool ok = run_layers(T, pos0 + T, T == 1, err, li, li + 1);
+    probe_ = nullptr;
+    dump_img_ = nullptr;
+    if (!ok) return false;
+    CK(cudaMemcpyAsync(x_out, x_, sizeof(float) * (size_t)T * c.n_embd, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    s.len = std::max(s.len, pos0 + T);
     return true;
 }
 

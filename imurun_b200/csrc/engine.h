@@ -69,6 +69,22 @@ struct DevLayer {
     float *q_norm = nullptr, *k_norm = nullptr;
 };
 
+// Debug record of one layer's int8 activations (Engine::layer_probe). Stage
+// s: 0 the attention-norm input, 1 the attention output, 2 the FFN-norm
+// input, 3 the SwiGLU product. f[s]: the float rows the stage quantised
+// (0, 2: before the RMSNorm); f[4], f[5]: gate and up rows when the product
+// is formed inside the down projection's prologue (f[3] then stays empty).
+// rk / r32: the int8 activations the kernels built, as the reference's
+// Q8ActK (276 B per 256 values) / Q8Act (40 B per 32 values) records.
+struct LayerProbe {
+    std::vector<float> f[6];
+    std::vector<uint8_t> rk[4], r32[4];
+    int rows[6] = {}, K[6] = {};
+    bool has_k[4] = {}, has_32[4] = {};
+};
+constexpr size_t kProbeChunkBytes = 294912;   // one GEMV launch's image dump (header + 4 tokens at K <= 28672)
+constexpr int kXChunkBytes = 272;             // image bytes per 256 int8 values (stream_common.cuh kXChunk)
+
 struct Seq {
     bool open = false;
     int len = 0;                 // positions holding valid KV
@@ -135,6 +151,11 @@ public:
     // the first index of the maximum; only that id comes back to the host.
     bool decode_argmax(int sid, int32_t id, const int32_t* recent, int n_recent, float penalty, int32_t* out,
                        std::string* err);
+    // Debug: run layer li alone on T hidden rows x_in (host, [T][E]) at
+    // positions pos0.. of sequence 0 (its KV rows of that layer are written),
+    // x_out = the layer's output rows; *p records every int8 activation the
+    // kernels built and the float rows they came from. Eager launches, one GPU.
+    bool layer_probe(int li, int pos0, const float* x_in, int T, float* x_out, LayerProbe* p, std::string* err);
     // One token for each of n sequences (n <= kMaxBatch).
     bool decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err);
     // Greedy decode of n_steps on the device with a captured CUDA graph.
@@ -179,7 +200,15 @@ private:
     void write_page_table(int sid);
     // distinct: the T tokens belong to T different sequences (decode steps),
     // so attention can append each token's K/V inside the fused kernel
-    bool run_layers(int T, int max_ctx, bool distinct, std::string* err);
+    bool run_layers(int T, int max_ctx, bool distinct, std::string* err, int l0 = 0, int l1 = -1);
+    bool probe_float(int idx, const float* dev, int rows, int K, std::string* err);
+    bool probe_planes(int stage, const ActQ& a, int rows, int K, bool want32, bool wantk, std::string* err);
+    bool probe_image(int stage, int rows, int K, std::string* err);
+    LayerProbe* probe_ = nullptr;
+    uint8_t* probe_img_ = nullptr;     // device: image dumps of the fused GEMV prologues
+    size_t probe_img_bytes_ = 0;
+    float* probe_h_ = nullptr;         // device: SwiGLU products of the unfused path
+    uint8_t* dump_img_ = nullptr;      // set around a probed fused GEMV call
     // keys (nullable): argmax keys per row accumulated by the output GEMV;
     // returns in *keyed whether they were (streamed kernel only)
     // need_logits = false: with argmax keys and tensor parallelism, the

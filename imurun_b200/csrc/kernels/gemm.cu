@@ -504,7 +504,9 @@ extern "C" int fbk_gemm(const GemvArgs* a, cudaStream_t st) {
     for (int s = 0; s < a->nseg; ++s) {
         const GemvSeg& g = a->seg[s];
         cudaError_t e;
-        if (g.type == T_Q4_K) e = launch_gemm<T_Q4_K>(g, a->act, a->K, a->T, err, st);
+        if (g.type == T_Q4_K && fbk_gemm_tc_eligible(&g, &a->act, a->K, a->T))
+            e = (cudaError_t)fbk_gemm_tc(&g, &a->act, a->K, a->T, err, st);
+        else if (g.type == T_Q4_K) e = launch_gemm<T_Q4_K>(g, a->act, a->K, a->T, err, st);
         else if (g.type == T_Q6_K) e = launch_gemm<T_Q6_K>(g, a->act, a->K, a->T, err, st);
         else e = launch_gemm<T_Q8_0>(g, a->act, a->K, a->T, err, st);
         if (e != cudaSuccess) return (int)e;

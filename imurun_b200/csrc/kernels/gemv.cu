@@ -455,6 +455,20 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     const bool wantk = jobs.xk_bytes > 0, want32 = jobs.x32_bytes > 0;
     build_ximage<PM>(args, xi, wantk, want32, s_part, wv, tr ? s_tseq : -1);
     consumers_sync();
+    if (args.img_dump && blockIdx.x == 0) {
+        // debug record of the prologue's output (layer probes): the image is
+        // the same in every CTA, so CTA 0's copy stands for all of them
+        if (threadIdx.x == 0) {
+            int* hdr = reinterpret_cast<int*>(args.img_dump);
+            hdr[0] = jobs.xk_bytes;
+            hdr[1] = jobs.x32_bytes;
+            hdr[2] = args.T;
+            hdr[3] = xi.n256;
+        }
+        const size_t nb = (size_t)args.T * (jobs.xk_bytes + jobs.x32_bytes);
+        for (size_t i = (size_t)threadIdx.x * 16; i < nb; i += (size_t)kConsumers * 32 * 16)
+            *reinterpret_cast<uint4*>(args.img_dump + 16 + i) = *reinterpret_cast<const uint4*>(xi.base + i);
+    }
     if (tr && threadIdx.x == 0) trace_ev(TR_GEMV, EV_READY, s_tseq);
     trace_cta(tcb, 2, TR_GEMV, EV_C_READY);
     WaitFail wf{};

@@ -74,6 +74,9 @@ struct GemvArgs {
     int swiglu;             // streamed kernel, 2 segments of equal rows (gate, up): the output
                             // is h = silu(gate) * up into segment 0's y (src/model.cpp:1501-1506)
     int* err;               // device error flag (nullable): 3 = weight read out of range
+    uint8_t* img_dump;      // debug (nullable, streamed kernel): CTA 0 copies its activation image here
+                            // after the prologue: 16-byte header (xk bytes, x32 bytes, T, n256 as int32)
+                            // then T * (xk + x32) bytes laid out as XImage (stream_common.cuh)
 };
 
 }  // namespace fb
@@ -94,6 +97,10 @@ int fbk_gemv_chunk(const fb::GemvArgs* args);
 // K % 256 == 0. fbk_gemm_eligible says whether a job qualifies
 // (FISH_NO_GEMM turns the path off).
 int fbk_gemm_eligible(const fb::GemvArgs* args);
+// Q4_K segments on the tcgen05 kernel (gemm_tc.cu): T >= 16, K % 256 == 0,
+// 16-byte aligned operands; fbk_gemm takes it for them when eligible.
+int fbk_gemm_tc_eligible(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T);
+int fbk_gemm_tc(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T, int* err, cudaStream_t st);
 int fbk_gemm(const fb::GemvArgs* args, cudaStream_t st);
 // 1 if fbk_gemv runs this call on the streamed kernel (the only one that
 // takes a prologue other than PRO_ACT).

@@ -23,6 +23,7 @@
 #include <cstring>
 #include <string>
 #include <thread>
+#include <map>
 #include <vector>
 
 namespace {
@@ -217,6 +218,102 @@ struct Writer {
     void kv_bool(const std::string& k, bool v) { str(k); u32(7); buf.push_back(v ? 1 : 0); }
 };
 
+// ---- byte-level BPE test vocabulary
+
+// GPT-2's byte alphabet: printable Latin-1 bytes keep their value, the
+// others map to 256, 257, ... in byte order (as UTF-8 text).
+std::string byte_char(int b) {
+    static std::vector<std::string> table = [] {
+        std::vector<std::string> t(256);
+        uint32_t next = 256;
+        for (int i = 0; i < 256; ++i) {
+            const bool keep = (i >= 0x21 && i <= 0x7E) || (i >= 0xA1 && i <= 0xAC) || (i >= 0xAE && i <= 0xFF);
+            const uint32_t cp = keep ? static_cast<uint32_t>(i) : next++;
+            std::string& o = t[i];
+            if (cp < 0x80) o += static_cast<char>(cp);
+            else { o += static_cast<char>(0xC0 | (cp >> 6)); o += static_cast<char>(0x80 | (cp & 0x3F)); }
+        }
+        return t;
+    }();
+    return table[b & 0xFF];
+}
+
+// Text the merges are learned from: words, numbers, contractions,
+// punctuation runs, code and a few non-Latin scripts.
+const char* kBpeCorpus =
+    "The quick brown fox jumps over the lazy dog. It's the 2024 edition, and we're told they'll ship 123456 units; "
+    "don't worry, I'm sure you've heard the news. Numbers like 3.14159 and 1,000,000 appear in the text, "
+    "as do dates such as 2023-11-05. Punctuation!!! Questions??? Ellipses... and dashes -- everywhere.\n"
+    "def train(model, data):\n    for batch in data:\n        loss = model(batch)\n        loss.backward()\n"
+    "    return model\n\n"
+    "Caf\xC3\xA9 na\xC3\xAFve r\xC3\xA9sum\xC3\xA9 \xC3\xBCber stra\xC3\x9F" "e; "
+    "\xD0\x9F\xD1\x80\xD0\xB8\xD0\xB2\xD0\xB5\xD1\x82 \xD0\xBC\xD0\xB8\xD1\x80; "
+    "\xE6\x97\xA5\xE6\x9C\xAC\xE8\xAA\x9E\xE3\x81\xAE\xE3\x83\x86\xE3\x82\xAD\xE3\x82\xB9\xE3\x83\x88. "
+    "the theory of the thing: there, then, those, these, this, that, than, thank. interesting internal international "
+    "information. running jumping swimming reading writing. hello world, hello there, hello again.\n";
+
+struct BpeVocab {
+    std::vector<std::string> tokens;
+    std::vector<int32_t> types;
+    std::vector<std::string> merges;
+    int bos = 0, eos = 0;
+};
+
+// 256 byte characters, then merges learned greedily on the corpus (the most
+// frequent adjacent pair, ties to the lower pair of ids; spaces attach to the
+// following word), then a few control tokens, then filler up to `vocab`.
+BpeVocab build_bpe_vocab(int vocab, int n_merges) {
+    BpeVocab v;
+    std::map<std::string, int> id;
+    auto add = [&](const std::string& t, int type) {
+        id.emplace(t, static_cast<int>(v.tokens.size()));
+        v.tokens.push_back(t);
+        v.types.push_back(type);
+    };
+    for (int b = 0; b < 256; ++b) add(byte_char(b), 1);
+    std::vector<std::vector<int>> words;
+    {
+        const std::string text = kBpeCorpus;
+        std::vector<int> cur;
+        for (size_t i = 0; i < text.size(); ++i) {
+            const unsigned char ch = static_cast<unsigned char>(text[i]);
+            if ((ch == ' ' || ch == '\n') && !cur.empty()) { words.push_back(cur); cur.clear(); }
+            cur.push_back(ch);
+        }
+        if (!cur.empty()) words.push_back(cur);
+    }
+    for (int m = 0; m < n_merges; ++m) {
+        std::map<std::pair<int, int>, int> count;
+        for (const auto& w : words)
+            for (size_t i = 0; i + 1 < w.size(); ++i) ++count[{w[i], w[i + 1]}];
+        std::pair<int, int> best{-1, -1};
+        int bc = 1;
+        for (const auto& [pr, c] : count)
+            if (c > bc) { bc = c; best = pr; }
+        if (best.first < 0) break;
+        const std::string joined = v.tokens[best.first] + v.tokens[best.second];
+        if (id.count(joined)) break;
+        v.merges.push_back(v.tokens[best.first] + " " + v.tokens[best.second]);
+        const int nid = static_cast<int>(v.tokens.size());
+        add(joined, 1);
+        for (auto& w : words) {
+            std::vector<int> o;
+            for (size_t i = 0; i < w.size(); ++i) {
+                if (i + 1 < w.size() && w[i] == best.first && w[i + 1] == best.second) { o.push_back(nid); ++i; }
+                else o.push_back(w[i]);
+            }
+            w.swap(o);
+        }
+    }
+    v.bos = static_cast<int>(v.tokens.size());
+    for (const char* sp : {"<|begin_of_text|>", "<|end_of_text|>", "<|start_header_id|>", "<|end_header_id|>",
+                           "<|eot_id|>", "<|im_start|>", "<|im_end|>"})
+        add(sp, 3);
+    v.eos = v.bos + 1;
+    for (int i = static_cast<int>(v.tokens.size()); i < vocab; ++i) add("<filler " + std::to_string(i) + ">", 1);
+    return v;
+}
+
 }  // namespace
 
 extern "C" {
@@ -235,6 +332,9 @@ typedef struct fish_synth_config {
     float wstd;                  // weight std (0.02)
     float router_std;            // MoE router std (1/64 variance -> 0.125)
     const char* chat_template;   // tokenizer.chat_template; nullptr or "" writes none
+    const char* bpe_pre;         // nullptr / "": SentencePiece dummy vocabulary; else a byte-level BPE
+                                 // vocabulary with this tokenizer.ggml.pre name (merges learned from
+                                 // a built-in text)
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -321,6 +421,25 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
         w.kv_u32(k("expert_count"), static_cast<uint32_t>(c->n_experts)); ++n_kv;
         w.kv_u32(k("expert_used_count"), static_cast<uint32_t>(c->n_experts_per_tok)); ++n_kv;
     }
+    if (c->bpe_pre && c->bpe_pre[0]) {
+        // byte-level BPE vocabulary (see build_bpe_vocab)
+        const BpeVocab bv = build_bpe_vocab(c->vocab, 400);
+        if (static_cast<int>(bv.tokens.size()) != c->vocab) return fail("vocabulary too small for the BPE tokens");
+        w.kv_str("tokenizer.ggml.model", "gpt2"); ++n_kv;
+        w.kv_str("tokenizer.ggml.pre", c->bpe_pre); ++n_kv;
+        w.str("tokenizer.ggml.tokens"); w.u32(9); w.u32(8); w.u64(bv.tokens.size());
+        for (const auto& t : bv.tokens) w.str(t);
+        ++n_kv;
+        w.str("tokenizer.ggml.token_type"); w.u32(9); w.u32(5); w.u64(bv.types.size());
+        for (int32_t t : bv.types) w.i32(t);
+        ++n_kv;
+        w.str("tokenizer.ggml.merges"); w.u32(9); w.u32(8); w.u64(bv.merges.size());
+        for (const auto& m : bv.merges) w.str(m);
+        ++n_kv;
+        w.kv_u32("tokenizer.ggml.bos_token_id", static_cast<uint32_t>(bv.bos)); ++n_kv;
+        w.kv_u32("tokenizer.ggml.eos_token_id", static_cast<uint32_t>(bv.eos)); ++n_kv;
+        w.kv_bool("tokenizer.ggml.add_bos_token", true); ++n_kv;
+    } else {
     // SentencePiece dummy vocabulary: <unk> <s> </s>, 256 byte tokens, then
     // "▁t<i>" pieces up to the vocabulary size.
     w.kv_str("tokenizer.ggml.model", "llama"); ++n_kv;
@@ -343,6 +462,7 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     w.kv_u32("tokenizer.ggml.eos_token_id", 2); ++n_kv;
     w.kv_u32("tokenizer.ggml.unknown_token_id", 0); ++n_kv;
     w.kv_bool("tokenizer.ggml.add_bos_token", true); ++n_kv;
+    }
     if (c->chat_template && c->chat_template[0]) { w.kv_str("tokenizer.chat_template", c->chat_template); ++n_kv; }
     std::memcpy(w.buf.data() + n_kv_pos, &n_kv, 8);
 

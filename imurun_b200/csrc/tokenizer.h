@@ -40,26 +40,40 @@ public:
     size_t size() const { return tokens_.size(); }
 
 private:
-    struct Seg { std::string text; bool special; };
-    std::vector<Seg> chat_segments(const Messages& msgs, ChatFormat f) const;
+    struct MergeTo {
+        int rank;
+        int32_t id;
+    };
+    struct TrieNode {
+        std::unordered_map<unsigned char, int> next;
+        int32_t id = -1;
+    };
+    static uint64_t pair_key(int32_t a, int32_t b) { return ((uint64_t)(uint32_t)a << 32) | (uint32_t)b; }
+    int32_t lookup(const std::string& s) const {
+        auto it = index_.find(s);
+        return it == index_.end() ? -1 : it->second;
+    }
+    bool load_vocab(const Gguf& g, std::string* err);
+    bool load_merges(const Gguf& g, std::string* err);
+    void detect_format(const Gguf& g);
+    void trie_insert(const std::string& s, int32_t id);
+    int32_t special_at(const std::string& s, size_t i, size_t* len) const;
+    std::vector<std::pair<std::string, bool>> chat_parts(const Messages& msgs, ChatFormat f) const;
     std::vector<int32_t> encode_plain(const std::string& text) const;
     std::vector<int32_t> encode_spm(const std::string& text) const;
     std::vector<int32_t> encode_bpe_piece(const std::string& piece) const;
     std::vector<std::string> pre_split(const std::string& text) const;
-    int32_t id_of(const std::string& s) const {
-        auto it = index_.find(s);
-        return it == index_.end() ? -1 : it->second;
-    }
 
     bool spm_ = false;
     std::vector<std::string> tokens_;
+    std::vector<std::string> texts_;       // decoded text of every token
     std::vector<int32_t> types_;
     std::vector<float> scores_;
     std::unordered_map<std::string, int32_t> index_;
-    std::unordered_map<uint64_t, std::pair<int, int32_t>> merges_;   // (a<<32|b) -> (rank, id)
-    std::vector<std::pair<std::string, int32_t>> specials_;          // longest first
+    std::unordered_map<uint64_t, MergeTo> ranks_;   // (left id, right id) -> merge rank and result
+    std::vector<TrieNode> trie_;                    // special tokens
     std::unordered_set<int32_t> eog_;
-    std::vector<int32_t> byte_ids_;
+    std::vector<int32_t> byte_ids_;                 // SPM <0xNN> tokens
     int32_t bos_ = 1, eos_ = 2, unk_ = 0;
     bool add_bos_ = true, space_prefix_ = true;
     int digits_ = 3;

@@ -71,8 +71,16 @@ ABI5_FUNCTIONS = [
 ]
 KERNEL_FUNCTIONS = [
     "fbx_quantize_acts", "fbx_rmsnorm", "fbx_matmul", "fbx_block_sums", "fbx_attention", "fbx_rope",
-    "fbx_argmax", "fbx_argmax_penalized", "fbx_embed", "fbx_time_matmul", "fbx_attention_static", "fbx_attention_decode",
+    "fbx_argmax", "fbx_argmax_penalized", "fbx_layer_probe", "fbx_embed", "fbx_time_matmul", "fbx_attention_static", "fbx_attention_decode",
 ]
+
+
+class LayerProbeOut(ctypes.Structure):
+    """fbx_layer_probe_out (include/fish/fish_kernels.h)."""
+    _fields_ = [
+        ("f", P * 4), ("qk", P * 4), ("q32", P * 4), ("gate3", P), ("up3", P),
+        ("rows", I * 4), ("K", I * 4), ("has_k", I * 4), ("has_32", I * 4), ("silu_in_prologue", I),
+    ]
 
 
 def _p(a):
@@ -111,6 +119,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "fbx_attention": ([P, P, P, I, I, I, I, I, I, I, P], I),
         "fbx_rope": ([P, P, I, I, I, I, I, I, F, I], I), "fbx_argmax": ([P, I, I, P], I),
         "fbx_argmax_penalized": ([P, I, P, I, F, P], I),
+        "fbx_layer_probe": ([P, I, I, P, I, P, P], I),
         "fbx_embed": ([I, P, I, I, P, I, P], I),
         "fbx_time_matmul": ([I, I, I, I, I, P, P], I),
         "fbx_attention_static": ([P, P, P, I, I, I, I, I, I, I, P, P], I),
@@ -225,6 +234,43 @@ class Model:
         out = np.zeros(max(n, 1), np.int32)
         self.lib.fish_session_pages(self.ctx, s, _p(out), out.size)
         return out[:n]
+
+    def layer_probe(self, layer: int, x, pos0: int) -> dict:
+        """fbx_layer_probe: one layer on hidden rows x [T][n_embd] at positions
+        pos0.., with every int8 activation the kernels built (stage s in 0..3:
+        attention-norm input, attention output, FFN-norm input, SwiGLU
+        product) as Q8ActK / Q8Act record bytes and the float rows they came
+        from."""
+        info = self.info
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        E, Q = info.n_embd, info.n_head * info.head_dim
+        kx = max(1, info.n_experts_per_tok) if info.n_experts > 0 else 1
+        F = info.n_ff
+        widths = [E, Q, E, F]
+        rows = [T, T, T, T * kx]
+        f = [np.zeros((rows[i], widths[i]), np.float32) for i in range(4)]
+        qk = [np.zeros((rows[i], max(1, widths[i] // 256) * 276), np.uint8) for i in range(4)]
+        q32 = [np.zeros((rows[i], max(1, widths[i] // 32) * 40), np.uint8) for i in range(4)]
+        gate3 = np.zeros((rows[3], F), np.float32)
+        up3 = np.zeros((rows[3], F), np.float32)
+        out = LayerProbeOut()
+        for i in range(4):
+            out.f[i] = f[i].ctypes.data
+            out.qk[i] = qk[i].ctypes.data
+            out.q32[i] = q32[i].ctypes.data
+        out.gate3 = gate3.ctypes.data
+        out.up3 = up3.ctypes.data
+        y = np.zeros_like(x)
+        self._check(self.lib.fbx_layer_probe(self.ctx, layer, pos0, _p(x), T, _p(y), ctypes.byref(out)),
+                    "fbx_layer_probe")
+        st = []
+        for i in range(4):
+            r = out.rows[i]
+            st.append({"rows": r, "K": out.K[i], "f": f[i][:r], "has_k": bool(out.has_k[i]),
+                       "has_32": bool(out.has_32[i]), "qk": qk[i][:r], "q32": q32[i][:r]})
+        return {"x_out": y, "stages": st, "silu_in_prologue": bool(out.silu_in_prologue),
+                "gate3": gate3[:out.rows[3]], "up3": up3[:out.rows[3]]}
 
     def stats(self) -> FishStats:
         st = FishStats()

@@ -48,6 +48,7 @@ class SynthConfig:
     wstd: float = 0.02
     router_std: float = 0.125
     chat_template: str = ""   # written as tokenizer.chat_template when not empty
+    bpe_pre: str = ""         # non-empty: byte-level BPE vocabulary with this tokenizer.ggml.pre name
 
 
 PRESETS = {
@@ -76,6 +77,7 @@ class _CConfig(ctypes.Structure):
         ("qkv_bias", ctypes.c_int), ("wtype", ctypes.c_int),
         ("seed", ctypes.c_ulonglong), ("wstd", ctypes.c_float), ("router_std", ctypes.c_float),
         ("chat_template", ctypes.c_char_p),
+        ("bpe_pre", ctypes.c_char_p),
     ]
 
 
@@ -97,7 +99,7 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
     c = _CConfig(cfg.arch.encode(), cfg.n_layers, cfg.n_embd, cfg.n_ff, cfg.n_head, cfg.n_head_kv,
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
-                 cfg.chat_template.encode())
+                 cfg.chat_template.encode(), cfg.bpe_pre.encode())
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

@@ -123,6 +123,39 @@ FISH_API int fbx_argmax_penalized(const float* x, int n, const int32_t* recent, 
  * quant.cpp:470-506) for ids[0..T) of a [n_rows][E] table. */
 FISH_API int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out);
 
+/* Debug probe of one transformer layer, for layer-wise parity tests (no
+ * counterpart in the reference's ABI; it restates one iteration of
+ * LlamaModel::forward's layer loop, model/fish/src/model.cpp:1654-1785). It
+ * runs layer `layer` of the model loaded in ctx on n_tok hidden rows x_in
+ * ([n_tok][n_embd] f32, host) at positions pos0.. of the context's sequence
+ * (writing that layer's K/V rows there; pos0 <= the sequence length), with
+ * the same kernels and fused prologues the forward uses for n_tok tokens,
+ * launched eagerly. x_out receives the layer's output rows. Stages: 0 the
+ * attention-norm input, 1 the attention output, 2 the FFN-norm input, 3 the
+ * SwiGLU product (n_tok * n_experts_per_tok rows for MoE layers). For each
+ * stage the caller may pass buffers (NULL = skip) for the float rows the
+ * stage quantised (f; stages 0 and 2 before their RMSNorm) and for the int8
+ * activations the kernels built, as the reference's Q8ActK records (qk,
+ * 276 B per 256 values) and Q8Act records (q32, 40 B per 32 values). When
+ * the SwiGLU product is formed inside the down projection's prologue, f[3]
+ * stays unwritten and gate3 / up3 receive its two inputs. rows/K/has_k/
+ * has_32 report what was recorded. Returns 0, or -1 with fish_last_error. */
+typedef struct {
+    float* f[4];
+    uint8_t* qk[4];
+    uint8_t* q32[4];
+    float* gate3;
+    float* up3;
+    int rows[4];
+    int K[4];
+    int has_k[4];
+    int has_32[4];
+    int silu_in_prologue;
+} fbx_layer_probe_out;
+struct fish_ctx;
+FISH_API int fbx_layer_probe(struct fish_ctx* ctx, int layer, int pos0, const float* x_in, int n_tok, float* x_out,
+                             fbx_layer_probe_out* out);
+
 /* Tokenizer of a GGUF file without loading its model: host code only, no
  * device needed. It is the tokenizer fish_load sets up for the same file
  * (vocabulary, merges or scores, special tokens, chat template), built from

@@ -70,6 +70,12 @@ class Oracle:
         L.or_model_kv_len.restype = I
         L.or_model_last_hidden.argtypes = [P, P, I]
         L.or_model_last_hidden.restype = I
+        L.or_model_layer.argtypes = [P, I, P, I, I, P]
+        L.or_model_layer.restype = I
+        L.or_model_layer_acts.argtypes = [P, I, P, I, I, P, P]
+        L.or_model_layer_acts.restype = I
+        L.or_model_tensor.argtypes = [P, ctypes.c_char_p, P, P, P, P]
+        L.or_model_tensor.restype = P
 
     # ---- activation quantisers
     def quantize_acts(self, x: np.ndarray) -> np.ndarray:
@@ -156,6 +162,50 @@ class OracleModel:
 
     def set_kv_len(self, n: int):
         self.o.L.or_model_set_kv_len(self.h, n)
+
+    def layer(self, layer: int, x: np.ndarray, pos0: int) -> np.ndarray:
+        """One layer alone on hidden rows x [n_tok][n_embd] at positions pos0..
+        (or_model_layer): returns the layer's output rows."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        if not self.o.L.or_model_layer(self.h, layer, _ptr(x), x.shape[0], pos0, _ptr(out)):
+            raise RuntimeError("oracle layer failed")
+        return out
+
+    def layer_acts(self, layer: int, x: np.ndarray, pos0: int, qk, q32) -> np.ndarray:
+        """One layer on hidden rows x with the given int8 activations at its
+        four quantisation points (qk / q32: per stage, Q8ActK / Q8Act record
+        bytes or None), or_model_layer_acts."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        keep = [None if a is None else np.ascontiguousarray(a) for a in list(qk) + list(q32)]
+        arr = (P * 8)(*[None if a is None else a.ctypes.data for a in keep])
+        if not self.o.L.or_model_layer_acts(self.h, layer, _ptr(x), x.shape[0], pos0, ctypes.addressof(arr), _ptr(out)):
+            raise RuntimeError("oracle layer failed")
+        return out
+
+    def tensor(self, name: str):
+        """(type, (ne0, ne1, ne2), address of the GGUF data) of a tensor, or None."""
+        t = ctypes.c_int(0)
+        ne = [ctypes.c_int64(0) for _ in range(3)]
+        a = self.o.L.or_model_tensor(self.h, name.encode(), ctypes.byref(t), ctypes.byref(ne[0]),
+                                     ctypes.byref(ne[1]), ctypes.byref(ne[2]))
+        if not a:
+            return None
+        return t.value, (ne[0].value, ne[1].value, ne[2].value), a
+
+    def tensor_rows(self, name: str, rows, expert: int = 0) -> np.ndarray:
+        """GGUF bytes of the given rows of a 2-D (or one expert of a 3-D) tensor."""
+        t, (n0, n1, _), a = self.tensor(name)
+        rb = row_bytes(t, n0)
+        base = a + expert * rb * n1
+        return np.stack([np.frombuffer(ctypes.string_at(int(base) + int(r) * int(rb), int(rb)), np.uint8) for r in rows])
+
+    def tensor_f32(self, name: str) -> np.ndarray:
+        t, (n0, n1, n2), a = self.tensor(name)
+        assert t == 0, "f32 tensors only"
+        n = n0 * n1 * n2
+        return np.frombuffer(ctypes.string_at(a, 4 * n), np.float32).copy()
 
     def close(self):
         if self.h:

@@ -467,6 +467,32 @@ void or_matmul(int type, const void* w, const float* x, int n_tok, int n_in,
     free(row);
 }
 
+/* or_matmul with the activations given as records instead of quantised
+ * here: qk (Q8ActK, rows of n_in/256 records) for types with a 256-layout
+ * kernel, q32 (Q8Act, rows of n_in/32 records) for the 32-layout ones; other
+ * weight types, or a NULL record array, take or_matmul's own path on x. */
+static void matmul_acts(int type, const void* w, const float* x, const void* qk, const void* q32, int n_tok, int n_in,
+                        int n_out, float* y) {
+    const uint64_t rb = or_row_bytes(type, (uint64_t)n_in);
+    const uint8_t* base = (const uint8_t*)w;
+    const int k_path = has_q8k_kernel(type) && (n_in % 256) == 0 && qk;
+    const int q_path = !k_path && has_q8_kernel(type) && (n_in % 32) == 0 && q32;
+    if (!k_path && !q_path) {
+        or_matmul(type, w, x, n_tok, n_in, n_out, y);
+        return;
+    }
+    for (int t = 0; t < n_tok; ++t) {
+        float* yt = y + (size_t)t * n_out;
+        if (k_path) {
+            const or_q8actk* a = (const or_q8actk*)qk + (size_t)t * (n_in / 256);
+            for (int i = 0; i < n_out; ++i) or_vec_dot_q8k(type, base + (size_t)i * rb, a, (uint64_t)n_in, yt + i);
+        } else {
+            const or_q8act* a = (const or_q8act*)q32 + (size_t)t * (n_in / 32);
+            for (int i = 0; i < n_out; ++i) or_vec_dot_q8(type, base + (size_t)i * rb, a, (uint64_t)n_in, yt + i);
+        }
+    }
+}
+
 /* ====================================================================== glue */
 
 /* ops.cpp:18-23: the sum of squares is accumulated in double. */
@@ -917,18 +943,19 @@ static const uint8_t* expert_ptr(const or_tensor* t, int e) {
 }
 
 /* model.cpp:1474-1515 (separate gate / up). out[n_tok][n_in]. */
-static void ffn_block(int tg, const void* wg, int tu, const void* wu, int td, const void* wd,
-                      const float* x, int n_tok, int n_in, int n_ff, float* out) {
+static void ffn_block_acts(int tg, const void* wg, int tu, const void* wu, int td, const void* wd,
+                           const float* x, int n_tok, int n_in, int n_ff, float* out, const void* xk, const void* x32,
+                           const void* hk, const void* h32) {
     float* g = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)n_ff);
     float* u = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)n_ff);
-    or_matmul(tg, wg, x, n_tok, n_in, n_ff, g);
-    or_matmul(tu, wu, x, n_tok, n_in, n_ff, u);
+    matmul_acts(tg, wg, x, xk, x32, n_tok, n_in, n_ff, g);
+    matmul_acts(tu, wu, x, xk, x32, n_tok, n_in, n_ff, u);
     for (int t = 0; t < n_tok; ++t) {
         float* gr = g + (size_t)t * n_ff;
         or_silu_inplace(gr, n_ff);
         for (int i = 0; i < n_ff; ++i) gr[i] *= u[(size_t)t * n_ff + i];
     }
-    or_matmul(td, wd, g, n_tok, n_ff, n_in, out);
+    matmul_acts(td, wd, g, hk, h32, n_tok, n_ff, n_in, out);
     free(g);
     free(u);
 }
@@ -937,7 +964,7 @@ static void ffn_block(int tg, const void* wg, int tu, const void* wu, int td, co
  * (partial_sort), renormalise when expert_weights_norm, then every used
  * expert in ascending expert order runs its FFN and is scatter-added with its
  * weight, the same order of float additions as the reference. */
-static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, float* out) {
+static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, float* out, const or_layer_acts* ov) {
     const or_model_info* c = &m->c;
     const int E = c->n_embd, NE = c->n_experts, K = c->n_experts_per_tok;
     float* r = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)NE);
@@ -965,10 +992,15 @@ static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, 
         for (int t = 0; t < n_tok; ++t) {
             for (int k = 0; k < K; ++k) {
                 if (sel[t * K + k] != ex) continue;
-                ffn_block(L->gate_exps->type, expert_ptr(L->gate_exps, ex),
-                          L->up_exps->type, expert_ptr(L->up_exps, ex),
-                          L->down_exps->type, expert_ptr(L->down_exps, ex),
-                          xb + (size_t)t * E, 1, E, c->n_ff_exp, tmp);
+                const int F = c->n_ff_exp, r = t * K + k;
+                ffn_block_acts(L->gate_exps->type, expert_ptr(L->gate_exps, ex),
+                               L->up_exps->type, expert_ptr(L->up_exps, ex),
+                               L->down_exps->type, expert_ptr(L->down_exps, ex),
+                               xb + (size_t)t * E, 1, E, F, tmp,
+                               ov && ov->qk[2] ? (const uint8_t*)ov->qk[2] + (size_t)t * (E / 256) * sizeof(or_q8actk) : NULL,
+                               ov && ov->q32[2] ? (const uint8_t*)ov->q32[2] + (size_t)t * (E / 32) * sizeof(or_q8act) : NULL,
+                               ov && ov->qk[3] ? (const uint8_t*)ov->qk[3] + (size_t)r * (F / 256) * sizeof(or_q8actk) : NULL,
+                               ov && ov->q32[3] ? (const uint8_t*)ov->q32[3] + (size_t)r * (F / 32) * sizeof(or_q8act) : NULL);
                 const float w = wsel[t * K + k];
                 for (int i = 0; i < E; ++i) out[(size_t)t * E + i] += w * tmp[i];
             }
@@ -980,33 +1012,25 @@ static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, 
     free(r);
 }
 
-/* model.cpp:1603-1811 */
-int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
-                     float* logits, float* logits_all) {
+/* One iteration of the layer loop of model.cpp:1654-1785: x [n_tok][E] is
+ * updated in place; layer li's K/V rows are stored at pos0..pos0+n_tok-1.
+ * Work buffers: xb, pr [n_tok][E]; q, at [n_tok][H*D]; k, v [n_tok][HKV*D]. */
+static void layer_forward(or_model* m, int li, float* x, int n_tok, int pos0, float* xb, float* q, float* k,
+                          float* v, float* at, float* pr, const or_layer_acts* ov) {
+    const void* const no[4] = {NULL, NULL, NULL, NULL};
+    const void* const* ak = ov ? ov->qk : no;
+    const void* const* a32 = ov ? ov->q32 : no;
     const or_model_info* c = &m->c;
-    if (!tokens || n_tok <= 0 || pos0 < 0 || pos0 + n_tok > c->n_ctx) return 0;
     const int E = c->n_embd, H = c->n_head, HKV = c->n_head_kv, D = c->head_dim;
     const int Q = H * D, KV = HKV * D;
     const float scale = 1.0f / sqrtf((float)D);
-    float* x = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
-    float* xb = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
-    float* q = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
-    float* k = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
-    float* v = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
-    float* at = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
-    float* pr = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
-    const uint64_t erow = or_row_bytes(m->embd->type, (uint64_t)E);
-    for (int t = 0; t < n_tok; ++t) {
-        if (tokens[t] < 0 || tokens[t] >= c->vocab) return 0;
-        or_dequant_row(m->embd->type, m->embd->data + (size_t)tokens[t] * erow, x + (size_t)t * E, (uint64_t)E);
-    }
     const int half = c->rot_dim / 2;
-    for (int li = 0; li < c->n_layers; ++li) {
+    {
         const or_layer* L = &m->L[li];
         for (int t = 0; t < n_tok; ++t) or_rmsnorm(xb + (size_t)t * E, x + (size_t)t * E, L->attn_norm, E, c->eps);
-        or_matmul(L->wq->type, L->wq->data, xb, n_tok, E, Q, q);
-        or_matmul(L->wk->type, L->wk->data, xb, n_tok, E, KV, k);
-        or_matmul(L->wv->type, L->wv->data, xb, n_tok, E, KV, v);
+        matmul_acts(L->wq->type, L->wq->data, xb, ak[0], a32[0], n_tok, E, Q, q);
+        matmul_acts(L->wk->type, L->wk->data, xb, ak[0], a32[0], n_tok, E, KV, k);
+        matmul_acts(L->wv->type, L->wv->data, xb, ak[0], a32[0], n_tok, E, KV, v);
         add_bias(q, n_tok, Q, L->bq);
         add_bias(k, n_tok, KV, L->bk);
         add_bias(v, n_tok, KV, L->bv);
@@ -1033,17 +1057,39 @@ int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
             }
         }
         or_attention(q, kc, vc, H, HKV, D, pos0, n_tok, at, scale, 0.0f, 0);
-        or_matmul(L->wo->type, L->wo->data, at, n_tok, Q, E, pr);
+        matmul_acts(L->wo->type, L->wo->data, at, ak[1], a32[1], n_tok, Q, E, pr);
         for (size_t i = 0; i < (size_t)n_tok * E; ++i) x[i] += pr[i];
         for (int t = 0; t < n_tok; ++t) or_rmsnorm(xb + (size_t)t * E, x + (size_t)t * E, L->ffn_norm, E, c->eps);
         if (c->n_experts > 0) {
-            moe_ffn(m, L, xb, n_tok, pr);
+            moe_ffn(m, L, xb, n_tok, pr, ov);
         } else {
-            ffn_block(L->wg->type, L->wg->data, L->wu->type, L->wu->data, L->wd->type, L->wd->data,
-                      xb, n_tok, E, c->n_ff, pr);
+            ffn_block_acts(L->wg->type, L->wg->data, L->wu->type, L->wu->data, L->wd->type, L->wd->data,
+                           xb, n_tok, E, c->n_ff, pr, ak[2], a32[2], ak[3], a32[3]);
         }
         for (size_t i = 0; i < (size_t)n_tok * E; ++i) x[i] += pr[i];
     }
+}
+
+/* model.cpp:1603-1811 */
+int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
+                     float* logits, float* logits_all) {
+    const or_model_info* c = &m->c;
+    if (!tokens || n_tok <= 0 || pos0 < 0 || pos0 + n_tok > c->n_ctx) return 0;
+    const int E = c->n_embd, H = c->n_head, HKV = c->n_head_kv, D = c->head_dim;
+    const int Q = H * D, KV = HKV * D;
+    float* x = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
+    float* xb = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
+    float* q = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
+    float* k = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
+    float* v = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
+    float* at = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
+    float* pr = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
+    const uint64_t erow = or_row_bytes(m->embd->type, (uint64_t)E);
+    for (int t = 0; t < n_tok; ++t) {
+        if (tokens[t] < 0 || tokens[t] >= c->vocab) return 0;
+        or_dequant_row(m->embd->type, m->embd->data + (size_t)tokens[t] * erow, x + (size_t)t * E, (uint64_t)E);
+    }
+    for (int li = 0; li < c->n_layers; ++li) layer_forward(m, li, x, n_tok, pos0, xb, q, k, v, at, pr, NULL);
     memcpy(m->last_x, x + (size_t)(n_tok - 1) * E, sizeof(float) * (size_t)E);
     const int rows = logits_all ? n_tok : 1;
     const int first = logits_all ? 0 : n_tok - 1;
@@ -1054,4 +1100,39 @@ int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
     m->kv_len = pos0 + n_tok;
     free(x); free(xb); free(q); free(k); free(v); free(at); free(pr);
     return 1;
+}
+
+int or_model_layer(or_model* m, int layer, const float* x_in, int n_tok, int pos0, float* x_out) {
+    return or_model_layer_acts(m, layer, x_in, n_tok, pos0, NULL, x_out);
+}
+
+int or_model_layer_acts(or_model* m, int layer, const float* x_in, int n_tok, int pos0, const or_layer_acts* acts,
+                        float* x_out) {
+    if (!m) return 0;
+    const or_model_info* c = &m->c;
+    if (!x_in || !x_out || layer < 0 || layer >= c->n_layers || n_tok <= 0 || pos0 < 0 ||
+        pos0 + n_tok > c->n_ctx)
+        return 0;
+    const int E = c->n_embd, Q = c->n_head * c->head_dim, KV = c->n_head_kv * c->head_dim;
+    float* xb = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
+    float* q = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
+    float* k = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
+    float* v = (float*)malloc(sizeof(float) * (size_t)n_tok * KV);
+    float* at = (float*)malloc(sizeof(float) * (size_t)n_tok * Q);
+    float* pr = (float*)malloc(sizeof(float) * (size_t)n_tok * E);
+    memcpy(x_out, x_in, sizeof(float) * (size_t)n_tok * E);
+    layer_forward(m, layer, x_out, n_tok, pos0, xb, q, k, v, at, pr, acts);
+    free(xb); free(q); free(k); free(v); free(at); free(pr);
+    return 1;
+}
+
+const void* or_model_tensor(const or_model* m, const char* name, int* type, int64_t* ne0, int64_t* ne1,
+                            int64_t* ne2) {
+    const or_tensor* t = m && name ? gguf_tensor(&m->g, name) : NULL;
+    if (!t) return NULL;
+    if (type) *type = t->type;
+    if (ne0) *ne0 = (int64_t)t->ne[0];
+    if (ne1) *ne1 = (int64_t)t->ne[1];
+    if (ne2) *ne2 = (int64_t)t->ne[2];
+    return t->data;
 }

@@ -115,6 +115,28 @@ int       or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int po
                            float* logits, float* logits_all);
 void      or_model_set_kv_len(or_model* m, int n);
 int       or_model_kv_len(const or_model* m);
+/* int8 activations to use instead of the oracle's own quantisation, per
+ * stage of a layer: 0 the attention-norm output (q/k/v input), 1 the
+ * attention output (wo input), 2 the FFN-norm output (gate/up input, experts
+ * included), 3 the SwiGLU product (down input; MoE: rows token * K + k in
+ * selection order). qk: Q8ActK records [rows][K/256]; q32: Q8Act records
+ * [rows][K/32]; a NULL entry leaves that stage to the oracle's quantiser. The
+ * router (F32 weights) keeps the float path, as in the reference. */
+typedef struct {
+    const void* qk[4];
+    const void* q32[4];
+} or_layer_acts;
+
+/* One layer alone (one iteration of the layer loop, model.cpp:1654-1785):
+ * x_out = layer `layer` applied to x_in [n_tok][n_embd] at positions pos0..;
+ * that layer's K/V rows are stored there. Returns 1, or 0 on a bad argument. */
+int       or_model_layer(or_model* m, int layer, const float* x_in, int n_tok, int pos0, float* x_out);
+/* The same with the int8 activations of `acts` (NULL: the oracle's own). */
+int       or_model_layer_acts(or_model* m, int layer, const float* x_in, int n_tok, int pos0,
+                              const or_layer_acts* acts, float* x_out);
+/* The mapped GGUF data of a tensor (NULL when absent), its type and dims. */
+const void* or_model_tensor(const or_model* m, const char* name, int* type, int64_t* ne0, int64_t* ne1,
+                            int64_t* ne2);
 /* Debug hook: copy of the final hidden state x (pre-norm) of the last token. */
 int       or_model_last_hidden(const or_model* m, float* out, int n);
 /* First index of the max value (model.cpp:1939-1946). */

@@ -1,0 +1,188 @@
+"""Layer-wise parity at the widths of every benchmark configuration, with the
+same int8 activations on both sides.
+
+Each configuration is checked on a 2-layer file of its own widths (Llama-3-8B,
+Qwen2.5-7B with qkv bias and NeoX RoPE, Mixtral-8x7B with 8 experts top-2,
+Llama-3-70B). Layer by layer, both engines get the SAME hidden rows: the
+embedding rows for layer 0, then the oracle's own output of the previous
+layer. Per layer, a prompt of P rows (the tensor-core GEMM path and the
+split-key prefill attention) and then one decode row at position P (the
+streamed GEMV with its fused prologues and the fused RoPE + KV append +
+decode attention) are run through `fbx_layer_probe`, which also returns every
+int8 activation the kernels built and the float rows they came from.
+
+Bars, per stage and layer:
+  * the layer's output rows equal the oracle's layer run on the SAME int8
+    activations (or_model_layer_acts: the GPU's records at the four
+    quantisation points) within the north-star bar |d| <= 1e-2 + 1e-3 |x|,
+    every element; what remains is float summation order;
+  * against the oracle's layer with its OWN quantisation the output is
+    reported and held to the reference's engine-vs-engine bar (max |d| <= 2%
+    of max |x|): an int8 rounding flip, set off by a 1-ulp float difference
+    in a stage input, moves a whole token row by up to a few 1e-2;
+  * the int8 activations are byte-identical to the oracle's quantisers
+    (or_quantize_acts_k / or_quantize_acts, pinned to the reference's
+    quantize_acts(_k), quant.cpp:400-434) applied to the same float rows:
+    stages 0 and 2 through the oracle's RMSNorm (ops.cpp:18-23) of the rows
+    the GPU normalised; stage 0's rows are the test's input, so there the
+    whole norm + quantise chain is pinned end to end;
+  * the per-block integer sums (sumi, mins) of sampled rows of every weight
+    matrix the stage feeds, on those real activations, are bit-exact against
+    the oracle's (the reference's integer kernels, quant_x86.cpp:299-495);
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+Q8ACTK = 276
+Q8ACT = 40
+BLK = {8: 32, 12: 256, 14: 256}
+
+# preset, prompt rows, sampled weight rows per matrix
+CONFIGS = [("llama8b", 20, 24), ("qwen7b", 20, 24), ("mixtral", 18, 16), ("llama70b", 17, 16)]
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from imurun_b200 import native
+    return native.load_library()
+
+
+@pytest.fixture(scope="module")
+def oracle():
+    from oracle.binding import Oracle
+    return Oracle()
+
+
+def _rms(oracle, x, w, eps):
+    return np.stack([oracle.rmsnorm(r, w, eps) for r in x])
+
+
+def _check_records(oracle, st, want_src, label):
+    """The stage's int8 activations equal the oracle quantisers' on want_src."""
+    K = st["K"]
+    assert st["rows"] == want_src.shape[0] and K == want_src.shape[1], label
+    n_rec = 0
+    if st["has_k"]:
+        for r in range(st["rows"]):
+            want = oracle.quantize_acts_k(want_src[r])
+            got = st["qk"][r][:K // 256 * Q8ACTK]
+            assert np.array_equal(got, want), f"{label} row {r}: Q8ActK bytes differ"
+            n_rec += K // 256
+    if st["has_32"]:
+        for r in range(st["rows"]):
+            want = oracle.quantize_acts(want_src[r])
+            got = st["q32"][r][:K // 32 * Q8ACT]
+            assert np.array_equal(got, want), f"{label} row {r}: Q8Act bytes differ"
+            n_rec += K // 32
+    assert n_rec > 0, f"{label}: no activation records"
+
+
+def _check_block_sums(gpu, oracle, om, st, names, rows, rng, label, expert=None):
+    """Per-block integer sums of sampled weight rows on the stage's real
+    activations (its first row): GPU kernel == oracle, bit for bit."""
+    from imurun_b200.native import _p
+    K = st["K"]
+    for name in names:
+        info = om.tensor(name)
+        assert info is not None, name
+        t, (n0, n1, _n2), _ = info
+        assert n0 == K, (name, n0, K)
+        if t not in BLK:
+            continue
+        acts = st["qk"][0][:K // 256 * Q8ACTK] if t in (12, 14) else st["q32"][0][:K // 32 * Q8ACT]
+        sel = np.sort(rng.choice(n1, size=min(rows, n1), replace=False))
+        w = np.ascontiguousarray(om.tensor_rows(name, sel, expert=expert or 0))
+        nb = K // BLK[t]
+        s = np.zeros((len(sel), nb), np.int32)
+        m = np.zeros((len(sel), nb), np.int32)
+        assert gpu.fbx_block_sums(t, _p(w), K, len(sel), _p(np.ascontiguousarray(acts)), _p(s), _p(m)) == 0
+        for i in range(len(sel)):
+            ws, wm = oracle.block_sums(t, w[i], acts, K)
+            assert np.array_equal(s[i], ws), f"{label} {name} row {sel[i]}: sumi differ"
+            if t == 12:
+                assert np.array_equal(m[i], wm), f"{label} {name} row {sel[i]}: mins differ"
+
+
+def _records(res):
+    """The GPU's int8 activations per stage, as the oracle's override input."""
+    qk = [st["qk"] if st["has_k"] else None for st in res["stages"]]
+    q32 = [st["q32"] if st["has_32"] else None for st in res["stages"]]
+    return qk, q32
+
+
+def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_exp, rows, rng, label):
+    st = res["stages"]
+    # the layer output on the same int8 activations: every element inside
+    # the north-star bar
+    d = np.abs(res["x_out"] - same_out)
+    bar = 1e-2 + 1e-3 * np.abs(same_out)
+    assert np.all(d <= bar), f"{label}: max |d| {d.max():.3g} (bar exceeded at {np.argmax(d - bar)})"
+    # against the oracle's own quantisation: reported; max |d| <= 2% of max |x|
+    d_own = np.abs(res["x_out"] - want_out)
+    inside = float(np.mean(d_own <= 1e-2 + 1e-3 * np.abs(want_out)))
+    print(f"{label}: same activations max |d| {d.max():.3g}; own activations max |d| {d_own.max():.3g}, "
+          f"{100 * inside:.2f}% inside the bar")
+    assert d_own.max() <= 0.02 * np.abs(want_out).max(), f"{label}: {d_own.max()}"
+    an = om.tensor_f32(f"blk.{layer}.attn_norm.weight")
+    fn = om.tensor_f32(f"blk.{layer}.ffn_norm.weight")
+    # stage 0: the rows the GPU normalised are the test's input rows
+    assert np.array_equal(st[0]["f"], x_in), label
+    _check_records(oracle, st[0], _rms(oracle, x_in, an, eps), f"{label} attn-norm")
+    _check_records(oracle, st[1], st[1]["f"], f"{label} attn-out")
+    _check_records(oracle, st[2], _rms(oracle, st[2]["f"], fn, eps), f"{label} ffn-norm")
+    if res["silu_in_prologue"]:
+        pytest.fail(f"{label}: the SwiGLU product was formed in a GEMV prologue (not the default path)")
+    _check_records(oracle, st[3], st[3]["f"], f"{label} swiglu")
+    p = f"blk.{layer}."
+    _check_block_sums(gpu, oracle, om, st[0], [p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"], rows,
+                      rng, label)
+    _check_block_sums(gpu, oracle, om, st[1], [p + "attn_output.weight"], rows, rng, label)
+    if n_exp:
+        e = int(rng.integers(0, n_exp))
+        _check_block_sums(gpu, oracle, om, st[2], [p + "ffn_gate_exps.weight", p + "ffn_up_exps.weight"], rows, rng,
+                          label, expert=e)
+        _check_block_sums(gpu, oracle, om, st[3], [p + "ffn_down_exps.weight"], rows, rng, label, expert=e)
+    else:
+        _check_block_sums(gpu, oracle, om, st[2], [p + "ffn_gate.weight", p + "ffn_up.weight"], rows, rng, label)
+        _check_block_sums(gpu, oracle, om, st[3], [p + "ffn_down.weight"], rows, rng, label)
+    return float(d.max())
+
+
+@pytest.mark.parametrize("preset,P,rows", CONFIGS, ids=[c[0] for c in CONFIGS])
+def test_layers_at_config_widths(gpu, oracle, synth_dir, monkeypatch, preset, P, rows):
+    from imurun_b200 import synth
+    from imurun_b200.native import Model
+    monkeypatch.delenv("FISH_KV_F32", raising=False)   # fp16 KV, the configurations' cache
+    cfg = synth.preset(preset, layers=2)
+    path = synth.cached(cfg, synth_dir)
+    om = oracle.load(path, 256, kv_f16=True)            # K/V rounded through fp16 like the device cache
+    rng = np.random.default_rng(7 + P)
+    ids = rng.integers(3, cfg.vocab, P + 1).astype(np.int32)
+    t, (E, _, _), _ = om.tensor("token_embd.weight")
+    emb = om.tensor_rows("token_embd.weight", ids)
+    h = np.stack([oracle.dequant(t, r, E) for r in emb]).astype(np.float32)
+    worst = []
+    with Model(path, 256) as gm:
+        for layer in range(cfg.n_layers):
+            # prompt rows: GEMM path, split-key prefill attention
+            res = gm.layer_probe(layer, h[:P], 0)
+            same = om.layer_acts(layer, h[:P], 0, *_records(res))
+            want = om.layer(layer, h[:P], 0)
+            worst.append(_check_layer(gpu, oracle, om, res, h[:P], want, same, layer, cfg.eps, cfg.n_experts, rows,
+                                      rng, f"{preset} layer {layer} prompt"))
+            # one decode row: fused GEMV prologues, fused decode attention
+            res1 = gm.layer_probe(layer, h[P:P + 1], P)
+            same1 = om.layer_acts(layer, h[P:P + 1], P, *_records(res1))
+            want1 = om.layer(layer, h[P:P + 1], P)
+            worst.append(_check_layer(gpu, oracle, om, res1, h[P:P + 1], want1, same1, layer, cfg.eps, cfg.n_experts,
+                                      rows, rng, f"{preset} layer {layer} decode"))
+            h = np.concatenate([want, want1])
+    om.close()
+    print(f"{preset}: max |d| per (layer, path) = {[round(w, 6) for w in worst]}")

@@ -4,12 +4,16 @@ the same synthetic GGUF with fish_load (its CPU engine) and tokenizes,
 detokenizes and formats chat prompts through its own C API
 (model/fish/include/fish/c_api.h:108-121); this library does the same from
 the GGUF's metadata through the host-only fbx_*_gguf entry points, which
-build the tokenizer fish_load builds. The synthetic vocabulary is
-SentencePiece-style (<unk> <s> </s>, 256 byte tokens, then "▁t<i>" pieces),
-so the cases exercise byte fallback, the space prefix, BOS, special-token
-text and the pieces that do match. The chat cases cover every format the
-reference detects, from files carrying a template with that format's
-marker."""
+build the tokenizer fish_load builds. Two vocabularies: SentencePiece-style
+(<unk> <s> </s>, 256 byte tokens, then "▁t<i>" pieces: byte fallback, the
+space prefix, BOS, special-token text and the pieces that do match), and
+byte-level BPE (256 byte characters, 400 merges learned from a built-in text,
+control tokens) under the llama3 and qwen2 pre-splits, where seeded random
+strings over a mix of letters, digits, contractions, punctuation, whitespace
+kinds, non-Latin scripts, emoji, special-token text and malformed UTF-8
+exercise every pre-split rule and the merge order. The chat cases cover
+every format the reference detects, from files carrying a template with
+that format's marker."""
 from __future__ import annotations
 
 import ctypes
@@ -63,11 +67,51 @@ def ours():
     return L
 
 
-@pytest.fixture(scope="module", params=["tiny", "qwen7b"])
+GGUFS = {
+    "tiny": lambda synth: synth.preset("tiny"),
+    "qwen7b": lambda synth: synth.preset("qwen7b", layers=1),
+    "bpe-llama3": lambda synth: synth.preset("tiny", layers=1, bpe_pre="llama-bpe"),
+    "bpe-qwen2": lambda synth: synth.preset("tiny", layers=1, bpe_pre="qwen2"),
+}
+
+
+@pytest.fixture(scope="module", params=list(GGUFS))
 def gguf(request, synth_dir):
     from imurun_b200 import synth
-    cfg = synth.preset("tiny") if request.param == "tiny" else synth.preset("qwen7b", layers=1)
-    return synth.cached(cfg, synth_dir)
+    return synth.cached(GGUFS[request.param](synth), synth_dir)
+
+
+# pieces the fuzz strings are drawn from
+PARTS = ["the", "The", "THE", "quick", "hello", "world", "running", " ", "  ", "   ", "\t", "\n", "\n\n", "\r\n",
+         " \n ", "'s", "'T", "'re", "'VE", "'m", "'ll", "'d", "'x", "'", "0", "7", "42", "2024", "123456789", "3.14",
+         "1,000", ".", "...", "!", "?!", "--", "(", ")", "{", "}", "**", "_", "-", "café", "naïve", "straße", "Привет",
+         "日本語", "テスト", "٣٤٥", "१२३", "²³", "½", "\u00a0", "\u3000", "\u1680", "\u2003", "\u0085", "🙂", "👍🏽",
+         "<|im_start|>", "<|eot_id|>", "<|begin_of_text|>", "<s>", "</s>", "<|end_header_id|>", "é", "ß", "×", "÷"]
+
+
+def _fuzz_texts(seed, n):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        parts = [PARTS[int(i)] for i in rng.integers(0, len(PARTS), int(rng.integers(1, 14)))]
+        t = "".join(parts).encode("utf-8")
+        if rng.random() < 0.2:          # malformed UTF-8: a stray lead or continuation byte
+            k = int(rng.integers(0, len(t) + 1))
+            t = t[:k] + bytes([int(rng.choice([0xC3, 0xE6, 0xF0, 0x80, 0xBF, 0xFF]))]) + t[k:]
+        out.append(t)
+    return out
+
+
+@pytest.mark.parametrize("seed", range(2))
+def test_tokenize_fuzz_matches_reference(ref_lib, ours, ref_ctx, gguf, seed):
+    for t in _fuzz_texts(1000 + seed, 30):
+        for bos in (0, 1):
+            want = _tok(ref_lib.fish_tokenize, ref_ctx, text=t, bos=bos)
+            got = _tok(ours.fbx_tokenize_gguf, str(gguf).encode(), text=t, bos=bos)
+            assert np.array_equal(got, want), (t, list(got), list(want))
+        ids = np.ascontiguousarray(want, np.int32)
+        assert _str(ours.fbx_detokenize_gguf, str(gguf).encode(), ids.ctypes.data, ids.size) == \
+            _str(ref_lib.fish_detokenize, ref_ctx, ids.ctypes.data, ids.size)
 
 
 @pytest.fixture(scope="module")
