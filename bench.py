@@ -387,6 +387,12 @@ def run_ours(args):
     prefill_tops = 2.0 * macs / prefill_s / 1e12
     m.close()
 
+    # the sharded configuration on the same N GPUs (strong scaling over one
+    # model), reported beside the replicas' value
+    sharded = None
+    if WORLD > 1 and args.sharded != "none":
+        sharded = sharded_measure(dist, args.sharded, 8, 3)
+
     cpu = None
     if RANK == 0 and WORLD == 1 and not args.no_cpu:
         v, kind, cores, dt, kname = cpu_reference_decode(path, 16, 8)
@@ -414,6 +420,7 @@ def run_ours(args):
                 "profile_note": "per-launch events of the eager multi-kernel path (streamed GEMV etc.), for comparison",
                 "decode_kernel": "k_step (one cooperative launch per greedy call)" if persistent else "graph of per-op kernels",
                 "profile_total_ms_per_step": round(total_ms / prof["steps"], 4),
+                "sharded": sharded,
             },
             "e2e": {"value": round(e2e_value, 3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4,
                     "generate_tok_s": round(gen_tps, 3) if gen_tps else None,
@@ -441,22 +448,21 @@ SHARDED = {
 }
 
 
-def run_sharded(args):
+def sharded_measure(dist, workload: str, K: int, W: int, batch: int = 0, prompt: int = 0, layers: int = 0) -> dict:
     """One model sharded over WORLD GPUs (tensor or expert parallelism; one
     process per GPU, NCCL group id from rank 0 over the gloo group): B
     sessions fork one shared random prompt (its KV pages referenced, not
     copied), then batched greedy decode steps. Every rank makes the same
     calls; each step's device time is the batch graph's CUDA-event time on the
-    engine stream, max over ranks. value = B tokens per step / step time."""
+    engine stream, max over ranks. Returns the measurement (every rank)."""
     from imurun_b200 import native, synth
     from imurun_b200.native import Model
-    preset, B, prompt, desc = SHARDED[args.workload]
-    B = args.batch or B
-    prompt = args.prompt or prompt
-    dist = dist_init()
-    cfg = synth.preset(preset, layers=args.layers) if args.layers else synth.preset(preset)
-    if args.layers:
-        desc += f"; TRUNCATED to {args.layers} layers (plumbing check, not the config)"
+    preset, B, P, desc = SHARDED[workload]
+    B = batch or B
+    P = prompt or P
+    cfg = synth.preset(preset, layers=layers) if layers else synth.preset(preset)
+    if layers:
+        desc += f"; TRUNCATED to {layers} layers (plumbing check, not the config)"
     d = os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")
     if RANK == 0:
         t0 = time.time()
@@ -466,17 +472,16 @@ def run_sharded(args):
     path = synth.cached(cfg, d)
     lib = native.load_library()
     gid = share_group_id(dist, lambda: native.tp_unique_id(lib))
-    K, W = args.steps, args.warmup
-    n_ctx = (prompt + W + K + 2 + 255) // 256 * 256
+    n_ctx = (P + W + K + 2 + 255) // 256 * 256
     t0 = time.time()
     m = Model(path, n_ctx, lib=lib, tp=(RANK, WORLD, gid) if WORLD > 1 else None)
     load_s = time.time() - t0
-    ids = np.random.default_rng(4321).integers(3, m.vocab, prompt).astype(np.int32)   # same on every rank
+    ids = np.random.default_rng(4321).integers(3, m.vocab, P).astype(np.int32)   # same on every rank
     barrier(dist)
     t0 = time.perf_counter()
     lg = m.prefill(ids, 0)
     prefill_s = max_over_ranks(dist, time.perf_counter() - t0)
-    sids = [0] + [m.session_fork(0, prompt) for _ in range(B - 1)]
+    sids = [0] + [m.session_fork(0, P) for _ in range(B - 1)]
     tok = np.full(B, int(np.argmax(lg)), np.int32)
     for _ in range(W):
         tok = m.decode_batch(sids, tok)[0]
@@ -496,28 +501,40 @@ def run_sharded(args):
     eng = json.loads(m.lib.fish_engine_json(m.ctx).decode())
     wbytes = float(eng["weights_device_bytes"])
     m.close()
-    peak, peak_kind = peaks()
+    peak, _ = peaks()
     step_s = dev_ms_max / K / 1e3
+    return {"workload": workload, "desc": desc, "batch": B, "prompt": P, "steps": K, "warmup": W,
+            "value": round(B / step_s, 3), "ms_per_step": round(step_s * 1e3, 4),
+            "e2e_tok_s": round(B * K / wall_s, 3), "prefill_tok_s": round(P / prefill_s, 1), "load_s": round(load_s, 1),
+            "weights_bytes_per_gpu": wbytes, "weights_gbs_per_gpu": round(wbytes / step_s / 1e9, 1),
+            "hbm_frac_per_gpu": round(wbytes / step_s / 1e9 / peak, 4),
+            "parallelism": f"{'tp' if workload.endswith('tp') else 'ep'}{WORLD}", "clocks": clk}
+
+
+def run_sharded(args):
+    """`--workload llama70b-tp / mixtral-ep`: the sharded measurement as the
+    bench line (value = B tokens per step / step time, strong scaling)."""
+    dist = dist_init()
+    r = sharded_measure(dist, args.workload, args.steps, args.warmup, args.batch, args.prompt, args.layers)
+    _, peak_kind = peaks()
     if RANK == 0:
         line = {
-            "metric": BASELINE["metric"], "value": round(B / step_s, 3), "unit": "tok/s", "n_gpus": WORLD,
-            "steps": K, "warmup": W, "ms_per_step": round(step_s * 1e3, 4), "higher_is_better": True,
+            "metric": BASELINE["metric"], "value": r["value"], "unit": "tok/s", "n_gpus": WORLD,
+            "steps": r["steps"], "warmup": r["warmup"], "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {
-                "workload": f"{desc}; batch {B} sessions forked from one {prompt}-token random prompt, {K} batched "
-                            "greedy decode steps",
-                "global_batch": B, "seq_len": prompt + W + K,
-                "parallelism": f"{'tp' if args.workload.endswith('tp') else 'ep'}{WORLD}",
-                "prefill_tok_s": round(prompt / prefill_s, 1), "load_s": round(load_s, 1),
-                "weights_bytes_per_gpu": wbytes,
-                "weights_gbs_per_gpu": round(wbytes / step_s / 1e9, 1),
-                "hbm_frac_per_gpu": round(wbytes / step_s / 1e9 / peak, 4),
+                "workload": f"{r['desc']}; batch {r['batch']} sessions forked from one {r['prompt']}-token random "
+                            f"prompt, {r['steps']} batched greedy decode steps",
+                "global_batch": r["batch"], "seq_len": r["prompt"] + r["warmup"] + r["steps"],
+                "parallelism": r["parallelism"], "prefill_tok_s": r["prefill_tok_s"], "load_s": r["load_s"],
+                "weights_bytes_per_gpu": r["weights_bytes_per_gpu"],
+                "weights_gbs_per_gpu": r["weights_gbs_per_gpu"], "hbm_frac_per_gpu": r["hbm_frac_per_gpu"],
                 "l2": "inputs larger than L2 (the rank's weights are streamed every step)",
             },
-            "e2e": {"value": round(B * K / wall_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
-                    "d2h_bytes_per_step": 4 * B},
+            "e2e": {"value": r["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 12 * r["batch"],
+                    "d2h_bytes_per_step": 4 * r["batch"]},
             "peak_kind": peak_kind,
-            "clocks": clk,
+            "clocks": r["clocks"],
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -536,6 +553,9 @@ def main():
                     help="llama8b: the headline config (replicas at N > 1); the others shard one model over N GPUs")
     ap.add_argument("--batch", type=int, default=0, help="sharded workloads: decode batch (default: the config's)")
     ap.add_argument("--prompt", type=int, default=0, help="sharded workloads: prompt tokens (default: the config's)")
+    ap.add_argument("--sharded", default=os.environ.get("FISH_BENCH_SHARDED", "llama70b-tp"),
+                    choices=["none"] + sorted(SHARDED),
+                    help="at N > 1, the sharded workload also measured and reported in config.sharded")
     ap.add_argument("--layers", type=int, default=0,
                     help="sharded workloads: truncate the model (a plumbing check; the line says so)")
     args = ap.parse_args()

@@ -92,6 +92,42 @@ int env_int(const char* name, int def) {
 
 // RoPE cos/sin table [n_ctx][rot/2], angles in double, stored as float times
 // the attention factor (the reference's table, src/ops.cpp:75-124).
+bool tp_plan(int n_head, int n_head_kv, int head_dim, int n_ff, int vocab, int n_experts, int rank, int world,
+             TpPlan* out, std::string* err) {
+    auto fail = [&](const char* why) {
+        if (err) *err = std::string("tensor parallelism: ") + why;
+        return false;
+    };
+    if (world < 1 || rank < 0 || rank >= world || !out) return fail("bad rank or world");
+    const bool moe = n_experts > 0;   // experts split over the ranks (expert parallelism), not their rows
+    if (n_head % world || n_head_kv % world || n_head % n_head_kv || (!moe && n_ff % world) ||
+        (moe && n_experts % world) || vocab % world || (vocab / world) % 8)
+        return fail("kv heads, FFN rows (experts) and vocab rows must split evenly over the ranks");
+    TpPlan p;
+    p.heads = n_head / world;
+    p.head0 = rank * p.heads;
+    p.kv_heads = n_head_kv / world;
+    p.kv_head0 = rank * p.kv_heads;
+    p.q_rows = p.heads * head_dim;
+    p.q_row0 = p.head0 * head_dim;
+    p.kv_rows = p.kv_heads * head_dim;
+    p.kv_row0 = p.kv_head0 * head_dim;
+    if (moe) {
+        p.experts = n_experts / world;
+        p.expert0 = rank * p.experts;
+    } else {
+        p.ff_rows = n_ff / world;
+        p.ff_row0 = rank * p.ff_rows;
+    }
+    p.vocab_rows = vocab / world;
+    p.vocab_row0 = rank * p.vocab_rows;
+    // (the loader checks that attn_output's and ffn_down's input slices are
+    // whole blocks of their weight type: then the per-block integer sums are
+    // the unsharded ones)
+    *out = p;
+    return true;
+}
+
 void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, std::vector<float>& sn) {
     const int rot = c.rot_dim, half = rot / 2;
     cs.assign((size_t)c.n_ctx * half, 0.0f);
@@ -144,6 +180,8 @@ Engine::~Engine() {
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
     cudaFree(step_ph_); cudaFree(step_ctl_); cudaFree(step_keys_); cudaFree(att_part_);
     cudaFree(tp_tmp_); cudaFree(tp_logits_); cudaFree(sel_loc_);
+    cudaFree(gg_); cudaFree(gu_); cudaFree(geo_); cudaFree(grp_src_); cudaFree(grp_pos_); cudaFree(grp_count_);
+    cudaFree(chunk_exp_); cudaFree(gact_mem_);
     if (nccl_) nccl_api(nullptr)->comm_destroy((ncclComm_t)nccl_);   // after the graphs that hold its calls
     if (probe_img_) cudaFree(probe_img_);
     if (probe_h_) cudaFree(probe_h_);
@@ -263,19 +301,16 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     c.out_rows = c.vocab;
     c.out_row0 = 0;
     if (tp_world_ > 1) {   // this rank's heads, FFN rows and vocab rows
-        const int N = tp_world_;
-        const bool moe = c.n_experts > 0;   // experts are split over the ranks (expert parallelism), not their rows
-        if (c.n_head_kv % N || (!moe && c.n_ff % N) || (moe && c.n_experts % N) || c.vocab % N || (c.vocab / N) % 8) {
-            if (err) *err = "tensor parallelism: kv heads, FFN rows (experts) and vocab rows must split evenly over the ranks";
+        TpPlan tp;
+        if (!tp_plan(c.n_head, c.n_head_kv, c.head_dim, c.n_ff, c.vocab, c.n_experts, tp_rank_, tp_world_, &tp, err))
             return false;
-        }
-        c.n_head /= N;
-        c.n_head_kv /= N;
-        if (!moe) c.n_ff /= N;
-        ep_n_ = moe ? c.n_experts / N : 0;
-        ep_e0_ = tp_rank_ * ep_n_;
-        c.out_rows = c.vocab / N;
-        c.out_row0 = tp_rank_ * c.out_rows;
+        c.n_head = tp.heads;
+        c.n_head_kv = tp.kv_heads;
+        if (c.n_experts == 0) c.n_ff = tp.ff_rows;
+        ep_n_ = tp.experts;
+        ep_e0_ = tp.expert0;
+        c.out_rows = tp.vocab_rows;
+        c.out_row0 = tp.vocab_row0;
     }
     {
         const std::string type = g.str(key("rope.scaling.type"), "none");
@@ -573,6 +608,28 @@ bool Engine::alloc_buffers(std::string* err) {
         CK(cudaMalloc(&sel_, sizeof(int32_t) * R));
         if (tp_world_ > 1) CK(cudaMalloc(&sel_loc_, sizeof(int32_t) * R));
         CK(cudaMalloc(&wsel_, sizeof(float) * R));
+        // expert grouping: local experts x kMaxBatch grouped rows
+        const int nel = tp_world_ > 1 ? (c.n_experts + tp_world_ - 1) / tp_world_ : c.n_experts;
+        grp_rows_ = nel * kMaxBatch;
+        const int FE = std::max(E, c.n_ff_exp);
+        const size_t gld = align_up((size_t)FE, 16);
+        CK(cudaMalloc(&gg_, sizeof(float) * (size_t)grp_rows_ * c.n_ff_exp));
+        CK(cudaMalloc(&gu_, sizeof(float) * (size_t)grp_rows_ * c.n_ff_exp));
+        CK(cudaMalloc(&geo_, sizeof(float) * (size_t)grp_rows_ * E));
+        CK(cudaMalloc(&grp_src_, sizeof(int32_t) * grp_rows_));
+        CK(cudaMalloc(&grp_pos_, sizeof(int32_t) * R));
+        CK(cudaMalloc(&grp_count_, sizeof(int32_t) * nel));
+        CK(cudaMalloc(&chunk_exp_, sizeof(int32_t) * nel * (kMaxBatch / 4)));
+        const size_t gq = (size_t)grp_rows_ * gld, g32 = (size_t)grp_rows_ * (FE / 32 + 1), g256 = (size_t)grp_rows_ * (FE / 256 + 1);
+        CK(cudaMalloc(&gact_mem_, 2 * gq + g32 * (4 + 4 + 2) + g256 * 4 + 1024));
+        uint8_t* gp = reinterpret_cast<uint8_t*>(gact_mem_);
+        gact_.q32 = reinterpret_cast<int8_t*>(gp); gp += gq;
+        gact_.qk = reinterpret_cast<int8_t*>(gp); gp += gq;
+        gact_.d32 = reinterpret_cast<float*>(gp); gp += align_up(g32 * 4, 16);
+        gact_.s32 = reinterpret_cast<int32_t*>(gp); gp += align_up(g32 * 4, 16);
+        gact_.dk = reinterpret_cast<float*>(gp); gp += align_up(g256 * 4, 16);
+        gact_.bsk = reinterpret_cast<int16_t*>(gp);
+        gact_.ld = (int)gld;
     }
     // activation planes: q32 | qk (R x ld each), d32 | s32 | bsk (R x max_k/32), dk (R x max_k/256)
     const size_t nq = (size_t)R * ld, n32 = (size_t)R * (max_k_ / 32 + 1), n256 = (size_t)R * (max_k_ / 256 + 1);
@@ -801,7 +858,8 @@ bool Engine::fusable(const DevW* const* ws, int n, int T) const {
 }
 
 bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
-                        const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro, bool swiglu) {
+                        const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro, bool swiglu,
+                        const int32_t* expert) {
     // T >= 16 tokens with quantised planes: one tensor-core launch per
     // segment; otherwise GEMV launches of up to 4 (streamed) or 8 tokens
     int chunk = 8;
@@ -816,7 +874,7 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
             p.seg[i].rows = ws[i]->n_out;
         }
         chunk = fbk_gemv_chunk(&p);
-        if (T >= 16 && !pro && !swiglu && fbk_gemm_eligible(&p)) chunk = T;
+        if (T >= 16 && !pro && !swiglu && !expert && fbk_gemm_eligible(&p)) chunk = T;
     }
     for (int t0 = 0; t0 < T; t0 += chunk) {
         const int nt = std::min(chunk, T - t0);
@@ -840,6 +898,8 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
             s.ldy = ldys[i];
             s.bias = biases ? biases[i] : nullptr;
             s.epi = epi;
+            s.expert = expert;
+            s.expert_bytes = ws[i]->expert_bytes;
             bytes += gemv_bytes(*ws[i], nt);
         }
         if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, bytes, fbk_gemm(&g, stream_));
@@ -1127,6 +1187,89 @@ bool Engine::run_step(int sid, int n_steps, int32_t* out_dev, std::string* err) 
     return true;
 }
 
+// ------------------------------------------------------------------ MoE
+
+// The expert FFNs of a batched step (model.cpp:1523-1599) with the rows
+// routed to each local expert gathered together: grouped rows e * T + j
+// (k_moe_group / k_moe_gather), gate/up and down over each expert's rows, so
+// its weights stream once per step, then the weighted combine through
+// grp_pos. Eager calls read the counts back and give each expert one call of
+// exactly its rows (the tensor-core GEMM from 16 rows); inside a graph
+// capture the counts stay on the device and every (expert, 4-row chunk)
+// launch reads its expert id (-1: no rows, no weight bytes fetched). Rows are
+// computed by the same kernels in either form, so the results are the same
+// bits as the one-row-per-call path.
+bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t* esel, int nel, float* out,
+                         std::string* err) {
+    const Config& c = cfg_;
+    const int K = c.n_experts_per_tok, F = c.n_ff_exp, E = c.n_embd;
+    const int nchunk = (T + 3) / 4;
+    if (nel * T > grp_rows_ || nchunk > kMaxBatch / 4) { if (err) *err = "MoE grouping: batch too large"; return false; }
+    CKP(PC_OTHER, 0, fbk_moe_group(esel, T, K, nel, grp_src_, grp_pos_, grp_count_, chunk_exp_, nchunk, stream_));
+    ActQ src = a, ga = gact_, gf = gact_;
+    src.K = E;
+    ga.K = E;
+    gf.K = F;
+    CKP(PC_OTHER, 0, fbk_moe_gather(&src, &ga, grp_src_, K, nel * T, E, stream_));
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    CK(cudaStreamIsCapturing(stream_, &cs));
+    const bool exact = cs == cudaStreamCaptureStatusNone;
+    std::vector<int32_t> cnt((size_t)nel, 0);
+    if (exact) {
+        CK(cudaMemcpyAsync(cnt.data(), grp_count_, sizeof(int32_t) * nel, cudaMemcpyDeviceToHost, stream_));
+        CK(cudaStreamSynchronize(stream_));
+    }
+    auto view = [](const DevW& w, int e) {
+        DevW v = w;
+        v.d = w.d + (size_t)e * w.expert_bytes;
+        v.n_exp = 1;
+        return v;
+    };
+    for (int e = 0; e < nel; ++e) {
+        const int r0 = e * T;
+        if (exact) {
+            if (!cnt[e]) continue;
+            const DevW gw = view(L.gate_exps, e), uw = view(L.up_exps, e);
+            const DevW* ws[2] = {&gw, &uw};
+            float* ys[2] = {gg_ + (size_t)r0 * F, gu_ + (size_t)r0 * F};
+            const int lds[2] = {F, F};
+            if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, r0, E), cnt[e], EPI_STORE, err)) return false;
+        } else {
+            for (int ch = 0; ch < nchunk; ++ch) {
+                const int nt = std::min(4, T - 4 * ch), rr = r0 + 4 * ch;
+                const DevW* ws[2] = {&L.gate_exps, &L.up_exps};
+                float* ys[2] = {gg_ + (size_t)rr * F, gu_ + (size_t)rr * F};
+                const int lds[2] = {F, F};
+                if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, rr, E), nt, EPI_STORE, err, nullptr, false,
+                                chunk_exp_ + e * nchunk + ch))
+                    return false;
+            }
+        }
+    }
+    CKP(PC_NORMQ, 0, fbk_silu_mul_quant(gg_, F, gu_, F, nel * T, F, probe_ ? probe_h_ : nullptr, F, &gf, want32_f_,
+                                        wantk_f_, stream_));
+    if (probe_ && !probe_grouped(3, gf, nel * T, T * K, F, err)) return false;
+    for (int e = 0; e < nel; ++e) {
+        const int r0 = e * T;
+        if (exact) {
+            if (!cnt[e]) continue;
+            const DevW dw = view(L.down_exps, e);
+            if (!gemv(dw, act_row(gf, r0, F), cnt[e], geo_ + (size_t)r0 * E, E, nullptr, EPI_STORE, nullptr, 0, nullptr,
+                      err))
+                return false;
+        } else {
+            for (int ch = 0; ch < nchunk; ++ch) {
+                const int nt = std::min(4, T - 4 * ch), rr = r0 + 4 * ch;
+                if (!gemv(L.down_exps, act_row(gf, rr, F), nt, geo_ + (size_t)rr * E, E, nullptr, EPI_STORE, nullptr, 0,
+                          chunk_exp_ + e * nchunk + ch, err))
+                    return false;
+            }
+        }
+    }
+    CKP(PC_OTHER, 0, fbk_moe_combine_grouped(out, E, geo_, grp_pos_, wsel_, T, K, E, stream_));
+    return true;
+}
+
 // ------------------------------------------------------------------ forward
 
 bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int l0, int l1) {
@@ -1214,6 +1357,16 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
             const bool ep = tp_world_ > 1;
             const int32_t* esel = ep ? sel_loc_ : sel_;
             if (ep) CKP(PC_OTHER, 0, fbk_moe_localize(sel_, T * K, ep_e0_, ep_n_, sel_loc_, stream_));
+            if (T > 1) {   // batched step: tokens grouped per expert
+                float* out = x_;
+                if (ep) {
+                    CK(cudaMemsetAsync(tp_tmp_, 0, sizeof(float) * (size_t)T * E, stream_));
+                    out = tp_tmp_;
+                }
+                if (!moe_grouped(L, a, T, esel, ep ? ep_n_ : NE, out, err)) return false;
+                if (ep && !tp_reduce_add(T, err)) return false;
+                continue;
+            }
             for (int t = 0; t < T; ++t) {
                 const ActQ ar = act_row(a, t, E);
                 for (int k = 0; k < K; ++k) {
@@ -1408,6 +1561,28 @@ bool Engine::probe_image(int stage, int rows, int K, std::string* err) {
     return true;
 }
 
+// Stage records of grouped rows (expert-major) back in routed-row order
+// r = t K + k, as the one-row-per-call path records them.
+bool Engine::probe_grouped(int stage, const ActQ& a, int grouped_rows, int rows, int K, std::string* err) {
+    LayerProbe& p = *probe_;
+    if (!probe_float(stage, probe_h_, grouped_rows, K, err)) return false;
+    if (!probe_planes(stage, a, grouped_rows, K, a.q32 && want32_f_, a.qk && wantk_f_, err)) return false;
+    std::vector<int32_t> pos((size_t)rows);
+    CK(cudaMemcpy(pos.data(), grp_pos_, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost));
+    auto regroup = [&](auto& v, size_t per_row) {
+        if (v.empty()) return;
+        std::remove_reference_t<decltype(v)> o(per_row * (size_t)rows);
+        for (int r = 0; r < rows; ++r)
+            if (pos[r] >= 0) std::copy_n(v.begin() + (size_t)pos[r] * per_row, per_row, o.begin() + (size_t)r * per_row);
+        v.swap(o);
+    };
+    regroup(p.f[stage], (size_t)K);
+    regroup(p.rk[stage], (size_t)(K / 256) * 276);
+    regroup(p.r32[stage], (size_t)(K / 32) * 40);
+    p.rows[stage] = rows;
+    return true;
+}
+
 bool Engine::layer_probe(int li, int pos0, const float* x_in, int T, float* x_out, LayerProbe* p, std::string* err) {
     const Config& c = cfg_;
     if (li < 0 || li >= c.n_layers || T <= 0 || T > kMaxBatch || pos0 < 0 || !x_in || !x_out || !p) {
@@ -1427,7 +1602,7 @@ bool Engine::layer_probe(int li, int pos0, const float* x_in, int T, float* x_ou
         probe_img_bytes_ = img_need;
     }
     const int F = c.n_experts > 0 ? c.n_ff_exp : c.n_ff;
-    const size_t h_need = (size_t)kMaxBatch * std::max(1, c.n_experts_per_tok) * F;
+    const size_t h_need = (size_t)std::max(kMaxBatch * std::max(1, c.n_experts_per_tok), grp_rows_) * F;
     if (!probe_h_) CK(cudaMalloc(&probe_h_, sizeof(float) * h_need));
     std::vector<int32_t> ids(T, 0);
     std::vector<int> sids(T, 0), pos(T);

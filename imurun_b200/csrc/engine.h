@@ -46,6 +46,23 @@ struct Config {
     int kv_dim() const { return n_head_kv * head_dim; }
 };
 
+// This rank's slices under tensor / expert parallelism over `world` ranks
+// (one process per GPU): heads and kv heads, the q / k / v rows and the
+// matching input slice of attn_output, FFN rows and the input slice of
+// ffn_down (dense), or experts (MoE), and vocab rows of the output
+// projection. Every slice is contiguous and rank-ordered; false (with err)
+// when the counts do not split evenly, the vocab slice is not whole 8-row
+// tiles, or an input slice is not whole 256-value blocks.
+struct TpPlan {
+    int head0 = 0, heads = 0, kv_head0 = 0, kv_heads = 0;
+    int q_row0 = 0, q_rows = 0, kv_row0 = 0, kv_rows = 0;   // also attn_output's input slice (q)
+    int ff_row0 = 0, ff_rows = 0;                             // also ffn_down's input slice (dense)
+    int expert0 = 0, experts = 0;                             // MoE
+    int vocab_row0 = 0, vocab_rows = 0;
+};
+bool tp_plan(int n_head, int n_head_kv, int head_dim, int n_ff, int vocab, int n_experts, int rank, int world,
+             TpPlan* out, std::string* err);
+
 // RoPE cos/sin table [n_ctx][rot_dim/2] for c (uses n_ctx, rot_dim,
 // freq_base and the scaling fields); ff = per-pair frequency factors or null.
 void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, std::vector<float>& sn);
@@ -204,6 +221,7 @@ private:
     bool probe_float(int idx, const float* dev, int rows, int K, std::string* err);
     bool probe_planes(int stage, const ActQ& a, int rows, int K, bool want32, bool wantk, std::string* err);
     bool probe_image(int stage, int rows, int K, std::string* err);
+    bool probe_grouped(int stage, const ActQ& a, int grouped_rows, int rows, int K, std::string* err);
     LayerProbe* probe_ = nullptr;
     uint8_t* probe_img_ = nullptr;     // device: image dumps of the fused GEMV prologues
     size_t probe_img_bytes_ = 0;
@@ -220,7 +238,10 @@ private:
               unsigned long long* keys = nullptr);
     bool gemv_group(const DevW* const* ws, float* const* ys, const int* ldys, const float* const* biases, int n,
                     const ActQ& a, int T, int epi, std::string* err, const GemvPro* pro = nullptr,
-                    bool swiglu = false);
+                    bool swiglu = false, const int32_t* expert = nullptr);
+    // MoE FFN of a batched step (T > 1) with the tokens grouped per expert:
+    // each expert's weights stream once over all rows routed to it
+    bool moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t* esel, int nel, float* out, std::string* err);
     // true when a T-token GEMV over these matrices can build its own int8
     // activations (streamed kernel with a prologue)
     bool fusable(const DevW* const* ws, int n, int T) const;
@@ -289,6 +310,12 @@ private:
     float* tp_tmp_ = nullptr;         // [kMaxBatch][E] partial sums of o / down
     float* tp_logits_ = nullptr;      // [world][kMaxBatch][out_rows] gathered vocab slices
     int32_t* sel_loc_ = nullptr;      // expert parallelism: routed experts as local ids (-1: another rank's)
+    // expert grouping (batched MoE steps): grouped rows e * T + j of local expert e
+    ActQ gact_{};                     // int8 activations of the grouped rows
+    int8_t* gact_mem_ = nullptr;
+    float *gg_ = nullptr, *gu_ = nullptr, *geo_ = nullptr;   // grouped gate / up (then h) / down outputs
+    int32_t *grp_src_ = nullptr, *grp_pos_ = nullptr, *grp_count_ = nullptr, *chunk_exp_ = nullptr;
+    int grp_rows_ = 0;                // capacity: local experts x kMaxBatch
     int ep_e0_ = 0, ep_n_ = 0;        // this rank's experts [ep_e0_, ep_e0_ + ep_n_)
     bool tp_reduce_add(int T, std::string* err);   // x += all-reduce(tp_tmp_)
     bool tp_gather_logits(int rows, float* logits_dev, std::string* err);

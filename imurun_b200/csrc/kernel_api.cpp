@@ -519,6 +519,23 @@ int fbx_argmax_penalized(const float* x, int n, const int32_t* recent, int n_rec
     return 0;
 }
 
+int fbx_tp_plan(int n_head, int n_head_kv, int head_dim, int n_ff, int vocab, int n_experts, int rank, int world,
+                int32_t* out) {
+    if (!out) return -1;
+    fb::TpPlan p;
+    if (!fb::tp_plan(n_head, n_head_kv, head_dim, n_ff, vocab, n_experts, rank, world, &p, nullptr)) return -1;
+    const int32_t v[14] = {p.head0, p.heads, p.kv_head0, p.kv_heads, p.q_row0, p.q_rows, p.kv_row0, p.kv_rows,
+                           p.ff_row0, p.ff_rows, p.expert0, p.experts, p.vocab_row0, p.vocab_rows};
+    std::memcpy(out, v, sizeof(v));
+    return 0;
+}
+
+int fbx_moe_localize_host(const int32_t* sel, int n, int e0, int n_local, int32_t* out) {
+    if (!sel || !out || n < 0 || n_local < 0) return -1;
+    for (int i = 0; i < n; ++i) out[i] = fb_localize_expert(sel[i], e0, n_local);
+    return 0;
+}
+
 int fbx_embed(int type, const void* table, int E, int n_rows, const int32_t* ids, int T, float* out) {
     if (!table || !ids || !out || E <= 0 || n_rows <= 0 || T <= 0) return -1;
     for (int t = 0; t < T; ++t) if (ids[t] < 0 || ids[t] >= n_rows) return -1;

@@ -18,20 +18,24 @@
 // order) are those of the GEMV kernels, so a row's value does not depend on
 // the kernel or on the number of tokens in the call.
 //
-// CTA tile: 128 weight rows (the TMEM lanes) x 32 tokens (the MMA N). Warps:
+// CTA tile: 128 weight rows (the TMEM lanes) x 64 tokens (the MMA N). Warps:
 //   0      TMA producer: per block, the raw Q4_K bytes of the 128 rows (one
-//          5-D tensor-map box over the tile-major device layout) and the 32
+//          5-D tensor-map box over the tile-major device layout) and the 64
 //          tokens' int8 activations (two 128-byte-swizzled 2-D boxes, the
-//          UMMA K-major SW128 layout) into a 4-stage ring;
-//   1      TMEM allocation and the MMA issue (one elected lane);
+//          UMMA K-major SW128 layout) into a 3-stage ring;
+//   1      TMEM allocation and the MMA issue (one elected lane, descriptors
+//          formed once and offset per instruction);
 //   2..5   expansion of the raw block into the three planes (one row per
 //          thread, written in the SW128 layout the MMA descriptors name);
-//   6..13  epilogue: tcgen05.ld of the three accumulators, the block's float
-//          term, the tree, and the output rows.
-// Accumulators: two passes of two blocks each in flight (3 planes x 32
-// columns per block), 384 of the 512 TMEM columns. Every wait is bounded;
-// a CTA that gives up raises the error flag, lets its copies and MMAs land,
-// frees its tensor memory and returns.
+//   6..21  epilogue: tcgen05.ld of the three accumulators, the block's float
+//          term and the GEMV-order tree (a warp: 32 rows x 16 tokens), the
+//          output rows.
+// Tensor memory (all 512 columns): two accumulator sets of one block each
+// (3 planes x 64 columns), so the MMAs of block s+1 run while block s is
+// drained, and the tree's two pending partial sums of every (row, token)
+// (columns 384..511); the running total and the third pending term stay in
+// registers. Every wait is bounded; a CTA that gives up raises the error
+// flag, lets its copies and MMAs land, frees its tensor memory and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -51,20 +55,24 @@ namespace fb {
 
 namespace tc {
 
-constexpr int BM = 128, BN = 32, NS = 4;
+constexpr int BM = 128, BN = 64, NS = 3;
 constexpr int kWBytes = BM * 144;                 // raw block of 128 rows
-constexpr int kXHalf = BN * 128;                  // 32 tokens x 128 activations (one SW128 box)
-constexpr int kStage = kWBytes + 2 * kXHalf;      // 26624 = 26 KiB
+constexpr int kXHalf = BN * 128;                  // 64 tokens x 128 activations (one SW128 box)
+constexpr int kStage = kWBytes + 2 * kXHalf;      // 34816 = 34 KiB
 constexpr int kPlane = BM * 128;                  // 128 rows x 128 values
 constexpr int kPlanes = 3 * kPlane;               // one half-block's three planes
 constexpr int kRingOff = 0;
-constexpr int kPlaneOff = NS * kStage;            // 106496 (1 KiB aligned)
-constexpr int kBarOff = kPlaneOff + 2 * kPlanes;  // 204800
+constexpr int kPlaneOff = NS * kStage;            // 104448 (1 KiB aligned)
+constexpr int kBarOff = kPlaneOff + 2 * kPlanes;  // 202752
 constexpr int kSmem = kBarOff + 256 + 1024;       // barriers + TMEM address + alignment slack
-constexpr int kThreads = 14 * 32;
+constexpr int kEpiWarps = 16;                     // 4 TMEM lane quarters x 4 runs of 16 tokens
+constexpr int kThreads = (6 + kEpiWarps) * 32;
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 3 * BN;                  // one block's three accumulators
+constexpr int kPaCol = 2 * kAccCols, kPbCol = kPaCol + BN;   // tree state: pending sums pa, pb
+constexpr int kMaxBlocks = 128;                   // K <= 32768
 static_assert(kStage % 1024 == 0 && kPlane % 1024 == 0, "SW128 atoms need 1 KiB alignment");
+static_assert(kPbCol + BN <= kTmemCols, "tensor memory budget");
 
 // barrier slots (uint64 each) at kBarOff
 enum { B_FULL = 0, B_EMPTY = NS, B_PFULL = 2 * NS, B_PEMPTY = 2 * NS + 2, B_AFULL = 2 * NS + 4, B_AEMPTY = 2 * NS + 6,
@@ -126,6 +134,14 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
@@ -140,21 +156,6 @@ constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN 
 
 // byte offset of (row, 16-byte chunk c) in a 128-byte-swizzled K-major tile
 __device__ __forceinline__ uint32_t sw128_off(int row, int c) { return (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4)); }
-
-// GEMV block order: the pairwise tree over a group's 8 blocks
-struct Tree {
-    float acc[16], pa[16], pb[16];
-};
-__device__ __forceinline__ void tree_pair(Tree& tr, const float (&u)[16], int pair) {
-    // u = t_{2 pair} + t_{2 pair + 1}
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        if (pair == 0) tr.pa[i] = u[i];
-        else if (pair == 1) tr.pa[i] = __fadd_rn(tr.pa[i], u[i]);
-        else if (pair == 2) tr.pb[i] = u[i];
-        else tr.acc[i] = __fadd_rn(tr.acc[i], __fadd_rn(tr.pa[i], __fadd_rn(tr.pb[i], u[i])));
-    }
-}
 
 }  // namespace tc
 
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     volatile int* s_abort = reinterpret_cast<volatile int*>(sm + kBarOff + 8 * B_COUNT + 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * BN, row0 = blockIdx.y * BM;
-    const int nsteps = args.nsteps, npass = (nsteps + 1) / 2;
+    const int nsteps = args.nsteps;
     pdl_trigger();
 
     if (threadIdx.x == 0) {
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             mbar_init(&bar[B_PFULL + i], 4);
             mbar_init(&bar[B_PEMPTY + i], 1);
             mbar_init(&bar[B_AFULL + i], 1);
-            mbar_init(&bar[B_AEMPTY + i], 8);
+            mbar_init(&bar[B_AEMPTY + i], kEpiWarps);
         }
         mbar_init(&bar[B_DRAIN], 1);
         mbar_fence_init();
@@ -224,14 +225,17 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                 mbar_wait_bounded(&bar[B_FULL + k % NS], (uint32_t)((k / NS) & 1));
         }
     } else if (warp == 1) {
-        // ---- MMA issue
+        // ---- MMA issue: block s accumulates into set s & 1
         if (lane == 0) {
+            // descriptor = start address >> 4 in the low bits: a byte offset X
+            // (16-byte multiple, inside shared memory) is + (X >> 4)
+            const uint64_t a0 = sw128_desc(sm + kPlaneOff), b0 = sw128_desc(sm + kRingOff + kWBytes);
             bool ok = true;
             int s = 0;
             for (; s < nsteps && ok; ++s) {
-                const int st = s % NS, p = s >> 1, ab = p & 1, bip = s & 1;
-                if (bip == 0 && p >= 2) {
-                    ok = mbar_wait(&bar[B_AEMPTY + ab], (uint32_t)(((p >> 1) - 1) & 1), s_abort);
+                const int st = s % NS, ab = s & 1;
+                if (s >= 2) {
+                    ok = mbar_wait(&bar[B_AEMPTY + ab], (uint32_t)(((s >> 1) - 1) & 1), s_abort);
                     tc_fence_after();
                 }
                 if (ok) ok = mbar_wait(&bar[B_FULL + st], (uint32_t)((s / NS) & 1), s_abort);
@@ -240,21 +244,21 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                     ok = mbar_wait(&bar[B_PFULL + pb], (uint32_t)((q >> 1) & 1), s_abort);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint8_t* planes = sm + kPlaneOff + pb * kPlanes;
-                    const uint8_t* xs = sm + kRingOff + st * kStage + kWBytes + h * kXHalf;
+                    const uint64_t ab0 = a0 + (uint64_t)((pb * kPlanes) >> 4);
+                    const uint64_t bb0 = b0 + (uint64_t)((st * kStage + h * kXHalf) >> 4);
 #pragma unroll
                     for (int j = 0; j < 3; ++j) {
-                        const uint32_t d = tmem + (uint32_t)(ab * 2 * kAccCols + bip * kAccCols + j * BN);
+                        const uint32_t d = tmem + (uint32_t)(ab * kAccCols + j * BN);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            umma_i8(d, sw128_desc(planes + j * kPlane + 32 * kk), sw128_desc(xs + 32 * kk), kIdesc,
-                                    (h > 0 || kk > 0) ? 1u : 0u);
+                            umma_i8(d, ab0 + (uint64_t)((j * kPlane + 32 * kk) >> 4), bb0 + (uint64_t)((32 * kk) >> 4),
+                                    kIdesc, (h > 0 || kk > 0) ? 1u : 0u);
                     }
                     umma_commit(&bar[B_PEMPTY + pb]);
                 }
                 if (!ok) break;
                 umma_commit(&bar[B_EMPTY + st]);
-                if (bip == 1 || s == nsteps - 1) umma_commit(&bar[B_AFULL + ab]);
+                umma_commit(&bar[B_AFULL + ab]);
             }
             if (!ok) {
                 if (args.err) atomicExch(args.err, 4);
@@ -323,70 +327,99 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
     } else {
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (its rows),
-        // columns of tokens 16 th .. 16 th + 15 of the tile
-        const int lg = warp & 3, th = (warp - 6) >> 2;
+        // columns of tokens 16 tq .. 16 tq + 15 of the tile
+        const int lg = warp & 3, tq = (warp - 6) >> 2;
         const int row = row0 + 32 * lg + lane;
         const bool row_ok = row < args.g.rows;
         const int K = args.K, nb = K / 256;
-        Tree tr;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * lg) << 16);
+        // per (row, token): acc (the running row value) and pc (a group's
+        // pending third term) in registers, pa / pb (its pending pair sums)
+        // in tensor memory; the GEMV order of a group's 8 block terms t_b is
+        //   ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7)), acc += group
+        float acc[16], pc[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) tr.acc[i] = tr.pa[i] = tr.pb[i] = 0.0f;
+        for (int i = 0; i < 16; ++i) acc[i] = pc[i] = 0.0f;
+        // one block's terms (t) into the tree: case bi of the group
+        auto push = [&](int bi, int c, const float (&t)[8]) {
+            const uint32_t ca = lane_base + (uint32_t)(kPaCol + 16 * tq + 8 * c);
+            const uint32_t cb = lane_base + (uint32_t)(kPbCol + 16 * tq + 8 * c);
+            float v[8], w[8];
+            int iv[8], iw[8];
+            switch (bi) {
+                case 0: tmem_st8(ca, t); break;
+                case 1: case 3:
+                    tmem_ld8(ca, iv);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        v[k] = __fadd_rn(__int_as_float(iv[k]), bi == 1 ? t[k] : __fadd_rn(pc[8 * c + k], t[k]));
+                    tmem_st8(ca, v);
+                    break;
+                case 2: case 6:
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) pc[8 * c + k] = t[k];
+                    break;
+                case 4: tmem_st8(cb, t); break;
+                case 5:
+                    tmem_ld8(cb, iw);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) w[k] = __fadd_rn(__int_as_float(iw[k]), t[k]);
+                    tmem_st8(cb, w);
+                    break;
+                default:
+                    tmem_ld8(ca, iv);
+                    tmem_ld8(cb, iw);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        acc[8 * c + k] = __fadd_rn(acc[8 * c + k],
+                            __fadd_rn(__int_as_float(iv[k]), __fadd_rn(__int_as_float(iw[k]), __fadd_rn(pc[8 * c + k], t[k]))));
+            }
+        };
         bool ok = true;
-        for (int p = 0; p < npass && ok; ++p) {
-            const int ab = p & 1;
-            ok = mbar_wait(&bar[B_AFULL + ab], (uint32_t)((p >> 1) & 1), s_abort);
+        for (int s = 0; s < nsteps && ok; ++s) {
+            const int ab = s & 1, bi = s & 7;
+            // this block's scales, fetched before the wait for its MMAs
+            float dx[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int t = t0 + 16 * tq + i;
+                dx[i] = t < args.T ? __ldg(args.dk + (size_t)t * nb + s) : 0.0f;
+            }
+            const uint32_t hw =
+                row_ok ? __ldg(reinterpret_cast<const uint32_t*>(args.g.w + block_offset_tm(T_Q4_K, K, row, s))) : 0u;
+            ok = mbar_wait(&bar[B_AFULL + ab], (uint32_t)((s >> 1) & 1), s_abort);
             if (!ok) break;
             tc_fence_after();
-            float u[16];
+            const float dw = h2f((uint16_t)(hw & 0xFFFFu)), dmw = h2f((uint16_t)(hw >> 16));
+            const uint32_t base = lane_base + (uint32_t)(ab * kAccCols + 16 * tq);
 #pragma unroll
-            for (int bip = 0; bip < 2; ++bip) {
-                const int s = 2 * p + bip;
-                if (s < nsteps) {
-                    float dw = 0.0f, dmw = 0.0f;
-                    if (row_ok) {
-                        const uint32_t hw =
-                            __ldg(reinterpret_cast<const uint32_t*>(args.g.w + block_offset_tm(T_Q4_K, K, row, s)));
-                        dw = h2f((uint16_t)(hw & 0xFFFFu));
-                        dmw = h2f((uint16_t)(hw >> 16));
-                    }
-                    const uint32_t base =
-                        tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)(ab * 2 * kAccCols + bip * kAccCols + 16 * th);
+            for (int c = 0; c < 2; ++c) {
+                int d0[8], d1[8], d2[8];
+                tmem_ld8(base + 8 * c, d0);
+                tmem_ld8(base + BN + 8 * c, d1);
+                tmem_ld8(base + 2 * BN + 8 * c, d2);
+                tmem_ld_wait();
+                if (c == 1) {   // the set's last read: let the next block's MMAs write it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar[B_AEMPTY + ab]);
+                }
+                float t[8];
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {   // two runs of 8 tokens
-                        int d0[8], d1[8], d2[8];
-                        tmem_ld8(base + 8 * hh, d0);
-                        tmem_ld8(base + BN + 8 * hh, d1);
-                        tmem_ld8(base + 2 * BN + 8 * hh, d2);
-                        tmem_ld_wait();
+                for (int k = 0; k < 8; ++k) t[k] = q4k_term(dw, dmw, dx[8 * c + k], 8 * d0[k] + d1[k], d2[k]);
+                push(bi, c, t);
+                // a row's last group may be short: its missing blocks add +0
+                if (s == nsteps - 1) {
+                    float z[8];
 #pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            const int i = 8 * hh + k, t = t0 + 16 * th + i;
-                            const float dx = t < args.T ? __ldg(args.dk + (size_t)t * nb + s) : 0.0f;
-                            const float term = q4k_term(dw, dmw, dx, 8 * d0[k] + d1[k], d2[k]);
-                            u[i] = bip == 0 ? term : __fadd_rn(u[i], term);
-                        }
-                    }
-                    // a row's last group may be short: its missing blocks add +0
-                    // in the GEMV order (zero pairs up to the group's close)
-                    if (s == nsteps - 1 && (s & 7) != 7) {
-                        const int bi = s & 7;
-                        if ((bi & 1) == 0) {
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) u[i] = __fadd_rn(u[i], 0.0f);
-                        }
-                        tree_pair(tr, u, bi >> 1);
-                        float z[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) z[i] = __fadd_rn(0.0f, 0.0f);
-                        for (int pp = (bi >> 1) + 1; pp < 4; ++pp) tree_pair(tr, z, pp);
-                    } else if (bip == 1) {
-                        tree_pair(tr, u, (s & 7) >> 1);
-                    }
+                    for (int k = 0; k < 8; ++k) z[k] = 0.0f;
+                    for (int zb = bi + 1; zb < 8; ++zb) push(zb, c, z);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar[B_AEMPTY + ab]);
+            tmem_st_wait();
         }
         if (!ok) {
             if (args.err && lane == 0) atomicExch(args.err, 4);
@@ -395,8 +428,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         if (ok && !*s_abort && row_ok) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const int t = t0 + 16 * th + i;
-                if (t < args.T) store_out(args.g, row, t, tr.acc[i]);
+                const int t = t0 + 16 * tq + i;
+                if (t < args.T) store_out(args.g, row, t, acc[i]);
             }
         }
     }
@@ -448,7 +481,7 @@ bool make_wmap(CUtensorMap* m, const uint8_t* base, int gb, int n_groups, int n_
 // aligned operands (TMA), at least 16 tokens. FISH_NO_TC=1 turns it off.
 extern "C" int fbk_gemm_tc_eligible(const GemvSeg* g, const ActQ* a, int K, int T) {
     static const bool off = getenv("FISH_NO_TC") != nullptr;
-    if (off || g->type != T_Q4_K || K % 256 || T < 16 || g->expert || g->amax) return 0;
+    if (off || g->type != T_Q4_K || K % 256 || K / 256 > tc::kMaxBlocks || T < 16 || g->expert || g->amax) return 0;
     if ((reinterpret_cast<uintptr_t>(g->w) & 15) || (reinterpret_cast<uintptr_t>(a->qk) & 15) || a->ld % 16) return 0;
     return encode_fn() ? 1 : 0;
 }

@@ -415,6 +415,31 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     }
     __syncthreads();
 
+    // every segment routed to an expert no row of this call uses (id -1:
+    // another rank's expert, or an empty chunk of a grouped MoE step): no
+    // weights, no arithmetic; the rows are zero, as the full path gives them
+    if (jobs.wait_first && !args.swiglu) {
+        pdl_wait();
+        bool idle = true;
+#pragma unroll
+        for (int i = 0; i < kMaxSeg; ++i)
+            if (i < args.nseg && (!args.seg[i].expert || __ldg(args.seg[i].expert) >= 0)) idle = false;
+        if (idle) {
+            if (warp < kConsumers) {
+                const int n_rows = (jv.t_end - jv.t_begin) * kTileRows;
+                for (int idx = threadIdx.x; idx < n_rows; idx += kConsumers * 32) {
+                    const int tile = jv.t_begin + idx / kTileRows;
+                    const int sg = seg_index(s_tile0, args.nseg, tile);
+                    const GemvSeg& g = s_seg[sg];
+                    const int row = (tile - s_tile0[sg]) * kTileRows + idx % kTileRows;
+                    if (row >= g.rows) continue;
+                    for (int t = 0; t < args.T; ++t) store_out(g, row, t, 0.0f);
+                }
+            }
+            return;
+        }
+    }
+
     if (warp == kConsumers) {   // producer
         if (lane == 0) {
             if (jobs.wait_first) pdl_wait();

@@ -198,6 +198,20 @@ int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* 
 // (e0 <= sel[i] < e0 + n), else -1 (the expert GEMVs write zero rows for -1).
 int fbk_moe_localize(const int32_t* sel, int n_sel, int e0, int n, int32_t* out, cudaStream_t st);
 }
+// A routed expert as this rank's local id (experts [e0, e0 + n) live here),
+// -1 for another rank's: the device kernel and host checks share it.
+__host__ __device__ inline int fb_localize_expert(int e, int e0, int n) { return (e >= e0 && e < e0 + n) ? e - e0 : -1; }
+extern "C" {
+// Expert grouping of a batched MoE step (misc.cu): rows routed to each local
+// expert gathered into grouped rows e T + j, per-chunk expert ids for GEMV
+// launches of 4 rows, and the weighted combine read back through grp_pos.
+int fbk_moe_group(const int32_t* esel, int T, int K, int nel, int32_t* grp_src, int32_t* grp_pos, int32_t* grp_count,
+                  int32_t* chunk_exp, int nchunk, cudaStream_t st);
+int fbk_moe_gather(const fb::ActQ* src, const fb::ActQ* dst, const int32_t* grp_src, int ksel, int n_rows, int K,
+                   cudaStream_t st);
+int fbk_moe_combine_grouped(float* x, int ldx, const float* eo, const int32_t* grp_pos, const float* wsel, int T, int K,
+                            int E, cudaStream_t st);
+}
 
 // ---------------------------------------------------------------- persistent decode step (step.cu)
 namespace fb {

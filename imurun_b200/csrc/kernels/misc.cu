@@ -281,9 +281,100 @@ __global__ void k_moe_localize(const int32_t* __restrict__ sel, int n_sel, int e
     pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n_sel) {
-        const int e = sel[i];
-        out[i] = (e >= e0 && e < e0 + n) ? e - e0 : -1;
+        out[i] = fb_localize_expert(sel[i], e0, n);
     }
+}
+
+// Expert grouping for batched MoE steps. The rows r = t K + k routed to
+// local expert e (ascending r) take grouped rows e T + j: grp_src[e T + j] =
+// r (-1 past the expert's count), grp_pos[r] = e T + j (-1 for another
+// rank's expert), grp_count[e] = j, chunk_exp[e nchunk + c] = e when rows
+// 4c .. of e are used, else -1 (a GEMV given -1 fetches no weights).
+__global__ void k_moe_group(const int32_t* __restrict__ esel, int T, int K, int nel, int32_t* grp_src,
+                            int32_t* grp_pos, int32_t* grp_count, int32_t* chunk_exp, int nchunk) {
+    pdl_trigger();
+    pdl_wait();
+    const int n = T * K;
+    for (int r = threadIdx.x; r < n; r += blockDim.x)
+        if (esel[r] < 0 || esel[r] >= nel) grp_pos[r] = -1;
+    for (int e = threadIdx.x; e < nel; e += blockDim.x) {
+        int j = 0;
+        for (int r = 0; r < n; ++r)
+            if (esel[r] == e) {
+                grp_src[e * T + j] = r;
+                grp_pos[r] = e * T + j;
+                ++j;
+            }
+        grp_count[e] = j;
+        for (int q = j; q < T; ++q) grp_src[e * T + q] = -1;
+        for (int c = 0; c < nchunk; ++c) chunk_exp[e * nchunk + c] = 4 * c < j ? e : -1;
+    }
+}
+
+// Grouped activation row g <- the int8 activations of token grp_src[g] / ksel
+// (all layouts the planes hold; a zero row for -1).
+__global__ void k_moe_gather(ActQ src, ActQ dst, const int32_t* __restrict__ grp_src, int ksel, int K) {
+    pdl_trigger();
+    pdl_wait();
+    const int g = blockIdx.x;
+    const int r = grp_src[g];
+    const int t = r >= 0 ? r / ksel : -1;
+    auto copy_bytes = [&](const int8_t* s, int8_t* d, int n) {   // n % 16 == 0, both 16-byte aligned
+        for (int i = threadIdx.x; i < n / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(d)[i] = t >= 0 ? reinterpret_cast<const uint4*>(s)[i] : make_uint4(0, 0, 0, 0);
+    };
+    if (src.qk && dst.qk) {
+        copy_bytes(src.qk + (size_t)(t < 0 ? 0 : t) * src.ld, dst.qk + (size_t)g * dst.ld, K);
+        for (int i = threadIdx.x; i < K / 256; i += blockDim.x)
+            dst.dk[(size_t)g * (K / 256) + i] = t >= 0 ? src.dk[(size_t)t * (K / 256) + i] : 0.0f;
+        for (int i = threadIdx.x; i < K / 32; i += blockDim.x)
+            dst.bsk[(size_t)g * (K / 32) + i] = t >= 0 ? src.bsk[(size_t)t * (K / 32) + i] : (int16_t)0;
+    }
+    if (src.q32 && dst.q32) {
+        copy_bytes(src.q32 + (size_t)(t < 0 ? 0 : t) * src.ld, dst.q32 + (size_t)g * dst.ld, K);
+        for (int i = threadIdx.x; i < K / 32; i += blockDim.x) {
+            dst.d32[(size_t)g * (K / 32) + i] = t >= 0 ? src.d32[(size_t)t * (K / 32) + i] : 0.0f;
+            dst.s32[(size_t)g * (K / 32) + i] = t >= 0 ? src.s32[(size_t)t * (K / 32) + i] : 0;
+        }
+    }
+}
+
+// x[t] += sum_k w[t K + k] eo[grp_pos[t K + k]] (zero for another rank's
+// expert), the float steps of k_moe_combine.
+__global__ void k_moe_combine_grouped(float* x, int ldx, const float* __restrict__ eo, const int32_t* __restrict__ grp_pos,
+                                      const float* __restrict__ wsel, int T, int K, int E) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < E; i += gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const int p = grp_pos[t * K + k];
+            acc = __fadd_rn(acc, __fmul_rn(wsel[t * K + k], p >= 0 ? eo[(size_t)p * E + i] : 0.0f));
+        }
+        x[(size_t)t * ldx + i] = __fadd_rn(x[(size_t)t * ldx + i], acc);
+    }
+}
+
+extern "C" int fbk_moe_group(const int32_t* esel, int T, int K, int nel, int32_t* grp_src, int32_t* grp_pos,
+                             int32_t* grp_count, int32_t* chunk_exp, int nchunk, cudaStream_t st) {
+    if (T <= 0 || nel <= 0) return 0;
+    return (int)fbk_launch(k_moe_group, dim3(1), dim3(256), 0, st, esel, T, K, nel, grp_src, grp_pos, grp_count,
+                           chunk_exp, nchunk);
+}
+
+extern "C" int fbk_moe_gather(const ActQ* src, const ActQ* dst, const int32_t* grp_src, int ksel, int n_rows, int K,
+                              cudaStream_t st) {
+    if (n_rows <= 0) return 0;
+    if (K % 256 && src->qk) return (int)cudaErrorInvalidValue;
+    return (int)fbk_launch(k_moe_gather, dim3(n_rows), dim3(128), 0, st, *src, *dst, grp_src, ksel, K);
+}
+
+extern "C" int fbk_moe_combine_grouped(float* x, int ldx, const float* eo, const int32_t* grp_pos, const float* wsel,
+                                       int T, int K, int E, cudaStream_t st) {
+    if (T <= 0) return 0;
+    return (int)fbk_launch(k_moe_combine_grouped, dim3((E + 255) / 256, T), dim3(256), 0, st, x, ldx, eo, grp_pos, wsel,
+                           T, K, E);
 }
 
 extern "C" int fbk_moe_localize(const int32_t* sel, int n_sel, int e0, int n, int32_t* out, cudaStream_t st) {

@@ -156,6 +156,21 @@ struct fish_ctx;
 FISH_API int fbx_layer_probe(struct fish_ctx* ctx, int layer, int pos0, const float* x_in, int n_tok, float* x_out,
                              fbx_layer_probe_out* out);
 
+/* Tensor / expert parallelism: rank `rank` of `world`'s slices, as the
+ * loader takes them under fish_tp_init (host code, no device): out[14] =
+ * head0, heads, kv_head0, kv_heads, q_row0, q_rows, kv_row0, kv_rows
+ * (also attn_output's input slice), ff_row0, ff_rows (also ffn_down's input
+ * slice; dense models), expert0, experts (MoE), vocab_row0, vocab_rows.
+ * -1 when the counts do not split evenly over the ranks or the vocabulary
+ * slice is not whole 8-row tiles. No counterpart in the reference, which
+ * runs on one device. */
+FISH_API int fbx_tp_plan(int n_head, int n_head_kv, int head_dim, int n_ff, int vocab, int n_experts, int rank,
+                         int world, int32_t* out);
+/* The routed experts sel[0..n) as local ids of the rank holding experts
+ * [e0, e0 + n_local), -1 for another rank's (host code; the device step's
+ * mapping). */
+FISH_API int fbx_moe_localize_host(const int32_t* sel, int n, int e0, int n_local, int32_t* out);
+
 /* Tokenizer of a GGUF file without loading its model: host code only, no
  * device needed. It is the tokenizer fish_load sets up for the same file
  * (vocabulary, merges or scores, special tokens, chat template), built from

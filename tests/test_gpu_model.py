@@ -451,6 +451,33 @@ def test_decode_batch_equals_single_decodes(gpu, tiny_gguf):
             m.session_close(t)
 
 
+@pytest.mark.parametrize("n", [2, 5, 16])
+def test_moe_grouped_batch_equals_single_decodes(gpu, synth_dir, n):
+    """Batched MoE decode groups the tokens per expert (inside the step
+    graph: one launch per (expert, 4-row chunk), expert ids read on the
+    device); each session's logits must equal its own single-token decode
+    (one GEMV per token and expert) bit for bit. The prompts' prefill runs
+    the eager grouped path (exact per-expert row counts)."""
+    from imurun_b200 import synth
+    from imurun_b200.native import Model
+    path = synth.cached(synth.preset("mixtral", layers=2, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=2), synth_dir)
+    rng = np.random.default_rng(40 + n)
+    prompts = [rng.integers(3, 32000, 9 + 2 * i).astype(np.int32) for i in range(n)]
+    nxt = rng.integers(3, 32000, n).astype(np.int32)
+    with Model(path, 1024) as m:
+        ss = [m.session_open() for _ in prompts]
+        for s, p in zip(ss, prompts):
+            m.session_prefill(s, p)
+        am, lg = m.decode_batch(ss, nxt, logits=True)
+        for i, (s, p) in enumerate(zip(ss, prompts)):
+            t = m.session_open()
+            m.session_prefill(t, p)
+            am1, lg1 = m.decode_batch([t], nxt[i:i + 1], logits=True)
+            assert np.array_equal(lg1[0], lg[i]), i
+            assert am1[0] == am[i]
+            m.session_close(t)
+
+
 @pytest.mark.parametrize("kv_f32", [0, 1])
 def test_persistent_step_matches_graph_path(gpu, synth_dir, monkeypatch, kv_f32):
     """The persistent decode kernel (k_step) against the graph path on one

@@ -5,6 +5,8 @@ the max-over-ranks timing and the barrier. No GPU and no NCCL are touched."""
 from __future__ import annotations
 
 import json
+
+import numpy as np
 import os
 import socket
 import subprocess
@@ -59,3 +61,105 @@ def test_rank_device_choice_without_visible_list():
     env.pop("CUDA_VISIBLE_DEVICES", None)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().splitlines()[-1] == "1", r.stdout + r.stderr
+
+
+SHARD_CODE = r"""
+import json, sys
+sys.path.insert(0, {root!r})
+import numpy as np
+import bench
+from imurun_b200 import native
+lib = native.load_library()
+dist = bench.dist_init()
+plans = {{}}
+for name, (H, HKV, D, F, V, NE) in {shapes!r}.items():
+    out = np.zeros(14, np.int32)
+    rc = lib.fbx_tp_plan(H, HKV, D, F, V, NE, bench.RANK, bench.WORLD, out.ctypes.data)
+    plans[name] = [int(rc)] + [int(v) for v in out]
+# expert localisation of one routed batch on this rank
+sel = np.array({sel!r}, np.int32)
+loc = np.zeros(sel.size, np.int32)
+NE = {n_exp}
+n_local = NE // bench.WORLD
+assert lib.fbx_moe_localize_host(sel.ctypes.data, sel.size, bench.RANK * n_local, n_local, loc.ctypes.data) == 0
+objs = [None] * bench.WORLD
+import torch.distributed as tdist
+tdist.all_gather_object(objs, {{"plans": plans, "loc": [int(v) for v in loc]}})
+if bench.RANK == 0:
+    with open({out!r}, "w") as f:
+        json.dump(objs, f)
+dist.destroy_process_group()
+"""
+
+# (n_head, n_head_kv, head_dim, n_ff, vocab, n_experts) of the benchmark configurations
+SHAPES = {"llama8b": (32, 8, 128, 14336, 128256, 0), "llama70b": (64, 8, 128, 28672, 128256, 0),
+          "mixtral": (32, 8, 128, 14336, 32000, 8), "qwen7b": (28, 4, 128, 18944, 152064, 0)}
+
+
+def _run_ranks(world, code, timeout=300):
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES=",".join(str(i) for i in range(world)))
+        procs.append(subprocess.Popen([sys.executable, "-c", code], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT))
+    logs = [p.communicate(timeout=timeout)[0].decode(errors="replace") for p in procs]
+    assert all(p.returncode == 0 for p in procs), "\n".join(logs)
+
+
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_shard_plans_partition_every_config(tmp_path, world):
+    """Each gloo rank computes its own slices with the loader's function
+    (fbx_tp_plan) and its expert localisation (fbx_moe_localize_host); rank 0
+    gathers them. Every slice kind must tile its range exactly once in rank
+    order; vocab slices are whole 8-row tiles; the K-quant input slices of
+    attn_output and ffn_down are whole 256-value blocks (so per-rank integer
+    block sums equal the unsharded ones); every routed expert is local on
+    exactly one rank, with its rank-local index."""
+    out = str(tmp_path / "plans.json")
+    sel = [0, 7, 3, 5, 1, 6, 2, 4, 7, 0, 5, 5]
+    _run_ranks(world, SHARD_CODE.format(root=str(ROOT), shapes=SHAPES, sel=sel, n_exp=8, out=out))
+    res = json.load(open(out))
+    assert len(res) == world
+    for name, (H, HKV, D, F, V, NE) in SHAPES.items():
+        plans = [r["plans"][name] for r in res]
+        if any(p[0] != 0 for p in plans):
+            # only allowed where the counts do not split (kv heads / FFN rows)
+            assert HKV % world or (NE == 0 and F % world) or (NE and NE % world), (name, world)
+            continue
+        p = np.array([q[1:] for q in plans])
+        for a, n, total in ((0, 1, H), (2, 3, HKV), (4, 5, H * D), (6, 7, HKV * D), (12, 13, V)):
+            assert p[0, a] == 0 and p[-1, a] + p[-1, n] == total, (name, a)
+            assert all(p[r, a] + p[r, n] == p[r + 1, a] for r in range(world - 1)), (name, a)
+        assert all(v % 8 == 0 for v in p[:, 13]), name
+        if NE:
+            assert p[0, 10] == 0 and p[-1, 10] + p[-1, 11] == NE and (p[:, 9] == 0).all()
+            k_slices = np.concatenate([p[:, 4], p[:, 5]])
+        else:
+            assert p[0, 8] == 0 and p[-1, 8] + p[-1, 9] == F and (p[:, 11] == 0).all()
+            assert all(p[r, 8] + p[r, 9] == p[r + 1, 8] for r in range(world - 1)), name
+            k_slices = np.concatenate([p[:, 4], p[:, 5], p[:, 8], p[:, 9]])
+        # the sharded configurations (70B tensor-parallel, Mixtral expert-
+        # parallel) give whole 256-value input blocks at 2/4/8 ranks; the
+        # Qwen-shaped model (one GPU, replicas) does not at 4 (the loader
+        # refuses that split for its K-quant weights)
+        if name in ("llama70b", "mixtral", "llama8b"):
+            assert all(v % 256 == 0 for v in k_slices), name
+    n_local = 8 // world
+    for i, e in enumerate(sel):
+        owners = [r for r in range(world) if res[r]["loc"][i] >= 0]
+        assert owners == [e // n_local], (i, e, owners)
+        assert res[owners[0]]["loc"][i] == e % n_local
+
+
+def test_shard_plan_rejects_uneven_splits():
+    lib = __import__("imurun_b200.native", fromlist=["x"]).load_library()
+    import numpy as np
+    out = np.zeros(14, np.int32)
+    assert lib.fbx_tp_plan(32, 8, 128, 14336, 128256, 0, 0, 3, out.ctypes.data) == -1   # 8 kv heads over 3
+    assert lib.fbx_tp_plan(32, 8, 128, 14336, 128256, 0, 2, 2, out.ctypes.data) == -1   # rank out of range
+    assert lib.fbx_tp_plan(32, 8, 128, 14336, 128260, 0, 0, 2, out.ctypes.data) == -1   # vocab slice not 8-row tiles
