@@ -29,6 +29,20 @@ Q8ACTK_BYTES = 276    # include/fish/quant.h:65-70
 BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
 
 
+def ref_root():
+    """The reference checkout (test infrastructure): REF_ROOT from the
+    environment, else the default the oracle Makefile names; None if absent."""
+    import os
+    root = os.environ.get("REF_ROOT")
+    if not root:
+        mk = Path(__file__).resolve().parent / "Makefile"
+        for ln in mk.read_text().splitlines():
+            if ln.startswith("REF_ROOT") and "?=" in ln:
+                root = ln.split("?=", 1)[1].strip()
+                break
+    return Path(root) if root and Path(root).exists() else None
+
+
 def row_bytes(t: int, n: int) -> int:
     be, bb = BLOCK[t]
     return n // be * bb

@@ -362,6 +362,70 @@ def test_greedy_generate_device_argmax_matches_host_sampler(gpu, tiny_gguf, pena
     lib.fish_destroy(ctx)
 
 
+def test_chat_turns_stats_and_cancel(gpu, tiny_gguf):
+    """The call sequence IMURUN's client makes for chat (model/fish_native.py:
+    load, model info, chat prompt and token count, fish_generate_chat with a
+    token callback on a worker thread, stats, cancel): two chat turns share
+    their prefix through the prefix cache (cached_tokens > 8 on turn 2, as the
+    reference's test_fish.py:231-249 checks), the stats carry the turn's
+    counts and rates, and fish_cancel from another thread mid-generation ends
+    the loop early with the tokens generated so far."""
+    import ctypes
+    import threading
+    from imurun_b200 import native
+    lib = native.load_library()
+    ctx = lib.fish_create()
+    assert lib.fish_load(ctx, str(tiny_gguf).encode(), 2048) == 0
+    info = native.FishModelInfo()
+    assert lib.fish_model_info_of(ctx, ctypes.byref(info)) == 0 and info.vocab == 32000
+
+    def chat_args(msgs):
+        roles = (ctypes.c_char_p * len(msgs))(*[r.encode() for r, _ in msgs])
+        contents = (ctypes.c_char_p * len(msgs))(*[c.encode() for _, c in msgs])
+        return ctypes.cast(roles, ctypes.c_void_p), ctypes.cast(contents, ctypes.c_void_p), len(msgs)
+
+    msgs = [("system", "be brief t300 t301 t302 t303"), ("user", "hello there t17 t99 t4000 t12 t12")]
+    n_chat = lib.fish_count_chat_tokens(ctx, *chat_args(msgs))
+    assert n_chat > 8
+    chunks = []
+    cb = native.FISH_TOKEN_CB(lambda text, tid, user: chunks.append((ctypes.string_at(text), tid)))
+    n1 = lib.fish_generate_chat(ctx, *chat_args(msgs), 16, 0.0, 40, 0.9, 1.1, cb, None)
+    assert n1 > 0 and len(chunks) > 0
+    st = native.FishStats()
+    lib.fish_get_stats(ctx, ctypes.byref(st))
+    assert st.prompt_tokens == n_chat and st.generated_tokens == n1 and st.cached_tokens == 0
+    assert st.tokens_per_second > 0 and st.prefill_tokens_per_second > 0
+    # turn 2: the history grows; its prefix comes from the cache
+    reply = b"".join(c for c, _ in chunks).decode("utf-8", "replace")
+    msgs2 = msgs + [("assistant", reply), ("user", "and more t5 t6 t7")]
+    n2 = lib.fish_generate_chat(ctx, *chat_args(msgs2), 16, 0.7, 40, 0.9, 1.1, cb, None)
+    assert n2 > 0
+    lib.fish_get_stats(ctx, ctypes.byref(st))
+    assert st.cached_tokens > 8
+    # cancel from another thread while the generating thread is in the loop
+    seen = []
+    started = threading.Event()
+
+    def on_tok(text, tid, user):
+        seen.append(tid)
+        if len(seen) == 5:
+            started.set()
+
+    cb2 = native.FISH_TOKEN_CB(on_tok)
+    res = {}
+    th = threading.Thread(target=lambda: res.setdefault(
+        "n", lib.fish_generate_chat(ctx, *chat_args(msgs2), 1500, 0.7, 40, 0.9, 1.0, cb2, None)))
+    th.start()
+    assert started.wait(60)
+    lib.fish_cancel(ctx)
+    th.join(60)
+    assert not th.is_alive()
+    assert 5 <= res["n"] < 1500, res
+    lib.fish_get_stats(ctx, ctypes.byref(st))
+    assert st.generated_tokens == res["n"]
+    lib.fish_destroy(ctx)
+
+
 class PageModel:
     """CPU model of the engine's page allocator: LIFO free list, refcounts,
     shared full pages on fork, copy-on-write of a shared partial page."""
