@@ -1351,7 +1351,11 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
         }
         if (c.n_experts > 0) {
             const int NE = c.n_experts, K = c.n_experts_per_tok, F = c.n_ff_exp;
-            if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
+            if (L.gate_inp.type == T_F32) {
+                CKP(PC_OTHER, 0, fbk_router_f32(L.gate_inp.d, L.gate_inp.stride, xb_, E, T, E, NE, router_, NE, stream_));
+            } else if (!gemv(L.gate_inp, a, T, router_, NE, nullptr, EPI_STORE, xb_, E, nullptr, err)) {
+                return false;
+            }
             CKP(PC_OTHER, 0, fbk_moe_route(router_, T, NE, K, c.expert_weights_norm ? 1 : 0, sel_, wsel_, stream_));
             // expert parallelism: experts of other ranks map to -1 (zero rows)
             const bool ep = tp_world_ > 1;

@@ -478,10 +478,12 @@ bool make_wmap(CUtensorMap* m, const uint8_t* base, int gb, int n_groups, int n_
 }  // namespace
 
 // Whether the tcgen05 kernel takes a Q4_K call: K a multiple of 256, 16-byte
-// aligned operands (TMA), at least 16 tokens. FISH_NO_TC=1 turns it off.
+// aligned operands (TMA), more than 32 tokens. FISH_NO_TC=1 turns it off.
 extern "C" int fbk_gemm_tc_eligible(const GemvSeg* g, const ActQ* a, int K, int T) {
     static const bool off = getenv("FISH_NO_TC") != nullptr;
-    if (off || g->type != T_Q4_K || K % 256 || K / 256 > tc::kMaxBlocks || T < 16 || g->expert || g->amax) return 0;
+    // up to 32 tokens the mma.sync kernel's narrow tiles (more CTAs on the
+    // weight stream) are faster; the 64-token tensor-memory tiles win above
+    if (off || g->type != T_Q4_K || K % 256 || K / 256 > tc::kMaxBlocks || T <= 32 || g->expert || g->amax) return 0;
     if ((reinterpret_cast<uintptr_t>(g->w) & 15) || (reinterpret_cast<uintptr_t>(a->qk) & 15) || a->ld % 16) return 0;
     return encode_fn() ? 1 : 0;
 }

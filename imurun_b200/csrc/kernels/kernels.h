@@ -202,6 +202,10 @@ int fbk_moe_localize(const int32_t* sel, int n_sel, int e0, int n, int32_t* out,
 // -1 for another rank's: the device kernel and host checks share it.
 __host__ __device__ inline int fb_localize_expert(int e, int e0, int n) { return (e >= e0 && e < e0 + n) ? e - e0 : -1; }
 extern "C" {
+// MoE router logits over F32 router rows: one warp per (token, expert),
+// double accumulation; any token count.
+int fbk_router_f32(const uint8_t* w, size_t ws, const float* x, int ldx, int T, int E, int NE, float* out, int ldo,
+                   cudaStream_t st);
 // Expert grouping of a batched MoE step (misc.cu): rows routed to each local
 // expert gathered into grouped rows e T + j, per-chunk expert ids for GEMV
 // launches of 4 rows, and the weighted combine read back through grp_pos.

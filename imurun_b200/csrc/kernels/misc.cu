@@ -285,6 +285,43 @@ __global__ void k_moe_localize(const int32_t* __restrict__ sel, int n_sel, int e
     }
 }
 
+// MoE router logits: out[t][e] = W_e . x_t for F32 router rows (row stride
+// ws bytes), one warp per (token, expert), products summed in double (the
+// reference's f32 matmul path accumulates in double) in a fixed order: lane
+// strides of 4 values, then a shuffle tree. The same kernel serves every
+// token count, so a token's routing does not depend on the batch.
+__global__ void k_router_f32(const uint8_t* __restrict__ w, size_t ws, const float* __restrict__ x, int ldx, int T,
+                             int E, int NE, float* out, int ldo) {
+    pdl_trigger();
+    pdl_wait();
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wid >= T * NE) return;
+    const int t = wid / NE, e = wid % NE;
+    const float* wr = reinterpret_cast<const float*>(w + (size_t)e * ws);
+    const float* xr = x + (size_t)t * ldx;
+    double s = 0.0;
+    for (int k = 4 * lane; k < E; k += 128) {
+        const float4 a = *reinterpret_cast<const float4*>(wr + k);
+        const float4 b = *reinterpret_cast<const float4*>(xr + k);
+        s += (double)a.x * b.x;
+        s += (double)a.y * b.y;
+        s += (double)a.z * b.z;
+        s += (double)a.w * b.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[(size_t)t * ldo + e] = (float)s;
+}
+
+extern "C" int fbk_router_f32(const uint8_t* w, size_t ws, const float* x, int ldx, int T, int E, int NE, float* out,
+                              int ldo, cudaStream_t st) {
+    if (T <= 0 || NE <= 0) return 0;
+    if (E % 4 || ws % 16 || ldx % 4 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return (int)cudaErrorInvalidValue;
+    const int warps = T * NE;
+    return (int)fbk_launch(k_router_f32, dim3((warps + 7) / 8), dim3(256), 0, st, w, ws, x, ldx, T, E, NE, out, ldo);
+}
+
 // Expert grouping for batched MoE steps. The rows r = t K + k routed to
 // local expert e (ascending r) take grouped rows e T + j: grp_src[e T + j] =
 // r (-1 past the expert's count), grp_pos[r] = e T + j (-1 for another
