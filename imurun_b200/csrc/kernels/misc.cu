@@ -286,10 +286,13 @@ __global__ void k_moe_localize(const int32_t* __restrict__ sel, int n_sel, int e
 }
 
 // MoE router logits: out[t][e] = W_e . x_t for F32 router rows (row stride
-// ws bytes), one warp per (token, expert), products summed in double (the
-// reference's f32 matmul path accumulates in double) in a fixed order: lane
-// strides of 4 values, then a shuffle tree. The same kernel serves every
-// token count, so a token's routing does not depend on the batch.
+// ws bytes), one warp per (token, expert). The reference sums f32 rows in
+// float lanes (quant.cpp:67-80 scalar, quant_x86.cpp:242-251 AVX2), two
+// orders that already differ from each other; here the products are summed
+// in double in a fixed order (lane strides of 4 values, then a shuffle tree),
+// so the logit is the exact dot product to within the final rounding. The
+// same kernel serves every token count: a token's routing does not depend on
+// the batch.
 __global__ void k_router_f32(const uint8_t* __restrict__ w, size_t ws, const float* __restrict__ x, int ldx, int T,
                              int E, int NE, float* out, int ldo) {
     pdl_trigger();

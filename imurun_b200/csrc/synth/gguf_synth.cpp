@@ -198,7 +198,7 @@ struct TensorSpec {
     std::string name;
     std::vector<uint64_t> ne;
     uint32_t type;
-    int fill;          // 0 random normal, 1 constant one
+    int fill;          // 0 random normal, 1 constant one, 2 one plus random normal
     float stddev;
     uint64_t offset = 0;
     uint64_t nbytes = 0;
@@ -322,7 +322,7 @@ extern "C" {
 // 12 = "Q4_K_M" mixture (token_embd Q4_K, output Q6_K, attn_v / ffn_down in
 // Q6_K on even layers and Q4_K on odd ones, every other matrix Q4_K).
 typedef struct fish_synth_config {
-    const char* arch;            // "llama" or "qwen2"
+    const char* arch;            // "llama", "qwen2" or "qwen3"
     int n_layers, n_embd, n_ff, n_head, n_head_kv, vocab, n_ctx_train;
     float eps, freq_base;
     int n_experts, n_experts_per_tok;
@@ -330,11 +330,13 @@ typedef struct fish_synth_config {
     int wtype;
     unsigned long long seed;
     float wstd;                  // weight std (0.02)
-    float router_std;            // MoE router std (1/64 variance -> 0.125)
+    float router_std;            // MoE router std (1/64: logits on a unit-RMS input of width 4096 ~ N(0, 1))
     const char* chat_template;   // tokenizer.chat_template; nullptr or "" writes none
     const char* bpe_pre;         // nullptr / "": SentencePiece dummy vocabulary; else a byte-level BPE
                                  // vocabulary with this tokenizer.ggml.pre name (merges learned from
                                  // a built-in text)
+    int qk_norm;                 // 1: per-head q/k RMSNorm weights (attn_q_norm / attn_k_norm, qwen3),
+                                 // 1 + N(0, 0.1) so they are not the identity
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -367,12 +369,16 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
             add(p + "attn_k.bias", {static_cast<uint64_t>(HKV * D)}, T_F32, 0, wstd);
             add(p + "attn_v.bias", {static_cast<uint64_t>(HKV * D)}, T_F32, 0, wstd);
         }
+        if (c->qk_norm) {
+            add(p + "attn_q_norm.weight", {static_cast<uint64_t>(D)}, T_F32, 2, 0.1f);
+            add(p + "attn_k_norm.weight", {static_cast<uint64_t>(D)}, T_F32, 2, 0.1f);
+        }
         add(p + "attn_output.weight", {static_cast<uint64_t>(H * D), static_cast<uint64_t>(E)}, tm, 0, wstd);
         add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
         if (c->n_experts > 0) {
             const uint64_t NE = static_cast<uint64_t>(c->n_experts);
             add(p + "ffn_gate_inp.weight", {static_cast<uint64_t>(E), NE}, T_F32, 0,
-                c->router_std > 0 ? c->router_std : 0.125f);
+                c->router_std > 0 ? c->router_std : 0.015625f);
             add(p + "ffn_gate_exps.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F), NE}, tm, 0, wstd);
             add(p + "ffn_up_exps.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F), NE}, tm, 0, wstd);
             add(p + "ffn_down_exps.weight", {static_cast<uint64_t>(F), static_cast<uint64_t>(E), NE}, tv, 0, wstd);
@@ -497,6 +503,8 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
                 const uint64_t nb = std::min(chunk, n_blocks - b0);
                 if (t.fill == 1) std::fill(vals.begin(), vals.begin() + static_cast<long>(nb * be), 1.0f);
                 else normals(seed, b0 * be, static_cast<size_t>(nb * be), t.stddev, vals.data());
+                if (t.fill == 2)
+                    for (uint64_t i = 0; i < nb * be; ++i) vals[static_cast<size_t>(i)] += 1.0f;
                 for (uint64_t b = 0; b < nb; ++b) {
                     uint8_t* o = data.data() + (b0 + b) * bb;
                     const float* x = vals.data() + b * be;

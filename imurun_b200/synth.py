@@ -14,6 +14,9 @@ Presets (shapes from the benchmark configurations):
             expert FFN 14336, vocab 32000, theta 1e6, Q4_K_M mixture
   llama70b  Llama-3-70B shape: 80 layers, 8192, 64/8 heads, FFN 28672,
             vocab 128256, theta 5e5, Q4_K_M mixture
+  qwen3     Qwen3-style layers (not a benchmark config): 4 layers, 1024,
+            16/8 heads, per-head q/k RMSNorm, no qkv bias, FFN 3072,
+            vocab 32000, theta 1e6, Q4_K_M mixture
 
 `layers=` truncates a preset (same widths, fewer blocks) for parity runs.
 """
@@ -46,9 +49,10 @@ class SynthConfig:
     wtype: int = 8          # 8 = all Q8_0, 12 = Q4_K_M mixture
     seed: int = 1234
     wstd: float = 0.02
-    router_std: float = 0.125
+    router_std: float = 0.015625   # 1/64: router logits on a unit-RMS 4096-wide input ~ N(0, 1)
     chat_template: str = ""   # written as tokenizer.chat_template when not empty
     bpe_pre: str = ""         # non-empty: byte-level BPE vocabulary with this tokenizer.ggml.pre name
+    qk_norm: int = 0          # 1: per-head q/k RMSNorm weights (qwen3)
 
 
 PRESETS = {
@@ -58,6 +62,9 @@ PRESETS = {
     "qwen7b": SynthConfig(arch="qwen2", n_layers=28, n_embd=3584, n_ff=18944, n_head=28,
                           n_head_kv=4, vocab=152064, freq_base=1000000.0, eps=1e-6,
                           qkv_bias=1, wtype=12, n_ctx_train=32768),
+    # Qwen3-shaped (not a benchmark config): per-head q/k RMSNorm, no qkv bias
+    "qwen3": SynthConfig(arch="qwen3", n_layers=4, n_embd=1024, n_ff=3072, n_head=16, n_head_kv=8,
+                         vocab=32000, freq_base=1000000.0, eps=1e-6, qk_norm=1, wtype=12),
     "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
                            vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
                            wtype=12, n_ctx_train=32768),
@@ -78,6 +85,7 @@ class _CConfig(ctypes.Structure):
         ("seed", ctypes.c_ulonglong), ("wstd", ctypes.c_float), ("router_std", ctypes.c_float),
         ("chat_template", ctypes.c_char_p),
         ("bpe_pre", ctypes.c_char_p),
+        ("qk_norm", ctypes.c_int),
     ]
 
 
@@ -99,7 +107,7 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
     c = _CConfig(cfg.arch.encode(), cfg.n_layers, cfg.n_embd, cfg.n_ff, cfg.n_head, cfg.n_head_kv,
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
-                 cfg.chat_template.encode(), cfg.bpe_pre.encode())
+                 cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm)
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

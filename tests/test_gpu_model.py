@@ -252,6 +252,21 @@ def test_qwen_shape_bias_neox_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
     assert compare_steps(g, o, "qwen-1L") >= 0.9
 
 
+def test_qwen3_qk_norm_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
+    """qwen3 architecture: per-head q/k RMSNorm (non-unit weights) before
+    NeoX RoPE, no qkv bias, 2 layers (model.cpp:1714-1722 of the reference)."""
+    from imurun_b200 import synth
+    from imurun_b200.native import Model
+    path = synth.cached(synth.preset("qwen3", layers=2), synth_dir)
+    monkeypatch.setenv("FISH_KV_F32", "1")
+    ids = np.random.default_rng(11).integers(3, 32000, 14).astype(np.int32)
+    with Model(path, 1024) as m:
+        g = run_teacher_forced(m, ids, 10, 4)
+    om = oracle.load(path, 1024)
+    o = oracle_teacher_forced(om, ids, 10, 4)
+    assert compare_steps(g, o, "qwen3-2L") >= 0.9
+
+
 def test_mixtral_shape_moe_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
     """8 experts, top-2 softmax router, renormalised weights, 1 layer."""
     from imurun_b200 import synth

@@ -153,6 +153,22 @@ def test_engine_noise_floor_llama8b_two_layers(oracle, reference, synth_dir):
     assert 0.25 <= min(fr) and max(fr) <= 0.6
 
 
+def test_live_reference_qwen3_qk_norm(oracle, reference, synth_dir):
+    """The qwen3 layers (per-head q/k RMSNorm with non-unit weights, NeoX
+    RoPE, no qkv bias): the restatement against the reference built here,
+    held to the CPU-vs-CPU floor (max |dlogit| <= 3% of max |logit|)."""
+    from imurun_b200 import synth
+    path = synth.cached(synth.preset("qwen3", layers=2), synth_dir)
+    ids = np.random.default_rng(12).integers(3, 32000, 20).astype(np.int32)
+    rm, om = reference.load(path, 1024), oracle.load(path, 1024)
+    qn = om.tensor_f32("blk.1.attn_q_norm.weight")
+    assert qn is not None and qn.shape == (64,) and np.abs(qn - 1).max() > 0.1
+    a = [rm.forward(ids[:16], 0)] + [rm.forward(ids[s:s + 1], s) for s in range(16, 20)]
+    b = [om.forward(ids[:16], 0)] + [om.forward(ids[s:s + 1], s) for s in range(16, 20)]
+    for x, y in zip(a, b):
+        assert np.abs(x - y).max() <= 0.03 * np.abs(x).max()
+
+
 @pytest.mark.parametrize("n_tok", [1, 5])
 def test_live_reference_attention(oracle, reference, n_tok):
     rng = np.random.default_rng(n_tok)

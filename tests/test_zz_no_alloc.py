@@ -98,3 +98,39 @@ def test_static_rejects_oversize(env):
     assert lib.fbx_attention_static(p, p, p, 0, 8192, 64, 8, 128, 7936, 256, p, None) == -1
     # misaligned pointer
     assert lib.fbx_attention_static(p + 4, p, p, 0, 1, 8, 8, 64, 0, 1, p, None) == -1
+
+
+def test_static_allocates_nothing(env):
+    """After the first call (which resolves the static scratch's address),
+    calls of every shape leave the device's free memory and torch's
+    reservation unchanged: the entry point allocates nothing."""
+    lib, torch = env
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream(dev)
+    bufs = []
+    for T, pos0, H, HKV, D in SHAPES:
+        n_keys = pos0 + T
+        g = torch.Generator(device=dev).manual_seed(T + pos0)
+        q = torch.randn((T, H * D), device=dev, generator=g)
+        k = torch.randn((n_keys, HKV * D), device=dev, generator=g).half()
+        v = torch.randn((n_keys, HKV * D), device=dev, generator=g).half()
+        out = torch.empty((T, H * D), device=dev)
+        bufs.append((q, k, v, out, T, pos0, H, HKV, D))
+
+    def call(b):
+        q, k, v, out, T, pos0, H, HKV, D = b
+        return lib.fbx_attention_static(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, pos0 + T, H, HKV, D, pos0, T,
+                                        out.data_ptr(), stream.cuda_stream)
+
+    assert call(bufs[0]) == 0
+    torch.cuda.synchronize(dev)
+    free0, _ = torch.cuda.mem_get_info(dev)
+    reserved0 = torch.cuda.memory_reserved(dev)
+    for _ in range(10):
+        for b in bufs:
+            assert call(b) == 0
+    torch.cuda.synchronize(dev)
+    free1, _ = torch.cuda.mem_get_info(dev)
+    assert free1 == free0, (free0, free1)
+    assert torch.cuda.memory_reserved(dev) == reserved0
+    assert all(bool(torch.isfinite(b[3]).all()) for b in bufs)
