@@ -174,7 +174,7 @@ Engine::~Engine() {
     cudaFree(warena_);
     cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
     cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
-    cudaFree(act_mem_); cudaFree(att_scratch_);
+    cudaFree(act_mem_); cudaFree(att_scratch_); cudaFree(dec_part_); cudaFree(gemm_part_);
     cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_); cudaFree(amax_keys_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
@@ -647,6 +647,12 @@ bool Engine::alloc_buffers(std::string* err) {
     att_chunk_ = 64;
     att_scratch_floats_ = fbk_attention_scratch_floats(att_chunk_, c.n_head, c.head_dim, c.n_ctx);
     CK(cudaMalloc(&att_scratch_, sizeof(float) * att_scratch_floats_));
+    // rank partials of batched decode attention (every token of a full batch)
+    dec_part_floats_ = fbk_attention_decode_part_floats(kMaxBatch, c.n_head, c.n_head_kv, c.head_dim);
+    CK(cudaMalloc(&dec_part_, sizeof(float) * dec_part_floats_));
+    // K-split partial values of the tensor-core GEMM on narrow matrices
+    gemm_part_floats_ = (size_t)16 << 20;
+    CK(cudaMalloc(&gemm_part_, sizeof(float) * gemm_part_floats_));
     CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
@@ -902,6 +908,8 @@ bool Engine::gemv_group(const DevW* const* ws, float* const* ys, const int* ldys
             s.expert_bytes = ws[i]->expert_bytes;
             bytes += gemv_bytes(*ws[i], nt);
         }
+        g.part = gemm_part_;
+        g.part_floats = gemm_part_floats_;
         if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, bytes, fbk_gemm(&g, stream_));
         else CKP(PC_GEMV, bytes, fbk_gemv(&g, stream_));
     }
@@ -947,6 +955,8 @@ bool Engine::gemv(const DevW& w, const ActQ& a, int T, float* y, int ldy, const 
         s.expert_bytes = w.expert_bytes;
         s.amax = keys ? keys + t0 : nullptr;
         s.key_row0 = keys ? cfg_.out_row0 : 0;   // argmax keys carry global vocab rows
+        g.part = gemm_part_;
+        g.part_floats = gemm_part_floats_;
         if (nt >= 16 && fbk_gemm_eligible(&g)) CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemm(&g, stream_));
         else CKP(PC_GEMV, gemv_bytes(w, nt), fbk_gemv(&g, stream_));
     }
@@ -1306,7 +1316,8 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
         }
         if (distinct && !no_fuse_) {
             CKP(PC_ATTN, 0, fbk_attention_decode(q_, Q, k_, v_, KV, T, H, HKV, D, scale, c.rot_dim, c.neox ? 1 : 0,
-                                                 rope_cos_, rope_sin_, kv, li, attn_, Q, stream_));
+                                                 rope_cos_, rope_sin_, kv, li, attn_, Q, dec_part_, dec_part_floats_,
+                                                 stream_));
         } else {
         CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
                                         rope_sin_, kv, li, stream_));

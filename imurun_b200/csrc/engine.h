@@ -282,6 +282,10 @@ private:
     int8_t* act_mem_ = nullptr;
     float* att_scratch_ = nullptr;
     size_t att_scratch_floats_ = 0;
+    float* dec_part_ = nullptr;   // batched decode attention: rank partials
+    size_t dec_part_floats_ = 0;
+    float* gemm_part_ = nullptr;  // tensor-core GEMM: K-split unit values
+    size_t gemm_part_floats_ = 0;
     int att_chunk_ = 32;
     int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;
     int32_t *greedy_out_ = nullptr, *greedy_step_ = nullptr;

@@ -143,6 +143,10 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
     TRY(dy.alloc(sizeof(float) * T * n_out));
     TRY(da.make(T + 8, n_in));
     TRY(cudaMemcpy(dx.p, x, sizeof(float) * T * n_in, cudaMemcpyHostToDevice));
+    // scratch for the tensor-core kernel's K split (half-group units)
+    DevBuf dpart;
+    const size_t part_floats = (size_t)((n_in / 256 + 3) / 4 + 1) * T * n_out;
+    TRY(dpart.alloc(sizeof(float) * part_floats));
     const bool quant = type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K;
     if (quant) TRY(fbk_quantize_rows(dx.as<float>(), n_in, T, n_in, &da.a, type == T_Q8_0, type != T_Q8_0, nullptr));
     // T >= 16 quantised rows go to the tensor-core kernel in one launch,
@@ -181,6 +185,8 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
         g.seg[0].y = dy.as<float>() + (size_t)t0 * n_out;
         g.seg[0].ldy = n_out;
         g.seg[0].epi = EPI_STORE;
+        g.part = dpart.as<float>();
+        g.part_floats = part_floats;
         if (fbk_gemm_eligible(&g)) TRY(fbk_gemm(&g, nullptr));
         else TRY(fbk_gemv(&g, nullptr));
     }
@@ -224,6 +230,10 @@ int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_p
     g.seg[0].y = dy.as<float>();
     g.seg[0].ldy = n_out;
     g.seg[0].epi = EPI_STORE;
+    DevBuf dpart;
+    g.part_floats = (size_t)((n_in / 256 + 3) / 4 + 1) * T * n_out;
+    TRY(dpart.alloc(sizeof(float) * g.part_floats));
+    g.part = dpart.as<float>();
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
@@ -426,7 +436,7 @@ int fbx_attention_decode(const float* q, const float* k_cache, const float* v_ca
     TRY(cudaMemcpy(ds.p, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice));
     TRY(fbk_attention_decode(dq.as<float>(), H * D, dk.as<float>(), dv.as<float>(), HKV * D, 1, H, HKV, D,
                              1.0f / std::sqrt((float)D), rot_dim, neox, dc.as<float>(), ds.as<float>(), tp.kv, 0,
-                             dout.as<float>(), H * D, nullptr));
+                             dout.as<float>(), H * D, nullptr, 0, nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(out, dout.p, sizeof(float) * H * D, cudaMemcpyDeviceToHost));
     if (k_stored || v_stored) {

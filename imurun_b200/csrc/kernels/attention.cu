@@ -641,6 +641,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
 // conflicts.
 constexpr int kTcKeys = 64;
 constexpr int kTcWarps = 4;
+// floats of one rank partial: max[8], sum[8], O[G][D]
+__host__ __device__ inline int dec_part_floats(int G, int D) { return 16 + G * D; }
 constexpr int kTcRs = kMaxD + 8;   // padded row stride (halves) for D = 128; D = 64 uses 72
 
 struct TcSmem {
@@ -689,18 +691,24 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int D>
+// GM (batched decode): the same C key ranks, launched as independent CTAs
+// (x = rank) instead of one cluster, each writing its partial (max, sum,
+// unnormalised O per head) to part[(t * HKV + hk) * C + r]; k_attn_decode_merge
+// then merges the C partials with the cluster merge's arithmetic and order, so
+// a token's output has the same bits on either path. Clusters of 16 CTAs are
+// placed about one per GPC at a time, which serialises large batches.
+template <int D, bool GM>
 __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const float* __restrict__ q, int ldq, const float* __restrict__ knew, const float* __restrict__ vnew, int ldkv,
     int H, int HKV, float scale, int rot, int neox, const float* __restrict__ rcos, const float* __restrict__ rsin,
-    KvView kv, int layer, float* __restrict__ out, int ldo) {
+    KvView kv, int layer, float* __restrict__ out, int ldo, float* __restrict__ part) {
     using L = TcSmem;
     constexpr int RS = D + 8;        // padded row stride (halves)
     constexpr int KS = D / 16;       // k-steps of q.k, m-tiles of p.V
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
-    cg::cluster_group cluster = cg::this_cluster();
-    const int C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
+    const int C = GM ? (int)gridDim.x : (int)cg::this_cluster().num_blocks();
+    const int r = GM ? (int)blockIdx.x : (int)cg::this_cluster().block_rank();
     pdl_trigger();
     const unsigned long long t_kernel = gtimer();
     const bool tr = tracing() && !tracing_all() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
@@ -1006,6 +1014,15 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
             if (d == 0) { cm[g] = M; cl[g] = Ls; }
         }
     }
+    if constexpr (GM) {
+        __syncthreads();
+        float* pp = part + ((size_t)(t * HKV + hk) * C + r) * dec_part_floats(G, D);
+        if (tid < G) { pp[tid] = cm[tid]; pp[8 + tid] = cl[tid]; }
+        for (int idx = tid; idx < G * D; idx += 32 * kTcWarps) pp[16 + idx] = co[(idx / D) * kMaxD + idx % D];
+        trace_cta(tcb, 2, TR_ATTN, EV_C_END);
+        return;
+    }
+    cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     if (tr && tid == 0) trace_ev(TR_ATTN, 7, s_tseq);
     // merge the C partials through distributed shared memory
@@ -1038,6 +1055,44 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     cluster.sync();
     if (tr && tid == 0) trace_ev(TR_ATTN, EV_END, s_tseq);
     trace_cta(tcb, 2, TR_ATTN, EV_C_END);
+}
+
+// The C rank partials of one (token, kv head) written by k_attn_decode_tc<D,
+// true>, merged as the cluster kernel merges them through distributed shared
+// memory (same loops, same order, same roundings).
+__global__ void __launch_bounds__(256) k_attn_decode_merge(const float* __restrict__ part, int C, int G, int D, int HKV,
+                                                           float* __restrict__ out, int ldo) {
+    pdl_trigger();
+    pdl_wait();
+    const int hk = blockIdx.x, t = blockIdx.y;
+    const int pf = dec_part_floats(G, D);
+    const float* pp = part + (size_t)(t * HKV + hk) * C * pf;
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D, d = idx % D;
+        float mv[16], lv[16], ov[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C) {
+                mv[rr] = pp[(size_t)rr * pf + g];
+                lv[rr] = pp[(size_t)rr * pf + 8 + g];
+                ov[rr] = pp[(size_t)rr * pf + 16 + idx];
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr)
+            if (rr < C) M = fmaxf(M, mv[rr]);
+        float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+            if (rr < C && mv[rr] != -INFINITY) {
+                const float w = expf(mv[rr] - M);
+                Ls += lv[rr] * w;
+                O += ov[rr] * w;
+            }
+        }
+        out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+    }
 }
 
 }  // namespace fb
@@ -1155,36 +1210,47 @@ static int launch_decode(const float* q, int ldq, const float* k, const float* v
                                    layer, out, ldo);
 }
 
-// Tensor-core decode attention for fp16 caches; cluster size as for the f32 kernel.
+// Tensor-core decode attention for fp16 caches; cluster size as for the f32
+// kernel. With part (batched decode) the ranks run as independent CTAs and a
+// merge launch follows.
+static int tc_cluster_size() {
+    const char* ev = getenv("FISH_ATTN_CLUSTER");
+    const int want = ev ? atoi(ev) : 16;
+    return (want == 1 || want == 2 || want == 4 || want == 8) ? want : 16;
+}
+
 template <int D>
 static int launch_decode_tc(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV,
                             float scale, int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer,
-                            float* out, int ldo, cudaStream_t st) {
+                            float* out, int ldo, float* part, cudaStream_t st) {
     static int cluster = 0;
     if (!cluster) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_decode_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode_tc<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)TcSmem::bytes);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_decode_tc<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_decode_tc<D, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_decode_tc<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)TcSmem::bytes);
         if (e != cudaSuccess) return (int)e;
-        const char* ev = getenv("FISH_ATTN_CLUSTER");
-        const int want = ev ? atoi(ev) : 16;
-        cluster = (want == 1 || want == 2 || want == 4 || want == 8) ? want : 16;
+        int c = tc_cluster_size();
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(cluster, 1, 1);
+        cfg.gridDim = dim3(c, 1, 1);
         cfg.blockDim = dim3(32 * kTcWarps);
         cfg.dynamicSmemBytes = TcSmem::bytes;
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = cluster;
+        at[0].val.clusterDim.x = c;
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, k_attn_decode_tc<D>, &cfg) != cudaSuccess || n < 1) {
+        if (cudaOccupancyMaxActiveClusters(&n, k_attn_decode_tc<D, false>, &cfg) != cudaSuccess || n < 1) {
             cudaGetLastError();
-            cluster = 8;
+            c = 8;
         }
+        cluster = c;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(cluster, HKV, T);
@@ -1192,32 +1258,52 @@ static int launch_decode_tc(const float* q, int ldq, const float* k, const float
     cfg.dynamicSmemBytes = TcSmem::bytes;
     cfg.stream = st;
     cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = cluster;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    int na = 1;
+    int na = 0;
+    if (!part) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = cluster;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
     if (fbk_pdl_enabled()) {
-        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[1].val.programmaticStreamSerializationAllowed = 1;
-        na = 2;
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
     }
     cfg.attrs = at;
     cfg.numAttrs = na;
-    return (int)cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox, rcos, rsin, kv,
-                                   layer, out, ldo);
+    if (!part)
+        return (int)cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D, false>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox,
+                                       rcos, rsin, kv, layer, out, ldo, (float*)nullptr);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D, true>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox,
+                                       rcos, rsin, kv, layer, out, ldo, part);
+    if (e != cudaSuccess) return (int)e;
+    return (int)fbk_launch(k_attn_decode_merge, dim3(HKV, T), dim3(256), 0, st, (const float*)part, cluster, H / HKV,
+                           D, HKV, out, ldo);
+}
+
+// Floats of the rank-partial scratch a batched decode of T tokens needs.
+extern "C" size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D) {
+    return (size_t)T * HKV * 16 * dec_part_floats(H / HKV, D);
 }
 
 extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H,
                                     int HKV, int D, float scale, int rot, int neox, const float* rcos, const float* rsin,
-                                    KvView kv, int layer, float* out, int ldo, cudaStream_t st) {
+                                    KvView kv, int layer, float* out, int ldo, float* part, size_t part_floats,
+                                    cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
     if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
     static const bool tc_off = getenv("FISH_ATTN_SIMT") != nullptr;
+    static const bool batch_cluster = getenv("FISH_ATTN_CLUSTER_BATCH") != nullptr;
     if (kv.f16 && !tc_off) {
-        if (D == 128) return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
-        return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
+        // batches of tokens: independent rank CTAs + merge (same bits as one cluster per token)
+        float* pp = (T > 1 && !batch_cluster && part && part_floats >= fbk_attention_decode_part_floats(T, H, HKV, D))
+                        ? part : nullptr;
+        if (D == 128)
+            return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp, st);
+        return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp, st);
     }
     if (kv.f16) return launch_decode<__half>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
     return launch_decode<float>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);

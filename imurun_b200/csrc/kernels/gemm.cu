@@ -504,8 +504,12 @@ extern "C" int fbk_gemm(const GemvArgs* a, cudaStream_t st) {
     for (int s = 0; s < a->nseg; ++s) {
         const GemvSeg& g = a->seg[s];
         cudaError_t e;
-        if (g.type == T_Q4_K && fbk_gemm_tc_eligible(&g, &a->act, a->K, a->T))
-            e = (cudaError_t)fbk_gemm_tc(&g, &a->act, a->K, a->T, err, st);
+        // tcgen05 above 32 tokens; at 16-32 tokens only on narrow matrices
+        // (at most 32 row tiles, K split over CTAs), where the mma.sync
+        // kernel's few CTAs each walk all of K
+        const bool narrow = (g.rows + 127) / 128 <= 32 && a->K >= 2048 && a->part;
+        if (g.type == T_Q4_K && (a->T > 32 || narrow) && fbk_gemm_tc_eligible(&g, &a->act, a->K, a->T))
+            e = (cudaError_t)fbk_gemm_tc(&g, &a->act, a->K, a->T, err, a->part, a->part_floats, st);
         else if (g.type == T_Q4_K) e = launch_gemm<T_Q4_K>(g, a->act, a->K, a->T, err, st);
         else if (g.type == T_Q6_K) e = launch_gemm<T_Q6_K>(g, a->act, a->K, a->T, err, st);
         else e = launch_gemm<T_Q8_0>(g, a->act, a->K, a->T, err, st);

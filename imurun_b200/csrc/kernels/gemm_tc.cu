@@ -39,6 +39,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -164,6 +165,12 @@ struct TcArgs {
     const float* dk;     // [T][K/256] activation scales
     int K, T, nsteps, n_full;   // nsteps = K / 256; n_full = blocks in whole 2048-value groups
     int* err;
+    // K split (narrow matrices): CTA z takes the half-group units (4 blocks)
+    // [z U, (z + 1) U) and writes each unit's tree value to
+    // part[(unit * T + t) * rows + row]; k_gemm_unit_reduce finishes the rows.
+    // U = 0: one CTA per (row tile, token tile) over all of K.
+    int units_per_cta;
+    float* part;
 };
 
 __global__ void __launch_bounds__(tc::kThreads, 1)
@@ -177,7 +184,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     volatile int* s_abort = reinterpret_cast<volatile int*>(sm + kBarOff + 8 * B_COUNT + 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * BN, row0 = blockIdx.y * BM;
-    const int nsteps = args.nsteps;
+    const bool split = args.units_per_cta > 0;
+    // this CTA's blocks [sb0, sb0 + nsteps) of the row (local step s = block sb0 + s)
+    const int sb0 = split ? 4 * (int)blockIdx.z * args.units_per_cta : 0;
+    const int nsteps = split ? min(args.nsteps - sb0, 4 * args.units_per_cta) : args.nsteps;
     pdl_trigger();
 
     if (threadIdx.x == 0) {
@@ -210,11 +220,12 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                 const int st = s % NS;
                 if (s >= NS && !mbar_wait(&bar[B_EMPTY + st], (uint32_t)(((s / NS) - 1) & 1), s_abort)) break;
                 uint8_t* stage = sm + kRingOff + st * kStage;
+                const int sg = sb0 + s;
                 mbar_expect_tx(&bar[B_FULL + st], (uint32_t)kStage);
-                if (s < args.n_full) tma_load_5d(stage, &wmap, 0, s & 7, 0, s >> 3, row0 / 8, &bar[B_FULL + st]);
-                else tma_load_5d(stage, &wtail, 0, s - args.n_full, 0, 0, row0 / 8, &bar[B_FULL + st]);
-                tma_load_2d(stage + kWBytes, &xmap, s * 256, t0, &bar[B_FULL + st]);
-                tma_load_2d(stage + kWBytes + kXHalf, &xmap, s * 256 + 128, t0, &bar[B_FULL + st]);
+                if (sg < args.n_full) tma_load_5d(stage, &wmap, 0, sg & 7, 0, sg >> 3, row0 / 8, &bar[B_FULL + st]);
+                else tma_load_5d(stage, &wtail, 0, sg - args.n_full, 0, 0, row0 / 8, &bar[B_FULL + st]);
+                tma_load_2d(stage + kWBytes, &xmap, sg * 256, t0, &bar[B_FULL + st]);
+                tma_load_2d(stage + kWBytes + kXHalf, &xmap, sg * 256 + 128, t0, &bar[B_FULL + st]);
             }
             if (s < nsteps) {
                 if (args.err) atomicExch(args.err, 4);
@@ -340,8 +351,19 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         float acc[16], pc[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc[i] = pc[i] = 0.0f;
-        // one block's terms (t) into the tree: case bi of the group
-        auto push = [&](int bi, int c, const float (&t)[8]) {
+        // split mode: a finished half-group unit's value for tokens 8c..8c+7
+        auto unit_out = [&](int unit, int c, const float (&v)[8]) {
+            if (!row_ok) return;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int t = t0 + 16 * tq + 8 * c + k;
+                if (t < args.T) args.part[((size_t)unit * args.T + t) * args.g.rows + row] = v[k];
+            }
+        };
+        // one block's terms (t) into the tree: case bi of the group; in split
+        // mode the half-group values ((t0 + t1) + (t2 + t3)) and
+        // ((t4 + t5) + (t6 + t7)) go out at bi = 3 and 7 instead
+        auto push = [&](int bi, int c, const float (&t)[8], int unit) {
             const uint32_t ca = lane_base + (uint32_t)(kPaCol + 16 * tq + 8 * c);
             const uint32_t cb = lane_base + (uint32_t)(kPbCol + 16 * tq + 8 * c);
             float v[8], w[8];
@@ -355,6 +377,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                     for (int k = 0; k < 8; ++k)
                         v[k] = __fadd_rn(__int_as_float(iv[k]), bi == 1 ? t[k] : __fadd_rn(pc[8 * c + k], t[k]));
                     tmem_st8(ca, v);
+                    if (split && bi == 3) unit_out(unit, c, v);
                     break;
                 case 2: case 6:
 #pragma unroll
@@ -369,6 +392,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                     tmem_st8(cb, w);
                     break;
                 default:
+                    if (split) {
+                        tmem_ld8(cb, iw);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) w[k] = __fadd_rn(__int_as_float(iw[k]), __fadd_rn(pc[8 * c + k], t[k]));
+                        unit_out(unit, c, w);
+                        break;
+                    }
                     tmem_ld8(ca, iv);
                     tmem_ld8(cb, iw);
                     tmem_ld_wait();
@@ -380,16 +411,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         };
         bool ok = true;
         for (int s = 0; s < nsteps && ok; ++s) {
-            const int ab = s & 1, bi = s & 7;
+            const int sg = sb0 + s, ab = s & 1, bi = sg & 7;
             // this block's scales, fetched before the wait for its MMAs
             float dx[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int t = t0 + 16 * tq + i;
-                dx[i] = t < args.T ? __ldg(args.dk + (size_t)t * nb + s) : 0.0f;
+                dx[i] = t < args.T ? __ldg(args.dk + (size_t)t * nb + sg) : 0.0f;
             }
             const uint32_t hw =
-                row_ok ? __ldg(reinterpret_cast<const uint32_t*>(args.g.w + block_offset_tm(T_Q4_K, K, row, s))) : 0u;
+                row_ok ? __ldg(reinterpret_cast<const uint32_t*>(args.g.w + block_offset_tm(T_Q4_K, K, row, sg))) : 0u;
             ok = mbar_wait(&bar[B_AFULL + ab], (uint32_t)((s >> 1) & 1), s_abort);
             if (!ok) break;
             tc_fence_after();
@@ -410,13 +441,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                 float t[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) t[k] = q4k_term(dw, dmw, dx[8 * c + k], 8 * d0[k] + d1[k], d2[k]);
-                push(bi, c, t);
+                push(bi, c, t, sg >> 2);
                 // a row's last group may be short: its missing blocks add +0
-                if (s == nsteps - 1) {
+                // (to the end of the group, or of the half-group unit)
+                if (sg == nb - 1) {
                     float z[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) z[k] = 0.0f;
-                    for (int zb = bi + 1; zb < 8; ++zb) push(zb, c, z);
+                    const int zend = split && bi < 4 ? 4 : 8;
+                    for (int zb = bi + 1; zb < zend; ++zb) push(zb, c, z, sg >> 2);
                 }
             }
             tmem_st_wait();
@@ -425,7 +458,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
             if (args.err && lane == 0) atomicExch(args.err, 4);
             *s_abort = 1;
         }
-        if (ok && !*s_abort && row_ok) {
+        if (ok && !*s_abort && row_ok && !split) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int t = t0 + 16 * tq + i;
@@ -439,6 +472,23 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+// The rows of a K-split call: group g = unit 2g + unit 2g + 1 (a missing
+// second half is +0, as the tree's zero pushes give), acc += group in order,
+// then the output step of the unsplit kernel.
+__global__ void __launch_bounds__(256) k_gemm_unit_reduce(GemvSeg g, const float* __restrict__ part, int n_units, int T) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    if (row >= g.rows || t >= T) return;
+    float acc = 0.0f;
+    for (int u = 0; u < n_units; u += 2) {
+        const float h0 = part[((size_t)u * T + t) * g.rows + row];
+        const float h1 = u + 1 < n_units ? part[((size_t)(u + 1) * T + t) * g.rows + row] : 0.0f;
+        acc = __fadd_rn(acc, __fadd_rn(h0, h1));
+    }
+    store_out(g, row, t, acc);
 }
 
 }  // namespace fb
@@ -477,18 +527,18 @@ bool make_wmap(CUtensorMap* m, const uint8_t* base, int gb, int n_groups, int n_
 
 }  // namespace
 
-// Whether the tcgen05 kernel takes a Q4_K call: K a multiple of 256, 16-byte
-// aligned operands (TMA), more than 32 tokens. FISH_NO_TC=1 turns it off.
+// Whether the tcgen05 kernel can take a Q4_K call: K a multiple of 256,
+// 16-byte aligned operands (TMA), at least 16 tokens. FISH_NO_TC=1 turns it
+// off. fbk_gemm routes 16-32 tokens here only for narrow matrices (K split).
 extern "C" int fbk_gemm_tc_eligible(const GemvSeg* g, const ActQ* a, int K, int T) {
     static const bool off = getenv("FISH_NO_TC") != nullptr;
-    // up to 32 tokens the mma.sync kernel's narrow tiles (more CTAs on the
-    // weight stream) are faster; the 64-token tensor-memory tiles win above
-    if (off || g->type != T_Q4_K || K % 256 || K / 256 > tc::kMaxBlocks || T <= 32 || g->expert || g->amax) return 0;
+    if (off || g->type != T_Q4_K || K % 256 || K / 256 > tc::kMaxBlocks || T < 16 || g->expert || g->amax) return 0;
     if ((reinterpret_cast<uintptr_t>(g->w) & 15) || (reinterpret_cast<uintptr_t>(a->qk) & 15) || a->ld % 16) return 0;
     return encode_fn() ? 1 : 0;
 }
 
-extern "C" int fbk_gemm_tc(const GemvSeg* g, const ActQ* a, int K, int T, int* err, cudaStream_t st) {
+extern "C" int fbk_gemm_tc(const GemvSeg* g, const ActQ* a, int K, int T, int* err, float* part, size_t part_floats,
+                           cudaStream_t st) {
     if (!fbk_gemm_tc_eligible(g, a, K, T)) return (int)cudaErrorInvalidValue;
     const int nb = K / 256, n_full_groups = nb / 8, tail = nb % 8;
     const int n_tiles = (g->rows + kTileRows - 1) / kTileRows;
@@ -525,8 +575,32 @@ extern "C" int fbk_gemm_tc(const GemvSeg* g, const ActQ* a, int K, int T, int* e
     args.nsteps = nb;
     args.n_full = 8 * n_full_groups;
     args.err = err;
+    args.units_per_cta = 0;
+    args.part = part;
     // token tiles fastest: the CTAs that share a 128-row weight tile run
     // together, so its bytes come from HBM once and from L2 after
-    const dim3 grid((T + tc::BN - 1) / tc::BN, (g->rows + tc::BM - 1) / tc::BM);
-    return (int)fbk_launch(k_gemm_tc_q4k, grid, dim3(tc::kThreads), (size_t)tc::kSmem, st, wmap, wtail, xmap, args);
+    dim3 grid((T + tc::BN - 1) / tc::BN, (g->rows + tc::BM - 1) / tc::BM);
+    // fewer tiles than SMs (one CTA fits an SM): split K in half-group units
+    // so about one CTA per SM streams the matrix
+    static const int sms = [] {
+        int dev = 0, n = 148;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+        return n;
+    }();
+    static const bool no_split = getenv("FISH_TC_NO_SPLIT") != nullptr;
+    const int tiles = (int)(grid.x * grid.y), n_units = (nb + 3) / 4;
+    if (part && !no_split && tiles < sms && n_units > 1 && (size_t)n_units * T * g->rows <= part_floats) {
+        const int want = std::min(n_units, (sms + tiles - 1) / tiles);   // CTAs per tile
+        const int U = (n_units + want - 1) / want;
+        const int splits = (n_units + U - 1) / U;
+        if (splits > 1) {
+            args.units_per_cta = U;
+            grid.z = splits;
+        }
+    }
+    cudaError_t e = fbk_launch(k_gemm_tc_q4k, grid, dim3(tc::kThreads), (size_t)tc::kSmem, st, wmap, wtail, xmap, args);
+    if (e != cudaSuccess || !args.units_per_cta) return (int)e;
+    return (int)fbk_launch(k_gemm_unit_reduce, dim3((g->rows + 255) / 256, T), dim3(256), 0, st, *g, (const float*)part,
+                           n_units, T);
 }

@@ -77,6 +77,8 @@ struct GemvArgs {
     uint8_t* img_dump;      // debug (nullable, streamed kernel): CTA 0 copies its activation image here
                             // after the prologue: 16-byte header (xk bytes, x32 bytes, T, n256 as int32)
                             // then T * (xk + x32) bytes laid out as XImage (stream_common.cuh)
+    float* part;            // tensor-core GEMM scratch for K-split calls (nullable: no split)
+    size_t part_floats;
 };
 
 }  // namespace fb
@@ -98,9 +100,13 @@ int fbk_gemv_chunk(const fb::GemvArgs* args);
 // (FISH_NO_GEMM turns the path off).
 int fbk_gemm_eligible(const fb::GemvArgs* args);
 // Q4_K segments on the tcgen05 kernel (gemm_tc.cu): T >= 16, K % 256 == 0,
-// 16-byte aligned operands; fbk_gemm takes it for them when eligible.
+// 16-byte aligned operands; fbk_gemm takes it above 32 tokens, and at 16-32
+// tokens for narrow matrices with K-split scratch.
 int fbk_gemm_tc_eligible(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T);
-int fbk_gemm_tc(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T, int* err, cudaStream_t st);
+// part: scratch for a K split of narrow matrices (n_units * T * rows floats,
+// n_units = ceil(K / 1024)); nullptr or too small runs unsplit.
+int fbk_gemm_tc(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T, int* err, float* part, size_t part_floats,
+                cudaStream_t st);
 int fbk_gemm(const fb::GemvArgs* args, cudaStream_t st);
 // 1 if fbk_gemv runs this call on the streamed kernel (the only one that
 // takes a prologue other than PRO_ACT).
@@ -163,11 +169,15 @@ int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float s
                   float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st);
 // Decode attention for T tokens of T distinct sequences, RoPE and the K/V
 // append fused: q and k/v are the raw projections [T][...]; the new rows are
-// stored at each token's position; out [T][H*D]. Page size 16. One cluster
-// of CTAs per (token, kv head); no scratch.
+// stored at each token's position; out [T][H*D]. Page size 16. One token:
+// one cluster of CTAs per kv head, merged in distributed shared memory. More
+// tokens with part (at least fbk_attention_decode_part_floats): the same key
+// ranks as independent CTAs writing partials to part, then a merge launch;
+// every token's output has the same bits on both paths.
 int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,
                          float scale, int rot, int neox, const float* rope_cos, const float* rope_sin, KvView kv,
-                         int layer, float* out, int ldo, cudaStream_t st);
+                         int layer, float* out, int ldo, float* part, size_t part_floats, cudaStream_t st);
+size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D);
 // Per-head RMSNorm in place (q/k norm), rows [T][n_heads*D].
 int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st);
 // MoE: x[t] += sum_k wsel[t][k] * eo[t][k][:]

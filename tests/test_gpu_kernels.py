@@ -160,17 +160,20 @@ def test_matmul_tall_small_batch(lib, oracle, t, T):
 
 
 @pytest.mark.parametrize("t", [8, 12, 14])
-@pytest.mark.parametrize("n_in", [4096, 3584])
+@pytest.mark.parametrize("n_in", [4096, 3584, 2816, 18944])
 @pytest.mark.parametrize("T", [16, 29, 37, 70])
 def test_matmul_rows_batch_invariant(lib, t, n_in, T):
     """A token's outputs are the same bits whatever the number of tokens in
-    the call: the tensor-core kernel (T = 16: a 16-token tile; 29, 37: one and
-    two 32-token tiles; 70: 64-token tiles) adds each block's float term in
-    the GEMV kernels' order
-    (pairwise over a group's blocks, groups in order, +0 for a short last
-    group: 3584 = 1 full + 1 partial group), so it matches the streamed GEMV
-    (T = 1) exactly. This is what makes a prefix-cache hit reproduce a fresh
-    prefill bit for bit."""
+    the call: the tensor-core kernels (T = 16: a 16-token tile; 29: a
+    32-token tile; 37, 70: the tcgen05 kernel's 64-token tiles for Q4_K) add
+    each block's float term in the GEMV kernels' order (pairwise over a
+    group's blocks, groups in order, +0 for a short last group: 3584 = 1 full
+    + 1 partial group), so they match the streamed GEMV (T = 1) exactly. With
+    200 rows the tcgen05 kernel splits K over CTAs in half-group units
+    (2816: an odd unit count, the last group's second half missing; 18944:
+    19 units) and the reduce adds the halves and the groups in the same
+    order. This is what makes a prefix-cache hit reproduce a fresh prefill
+    bit for bit."""
     rng = np.random.default_rng(7 * t + n_in)
     n_out = 200
     w = rand_rows(t, n_in, n_out, rng)

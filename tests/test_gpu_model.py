@@ -254,7 +254,13 @@ def test_qwen_shape_bias_neox_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
 
 def test_qwen3_qk_norm_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
     """qwen3 architecture: per-head q/k RMSNorm (non-unit weights) before
-    NeoX RoPE, no qkv bias, 2 layers (model.cpp:1714-1722 of the reference)."""
+    NeoX RoPE, no qkv bias, 2 layers (model.cpp:1714-1722 of the reference).
+
+    On this model the two CPU engines (reference vs restatement, same ids and
+    steps) keep 71-75% of logits inside 1e-2 + 1e-3|l| with max |dlogit|
+    1.4-1.6% of max |logit| (test_oracle_pin.py::
+    test_live_reference_qwen3_qk_norm pins it); the GPU is held to that
+    floor: >= 60% inside, max <= 3%, argmax with the margin guard."""
     from imurun_b200 import synth
     from imurun_b200.native import Model
     path = synth.cached(synth.preset("qwen3", layers=2), synth_dir)
@@ -264,7 +270,7 @@ def test_qwen3_qk_norm_vs_oracle(gpu, oracle, synth_dir, monkeypatch):
         g = run_teacher_forced(m, ids, 10, 4)
     om = oracle.load(path, 1024)
     o = oracle_teacher_forced(om, ids, 10, 4)
-    assert compare_steps(g, o, "qwen3-2L") >= 0.9
+    assert compare_steps(g, o, "qwen3-2L", rel_max=0.03) >= 0.6
 
 
 def test_mixtral_shape_moe_vs_oracle(gpu, oracle, synth_dir, monkeypatch):

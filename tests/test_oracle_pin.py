@@ -155,18 +155,22 @@ def test_engine_noise_floor_llama8b_two_layers(oracle, reference, synth_dir):
 
 def test_live_reference_qwen3_qk_norm(oracle, reference, synth_dir):
     """The qwen3 layers (per-head q/k RMSNorm with non-unit weights, NeoX
-    RoPE, no qkv bias): the restatement against the reference built here,
-    held to the CPU-vs-CPU floor (max |dlogit| <= 3% of max |logit|)."""
+    RoPE, no qkv bias): the restatement against the reference built here on
+    the GPU test's ids and steps (prefill 10, 4 decode steps). Measured: 71-75%
+    of logits inside 1e-2 + 1e-3|l| per step, max |dlogit| 1.4-1.6% of max
+    |logit| (int8 rounding flips); held at >= 65% and <= 2.5%."""
     from imurun_b200 import synth
     path = synth.cached(synth.preset("qwen3", layers=2), synth_dir)
-    ids = np.random.default_rng(12).integers(3, 32000, 20).astype(np.int32)
+    ids = np.random.default_rng(11).integers(3, 32000, 14).astype(np.int32)
     rm, om = reference.load(path, 1024), oracle.load(path, 1024)
     qn = om.tensor_f32("blk.1.attn_q_norm.weight")
     assert qn is not None and qn.shape == (64,) and np.abs(qn - 1).max() > 0.1
-    a = [rm.forward(ids[:16], 0)] + [rm.forward(ids[s:s + 1], s) for s in range(16, 20)]
-    b = [om.forward(ids[:16], 0)] + [om.forward(ids[s:s + 1], s) for s in range(16, 20)]
+    a = [rm.forward(ids[:10], 0)] + [rm.forward(ids[s:s + 1], s) for s in range(10, 14)]
+    b = [om.forward(ids[:10], 0)] + [om.forward(ids[s:s + 1], s) for s in range(10, 14)]
     for x, y in zip(a, b):
-        assert np.abs(x - y).max() <= 0.03 * np.abs(x).max()
+        d = np.abs(x - y)
+        assert d.max() <= 0.025 * np.abs(x).max()
+        assert np.mean(d <= 1e-2 + 1e-3 * np.abs(x)) >= 0.65
 
 
 @pytest.mark.parametrize("n_tok", [1, 5])
