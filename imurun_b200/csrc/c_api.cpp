@@ -917,12 +917,12 @@ const char* fish_engine_json(fish_ctx* ctx) {
                   "\"last_decode_device_ms\":%.6f,\"kernel_error\":%d,\"wait_failures\":%d,"
                   "\"step_kernel\":%d,\"step_grid\":%d,\"step_ring_slots\":%d,\"step_slot_bytes\":%d,"
                   "\"step_weight_bytes\":%.0f,\"last_step_ms\":%.6f,\"last_batch_device_ms\":%.6f,"
-                  "\"tp_world\":%d,\"wait_records\":",
+                  "\"last_batch_prefix_blocks\":%d,\"tp_world\":%d,\"wait_records\":",
                   e.device_name().c_str(), e.page_size(), e.free_pages(), (unsigned long long)e.kv_bytes(),
                   (unsigned long long)e.device_weight_bytes(), e.graph_kernels(0), e.graph_kernels(1),
                   (double)e.last_greedy_ms(), kerr, nwr, e.step_ready() ? 1 : 0, e.step_grid(), e.step_stages(),
                   e.step_slot_bytes(), e.step_weight_bytes(), (double)e.last_step_ms(), (double)e.last_batch_ms(),
-                  e.tp_world());
+                  e.last_prefix_blocks(), e.tp_world());
     buf = std::string(b) + recs + ",\"step_unavailable\":\"" + e.step_why() + "\"}";
     return buf.c_str();
 }

@@ -175,6 +175,7 @@ Engine::~Engine() {
     cudaFree(x_); cudaFree(xb_); cudaFree(q_); cudaFree(k_); cudaFree(v_); cudaFree(attn_);
     cudaFree(g_); cudaFree(u_); cudaFree(logits_); cudaFree(router_); cudaFree(eo_); cudaFree(sel_); cudaFree(wsel_);
     cudaFree(act_mem_); cudaFree(att_scratch_); cudaFree(dec_part_); cudaFree(gemm_part_);
+    cudaFree(pre_blocks_); cudaFree(pre_state_);
     cudaFree(ids_); cudaFree(tok_seq_); cudaFree(tok_pos_); cudaFree(argmax_); cudaFree(greedy_out_); cudaFree(greedy_step_); cudaFree(amax_keys_);
     cudaFree(kv_pool_); cudaFree(pt_arena_);
     cudaFree(rope_cos_); cudaFree(rope_sin_); cudaFree(out_norm_);
@@ -653,6 +654,13 @@ bool Engine::alloc_buffers(std::string* err) {
     // K-split partial values of the tensor-core GEMM on narrow matrices
     gemm_part_floats_ = (size_t)16 << 20;
     CK(cudaMalloc(&gemm_part_, sizeof(float) * gemm_part_floats_));
+    // shared-prefix attention of batched decode: the prefix length (set
+    // before each step) and the warps' states, for batches of up to
+    // kPrefixMaxBatch sessions
+    CK(cudaMalloc(&pre_blocks_, sizeof(int32_t)));
+    CK(cudaMemset(pre_blocks_, 0, sizeof(int32_t)));
+    pre_state_floats_ = fbk_attention_prefix_state_floats(kPrefixMaxBatch, c.n_head_kv, c.head_dim);
+    CK(cudaMalloc(&pre_state_, sizeof(float) * pre_state_floats_));
     CK(cudaMalloc(&ids_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_seq_, sizeof(int32_t) * kMaxBatch));
     CK(cudaMalloc(&tok_pos_, sizeof(int32_t) * kMaxBatch));
@@ -662,7 +670,7 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMalloc(&greedy_out_, sizeof(int32_t) * greedy_cap_));
     CK(cudaMalloc(&greedy_step_, sizeof(int32_t)));
     CK(cudaMalloc(&recent_dev_, sizeof(int32_t) * kMaxRecent));
-    CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * (3 * kMaxBatch + kMaxRecent)));
+    CK(cudaMallocHost(&h_pinned_, sizeof(int32_t) * (3 * kMaxBatch + kMaxRecent + 4)));
     // the kernels' shared error flag is allocated on first use; make that use
     // now, so a context's first launches may be inside a graph capture
     if (!fbk_gemv_error_flag()) {
@@ -1317,7 +1325,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
         if (distinct && !no_fuse_) {
             CKP(PC_ATTN, 0, fbk_attention_decode(q_, Q, k_, v_, KV, T, H, HKV, D, scale, c.rot_dim, c.neox ? 1 : 0,
                                                  rope_cos_, rope_sin_, kv, li, attn_, Q, dec_part_, dec_part_floats_,
-                                                 stream_));
+                                                 pre_blocks_, pre_state_, pre_state_floats_, stream_));
         } else {
         CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
                                         rope_sin_, kv, li, stream_));
@@ -1880,6 +1888,28 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
         pos[i] = seqs_[sid].len;
     }
     if (!upload_tokens(ids, sids, pos.data(), n, err)) return false;
+    // the 64-key blocks every session of the batch holds on the same pages,
+    // below every token's own position: attention reads them once for all
+    {
+        int bp = 0;
+        if (n >= 2 && n <= kPrefixMaxBatch) {
+            const std::vector<int>& p0 = seqs_[sids[0]].pages;
+            size_t common = p0.size();
+            for (int i = 1; i < n && common > 0; ++i) {
+                const std::vector<int>& pi = seqs_[sids[i]].pages;
+                size_t j = 0;
+                while (j < common && j < pi.size() && pi[j] == p0[j]) ++j;
+                common = j;
+            }
+            long long lp = (long long)common * kPageSize;
+            for (int i = 0; i < n; ++i) lp = std::min<long long>(lp, pos[i]);
+            bp = (int)std::min<long long>(lp / 64, fbk_attention_prefix_max_blocks());
+        }
+        int32_t* hb = h_pinned_ + 3 * kMaxBatch + kMaxRecent;
+        *hb = bp;
+        last_prefix_blocks_ = bp;
+        CK(cudaMemcpyAsync(pre_blocks_, hb, sizeof(int32_t), cudaMemcpyHostToDevice, stream_));
+    }
     if (use_graphs_) {
         if (!graphs_.count(n) && !capture_graph(n, err)) return false;
         CK(cudaEventRecord(ev0_, stream_));

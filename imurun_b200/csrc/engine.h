@@ -24,6 +24,7 @@ namespace fb {
 
 constexpr int kMaxBatch = 256;   // tokens per forward (reference max_batch_, model.h:292)
 constexpr int kPageSize = 16;    // KV positions per page
+constexpr int kPrefixMaxBatch = 64;   // batched decode: sessions whose shared prefix attention reads once
 
 struct Config {
     std::string arch = "llama";
@@ -180,6 +181,7 @@ public:
     // Device time (CUDA events on the engine stream) of the last greedy run.
     float last_greedy_ms() const { return last_greedy_ms_; }
     float last_batch_ms() const { return last_batch_ms_; }   // device time of the last batched decode step
+    int last_prefix_blocks() const { return last_prefix_blocks_; }   // its shared-prefix 64-key blocks
     // Kernel nodes of the captured step graph for T tokens (0 if none yet).
     int graph_kernels(int T) const {
         auto it = graph_kernels_.find(T);
@@ -286,6 +288,10 @@ private:
     size_t dec_part_floats_ = 0;
     float* gemm_part_ = nullptr;  // tensor-core GEMM: K-split unit values
     size_t gemm_part_floats_ = 0;
+    int32_t* pre_blocks_ = nullptr;   // batched decode: shared-prefix 64-key blocks (set before each step)
+    float* pre_state_ = nullptr;      // shared-prefix attention: warp states
+    size_t pre_state_floats_ = 0;
+    int last_prefix_blocks_ = 0;
     int att_chunk_ = 32;
     int32_t *ids_ = nullptr, *tok_seq_ = nullptr, *tok_pos_ = nullptr, *argmax_ = nullptr;
     int32_t *greedy_out_ = nullptr, *greedy_step_ = nullptr;

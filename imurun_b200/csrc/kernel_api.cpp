@@ -436,7 +436,7 @@ int fbx_attention_decode(const float* q, const float* k_cache, const float* v_ca
     TRY(cudaMemcpy(ds.p, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice));
     TRY(fbk_attention_decode(dq.as<float>(), H * D, dk.as<float>(), dv.as<float>(), HKV * D, 1, H, HKV, D,
                              1.0f / std::sqrt((float)D), rot_dim, neox, dc.as<float>(), ds.as<float>(), tp.kv, 0,
-                             dout.as<float>(), H * D, nullptr, 0, nullptr));
+                             dout.as<float>(), H * D, nullptr, 0, nullptr, nullptr, 0, nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(out, dout.p, sizeof(float) * H * D, cudaMemcpyDeviceToHost));
     if (k_stored || v_stored) {

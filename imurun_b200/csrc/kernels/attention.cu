@@ -691,6 +691,197 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// ---- pieces shared by the decode kernel and the shared-prefix kernel; a
+// token's arithmetic is the same wherever they run, so every path gives it
+// the same bits
+
+// q of one token rotated for its position (cs, sn: the position's table row)
+// into sq[g * kMaxD + d]; threads tid of nt take the pairs in any order
+__device__ __forceinline__ void tc_rotate_q(float* sq, const float* qr, int G, int qstride, int D, int half, int neox,
+                                            const float* cs, const float* sn, int tid, int nt) {
+    for (int idx = tid; idx < G * (D / 2); idx += nt) {
+        const int g = idx / (D / 2), i = idx % (D / 2);
+        const float* hv = qr + (size_t)g * qstride;
+        if (i < half) {
+            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            const float x0 = hv[a], x1 = hv[b];
+            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
+        } else {
+            sq[g * kMaxD + 2 * i] = hv[2 * i];
+            sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
+        }
+    }
+}
+
+// q as the B operand (k = dims, n = heads): lane holds head lane/4, dims
+// 2(lane%4) + {0, 1, 8, 9} of each 16-dim step, as hi and lo halves
+template <int KS>
+__device__ __forceinline__ void tc_q_frags(const float* sq, int G, int lane, uint32_t (&qh)[KS][2], uint32_t (&ql)[KS][2]) {
+    const int gq = lane >> 2, k0 = 2 * (lane & 3);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int d = 16 * ks + k0 + 8 * e;
+            const float x0 = gq < G ? sq[gq * kMaxD + d] : 0.0f, x1 = gq < G ? sq[gq * kMaxD + d + 1] : 0.0f;
+            float h0, l0, h1, l1;
+            split_h(x0, h0, l0);
+            split_h(x1, h1, l1);
+            qh[ks][e] = pack_h2(h0, h1);
+            ql[ks][e] = pack_h2(l0, l1);
+        }
+    }
+}
+
+// One warp's 16 keys [kw, kw + 16) of a 64-key block (K, V: the block's
+// rows at stride D + 8 halves; kb keys valid) into its online softmax state
+// (m_r, l_r for the lane's two heads, O^T fragments acc).
+template <int D>
+__device__ __forceinline__ void tc_warp_block(const __half* K, const __half* V, int kw, int kb, float scale,
+                                              const uint32_t (&qh)[D / 16][2], const uint32_t (&ql)[D / 16][2],
+                                              float (&m_r)[2], float (&l_r)[2], float (&acc)[D / 16][4], __half* pw,
+                                              int lane) {
+    constexpr int RS = D + 8, KS = D / 16;
+    if (kw >= kb) return;
+    const int gq = lane >> 2, k0 = 2 * (lane & 3), h0 = 2 * (lane & 3);
+    const int r_in = (lane & 7) + ((lane >> 3) & 1) * 8, c_in = (lane >> 4) * 8;       // ldmatrix (K rows)
+    const int key_in = (lane & 7) + ((lane >> 4) & 1) * 8, dim_in = ((lane >> 3) & 1) * 8;  // ldmatrix.trans (V)
+    // scores S^T[16 keys][8 heads]: the q hi and lo products in two
+    // independent accumulation chains, added at the end
+    float c[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cl4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, K + (size_t)(kw + r_in) * RS + 16 * ks + c_in);
+        mma16816(c, a, qh[ks][0], qh[ks][1]);
+        mma16816(cl4, a, ql[ks][0], ql[ks][1]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] = __fadd_rn(c[e], cl4[e]);
+    // c0: (key lane/4, head h0), c1: (lane/4, h0+1), c2: (lane/4+8, h0), c3: (lane/4+8, h0+1)
+    const int ka = kw + (lane >> 2), kb2 = ka + 8;
+    float sc[4];
+    sc[0] = ka < kb ? __fmul_rn(c[0], scale) : -INFINITY;
+    sc[1] = ka < kb ? __fmul_rn(c[1], scale) : -INFINITY;
+    sc[2] = kb2 < kb ? __fmul_rn(c[2], scale) : -INFINITY;
+    sc[3] = kb2 < kb ? __fmul_rn(c[3], scale) : -INFINITY;
+    float corr[2], p[4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        float mx = fmaxf(sc[e], sc[e + 2]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(m_r[e], mx);
+        corr[e] = m_r[e] == -INFINITY ? 0.0f : expf(m_r[e] - mn);
+        p[e] = sc[e] == -INFINITY ? 0.0f : expf(sc[e] - mn);
+        p[e + 2] = sc[e + 2] == -INFINITY ? 0.0f : expf(sc[e + 2] - mn);
+        float sum = p[e] + p[e + 2];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        l_r[e] = __fmaf_rn(l_r[e], corr[e], sum);
+        m_r[e] = mn;
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+        acc[mt][0] = __fmul_rn(acc[mt][0], corr[0]);
+        acc[mt][1] = __fmul_rn(acc[mt][1], corr[1]);
+        acc[mt][2] = __fmul_rn(acc[mt][2], corr[0]);
+        acc[mt][3] = __fmul_rn(acc[mt][3], corr[1]);
+    }
+    // P^T as the B operand of p.V (k = keys, n = heads): transpose through shared memory
+    {
+        const int kr = lane >> 2;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int hh = h0 + (e & 1), kk = kr + 8 * (e >> 1);
+            float ph, pl;
+            split_h(p[e], ph, pl);
+            pw[(0 * 8 + hh) * 16 + kk] = __float2half_rn(ph);
+            pw[(1 * 8 + hh) * 16 + kk] = __float2half_rn(pl);
+        }
+    }
+    __syncwarp();
+    const uint32_t pbh0 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0);
+    const uint32_t pbh1 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0 + 8);
+    const uint32_t pbl0 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0);
+    const uint32_t pbl1 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0 + 8);
+    __syncwarp();
+    // O^T[D][8 heads] += V^T[D][16 keys] . P^T[16 keys][8 heads]
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_t(a, V + (size_t)(kw + key_in) * RS + 16 * mt + dim_in);
+        mma16816(acc[mt], a, pbh0, pbh1);
+        mma16816(acc[mt], a, pbl0, pbl1);
+    }
+}
+
+// a warp's state (max, sum, O) into the CTA's per-warp partial arrays
+template <int KS>
+__device__ __forceinline__ void tc_store_warp(float* wm, float* wl, float* wo, int warp, int lane, const float (&m_r)[2],
+                                              const float (&l_r)[2], const float (&acc)[KS][4]) {
+    const int h0 = 2 * (lane & 3);
+    if (lane < 4) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            wm[warp * 8 + h0 + e] = m_r[e];
+            wl[warp * 8 + h0 + e] = l_r[e];
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+        const int d = 16 * mt + (lane >> 2);
+        wo[((size_t)warp * 8 + h0) * kMaxD + d] = acc[mt][0];
+        wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d] = acc[mt][1];
+        wo[((size_t)warp * 8 + h0) * kMaxD + d + 8] = acc[mt][2];
+        wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d + 8] = acc[mt][3];
+    }
+}
+
+// the 4 warps' partials -> the CTA's (cm, cl, co); threads tid of nt
+__device__ __forceinline__ void tc_merge_warps(const float* wm, const float* wl, const float* wo, float* cm, float* cl,
+                                               float* co, int G, int D, int tid, int nt) {
+    for (int idx = tid; idx < G * D; idx += nt) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, wm[w * 8 + g]);
+        float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) {
+            const float mw = wm[w * 8 + g];
+            if (mw == -INFINITY) continue;
+            const float cw = expf(mw - M);
+            Ls = __fmaf_rn(wl[w * 8 + g], cw, Ls);
+            O = __fmaf_rn(wo[((size_t)w * 8 + g) * kMaxD + d], cw, O);
+        }
+        co[g * kMaxD + d] = O;
+        if (d == 0) { cm[g] = M; cl[g] = Ls; }
+    }
+}
+
+// a warp's online-softmax state in global memory between the shared-prefix
+// kernel and the decode kernel: floats [j][lane], j = m0 m1 l0 l1 acc...
+__host__ __device__ constexpr int kStateFloats(int KS) { return 4 + 4 * KS; }
+template <int KS, bool STORE>
+__device__ __forceinline__ void tc_state_io(float* base, int lane, float (&m_r)[2], float (&l_r)[2], float (&acc)[KS][4]) {
+    auto io = [&](int j, float& v) {
+        if (STORE) base[j * 32 + lane] = v;
+        else v = base[j * 32 + lane];
+    };
+    io(0, m_r[0]); io(1, m_r[1]); io(2, l_r[0]); io(3, l_r[1]);
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) io(4 + 4 * mt + e, acc[mt][e]);
+}
+
+// Shared-prefix blocks a rank of the prefix kernel keeps resident.
+constexpr int kPreMaxBlocks = 4;
+
 // GM (batched decode): the same C key ranks, launched as independent CTAs
 // (x = rank) instead of one cluster, each writing its partial (max, sum,
 // unnormalised O per head) to part[(t * HKV + hk) * C + r]; k_attn_decode_merge
@@ -701,7 +892,8 @@ template <int D, bool GM>
 __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const float* __restrict__ q, int ldq, const float* __restrict__ knew, const float* __restrict__ vnew, int ldkv,
     int H, int HKV, float scale, int rot, int neox, const float* __restrict__ rcos, const float* __restrict__ rsin,
-    KvView kv, int layer, float* __restrict__ out, int ldo, float* __restrict__ part) {
+    KvView kv, int layer, float* __restrict__ out, int ldo, float* __restrict__ part, const int* __restrict__ pre,
+    const float* __restrict__ pstate) {
     using L = TcSmem;
     constexpr int RS = D + 8;        // padded row stride (halves)
     constexpr int KS = D / 16;       // k-steps of q.k, m-tiles of p.V
@@ -710,6 +902,17 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const int C = GM ? (int)gridDim.x : (int)cg::this_cluster().num_blocks();
     const int r = GM ? (int)blockIdx.x : (int)cg::this_cluster().block_rank();
     pdl_trigger();
+    // Blocks of this rank: b = r + C i. With a shared prefix (batched decode,
+    // pre = its 64-key blocks, set before the step) the first i0 of them were
+    // walked by k_attn_prefix_tc: their warp states wait in pstate, or, when
+    // no block of the rank is left here, the rank partial is already in part.
+    const int pos = kv.tok_pos[blockIdx.z], n_keys = pos + 1;
+    const int n_blocks = (n_keys + kTcKeys - 1) / kTcKeys;
+    const int bp = GM && pre ? min(*pre, C * kPreMaxBlocks) : 0;
+    const int i0 = r < bp ? (bp - r + C - 1) / C : 0;
+    const int nb_all = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
+    if (GM && i0 > 0 && nb_all == i0) return;
+    const int nb_mine = nb_all - i0;
     const unsigned long long t_kernel = gtimer();
     const bool tr = tracing() && !tracing_all() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
     __shared__ int s_tseq;
@@ -736,15 +939,12 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     float* sq = reinterpret_cast<float*>(smem + L::off_q);
     __half* sp = reinterpret_cast<__half*>(smem + L::off_p);
     float* snew = reinterpret_cast<float*>(smem + L::off_n);
-    const int pos = kv.tok_pos[t], n_keys = pos + 1;
-    const int n_blocks = (n_keys + kTcKeys - 1) / kTcKeys;
-    const int nb_mine = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
     const int seq = kv.tok_seq[t];
     const int b_own = pos / kTcKeys;
 
     // warp 0: one bulk copy per K row and per V row of my i-th block (slot i & 1)
     auto issue = [&](int i) {
-        const int b = r + C * i, j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0), np = (kb + 15) / 16;
+        const int b = r + C * (i0 + i), j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0), np = (kb + 15) / 16;
         uint64_t* br = &bar[i & 1];
         int page = 0;
         if (lane < np) {
@@ -797,19 +997,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     if (tr && threadIdx.x == 0) trace_ev(TR_ATTN, EV_WAITED, s_tseq);
     const float* qr = q + (size_t)t * ldq + (size_t)hk * G * D;
     const int wt = 32 * kIssuer;   // threads doing the rotation
-    for (int idx = tid; warp < kIssuer && idx < G * (D / 2); idx += wt) {
-        const int g = idx / (D / 2), i = idx % (D / 2);
-        const float* hv = qr + (size_t)g * D;
-        if (i < half) {
-            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
-            const float x0 = hv[a], x1 = hv[b];
-            sq[g * kMaxD + a] = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
-            sq[g * kMaxD + b] = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
-        } else {
-            sq[g * kMaxD + 2 * i] = hv[2 * i];
-            sq[g * kMaxD + 2 * i + 1] = hv[2 * i + 1];
-        }
-    }
+    if (warp < kIssuer) tc_rotate_q(sq, qr, G, D, D, half, neox, cs, sn, tid, wt);
     if (b_own % C == r && warp < kIssuer) {
         const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
         const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
@@ -844,34 +1032,19 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     __syncthreads();
     if (tr && tid == 0) trace_ev(TR_ATTN, 4, s_tseq);
 
-    // q as the B operand (k = dims, n = heads): lane holds head lane/4, dims
-    // 2(lane%4) + {0, 1, 8, 9} of each 16-dim step, as hi and lo halves
-    const int gq = lane >> 2, k0 = 2 * (lane & 3);
     uint32_t qh[KS][2], ql[KS][2];
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int d = 16 * ks + k0 + 8 * e;
-            const float x0 = gq < G ? sq[gq * kMaxD + d] : 0.0f, x1 = gq < G ? sq[gq * kMaxD + d + 1] : 0.0f;
-            float h0, l0, h1, l1;
-            split_h(x0, h0, l0);
-            split_h(x1, h1, l1);
-            qh[ks][e] = pack_h2(h0, h1);
-            ql[ks][e] = pack_h2(l0, l1);
-        }
-    }
-    // this lane's two heads in the score and output fragments
-    const int h0 = 2 * (lane & 3);
+    tc_q_frags<KS>(sq, G, lane, qh, ql);
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
     float acc[KS][4];
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+    if (i0 > 0) {   // continue from the shared-prefix kernel's state of this warp
+        float* sb = const_cast<float*>(pstate) + ((((size_t)t * HKV + hk) * C + r) * kTcWarps + warp) * 32 * kStateFloats(KS);
+        tc_state_io<KS, false>(sb, lane, m_r, l_r, acc);
+    }
     __half* pw = sp + (size_t)warp * 2 * 8 * 16;   // [hi/lo][8 heads][16 keys]
-    const int r_in = (lane & 7) + ((lane >> 3) & 1) * 8, c_in = (lane >> 4) * 8;       // ldmatrix (K rows)
-    const int key_in = (lane & 7) + ((lane >> 4) & 1) * 8, dim_in = ((lane >> 3) & 1) * 8;  // ldmatrix.trans (V)
     int failed_at = -1;
     for (int i = 0; i < nb_mine; ++i) {
         const bool ok = mbar_wait(&bar[i & 1], (uint32_t)((i >> 1) & 1), s_abort);
@@ -879,7 +1052,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
             failed_at = i;
             break;
         }
-        const int b = r + C * i, j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0);
+        const int b = r + C * (i0 + i), j0 = b * kTcKeys, kb = min(kTcKeys, n_keys - j0);
         __half* K = sk + (size_t)(i & 1) * L::ring;
         __half* V = sv + (size_t)(i & 1) * L::ring;
         if (b == b_own) {
@@ -890,76 +1063,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
             }
             __syncthreads();
         }
-        const int kw = 16 * warp;   // this warp's first key in the block
-        if (kw < kb) {
-            // scores S^T[16 keys][8 heads]
-            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                uint32_t a[4];
-                ldsm_x4(a, K + (size_t)(kw + r_in) * RS + 16 * ks + c_in);
-                mma16816(c, a, qh[ks][0], qh[ks][1]);
-                mma16816(c, a, ql[ks][0], ql[ks][1]);
-            }
-            // c0: (key lane/4, head h0), c1: (lane/4, h0+1), c2: (lane/4+8, h0), c3: (lane/4+8, h0+1)
-            const int ka = kw + (lane >> 2), kb2 = ka + 8;
-            float s[4];
-            s[0] = ka < kb ? __fmul_rn(c[0], scale) : -INFINITY;
-            s[1] = ka < kb ? __fmul_rn(c[1], scale) : -INFINITY;
-            s[2] = kb2 < kb ? __fmul_rn(c[2], scale) : -INFINITY;
-            s[3] = kb2 < kb ? __fmul_rn(c[3], scale) : -INFINITY;
-            float corr[2], p[4];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                float mx = fmaxf(s[e], s[e + 2]);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mn = fmaxf(m_r[e], mx);
-                corr[e] = m_r[e] == -INFINITY ? 0.0f : expf(m_r[e] - mn);
-                p[e] = s[e] == -INFINITY ? 0.0f : expf(s[e] - mn);
-                p[e + 2] = s[e + 2] == -INFINITY ? 0.0f : expf(s[e + 2] - mn);
-                float sum = p[e] + p[e + 2];
-                sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-                l_r[e] = l_r[e] * corr[e] + sum;
-                m_r[e] = mn;
-            }
-#pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-                acc[mt][0] *= corr[0];
-                acc[mt][1] *= corr[1];
-                acc[mt][2] *= corr[0];
-                acc[mt][3] *= corr[1];
-            }
-            // P^T as the B operand of p.V (k = keys, n = heads): transpose through shared memory
-            {
-                const int kr = lane >> 2;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int hh = h0 + (e & 1), kk = kr + 8 * (e >> 1);
-                    float ph, pl;
-                    split_h(p[e], ph, pl);
-                    pw[(0 * 8 + hh) * 16 + kk] = __float2half_rn(ph);
-                    pw[(1 * 8 + hh) * 16 + kk] = __float2half_rn(pl);
-                }
-            }
-            __syncwarp();
-            const uint32_t pbh0 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0);
-            const uint32_t pbh1 = *reinterpret_cast<const uint32_t*>(pw + (0 * 8 + gq) * 16 + k0 + 8);
-            const uint32_t pbl0 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0);
-            const uint32_t pbl1 = *reinterpret_cast<const uint32_t*>(pw + (1 * 8 + gq) * 16 + k0 + 8);
-            __syncwarp();
-            // O^T[D][8 heads] += V^T[D][16 keys] . P^T[16 keys][8 heads]
-#pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-                uint32_t a[4];
-                ldsm_x4_t(a, V + (size_t)(kw + key_in) * RS + 16 * mt + dim_in);
-                mma16816(acc[mt], a, pbh0, pbh1);
-                mma16816(acc[mt], a, pbl0, pbl1);
-            }
-        }
+        tc_warp_block<D>(K, V, 16 * warp, kb, scale, qh, ql, m_r, l_r, acc, pw, lane);
         __syncthreads();
         if (warp == kIssuer && i + 2 < nb_mine) issue(i + 2);
     }
@@ -980,39 +1084,9 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
         if (tid < 8) { cm[tid] = -INFINITY; cl[tid] = 0.0f; }
     } else {
         // the warps' partials (max, sum, unnormalised O) -> the CTA's
-        if (lane < 4) {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                wm[warp * 8 + h0 + e] = m_r[e];
-                wl[warp * 8 + h0 + e] = l_r[e];
-            }
-        }
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-            const int d = 16 * mt + (lane >> 2);
-            wo[((size_t)warp * 8 + h0) * kMaxD + d] = acc[mt][0];
-            wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d] = acc[mt][1];
-            wo[((size_t)warp * 8 + h0) * kMaxD + d + 8] = acc[mt][2];
-            wo[((size_t)warp * 8 + h0 + 1) * kMaxD + d + 8] = acc[mt][3];
-        }
+        tc_store_warp<KS>(wm, wl, wo, warp, lane, m_r, l_r, acc);
         __syncthreads();
-        for (int idx = tid; idx < G * D; idx += 32 * kTcWarps) {
-            const int g = idx / D, d = idx % D;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, wm[w * 8 + g]);
-            float Ls = 0.0f, O = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kTcWarps; ++w) {
-                const float mw = wm[w * 8 + g];
-                if (mw == -INFINITY) continue;
-                const float cw = expf(mw - M);
-                Ls += wl[w * 8 + g] * cw;
-                O += wo[((size_t)w * 8 + g) * kMaxD + d] * cw;
-            }
-            co[g * kMaxD + d] = O;
-            if (d == 0) { cm[g] = M; cl[g] = Ls; }
-        }
+        tc_merge_warps(wm, wl, wo, cm, cl, co, G, D, tid, 32 * kTcWarps);
     }
     if constexpr (GM) {
         __syncthreads();
@@ -1046,8 +1120,8 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
         for (int rr = 0; rr < 16; ++rr) {
             if (rr < C && mv[rr] != -INFINITY) {
                 const float w = expf(mv[rr] - M);
-                Ls += lv[rr] * w;
-                O += ov[rr] * w;
+                Ls = __fmaf_rn(lv[rr], w, Ls);
+                O = __fmaf_rn(ov[rr], w, O);
             }
         }
         out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
@@ -1087,11 +1161,169 @@ __global__ void __launch_bounds__(256) k_attn_decode_merge(const float* __restri
         for (int rr = 0; rr < 16; ++rr) {
             if (rr < C && mv[rr] != -INFINITY) {
                 const float w = expf(mv[rr] - M);
-                Ls += lv[rr] * w;
-                O += ov[rr] * w;
+                Ls = __fmaf_rn(lv[rr], w, Ls);
+                O = __fmaf_rn(ov[rr], w, O);
             }
         }
         out[(size_t)t * ldo + ((size_t)hk * G + g) * D + d] = Ls > 0.0f ? O / Ls : 0.0f;
+    }
+}
+
+// Shared prefix of a batched decode (the sessions' first bp 64-key blocks
+// sit on the same pages): CTA (rank r, kv head, 8 tokens) brings the rank's
+// prefix blocks (b = r + C i < bp, at most kPreMaxBlocks) into shared memory
+// once and runs, for each token, the decode kernel's four warps over them
+// (tc_warp_block, same order), so those keys cross HBM once per step instead
+// of once per session. A token for which the rank has more blocks leaves its
+// warps' states in pstate for k_attn_decode_tc; otherwise the CTA merges them
+// as the decode kernel does and writes the rank partial. Eight warps: two
+// tokens at a time.
+struct PreSmem {
+    static constexpr size_t tile = (size_t)kTcKeys * kTcRs;                   // halves of one K or V block
+    static constexpr size_t off_k = 128;                                       // barriers + abort flag below
+    static constexpr size_t off_v = off_k + kPreMaxBlocks * tile * 2;
+    static constexpr size_t off_q = off_v + kPreMaxBlocks * tile * 2;           // [8 tokens][8][kMaxD] f32
+    static constexpr size_t off_r = off_q + sizeof(float) * 8 * 8 * kMaxD;     // [8 tokens][cos, sin][kMaxD / 2]
+    static constexpr size_t off_p = off_r + sizeof(float) * 8 * kMaxD;         // [8 warps][2][8][16] f16
+    static constexpr size_t off_wm = off_p + 2 * 8 * 2 * 8 * 16;               // [2][4 warps][8]
+    static constexpr size_t off_wl = off_wm + sizeof(float) * 2 * kTcWarps * 8;
+    static constexpr size_t off_wo = off_wl + sizeof(float) * 2 * kTcWarps * 8; // [2][4][8][kMaxD]
+    static constexpr size_t off_cm = off_wo + sizeof(float) * 2 * kTcWarps * 8 * kMaxD;  // [2][8]
+    static constexpr size_t off_cl = off_cm + sizeof(float) * 2 * 8;
+    static constexpr size_t off_co = off_cl + sizeof(float) * 2 * 8;           // [2][8][kMaxD]
+    static constexpr size_t bytes = off_co + sizeof(float) * 2 * 8 * kMaxD;
+};
+constexpr int kPreTokens = 8;
+
+template <int D>
+__global__ void __launch_bounds__(256) k_attn_prefix_tc(const float* __restrict__ q, int ldq, int H, int HKV, float scale,
+                                                        int rot, int neox, const float* __restrict__ rcos,
+                                                        const float* __restrict__ rsin, KvView kv, int layer, int T,
+                                                        const int* __restrict__ pre, float* __restrict__ pstate,
+                                                        float* __restrict__ part) {
+    using L = PreSmem;
+    constexpr int RS = D + 8, KS = D / 16;
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    const int C = (int)gridDim.x, r = (int)blockIdx.x, hk = (int)blockIdx.y, G = H / HKV;
+    const int bp = min(*pre, C * kPreMaxBlocks);
+    const int nbp = r < bp ? (bp - r + C - 1) / C : 0;
+    const int tb = (int)blockIdx.z * kPreTokens;
+    if (nbp == 0 || tb >= T) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ntok = min(kPreTokens, T - tb);
+    __shared__ int s_pos[kPreTokens];
+    if (tid < ntok) s_pos[tid] = kv.tok_pos[tb + tid];   // set before the step
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 64);
+    __half* sk = reinterpret_cast<__half*>(smem + L::off_k);
+    __half* sv = reinterpret_cast<__half*>(smem + L::off_v);
+    if (tid == 0) {
+        *s_abort = 0;
+        for (int i = 0; i < kPreMaxBlocks; ++i) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    // the prefix pages are the same for every token of the batch (set before
+    // the step from the page tables): read them through the first token's
+    if (warp == 0) {
+        const int seq = kv.tok_seq[tb];
+        for (int i = 0; i < nbp; ++i) {
+            const int j0 = (r + C * i) * kTcKeys;   // a full block: 4 pages
+            int page = 0;
+            if (lane < 4) {
+                page = kv.pt[(size_t)seq * kv.pt_stride + j0 / 16 + lane];
+                if (page < 0 || page >= kv.n_pages) {
+                    if (kv.err) atomicExch(kv.err, 5);
+                    page = 0;
+                }
+            }
+            if (lane == 0) mbar_expect_tx(&bar[i], (uint32_t)(2 * kTcKeys * D * 2));
+            __syncwarp();
+            for (int k = 0; k < 2; ++k) {
+                const int rr = lane + 32 * k;
+                const int pg = __shfl_sync(0xffffffffu, page, rr >> 4);
+                const size_t off = (size_t)pg * kv.page_stride + (size_t)layer * kv.layer_stride +
+                                   (size_t)hk * kv.head_stride + (size_t)(rr & 15) * D;
+                bulk_g2s(sk + (size_t)i * L::tile + (size_t)rr * RS, reinterpret_cast<const __half*>(kv.k) + off,
+                         (uint32_t)(D * 2), &bar[i]);
+                bulk_g2s(sv + (size_t)i * L::tile + (size_t)rr * RS, reinterpret_cast<const __half*>(kv.v) + off,
+                         (uint32_t)(D * 2), &bar[i]);
+            }
+        }
+    }
+    // the group's q rows (raw) and their positions' rotation rows, with
+    // independent loads, then every row rotated in place
+    const int half = rot / 2, GD = G * D;
+    float* sqa = reinterpret_cast<float*>(smem + L::off_q);
+    float* srot = reinterpret_cast<float*>(smem + L::off_r);
+    for (int i = tid; i < ntok * half; i += 256) {
+        const int u = i / half, j = i % half;
+        srot[u * kMaxD + j] = rcos[(size_t)s_pos[u] * half + j];
+        srot[u * kMaxD + kMaxD / 2 + j] = rsin[(size_t)s_pos[u] * half + j];
+    }
+    pdl_wait();
+    for (int i = tid; i < ntok * (GD / 4); i += 256) {
+        const int u = i / (GD / 4), j = 4 * (i % (GD / 4));
+        const float4 v4 = *reinterpret_cast<const float4*>(q + (size_t)(tb + u) * ldq + (size_t)hk * GD + j);
+        *reinterpret_cast<float4*>(sqa + (size_t)u * 8 * kMaxD + (j / D) * kMaxD + j % D) = v4;
+    }
+    __syncthreads();
+    for (int u = 0; u < ntok; ++u)   // pairs (a, b) are disjoint: in place
+        tc_rotate_q(sqa + (size_t)u * 8 * kMaxD, sqa + (size_t)u * 8 * kMaxD, G, kMaxD, D, half, neox,
+                    srot + u * kMaxD, srot + u * kMaxD + kMaxD / 2, tid, 256);
+    bool ok = true;
+    for (int i = 0; i < nbp && ok; ++i) ok = mbar_wait(&bar[i], 0u, s_abort);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+            if (kv.err) atomicExch(kv.err, 6);
+            for (int i = 0; i < nbp; ++i) mbar_wait_bounded(&bar[i], 0u);
+        }
+        return;
+    }
+    const int slot = warp >> 2, w = warp & 3, stid = tid & 127;
+    __half* pw = reinterpret_cast<__half*>(smem + L::off_p) + (size_t)warp * 2 * 8 * 16;
+    float* wm = reinterpret_cast<float*>(smem + L::off_wm) + slot * kTcWarps * 8;
+    float* wl = reinterpret_cast<float*>(smem + L::off_wl) + slot * kTcWarps * 8;
+    float* wo = reinterpret_cast<float*>(smem + L::off_wo) + (size_t)slot * kTcWarps * 8 * kMaxD;
+    float* cm = reinterpret_cast<float*>(smem + L::off_cm) + slot * 8;
+    float* cl = reinterpret_cast<float*>(smem + L::off_cl) + slot * 8;
+    float* co = reinterpret_cast<float*>(smem + L::off_co) + (size_t)slot * 8 * kMaxD;
+    for (int pr = 0; pr < kPreTokens / 2; ++pr) {
+        const int u = 2 * pr + slot, t = tb + u;
+        const bool tv = t < T;
+        const int pos = tv ? s_pos[u] : 0;
+        const float* sq = sqa + (size_t)u * 8 * kMaxD;
+        // does the rank have blocks of this token past the prefix?
+        const int n_blocks = (pos + 1 + kTcKeys - 1) / kTcKeys;
+        const bool more = (n_blocks - r + C - 1) / C > nbp;
+        if (tv) {
+            uint32_t qh[KS][2], ql[KS][2];
+            tc_q_frags<KS>(sq, G, lane, qh, ql);
+            float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+            float acc[KS][4];
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+            for (int i = 0; i < nbp; ++i)
+                tc_warp_block<D>(sk + (size_t)i * L::tile, sv + (size_t)i * L::tile, 16 * w, kTcKeys, scale, qh, ql, m_r,
+                                 l_r, acc, pw, lane);
+            if (more) {
+                float* sb = pstate + ((((size_t)t * HKV + hk) * C + r) * kTcWarps + w) * 32 * kStateFloats(KS);
+                tc_state_io<KS, true>(sb, lane, m_r, l_r, acc);
+            } else {
+                tc_store_warp<KS>(wm, wl, wo, w, lane, m_r, l_r, acc);
+            }
+        }
+        __syncthreads();
+        if (tv && !more) tc_merge_warps(wm, wl, wo, cm, cl, co, G, D, stid, 128);
+        __syncthreads();
+        if (tv && !more) {
+            float* pp = part + ((size_t)(t * HKV + hk) * C + r) * dec_part_floats(G, D);
+            if (stid < G) { pp[stid] = cm[stid]; pp[8 + stid] = cl[stid]; }
+            for (int idx = stid; idx < G * D; idx += 128) pp[16 + idx] = co[(idx / D) * kMaxD + idx % D];
+        }
     }
 }
 
@@ -1222,7 +1454,7 @@ static int tc_cluster_size() {
 template <int D>
 static int launch_decode_tc(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV,
                             float scale, int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer,
-                            float* out, int ldo, float* part, cudaStream_t st) {
+                            float* out, int ldo, float* part, const int* pre, float* pstate, cudaStream_t st) {
     static int cluster = 0;
     if (!cluster) {
         cudaError_t e = cudaFuncSetAttribute(k_attn_decode_tc<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1232,6 +1464,9 @@ static int launch_decode_tc(const float* q, int ldq, const float* k, const float
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_attn_decode_tc<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)TcSmem::bytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_prefix_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)PreSmem::bytes);
         if (e != cudaSuccess) return (int)e;
         int c = tc_cluster_size();
         cudaLaunchConfig_t cfg{};
@@ -1275,9 +1510,17 @@ static int launch_decode_tc(const float* q, int ldq, const float* k, const float
     cfg.numAttrs = na;
     if (!part)
         return (int)cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D, false>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox,
-                                       rcos, rsin, kv, layer, out, ldo, (float*)nullptr);
+                                       rcos, rsin, kv, layer, out, ldo, (float*)nullptr, (const int*)nullptr,
+                                       (const float*)nullptr);
+    if (pre) {
+        // the shared prefix once for all tokens (exits at once when there is none)
+        cudaError_t e = fbk_launch(k_attn_prefix_tc<D>, dim3(cluster, HKV, (T + kPreTokens - 1) / kPreTokens), dim3(256),
+                                   PreSmem::bytes, st, q, ldq, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, T, pre,
+                                   pstate, part);
+        if (e != cudaSuccess) return (int)e;
+    }
     cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_decode_tc<D, true>, q, ldq, k, v, ldkv, H, HKV, scale, rot, neox,
-                                       rcos, rsin, kv, layer, out, ldo, part);
+                                       rcos, rsin, kv, layer, out, ldo, part, pre, (const float*)pstate);
     if (e != cudaSuccess) return (int)e;
     return (int)fbk_launch(k_attn_decode_merge, dim3(HKV, T), dim3(256), 0, st, (const float*)part, cluster, H / HKV,
                            D, HKV, out, ldo);
@@ -1287,11 +1530,16 @@ static int launch_decode_tc(const float* q, int ldq, const float* k, const float
 extern "C" size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D) {
     return (size_t)T * HKV * 16 * dec_part_floats(H / HKV, D);
 }
+extern "C" int fbk_attention_prefix_max_blocks(void) { return 16 * kPreMaxBlocks; }
+// Floats of the warp-state scratch of the shared-prefix kernel for T tokens.
+extern "C" size_t fbk_attention_prefix_state_floats(int T, int HKV, int D) {
+    return (size_t)T * HKV * 16 * kTcWarps * 32 * kStateFloats(D / 16);
+}
 
 extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H,
                                     int HKV, int D, float scale, int rot, int neox, const float* rcos, const float* rsin,
                                     KvView kv, int layer, float* out, int ldo, float* part, size_t part_floats,
-                                    cudaStream_t st) {
+                                    const int* pre, float* pstate, size_t pstate_floats, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
     if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
@@ -1301,9 +1549,13 @@ extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, con
         // batches of tokens: independent rank CTAs + merge (same bits as one cluster per token)
         float* pp = (T > 1 && !batch_cluster && part && part_floats >= fbk_attention_decode_part_floats(T, H, HKV, D))
                         ? part : nullptr;
+        static const bool no_prefix = getenv("FISH_ATTN_NO_PREFIX") != nullptr;
+        const bool pf = pp && pre && pstate && !no_prefix && pstate_floats >= fbk_attention_prefix_state_floats(T, HKV, D);
         if (D == 128)
-            return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp, st);
-        return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp, st);
+            return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo,
+                                         pp, pf ? pre : nullptr, pf ? pstate : nullptr, st);
+        return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp,
+                                    pf ? pre : nullptr, pf ? pstate : nullptr, st);
     }
     if (kv.f16) return launch_decode<__half>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);
     return launch_decode<float>(q, ldq, k, v, ldkv, T, H, HKV, D, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, st);

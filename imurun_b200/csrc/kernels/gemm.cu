@@ -26,6 +26,7 @@
 // copied to shared memory with cp.async into an NS-stage ring. Nibbles /
 // 6-bit codes are unpacked into A fragments in registers (Q4_K low nibbles of
 // qs words are already four int8 in fragment order).
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 
@@ -96,7 +97,8 @@ struct StageLayout {
 };
 
 template <int W, int BM, int BN, int NS, int FT, int JT>
-__global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err) {
+__global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err, int upc,
+                                                                    float* part) {
     using L = StageLayout<W, BM, BN>;
     constexpr int WB = L::WB;
     // warps of 16 FT rows x 8 JT tokens: BM / (16 FT) along rows, BN / (8 JT) along tokens
@@ -108,13 +110,19 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
     const int row0 = blockIdx.x * kBM, t0 = blockIdx.y * kBN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int wr = warp % WRN, wc = warp / WRN;   // rows 16 FT wr .., tokens 8 JT wc ..
-    const int nsteps = K / 256;
+    // K split (upc > 0): this CTA takes the half-group units (4 blocks)
+    // [z upc, (z + 1) upc) and writes each unit's tree value to
+    // part[(unit * T + t) * rows + row] for k_gemm_unit_reduce
+    const bool split = upc > 0;
+    const int sb0 = split ? 4 * (int)blockIdx.z * upc : 0;
+    const int nsteps = split ? min(K / 256 - sb0, 4 * upc) : K / 256;
     const uint8_t* wend = g.w + g.w_bytes;
 
     // Issue the copies of step s into stage buffer b; returns this thread's
     // token scale for the step (K-quants: dk of token t0 + tid), stored by
     // the caller once the current step's arithmetic is done.
-    auto issue = [&](int s, uint8_t* b) -> float {
+    auto issue = [&](int sl, uint8_t* b) -> float {
+        const int s = sb0 + sl;   // block of the row
         constexpr int WCH = W == T_Q4_K ? 9 : (W == T_Q6_K ? 13 : 16);   // 16-byte chunks of codes per row
         constexpr int NCH = W == T_Q4_K ? WCH : WCH + 1;                 // + the scale-table chunk
         for (int i = tid; i < kBM * NCH; i += kGemmThreads) {
@@ -174,40 +182,62 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
     //   ((t0 + t1) + (t2 + t3)) + ((t4 + t5) + (t6 + t7)), then acc += group.
     // Block bi of the group is the same for the whole CTA: one branch per
     // block, every output inside it.
-    auto tree_push = [&](const float (&t)[FT][JT][4], int bi) {
+    // split mode: a finished half-group unit's value of output (f, j, c)
+    auto unit_store = [&](int f, int j, int c, float v, int unit) {
+        const int row = row0 + 16 * FT * wr + 16 * f + 8 * (c >> 1) + gid;
+        const int t = t0 + 8 * JT * wc + 8 * j + 2 * tig + (c & 1);
+        if (row < g.rows && t < T) part[((size_t)unit * T + t) * g.rows + row] = v;
+    };
+    // in split mode the half-group values ((t0 + t1) + (t2 + t3)) and
+    // ((t4 + t5) + (t6 + t7)) go out at bi = 3 and 7 instead of acc += group
+    auto tree_push = [&](const float (&t)[FT][JT][4], int bi, int unit) {
 #define FB_EACH for (int f = 0; f < FT; ++f) for (int j = 0; j < JT; ++j) for (int c = 0; c < 4; ++c)
         switch (bi) {
             case 0: _Pragma("unroll") FB_EACH pa[f][j][c] = t[f][j][c]; break;
             case 1: _Pragma("unroll") FB_EACH pa[f][j][c] = __fadd_rn(pa[f][j][c], t[f][j][c]); break;
             case 2: _Pragma("unroll") FB_EACH pc[f][j][c] = t[f][j][c]; break;
-            case 3: _Pragma("unroll") FB_EACH pa[f][j][c] = __fadd_rn(pa[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c])); break;
+            case 3:
+                _Pragma("unroll") FB_EACH {
+                    pa[f][j][c] = __fadd_rn(pa[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c]));
+                    if (split) unit_store(f, j, c, pa[f][j][c], unit);
+                }
+                break;
             case 4: _Pragma("unroll") FB_EACH pb[f][j][c] = t[f][j][c]; break;
             case 5: _Pragma("unroll") FB_EACH pb[f][j][c] = __fadd_rn(pb[f][j][c], t[f][j][c]); break;
             case 6: _Pragma("unroll") FB_EACH pc[f][j][c] = t[f][j][c]; break;
             default:
-                _Pragma("unroll") FB_EACH acc[f][j][c] = __fadd_rn(
-                    acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c]))));
+                if (split) {
+                    _Pragma("unroll") FB_EACH unit_store(f, j, c, __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c])), unit);
+                } else {
+                    _Pragma("unroll") FB_EACH acc[f][j][c] = __fadd_rn(
+                        acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t[f][j][c]))));
+                }
         }
 #undef FB_EACH
     };
     // the same steps for one output (the Q6_K path: its 16 scale groups
     // leave fewer registers for a whole tile of terms)
-    auto tree_push1 = [&](int f, int j, int c, float t, int bi) {
+    auto tree_push1 = [&](int f, int j, int c, float t, int bi, int unit) {
         switch (bi) {
             case 0: pa[f][j][c] = t; break;
             case 1: pa[f][j][c] = __fadd_rn(pa[f][j][c], t); break;
             case 2: pc[f][j][c] = t; break;
-            case 3: pa[f][j][c] = __fadd_rn(pa[f][j][c], __fadd_rn(pc[f][j][c], t)); break;
+            case 3:
+                pa[f][j][c] = __fadd_rn(pa[f][j][c], __fadd_rn(pc[f][j][c], t));
+                if (split) unit_store(f, j, c, pa[f][j][c], unit);
+                break;
             case 4: pb[f][j][c] = t; break;
             case 5: pb[f][j][c] = __fadd_rn(pb[f][j][c], t); break;
             case 6: pc[f][j][c] = t; break;
             default:
-                acc[f][j][c] = __fadd_rn(acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t))));
+                if (split) unit_store(f, j, c, __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t)), unit);
+                else acc[f][j][c] = __fadd_rn(acc[f][j][c], __fadd_rn(pa[f][j][c], __fadd_rn(pb[f][j][c], __fadd_rn(pc[f][j][c], t))));
         }
     };
-    // after block bi of a group that ends there (bi < 7: the row's last
-    // group is short; the GEMV adds +0 for its missing blocks)
-    auto tree_close = [&](int bi) {
+    // after block bi of a group that ends there (the row's last group is
+    // short; the GEMV adds +0 for its missing blocks), to the end of the
+    // group, or of the half-group unit in split mode
+    auto tree_close = [&](int bi, int unit) {
         float zero[FT][JT][4];
 #pragma unroll
         for (int f = 0; f < FT; ++f)
@@ -215,7 +245,8 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
             for (int j = 0; j < JT; ++j)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) zero[f][j][c] = 0.0f;
-        for (int z = bi + 1; z < 8; ++z) tree_push(zero, z);
+        const int zend = split && bi < 4 ? 4 : 8;
+        for (int z = bi + 1; z < zend; ++z) tree_push(zero, z, unit);
     };
 
     // steps 0 .. NS-2 in flight before the loop; every iteration commits one
@@ -242,7 +273,8 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
         const uint8_t* sW = cur + L::w_off;
         const uint8_t* sX = cur + L::x_off;
         const float* sD = reinterpret_cast<const float*>(cur + L::d_off);
-        const int bi = s & 7;   // block (Q8_0: eighth) of the step within its group
+        const int sg = sb0 + s, unit = sg >> 2;
+        const int bi = sg & 7;   // block (Q8_0: eighth) of the step within its group
         // this thread's rows (local): fragment f, h = 0: gid, h = 1: gid + 8;
         // tokens (local): fragment j, columns 2 tig, 2 tig + 1
         if (W == T_Q4_K) {
@@ -322,7 +354,7 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                             tt[f][j][2 * h + e] = q4k_term(dw[f][h], dmw[f][h], dx, sumi[f][j][2 * h + e], mn[f][j][2 * h + e]);
                 }
             }
-            tree_push(tt, bi);
+            tree_push(tt, bi, unit);
         } else if (W == T_Q6_K) {
             float dw[FT][2];
 #pragma unroll
@@ -377,7 +409,7 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     for (int f = 0; f < FT; ++f)
 #pragma unroll
                         for (int h = 0; h < 2; ++h)
-                            tree_push1(f, j, 2 * h + e, scaled_term(dw[f][h], dx, sumi[f][j][2 * h + e]), bi);
+                            tree_push1(f, j, 2 * h + e, scaled_term(dw[f][h], dx, sumi[f][j][2 * h + e]), bi, unit);
                 }
         } else {   // Q8_0: eight 32-value blocks per step, summed in block order (a GEMV lane's share)
             float cs[FT][JT][4];
@@ -419,13 +451,14 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
                     }
                 }
             }
-            tree_push(cs, bi);
+            tree_push(cs, bi, unit);
         }
-        if (bi != 7 && s + 1 == nsteps) tree_close(bi);   // the row's short last group
+        if (sg + 1 == K / 256 && bi != 7 && !(split && bi == 3)) tree_close(bi, unit);   // the row's short last group
         if (W != T_Q8_0 && sn < nsteps && tid < kBN) reinterpret_cast<float*>(nxt + L::d_off)[tid] = dx_next;
         __syncthreads();   // the stage is read; the next issue may overwrite it
     }
     // epilogue: bias, residual add (store_out)
+    if (split) return;
 #pragma unroll
     for (int f = 0; f < FT; ++f)
 #pragma unroll
@@ -454,14 +487,38 @@ static int gemm_num_sms() {
 }
 
 template <int W, int BM, int BN, int NS, int FT, int JT>
-static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int T, int* err, cudaStream_t st) {
+static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int T, int* err, float* part,
+                                    size_t part_floats, cudaStream_t st) {
     constexpr size_t smem = NS * (size_t)StageLayout<W, BM, BN>::bytes;
     constexpr int threads = BM * BN / (4 * FT * JT);   // 32 x warps
     static cudaError_t attr = cudaFuncSetAttribute(k_gemm_q<W, BM, BN, NS, FT, JT>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (attr != cudaSuccess) return attr;
-    const dim3 grid((g.rows + BM - 1) / BM, (T + BN - 1) / BN);
-    return fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT>, grid, dim3(threads), smem, st, g, a, K, T, err);
+    // resident CTAs the device holds at once
+    static const int capacity = [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemm_q<W, BM, BN, NS, FT, JT>, threads, smem) != cudaSuccess)
+            n = 1;
+        return std::max(1, n) * gemm_num_sms();
+    }();
+    dim3 grid((g.rows + BM - 1) / BM, (T + BN - 1) / BN);
+    // fewer tiles than resident CTAs: split K in half-group units so the
+    // device fills (every unit's value is kept apart and the reduce adds them
+    // in the unsplit order)
+    static const bool no_split = getenv("FISH_GEMM_NO_SPLIT") != nullptr;
+    const int tiles = (int)(grid.x * grid.y), n_units = (K / 256 + 3) / 4;
+    int upc = 0;
+    if (part && !no_split && tiles < capacity && n_units > 1 && (size_t)n_units * T * g.rows <= part_floats) {
+        const int want = std::min(n_units, (capacity + tiles - 1) / tiles);
+        if (want > 1) {
+            upc = (n_units + want - 1) / want;
+            grid.z = (n_units + upc - 1) / upc;
+            if (grid.z <= 1) upc = 0, grid.z = 1;
+        }
+    }
+    cudaError_t e = fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT>, grid, dim3(threads), smem, st, g, a, K, T, err, upc, part);
+    if (e != cudaSuccess || !upc) return e;
+    return (cudaError_t)fbk_gemm_unit_reduce(&g, part, n_units, T, st);
 }
 
 // Token tile by call size: up to 64 tokens (batched decode, short prompts)
@@ -470,7 +527,8 @@ static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int 
 // 14336x4096 Q6_K at 64 tokens 203 -> 160 us); longer prompts use 64-token
 // tiles (each weight step serves more tokens) double-buffered.
 template <int W>
-static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, int* err, cudaStream_t st) {
+static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, int* err, float* part, size_t pf,
+                               cudaStream_t st) {
     static const int bn_env = [] {
         const char* e = getenv("FISH_GEMM_BN");
         return e ? atoi(e) : 0;
@@ -480,11 +538,11 @@ static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, in
     // 32-row tiles, so twice the CTAs share the long K loop
     static const int sms = gemm_num_sms();
     const bool rows32 = bn < 64 && (g.rows + 63) / 64 < sms;
-    if (bn == 16) return rows32 ? launch_gemm_tile<W, 32, 16, 4, 1, 1>(g, a, K, T, err, st)    // 4 warps of 16 x 8
-                                : launch_gemm_tile<W, 64, 16, 4, 1, 1>(g, a, K, T, err, st);   // 8 warps of 16 x 8
-    if (bn == 32) return rows32 ? launch_gemm_tile<W, 32, 32, 4, 1, 2>(g, a, K, T, err, st)    // 4 warps of 16 x 16
-                                : launch_gemm_tile<W, 64, 32, 4, 1, 2>(g, a, K, T, err, st);   // 8 warps of 16 x 16
-    return launch_gemm_tile<W, 64, 64, 2, 2, 2>(g, a, K, T, err, st);                           // 8 warps of 32 x 16
+    if (bn == 16) return rows32 ? launch_gemm_tile<W, 32, 16, 4, 1, 1>(g, a, K, T, err, part, pf, st)    // 4 warps of 16 x 8
+                                : launch_gemm_tile<W, 64, 16, 4, 1, 1>(g, a, K, T, err, part, pf, st);   // 8 warps of 16 x 8
+    if (bn == 32) return rows32 ? launch_gemm_tile<W, 32, 32, 4, 1, 2>(g, a, K, T, err, part, pf, st)    // 4 warps of 16 x 16
+                                : launch_gemm_tile<W, 64, 32, 4, 1, 2>(g, a, K, T, err, part, pf, st);   // 8 warps of 16 x 16
+    return launch_gemm_tile<W, 64, 64, 2, 2, 2>(g, a, K, T, err, part, pf, st);                           // 8 warps of 32 x 16
 }
 
 extern "C" int fbk_gemm_eligible(const GemvArgs* a) {
@@ -510,9 +568,9 @@ extern "C" int fbk_gemm(const GemvArgs* a, cudaStream_t st) {
         const bool narrow = (g.rows + 127) / 128 <= 32 && a->K >= 2048 && a->part;
         if (g.type == T_Q4_K && (a->T > 32 || narrow) && fbk_gemm_tc_eligible(&g, &a->act, a->K, a->T))
             e = (cudaError_t)fbk_gemm_tc(&g, &a->act, a->K, a->T, err, a->part, a->part_floats, st);
-        else if (g.type == T_Q4_K) e = launch_gemm<T_Q4_K>(g, a->act, a->K, a->T, err, st);
-        else if (g.type == T_Q6_K) e = launch_gemm<T_Q6_K>(g, a->act, a->K, a->T, err, st);
-        else e = launch_gemm<T_Q8_0>(g, a->act, a->K, a->T, err, st);
+        else if (g.type == T_Q4_K) e = launch_gemm<T_Q4_K>(g, a->act, a->K, a->T, err, a->part, a->part_floats, st);
+        else if (g.type == T_Q6_K) e = launch_gemm<T_Q6_K>(g, a->act, a->K, a->T, err, a->part, a->part_floats, st);
+        else e = launch_gemm<T_Q8_0>(g, a->act, a->K, a->T, err, a->part, a->part_floats, st);
         if (e != cudaSuccess) return (int)e;
     }
     return 0;

@@ -601,6 +601,9 @@ extern "C" int fbk_gemm_tc(const GemvSeg* g, const ActQ* a, int K, int T, int* e
     }
     cudaError_t e = fbk_launch(k_gemm_tc_q4k, grid, dim3(tc::kThreads), (size_t)tc::kSmem, st, wmap, wtail, xmap, args);
     if (e != cudaSuccess || !args.units_per_cta) return (int)e;
-    return (int)fbk_launch(k_gemm_unit_reduce, dim3((g->rows + 255) / 256, T), dim3(256), 0, st, *g, (const float*)part,
-                           n_units, T);
+    return fbk_gemm_unit_reduce(g, part, n_units, T, st);
+}
+
+extern "C" int fbk_gemm_unit_reduce(const GemvSeg* g, const float* part, int n_units, int T, cudaStream_t st) {
+    return (int)fbk_launch(k_gemm_unit_reduce, dim3((g->rows + 255) / 256, T), dim3(256), 0, st, *g, part, n_units, T);
 }

@@ -108,6 +108,10 @@ int fbk_gemm_tc_eligible(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T);
 int fbk_gemm_tc(const fb::GemvSeg* g, const fb::ActQ* a, int K, int T, int* err, float* part, size_t part_floats,
                 cudaStream_t st);
 int fbk_gemm(const fb::GemvArgs* args, cudaStream_t st);
+// The rows of a K-split tensor-core call: the half-group unit values in part
+// [n_units][T][rows] added as the unsplit kernels add them (group = first
+// half + second half, then acc += group in order), then the output step.
+int fbk_gemm_unit_reduce(const fb::GemvSeg* g, const float* part, int n_units, int T, cudaStream_t st);
 // 1 if fbk_gemv runs this call on the streamed kernel (the only one that
 // takes a prologue other than PRO_ACT).
 int fbk_gemv_streamable(const fb::GemvArgs* args);
@@ -174,10 +178,20 @@ int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int D, float s
 // tokens with part (at least fbk_attention_decode_part_floats): the same key
 // ranks as independent CTAs writing partials to part, then a merge launch;
 // every token's output has the same bits on both paths.
+// pre (device int, nullable): the number of leading 64-key blocks every
+// token's sequence shares page for page, written before the step; with
+// pstate (fbk_attention_prefix_state_floats) those blocks are read once for
+// all tokens by a shared-prefix kernel whose warps continue into the decode
+// kernel, again with the same bits per token.
 int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,
                          float scale, int rot, int neox, const float* rope_cos, const float* rope_sin, KvView kv,
-                         int layer, float* out, int ldo, float* part, size_t part_floats, cudaStream_t st);
+                         int layer, float* out, int ldo, float* part, size_t part_floats, const int* pre, float* pstate,
+                         size_t pstate_floats, cudaStream_t st);
 size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D);
+size_t fbk_attention_prefix_state_floats(int T, int HKV, int D);
+// Blocks of 64 keys the shared-prefix kernel covers at most (16 key ranks x
+// the blocks a rank keeps resident).
+int fbk_attention_prefix_max_blocks(void);
 // Per-head RMSNorm in place (q/k norm), rows [T][n_heads*D].
 int fbk_head_rmsnorm(float* x, int ldx, int T, int n_heads, int D, const float* w, float eps, cudaStream_t st);
 // MoE: x[t] += sum_k wsel[t][k] * eo[t][k][:]

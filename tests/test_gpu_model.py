@@ -536,6 +536,44 @@ def test_decode_batch_equals_single_decodes(gpu, tiny_gguf):
             m.session_close(t)
 
 
+@pytest.mark.parametrize("P,n", [(700, 5), (2100, 17), (4200, 3)])
+def test_shared_prefix_batch_equals_single_decodes(gpu, tiny_gguf, P, n):
+    """Sessions forked from one P-token prompt (its pages shared), each with
+    its own suffix, decoded as one batch: attention reads the shared 64-key
+    blocks once for all sessions (the shared-prefix kernel, whose warps hand
+    their state to the decode kernel) and every session's logits equal, bit
+    for bit, those of the same session decoded alone (one cluster per kv
+    head). P = 700: ranks with one prefix block; 2100: two; 4200: four (the
+    resident maximum) plus a capped remainder; n = 17: three token groups."""
+    import json
+    from imurun_b200.native import Model
+    rng = np.random.default_rng(P + n)
+    prompt = rng.integers(3, 32000, P).astype(np.int32)
+    suffixes = [rng.integers(3, 32000, 3 + 7 * i % 40).astype(np.int32) for i in range(n)]
+    nxt = rng.integers(3, 32000, (2, n)).astype(np.int32)
+    with Model(tiny_gguf, 4608) as m:
+        m.prefill(prompt, 0)
+        ss = [m.session_fork(0, P) for _ in range(n)]
+        for s, u in zip(ss, suffixes):
+            m.session_prefill(s, u)
+        got = []
+        for step in range(2):
+            am, lg = m.decode_batch(ss, nxt[step], logits=True)
+            got.append(lg)
+            eng = json.loads(m.lib.fish_engine_json(m.ctx).decode())
+            want_blocks = min(P // 64, 64)
+            assert eng["last_batch_prefix_blocks"] == want_blocks, eng["last_batch_prefix_blocks"]
+        for s in ss:
+            m.session_close(s)
+        for i, u in enumerate(suffixes):
+            t = m.session_fork(0, P)
+            m.session_prefill(t, u)
+            for step in range(2):
+                am1, lg1 = m.decode_batch([t], nxt[step, i:i + 1], logits=True)
+                assert np.array_equal(lg1[0], got[step][i]), (i, step, float(np.abs(lg1[0] - got[step][i]).max()))
+            m.session_close(t)
+
+
 @pytest.mark.parametrize("n", [2, 5, 16])
 def test_moe_grouped_batch_equals_single_decodes(gpu, synth_dir, n):
     """Batched MoE decode groups the tokens per expert (inside the step
