@@ -521,11 +521,12 @@ static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int 
     return (cudaError_t)fbk_gemm_unit_reduce(&g, part, n_units, T, st);
 }
 
-// Token tile by call size: up to 64 tokens (batched decode, short prompts)
-// the weight stream bounds the time, so 16- or 32-token tiles with four
-// stages in flight (33-64 tokens: two 32-token tiles beat one 64-token tile,
-// 14336x4096 Q6_K at 64 tokens 203 -> 160 us); longer prompts use 64-token
-// tiles (each weight step serves more tokens) double-buffered.
+// Token tile by call size: up to 32 tokens 16- or 32-token tiles with four
+// stages in flight; longer prompts 64-token tiles (each weight step serves
+// more tokens) double-buffered. At 33-64 tokens the 64-token tile (with the
+// K split filling the device) wins on mid-sized matrices (Q6_K at 64 tokens:
+// 18944x3584 221 -> 158 us, 14336x4096 181 -> 157 us) but not on very wide
+// or narrow ones (152064 rows 909 vs 945 us, 512 rows 19 vs 25 us).
 template <int W>
 static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, int* err, float* part, size_t pf,
                                cudaStream_t st) {
@@ -533,10 +534,12 @@ static cudaError_t launch_gemm(const GemvSeg& g, const ActQ& a, int K, int T, in
         const char* e = getenv("FISH_GEMM_BN");
         return e ? atoi(e) : 0;
     }();
-    const int bn = bn_env == 16 || bn_env == 32 || bn_env == 64 ? bn_env : (T <= 16 ? 16 : T <= 64 ? 32 : 64);
+    static const int sms = gemm_num_sms();
+    const bool mid = g.rows >= 2048 && g.rows <= 128 * sms && part;
+    const int bn = bn_env == 16 || bn_env == 32 || bn_env == 64 ? bn_env
+                                                              : (T <= 16 ? 16 : T <= 32 ? 32 : (T <= 64 && !mid) ? 32 : 64);
     // narrow token tiles on matrices with fewer 64-row tiles than SMs:
     // 32-row tiles, so twice the CTAs share the long K loop
-    static const int sms = gemm_num_sms();
     const bool rows32 = bn < 64 && (g.rows + 63) / 64 < sms;
     if (bn == 16) return rows32 ? launch_gemm_tile<W, 32, 16, 4, 1, 1>(g, a, K, T, err, part, pf, st)    // 4 warps of 16 x 8
                                 : launch_gemm_tile<W, 64, 16, 4, 1, 1>(g, a, K, T, err, part, pf, st);   // 8 warps of 16 x 8
