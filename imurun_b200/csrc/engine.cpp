@@ -1221,67 +1221,71 @@ bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t*
                          std::string* err) {
     const Config& c = cfg_;
     const int K = c.n_experts_per_tok, F = c.n_ff_exp, E = c.n_embd;
-    const int nchunk = (T + 3) / 4;
-    if (nel * T > grp_rows_ || nchunk > kMaxBatch / 4) { if (err) *err = "MoE grouping: batch too large"; return false; }
-    CKP(PC_OTHER, 0, fbk_moe_group(esel, T, K, nel, grp_src_, grp_pos_, grp_count_, chunk_exp_, nchunk, stream_));
+    // 4-row slots, packed per expert; in a captured graph every slot is a
+    // launch whose expert is read on the device (idle slots exit at once)
+    const int nslot = fbk_moe_slots(T, K, nel), rows = 4 * nslot;
+    if (rows > grp_rows_ || nslot > nel * (kMaxBatch / 4)) { if (err) *err = "MoE grouping: batch too large"; return false; }
+    CKP(PC_OTHER, 0, fbk_moe_group(esel, T, K, nel, grp_src_, grp_pos_, grp_count_, chunk_exp_, nslot, stream_));
     ActQ src = a, ga = gact_, gf = gact_;
     src.K = E;
     ga.K = E;
     gf.K = F;
-    CKP(PC_OTHER, 0, fbk_moe_gather(&src, &ga, grp_src_, K, nel * T, E, stream_));
+    CKP(PC_OTHER, 0, fbk_moe_gather(&src, &ga, grp_src_, K, rows, E, stream_));
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     CK(cudaStreamIsCapturing(stream_, &cs));
     const bool exact = cs == cudaStreamCaptureStatusNone;
-    std::vector<int32_t> cnt((size_t)nel, 0);
+    std::vector<int32_t> cnt((size_t)nel, 0), row0((size_t)nel, 0);
     if (exact) {
         CK(cudaMemcpyAsync(cnt.data(), grp_count_, sizeof(int32_t) * nel, cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
+        for (int e = 1; e < nel; ++e) row0[e] = row0[e - 1] + 4 * ((cnt[e - 1] + 3) / 4);   // the kernel's packing
     }
+    const int nt4 = std::min(4, T);   // an expert has at most T rows: a slot's rows lie in its first nt4
     auto view = [](const DevW& w, int e) {
         DevW v = w;
         v.d = w.d + (size_t)e * w.expert_bytes;
         v.n_exp = 1;
         return v;
     };
-    for (int e = 0; e < nel; ++e) {
-        const int r0 = e * T;
-        if (exact) {
+    if (exact) {
+        for (int e = 0; e < nel; ++e) {
             if (!cnt[e]) continue;
+            const int r0 = row0[e];
             const DevW gw = view(L.gate_exps, e), uw = view(L.up_exps, e);
             const DevW* ws[2] = {&gw, &uw};
             float* ys[2] = {gg_ + (size_t)r0 * F, gu_ + (size_t)r0 * F};
             const int lds[2] = {F, F};
             if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, r0, E), cnt[e], EPI_STORE, err)) return false;
-        } else {
-            for (int ch = 0; ch < nchunk; ++ch) {
-                const int nt = std::min(4, T - 4 * ch), rr = r0 + 4 * ch;
-                const DevW* ws[2] = {&L.gate_exps, &L.up_exps};
-                float* ys[2] = {gg_ + (size_t)rr * F, gu_ + (size_t)rr * F};
-                const int lds[2] = {F, F};
-                if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, rr, E), nt, EPI_STORE, err, nullptr, false,
-                                chunk_exp_ + e * nchunk + ch))
-                    return false;
-            }
+        }
+    } else {
+        for (int sl = 0; sl < nslot; ++sl) {
+            const int rr = 4 * sl;
+            const DevW* ws[2] = {&L.gate_exps, &L.up_exps};
+            float* ys[2] = {gg_ + (size_t)rr * F, gu_ + (size_t)rr * F};
+            const int lds[2] = {F, F};
+            if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, rr, E), nt4, EPI_STORE, err, nullptr, false,
+                            chunk_exp_ + sl))
+                return false;
         }
     }
-    CKP(PC_NORMQ, 0, fbk_silu_mul_quant(gg_, F, gu_, F, nel * T, F, probe_ ? probe_h_ : nullptr, F, &gf, want32_f_,
+    CKP(PC_NORMQ, 0, fbk_silu_mul_quant(gg_, F, gu_, F, rows, F, probe_ ? probe_h_ : nullptr, F, &gf, want32_f_,
                                         wantk_f_, stream_));
-    if (probe_ && !probe_grouped(3, gf, nel * T, T * K, F, err)) return false;
-    for (int e = 0; e < nel; ++e) {
-        const int r0 = e * T;
-        if (exact) {
+    if (probe_ && !probe_grouped(3, gf, rows, T * K, F, err)) return false;
+    if (exact) {
+        for (int e = 0; e < nel; ++e) {
             if (!cnt[e]) continue;
+            const int r0 = row0[e];
             const DevW dw = view(L.down_exps, e);
             if (!gemv(dw, act_row(gf, r0, F), cnt[e], geo_ + (size_t)r0 * E, E, nullptr, EPI_STORE, nullptr, 0, nullptr,
                       err))
                 return false;
-        } else {
-            for (int ch = 0; ch < nchunk; ++ch) {
-                const int nt = std::min(4, T - 4 * ch), rr = r0 + 4 * ch;
-                if (!gemv(L.down_exps, act_row(gf, rr, F), nt, geo_ + (size_t)rr * E, E, nullptr, EPI_STORE, nullptr, 0,
-                          chunk_exp_ + e * nchunk + ch, err))
-                    return false;
-            }
+        }
+    } else {
+        for (int sl = 0; sl < nslot; ++sl) {
+            const int rr = 4 * sl;
+            if (!gemv(L.down_exps, act_row(gf, rr, F), nt4, geo_ + (size_t)rr * E, E, nullptr, EPI_STORE, nullptr, 0,
+                      chunk_exp_ + sl, err))
+                return false;
         }
     }
     CKP(PC_OTHER, 0, fbk_moe_combine_grouped(out, E, geo_, grp_pos_, wsel_, T, K, E, stream_));

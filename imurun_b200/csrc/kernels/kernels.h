@@ -231,10 +231,13 @@ extern "C" {
 int fbk_router_f32(const uint8_t* w, size_t ws, const float* x, int ldx, int T, int E, int NE, float* out, int ldo,
                    cudaStream_t st);
 // Expert grouping of a batched MoE step (misc.cu): rows routed to each local
-// expert gathered into grouped rows e T + j, per-chunk expert ids for GEMV
-// launches of 4 rows, and the weighted combine read back through grp_pos.
+// expert packed into consecutive 4-row slots (expert e from slot
+// sum_{e' < e} ceil(count_e' / 4)), the expert of every slot for GEMV
+// launches of 4 rows (-1 past the used slots), and the weighted combine read
+// back through grp_pos. nslot >= fbk_moe_slots(T, K, nel).
 int fbk_moe_group(const int32_t* esel, int T, int K, int nel, int32_t* grp_src, int32_t* grp_pos, int32_t* grp_count,
-                  int32_t* chunk_exp, int nchunk, cudaStream_t st);
+                  int32_t* chunk_exp, int nslot, cudaStream_t st);
+int fbk_moe_slots(int T, int K, int nel);
 int fbk_moe_gather(const fb::ActQ* src, const fb::ActQ* dst, const int32_t* grp_src, int ksel, int n_rows, int K,
                    cudaStream_t st);
 int fbk_moe_combine_grouped(float* x, int ldx, const float* eo, const int32_t* grp_pos, const float* wsel, int T, int K,
