@@ -1316,10 +1316,13 @@ __global__ void __launch_bounds__(256) k_attn_prefix_tc(const float* __restrict_
                 tc_store_warp<KS>(wm, wl, wo, w, lane, m_r, l_r, acc);
             }
         }
-        __syncthreads();
-        if (tv && !more) tc_merge_warps(wm, wl, wo, cm, cl, co, G, D, stid, 128);
-        __syncthreads();
+        // the two token slots share only the (read-only) prefix tiles: each
+        // merges on its own 128-thread barrier (tv and more are the same for
+        // the slot's four warps)
         if (tv && !more) {
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + slot) : "memory");   // warp partials written
+            tc_merge_warps(wm, wl, wo, cm, cl, co, G, D, stid, 128);
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + slot) : "memory");   // the CTA partial written
             float* pp = part + ((size_t)(t * HKV + hk) * C + r) * dec_part_floats(G, D);
             if (stid < G) { pp[stid] = cm[stid]; pp[8 + stid] = cl[stid]; }
             for (int idx = stid; idx < G * D; idx += 128) pp[16 + idx] = co[(idx / D) * kMaxD + idx % D];

@@ -96,7 +96,7 @@ struct StageLayout {
     static constexpr int bytes = d_off + BN * 8 * 4;
 };
 
-template <int W, int BM, int BN, int NS, int FT, int JT>
+template <int W, int BM, int BN, int NS, int FT, int JT, bool SPLIT>
 __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, ActQ a, int K, int T, int* err, int upc,
                                                                     float* part) {
     using L = StageLayout<W, BM, BN>;
@@ -110,10 +110,11 @@ __global__ void __launch_bounds__(BM * BN / (4 * FT * JT)) k_gemm_q(GemvSeg g, A
     const int row0 = blockIdx.x * kBM, t0 = blockIdx.y * kBN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int wr = warp % WRN, wc = warp / WRN;   // rows 16 FT wr .., tokens 8 JT wc ..
-    // K split (upc > 0): this CTA takes the half-group units (4 blocks)
+    // K split (SPLIT, compiled apart so the unsplit kernel keeps its
+    // registers): this CTA takes the half-group units (4 blocks)
     // [z upc, (z + 1) upc) and writes each unit's tree value to
     // part[(unit * T + t) * rows + row] for k_gemm_unit_reduce
-    const bool split = upc > 0;
+    constexpr bool split = SPLIT;
     const int sb0 = split ? 4 * (int)blockIdx.z * upc : 0;
     const int nsteps = split ? min(K / 256 - sb0, 4 * upc) : K / 256;
     const uint8_t* wend = g.w + g.w_bytes;
@@ -491,13 +492,20 @@ static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int 
                                     size_t part_floats, cudaStream_t st) {
     constexpr size_t smem = NS * (size_t)StageLayout<W, BM, BN>::bytes;
     constexpr int threads = BM * BN / (4 * FT * JT);   // 32 x warps
-    static cudaError_t attr = cudaFuncSetAttribute(k_gemm_q<W, BM, BN, NS, FT, JT>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static cudaError_t attr = [] {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_q<W, BM, BN, NS, FT, JT, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_gemm_q<W, BM, BN, NS, FT, JT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem);
+        return e;
+    }();
     if (attr != cudaSuccess) return attr;
     // resident CTAs the device holds at once
     static const int capacity = [] {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemm_q<W, BM, BN, NS, FT, JT>, threads, smem) != cudaSuccess)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemm_q<W, BM, BN, NS, FT, JT, true>, threads, smem) !=
+            cudaSuccess)
             n = 1;
         return std::max(1, n) * gemm_num_sms();
     }();
@@ -516,8 +524,11 @@ static cudaError_t launch_gemm_tile(const GemvSeg& g, const ActQ& a, int K, int 
             if (grid.z <= 1) upc = 0, grid.z = 1;
         }
     }
-    cudaError_t e = fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT>, grid, dim3(threads), smem, st, g, a, K, T, err, upc, part);
-    if (e != cudaSuccess || !upc) return e;
+    if (!upc) return fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT, false>, grid, dim3(threads), smem, st, g, a, K, T, err, 0,
+                                (float*)nullptr);
+    cudaError_t e = fbk_launch(k_gemm_q<W, BM, BN, NS, FT, JT, true>, grid, dim3(threads), smem, st, g, a, K, T, err, upc,
+                               part);
+    if (e != cudaSuccess) return e;
     return (cudaError_t)fbk_gemm_unit_reduce(&g, part, n_units, T, st);
 }
 
