@@ -4,6 +4,7 @@
 #include <fish/fish_kernels.h>
 
 #include <cuda_fp16.h>
+#include <cuda_profiler_api.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -194,6 +195,8 @@ int fbx_matmul(int type, const void* w, int n_in, int n_out, const float* x, int
     TRY(cudaMemcpy(y, dy.p, sizeof(float) * T * n_out, cudaMemcpyDeviceToHost));
     return 0;
 }
+
+int fbx_profiler(int start) { return (int)(start ? cudaProfilerStart() : cudaProfilerStop()); }
 
 int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch, double* bytes_per_launch) {
     if (!ms_per_launch || n_in <= 0 || n_out <= 0 || T <= 0 || T > kMaxBatch || iters <= 0) return -1;

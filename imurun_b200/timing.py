@@ -3,6 +3,8 @@
     python -m imurun_b200.timing matmul --type 12 --n-in 4096 --n-out 14336 [--tokens 1] [--iters 20]
     python -m imurun_b200.timing attention --pos 575 [--heads 32 --kv-heads 8 --dim 128 --calls 3]
     python -m imurun_b200.timing prefill --tokens 512 [--layers 32]
+    python -m imurun_b200.timing greedy --layers 32 --steps 3 --prompt 512
+    python -m imurun_b200.timing batch --preset qwen7b --prompt 2048 --sessions 64 --suffix 128 [--layers 0]
 
 Runs fbx_time_matmul: 3 warm-up launches, then `iters` launches timed with
 CUDA events, each launch reading a different copy of the weights (>= 512 MB
@@ -92,6 +94,40 @@ def greedy(layers: int, steps: int, prompt: int = 0) -> dict:
     return {"layers": layers, "steps": steps, "ids": [int(v) for v in out], "seconds": round(dt, 5)}
 
 
+def batch(preset: str, prompt: int, sessions: int, suffix: int, layers: int, steps: int = 5) -> dict:
+    """One batched greedy decode step of `sessions` sessions forked from one
+    `prompt`-token random prompt (its KV pages shared), each with its own
+    `suffix` random ids, on the synthetic GGUF of `preset` (`layers` > 0
+    truncates it). Three warm-up steps, `steps` steps each timed with CUDA
+    events on the engine stream (`last_batch_device_ms`), then one more step
+    inside a profiler capture range (fbx_profiler), so that
+    `ncu --profile-from-start off` records exactly one step."""
+    import os
+    from . import synth
+    from .native import Model
+    cfg = synth.preset(preset, layers=layers) if layers else synth.preset(preset)
+    path = synth.cached(cfg, os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
+    rng = np.random.default_rng(1)
+    with Model(path, (prompt + suffix + steps + 64 + 255) // 256 * 256) as m:
+        m.prefill(rng.integers(3, m.vocab, prompt).astype(np.int32), 0)
+        sids = [m.session_fork(0, prompt) for _ in range(sessions)]
+        tok = np.zeros(sessions, np.int32)
+        for i, sid in enumerate(sids):
+            if suffix:
+                tok[i] = int(np.argmax(m.session_prefill(sid, rng.integers(3, m.vocab, suffix).astype(np.int32))))
+        for _ in range(3):
+            tok = m.decode_batch(sids, tok)[0]
+        ms = []
+        for _ in range(steps):
+            tok = m.decode_batch(sids, tok)[0]
+            ms.append(float(json.loads(m.lib.fish_engine_json(m.ctx).decode())["last_batch_device_ms"]))
+        m.lib.fbx_profiler(1)
+        tok = m.decode_batch(sids, tok)[0]
+        m.lib.fbx_profiler(0)
+    return {"preset": preset, "prompt": prompt, "sessions": sessions, "suffix": suffix, "layers": layers or cfg.n_layers,
+            "step_ms": [round(v, 4) for v in ms], "tok_s": round(sessions / (sum(ms) / len(ms) / 1e3), 1)}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -114,7 +150,17 @@ def main() -> None:
     gr.add_argument("--layers", type=int, default=2)
     gr.add_argument("--steps", type=int, default=3)
     gr.add_argument("--prompt", type=int, default=0)
+    bt = sub.add_parser("batch")
+    bt.add_argument("--preset", default="qwen7b")
+    bt.add_argument("--prompt", type=int, default=2048)
+    bt.add_argument("--sessions", type=int, default=64)
+    bt.add_argument("--suffix", type=int, default=128)
+    bt.add_argument("--layers", type=int, default=0)
+    bt.add_argument("--steps", type=int, default=5)
     a = ap.parse_args()
+    if a.cmd == "batch":
+        print(json.dumps(batch(a.preset, a.prompt, a.sessions, a.suffix, a.layers, a.steps)), flush=True)
+        return
     if a.cmd == "prefill":
         print(json.dumps(prefill(a.tokens, a.layers)), flush=True)
         return

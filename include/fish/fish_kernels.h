@@ -81,6 +81,12 @@ FISH_API int fbx_rope(float* q, float* k, int T, int H, int HKV, int D, int rot_
 FISH_API int fbx_time_matmul(int type, int n_in, int n_out, int T, int iters, float* ms_per_launch,
                              double* bytes_per_launch);
 
+/* Marks the start (start != 0) or end of a profiler capture range
+ * (cudaProfilerStart / cudaProfilerStop), for captures of one step with the
+ * profiler set not to record from the program's start. No reference
+ * counterpart. Returns the CUDA error. */
+FISH_API int fbx_profiler(int start);
+
 /* Causal GQA attention like fbx_attention, on DEVICE buffers, allocating
  * nothing. No counterpart in the reference: it serves callers that cannot
  * allocate device memory on the call path (a serving loop that gave all free
