@@ -246,6 +246,7 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     CK(cudaEventCreate(&pe1_));
     use_graphs_ = env_int("FISH_NO_GRAPHS", 0) == 0;
     no_fuse_ = env_int("FISH_NO_FUSE", 0) != 0;
+    prefill_simt_ = env_int("FISH_ATTN_PREFILL_SIMT", 0) != 0;
     fbk_set_pdl(env_int("FISH_NO_PDL", 0) == 0 ? 1 : 0);
     gguf_ = Gguf::open(path, err);
     if (!gguf_) return false;
@@ -1333,6 +1334,10 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
         } else {
         CKP(PC_ROPE, 0, fbk_rope_append(q_, Q, k_, v_, KV, T, H, HKV, D, c.rot_dim, c.neox ? 1 : 0, rope_cos_,
                                         rope_sin_, kv, li, stream_));
+        // one sequence (a prefill), fp16 cache: the tensor-core kernel over all T tokens
+        if (!distinct && kv.f16 && !prefill_simt_) {
+            CKP(PC_ATTN, 0, fbk_attention_prefill(q_, Q, T, H, HKV, D, scale, kv, li, attn_, Q, stream_));
+        } else
         for (int t0 = 0; t0 < T; t0 += att_chunk_) {
             const int nt = std::min(att_chunk_, T - t0);
             KvView kvc = kv;

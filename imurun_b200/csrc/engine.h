@@ -331,6 +331,7 @@ private:
     bool tp_gather_logits(int rows, float* logits_dev, std::string* err);
     bool use_graphs_ = true;
     bool no_fuse_ = false;     // FISH_NO_FUSE: separate norm/quant kernels before every GEMV
+    bool prefill_simt_ = false;   // FISH_ATTN_PREFILL_SIMT: prefill attention on the SIMT split-key kernel
     // persistent step
     bool run_step(int sid, int n_steps, int32_t* out_dev, std::string* err);
     int step_state_ = 0;       // 0 not built, 1 ready, -1 unavailable

@@ -355,8 +355,10 @@ struct TestPool {
     }
 };
 
-int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0, int T,
-                  int kv_f16, float* out) {
+// fbx_attention / fbx_attention_prefill: the cache built from host K/V rows,
+// then the split-key kernel (tc = 0) or the tensor-core prefill kernel
+static int attention_host(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0,
+                          int T, int kv_f16, float* out, int tc) {
     if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || (D != 64 && D != 128)) return -1;
     TRY(check_device());
     TestPool tp;
@@ -384,11 +386,25 @@ int fbx_attention(const float* q, const float* k, const float* v, int n_keys, in
     TRY(dout.alloc(sizeof(float) * T * H * D));
     TRY(scratch.alloc(sizeof(float) * sf));
     TRY(cudaMemcpy(dq.p, q, sizeof(float) * T * H * D, cudaMemcpyHostToDevice));
-    TRY(fbk_attention(dq.as<float>(), H * D, T, H, HKV, D, 1.0f / std::sqrt((float)D), tp.kv, 0, dout.as<float>(), H * D,
-                      scratch.as<float>(), sf, pos0 + T, nullptr));
+    if (tc)
+        TRY(fbk_attention_prefill(dq.as<float>(), H * D, T, H, HKV, D, 1.0f / std::sqrt((float)D), tp.kv, 0,
+                                  dout.as<float>(), H * D, nullptr));
+    else
+        TRY(fbk_attention(dq.as<float>(), H * D, T, H, HKV, D, 1.0f / std::sqrt((float)D), tp.kv, 0, dout.as<float>(),
+                          H * D, scratch.as<float>(), sf, pos0 + T, nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(out, dout.p, sizeof(float) * T * H * D, cudaMemcpyDeviceToHost));
     return 0;
+}
+
+int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0, int T,
+                  int kv_f16, float* out) {
+    return attention_host(q, k, v, n_keys, H, HKV, D, pos0, T, kv_f16, out, 0);
+}
+
+int fbx_attention_prefill(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0,
+                          int T, float* out) {
+    return attention_host(q, k, v, n_keys, H, HKV, D, pos0, T, 1, out, 1);
 }
 
 int fbx_attention_decode(const float* q, const float* k_cache, const float* v_cache, const float* k_new,

@@ -1330,6 +1330,217 @@ __global__ void __launch_bounds__(256) k_attn_prefix_tc(const float* __restrict_
     }
 }
 
+// ================================================================ prefill, tensor cores (fp16 KV)
+// Causal attention for the T query tokens of one sequence (a prefill or a
+// session's suffix): CTA = (16 consecutive query tokens, kv head); warp g
+// takes query head g of the kv head's group, its 16 tokens as the MMA rows.
+// 64-key K/V tiles of the sequence's pages come in by cp.async into a
+// two-stage ring (rows padded to D + 8 halves); per tile the scores
+// S[16 tokens][64 keys] = Q.K^T and O += P.V run on mma.sync m16n8k16 (f16
+// in, f32 accumulation) in the register layout where the score accumulator
+// is the next MMA's P operand; q and p are split into f16 high and low parts
+// (x = hi + lo to about 2^-22 relative), both multiplied, so the products
+// keep f32 accuracy; K and V are the cache's f16 values. Online softmax per
+// row, causal mask j <= pos(token).
+constexpr int kPfKeys = 64;
+constexpr int kPfRows = 16;
+
+template <int D>
+struct PfSmem {
+    static constexpr int RS = D + 8;                        // padded row (halves)
+    static constexpr size_t tile = (size_t)kPfKeys * RS;    // halves of one K or V tile
+    static constexpr size_t off_k = 0;                      // [2 stages][64][RS]
+    static constexpr size_t off_v = off_k + 2 * tile * 2;
+    static constexpr size_t bytes = off_v + 2 * tile * 2;
+};
+
+__device__ __forceinline__ void pf_cp16(void* dst, const void* src, bool valid) {
+    const int n = valid ? 16 : 0;   // zero fill past the sequence
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void pf_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pf_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(32 * kMaxG) k_attn_prefill_tc(const float* __restrict__ q, int ldq, int T, int H,
+                                                                 int HKV, float scale, KvView kv, int layer,
+                                                                 float* __restrict__ out, int ldo) {
+    using L = PfSmem<D>;
+    constexpr int RS = L::RS, KS = D / 16, DN = D / 8;
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int G = H / HKV, hk = blockIdx.y, t0 = blockIdx.x * kPfRows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+    const int nth = 32 * G;
+    __half* sk = reinterpret_cast<__half*>(smem + L::off_k);
+    __half* sv = reinterpret_cast<__half*>(smem + L::off_v);
+    const int seq = kv.tok_seq[t0];
+    const int tlast = min(T, t0 + kPfRows) - 1;
+    const int pos_max = kv.tok_pos[tlast];
+    const int n_tiles = (pos_max + kPfKeys) / kPfKeys;
+    // this thread's two rows (tokens gid, gid + 8 of the tile) and their positions
+    const int ta = t0 + gid, tb = t0 + gid + 8;
+    const int pa = ta < T ? kv.tok_pos[ta] : -1, pb = tb < T ? kv.tok_pos[tb] : -1;
+    // K and V rows of key tile kt (keys 64 kt ..) into stage st; rows past
+    // pos_max are zero-filled (and masked below)
+    auto load_tile = [&](int kt, int st) {
+        constexpr int CH = D / 8;   // 16-byte chunks per row
+        for (int i = tid; i < kPfKeys * CH; i += nth) {
+            const int rr = i / CH, c = i % CH, j = kt * kPfKeys + rr;
+            const bool ok = j <= pos_max;
+            size_t off = 0;
+            if (ok) {
+                int page = kv.pt[(size_t)seq * kv.pt_stride + j / kv.page_size];
+                if (page < 0 || page >= kv.n_pages) {
+                    if (kv.err) atomicExch(kv.err, 5);
+                    page = 0;
+                }
+                off = (size_t)page * kv.page_stride + (size_t)layer * kv.layer_stride + (size_t)hk * kv.head_stride +
+                      (size_t)(j % kv.page_size) * D + 8 * c;
+            }
+            pf_cp16(sk + (size_t)st * L::tile + (size_t)rr * RS + 8 * c, reinterpret_cast<const __half*>(kv.k) + off, ok);
+            pf_cp16(sv + (size_t)st * L::tile + (size_t)rr * RS + 8 * c, reinterpret_cast<const __half*>(kv.v) + off, ok);
+        }
+        pf_commit();
+    };
+    load_tile(0, 0);
+
+    // q of this warp's head for the two rows as A fragments, hi and lo parts
+    const int h = hk * G + warp;
+    uint32_t qh[KS][4], ql[KS][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = (e & 1) ? tb : ta, d = 16 * ks + 2 * tig + 8 * (e >> 1);
+            const bool ok = row < T;
+            const float x0 = ok ? q[(size_t)row * ldq + (size_t)h * D + d] : 0.0f;
+            const float x1 = ok ? q[(size_t)row * ldq + (size_t)h * D + d + 1] : 0.0f;
+            float h0, l0, h1, l1;
+            split_h(x0, h0, l0);
+            split_h(x1, h1, l1);
+            qh[ks][e] = pack_h2(h0, h1);
+            ql[ks][e] = pack_h2(l0, l1);
+        }
+    }
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+    float o[DN][4];
+#pragma unroll
+    for (int dn = 0; dn < DN; ++dn)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[dn][c] = 0.0f;
+
+    for (int kt = 0; kt < n_tiles; ++kt) {
+        if (kt + 1 < n_tiles) {
+            load_tile(kt + 1, (kt + 1) & 1);
+            pf_wait<1>();
+        } else {
+            pf_wait<0>();
+        }
+        __syncthreads();
+        const __half* K = sk + (size_t)(kt & 1) * L::tile;
+        const __half* V = sv + (size_t)(kt & 1) * L::tile;
+        // S[16 rows][64 keys] in 8 n-tiles of 8 keys
+        float s[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) s[nt][c] = 0.0f;
+        const int mi = lane >> 3;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b[4];   // b0, b1 of n-tiles 2 np and 2 np + 1
+                ldsm_x4(b, K + (size_t)(16 * np + (mi >> 1) * 8 + (lane & 7)) * RS + 16 * ks + (mi & 1) * 8);
+                mma16816(s[2 * np], qh[ks], b[0], b[1]);
+                mma16816(s[2 * np], ql[ks], b[0], b[1]);
+                mma16816(s[2 * np + 1], qh[ks], b[2], b[3]);
+                mma16816(s[2 * np + 1], ql[ks], b[2], b[3]);
+            }
+        }
+        // scale, causal mask, online softmax per row (the row's 4 lanes hold its 64 keys)
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int j = kt * kPfKeys + 8 * nt + 2 * tig + (c & 1);
+                const int pr = (c >> 1) ? pb : pa;
+                s[nt][c] = j <= pr ? __fmul_rn(s[nt][c], scale) : -INFINITY;
+                mx[c >> 1] = fmaxf(mx[c >> 1], s[nt][c]);
+            }
+        float corr[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 1));
+            mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 2));
+            const float mn = fmaxf(m_r[e], mx[e]);
+            corr[e] = m_r[e] == -INFINITY ? 0.0f : expf(m_r[e] - mn);
+            m_r[e] = mn;
+        }
+        float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float p = s[nt][c] == -INFINITY ? 0.0f : expf(s[nt][c] - m_r[c >> 1]);
+                s[nt][c] = p;
+                sum[c >> 1] += p;
+            }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            sum[e] += __shfl_xor_sync(0xffffffffu, sum[e], 1);
+            sum[e] += __shfl_xor_sync(0xffffffffu, sum[e], 2);
+            l_r[e] = __fmaf_rn(l_r[e], corr[e], sum[e]);
+        }
+#pragma unroll
+        for (int dn = 0; dn < DN; ++dn) {
+            o[dn][0] = __fmul_rn(o[dn][0], corr[0]);
+            o[dn][1] = __fmul_rn(o[dn][1], corr[0]);
+            o[dn][2] = __fmul_rn(o[dn][2], corr[1]);
+            o[dn][3] = __fmul_rn(o[dn][3], corr[1]);
+        }
+        // O += P.V: P's accumulator fragments of n-tiles 2 kk, 2 kk + 1 are
+        // the A fragment of k-step kk (keys 16 kk ..), hi and lo parts
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t ph[4], pl[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float* src = s[2 * kk + (e >> 1)] + 2 * (e & 1);
+                float h0, l0, h1, l1;
+                split_h(src[0], h0, l0);
+                split_h(src[1], h1, l1);
+                ph[e] = pack_h2(h0, h1);
+                pl[e] = pack_h2(l0, l1);
+            }
+#pragma unroll
+            for (int dp = 0; dp < DN / 2; ++dp) {
+                uint32_t b[4];   // b0, b1 of d n-tiles 2 dp and 2 dp + 1
+                ldsm_x4_t(b, V + (size_t)(16 * kk + (mi & 1) * 8 + (lane & 7)) * RS + 16 * dp + (mi >> 1) * 8);
+                mma16816(o[2 * dp], ph, b[0], b[1]);
+                mma16816(o[2 * dp], pl, b[0], b[1]);
+                mma16816(o[2 * dp + 1], ph, b[2], b[3]);
+                mma16816(o[2 * dp + 1], pl, b[2], b[3]);
+            }
+        }
+        __syncthreads();   // the stage is read; the next load may overwrite it
+    }
+    // O / l for the two rows
+#pragma unroll
+    for (int dn = 0; dn < DN; ++dn)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int row = (c >> 1) ? tb : ta;
+            if (row >= T) continue;
+            const float l = l_r[c >> 1];
+            out[(size_t)row * ldo + (size_t)h * D + 8 * dn + 2 * tig + (c & 1)] = l > 0.0f ? o[dn][c] / l : 0.0f;
+        }
+}
+
 }  // namespace fb
 
 using namespace fb;
@@ -1534,6 +1745,26 @@ extern "C" size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D)
     return (size_t)T * HKV * 16 * dec_part_floats(H / HKV, D);
 }
 extern "C" int fbk_attention_prefix_max_blocks(void) { return 16 * kPreMaxBlocks; }
+
+template <int D>
+static int launch_prefill_tc(const float* q, int ldq, int T, int H, int HKV, float scale, KvView kv, int layer,
+                             float* out, int ldo, cudaStream_t st) {
+    static const cudaError_t attr = cudaFuncSetAttribute(k_attn_prefill_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         (int)PfSmem<D>::bytes);
+    if (attr != cudaSuccess) return (int)attr;
+    return (int)fbk_launch(k_attn_prefill_tc<D>, dim3((T + kPfRows - 1) / kPfRows, HKV), dim3(32 * (H / HKV)),
+                           PfSmem<D>::bytes, st, q, ldq, T, H, HKV, scale, kv, layer, out, ldo);
+}
+
+extern "C" int fbk_attention_prefill(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv,
+                                     int layer, float* out, int ldo, cudaStream_t st) {
+    if (T <= 0) return 0;
+    const int G = H / HKV;
+    if (!kv.f16 || G > kMaxG || G * HKV != H || (D != 64 && D != 128) || kv.page_size != 16)
+        return (int)cudaErrorInvalidValue;
+    if (D == 128) return launch_prefill_tc<128>(q, ldq, T, H, HKV, scale, kv, layer, out, ldo, st);
+    return launch_prefill_tc<64>(q, ldq, T, H, HKV, scale, kv, layer, out, ldo, st);
+}
 // Floats of the warp-state scratch of the shared-prefix kernel for T tokens.
 extern "C" size_t fbk_attention_prefix_state_floats(int T, int HKV, int D) {
     return (size_t)T * HKV * 16 * kTcWarps * 32 * kStateFloats(D / 16);

@@ -188,6 +188,12 @@ int fbk_attention_decode(const float* q, int ldq, const float* k, const float* v
                          int layer, float* out, int ldo, float* part, size_t part_floats, const int* pre, float* pstate,
                          size_t pstate_floats, cudaStream_t st);
 size_t fbk_attention_decode_part_floats(int T, int H, int HKV, int D);
+// Prefill attention on tensor cores for the T tokens of ONE sequence at
+// consecutive positions (kv.tok_seq / kv.tok_pos of token 0 ..), whose K/V
+// rows are already in the fp16 cache (RoPE applied by fbk_rope_append): a
+// CTA per (16 tokens, kv head), no scratch. D 64 or 128, G <= 8, page 16.
+int fbk_attention_prefill(const float* q, int ldq, int T, int H, int HKV, int D, float scale, KvView kv, int layer,
+                          float* out, int ldo, cudaStream_t st);
 size_t fbk_attention_prefix_state_floats(int T, int HKV, int D);
 // Blocks of 64 keys the shared-prefix kernel covers at most (16 key ranks x
 // the blocks a rank keeps resident).

@@ -72,7 +72,7 @@ ABI5_FUNCTIONS = [
 KERNEL_FUNCTIONS = [
     "fbx_quantize_acts", "fbx_rmsnorm", "fbx_matmul", "fbx_block_sums", "fbx_attention", "fbx_rope",
     "fbx_argmax", "fbx_argmax_penalized", "fbx_layer_probe", "fbx_tp_plan", "fbx_moe_localize_host", "fbx_embed", "fbx_time_matmul", "fbx_attention_static", "fbx_attention_decode",
-    "fbx_profiler",
+    "fbx_profiler", "fbx_attention_prefill",
 ]
 
 
@@ -125,6 +125,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "fbx_embed": ([I, P, I, I, P, I, P], I),
         "fbx_time_matmul": ([I, I, I, I, I, P, P], I),
         "fbx_profiler": ([I], I),
+        "fbx_attention_prefill": ([P, P, P, I, I, I, I, I, I, P], I),
         "fbx_attention_static": ([P, P, P, I, I, I, I, I, I, I, P, P], I),
         "fbx_attention_decode": ([P, P, P, P, P, I, I, I, I, I, I, F, I, P, P, P], I),
     }

@@ -50,6 +50,13 @@ FISH_API int fbx_block_sums(int type, const void* w, int n_in, int n_out, const 
 FISH_API int fbx_attention(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D,
                            int pos0, int T, int kv_f16, float* out);
 
+/* The same causal attention on the tensor-core prefill kernel the engine
+ * uses for a prompt (fp16 cache; the T queries one sequence's tokens at
+ * positions pos0..pos0+T-1; G = H/HKV <= 8). No reference counterpart beyond
+ * fbx_attention's. */
+FISH_API int fbx_attention_prefill(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D,
+                                   int pos0, int T, float* out);
+
 /* One decode step of one sequence with the fused kernel the engine uses for
  * single-token steps: q [H*D] and the new k/v [HKV*D] are the raw
  * projections of the token at position pos; RoPE (reference ops.cpp:126-156,

@@ -248,6 +248,33 @@ def test_attention_vs_oracle(lib, oracle, f16, T, pos0, H, HKV, D):
     assert np.max(np.abs(out - want)) <= 2e-5 * max(1.0, np.max(np.abs(want)))
 
 
+@pytest.mark.parametrize("T,pos0,H,HKV,D", [(5, 0, 8, 4, 64), (16, 40, 32, 8, 128), (37, 120, 28, 4, 128),
+                                            (70, 1000, 64, 8, 128), (256, 256, 32, 8, 128), (33, 7, 8, 8, 64),
+                                            (19, 63, 16, 2, 128)])
+def test_attention_prefill_tc_vs_oracle(lib, oracle, T, pos0, H, HKV, D):
+    """The tensor-core prefill kernel (16 tokens x kv head per CTA, 64-key
+    tiles, q and p as f16 hi + lo parts) against the oracle's attention on the
+    same fp16 cache, with the attention tests' bar (2e-5 of the output scale):
+    partial query tiles, key tiles cut by the causal mask, G = 1 .. 8."""
+    rng = np.random.default_rng(T + pos0 + H + 5)
+    n_keys = pos0 + T
+    q = rng.standard_normal((T, H * D)).astype(np.float32)
+    k = rng.standard_normal((n_keys, HKV * D)).astype(np.float32)
+    v = rng.standard_normal((n_keys, HKV * D)).astype(np.float32)
+    out = np.zeros((T, H * D), np.float32)
+    assert lib.fbx_attention_prefill(_p(q), _p(k), _p(v), n_keys, H, HKV, D, pos0, T, _p(out)) == 0
+    k16, v16 = oracle.fp16_round(k), oracle.fp16_round(v)
+    want = oracle.attention(q, k16, v16, H, HKV, D, pos0, T, 1.0 / np.sqrt(D))
+    assert np.max(np.abs(out - want)) <= 2e-5 * max(1.0, np.max(np.abs(want)))
+    # a token's row does not depend on the other tokens of the call (what a
+    # prefix-cache hit relies on): the last rows alone, same cache, same bits
+    a = T // 2
+    tail = np.zeros((T - a, H * D), np.float32)
+    qt = np.ascontiguousarray(q[a:])
+    assert lib.fbx_attention_prefill(_p(qt), _p(k), _p(v), n_keys, H, HKV, D, pos0 + a, T - a, _p(tail)) == 0
+    assert np.array_equal(tail, out[a:])
+
+
 @pytest.mark.parametrize("f16", [0, 1])
 @pytest.mark.parametrize("pos,H,HKV,D,rot,neox", [(0, 8, 4, 64, 64, 0), (37, 32, 8, 128, 128, 0),
                                                   (200, 28, 4, 128, 128, 1), (1000, 64, 8, 128, 128, 0),
