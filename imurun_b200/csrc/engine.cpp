@@ -1222,11 +1222,13 @@ bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t*
                          std::string* err) {
     const Config& c = cfg_;
     const int K = c.n_experts_per_tok, F = c.n_ff_exp, E = c.n_embd;
-    // 4-row slots, packed per expert; in a captured graph every slot is a
-    // launch whose expert is read on the device (idle slots exit at once)
-    const int nslot = fbk_moe_slots(T, K, nel), rows = 4 * nslot;
+    // slots of S rows (the streamed GEMV's token count: 8, or 4 for small
+    // batches), packed per expert; in a captured graph every slot is a launch
+    // whose expert is read on the device (idle slots exit at once)
+    const int S = T > 4 ? 8 : 4;
+    const int nslot = fbk_moe_slots(T, K, nel, S), rows = S * nslot;
     if (rows > grp_rows_ || nslot > nel * (kMaxBatch / 4)) { if (err) *err = "MoE grouping: batch too large"; return false; }
-    CKP(PC_OTHER, 0, fbk_moe_group(esel, T, K, nel, grp_src_, grp_pos_, grp_count_, chunk_exp_, nslot, stream_));
+    CKP(PC_OTHER, 0, fbk_moe_group(esel, T, K, nel, grp_src_, grp_pos_, grp_count_, chunk_exp_, nslot, S, stream_));
     ActQ src = a, ga = gact_, gf = gact_;
     src.K = E;
     ga.K = E;
@@ -1239,9 +1241,9 @@ bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t*
     if (exact) {
         CK(cudaMemcpyAsync(cnt.data(), grp_count_, sizeof(int32_t) * nel, cudaMemcpyDeviceToHost, stream_));
         CK(cudaStreamSynchronize(stream_));
-        for (int e = 1; e < nel; ++e) row0[e] = row0[e - 1] + 4 * ((cnt[e - 1] + 3) / 4);   // the kernel's packing
+        for (int e = 1; e < nel; ++e) row0[e] = row0[e - 1] + S * ((cnt[e - 1] + S - 1) / S);   // the kernel's packing
     }
-    const int nt4 = std::min(4, T);   // an expert has at most T rows: a slot's rows lie in its first nt4
+    const int nts = std::min(S, T);   // an expert has at most T rows: a slot's rows lie in its first nts
     auto view = [](const DevW& w, int e) {
         DevW v = w;
         v.d = w.d + (size_t)e * w.expert_bytes;
@@ -1260,11 +1262,11 @@ bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t*
         }
     } else {
         for (int sl = 0; sl < nslot; ++sl) {
-            const int rr = 4 * sl;
+            const int rr = S * sl;
             const DevW* ws[2] = {&L.gate_exps, &L.up_exps};
             float* ys[2] = {gg_ + (size_t)rr * F, gu_ + (size_t)rr * F};
             const int lds[2] = {F, F};
-            if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, rr, E), nt4, EPI_STORE, err, nullptr, false,
+            if (!gemv_group(ws, ys, lds, nullptr, 2, act_row(ga, rr, E), nts, EPI_STORE, err, nullptr, false,
                             chunk_exp_ + sl))
                 return false;
         }
@@ -1283,8 +1285,8 @@ bool Engine::moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t*
         }
     } else {
         for (int sl = 0; sl < nslot; ++sl) {
-            const int rr = 4 * sl;
-            if (!gemv(L.down_exps, act_row(gf, rr, F), nt4, geo_ + (size_t)rr * E, E, nullptr, EPI_STORE, nullptr, 0,
+            const int rr = S * sl;
+            if (!gemv(L.down_exps, act_row(gf, rr, F), nts, geo_ + (size_t)rr * E, E, nullptr, EPI_STORE, nullptr, 0,
                       chunk_exp_ + sl, err))
                 return false;
         }

@@ -100,7 +100,7 @@ struct LayerProbe {
     int rows[6] = {}, K[6] = {};
     bool has_k[4] = {}, has_32[4] = {};
 };
-constexpr size_t kProbeChunkBytes = 294912;   // one GEMV launch's image dump (header + 4 tokens at K <= 28672)
+constexpr size_t kProbeChunkBytes = 589824;   // one GEMV launch's image dump (header + 8 tokens at K <= 28672)
 constexpr int kXChunkBytes = 272;             // image bytes per 256 int8 values (stream_common.cuh kXChunk)
 
 struct Seq {

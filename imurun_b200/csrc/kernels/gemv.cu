@@ -7,7 +7,7 @@
 // Every integer the reference forms per block (Q4_K sumi and mins, Q6_K sumi,
 // Q8_0 s) is formed whole by one thread (unit_math.cuh) and converted to float
 // once. Two kernels:
-//   k_gemv_stream  quantised rows, T <= 4 (decode). A producer warp streams
+//   k_gemv_stream  quantised rows, T <= 8 (decode). A producer warp streams
 //                  (8-row tile x 2048-value group) stages — one contiguous
 //                  bulk copy each, thanks to the tile-major layout — into a
 //                  ring of shared-memory slots guarded by mbarriers. Eight
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(32 * (kConsumers + 1), NT == 1 ? 2 : 1) k_gemv
     __shared__ int s_tseq;
     __shared__ GemvSeg s_seg[kMaxSeg];
     __shared__ int s_tile0[kMaxSeg + 1];
-    __shared__ unsigned long long s_best[kConsumers][4];
+    __shared__ unsigned long long s_best[kConsumers][kMaxStreamTokens];
     __shared__ long long s_pw, s_cw;   // summed wait cycles (all-CTA tracing)
     const int K = args.K, G = jobs.n_groups, S = jobs.stages;
     int n_tiles = jobs.tile0[0];
@@ -613,20 +613,28 @@ static int stream_smem_optin(StreamKernel k, int dyn) {
     return 0;
 }
 
-template <int NT>
-static int launch_stream(const GemvArgs* a, cudaStream_t st) {
-    static const int want_cps = std::max(1, std::min(4, env_or("FISH_GEMV_CTA_PER_SM", 2)));
-    static int max_smem = 0;   // dynamic shared memory one CTA may take
-    if (!max_smem) {
+// Dynamic shared memory one streamed-GEMV CTA may take (the opt-in maximum
+// less the kernel's static shared memory; 0 when unknown).
+static int stream_max_smem() {
+    static const int v = [] {
         int dev = 0, optin = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+            return 0;
         cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, k_gemv_stream<NT, TM_ALL, -1>) != cudaSuccess) return (int)cudaGetLastError();
-        const int dyn = optin - (int)fa.sharedSizeBytes;
-        if (dyn <= 0) return (int)cudaErrorInvalidValue;
-        max_smem = dyn;
-    }
+        if (cudaFuncGetAttributes(&fa, k_gemv_stream<4, TM_ALL, -1>) != cudaSuccess) return 0;
+        return std::max(0, optin - (int)fa.sharedSizeBytes);
+    }();
+    return v;
+}
+
+// The streamed launch of a call of NT tokens: jobs, CTAs, ring stages and
+// shared memory; false when not even the minimum ring fits next to the
+// activation images.
+static bool stream_plan(const GemvArgs* a, int NT, StreamJobs* out, int* ctas_out, size_t* smem_out) {
+    static const int want_cps = std::max(1, std::min(4, env_or("FISH_GEMV_CTA_PER_SM", 2)));
+    const int max_smem = stream_max_smem();
+    if (max_smem <= 0) return false;
     StreamJobs jobs{};
     bool wantk = false, want32 = false;
     int slot = 0;
@@ -643,10 +651,8 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
     for (int s = 0; s < a->nseg; ++s) jobs.tile0[s + 1] = jobs.tile0[s] + (a->seg[s].rows + kTileRows - 1) / kTileRows;
     for (int s = a->nseg; s < kMaxSeg; ++s) jobs.tile0[s + 1] = jobs.tile0[s];
     jobs.pair = a->swiglu ? 1 : 0;
-    if (jobs.pair && (a->nseg != 2 || a->seg[0].rows != a->seg[1].rows || a->seg[0].epi != EPI_STORE))
-        return (int)cudaErrorInvalidValue;
+    if (jobs.pair && (a->nseg != 2 || a->seg[0].rows != a->seg[1].rows || a->seg[0].epi != EPI_STORE)) return false;
     jobs.n_groups = row_groups(a->seg[0].type, a->K);
-    jobs.err = fbk_gemv_error_flag();
     const int n_tiles = jobs.tile0[a->nseg];
     const int unit = jobs.pair ? 2 : 1;
     jobs.n_units = (n_tiles + unit - 1) / unit;
@@ -663,17 +669,30 @@ static int launch_stream(const GemvArgs* a, cudaStream_t st) {
         smem = kHdrBytes + xbytes + part + (size_t)stages * slot;
         if (stages >= kPairs || cps == 1) break;
     }
-    if (stages < kPairs) return (int)cudaErrorInvalidValue;
+    if (stages < kPairs) return false;
     jobs.stages = stages;
+    *out = jobs;
+    *ctas_out = ctas;
+    *smem_out = smem;
+    return true;
+}
+
+template <int NT>
+static int launch_stream(const GemvArgs* a, cudaStream_t st) {
+    StreamJobs jobs{};
+    int ctas = 0;
+    size_t smem = 0;
+    if (!stream_plan(a, NT, &jobs, &ctas, &smem)) return (int)cudaErrorInvalidValue;
+    jobs.err = fbk_gemv_error_flag();
     int tm = 0;
     for (int s = 0; s < a->nseg; ++s) tm |= type_bit(a->seg[s].type);
     const StreamKernel kern = stream_variant<NT>(tm, a->pro.mode);
-    if (const int e = stream_smem_optin(kern, max_smem)) return e;
+    if (const int e = stream_smem_optin(kern, stream_max_smem())) return e;
     return (int)fbk_launch(kern, dim3(ctas), dim3(32 * (kConsumers + 1)), smem, st, *a, jobs);
 }
 
 extern "C" int fbk_gemv_streamable(const GemvArgs* a) {
-    if (a->T <= 0 || a->T > 4 || a->nseg <= 0) return 0;
+    if (a->T <= 0 || a->T > 8 || a->nseg <= 0) return 0;
     const int g0 = row_groups(a->seg[0].type, a->K);
     for (int s = 0; s < a->nseg; ++s) {
         const int t = a->seg[s].type;
@@ -683,11 +702,20 @@ extern "C" int fbk_gemv_streamable(const GemvArgs* a) {
     }
     if (a->K % 8) return 0;
     static const bool stream_off = getenv("FISH_GEMV_DIRECT") != nullptr;
-    return stream_off ? 0 : 1;
+    if (stream_off) return 0;
+    if (a->T > 4) {   // an 8-token launch: its activation images must leave room for the ring
+        StreamJobs j{};
+        int c = 0;
+        size_t m = 0;
+        if (!stream_plan(a, 8, &j, &c, &m)) return 0;
+    }
+    return 1;
 }
 
 extern "C" int fbk_gemv_chunk(const GemvArgs* a) {
     GemvArgs p = *a;
+    p.T = 8;
+    if (fbk_gemv_streamable(&p)) return 8;
     p.T = 4;
     return fbk_gemv_streamable(&p) ? 4 : 8;
 }
@@ -698,6 +726,7 @@ extern "C" int fbk_gemv(const GemvArgs* a, cudaStream_t st) {
     if (fbk_gemv_streamable(a)) {
         if (a->T == 1) return launch_stream<1>(a, st);
         if (a->T == 2) return launch_stream<2>(a, st);
+        if (a->T > 4) return launch_stream<8>(a, st);
         return launch_stream<4>(a, st);
     }
     if (a->pro.mode != PRO_ACT || a->swiglu) return (int)cudaErrorInvalidValue;

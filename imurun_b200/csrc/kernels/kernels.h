@@ -70,7 +70,7 @@ struct GemvArgs {
     ActQ act;               // quantised activations (per type layout)
     const float* xf;        // f32 activations [T][ldxf] for F32/F16 weights
     int ldxf;
-    GemvPro pro;            // streamed kernel only (T <= 4, quantised segments)
+    GemvPro pro;            // streamed kernel only (T <= 8, quantised segments)
     int swiglu;             // streamed kernel, 2 segments of equal rows (gate, up): the output
                             // is h = silu(gate) * up into segment 0's y (src/model.cpp:1501-1506)
     int* err;               // device error flag (nullable): 3 = weight read out of range
@@ -90,9 +90,8 @@ int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T,
 int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                        const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);
-// Tokens per GEMV launch when a call has more than fit one: 4 where the
-// streamed kernel takes the segments (two 4-token launches outrun the direct
-// kernel's 8-token launch several times over), else 8.
+// Tokens per GEMV launch when a call has more than fit one: 8 (the streamed
+// kernel's and the direct kernel's largest token count).
 int fbk_gemv_chunk(const fb::GemvArgs* args);
 // Batched products on the int8 tensor cores (gemm.cu): T >= 16 tokens,
 // quantised planes already built (PRO_ACT), Q4_K / Q6_K / Q8_0 segments,
@@ -237,13 +236,13 @@ extern "C" {
 int fbk_router_f32(const uint8_t* w, size_t ws, const float* x, int ldx, int T, int E, int NE, float* out, int ldo,
                    cudaStream_t st);
 // Expert grouping of a batched MoE step (misc.cu): rows routed to each local
-// expert packed into consecutive 4-row slots (expert e from slot
-// sum_{e' < e} ceil(count_e' / 4)), the expert of every slot for GEMV
-// launches of 4 rows (-1 past the used slots), and the weighted combine read
-// back through grp_pos. nslot >= fbk_moe_slots(T, K, nel).
+// expert packed into consecutive slots of S = 4 or 8 rows (expert e from
+// slot sum_{e' < e} ceil(count_e' / S)), the expert of every slot for GEMV
+// launches of S rows (-1 past the used slots), and the weighted combine read
+// back through grp_pos. nslot >= fbk_moe_slots(T, K, nel, S).
 int fbk_moe_group(const int32_t* esel, int T, int K, int nel, int32_t* grp_src, int32_t* grp_pos, int32_t* grp_count,
-                  int32_t* chunk_exp, int nslot, cudaStream_t st);
-int fbk_moe_slots(int T, int K, int nel);
+                  int32_t* chunk_exp, int nslot, int S, cudaStream_t st);
+int fbk_moe_slots(int T, int K, int nel, int S);
 int fbk_moe_gather(const fb::ActQ* src, const fb::ActQ* dst, const int32_t* grp_src, int ksel, int n_rows, int K,
                    cudaStream_t st);
 int fbk_moe_combine_grouped(float* x, int ldx, const float* eo, const int32_t* grp_pos, const float* wsel, int T, int K,

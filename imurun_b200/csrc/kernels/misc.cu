@@ -325,17 +325,18 @@ extern "C" int fbk_router_f32(const uint8_t* w, size_t ws, const float* x, int l
     return (int)fbk_launch(k_router_f32, dim3((warps + 7) / 8), dim3(256), 0, st, w, ws, x, ldx, T, E, NE, out, ldo);
 }
 
-// Expert grouping for batched MoE steps, packed in 4-row slots. Expert e
-// owns ceil(count_e / 4) consecutive slots from slot s0(e) = sum over e' < e
-// of ceil(count_e' / 4); the rows r = t K + k routed to it (ascending r) take
-// packed rows 4 s0(e) + j: grp_src[4 s0(e) + j] = r (-1 for the slot's pad
-// rows and for unused slots), grp_pos[r] = 4 s0(e) + j (-1 for another
+// Expert grouping for batched MoE steps, packed in slots of S rows (S = 4 or
+// 8, the GEMV launch's token count). Expert e owns ceil(count_e / S)
+// consecutive slots from slot s0(e) = sum over e' < e of ceil(count_e' / S);
+// the rows r = t K + k routed to it (ascending r) take packed rows
+// S s0(e) + j: grp_src[S s0(e) + j] = r (-1 for the slot's pad rows and for
+// unused slots), grp_pos[r] = S s0(e) + j (-1 for another
 // rank's expert), grp_count[e] = count_e, chunk_exp[s] = the expert of slot s
 // (-1 past the used slots: a GEMV given -1 fetches no weights). The caller
 // sizes nslot with a bound on the used slots; dynamic shared memory holds
 // nel + 1 ints.
 __global__ void k_moe_group(const int32_t* __restrict__ esel, int T, int K, int nel, int32_t* grp_src,
-                            int32_t* grp_pos, int32_t* grp_count, int32_t* chunk_exp, int nslot) {
+                            int32_t* grp_pos, int32_t* grp_count, int32_t* chunk_exp, int nslot, int S) {
     extern __shared__ int s_slot[];   // [nel + 1]: first slot of each expert, then the total
     pdl_trigger();
     pdl_wait();
@@ -346,7 +347,7 @@ __global__ void k_moe_group(const int32_t* __restrict__ esel, int T, int K, int 
         int j = 0;
         for (int r = 0; r < n; ++r) j += esel[r] == e;
         grp_count[e] = j;
-        s_slot[e + 1] = (j + 3) / 4;
+        s_slot[e + 1] = (j + S - 1) / S;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -356,21 +357,21 @@ __global__ void k_moe_group(const int32_t* __restrict__ esel, int T, int K, int 
     __syncthreads();
     const int used = min(s_slot[nel], nslot);
     for (int e = threadIdx.x; e < nel; e += blockDim.x) {
-        const int s0 = s_slot[e], s1 = min(s_slot[e + 1], nslot), base = 4 * s0;
+        const int s0 = s_slot[e], s1 = min(s_slot[e + 1], nslot), base = S * s0;
         int j = 0;
         for (int r = 0; r < n; ++r)
             if (esel[r] == e) {
-                const bool fits = base + j < 4 * s1;
+                const bool fits = base + j < S * s1;
                 if (fits) grp_src[base + j] = r;
                 grp_pos[r] = fits ? base + j : -1;
                 ++j;
             }
-        for (int q = base + j; q < 4 * s1; ++q) grp_src[q] = -1;
+        for (int q = base + j; q < S * s1; ++q) grp_src[q] = -1;
         for (int s = s0; s < s1; ++s) chunk_exp[s] = e;
     }
     for (int s = used + threadIdx.x; s < nslot; s += blockDim.x) {
         chunk_exp[s] = -1;
-        for (int q = 0; q < 4; ++q) grp_src[4 * s + q] = -1;
+        for (int q = 0; q < S; ++q) grp_src[S * s + q] = -1;
     }
 }
 
@@ -420,19 +421,20 @@ __global__ void k_moe_combine_grouped(float* x, int ldx, const float* __restrict
 }
 
 extern "C" int fbk_moe_group(const int32_t* esel, int T, int K, int nel, int32_t* grp_src, int32_t* grp_pos,
-                             int32_t* grp_count, int32_t* chunk_exp, int nslot, cudaStream_t st) {
+                             int32_t* grp_count, int32_t* chunk_exp, int nslot, int S, cudaStream_t st) {
     if (T <= 0 || nel <= 0) return 0;
+    if (S != 4 && S != 8) return (int)cudaErrorInvalidValue;
     return (int)fbk_launch(k_moe_group, dim3(1), dim3(256), sizeof(int) * (nel + 1), st, esel, T, K, nel, grp_src,
-                           grp_pos, grp_count, chunk_exp, nslot);
+                           grp_pos, grp_count, chunk_exp, nslot, S);
 }
 
-// Slots a grouping of T tokens x K selections over nel experts can use: each
-// expert takes ceil(c / 4) <= (c + 3) / 4 slots for its c <= T rows, so the
-// sum is at most floor((T K + 3 m) / 4), m = experts with rows <= min(nel, T K),
-// and at most nel ceil(T / 4).
-extern "C" int fbk_moe_slots(int T, int K, int nel) {
+// Slots of S rows a grouping of T tokens x K selections over nel experts can
+// use: each expert takes ceil(c / S) <= (c + S - 1) / S slots for its c <= T
+// rows, so the sum is at most floor((T K + (S - 1) m) / S), m = experts with
+// rows <= min(nel, T K), and at most nel ceil(T / S).
+extern "C" int fbk_moe_slots(int T, int K, int nel, int S) {
     const int tk = T * K, m = nel < tk ? nel : tk;
-    const int a = (tk + 3 * m) / 4, b = nel * ((T + 3) / 4);
+    const int a = (tk + (S - 1) * m) / S, b = nel * ((T + S - 1) / S);
     return a < b ? a : b;
 }
 

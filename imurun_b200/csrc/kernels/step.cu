@@ -472,7 +472,7 @@ __device__ __noinline__ void step_prologue(const GemvArgs* sa, int xk, int x32, 
 // (failure recorded). The job and ring views are built after the prologue so
 // they are not live across it.
 __device__ __forceinline__ int gemv_phase(const StepArgs& A, GemvArgs& s_args, const int* s_tile0, const int* s_meta,
-                                          double* s_part, unsigned long long (*s_best)[4], unsigned long long* cw,
+                                          double* s_part, unsigned long long (*s_best)[kMaxStreamTokens], unsigned long long* cw,
                                           int gbase, int step, int p, int& ev) {
     int t_begin, t_end;
     phase_tiles(s_meta[0], s_args.swiglu, n_tiles_of(s_tile0, s_args.nseg), t_begin, t_end);
@@ -564,7 +564,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(StepArgs A) {
     __shared__ int p_tile0[kMaxSeg + 1];
     __shared__ int p_meta[8];
     __shared__ double s_part[kNormWarps];
-    __shared__ unsigned long long s_best[kConsumers][4];
+    __shared__ unsigned long long s_best[kConsumers][kMaxStreamTokens];
     __shared__ int s_bad;
     volatile int* sbad = &s_bad;
     __shared__ int s_gbase, s_tok;         // consumers: ring stage of the phase, current token

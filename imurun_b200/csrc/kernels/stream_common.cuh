@@ -17,6 +17,7 @@ constexpr int kXChunk = 272;   // bytes per 256 activation int8 (16 B pad: no ba
 constexpr int kConsumers = 8;            // consumer warps: 4 pairs, a pair per stage
 constexpr int kPairs = kConsumers / 2;
 constexpr int kMaxStages = 32;           // ring slots at most
+constexpr int kMaxStreamTokens = 8;      // tokens of one streamed launch at most
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
@@ -777,7 +778,9 @@ __device__ __forceinline__ bool consume_stages_w(const RingView& rg, const JobVi
 // group order, through the epilogue: store/add (+bias), SwiGLU of (gate, up)
 // tile pairs into segment 0, argmax keys (one atomic per token and CTA).
 template <int NT>
-__device__ __forceinline__ void reduce_rows(const JobView& j, const float* part, unsigned long long (*s_best)[4]) {
+__device__ __forceinline__ void reduce_rows(const JobView& j, const float* part,
+                                            unsigned long long (*s_best)[kMaxStreamTokens]) {
+    static_assert(NT <= kMaxStreamTokens, "argmax key slots per warp");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = j.G, T = j.T;
     unsigned long long best[NT];
