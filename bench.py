@@ -586,9 +586,12 @@ def run_prefix(args):
     clocks.start()
     dev_ms = 0.0
     t0 = time.perf_counter()
+    prefix_blocks = 0
     for _ in range(K):
         tok = m.decode_batch(sids, tok)[0]
-        dev_ms += float(json.loads(m.lib.fish_engine_json(m.ctx).decode())["last_batch_device_ms"])
+        eng_step = json.loads(m.lib.fish_engine_json(m.ctx).decode())
+        dev_ms += float(eng_step["last_batch_device_ms"])
+        prefix_blocks = int(eng_step.get("last_batch_prefix_blocks", 0))
     wall_s = time.perf_counter() - t0
     clk = clocks.stop()
     barrier(dist)
@@ -620,8 +623,10 @@ def run_prefix(args):
                 "unique_hbm_frac": round(unique / step_s / 1e9 / peak, 4),
                 "per_session_read_bytes_per_step": round(per_session),
                 "per_session_read_gbs": round(per_session / step_s / 1e9, 1),
-                "attention": "per-session decode attention over each session's pages (the shared prefix pages are "
-                             "read once per session, mostly from L2); no cascade kernel",
+                "attention": "shared-prefix (cascade) attention: the sessions' common 64-key blocks are read once "
+                             "per step for the whole batch, each session's own keys by its rank CTAs, the partials "
+                             "merged per session (same bits as decoding each session alone)",
+                "prefix_blocks_shared": prefix_blocks,
                 "peak_kind": peak_kind,
                 "l2": "inputs larger than L2 (4.4 GB of weights streamed per step)",
             },
