@@ -464,11 +464,21 @@ def sharded_measure(dist, workload: str, K: int, W: int, batch: int = 0, prompt:
     if layers:
         desc += f"; TRUNCATED to {layers} layers (plumbing check, not the config)"
     d = os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")
+    why = None
     if RANK == 0:
         t0 = time.time()
-        p = synth.cached(cfg, d)
-        log(f"[bench] model {p} ({p.stat().st_size / 1e9:.2f} GB, {time.time() - t0:.1f} s)")
-    barrier(dist)
+        try:
+            p = synth.cached(cfg, d)
+            log(f"[bench] model {p} ({p.stat().st_size / 1e9:.2f} GB, {time.time() - t0:.1f} s)")
+        except (RuntimeError, OSError) as e:   # e.g. no room for the synthetic file: every rank skips
+            why = f"synthetic {preset} GGUF not written: {e}"
+            log(f"[bench] {why}")
+    if dist is not None:
+        box = [why]
+        dist.broadcast_object_list(box, src=0)
+        why = box[0]
+    if why:
+        return {"workload": workload, "desc": desc, "unavailable": why}
     path = synth.cached(cfg, d)
     lib = native.load_library()
     gid = share_group_id(dist, lambda: native.tp_unique_id(lib))
@@ -516,6 +526,11 @@ def run_sharded(args):
     bench line (value = B tokens per step / step time, strong scaling)."""
     dist = dist_init()
     r = sharded_measure(dist, args.workload, args.steps, args.warmup, args.batch, args.prompt, args.layers)
+    if "unavailable" in r:   # this workload was asked for by name: fail loudly
+        if dist is not None:
+            dist.destroy_process_group()
+        log(f"[bench] {args.workload}: {r['unavailable']}")
+        return 1
     _, peak_kind = peaks()
     if RANK == 0:
         line = {

@@ -115,14 +115,44 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
     return Path(path)
 
 
+def size_estimate(cfg: SynthConfig) -> int:
+    """The file's bytes to within a few percent (the Q4_K_M mixture rule:
+    Q4_K at 0.5625 bytes per weight, Q6_K at 0.8203 for the output matrix and
+    half the attn_v / ffn_down matrices; Q8_0 at 1.0625), plus slack, for a
+    free-space check."""
+    E, F, H = cfg.n_embd, cfg.n_ff, cfg.n_head
+    D = E // H
+    HKV = cfg.n_head_kv or H
+    q8 = cfg.wtype == 8
+    r4, r6 = (1.0625, 1.0625) if q8 else (0.5625, 0.8203)
+    rv = r4 if q8 else (r4 + r6) / 2
+    ne = max(1, cfg.n_experts)
+    per_layer = (E * (H * D + HKV * D) * r4 + E * HKV * D * rv + H * D * E * r4
+                 + ne * (2 * E * F * r4 + F * E * rv) + 4 * E * max(0, cfg.n_experts) + 8 * E)
+    total = cfg.vocab * E * r4 + cfg.vocab * E * (r4 if q8 else r6) + cfg.n_layers * per_layer
+    return int(total * 1.03) + (64 << 20)
+
+
 def cached(cfg: SynthConfig, directory: str | os.PathLike | None = None, threads: int = 0) -> Path:
-    """Write the model once per (config) into a cache directory and reuse it."""
+    """Write the model once per (config) into a cache directory and reuse it.
+    Refuses to start when the directory's file system has less free space
+    than the file needs, and removes a partial file when the write fails."""
+    import shutil
     d = Path(directory or os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth"))
     d.mkdir(parents=True, exist_ok=True)
     key = int(hashlib.sha1(repr(cfg).encode()).hexdigest()[:12], 16)
     path = d / f"{cfg.arch}_L{cfg.n_layers}_E{cfg.n_embd}_w{cfg.wtype}_s{cfg.seed}_{key:012x}.gguf"
     if not path.exists():
         tmp = path.with_suffix(".tmp")
-        write(tmp, cfg, threads)
+        tmp.unlink(missing_ok=True)
+        need, free = size_estimate(cfg), shutil.disk_usage(d).free
+        if free < need:
+            raise RuntimeError(f"not enough disk space in {d} for the synthetic model: "
+                               f"{need / 1e9:.1f} GB needed, {free / 1e9:.1f} GB free")
+        try:
+            write(tmp, cfg, threads)
+        except BaseException:
+            tmp.unlink(missing_ok=True)
+            raise
         tmp.rename(path)
     return path

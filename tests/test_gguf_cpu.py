@@ -73,3 +73,29 @@ def test_gguf_digest_matches_reference(ref_lib, ours, synth_dir, name):
 
 def test_unreadable_file(ours):
     assert ours.fbx_gguf_digest(b"/nonexistent.gguf", None, 0, None, 0) == -1
+
+
+def test_synth_refuses_without_disk_space_and_leaves_no_partial_file(tmp_path, monkeypatch):
+    """The synthetic-model cache checks free space against the file's size
+    before writing (a 70B file is 42.5 GB) and leaves no partial file behind
+    when it refuses or when a write fails."""
+    import shutil
+    from collections import namedtuple
+    from imurun_b200 import synth
+    cfg = synth.preset("llama70b")
+    est = synth.size_estimate(cfg)
+    assert 42e9 < est < 46e9   # the real file is 42.5 GB
+    Usage = namedtuple("Usage", "total used free")
+    monkeypatch.setattr(shutil, "disk_usage", lambda p: Usage(10 ** 12, 10 ** 12 - 10 ** 9, 10 ** 9))
+    with pytest.raises(RuntimeError, match="not enough disk space"):
+        synth.cached(cfg, tmp_path)
+    assert list(tmp_path.iterdir()) == []
+
+    def failing_write(path, c, threads=0):
+        open(path, "wb").write(b"partial")
+        raise RuntimeError("fish_synth_write failed: write failed")
+    monkeypatch.setattr(shutil, "disk_usage", lambda p: Usage(10 ** 12, 0, 10 ** 12))
+    monkeypatch.setattr(synth, "write", failing_write)
+    with pytest.raises(RuntimeError, match="write failed"):
+        synth.cached(synth.preset("tiny"), tmp_path)
+    assert list(tmp_path.iterdir()) == []
