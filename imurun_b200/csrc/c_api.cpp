@@ -44,6 +44,12 @@ struct fish_ctx {
     std::vector<float> logits;
     int tp_rank = 0, tp_world = 1;       // set by fish_tp_init for the next fish_load
     unsigned char tp_id[128] = {};
+    // speculative decoding: the draft engine, the ids its sequence 0 holds,
+    // the longest draft per round
+    std::unique_ptr<fb::Engine> draft;
+    std::vector<int32_t> draft_ids;
+    int draft_k = 5;
+    std::vector<int32_t> last_ids;       // the ids the last generation emitted
 };
 
 namespace {
@@ -133,6 +139,8 @@ int load_locked(fish_ctx* ctx, const char* path, int n_ctx) {
         ctx->adapter_scale = 1.0f;
         return -4;
     }
+    ctx->draft.reset();          // a draft belongs to one target vocabulary
+    ctx->draft_ids.clear();
     ctx->eng.reset();
     ctx->tok.reset();
     auto eng = std::make_unique<fb::Engine>();
@@ -214,21 +222,165 @@ int generate_ids_locked(fish_ctx* ctx, std::vector<int32_t> ids, int max_tokens,
     std::vector<int32_t> recent;
     const size_t recent_cap = 128;
     for (size_t i = ids.size() > recent_cap ? ids.size() - recent_cap : 0; i < ids.size(); ++i) recent.push_back(ids[i]);
+    ctx->last_ids.clear();
+    auto remember = [&](int32_t t) {
+        ctx->last_ids.push_back(t);
+        recent.push_back(t);
+        if (recent.size() > recent_cap) recent.erase(recent.begin());
+    };
+    // the sampler's penalty window (repeat_last_n of the capped history)
+    const int window = std::min<int>(sp.repeat_last_n > 0 ? sp.repeat_last_n : 64, (int)recent_cap);
     int generated = 0;
     int next = -1;
     if (!ctx->cancel) next = ctx->sampler.sample(ctx->logits.data(), c.vocab, sp, recent);
-    while (next >= 0 && generated < max_tokens && pos < c.n_ctx) {
+
+    // Speculative decoding (reference c_api.cpp:630-773). Each round the
+    // draft proposes up to k tokens, the target verifies [next, drafts] in
+    // one forward, and the drafts are accepted left to right by the rejection
+    // rule (accept d with probability min(1, p(d)/q(d)); on a rejection the
+    // replacement is drawn from max(0, p - q)), which leaves the target's
+    // sampling distribution unchanged; both caches are cut back to what was
+    // committed. k adapts: +1 after a fully accepted round, else accepted+1.
+    // The verify forward is the batched decode step over consecutive
+    // positions of one sequence, so each row's logits are the bits plain
+    // decode gives at that position. Greedy (temperature <= 0) makes p and q
+    // one-hot: a draft is accepted iff it is the target's penalised argmax,
+    // the engines return argmaxes and no logits cross to the host, and the
+    // ids equal plain greedy decoding's. The accept test draws from the
+    // sampler's own seeded stream, so a seeded run is reproducible.
+    fb::Engine* D = ctx->draft.get();
+    const int k_max = ctx->draft_k;
+    int k = std::max(1, std::min(k_max, 3));
+    ctx->stats.draft_proposed = 0;
+    ctx->stats.draft_accepted = 0;
+    const bool greedy = sp.temperature <= 0.0f;
+    std::vector<std::vector<float>> q(D ? (size_t)k_max : 0);
+    std::vector<float> p, residual, dlogits, vlogits;
+    std::vector<int32_t> drafts, verify, hist, vam;
+    bool stopped = false;
+
+    while (!stopped && next >= 0 && generated < max_tokens && pos < c.n_ctx) {
         if (ctx->cancel) break;
         if (ctx->tok->is_eog(next)) break;
         emit_utf8(cb, user, ctx->tok->token_text(next), next, pending, sink);
-        recent.push_back(next);
-        if (recent.size() > recent_cap) recent.erase(recent.begin());
+        remember(next);
         ++generated;
         std::string err;
-        if (sp.temperature <= 0.0f) {
+
+        if (D && generated < max_tokens && pos + k_max + 2 <= c.n_ctx) {
+            // 0. the draft's sequence holds its longest common prefix with
+            //    the committed ids; forward the rest
+            size_t common = 0;
+            while (common < ctx->draft_ids.size() && common < (size_t)pos && ctx->draft_ids[common] == ctx->cache_ids[common])
+                ++common;
+            bool ok = D->seq_truncate(0, (int)common);
+            ctx->draft_ids.resize(ok ? common : 0);
+            while (ok && (int)ctx->draft_ids.size() < pos) {
+                const int dp = (int)ctx->draft_ids.size();
+                const int n = std::min(fb::kMaxBatch, pos - dp);
+                // a few committed tokens (the usual catch-up after a
+                // rejection) through the captured decode step, a prompt
+                // through the prefill kernels
+                ok = n <= 16 ? D->verify(0, ctx->cache_ids.data() + dp, n, nullptr, 0, 0, 1.0f, nullptr, nullptr, &err)
+                             : D->forward(0, ctx->cache_ids.data() + dp, n, nullptr, nullptr, nullptr, &err);
+                if (ok) ctx->draft_ids.insert(ctx->draft_ids.end(), ctx->cache_ids.begin() + dp, ctx->cache_ids.begin() + dp + n);
+            }
+            // 1. the draft proposes up to k tokens
+            drafts.clear();
+            std::vector<int32_t> recent_d = recent;
+            int32_t cur = next;
+            for (int j = 0; ok && j < k; ++j) {
+                int32_t d = -1;
+                if (greedy) {
+                    const int nw = std::min<int>(window, (int)recent_d.size());
+                    ok = D->decode_argmax(0, cur, recent_d.data() + recent_d.size() - nw, nw, sp.repeat_penalty, &d, &err);
+                } else {
+                    dlogits.resize((size_t)c.vocab);
+                    ok = D->forward(0, &cur, 1, dlogits.data(), nullptr, nullptr, &err);
+                    if (ok) {
+                        ctx->sampler.distribution(dlogits.data(), c.vocab, sp, recent_d, q[(size_t)j]);
+                        d = ctx->sampler.draw(q[(size_t)j].data(), c.vocab);
+                    }
+                }
+                if (!ok) break;
+                ctx->draft_ids.push_back(cur);
+                if (d < 0) break;
+                drafts.push_back(d);
+                recent_d.push_back(d);
+                if (recent_d.size() > recent_cap) recent_d.erase(recent_d.begin());
+                cur = d;
+                if (ctx->tok->is_eog(d)) break;   // nothing useful can follow
+            }
+            if (!ok) {   // the draft engine failed: plain decode from here on
+                ctx->draft.reset();
+                ctx->draft_ids.clear();
+                D = nullptr;
+                ctx->stats.draft_active = 0;
+            }
+            if (!drafts.empty()) {
+                ctx->stats.draft_proposed += (int)drafts.size();
+                const int n = (int)drafts.size();
+                verify.assign(1, next);
+                verify.insert(verify.end(), drafts.begin(), drafts.end());
+                // 2. the target verifies [next, d_0 .. d_{n-1}] in one forward
+                if (greedy) {
+                    hist = recent;
+                    hist.insert(hist.end(), drafts.begin(), drafts.end());
+                    vam.resize((size_t)n + 1);
+                    ok = e.verify(0, verify.data(), n + 1, hist.data(), (int)recent.size(), window, sp.repeat_penalty,
+                                  vam.data(), nullptr, &err);
+                } else {
+                    vlogits.resize((size_t)(n + 1) * c.vocab);
+                    ok = e.verify(0, verify.data(), n + 1, nullptr, 0, 0, 1.0f, nullptr, vlogits.data(), &err);
+                }
+                if (!ok) {
+                    ctx->err = "decode failed: " + err;
+                    ctx->cache_ids.clear();
+                    break;
+                }
+                ctx->cache_ids.push_back(next);
+                ++pos;
+                // 3. accept / reject left to right
+                int accepted = 0;
+                int32_t replacement = -1;
+                for (int j = 0; j < n; ++j) {
+                    const int32_t d = drafts[(size_t)j];
+                    if (greedy) {
+                        if (vam[(size_t)j] != d) { replacement = vam[(size_t)j]; break; }
+                    } else {
+                        ctx->sampler.distribution(vlogits.data() + (size_t)j * c.vocab, c.vocab, sp, recent, p);
+                        replacement = ctx->sampler.verify_draft(p, q[(size_t)j], d, residual);
+                        if (replacement >= 0) break;
+                    }
+                    // accepted: d is committed at position pos
+                    ++accepted;
+                    ++ctx->stats.draft_accepted;
+                    if (ctx->tok->is_eog(d)) { stopped = true; break; }
+                    emit_utf8(cb, user, ctx->tok->token_text(d), d, pending, sink);
+                    remember(d);
+                    ++generated;
+                    ctx->cache_ids.push_back(d);
+                    ++pos;
+                    if (generated >= max_tokens) { stopped = true; break; }
+                }
+                // 4. cut the target's cache back to the committed length
+                e.seq_truncate(0, pos);
+                k = accepted == n ? std::min(k_max, k + 1) : std::max(1, accepted + 1);
+                if (stopped) break;
+                if (replacement >= 0) {
+                    next = replacement;
+                } else if (greedy) {
+                    next = vam[(size_t)n];   // the bonus token after the last accepted draft
+                } else {
+                    next = ctx->sampler.sample(vlogits.data() + (size_t)n * c.vocab, c.vocab, sp, recent);
+                }
+                continue;
+            }
+        }
+
+        if (greedy) {
             // greedy: penalty and argmax on the device, only the id comes back
             // (the sampler's window: the last repeat_last_n ids of `recent`)
-            const int window = sp.repeat_last_n > 0 ? sp.repeat_last_n : 64;
             const size_t start = recent.size() > (size_t)window ? recent.size() - window : 0;
             int32_t am = 0;
             if (!e.decode_argmax(0, next, recent.data() + start, (int)(recent.size() - start), sp.repeat_penalty, &am,
@@ -285,6 +437,7 @@ void fish_destroy(fish_ctx* ctx) {
     ctx->cancel = true;
     {
         std::lock_guard<std::mutex> lock(ctx->mu);
+        ctx->draft.reset();
         ctx->eng.reset();
         ctx->tok.reset();
     }
@@ -534,6 +687,52 @@ int fbx_sample(const float* logits, int n_vocab, float temperature, int top_k, f
     return 0;
 }
 
+int fbx_sample_distribution(const float* logits, int n_vocab, float temperature, int top_k, float top_p,
+                            float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, float* probs) {
+    if (!logits || n_vocab <= 0 || !probs || n_recent < 0 || (n_recent > 0 && !recent)) return -1;
+    fb::SampleParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.repeat_penalty = repeat_penalty;
+    p.repeat_last_n = repeat_last_n;
+    fb::Sampler s(1);
+    const std::vector<int32_t> rec(recent, recent + n_recent);
+    std::vector<float> work(logits, logits + n_vocab), out;
+    s.distribution(work.data(), n_vocab, p, rec, out);
+    std::memcpy(probs, out.data(), sizeof(float) * (size_t)n_vocab);
+    return 0;
+}
+
+int fbx_sample_draw(const float* weights, int n, uint64_t seed, int n_draws, int32_t* out) {
+    if (!weights || n <= 0 || n_draws < 0 || (n_draws > 0 && !out)) return -1;
+    fb::Sampler s(seed);
+    for (int i = 0; i < n_draws; ++i) out[i] = s.draw(weights, n);
+    return 0;
+}
+
+int fbx_last_generated(fish_ctx* ctx, int32_t* out, int cap) {
+    if (!ctx || cap < 0 || (cap > 0 && !out)) return -1;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const int n = (int)ctx->last_ids.size();
+    std::copy(ctx->last_ids.begin(), ctx->last_ids.begin() + std::min(n, cap), out);
+    return n;
+}
+
+int fbx_speculative_draws(const float* p, const float* q, int n, uint64_t seed, int n_trials, int32_t* out) {
+    if (!p || !q || n <= 0 || n_trials < 0 || (n_trials > 0 && !out)) return -1;
+    fb::Sampler s(seed);
+    const std::vector<float> pv(p, p + n), qv(q, q + n);
+    std::vector<float> residual;
+    for (int i = 0; i < n_trials; ++i) {
+        const int32_t d = s.draw(q, n);
+        if (d < 0) { out[i] = -1; continue; }
+        const int32_t r = s.verify_draft(pv, qv, d, residual);
+        out[i] = r < 0 ? d : r;
+    }
+    return 0;
+}
+
 int fish_generate(fish_ctx* ctx, const char* prompt, int add_bos, int max_tokens, float temperature, int top_k,
                   float top_p, float repeat_penalty, fish_token_cb cb, void* user) {
     if (!ctx || !prompt) return -1;
@@ -570,7 +769,9 @@ void fish_reset(fish_ctx* ctx) {
     if (!ctx) return;
     std::lock_guard<std::mutex> lock(ctx->mu);
     if (ctx->eng) ctx->eng->seq_truncate(0, 0);
+    if (ctx->draft) ctx->draft->seq_truncate(0, 0);
     ctx->cache_ids.clear();
+    ctx->draft_ids.clear();
 }
 
 void fish_get_stats(fish_ctx* ctx, fish_stats* out) {
@@ -623,18 +824,49 @@ const char* fish_specs_json(fish_ctx* ctx) {
     return buf.c_str();
 }
 
+// The draft model for speculative decoding (reference c_api.cpp:410-447):
+// same vocabulary, BOS and token table as the target (-3 otherwise), k
+// tokens proposed per round at most (default 5, capped at 16). The draft is
+// a second engine on the target's GPU with the target's context length.
 int fish_set_draft(fish_ctx* ctx, const char* path, int k) {
     if (!ctx || !path) return -1;
-    (void)k;
     std::lock_guard<std::mutex> lock(ctx->mu);
-    if (!ctx->eng) { ctx->err = "load the target model first"; return -1; }
-    ctx->err = "draft: speculative decoding is not available in the B200 engine yet";
-    return -2;
+    if (!ctx->eng || !ctx->tok) { ctx->err = "load the target model first"; return -1; }
+    if (ctx->eng->tp_world() > 1) {
+        ctx->err = "draft: speculative decoding with a tensor-parallel target is not supported";
+        return -2;
+    }
+    ctx->draft.reset();
+    ctx->draft_ids.clear();
+    ctx->stats.draft_active = 0;
+    auto d = std::make_unique<fb::Engine>();
+    std::string err;
+    if (!d->load(path, ctx->eng->cfg().n_ctx, &err)) { ctx->err = "draft: " + err; return -2; }
+    const fb::Config& t = ctx->eng->cfg();
+    const fb::Config& c = d->cfg();
+    if (c.vocab != t.vocab || c.bos != t.bos) {
+        ctx->err = "draft model has a different vocabulary (" + std::to_string(c.vocab) + " vs " +
+                   std::to_string(t.vocab) + ")";
+        return -3;
+    }
+    const fb::MetaValue* tt = ctx->eng->gguf().meta("tokenizer.ggml.tokens");
+    const fb::MetaValue* dt = d->gguf().meta("tokenizer.ggml.tokens");
+    if (tt && dt && (tt->sarr.size() != dt->sarr.size() || (tt->sarr.size() > 1000 && tt->sarr[1000] != dt->sarr[1000]))) {
+        ctx->err = "draft model tokenizer differs from the target";
+        return -3;
+    }
+    ctx->draft = std::move(d);
+    ctx->draft_k = k > 0 ? std::min(k, 16) : 5;
+    ctx->stats.draft_active = 1;
+    ctx->err.clear();
+    return 0;
 }
 
 void fish_clear_draft(fish_ctx* ctx) {
     if (!ctx) return;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    ctx->draft.reset();
+    ctx->draft_ids.clear();
     ctx->stats.draft_active = 0;
 }
 

@@ -1886,20 +1886,48 @@ bool Engine::decode_argmax(int sid, int32_t id, const int32_t* recent, int n_rec
     return true;
 }
 
-bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err) {
-    if (n <= 0 || n > kMaxBatch) { if (err) *err = "bad batch size"; return false; }
-    const Config& c = cfg_;
-    std::vector<int> pos(n);
-    for (int i = 0; i < n; ++i) {
-        const int sid = sids[i];
-        if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session in batch"; return false; }
-        for (int j = 0; j < i; ++j) if (sids[j] == sid) { if (err) *err = "session repeated in one batch"; return false; }
-        if (ids[i] < 0 || ids[i] >= c.vocab) { if (err) *err = "token id out of range"; return false; }
-        if (!ensure_pages(sid, seqs_[sid].len + 1, err)) return false;
-        pos[i] = seqs_[sid].len;
+bool Engine::verify(int sid, const int32_t* ids, int T, const int32_t* hist, int base, int window, float penalty,
+                    int32_t* argmax, float* logits_all, std::string* err) {
+    if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session"; return false; }
+    if (T <= 0 || T > kMaxBatch) { if (err) *err = "bad token count"; return false; }
+    const bool pen = argmax && penalty > 0.0f && penalty != 1.0f && window > 0;
+    if (pen && (!hist || base < 0 || window > kMaxRecent || base + T - 1 > kMaxRecent)) {
+        if (err) *err = "penalty window too long";
+        return false;
     }
-    if (!upload_tokens(ids, sids, pos.data(), n, err)) return false;
-    // the 64-key blocks every session of the batch holds on the same pages,
+    const Config& c = cfg_;
+    for (int t = 0; t < T; ++t)
+        if (ids[t] < 0 || ids[t] >= c.vocab) { if (err) *err = "token id out of range"; return false; }
+    Seq& s = seqs_[sid];
+    const int pos0 = s.len;
+    if (!ensure_pages(sid, pos0 + T, err)) return false;
+    std::vector<int> sids(T, sid), pos(T);
+    for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
+    if (!step_tokens(sids.data(), ids, pos.data(), T, err)) return false;   // its upload waited for the stream
+    if (pen) {
+        const int n_hist = base + T - 1;
+        int32_t* hr = h_pinned_ + 3 * kMaxBatch;
+        std::copy(hist, hist + n_hist, hr);
+        if (n_hist > 0) CK(cudaMemcpyAsync(recent_dev_, hr, sizeof(int32_t) * n_hist, cudaMemcpyHostToDevice, stream_));
+        CK(fbk_argmax_penalized_rows(logits_, c.vocab, T, c.vocab, recent_dev_, base, window, penalty, argmax_, stream_));
+    }
+    if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * T, cudaMemcpyDeviceToHost, stream_));
+    if (logits_all) CK(cudaMemcpyAsync(logits_all, logits_, sizeof(float) * (size_t)T * c.vocab, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    s.len = pos0 + T;
+    return true;
+}
+
+// One decode step of n tokens, token i at position pos[i] of sequence
+// sids[i] (pages already ensured): the batched-decode graph for n (or its
+// eager launches), logits in logits_ and first-maximum ids in argmax_.
+// Tokens of one sequence at consecutive positions attend causally: every
+// token's K/V row is appended before the attention kernel reads keys up to
+// its own position.
+bool Engine::step_tokens(const int* sids, const int32_t* ids, const int* pos, int n, std::string* err) {
+    const Config& c = cfg_;
+    if (!upload_tokens(ids, sids, pos, n, err)) return false;
+    // the 64-key blocks every token of the step holds on the same pages,
     // below every token's own position: attention reads them once for all
     {
         int bp = 0;
@@ -1934,6 +1962,22 @@ bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* a
         if (!run_head(0, n, logits_, err)) return false;
         CK(fbk_argmax(logits_, c.vocab, n, c.vocab, argmax_, stream_));
     }
+    return true;
+}
+
+bool Engine::decode_batch(const int* sids, const int32_t* ids, int n, int32_t* argmax, float* logits, std::string* err) {
+    if (n <= 0 || n > kMaxBatch) { if (err) *err = "bad batch size"; return false; }
+    const Config& c = cfg_;
+    std::vector<int> pos(n);
+    for (int i = 0; i < n; ++i) {
+        const int sid = sids[i];
+        if (sid < 0 || sid >= max_seqs_ || !seqs_[sid].open) { if (err) *err = "bad session in batch"; return false; }
+        for (int j = 0; j < i; ++j) if (sids[j] == sid) { if (err) *err = "session repeated in one batch"; return false; }
+        if (ids[i] < 0 || ids[i] >= c.vocab) { if (err) *err = "token id out of range"; return false; }
+        if (!ensure_pages(sid, seqs_[sid].len + 1, err)) return false;
+        pos[i] = seqs_[sid].len;
+    }
+    if (!step_tokens(sids, ids, pos.data(), n, err)) return false;
     if (argmax) CK(cudaMemcpyAsync(argmax, argmax_, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, stream_));
     if (logits) CK(cudaMemcpyAsync(logits, logits_, sizeof(float) * (size_t)n * c.vocab, cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));

@@ -169,6 +169,15 @@ public:
     // the first index of the maximum; only that id comes back to the host.
     bool decode_argmax(int sid, int32_t id, const int32_t* recent, int n_recent, float penalty, int32_t* out,
                        std::string* err);
+    // Speculative verification: T tokens onto sid at consecutive positions
+    // through the batched-decode step (each token's logits are the bits a
+    // single-token decode at that position gives). argmax (host, T): the
+    // sampler's greedy branch per row, row t penalised by the last `window`
+    // ids of hist[0 .. base + t) (the window once the first t tokens were
+    // accepted; no penalty when penalty is 1 or window 0). logits_all (host,
+    // T*vocab) optional.
+    bool verify(int sid, const int32_t* ids, int T, const int32_t* hist, int base, int window, float penalty,
+                int32_t* argmax, float* logits_all, std::string* err);
     // Debug: run layer li alone on T hidden rows x_in (host, [T][E]) at
     // positions pos0.. of sequence 0 (its KV rows of that layer are written),
     // x_out = the layer's output rows; *p records every int8 activation the
@@ -220,6 +229,7 @@ private:
     // distinct: the T tokens belong to T different sequences (decode steps),
     // so attention can append each token's K/V inside the fused kernel
     bool run_layers(int T, int max_ctx, bool distinct, std::string* err, int l0 = 0, int l1 = -1);
+    bool step_tokens(const int* sids, const int32_t* ids, const int* pos, int n, std::string* err);
     bool probe_float(int idx, const float* dev, int rows, int K, std::string* err);
     bool probe_planes(int stage, const ActQ& a, int rows, int K, bool want32, bool wantk, std::string* err);
     bool probe_image(int stage, int rows, int K, std::string* err);

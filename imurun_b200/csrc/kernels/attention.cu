@@ -312,6 +312,53 @@ __device__ __forceinline__ float to_store(float x, const __half*) { return __hal
 __device__ __forceinline__ float to_store(float x, const float*) { return x; }
 __device__ __forceinline__ void put(__half* p, float x) { *p = __float2half_rn(x); }
 __device__ __forceinline__ void put(float* p, float x) { *p = x; }
+
+// Rows of the token's own sequence that this launch stores: when the tokens
+// before t in the launch are the same sequence at positions pos-1, pos-2, ...
+// (speculative verification runs a draft's tokens as one decode step), the
+// K/V rows of those positions are being stored by other CTAs while this one
+// runs, so the bulk copies may bring stale rows. Returns how many positions
+// below pos are such rows (0 when every token is its own sequence).
+__device__ __forceinline__ int fresh_rows(const KvView& kv, int t, int seq, int pos) {
+    int nf = 0;
+    while (nf < t && kv.tok_seq[t - 1 - nf] == seq && kv.tok_pos[t - 1 - nf] == pos - 1 - nf) ++nf;
+    return nf;
+}
+
+// Rebuild the fresh rows that fall in block [j0, j0 + kb) of the shared K/V
+// tiles (row stride rs elements) from the step's k/v projections, exactly as
+// their owner CTAs store them: the rotation at the row's own position, then
+// the rounding to the cache's element type.
+template <class E>
+__device__ void put_fresh_rows(E* K, E* V, int rs, int j0, int kb, int pos, int nf, int t, const float* knew,
+                               const float* vnew, int ldkv, int hk, int D, int half, int neox, const float* rcos,
+                               const float* rsin, int tid, int nt) {
+    const int lo = max(j0, pos - nf), hi = min(j0 + kb, pos), pairs = D / 2;
+    for (int idx = tid; idx < (hi - lo) * pairs; idx += nt) {
+        const int j = lo + idx / pairs, i = idx % pairs, u = t - (pos - j);
+        const float* kr = knew + (size_t)u * ldkv + (size_t)hk * D;
+        const float* vr = vnew + (size_t)u * ldkv + (size_t)hk * D;
+        E* kd = K + (size_t)(j - j0) * rs;
+        E* vd = V + (size_t)(j - j0) * rs;
+        int a = 2 * i, b = 2 * i + 1;
+        float k0, k1;
+        if (i < half) {
+            a = neox ? i : 2 * i;
+            b = neox ? i + half : 2 * i + 1;
+            const float cs = rcos[(size_t)j * half + i], sn = rsin[(size_t)j * half + i];
+            const float x0 = kr[a], x1 = kr[b];
+            k0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            k1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        } else {
+            k0 = kr[a];
+            k1 = kr[b];
+        }
+        put(kd + a, k0);
+        put(kd + b, k1);
+        put(vd + 2 * i, vr[2 * i]);
+        put(vd + 2 * i + 1, vr[2 * i + 1]);
+    }
+}
 __device__ __forceinline__ float get(const __half* p) { return __half2float(*p); }
 __device__ __forceinline__ float get(const float* p) { return *p; }
 
@@ -392,6 +439,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     const int seq = kv.tok_seq[t];
     const size_t pblk = (size_t)16 * D;   // elements of one page's piece of this head
     const int b_own = pos / kDecKeys;
+    const int nf = fresh_rows(kv, t, seq, pos);
 
     // bulk copies of my i-th block into slot i & 1: lane 0 sets the expected
     // bytes, lane pp (< 4) reads its page-table entry and copies that page
@@ -502,6 +550,11 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
                 put(K + (size_t)rr * D + d, snew[d]);
                 put(V + (size_t)rr * D + d, snew[kMaxD + d]);
             }
+            __syncthreads();
+        }
+        if (nf > 0 && j0 < pos && j0 + kb > pos - nf) {
+            put_fresh_rows(K, V, D, j0, kb, pos, nf, t, knew, vnew, ldkv, hk, D, half, neox, rcos, rsin, tid,
+                           kDecThreads);
             __syncthreads();
         }
         // scores: warp w holds keys 16w .. 16w+15, four per pass, 8 lanes per key
@@ -941,6 +994,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     float* snew = reinterpret_cast<float*>(smem + L::off_n);
     const int seq = kv.tok_seq[t];
     const int b_own = pos / kTcKeys;
+    const int nf = fresh_rows(kv, t, seq, pos);
 
     // warp 0: one bulk copy per K row and per V row of my i-th block (slot i & 1)
     auto issue = [&](int i) {
@@ -1061,6 +1115,11 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
                 K[(size_t)rr * RS + d] = __float2half_rn(snew[d]);
                 V[(size_t)rr * RS + d] = __float2half_rn(snew[kMaxD + d]);
             }
+            __syncthreads();
+        }
+        if (nf > 0 && j0 < pos && j0 + kb > pos - nf) {
+            put_fresh_rows(K, V, RS, j0, kb, pos, nf, t, knew, vnew, ldkv, hk, D, half, neox, rcos, rsin, tid,
+                           32 * kTcWarps);
             __syncthreads();
         }
         tc_warp_block<D>(K, V, 16 * warp, kb, scale, qh, ql, m_r, l_r, acc, pw, lane);

@@ -216,6 +216,11 @@ int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out, cudaStrea
 constexpr int kMaxRecent = 256;
 int fbk_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty, int32_t* out,
                          cudaStream_t st);
+// The same for `rows` rows of ldx floats: row r is penalised by the last
+// `window` ids (<= kMaxRecent) of hist[0 .. base + r) and out[r] is its
+// first maximum (the target's greedy choice after each accepted draft token).
+int fbk_argmax_penalized_rows(const float* x, int n, int rows, int ldx, const int32_t* hist, int base, int window,
+                              float penalty, int32_t* out, cudaStream_t st);
 // Argmax keys (value, first index) accumulated by a GEMV's epilogue
 // (GemvSeg::amax): decode them into out[t] / advance a greedy loop like
 // fbk_greedy_advance, and reset the keys for the next step.

@@ -92,10 +92,18 @@ __global__ void k_argmax(const float* __restrict__ x, int n, int ldx, int32_t* o
 // v = v > 0 ? v / p : v * p once (src/sampler.cpp: penalise, then argmax), so
 // an id seen c times is penalised c times in a row. A bitmap of the window's
 // ids in shared memory keeps the scan at one load per logit.
-__global__ void k_argmax_penalized(const float* __restrict__ x, int n, const int32_t* __restrict__ recent,
-                                   int n_recent, float penalty, int32_t* out) {
+// One CTA per row: row r's window is the last `window` ids of
+// hist[0 .. base + r), the sampler's window once the first r tokens of the
+// forward that made these rows were accepted (speculative verification).
+__global__ void k_argmax_penalized(const float* __restrict__ logits, int n, int ldx, const int32_t* __restrict__ hist,
+                                   int base, int window, float penalty, int32_t* outs) {
     pdl_trigger();
     pdl_wait();
+    const float* x = logits + (size_t)blockIdx.x * ldx;
+    const int end = base + (int)blockIdx.x;
+    const int n_recent = min(end, window);
+    const int32_t* recent = hist + (end - n_recent);
+    int32_t* out = outs + blockIdx.x;
     extern __shared__ uint32_t s_bits[];
     __shared__ int s_id[kMaxRecent];
     __shared__ float s_val[kMaxRecent];
@@ -497,7 +505,13 @@ extern "C" int fbk_argmax(const float* x, int n, int rows, int ldx, int32_t* out
 
 extern "C" int fbk_argmax_penalized(const float* x, int n, const int32_t* recent, int n_recent, float penalty,
                                     int32_t* out, cudaStream_t st) {
-    if (n <= 0 || n_recent < 0 || n_recent > kMaxRecent) return (int)cudaErrorInvalidValue;
+    return fbk_argmax_penalized_rows(x, n, 1, n, recent, n_recent, n_recent, penalty, out, st);
+}
+
+extern "C" int fbk_argmax_penalized_rows(const float* x, int n, int rows, int ldx, const int32_t* hist, int base,
+                                         int window, float penalty, int32_t* out, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    if (n <= 0 || ldx < n || base < 0 || window < 0 || window > kMaxRecent) return (int)cudaErrorInvalidValue;
     const size_t smem = sizeof(uint32_t) * (size_t)((n + 31) / 32);
     if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
     static bool attr = false;
@@ -507,7 +521,8 @@ extern "C" int fbk_argmax_penalized(const float* x, int n, const int32_t* recent
         if (e != cudaSuccess) return (int)e;
         attr = true;
     }
-    return (int)fbk_launch(k_argmax_penalized, dim3(1), dim3(1024), smem, st, x, n, recent, n_recent, penalty, out);
+    return (int)fbk_launch(k_argmax_penalized, dim3(rows), dim3(1024), smem, st, x, n, ldx, hist, base, window,
+                           penalty, out);
 }
 
 extern "C" int fbk_moe_route(const float* logits, int T, int NE, int K, int norm, int32_t* sel, float* wsel,

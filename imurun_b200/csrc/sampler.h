@@ -27,6 +27,25 @@ public:
     int32_t sample(float* logits, int n_vocab, const SampleParams& p, const std::vector<int32_t>& recent);
     // the penalty step alone (used before an on-device greedy argmax)
     static void penalise(float* logits, int n_vocab, const SampleParams& p, const std::vector<int32_t>& recent);
+    // The distribution sample() draws from, as probabilities over the whole
+    // vocabulary (speculative decoding compares the target's and the
+    // draft's): penalty, then a one-hot of the first maximum (temperature
+    // <= 0) or temperature, top-k, softmax and the nucleus cut renormalised
+    // (reference sampler.cpp:42-89). logits are modified in place.
+    void distribution(float* logits, int n_vocab, const SampleParams& p, const std::vector<int32_t>& recent,
+                      std::vector<float>& probs);
+    // An index drawn in proportion to the positive weights (-1 when none).
+    int32_t draw(const float* w, int n);
+    // A uniform draw in [0, 1) from the same stream.
+    double uniform();
+    // Speculative verification of one draft token d drawn from q against the
+    // target's distribution p (reference c_api.cpp:719-741): d is kept with
+    // probability min(1, p(d)/q(d)); otherwise the replacement is drawn from
+    // max(0, p - q), or from p when that is all zero. Returns -1 when d is
+    // kept, else the replacement; the result is distributed as p. The accept
+    // test draws from this sampler's seeded stream.
+    int32_t verify_draft(const std::vector<float>& p, const std::vector<float>& q, int32_t d,
+                         std::vector<float>& residual);
 
 private:
     std::mt19937_64 rng_;

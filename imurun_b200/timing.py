@@ -5,6 +5,7 @@
     python -m imurun_b200.timing prefill --tokens 512 [--layers 32]
     python -m imurun_b200.timing greedy --layers 32 --steps 3 --prompt 512
     python -m imurun_b200.timing batch --preset qwen7b --prompt 2048 --sessions 64 --suffix 128 [--layers 0]
+    python -m imurun_b200.timing spec --preset llama8b --draft-layers 2 --k 5 --tokens 128 [--penalty 1.0]
 
 Runs fbx_time_matmul: 3 warm-up launches, then `iters` launches timed with
 CUDA events, each launch reading a different copy of the weights (>= 512 MB
@@ -128,6 +129,48 @@ def batch(preset: str, prompt: int, sessions: int, suffix: int, layers: int, ste
             "step_ms": [round(v, 4) for v in ms], "tok_s": round(sessions / (sum(ms) / len(ms) / 1e3), 1)}
 
 
+def spec(preset: str, draft_layers: int, k: int, tokens: int, penalty: float) -> dict:
+    """Greedy generation of `tokens` ids through fish_generate on the synthetic
+    GGUF of `preset`, plain and with a draft model: the same preset truncated
+    to `draft_layers` layers. The synthetic weights are seeded by tensor name,
+    so the draft is the target's own first layers, embedding and output head
+    (a layer-skip draft). Reports tok/s of both (the stats' decode rate, host
+    loop included), the draft's acceptance and the first index where the two
+    id sequences differ (-1: identical)."""
+    import ctypes
+    import os
+    from . import synth
+    d = os.environ.get("FISH_SYNTH_DIR", "/tmp/fish_synth")
+    tgt = synth.cached(synth.preset(preset), d)
+    drf = synth.cached(synth.preset(preset, layers=draft_layers), d)
+    lib = native.load_library()
+    lib.fbx_last_generated.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    lib.fbx_last_generated.restype = ctypes.c_int
+    prompt = b"the quick brown fox jumps over the lazy dog, and then it runs far away into the woods " * 4
+    out = {"preset": preset, "draft_layers": draft_layers, "k": k, "tokens": tokens, "penalty": penalty}
+    runs = {}
+    for name, draft in (("plain", None), ("draft", drf)):
+        ctx = lib.fish_create()
+        assert lib.fish_load(ctx, str(tgt).encode(), 4096) == 0, lib.fish_last_error(ctx)
+        if draft is not None:
+            assert lib.fish_set_draft(ctx, str(draft).encode(), k) == 0, lib.fish_last_error(ctx)
+        no_cb = native.FISH_TOKEN_CB()
+        lib.fish_generate(ctx, prompt, 1, 16, 0.0, 40, 0.9, penalty, no_cb, None)   # warm-up
+        n = lib.fish_generate(ctx, prompt, 1, tokens, 0.0, 40, 0.9, penalty, no_cb, None)
+        st = native.FishStats()
+        lib.fish_get_stats(ctx, ctypes.byref(st))
+        ids = np.zeros(max(n, 1), np.int32)
+        lib.fbx_last_generated(ctx, ids.ctypes.data, ids.size)
+        runs[name] = ids[:n].tolist()
+        out[name] = {"generated": n, "tok_s": round(st.tokens_per_second, 1),
+                     "proposed": st.draft_proposed, "accepted": st.draft_accepted}
+        lib.fish_destroy(ctx)
+    a, b = runs["plain"], runs["draft"]
+    out["first_difference"] = next((i for i in range(min(len(a), len(b))) if a[i] != b[i]),
+                                   -1 if len(a) == len(b) else min(len(a), len(b)))
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -157,7 +200,16 @@ def main() -> None:
     bt.add_argument("--suffix", type=int, default=128)
     bt.add_argument("--layers", type=int, default=0)
     bt.add_argument("--steps", type=int, default=5)
+    sp = sub.add_parser("spec")
+    sp.add_argument("--preset", default="llama8b")
+    sp.add_argument("--draft-layers", type=int, default=2)
+    sp.add_argument("--k", type=int, default=5)
+    sp.add_argument("--tokens", type=int, default=128)
+    sp.add_argument("--penalty", type=float, default=1.0)
     a = ap.parse_args()
+    if a.cmd == "spec":
+        print(json.dumps(spec(a.preset, a.draft_layers, a.k, a.tokens, a.penalty)), flush=True)
+        return
     if a.cmd == "batch":
         print(json.dumps(batch(a.preset, a.prompt, a.sessions, a.suffix, a.layers, a.steps)), flush=True)
         return

@@ -208,6 +208,37 @@ FISH_API int fbx_sample(const float* logits, int n_vocab, float temperature, int
                         float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent, uint64_t seed,
                         int n_draws, int32_t* out);
 
+/* The distribution fbx_sample draws from, as probabilities over the whole
+ * vocabulary (host code only): after the penalty, a one-hot of the first
+ * maximum when temperature <= 0, else the top-k softmax cut at top_p and
+ * renormalised, zero elsewhere; speculative decoding compares the target's
+ * and the draft's. Replaces the reference's Sampler::distribution
+ * (model/fish/include/fish/sampler.h:32-37). Returns 0, or -1 on bad
+ * arguments. */
+FISH_API int fbx_sample_distribution(const float* logits, int n_vocab, float temperature, int top_k, float top_p,
+                                     float repeat_penalty, int repeat_last_n, const int32_t* recent, int n_recent,
+                                     float* probs);
+/* n_draws indices drawn in proportion to the positive weights (-1 when there
+ * are none) from one std::mt19937_64 seeded with `seed` (host code only).
+ * Replaces the reference's Sampler::draw (model/fish/include/fish/sampler.h:39-40).
+ * Returns 0, or -1 on bad arguments. */
+FISH_API int fbx_sample_draw(const float* weights, int n, uint64_t seed, int n_draws, int32_t* out);
+
+/* The token ids the context's last fish_generate* call emitted, in order (the
+ * ids behind its token callbacks; test observability, host code only):
+ * copies min(count, cap) of them and returns the count, -1 on bad
+ * arguments. */
+FISH_API int fbx_last_generated(struct fish_ctx* ctx, int32_t* out, int cap);
+
+/* The rejection rule of speculative decoding on fixed distributions (host
+ * code only): n_trials times, a draft token d is drawn from q and verified
+ * against p (kept with probability min(1, p(d)/q(d)), else replaced by a draw
+ * from max(0, p - q)); out[i] = the committed token, which is distributed as
+ * p. One std::mt19937_64 seeded with `seed`. The step fish_generate takes per
+ * draft token when a draft model is set (model/fish/src/c_api.cpp:719-741).
+ * Returns 0, or -1 on bad arguments. */
+FISH_API int fbx_speculative_draws(const float* p, const float* q, int n, uint64_t seed, int n_trials, int32_t* out);
+
 /* fish_count_chat_tokens and fish_chat_format for the GGUF at gguf_path with
  * no model loaded (host code only, model/fish/src/c_api.cpp:384-397): returns
  * the token count of the formatted chat, and writes the chat format's name

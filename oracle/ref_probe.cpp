@@ -133,6 +133,29 @@ __attribute__((visibility("default"))) void ref_sample(const float* logits, int 
         out[i] = s.sample(work.data(), n_vocab, p, rec);
     }
 }
+/* The reference's Sampler::distribution and Sampler::draw behind the same
+ * arguments as the library's fbx_sample_distribution / fbx_sample_draw. */
+__attribute__((visibility("default"))) void ref_distribution(const float* logits, int n_vocab, float temperature,
+                                                             int top_k, float top_p, float repeat_penalty,
+                                                             int repeat_last_n, const int32_t* recent, int n_recent,
+                                                             float* probs) {
+    SampleParams p;
+    p.temperature = temperature;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.repeat_penalty = repeat_penalty;
+    p.repeat_last_n = repeat_last_n;
+    Sampler s(1);
+    std::vector<int32_t> rec(recent, recent + n_recent);
+    std::vector<float> work(logits, logits + n_vocab), out;
+    s.distribution(work.data(), n_vocab, p, rec, out);
+    std::memcpy(probs, out.data(), sizeof(float) * static_cast<size_t>(n_vocab));
+}
+__attribute__((visibility("default"))) void ref_draw(const float* weights, int n, unsigned long long seed,
+                                                     int n_draws, int32_t* out) {
+    Sampler s(seed);
+    for (int i = 0; i < n_draws; ++i) out[i] = s.draw(weights, n);
+}
 /* The same digest as the library's fbx_gguf_digest, from the reference's own
  * GgufFile reader (include/fish/gguf.h:77-116): tensor directory and the
  * requested metadata keys, arrays reduced to counts and an FNV-1a digest. */

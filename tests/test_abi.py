@@ -83,12 +83,21 @@ def test_version_and_context_lifecycle(lib):
     assert lib.fish_kv_len(ctx) == -1
     assert lib.fish_prefill_ids(ctx, None, 0, 0, None) == -1
     # adapter requested before a model: remembered, reported as pending
-    from imurun_b200.native import FishAdapterInfo
+    from imurun_b200.native import FishAdapterInfo, FishStats
     assert lib.fish_set_adapter(ctx, b"/tmp/x/lora.gguf", 1.0) == 0
     info = FishAdapterInfo()
     assert lib.fish_adapter_info_of(ctx, ctypes.byref(info)) == 0
     assert info.pending == 1 and info.name == b"lora.gguf"
     assert lib.fish_clear_adapter(ctx) == 0
+    # a draft model needs a loaded target (reference c_api.cpp:410-413)
+    assert lib.fish_set_draft(ctx, b"/tmp/x/draft.gguf", 4) == -1
+    assert b"target" in lib.fish_last_error(ctx)
+    assert lib.fish_set_draft(None, b"x", 4) == -1
+    lib.fish_clear_draft(ctx)
+    lib.fish_clear_draft(None)
+    st = FishStats()
+    lib.fish_get_stats(ctx, ctypes.byref(st))
+    assert st.draft_active == 0
     lib.fish_destroy(ctx)
 
 
