@@ -427,7 +427,7 @@ extern "C" {
 
 const char* fish_version(void) { return "fish-b200 0.1.0"; }
 int fish_abi_version(void) { return FISH_ABI_VERSION; }
-const char* fish_supported_archs(void) { return "llama,qwen2,qwen2moe,qwen3,qwen3moe"; }
+const char* fish_supported_archs(void) { return "llama,qwen2,qwen2moe,qwen3,qwen3moe,gemma2,phi3"; }
 const char* fish_kernel_name(void) { return "cuda-sm100a"; }
 
 fish_ctx* fish_create(void) { return new (std::nothrow) fish_ctx(); }

@@ -254,8 +254,10 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     Config& c = cfg_;
     // model.cpp:403-470: metadata under the architecture prefix
     c.arch = g.str("general.architecture", "llama");
-    if (c.arch != "llama" && c.arch != "qwen2" && c.arch != "qwen3" && c.arch != "qwen2moe" && c.arch != "qwen3moe") {
-        if (err) *err = "unsupported architecture: " + c.arch + " (the B200 engine runs llama, qwen2, qwen3 and their MoE variants)";
+    if (c.arch != "llama" && c.arch != "qwen2" && c.arch != "qwen3" && c.arch != "qwen2moe" && c.arch != "qwen3moe" &&
+        c.arch != "gemma2" && c.arch != "phi3") {
+        if (err) *err = "unsupported architecture: " + c.arch +
+                        " (the B200 engine runs llama, qwen2, qwen3, their MoE variants, gemma2 and phi3)";
         return false;
     }
     auto key = [&](const char* k) { return c.arch + "." + k; };
@@ -290,6 +292,16 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     c.rot_dim = (int)g.u64(key("rope.dimension_count"), (uint64_t)c.head_dim);
     if (c.rot_dim <= 0 || c.rot_dim > c.head_dim) c.rot_dim = c.head_dim;
     c.neox = c.arch != "llama";
+    if (c.arch == "gemma2") {   // src/model.cpp:488-496
+        if (tp_world_ > 1) { if (err) *err = "tensor parallelism is not supported for gemma2"; return false; }
+        c.norm_plus_one = true;
+        c.gelu = true;
+        c.post_norms = true;
+        c.embd_scale = std::sqrt((float)c.n_embd);
+        c.attn_softcap = (float)g.f64(key("attn_logit_softcapping"), 50.0);
+        c.final_softcap = (float)g.f64(key("final_logit_softcapping"), 30.0);
+        c.sliding_window = (int)g.u64(key("attention.sliding_window"), 4096);
+    }
     const int model_ctx = c.n_ctx_train;
     c.n_ctx = n_ctx > 0 ? std::min(n_ctx, model_ctx > 0 ? model_ctx : n_ctx) : std::min(4096, model_ctx);
     if (c.n_ctx < 32) { if (err) *err = "context too small"; return false; }
@@ -314,6 +326,7 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         c.out_rows = tp.vocab_rows;
         c.out_row0 = tp.vocab_row0;
     }
+    std::string longrope;   // the longrope factor tensor in use (phi3)
     {
         const std::string type = g.str(key("rope.scaling.type"), "none");
         const float factor = (float)g.f64(key("rope.scaling.factor"), 1.0);
@@ -323,6 +336,13 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
             c.yarn_factor = factor;
             c.yarn_orig_ctx = orig > 0 ? orig : model_ctx;
             c.yarn_attn_factor = (float)g.f64(key("rope.scaling.attn_factor"), 1.0);
+        } else if (type == "longrope") {
+            // phi3 (src/model.cpp:522-530): per-pair factors, the long set
+            // beyond the original context, the short set within it; the
+            // attention factor scales the rotation
+            longrope = (orig > 0 && c.n_ctx > orig) ? "rope_factors_long.weight" : "rope_factors_short.weight";
+            if (!g.find(longrope)) longrope = "rope_factors_short.weight";
+            c.mscale = (float)g.f64(key("rope.scaling.attn_factor"), 1.0);
         }
     }
 
@@ -337,6 +357,7 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
             if (err) *err = std::string("tensor type ") + ggml_type_name(t->type) + " is not supported on the B200 path yet (" + name + ")";
             return false;
         }
+        w.name = name;
         w.type = t->type;
         w.n_in = (int)t->ne[0];
         w.n_out = t->ne.size() > 1 ? (int)t->ne[1] : 1;
@@ -352,9 +373,10 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     };
     // tensor-parallel shards: a row range, or a range of input values (whole
     // blocks, so a shard's block integers are the unsharded ones)
+    // (row0 adds to the view's own first row: a shard of one part of a fused tensor)
     auto shard_rows = [&](DevW& w, int n, int row0) {
         w.n_out = n;
-        w.row0 = row0;
+        w.row0 += row0;
         w.expert_bytes = dev_matrix_bytes(w.type, w.n_in, w.n_out);
     };
     auto shard_k = [&](DevW& w, int n, int k0, const std::string& name) -> bool {
@@ -377,9 +399,22 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     for (int i = 0; i < c.n_layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
         DevLayer& L = layers_[i];
-        if (!bind(p + "attn_q.weight", L.wq, true) || !bind(p + "attn_k.weight", L.wk, true) ||
-            !bind(p + "attn_v.weight", L.wv, true) || !bind(p + "attn_output.weight", L.wo, true))
+        if (g.find(p + "attn_qkv.weight")) {
+            // phi3: fused q|k|v rows (src/model.cpp:253, 1665-1674): three
+            // views of one tensor, each uploaded as its own matrix
+            const int Q = c.n_head_model * c.head_dim, KV = c.n_head_kv_model * c.head_dim;   // whole-model rows
+            DevW f;
+            if (!bind(p + "attn_qkv.weight", f, true)) return false;
+            if (f.n_out != Q + 2 * KV) { if (err) *err = "fused attn_qkv has an unexpected shape in layer " + std::to_string(i); return false; }
+            L.wq = L.wk = L.wv = f;
+            shard_rows(L.wq, Q, 0);
+            shard_rows(L.wk, KV, Q);
+            shard_rows(L.wv, KV, Q + KV);
+            if (!bind(p + "attn_output.weight", L.wo, true)) return false;
+        } else if (!bind(p + "attn_q.weight", L.wq, true) || !bind(p + "attn_k.weight", L.wk, true) ||
+                   !bind(p + "attn_v.weight", L.wv, true) || !bind(p + "attn_output.weight", L.wo, true)) {
             return false;
+        }
         if (tp_world_ > 1) {
             const int Q = c.q_dim(), KV = c.kv_dim(), r = tp_rank_;
             shard_rows(L.wq, Q, r * Q);
@@ -400,9 +435,20 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
                 }
             }
         } else {
-            if (!bind(p + "ffn_gate.weight", L.wg, true) || !bind(p + "ffn_up.weight", L.wu, true) ||
-                !bind(p + "ffn_down.weight", L.wd, true))
+            if (!g.find(p + "ffn_gate.weight")) {
+                // phi3: fused gate|up, ffn_up holding 2 n_ff rows, gate first
+                // (src/model.cpp:310-316, 1481-1489)
+                DevW f;
+                if (!bind(p + "ffn_up.weight", f, true) || !bind(p + "ffn_down.weight", L.wd, true)) return false;
+                const int Fm = c.n_ff_model;
+                if (f.n_out != 2 * Fm) { if (err) *err = "missing tensor " + p + "ffn_gate.weight"; return false; }
+                L.wg = L.wu = f;
+                shard_rows(L.wg, Fm, 0);
+                shard_rows(L.wu, Fm, Fm);
+            } else if (!bind(p + "ffn_gate.weight", L.wg, true) || !bind(p + "ffn_up.weight", L.wu, true) ||
+                       !bind(p + "ffn_down.weight", L.wd, true)) {
                 return false;
+            }
             if (tp_world_ > 1) {
                 const int F = c.n_ff, r = tp_rank_;
                 shard_rows(L.wg, F, r * F);
@@ -435,7 +481,9 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
 
     // small vectors
     // row0 / n: this rank's slice of the vector (biases of sharded rows)
-    auto dev_vec = [&](const std::string& name, float** out, bool required, int row0 = 0, int n = -1) -> bool {
+    // plus_one: a norm weight stored as w - 1 (gemma2, src/model.cpp:241-245)
+    auto dev_vec = [&](const std::string& name, float** out, bool required, int row0 = 0, int n = -1,
+                       bool plus_one = false) -> bool {
         const Tensor* t = g.find(name);
         if (!t) {
             if (required && err) *err = "missing tensor " + name;
@@ -443,6 +491,7 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         }
         std::vector<float> v;
         if (!host_vec(t, v)) { if (err) *err = "bad vector " + name; return false; }
+        if (plus_one) for (float& x : v) x += 1.0f;
         if (n >= 0) {
             if (row0 + n > (int)v.size()) { if (err) *err = "bad vector slice " + name; return false; }
             v = std::vector<float>(v.begin() + row0, v.begin() + row0 + n);
@@ -458,7 +507,11 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         const std::string p = "blk." + std::to_string(i) + ".";
         DevLayer& L = layers_[i];
         const int sq = tp_world_ > 1 ? c.q_dim() : -1, skv = tp_world_ > 1 ? c.kv_dim() : -1;
-        if (!dev_vec(p + "attn_norm.weight", &L.attn_norm, true) || !dev_vec(p + "ffn_norm.weight", &L.ffn_norm, true) ||
+        const bool p1 = c.norm_plus_one;
+        if (!dev_vec(p + "attn_norm.weight", &L.attn_norm, true, 0, -1, p1) ||
+            !dev_vec(p + "ffn_norm.weight", &L.ffn_norm, true, 0, -1, p1) ||
+            (c.post_norms && (!dev_vec(p + "post_attention_norm.weight", &L.post_attn_norm, true, 0, -1, p1) ||
+                              !dev_vec(p + "post_ffw_norm.weight", &L.post_ffn_norm, true, 0, -1, p1))) ||
             !dev_vec(p + "attn_q.bias", &L.bq, false, tp_rank_ * c.q_dim(), sq) ||
             !dev_vec(p + "attn_k.bias", &L.bk, false, tp_rank_ * c.kv_dim(), skv) ||
             !dev_vec(p + "attn_v.bias", &L.bv, false, tp_rank_ * c.kv_dim(), skv) ||
@@ -471,13 +524,15 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
         const Tensor* t = g.find("output_norm.weight");
         std::vector<float> v;
         if (!t || !host_vec(t, v)) { if (err) *err = "missing output_norm.weight"; return false; }
+        if (c.norm_plus_one) for (float& x : v) x += 1.0f;
         CK(cudaMalloc(&out_norm_, v.size() * sizeof(float)));
         CK(cudaMemcpy(out_norm_, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
     }
     {
         std::vector<float> ff, cs, sn;
-        const Tensor* rf = g.find("rope_freqs.weight");
-        if (rf && (!host_vec(rf, ff) || (int)ff.size() != c.rot_dim / 2)) { if (err) *err = "bad rope_freqs"; return false; }
+        // longrope factors (phi3), else Llama-3 style rope_freqs (src/model.cpp:532-543)
+        const Tensor* rf = g.find(longrope.empty() ? std::string("rope_freqs.weight") : longrope);
+        if (rf && (!host_vec(rf, ff) || (int)ff.size() != c.rot_dim / 2)) { if (err) *err = "bad rope factors"; return false; }
         build_rope_table(c, ff.empty() ? nullptr : ff.data(), cs, sn);
         CK(cudaMalloc(&rope_cos_, cs.size() * sizeof(float)));
         CK(cudaMalloc(&rope_sin_, sn.size() * sizeof(float)));
@@ -495,9 +550,9 @@ bool Engine::upload_weights(std::string* err) {
     struct Job { const Tensor* t; DevW* w; size_t off; };
     std::vector<Job> jobs;
     size_t total = 0;
-    auto add = [&](const std::string& name, DevW* w) {
+    auto add = [&](const std::string&, DevW* w) {
         if (w->type < 0) return;
-        const Tensor* t = g.find(name);
+        const Tensor* t = g.find(w->name);
         if (!t) return;
         jobs.push_back({t, w, total});
         total = align_up(total + w->expert_bytes * (size_t)w->n_exp, 256);
@@ -600,8 +655,10 @@ bool Engine::alloc_buffers(std::string* err) {
     CK(cudaMalloc(&g_, sizeof(float) * (size_t)R * F));
     CK(cudaMalloc(&u_, sizeof(float) * (size_t)R * F));
     CK(cudaMalloc(&logits_, sizeof(float) * (size_t)kMaxBatch * c.vocab));
-    if (tp_world_ > 1) {
+    if (tp_world_ > 1 || c.post_norms) {   // gemma2: the o / down rows before their post norm
         CK(cudaMalloc(&tp_tmp_, sizeof(float) * (size_t)kMaxBatch * E));
+    }
+    if (tp_world_ > 1) {
         CK(cudaMalloc(&tp_logits_, sizeof(float) * (size_t)tp_world_ * kMaxBatch * c.out_rows));
     }
     if (c.n_experts > 0) {
@@ -1044,6 +1101,11 @@ bool Engine::step_ready() {
     if (c.n_experts > 0) { step_why_ = "mixture of experts"; return false; }
     if (tp_world_ > 1) { step_why_ = "tensor parallel"; return false; }
     if (c.qk_norm) { step_why_ = "q/k norm"; return false; }
+    if (c.post_norms || c.gelu || c.attn_softcap > 0.0f || c.final_softcap > 0.0f || c.sliding_window > 0 ||
+        c.embd_scale != 1.0f) {
+        step_why_ = "gemma2 layer form";
+        return false;
+    }
     const int G = c.n_head_kv > 0 ? c.n_head / c.n_head_kv : 0;
     if (c.head_dim != 128 || c.n_head % c.n_head_kv || !(G == 1 || G == 2 || G == 4 || G == 8) || c.rot_dim > 128 ||
         c.rot_dim % 2) {
@@ -1301,11 +1363,13 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
     const Config& c = cfg_;
     const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim(), H = c.n_head, HKV = c.n_head_kv, D = c.head_dim;
     const float scale = 1.0f / std::sqrt((float)D);
-    const KvView kv = kv_view();
+    KvView kv = kv_view();
+    kv.softcap = c.attn_softcap;
     ActQ a = act_;
     if (l1 < 0) l1 = c.n_layers;
     for (int li = l0; li < l1; ++li) {
         const DevLayer& L = layers_[li];
+        kv.window = (c.sliding_window > 0 && li % 2 == 0) ? c.sliding_window : 0;   // gemma2: even layers
         a.K = E;
         {
             const DevW* ws[3] = {&L.wq, &L.wk, &L.wv};
@@ -1353,9 +1417,10 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
         {
             // tensor parallelism: this rank's heads give a partial sum of o,
             // all-reduced before the residual add
-            const bool tp = tp_world_ > 1;
-            float* oy = tp ? tp_tmp_ : x_;
-            const int oepi = tp ? EPI_STORE : EPI_ADD;
+            // gemma2: o rows into tp_tmp_, then x += post_norm(o)
+            const bool tp = tp_world_ > 1, post = L.post_attn_norm != nullptr;
+            float* oy = tp || post ? tp_tmp_ : x_;
+            const int oepi = tp || post ? EPI_STORE : EPI_ADD;
             const DevW* wo[1] = {&L.wo};
             if (probe_ && !probe_float(1, attn_, T, Q, err)) return false;
             if (fusable(wo, 1, T)) {
@@ -1370,6 +1435,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
                 if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err)) return false;
             }
             if (tp && !tp_reduce_add(T, err)) return false;
+            if (post) CKP(PC_NORMQ, 0, fbk_rmsnorm_add(x_, E, tp_tmp_, E, L.post_attn_norm, c.eps, T, E, stream_));
         }
         a.K = E;
         const DevW* wgu[2] = {&L.wg, &L.wu};
@@ -1434,9 +1500,10 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
                 float* ys[2] = {g_, u_};
                 const int lds[2] = {F, F};
                 if (fuse_ffn) {
+                    // SwiGLU in the epilogue; GELU (gemma2) in its own kernel below
                     const GemvPro pro{PRO_NORM, x_, E, nullptr, 0, L.ffn_norm, c.eps};
                     if (probe_) dump_img_ = probe_img_;
-                    const bool ok = gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro, true);
+                    const bool ok = gemv_group(wgu, ys, lds, nullptr, 2, a, T, EPI_STORE, err, &pro, !c.gelu);
                     dump_img_ = nullptr;
                     if (!ok || (probe_ && !probe_image(2, T, E, err))) return false;
                 } else {
@@ -1444,11 +1511,18 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
                 }
             }
             a.K = F;
-            const bool tp = tp_world_ > 1;
-            float* dy = tp ? tp_tmp_ : x_;
-            const int depi = tp ? EPI_STORE : EPI_ADD;
+            const bool tp = tp_world_ > 1, post = L.post_ffn_norm != nullptr;
+            float* dy = tp || post ? tp_tmp_ : x_;
+            const int depi = tp || post ? EPI_STORE : EPI_ADD;
             const DevW* wd[1] = {&L.wd};
-            if (fuse_ffn && fusable(wd, 1, T)) {   // h = silu(g) * u already in g_
+            if (c.gelu) {   // h = gelu(g) * u, quantised, then the down projection
+                CKP(PC_NORMQ, 0, fbk_act_mul_quant(g_, F, u_, F, T, F, probe_ ? probe_h_ : nullptr, F, &a, want32_f_,
+                                                   wantk_f_, 1, stream_));
+                if (probe_ && (!probe_float(3, probe_h_, T, F, err) ||
+                               !probe_planes(3, a, T, F, want32_f_, wantk_f_, err)))
+                    return false;
+                if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err)) return false;
+            } else if (fuse_ffn && fusable(wd, 1, T)) {   // h = silu(g) * u already in g_
                 const GemvPro pro{PRO_QUANT, g_, F, nullptr, 0, nullptr, 0.0f};
                 if (probe_ && !probe_float(3, g_, T, F, err)) return false;
                 if (probe_) dump_img_ = probe_img_;
@@ -1471,6 +1545,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
                 if (!gemv(L.wd, a, T, dy, E, nullptr, depi, nullptr, 0, nullptr, err)) return false;
             }
             if (tp && !tp_reduce_add(T, err)) return false;
+            if (post) CKP(PC_NORMQ, 0, fbk_rmsnorm_add(x_, E, tp_tmp_, E, L.post_ffn_norm, c.eps, T, E, stream_));
         }
     }
     return true;
@@ -1671,6 +1746,9 @@ bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err, unsi
     float* ydst = tp ? tp_logits_ + (size_t)tp_rank_ * n * c.out_rows : logits_dev;
     const int ldy = tp ? c.out_rows : c.vocab;
     bool k = false;
+    // gemma2's final soft cap comes before any argmax: the GEMV's argmax keys
+    // would see the uncapped logits
+    if (c.final_softcap > 0.0f) keys = nullptr;
     if (fusable(wo, 1, n)) {
         const GemvPro pro{PRO_NORM, x_ + (size_t)row0 * E, E, nullptr, 0, out_norm_, c.eps};
         k = keys != nullptr;
@@ -1680,6 +1758,7 @@ bool Engine::run_head(int row0, int n, float* logits_dev, std::string* err, unsi
                                            wantk_e_, stream_));
         if (!gemv(out_w_, a, n, ydst, ldy, nullptr, EPI_STORE, xb_, E, nullptr, err)) return false;
     }
+    if (c.final_softcap > 0.0f) CKP(PC_OTHER, 0, fbk_softcap(ydst, c.out_rows, n, ldy, c.final_softcap, stream_));
     if (keyed) *keyed = k;
     if (tp) {
         if (k && nccl_api(err)->all_reduce(keys, keys, (size_t)n, ncclUint64, ncclMax, (ncclComm_t)nccl_, stream_) !=
@@ -1783,12 +1862,19 @@ bool Engine::upload_tokens(const int32_t* ids, const int* sids, const int* pos, 
     return true;
 }
 
+bool Engine::embed_rows(int T, std::string* err) {
+    const Config& c = cfg_;
+    CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, T, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
+    if (c.embd_scale != 1.0f) CKP(PC_OTHER, 0, fbk_scale(x_, (size_t)T * c.n_embd, c.embd_scale, stream_));
+    return true;
+}
+
 bool Engine::capture_graph(int key, std::string* err) {
     const int T = key == 0 ? 1 : key;
     cudaGraph_t graph = nullptr;
     CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
     std::string e2;
-    bool ok = fbk_embed(embd_.type, embd_.d, cfg_.n_embd, embd_.n_out, ids_, T, x_, cfg_.n_embd, fbk_gemv_error_flag(), stream_) == 0;
+    bool ok = embed_rows(T, &e2);
     ok = ok && run_layers(T, cfg_.n_ctx, true, &e2);
     bool keyed = false;
     ok = ok && run_head(0, T, logits_, &e2, amax_keys_, &keyed, key != 0);
@@ -1840,7 +1926,7 @@ bool Engine::forward(int sid, const int32_t* ids, int T, float* logits_last, flo
         if (!graphs_.count(1) && !capture_graph(1, err)) return false;
         CK(cudaGraphLaunch(graphs_[1], stream_));
     } else {
-        CKP(PC_OTHER, 0, fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, T, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
+        if (!embed_rows(T, err)) return false;
         if (!run_layers(T, pos0 + T, T == 1, err)) return false;
         const int row0 = all ? 0 : T - 1;
         if (!run_head(row0, nrows, logits_, err)) return false;
@@ -1875,7 +1961,7 @@ bool Engine::decode_argmax(int sid, int32_t id, const int32_t* recent, int n_rec
         if (!graphs_.count(1) && !capture_graph(1, err)) return false;
         CK(cudaGraphLaunch(graphs_[1], stream_));
     } else {
-        CK(fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, 1, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
+        if (!embed_rows(1, err)) return false;
         if (!run_layers(1, pos0 + 1, true, err)) return false;
         if (!run_head(0, 1, logits_, err)) return false;
     }
@@ -1931,7 +2017,7 @@ bool Engine::step_tokens(const int* sids, const int32_t* ids, const int* pos, in
     // below every token's own position: attention reads them once for all
     {
         int bp = 0;
-        if (n >= 2 && n <= kPrefixMaxBatch) {
+        if (n >= 2 && n <= kPrefixMaxBatch && c.attn_softcap <= 0.0f && c.sliding_window <= 0) {
             const std::vector<int>& p0 = seqs_[sids[0]].pages;
             size_t common = p0.size();
             for (int i = 1; i < n && common > 0; ++i) {
@@ -1957,7 +2043,7 @@ bool Engine::step_tokens(const int* sids, const int32_t* ids, const int* pos, in
     } else {
         int max_ctx = 0;
         for (int i = 0; i < n; ++i) max_ctx = std::max(max_ctx, pos[i] + 1);
-        CK(fbk_embed(embd_.type, embd_.d, c.n_embd, embd_.n_out, ids_, n, x_, c.n_embd, fbk_gemv_error_flag(), stream_));
+        if (!embed_rows(n, err)) return false;
         if (!run_layers(n, max_ctx, true, err)) return false;
         if (!run_head(0, n, logits_, err)) return false;
         CK(fbk_argmax(logits_, c.vocab, n, c.vocab, argmax_, stream_));

@@ -33,6 +33,13 @@ struct Config {
     float eps = 1e-5f, freq_base = 10000.0f;
     int bos = 1, eos = 2;
     bool tied_output = false, neox = false, qk_norm = false;
+    // gemma2 (src/model.cpp:488-496): norm weights stored as w - 1, GELU in
+    // the FFN, the embedding scaled by sqrt(n_embd), attention-score and
+    // final-logit soft caps, a sliding window on the even layers, and
+    // post-attention / post-FFN norms before the residual adds
+    bool norm_plus_one = false, gelu = false, post_norms = false;
+    float embd_scale = 1.0f, attn_softcap = 0.0f, final_softcap = 0.0f;
+    int sliding_window = 0;
     int n_experts = 0, n_experts_per_tok = 0, n_ff_exp = 0;
     // tensor parallelism: the head counts and n_ff above are this rank's
     // shares; the model's own values are kept here (equal without it)
@@ -69,6 +76,7 @@ bool tp_plan(int n_head, int n_head_kv, int head_dim, int n_ff, int vocab, int n
 void build_rope_table(const Config& c, const float* ff, std::vector<float>& cs, std::vector<float>& sn);
 
 struct DevW {
+    std::string name;   // the GGUF tensor it is uploaded from (a fused tensor for phi3's q/k/v and gate/up views)
     int type = -1;
     int n_in = 0, n_out = 0, n_exp = 1;   // this rank's shard (the whole tensor without tensor parallelism)
     // shard of the GGUF tensor: rows [row0, row0 + n_out) of its n_out_src,
@@ -85,6 +93,7 @@ struct DevLayer {
     DevW wq, wk, wv, wo, wg, wu, wd, gate_inp, gate_exps, up_exps, down_exps;
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
+    float *post_attn_norm = nullptr, *post_ffn_norm = nullptr;   // gemma2
 };
 
 // Debug record of one layer's int8 activations (Engine::layer_probe). Stage
@@ -230,6 +239,8 @@ private:
     // so attention can append each token's K/V inside the fused kernel
     bool run_layers(int T, int max_ctx, bool distinct, std::string* err, int l0 = 0, int l1 = -1);
     bool step_tokens(const int* sids, const int32_t* ids, const int* pos, int n, std::string* err);
+    // embedding rows of the T ids in ids_ into x_ (scaled for gemma2)
+    bool embed_rows(int T, std::string* err);
     bool probe_float(int idx, const float* dev, int rows, int K, std::string* err);
     bool probe_planes(int stage, const ActQ& a, int rows, int K, bool want32, bool wantk, std::string* err);
     bool probe_image(int stage, int rows, int K, std::string* err);

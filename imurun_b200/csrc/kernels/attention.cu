@@ -29,6 +29,16 @@ __device__ __forceinline__ size_t kv_off(const KvView& kv, int layer, int head, 
            (size_t)(pos % kv.page_size) * (kv.head_stride / kv.page_size);
 }
 
+// Gemma-2's attention-score soft cap (ops.cpp attention_batch): the scaled
+// score s becomes cap * tanh(s / cap); cap 0 leaves it unchanged.
+__device__ __forceinline__ float soft_cap(float s, float cap) {
+    return cap > 0.0f ? __fmul_rn(cap, tanhf(__fdiv_rn(s, cap))) : s;
+}
+// First key a token at pos sees under a sliding window (0 without one).
+__device__ __forceinline__ int window_lo(const KvView& kv, int pos) {
+    return kv.window > 0 ? max(0, pos - kv.window + 1) : 0;
+}
+
 __global__ void k_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int H, int HKV, int D,
                               int rot, int neox, const float* rcos, const float* rsin, KvView kv, int layer) {
     pdl_trigger();
@@ -128,6 +138,7 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
     const int jb = j0 + 32 * warp;
     const int j = jb + lane;
     const bool valid = j < n_keys;
+    const bool live = valid && j >= window_lo(kv, n_keys - 1);
     float sc[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) sc[g] = 0.0f;
@@ -168,9 +179,9 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) {
         if (g >= G) break;
-        const float s = valid ? __fmul_rn(sc[g], scale) : -INFINITY;
+        const float s = live ? soft_cap(__fmul_rn(sc[g], scale), kv.softcap) : -INFINITY;
         m[g] = warp_max(s);
-        sc[g] = valid ? expf(s - m[g]) : 0.0f;
+        sc[g] = live ? expf(s - m[g]) : 0.0f;
         l[g] = warp_sum(sc[g]);
     }
     // P.V, lane owns dims [dper*lane, dper*lane + dper)
@@ -440,6 +451,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     const size_t pblk = (size_t)16 * D;   // elements of one page's piece of this head
     const int b_own = pos / kDecKeys;
     const int nf = fresh_rows(kv, t, seq, pos);
+    const int jlo = window_lo(kv, pos);
 
     // bulk copies of my i-th block into slot i & 1: lane 0 sets the expected
     // bytes, lane pp (< 4) reads its page-table entry and copies that page
@@ -595,7 +607,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
                     a += __shfl_xor_sync(0xffffffffu, a, 1);
                     a += __shfl_xor_sync(0xffffffffu, a, 2);
                     a += __shfl_xor_sync(0xffffffffu, a, 4);
-                    if (part == 0 && valid) ss[g * kDecKeys + key] = __fmul_rn(a, scale);
+                    if (part == 0 && valid)
+                        ss[g * kDecKeys + key] = j0 + key >= jlo ? soft_cap(__fmul_rn(a, scale), kv.softcap) : -INFINITY;
                 }
             }
         }
@@ -607,8 +620,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             const float s1 = lane + 32 < kb ? ss[g * kDecKeys + lane + 32] : -INFINITY;
             const float mb = warp_max(fmaxf(s0, s1));
             const float mo = sm[g], mn = fmaxf(mo, mb);
-            const float p0 = lane < kb ? expf(s0 - mn) : 0.0f;
-            const float p1 = lane + 32 < kb ? expf(s1 - mn) : 0.0f;
+            const float p0 = s0 > -INFINITY ? expf(s0 - mn) : 0.0f;
+            const float p1 = s1 > -INFINITY ? expf(s1 - mn) : 0.0f;
             const float sum = warp_sum(p0 + p1);
             ss[g * kDecKeys + lane] = p0;
             ss[g * kDecKeys + lane + 32] = p1;
@@ -791,12 +804,12 @@ __device__ __forceinline__ void tc_q_frags(const float* sq, int G, int lane, uin
 // rows at stride D + 8 halves; kb keys valid) into its online softmax state
 // (m_r, l_r for the lane's two heads, O^T fragments acc).
 template <int D>
-__device__ __forceinline__ void tc_warp_block(const __half* K, const __half* V, int kw, int kb, float scale,
-                                              const uint32_t (&qh)[D / 16][2], const uint32_t (&ql)[D / 16][2],
-                                              float (&m_r)[2], float (&l_r)[2], float (&acc)[D / 16][4], __half* pw,
-                                              int lane) {
+__device__ __forceinline__ void tc_warp_block(const __half* K, const __half* V, int kw, int kb, int klo, float cap,
+                                              float scale, const uint32_t (&qh)[D / 16][2],
+                                              const uint32_t (&ql)[D / 16][2], float (&m_r)[2], float (&l_r)[2],
+                                              float (&acc)[D / 16][4], __half* pw, int lane) {
     constexpr int RS = D + 8, KS = D / 16;
-    if (kw >= kb) return;
+    if (kw >= kb || kw + 16 <= klo) return;
     const int gq = lane >> 2, k0 = 2 * (lane & 3), h0 = 2 * (lane & 3);
     const int r_in = (lane & 7) + ((lane >> 3) & 1) * 8, c_in = (lane >> 4) * 8;       // ldmatrix (K rows)
     const int key_in = (lane & 7) + ((lane >> 4) & 1) * 8, dim_in = ((lane >> 3) & 1) * 8;  // ldmatrix.trans (V)
@@ -815,10 +828,11 @@ __device__ __forceinline__ void tc_warp_block(const __half* K, const __half* V, 
     // c0: (key lane/4, head h0), c1: (lane/4, h0+1), c2: (lane/4+8, h0), c3: (lane/4+8, h0+1)
     const int ka = kw + (lane >> 2), kb2 = ka + 8;
     float sc[4];
-    sc[0] = ka < kb ? __fmul_rn(c[0], scale) : -INFINITY;
-    sc[1] = ka < kb ? __fmul_rn(c[1], scale) : -INFINITY;
-    sc[2] = kb2 < kb ? __fmul_rn(c[2], scale) : -INFINITY;
-    sc[3] = kb2 < kb ? __fmul_rn(c[3], scale) : -INFINITY;
+    const bool va = ka < kb && ka >= klo, vb = kb2 < kb && kb2 >= klo;
+    sc[0] = va ? soft_cap(__fmul_rn(c[0], scale), cap) : -INFINITY;
+    sc[1] = va ? soft_cap(__fmul_rn(c[1], scale), cap) : -INFINITY;
+    sc[2] = vb ? soft_cap(__fmul_rn(c[2], scale), cap) : -INFINITY;
+    sc[3] = vb ? soft_cap(__fmul_rn(c[3], scale), cap) : -INFINITY;
     float corr[2], p[4];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -995,6 +1009,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const int seq = kv.tok_seq[t];
     const int b_own = pos / kTcKeys;
     const int nf = fresh_rows(kv, t, seq, pos);
+    const int jlo = window_lo(kv, pos);
 
     // warp 0: one bulk copy per K row and per V row of my i-th block (slot i & 1)
     auto issue = [&](int i) {
@@ -1122,7 +1137,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
                            32 * kTcWarps);
             __syncthreads();
         }
-        tc_warp_block<D>(K, V, 16 * warp, kb, scale, qh, ql, m_r, l_r, acc, pw, lane);
+        tc_warp_block<D>(K, V, 16 * warp, kb, jlo - j0, kv.softcap, scale, qh, ql, m_r, l_r, acc, pw, lane);
         __syncthreads();
         if (warp == kIssuer && i + 2 < nb_mine) issue(i + 2);
     }
@@ -1366,7 +1381,7 @@ __global__ void __launch_bounds__(256) k_attn_prefix_tc(const float* __restrict_
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
             for (int i = 0; i < nbp; ++i)
-                tc_warp_block<D>(sk + (size_t)i * L::tile, sv + (size_t)i * L::tile, 16 * w, kTcKeys, scale, qh, ql, m_r,
+                tc_warp_block<D>(sk + (size_t)i * L::tile, sv + (size_t)i * L::tile, 16 * w, kTcKeys, 0, 0.0f, scale, qh, ql, m_r,
                                  l_r, acc, pw, lane);
             if (more) {
                 float* sb = pstate + ((((size_t)t * HKV + hk) * C + r) * kTcWarps + w) * 32 * kStateFloats(KS);
@@ -1528,7 +1543,8 @@ __global__ void __launch_bounds__(32 * kMaxG) k_attn_prefill_tc(const float* __r
             for (int c = 0; c < 4; ++c) {
                 const int j = kt * kPfKeys + 8 * nt + 2 * tig + (c & 1);
                 const int pr = (c >> 1) ? pb : pa;
-                s[nt][c] = j <= pr ? __fmul_rn(s[nt][c], scale) : -INFINITY;
+                s[nt][c] = j <= pr && (kv.window <= 0 || j > pr - kv.window)
+                               ? soft_cap(__fmul_rn(s[nt][c], scale), kv.softcap) : -INFINITY;
                 mx[c >> 1] = fmaxf(mx[c >> 1], s[nt][c]);
             }
         float corr[2];
@@ -1843,7 +1859,9 @@ extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, con
         float* pp = (T > 1 && !batch_cluster && part && part_floats >= fbk_attention_decode_part_floats(T, H, HKV, D))
                         ? part : nullptr;
         static const bool no_prefix = getenv("FISH_ATTN_NO_PREFIX") != nullptr;
-        const bool pf = pp && pre && pstate && !no_prefix && pstate_floats >= fbk_attention_prefix_state_floats(T, HKV, D);
+        // the shared-prefix kernel reads blocks for every token alike: no soft cap, no window
+        const bool pf = pp && pre && pstate && !no_prefix && kv.softcap <= 0.0f && kv.window <= 0 &&
+                        pstate_floats >= fbk_attention_prefix_state_floats(T, HKV, D);
         if (D == 128)
             return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo,
                                          pp, pf ? pre : nullptr, pf ? pstate : nullptr, st);

@@ -89,6 +89,16 @@ int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float eps, int T,
                       const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
 int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                        const fb::ActQ* a, int want32, int wantk, cudaStream_t st);
+// h = act(g) * u, quantised: act = silu, or the tanh form of GELU (gelu = 1)
+int fbk_act_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
+                      const fb::ActQ* a, int want32, int wantk, int gelu, cudaStream_t st);
+// x[t] += rmsnorm(y[t]) * w over K values (post norms)
+int fbk_rmsnorm_add(float* x, int ldx, const float* y, int ldy, const float* w, float eps, int T, int K,
+                    cudaStream_t st);
+// x[i] *= s for n floats
+int fbk_scale(float* x, size_t n, float s, cudaStream_t st);
+// rows of n logits (stride ldx): cap * tanh(x / cap)
+int fbk_softcap(float* x, int n, int rows, int ldx, float cap, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);
 // Tokens per GEMV launch when a call has more than fit one: 8 (the streamed
 // kernel's and the direct kernel's largest token count).
@@ -157,6 +167,10 @@ struct KvView {
     int f16;
     int n_pages;             // pages in the pool (page indices outside are clamped and flagged)
     int* err;                // device error flag (nullable): 5 = page index out of range
+    // gemma2: scores become softcap * tanh(score / softcap) (0: off), and a
+    // token at pos sees keys pos - window + 1 .. pos only (0: all keys)
+    float softcap = 0.0f;
+    int window = 0;
 };
 // RoPE on q (in place) and k, then K/V stored at each token's position.
 int fbk_rope_append(float* q, int ldq, const float* k, const float* v, int ldkv, int T, int H, int HKV, int D,

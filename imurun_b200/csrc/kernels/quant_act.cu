@@ -10,6 +10,8 @@
 // Work split: a row of K values is cut into 256-value chunks; one warp owns a
 // chunk (lane = 8 consecutive values) and a CTA of 4 warps owns 4 chunks, so a
 // single decode token still spreads over K/1024 CTAs.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -145,10 +147,18 @@ __global__ void __launch_bounds__(32 * kNormWarps) k_rmsnorm_quant(const float* 
     if (want32 || wantk) quant_chunk(v, lane, K, t, c, a, want32, wantk);
 }
 
-// h = silu(g) * u (src/ops.cpp:25-31, src/model.cpp:1501-1506), then quantised.
+// h = act(g) * u, then quantised: act = silu (src/ops.cpp:25-31,
+// src/model.cpp:1501-1506), or with gelu set the tanh form of GELU
+// (src/ops.cpp:32-38, gemma2), 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))).
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float c = 0.7978845608028654f;
+    const float v3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(__fmul_rn(c, __fadd_rn(v, v3)))));
+}
+
 __global__ void __launch_bounds__(128) k_silu_mul_quant(const float* __restrict__ g, int ldg, const float* __restrict__ u,
                                                         int ldu, int F, float* __restrict__ h, int ldh, ActQ a,
-                                                        int want32, int wantk) {
+                                                        int want32, int wantk, int gelu) {
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.y, lane = threadIdx.x & 31;
@@ -159,7 +169,7 @@ __global__ void __launch_bounds__(128) k_silu_mul_quant(const float* __restrict_
     load8(u + (size_t)t * ldu, c * 256, lane, F, uv);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float sv = __fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i])));
+        const float sv = gelu ? gelu_tanh(gv[i]) : __fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i])));
         v[i] = __fmul_rn(sv, uv[i]);
     }
     const int i0 = c * 256 + 8 * lane;
@@ -169,6 +179,57 @@ __global__ void __launch_bounds__(128) k_silu_mul_quant(const float* __restrict_
         for (int i = 0; i < 8; ++i) if (i0 + i < F) o[i] = v[i];
     }
     if (want32 || wantk) quant_chunk(v, lane, F, t, c, a, want32, wantk);
+}
+
+// Gemma-2's post norms (src/model.cpp post_attention_norm / post_ffw_norm):
+// x[t] += rmsnorm(y[t]) * w, the norm's squares summed in the order of every
+// other RMSNorm here (sumsq8 per 256-value chunk, chunks by warp, warps in
+// order).
+__global__ void __launch_bounds__(32 * kNormWarps) k_rmsnorm_add(float* __restrict__ x, int ldx,
+                                                                const float* __restrict__ y, int ldy,
+                                                                const float* __restrict__ w, float eps, int K) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ double part[kNormWarps];
+    const int t = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_chunks = (K + 255) / 256;
+    const float* yr = y + (size_t)t * ldy;
+    double s = 0.0;
+    for (int c = warp; c < n_chunks; c += kNormWarps) {
+        float v[8];
+        load8(yr, c * 256, lane, K, v);
+        s = __dadd_rn(s, sumsq8(v));
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) part[warp] = s;
+    __syncthreads();
+    const float sc = norm_total(part, K, eps);
+    const int c = blockIdx.x * kNormWarps + warp;
+    if (c >= n_chunks) return;
+    float v[8];
+    load8(yr, c * 256, lane, K, v);
+    const int i0 = c * 256 + 8 * lane;
+    float* xr = x + (size_t)t * ldx;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i0 + i < K) xr[i0 + i] = __fadd_rn(xr[i0 + i], __fmul_rn(__fmul_rn(v[i], sc), w[i0 + i]));
+}
+
+// x[i] *= s (gemma2's embedding scale, src/model.cpp:1624-1627)
+__global__ void k_scale(float* __restrict__ x, size_t n, float s) {
+    pdl_trigger();
+    pdl_wait();
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = __fmul_rn(x[i], s);
+}
+
+// cap * tanh(x / cap) (gemma2's final logit soft cap, src/model.cpp:1802-1805)
+__global__ void k_softcap(float* __restrict__ x, int n, int ldx, float cap) {
+    pdl_trigger();
+    pdl_wait();
+    float* r = x + (size_t)blockIdx.y * ldx;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        r[i] = __fmul_rn(cap, tanhf(__fdiv_rn(r[i], cap)));
 }
 
 }  // namespace fb
@@ -198,8 +259,33 @@ extern "C" int fbk_rmsnorm_quant(const float* x, int ldx, const float* w, float 
 
 extern "C" int fbk_silu_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
                                   const ActQ* a, int want32, int wantk, cudaStream_t st) {
+    return fbk_act_mul_quant(g, ldg, u, ldu, T, F, h, ldh, a, want32, wantk, 0, st);
+}
+
+extern "C" int fbk_act_mul_quant(const float* g, int ldg, const float* u, int ldu, int T, int F, float* h, int ldh,
+                                 const ActQ* a, int want32, int wantk, int gelu, cudaStream_t st) {
     if (T <= 0) return 0;
     if (F % 8 || ldg % 4 || ldu % 4) return (int)cudaErrorInvalidValue;
     return (int)fbk_launch(k_silu_mul_quant, qgrid(F, T), dim3(32 * kQWarps), 0, st, g, ldg, u, ldu, F, h, ldh, *a, want32,
-                           wantk);
+                           wantk, gelu);
+}
+
+extern "C" int fbk_rmsnorm_add(float* x, int ldx, const float* y, int ldy, const float* w, float eps, int T, int K,
+                               cudaStream_t st) {
+    if (T <= 0) return 0;
+    if (K % 8 || ldy % 4) return (int)cudaErrorInvalidValue;
+    const dim3 grid(((K + 255) / 256 + kNormWarps - 1) / kNormWarps, T);
+    return (int)fbk_launch(k_rmsnorm_add, grid, dim3(32 * kNormWarps), 0, st, x, ldx, y, ldy, w, eps, K);
+}
+
+extern "C" int fbk_scale(float* x, size_t n, float s, cudaStream_t st) {
+    if (n == 0) return 0;
+    const int ctas = (int)std::min<size_t>(1184, (n + 255) / 256);
+    return (int)fbk_launch(k_scale, dim3(ctas), dim3(256), 0, st, x, n, s);
+}
+
+extern "C" int fbk_softcap(float* x, int n, int rows, int ldx, float cap, cudaStream_t st) {
+    if (rows <= 0 || n <= 0) return 0;
+    if (!(cap > 0.0f)) return (int)cudaErrorInvalidValue;
+    return (int)fbk_launch(k_softcap, dim3((n + 1023) / 1024, rows), dim3(256), 0, st, x, n, ldx, cap);
 }

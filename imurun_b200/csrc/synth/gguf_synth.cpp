@@ -337,6 +337,14 @@ typedef struct fish_synth_config {
                                  // a built-in text)
     int qk_norm;                 // 1: per-head q/k RMSNorm weights (attn_q_norm / attn_k_norm, qwen3),
                                  // 1 + N(0, 0.1) so they are not the identity
+    // gemma2: attention-score and final-logit soft caps (0: the format's
+    // defaults 50 / 30) and the sliding window of the even layers (0: 4096)
+    float attn_softcap, final_softcap;
+    int sliding_window;
+    // phi3 longrope: rope.scaling.original_context_length (0: n_ctx_train)
+    // and rope.scaling.attn_factor (0: 1)
+    int rope_orig_ctx;
+    float rope_attn_factor;
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -356,11 +364,30 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     auto add = [&](const std::string& n, std::vector<uint64_t> ne, uint32_t t, int fill, float sd) {
         ts.push_back(TensorSpec{n, std::move(ne), t, fill, sd});
     };
+    // gemma2 stores its norm weights as w with 1 + w applied (so N(0, 0.1)
+    // here is 1 + N(0, 0.1)), adds post-attention / post-FFN norms and ties
+    // the output to the embedding; phi3 fuses q|k|v and gate|up and carries
+    // longrope factor vectors
+    const bool gemma2 = arch == "gemma2", phi3 = arch == "phi3";
+    const int nfill = gemma2 ? 0 : 1;
+    const float nsd = gemma2 ? 0.1f : 0.0f;
     add("token_embd.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(c->vocab)}, tm, 0, wstd);
+    if (phi3) {
+        add("rope_factors_short.weight", {static_cast<uint64_t>(D / 2)}, T_F32, 2, 0.05f);
+        add("rope_factors_long.weight", {static_cast<uint64_t>(D / 2)}, T_F32, 2, 0.25f);
+    }
     for (int i = 0; i < c->n_layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
         const uint32_t tv = q8 ? T_Q8_0 : ((i % 2) == 0 ? T_Q6_K : T_Q4_K);
-        add(p + "attn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
+        add(p + "attn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
+        if (phi3) {
+            add(p + "attn_qkv.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>((H + 2 * HKV) * D)}, tm, 0, wstd);
+            add(p + "attn_output.weight", {static_cast<uint64_t>(H * D), static_cast<uint64_t>(E)}, tm, 0, wstd);
+            add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
+            add(p + "ffn_up.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(2 * F)}, tm, 0, wstd);
+            add(p + "ffn_down.weight", {static_cast<uint64_t>(F), static_cast<uint64_t>(E)}, tv, 0, wstd);
+            continue;
+        }
         add(p + "attn_q.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(H * D)}, tm, 0, wstd);
         add(p + "attn_k.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(HKV * D)}, tm, 0, wstd);
         add(p + "attn_v.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(HKV * D)}, tv, 0, wstd);
@@ -374,7 +401,9 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
             add(p + "attn_k_norm.weight", {static_cast<uint64_t>(D)}, T_F32, 2, 0.1f);
         }
         add(p + "attn_output.weight", {static_cast<uint64_t>(H * D), static_cast<uint64_t>(E)}, tm, 0, wstd);
-        add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
+        if (gemma2) add(p + "post_attention_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
+        add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
+        if (gemma2) add(p + "post_ffw_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
         if (c->n_experts > 0) {
             const uint64_t NE = static_cast<uint64_t>(c->n_experts);
             add(p + "ffn_gate_inp.weight", {static_cast<uint64_t>(E), NE}, T_F32, 0,
@@ -388,8 +417,9 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
             add(p + "ffn_down.weight", {static_cast<uint64_t>(F), static_cast<uint64_t>(E)}, tv, 0, wstd);
         }
     }
-    add("output_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
-    add("output.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(c->vocab)}, q8 ? T_Q8_0 : T_Q6_K, 0, wstd);
+    add("output_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
+    if (!gemma2)
+        add("output.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(c->vocab)}, q8 ? T_Q8_0 : T_Q6_K, 0, wstd);
 
     for (auto& t : ts) {
         if (t.ne[0] % block_elems(t.type)) return fail("row not a whole number of blocks");
@@ -423,6 +453,17 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     w.kv_f32(k("attention.layer_norm_rms_epsilon"), c->eps > 0 ? c->eps : 1e-5f); ++n_kv;
     w.kv_f32(k("rope.freq_base"), c->freq_base > 0 ? c->freq_base : 10000.0f); ++n_kv;
     w.kv_u32(k("vocab_size"), static_cast<uint32_t>(c->vocab)); ++n_kv;
+    if (gemma2) {
+        w.kv_f32(k("attn_logit_softcapping"), c->attn_softcap > 0 ? c->attn_softcap : 50.0f); ++n_kv;
+        w.kv_f32(k("final_logit_softcapping"), c->final_softcap > 0 ? c->final_softcap : 30.0f); ++n_kv;
+        w.kv_u32(k("attention.sliding_window"), static_cast<uint32_t>(c->sliding_window > 0 ? c->sliding_window : 4096)); ++n_kv;
+    }
+    if (phi3) {
+        w.kv_str(k("rope.scaling.type"), "longrope"); ++n_kv;
+        w.kv_u32(k("rope.scaling.original_context_length"),
+                 static_cast<uint32_t>(c->rope_orig_ctx > 0 ? c->rope_orig_ctx : (c->n_ctx_train > 0 ? c->n_ctx_train : 8192))); ++n_kv;
+        w.kv_f32(k("rope.scaling.attn_factor"), c->rope_attn_factor > 0 ? c->rope_attn_factor : 1.0f); ++n_kv;
+    }
     if (c->n_experts > 0) {
         w.kv_u32(k("expert_count"), static_cast<uint32_t>(c->n_experts)); ++n_kv;
         w.kv_u32(k("expert_used_count"), static_cast<uint32_t>(c->n_experts_per_tok)); ++n_kv;

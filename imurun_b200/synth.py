@@ -53,6 +53,11 @@ class SynthConfig:
     chat_template: str = ""   # written as tokenizer.chat_template when not empty
     bpe_pre: str = ""         # non-empty: byte-level BPE vocabulary with this tokenizer.ggml.pre name
     qk_norm: int = 0          # 1: per-head q/k RMSNorm weights (qwen3)
+    attn_softcap: float = 0.0   # gemma2: score soft cap (0: 50)
+    final_softcap: float = 0.0  # gemma2: logit soft cap (0: 30)
+    sliding_window: int = 0     # gemma2: window of the even layers (0: 4096)
+    rope_orig_ctx: int = 0      # phi3 longrope: original context (0: n_ctx_train)
+    rope_attn_factor: float = 0.0   # phi3 longrope: rotation scale (0: 1)
 
 
 PRESETS = {
@@ -65,6 +70,15 @@ PRESETS = {
     # Qwen3-shaped (not a benchmark config): per-head q/k RMSNorm, no qkv bias
     "qwen3": SynthConfig(arch="qwen3", n_layers=4, n_embd=1024, n_ff=3072, n_head=16, n_head_kv=8,
                          vocab=32000, freq_base=1000000.0, eps=1e-6, qk_norm=1, wtype=12),
+    # Gemma2-shaped (not a benchmark config): soft caps small enough to bite
+    # on random weights, a 64-position window on the even layers
+    "gemma2": SynthConfig(arch="gemma2", n_layers=4, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=4,
+                          vocab=32000, freq_base=10000.0, eps=1e-6, wtype=12, attn_softcap=0.5,
+                          final_softcap=2.0, sliding_window=64),
+    # Phi3-shaped (not a benchmark config): fused q|k|v and gate|up, longrope
+    # factors (the long set past a 512-position original context)
+    "phi3": SynthConfig(arch="phi3", n_layers=4, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=8,
+                        vocab=32000, freq_base=10000.0, wtype=12, rope_orig_ctx=512, rope_attn_factor=1.19),
     "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
                            vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
                            wtype=12, n_ctx_train=32768),
@@ -86,6 +100,9 @@ class _CConfig(ctypes.Structure):
         ("chat_template", ctypes.c_char_p),
         ("bpe_pre", ctypes.c_char_p),
         ("qk_norm", ctypes.c_int),
+        ("attn_softcap", ctypes.c_float), ("final_softcap", ctypes.c_float),
+        ("sliding_window", ctypes.c_int),
+        ("rope_orig_ctx", ctypes.c_int), ("rope_attn_factor", ctypes.c_float),
     ]
 
 
@@ -107,7 +124,8 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
     c = _CConfig(cfg.arch.encode(), cfg.n_layers, cfg.n_embd, cfg.n_ff, cfg.n_head, cfg.n_head_kv,
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
-                 cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm)
+                 cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm, cfg.attn_softcap,
+                 cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor)
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

@@ -19,7 +19,9 @@ from imurun_b200 import native
 P, I, CP = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
 SUFFIXES = ["block_count", "context_length", "embedding_length", "feed_forward_length",
             "attention.head_count", "attention.head_count_kv", "attention.layer_norm_rms_epsilon",
-            "rope.freq_base", "rope.dimension_count", "expert_count", "expert_used_count", "vocab_size"]
+            "rope.freq_base", "rope.dimension_count", "expert_count", "expert_used_count", "vocab_size",
+            "attn_logit_softcapping", "final_logit_softcapping", "attention.sliding_window",
+            "rope.scaling.type", "rope.scaling.original_context_length", "rope.scaling.attn_factor"]
 GENERAL = ["general.architecture", "general.name", "general.alignment", "tokenizer.ggml.model",
            "tokenizer.ggml.tokens", "tokenizer.ggml.scores", "tokenizer.ggml.token_type",
            "tokenizer.ggml.bos_token_id", "tokenizer.ggml.eos_token_id", "tokenizer.ggml.add_bos_token",
@@ -54,13 +56,15 @@ def _digest(fn, path, keys):
     return buf.raw[:n].decode()
 
 
-@pytest.mark.parametrize("name", ["tiny", "qwen7b", "mixtral"])
+@pytest.mark.parametrize("name", ["tiny", "qwen7b", "mixtral", "gemma2", "phi3"])
 def test_gguf_digest_matches_reference(ref_lib, ours, synth_dir, name):
     from imurun_b200 import synth
     cfg = {"tiny": lambda: synth.preset("tiny"),
            "qwen7b": lambda: synth.preset("qwen7b", layers=1),
            "mixtral": lambda: synth.preset("mixtral", layers=1, n_embd=512, n_ff=1024, n_head=8,
-                                                 n_head_kv=2)}[name]()
+                                                 n_head_kv=2),
+           "gemma2": lambda: synth.preset("gemma2", layers=1),
+           "phi3": lambda: synth.preset("phi3", layers=1)}[name]()
     path = synth.cached(cfg, synth_dir)
     arch_line = _digest(ours.fbx_gguf_digest, path, ["general.architecture"]).splitlines()[-1]
     arch = arch_line.split(" ", 3)[3]
