@@ -446,17 +446,19 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
     float* snew = reinterpret_cast<float*>(smem + L::off_n);
     const int pos = kv.tok_pos[t], n_keys = pos + 1;
     const int n_blocks = (n_keys + kDecKeys - 1) / kDecKeys;
-    const int nb_mine = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
+    // blocks wholly below a sliding window are skipped: this rank's blocks
+    // are b0 + r + C i
+    const int jlo = window_lo(kv, pos), b0 = jlo / kDecKeys;
+    const int nb_mine = r < n_blocks - b0 ? (n_blocks - b0 - r + C - 1) / C : 0;
     const int seq = kv.tok_seq[t];
     const size_t pblk = (size_t)16 * D;   // elements of one page's piece of this head
     const int b_own = pos / kDecKeys;
     const int nf = fresh_rows(kv, t, seq, pos);
-    const int jlo = window_lo(kv, pos);
 
     // bulk copies of my i-th block into slot i & 1: lane 0 sets the expected
     // bytes, lane pp (< 4) reads its page-table entry and copies that page
     auto issue = [&](int i) {   // called by all lanes of warp 0
-        const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0), np = (kb + 15) / 16;
+        const int b = b0 + r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0), np = (kb + 15) / 16;
         uint64_t* br = &bar[i & 1];
         if (lane == 0) mbar_expect_tx(br, (uint32_t)(2 * np * pblk * sizeof(E)));
         __syncwarp();
@@ -504,7 +506,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         }
     }
     // the token's own position: rotate k, store k and v, keep the stored values
-    if (b_own % C == r) {
+    if ((b_own - b0) % C == r) {
         const float* kr = knew + (size_t)t * ldkv + (size_t)hk * D;
         const float* vr = vnew + (size_t)t * ldkv + (size_t)hk * D;
         const size_t base = kv_off(kv, layer, hk, t, pos);
@@ -553,7 +555,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             break;
         }
         if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 5, s_tseq);   // first block landed
-        const int b = r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0);
+        const int b = b0 + r + C * i, j0 = b * kDecKeys, kb = min(kDecKeys, n_keys - j0);
         E* K = sk + (size_t)(i & 1) * L::kv_elems;
         E* V = sv + (size_t)(i & 1) * L::kv_elems;
         if (b == b_own) {
@@ -975,10 +977,14 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     // no block of the rank is left here, the rank partial is already in part.
     const int pos = kv.tok_pos[blockIdx.z], n_keys = pos + 1;
     const int n_blocks = (n_keys + kTcKeys - 1) / kTcKeys;
+    // Blocks wholly below a sliding window are skipped the same way (the
+    // rank's first i0 blocks, with no state to take over; a window and a
+    // shared prefix never come together).
     const int bp = GM && pre ? min(*pre, C * kPreMaxBlocks) : 0;
-    const int i0 = r < bp ? (bp - r + C - 1) / C : 0;
+    const int bs = bp > 0 ? bp : window_lo(kv, pos) / kTcKeys;
+    const int i0 = r < bs ? (bs - r + C - 1) / C : 0;
     const int nb_all = r < n_blocks ? (n_blocks - r + C - 1) / C : 0;
-    if (GM && i0 > 0 && nb_all == i0) return;
+    if (GM && bp > 0 && i0 > 0 && nb_all == i0) return;
     const int nb_mine = nb_all - i0;
     const unsigned long long t_kernel = gtimer();
     const bool tr = tracing() && !tracing_all() && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
@@ -1009,7 +1015,6 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     const int seq = kv.tok_seq[t];
     const int b_own = pos / kTcKeys;
     const int nf = fresh_rows(kv, t, seq, pos);
-    const int jlo = window_lo(kv, pos);
 
     // warp 0: one bulk copy per K row and per V row of my i-th block (slot i & 1)
     auto issue = [&](int i) {
@@ -1109,7 +1114,7 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
     for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
-    if (i0 > 0) {   // continue from the shared-prefix kernel's state of this warp
+    if (bp > 0 && i0 > 0) {   // continue from the shared-prefix kernel's state of this warp
         float* sb = const_cast<float*>(pstate) + ((((size_t)t * HKV + hk) * C + r) * kTcWarps + warp) * 32 * kStateFloats(KS);
         tc_state_io<KS, false>(sb, lane, m_r, l_r, acc);
     }
@@ -1137,7 +1142,8 @@ __global__ void __launch_bounds__(32 * kTcWarps) k_attn_decode_tc(
                            32 * kTcWarps);
             __syncthreads();
         }
-        tc_warp_block<D>(K, V, 16 * warp, kb, jlo - j0, kv.softcap, scale, qh, ql, m_r, l_r, acc, pw, lane);
+        tc_warp_block<D>(K, V, 16 * warp, kb, window_lo(kv, pos) - j0, kv.softcap, scale, qh, ql, m_r, l_r, acc, pw,
+                         lane);
         __syncthreads();
         if (warp == kIssuer && i + 2 < nb_mine) issue(i + 2);
     }
@@ -1479,7 +1485,9 @@ __global__ void __launch_bounds__(32 * kMaxG) k_attn_prefill_tc(const float* __r
         }
         pf_commit();
     };
-    load_tile(0, 0);
+    // key tiles wholly below every row's sliding window are skipped
+    const int kt_lo = kv.window > 0 ? max(0, kv.tok_pos[t0] - kv.window + 1) / kPfKeys : 0;
+    load_tile(kt_lo, kt_lo & 1);
 
     // q of this warp's head for the two rows as A fragments, hi and lo parts
     const int h = hk * G + warp;
@@ -1506,7 +1514,7 @@ __global__ void __launch_bounds__(32 * kMaxG) k_attn_prefill_tc(const float* __r
 #pragma unroll
         for (int c = 0; c < 4; ++c) o[dn][c] = 0.0f;
 
-    for (int kt = 0; kt < n_tiles; ++kt) {
+    for (int kt = kt_lo; kt < n_tiles; ++kt) {
         if (kt + 1 < n_tiles) {
             load_tile(kt + 1, (kt + 1) & 1);
             pf_wait<1>();
