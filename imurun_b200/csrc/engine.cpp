@@ -305,8 +305,8 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     const int model_ctx = c.n_ctx_train;
     c.n_ctx = n_ctx > 0 ? std::min(n_ctx, model_ctx > 0 ? model_ctx : n_ctx) : std::min(4096, model_ctx);
     if (c.n_ctx < 32) { if (err) *err = "context too small"; return false; }
-    if ((c.head_dim != 64 && c.head_dim != 128) || c.n_head / c.n_head_kv > 8) {
-        if (err) *err = "attention shape not supported by the B200 kernels (head_dim 64 or 128, <= 8 q heads per kv head)";
+    if ((c.head_dim != 64 && c.head_dim != 96 && c.head_dim != 128) || c.n_head / c.n_head_kv > 8) {
+        if (err) *err = "attention shape not supported by the B200 kernels (head_dim 64, 96 or 128, <= 8 q heads per kv head)";
         return false;
     }
     c.n_head_model = c.n_head;

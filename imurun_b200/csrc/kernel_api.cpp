@@ -359,7 +359,8 @@ struct TestPool {
 // then the split-key kernel (tc = 0) or the tensor-core prefill kernel
 static int attention_host(const float* q, const float* k, const float* v, int n_keys, int H, int HKV, int D, int pos0,
                           int T, int kv_f16, float* out, int tc) {
-    if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || (D != 64 && D != 128)) return -1;
+    if (!q || !k || !v || !out || T <= 0 || pos0 < 0 || pos0 + T > n_keys || H % HKV || (D != 64 && D != 96 && D != 128))
+        return -1;
     TRY(check_device());
     TestPool tp;
     TRY(tp.make(n_keys, HKV, D, kv_f16, T, pos0));
@@ -411,7 +412,7 @@ int fbx_attention_decode(const float* q, const float* k_cache, const float* v_ca
                          const float* v_new, int pos, int H, int HKV, int D, int rot_dim, int neox, float freq_base,
                          int kv_f16, float* out, float* k_stored, float* v_stored) {
     if (!q || !k_new || !v_new || !out || pos < 0 || (pos > 0 && (!k_cache || !v_cache)) || H % HKV ||
-        (D != 64 && D != 128) || rot_dim <= 0 || rot_dim > D || rot_dim % 2)
+        (D != 64 && D != 96 && D != 128) || rot_dim <= 0 || rot_dim > D || rot_dim % 2)
         return -1;
     TRY(check_device());
     const int n_keys = pos + 1;

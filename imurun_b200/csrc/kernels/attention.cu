@@ -209,6 +209,10 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
                         const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
                         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
                         vf[u][0] = a.x; vf[u][1] = a.y; vf[u][2] = b.x; vf[u][3] = b.y;
+                    } else if (dper == 3) {
+                        const __half* hv = reinterpret_cast<const __half*>(kv.v) + off;
+#pragma unroll
+                        for (int e = 0; e < 3; ++e) vf[u][e] = __half2float(hv[e]);
                     } else {
                         const float2 a = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.v) + off));
                         vf[u][0] = a.x; vf[u][1] = a.y;
@@ -217,6 +221,10 @@ __global__ void __launch_bounds__(32 * NW) k_attn_split(const float* __restrict_
                     if (dper == 4) {
                         const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.v) + off);
                         vf[u][0] = a.x; vf[u][1] = a.y; vf[u][2] = a.z; vf[u][3] = a.w;
+                    } else if (dper == 3) {
+                        const float* fv = reinterpret_cast<const float*>(kv.v) + off;
+#pragma unroll
+                        for (int e = 0; e < 3; ++e) vf[u][e] = fv[e];
                     } else {
                         const float2 a = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.v) + off);
                         vf[u][0] = a.x; vf[u][1] = a.y;
@@ -396,6 +404,18 @@ __device__ __forceinline__ void ld_vals(const float* p, float (&f)[16]) {
         f[4 * c] = a.x; f[4 * c + 1] = a.y; f[4 * c + 2] = a.z; f[4 * c + 3] = a.w;
     }
 }
+
+// 12 dims per lane (D = 96): halves at an 8-byte boundary, floats at 16
+__device__ __forceinline__ void ld_vals12(const __half* p, float (&f)[16]) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(p + 4 * c);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        f[4 * c] = a.x; f[4 * c + 1] = a.y; f[4 * c + 2] = b.x; f[4 * c + 3] = b.y;
+    }
+}
+__device__ __forceinline__ void ld_vals12(const float* p, float (&f)[16]) { ld_vals<12>(p, f); }
 
 template <class E>
 struct DecSmem {
@@ -582,6 +602,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
             if (valid) {
                 float kf[16];
                 if (dpp == 16) ld_vals<16>(K + (size_t)key * D + 16 * part, kf);
+                else if (dpp == 12) ld_vals12(K + (size_t)key * D + 12 * part, kf);
                 else ld_vals<8>(K + (size_t)key * D + 8 * part, kf);
 #pragma unroll
                 for (int g = 0; g < kMaxG; ++g) {
@@ -637,8 +658,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(
         __syncthreads();
         if (tr && tid == 0 && i == 0) trace_ev(TR_ATTN, 9, s_tseq);   // softmax done
         // p.V: thread = one dim of one head (heads tid / D, tid / D + 128 / D, ...)
-        for (int g = tid / D; g < G; g += kDecThreads / D) {
-            const int d = tid % D;
+        for (int idx = tid; idx < G * D; idx += kDecThreads) {
+            const int g = idx / D, d = idx % D;
             float o = so[g * kMaxD + d] * sc[g];
             const float* pg = ss + g * kDecKeys;
             for (int j = 0; j < kb; ++j) o = fmaf(pg[j], get(V + (size_t)j * D + d), o);
@@ -1663,7 +1684,7 @@ extern "C" int fbk_attention(const float* q, int ldq, int T, int H, int HKV, int
                              float* out, int ldo, float* scratch, size_t scratch_floats, int max_ctx, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
-    if (G > kMaxG || (D != 64 && D != 128)) return (int)cudaErrorInvalidValue;
+    if (G > kMaxG || (D != 64 && D != 96 && D != 128)) return (int)cudaErrorInvalidValue;
     const int nw = attn_warps(max_ctx);
     const int n_splits = (max_ctx + 32 * nw - 1) / (32 * nw);
     if (fbk_attention_call_floats(T, H, D, max_ctx) > scratch_floats) return (int)cudaErrorInvalidValue;
@@ -1843,9 +1864,10 @@ extern "C" int fbk_attention_prefill(const float* q, int ldq, int T, int H, int 
                                      int layer, float* out, int ldo, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
-    if (!kv.f16 || G > kMaxG || G * HKV != H || (D != 64 && D != 128) || kv.page_size != 16)
+    if (!kv.f16 || G > kMaxG || G * HKV != H || (D != 64 && D != 96 && D != 128) || kv.page_size != 16)
         return (int)cudaErrorInvalidValue;
     if (D == 128) return launch_prefill_tc<128>(q, ldq, T, H, HKV, scale, kv, layer, out, ldo, st);
+    if (D == 96) return launch_prefill_tc<96>(q, ldq, T, H, HKV, scale, kv, layer, out, ldo, st);
     return launch_prefill_tc<64>(q, ldq, T, H, HKV, scale, kv, layer, out, ldo, st);
 }
 // Floats of the warp-state scratch of the shared-prefix kernel for T tokens.
@@ -1859,7 +1881,7 @@ extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, con
                                     const int* pre, float* pstate, size_t pstate_floats, cudaStream_t st) {
     if (T <= 0) return 0;
     const int G = H / HKV;
-    if (G > kMaxG || (D != 64 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
+    if (G > kMaxG || (D != 64 && D != 96 && D != 128) || kv.page_size != 16) return (int)cudaErrorInvalidValue;
     static const bool tc_off = getenv("FISH_ATTN_SIMT") != nullptr;
     static const bool batch_cluster = getenv("FISH_ATTN_CLUSTER_BATCH") != nullptr;
     if (kv.f16 && !tc_off) {
@@ -1873,6 +1895,9 @@ extern "C" int fbk_attention_decode(const float* q, int ldq, const float* k, con
         if (D == 128)
             return launch_decode_tc<128>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo,
                                          pp, pf ? pre : nullptr, pf ? pstate : nullptr, st);
+        if (D == 96)
+            return launch_decode_tc<96>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo,
+                                        pp, pf ? pre : nullptr, pf ? pstate : nullptr, st);
         return launch_decode_tc<64>(q, ldq, k, v, ldkv, T, H, HKV, scale, rot, neox, rcos, rsin, kv, layer, out, ldo, pp,
                                     pf ? pre : nullptr, pf ? pstate : nullptr, st);
     }

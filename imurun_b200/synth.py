@@ -79,6 +79,9 @@ PRESETS = {
     # factors (the long set past a 512-position original context)
     "phi3": SynthConfig(arch="phi3", n_layers=4, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=8,
                         vocab=32000, freq_base=10000.0, wtype=12, rope_orig_ctx=512, rope_attn_factor=1.19),
+    # Phi-3-mini's head dimension (96) on the phi3 layout
+    "phi3-d96": SynthConfig(arch="phi3", n_layers=4, n_embd=768, n_ff=2048, n_head=8, n_head_kv=8,
+                            vocab=32000, freq_base=10000.0, wtype=12, rope_orig_ctx=512, rope_attn_factor=1.19),
     "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
                            vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
                            wtype=12, n_ctx_train=32768),

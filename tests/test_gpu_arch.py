@@ -9,7 +9,8 @@ itself (oracle/_ref, compiled from the reference's sources), which runs both:
   64-position window are small enough to change every output;
 * phi3 (src/model.cpp:253, 310-316, 522-530): fused q|k|v and gate|up
   tensors, longrope factors (the long set: the 1024-position context exceeds
-  the file's 512-position original context) and the rotation scale.
+  the file's 512-position original context) and the rotation scale; also at
+  Phi-3-mini's head dimension 96 ("phi3-d96").
 
 Teacher-forced like tests/test_gpu_model.py: a 192-id prompt (past the
 window), then 8 single-token steps, with the f32 cache on the SIMT kernels and
@@ -46,7 +47,7 @@ def gpu():
 
 
 @pytest.mark.parametrize("kv_f32", [0, 1])
-@pytest.mark.parametrize("preset", ["gemma2", "phi3"])
+@pytest.mark.parametrize("preset", ["gemma2", "phi3", "phi3-d96"])
 def test_arch_variant_vs_reference(gpu, reference, synth_dir, monkeypatch, preset, kv_f32):
     from imurun_b200 import synth
     from imurun_b200.native import Model
@@ -62,13 +63,15 @@ def test_arch_variant_vs_reference(gpu, reference, synth_dir, monkeypatch, prese
     assert compare_steps(g, r, f"{preset} kv_f32={kv_f32}", rel_max=rel_max) >= frac
 
 
-def test_gemma2_batch_equals_single_decodes(gpu, synth_dir):
+@pytest.mark.parametrize("preset", ["gemma2", "phi3-d96"])
+def test_batch_equals_single_decodes(gpu, synth_dir, preset):
     """Batched decode (rank CTAs + merge) equals single-token decode (one
-    cluster per kv head) bit for bit with the soft cap and the window on,
-    at contexts on both sides of the 64-position window."""
+    cluster per kv head) bit for bit: gemma2 with the soft cap and the window
+    on, at contexts on both sides of the 64-position window; phi3 with head
+    dimension 96."""
     from imurun_b200 import synth
     from imurun_b200.native import Model
-    path = synth.cached(synth.preset("gemma2"), synth_dir)
+    path = synth.cached(synth.preset(preset), synth_dir)
     rng = np.random.default_rng(5)
     prompts = [rng.integers(3, 32000, n).astype(np.int32) for n in (20, 63, 64, 65, 150, 300)]
     nxt = rng.integers(3, 32000, len(prompts)).astype(np.int32)

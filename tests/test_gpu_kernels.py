@@ -232,7 +232,8 @@ def test_rope_bit_exact(lib, oracle, neox):
 
 @pytest.mark.parametrize("f16", [0, 1])
 @pytest.mark.parametrize("T,pos0,H,HKV,D", [(1, 0, 8, 4, 64), (1, 300, 32, 8, 128), (7, 120, 28, 4, 128),
-                                            (33, 0, 8, 8, 64), (1, 1000, 64, 8, 128)])
+                                            (33, 0, 8, 8, 64), (1, 1000, 64, 8, 128), (9, 70, 12, 4, 96),
+                                            (1, 2500, 32, 32, 96)])
 def test_attention_vs_oracle(lib, oracle, f16, T, pos0, H, HKV, D):
     rng = np.random.default_rng(T + pos0 + H)
     n_keys = pos0 + T
@@ -250,7 +251,7 @@ def test_attention_vs_oracle(lib, oracle, f16, T, pos0, H, HKV, D):
 
 @pytest.mark.parametrize("T,pos0,H,HKV,D", [(5, 0, 8, 4, 64), (16, 40, 32, 8, 128), (37, 120, 28, 4, 128),
                                             (70, 1000, 64, 8, 128), (256, 256, 32, 8, 128), (33, 7, 8, 8, 64),
-                                            (19, 63, 16, 2, 128)])
+                                            (19, 63, 16, 2, 128), (21, 100, 32, 32, 96), (40, 0, 12, 4, 96)])
 def test_attention_prefill_tc_vs_oracle(lib, oracle, T, pos0, H, HKV, D):
     """The tensor-core prefill kernel (16 tokens x kv head per CTA, 64-key
     tiles, q and p as f16 hi + lo parts) against the oracle's attention on the
@@ -278,7 +279,9 @@ def test_attention_prefill_tc_vs_oracle(lib, oracle, T, pos0, H, HKV, D):
 @pytest.mark.parametrize("f16", [0, 1])
 @pytest.mark.parametrize("pos,H,HKV,D,rot,neox", [(0, 8, 4, 64, 64, 0), (37, 32, 8, 128, 128, 0),
                                                   (200, 28, 4, 128, 128, 1), (1000, 64, 8, 128, 128, 0),
-                                                  (3000, 8, 8, 64, 32, 1), (70, 16, 2, 128, 64, 0)])
+                                                  (3000, 8, 8, 64, 32, 1), (70, 16, 2, 128, 64, 0),
+                                                  (300, 32, 32, 96, 96, 1), (65, 12, 4, 96, 96, 0),
+                                                  (1000, 8, 8, 96, 64, 1)])
 def test_fused_decode_attention(lib, oracle, f16, pos, H, HKV, D, rot, neox):
     """RoPE + KV append + attention in one kernel vs the unfused pieces:
     RoPE on the GPU (bit-exact with the oracle, test_rope_bit_exact) then the
