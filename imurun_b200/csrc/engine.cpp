@@ -427,6 +427,21 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
                 !bind(p + "ffn_up_exps.weight", L.up_exps, true) || !bind(p + "ffn_down_exps.weight", L.down_exps, true))
                 return false;
             c.n_ff_exp = L.gate_exps.n_out;
+            // the shared expert every token also takes (qwen2moe, src/model.cpp:303-308, 1582-1599)
+            if (!bind(p + "ffn_gate_shexp.weight", L.shexp_gate, false) || !bind(p + "ffn_up_shexp.weight", L.shexp_up, false) ||
+                !bind(p + "ffn_down_shexp.weight", L.shexp_down, false) ||
+                !bind(p + "ffn_gate_inp_shexp.weight", L.shexp_gate_inp, false))
+                return false;
+            if (L.shexp_gate.type >= 0 && L.shexp_up.type >= 0 && L.shexp_down.type >= 0) {
+                if (L.shexp_up.n_out != L.shexp_gate.n_out || L.shexp_down.n_in != L.shexp_gate.n_out ||
+                    (L.shexp_gate_inp.type >= 0 && (L.shexp_gate_inp.n_out != 1 || L.shexp_gate_inp.n_in != c.n_embd))) {
+                    if (err) *err = "shared expert tensors of layer " + std::to_string(i) + " have inconsistent shapes";
+                    return false;
+                }
+                c.n_ff_shexp = std::max(c.n_ff_shexp, L.shexp_gate.n_out);
+            } else {
+                L.shexp_gate = L.shexp_up = L.shexp_down = L.shexp_gate_inp = DevW{};
+            }
             if (tp_world_ > 1) {   // this rank's experts
                 for (DevW* w : {&L.gate_exps, &L.up_exps, &L.down_exps}) {
                     if (w->n_exp != c.n_experts) { if (err) *err = "expert tensor count differs from expert_count"; return false; }
@@ -459,13 +474,14 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
     }
     // activation layouts each consumer needs
     for (const DevLayer& L : layers_) {
-        for (const DevW* w : {&L.wq, &L.wk, &L.wv, &L.wg, &L.wu, &L.gate_exps, &L.up_exps}) {
+        for (const DevW* w : {&L.wq, &L.wk, &L.wv, &L.wg, &L.wu, &L.gate_exps, &L.up_exps, &L.shexp_gate, &L.shexp_up,
+                              &L.shexp_gate_inp}) {
             if (w->type == T_Q8_0) want32_e_ = true;
             if (w->type == T_Q4_K || w->type == T_Q6_K) wantk_e_ = true;
         }
         if (L.wo.type == T_Q8_0) want32_q_ = true;
         if (L.wo.type == T_Q4_K || L.wo.type == T_Q6_K) wantk_q_ = true;
-        for (const DevW* w : {&L.wd, &L.down_exps}) {
+        for (const DevW* w : {&L.wd, &L.down_exps, &L.shexp_down}) {
             if (w->type == T_Q8_0) want32_f_ = true;
             if (w->type == T_Q4_K || w->type == T_Q6_K) wantk_f_ = true;
         }
@@ -567,6 +583,7 @@ bool Engine::upload_weights(std::string* err) {
         add(p + "ffn_gate.weight", &L.wg); add(p + "ffn_up.weight", &L.wu); add(p + "ffn_down.weight", &L.wd);
         add(p + "ffn_gate_inp.weight", &L.gate_inp); add(p + "ffn_gate_exps.weight", &L.gate_exps);
         add(p + "ffn_up_exps.weight", &L.up_exps); add(p + "ffn_down_exps.weight", &L.down_exps);
+        add("", &L.shexp_gate); add("", &L.shexp_up); add("", &L.shexp_down); add("", &L.shexp_gate_inp);
     }
     weights_dev_bytes_ = total;
     CK(cudaMalloc(&warena_, total + 256));
@@ -642,7 +659,7 @@ bool Engine::alloc_buffers(std::string* err) {
     const Config& c = cfg_;
     const int E = c.n_embd, Q = c.q_dim(), KV = c.kv_dim();
     const int K = std::max(1, c.n_experts_per_tok);
-    const int F = std::max(c.n_ff, c.n_ff_exp);
+    const int F = std::max(std::max(c.n_ff, c.n_ff_exp), c.n_ff_shexp);
     max_k_ = std::max(std::max(E, Q), F);
     const int R = kMaxBatch * K;   // rows of the expert-expanded activations
     const size_t ld = align_up((size_t)max_k_, 16);
@@ -1465,6 +1482,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
                 }
                 if (!moe_grouped(L, a, T, esel, ep ? ep_n_ : NE, out, err)) return false;
                 if (ep && !tp_reduce_add(T, err)) return false;
+                if (L.shexp_gate.ok() && !shared_expert(L, a, T, err)) return false;
                 continue;
             }
             for (int t = 0; t < T; ++t) {
@@ -1494,6 +1512,7 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
             } else {
                 CKP(PC_OTHER, 0, fbk_moe_combine(x_, E, eo_, wsel_, T, K, E, stream_));
             }
+            if (L.shexp_gate.ok() && !shared_expert(L, a, T, err)) return false;
         } else {
             const int F = c.n_ff;
             {
@@ -1548,6 +1567,39 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
             if (post) CKP(PC_NORMQ, 0, fbk_rmsnorm_add(x_, E, tp_tmp_, E, L.post_ffn_norm, c.eps, T, E, stream_));
         }
     }
+    return true;
+}
+
+// The shared expert of a qwen2moe layer (src/model.cpp:1582-1599): every
+// token's normed input (xb_, quantised again: the routed experts reused the
+// activation planes) through gate/up, SwiGLU and down, scaled by the
+// sigmoid of its own one-row gate when the layer has one, added to x. Every
+// rank of an expert-parallel group holds it whole and adds it after the
+// all-reduce of the routed experts.
+bool Engine::shared_expert(const DevLayer& L, ActQ a, int T, std::string* err) {
+    const Config& c = cfg_;
+    const int E = c.n_embd, Fs = L.shexp_gate.n_out;
+    a.K = E;
+    CKP(PC_NORMQ, 0, fbk_quantize_rows(xb_, E, T, E, &a, want32_e_, wantk_e_, stream_));
+    const DevW* gu[2] = {&L.shexp_gate, &L.shexp_up};
+    float* ys[2] = {g_, u_};
+    const int lds[2] = {Fs, Fs};
+    if (!gemv_group(gu, ys, lds, nullptr, 2, a, T, EPI_STORE, err)) return false;
+    // the gate before the planes are reused: one logit per token into router_
+    const bool gated = L.shexp_gate_inp.ok();
+    if (gated) {
+        if (L.shexp_gate_inp.type == T_F32) {
+            CKP(PC_OTHER, 0, fbk_router_f32(L.shexp_gate_inp.d, L.shexp_gate_inp.stride, xb_, E, T, E, 1, router_, 1,
+                                            stream_));
+        } else if (!gemv(L.shexp_gate_inp, a, T, router_, 1, nullptr, EPI_STORE, xb_, E, nullptr, err)) {
+            return false;
+        }
+    }
+    CKP(PC_OTHER, 0, fbk_sigmoid(gated ? router_ : nullptr, router_, T, stream_));
+    a.K = Fs;
+    CKP(PC_NORMQ, 0, fbk_silu_mul_quant(g_, Fs, u_, Fs, T, Fs, nullptr, Fs, &a, want32_f_, wantk_f_, stream_));
+    if (!gemv(L.shexp_down, a, T, eo_, E, nullptr, EPI_STORE, nullptr, 0, nullptr, err)) return false;
+    CKP(PC_OTHER, 0, fbk_moe_combine(x_, E, eo_, router_, T, 1, E, stream_));
     return true;
 }
 

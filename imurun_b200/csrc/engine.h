@@ -41,6 +41,7 @@ struct Config {
     float embd_scale = 1.0f, attn_softcap = 0.0f, final_softcap = 0.0f;
     int sliding_window = 0;
     int n_experts = 0, n_experts_per_tok = 0, n_ff_exp = 0;
+    int n_ff_shexp = 0;   // qwen2moe: rows of the shared expert (0: none)
     // tensor parallelism: the head counts and n_ff above are this rank's
     // shares; the model's own values are kept here (equal without it)
     int n_head_model = 0, n_head_kv_model = 0, n_ff_model = 0;
@@ -91,6 +92,7 @@ struct DevW {
 
 struct DevLayer {
     DevW wq, wk, wv, wo, wg, wu, wd, gate_inp, gate_exps, up_exps, down_exps;
+    DevW shexp_gate, shexp_up, shexp_down, shexp_gate_inp;   // qwen2moe shared expert (optional)
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
     float *post_attn_norm = nullptr, *post_ffn_norm = nullptr;   // gemma2
@@ -265,6 +267,8 @@ private:
     // MoE FFN of a batched step (T > 1) with the tokens grouped per expert:
     // each expert's weights stream once over all rows routed to it
     bool moe_grouped(const DevLayer& L, const ActQ& a, int T, const int32_t* esel, int nel, float* out, std::string* err);
+    // qwen2moe: x += gate * down(silu(gate(xb)) * up(xb)) for the T normed rows in xb_
+    bool shared_expert(const DevLayer& L, ActQ a, int T, std::string* err);
     // true when a T-token GEMV over these matrices can build its own int8
     // activations (streamed kernel with a prologue)
     bool fusable(const DevW* const* ws, int n, int T) const;

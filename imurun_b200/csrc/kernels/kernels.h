@@ -97,6 +97,8 @@ int fbk_rmsnorm_add(float* x, int ldx, const float* y, int ldy, const float* w, 
                     cudaStream_t st);
 // x[i] *= s for n floats
 int fbk_scale(float* x, size_t n, float s, cudaStream_t st);
+// y[i] = sigmoid(x[i]) for n values (x null: y = 1)
+int fbk_sigmoid(const float* x, float* y, int n, cudaStream_t st);
 // rows of n logits (stride ldx): cap * tanh(x / cap)
 int fbk_softcap(float* x, int n, int rows, int ldx, float cap, cudaStream_t st);
 int fbk_gemv(const fb::GemvArgs* args, cudaStream_t st);

@@ -223,6 +223,15 @@ __global__ void k_scale(float* __restrict__ x, size_t n, float s) {
         x[i] = __fmul_rn(x[i], s);
 }
 
+// y = 1 / (1 + exp(-x)), or 1 where x is null (the shared expert's gate,
+// src/model.cpp:1588-1592)
+__global__ void k_sigmoid(const float* __restrict__ x, float* __restrict__ y, int n) {
+    pdl_trigger();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        y[i] = x ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x[i]))) : 1.0f;
+}
+
 // cap * tanh(x / cap) (gemma2's final logit soft cap, src/model.cpp:1802-1805)
 __global__ void k_softcap(float* __restrict__ x, int n, int ldx, float cap) {
     pdl_trigger();
@@ -282,6 +291,11 @@ extern "C" int fbk_scale(float* x, size_t n, float s, cudaStream_t st) {
     if (n == 0) return 0;
     const int ctas = (int)std::min<size_t>(1184, (n + 255) / 256);
     return (int)fbk_launch(k_scale, dim3(ctas), dim3(256), 0, st, x, n, s);
+}
+
+extern "C" int fbk_sigmoid(const float* x, float* y, int n, cudaStream_t st) {
+    if (n <= 0) return 0;
+    return (int)fbk_launch(k_sigmoid, dim3((n + 255) / 256), dim3(256), 0, st, x, y, n);
 }
 
 extern "C" int fbk_softcap(float* x, int n, int rows, int ldx, float cap, cudaStream_t st) {

@@ -345,6 +345,9 @@ typedef struct fish_synth_config {
     // and rope.scaling.attn_factor (0: 1)
     int rope_orig_ctx;
     float rope_attn_factor;
+    // MoE: rows of a shared expert every token takes (0: none), with a
+    // one-row F32 sigmoid gate (qwen2moe)
+    int n_ff_shexp;
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -411,6 +414,14 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
             add(p + "ffn_gate_exps.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F), NE}, tm, 0, wstd);
             add(p + "ffn_up_exps.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F), NE}, tm, 0, wstd);
             add(p + "ffn_down_exps.weight", {static_cast<uint64_t>(F), static_cast<uint64_t>(E), NE}, tv, 0, wstd);
+            if (c->n_ff_shexp > 0) {
+                const uint64_t FS = static_cast<uint64_t>(c->n_ff_shexp);
+                add(p + "ffn_gate_inp_shexp.weight", {static_cast<uint64_t>(E)}, T_F32, 0,
+                    c->router_std > 0 ? c->router_std : 0.015625f);
+                add(p + "ffn_gate_shexp.weight", {static_cast<uint64_t>(E), FS}, tm, 0, wstd);
+                add(p + "ffn_up_shexp.weight", {static_cast<uint64_t>(E), FS}, tm, 0, wstd);
+                add(p + "ffn_down_shexp.weight", {FS, static_cast<uint64_t>(E)}, tv, 0, wstd);
+            }
         } else {
             add(p + "ffn_gate.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F)}, tm, 0, wstd);
             add(p + "ffn_up.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(F)}, tm, 0, wstd);
@@ -467,6 +478,10 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     if (c->n_experts > 0) {
         w.kv_u32(k("expert_count"), static_cast<uint32_t>(c->n_experts)); ++n_kv;
         w.kv_u32(k("expert_used_count"), static_cast<uint32_t>(c->n_experts_per_tok)); ++n_kv;
+        w.kv_u32(k("expert_feed_forward_length"), static_cast<uint32_t>(F)); ++n_kv;
+        if (c->n_ff_shexp > 0) {
+            w.kv_u32(k("expert_shared_feed_forward_length"), static_cast<uint32_t>(c->n_ff_shexp)); ++n_kv;
+        }
     }
     if (c->bpe_pre && c->bpe_pre[0]) {
         // byte-level BPE vocabulary (see build_bpe_vocab)

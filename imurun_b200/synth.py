@@ -58,6 +58,7 @@ class SynthConfig:
     sliding_window: int = 0     # gemma2: window of the even layers (0: 4096)
     rope_orig_ctx: int = 0      # phi3 longrope: original context (0: n_ctx_train)
     rope_attn_factor: float = 0.0   # phi3 longrope: rotation scale (0: 1)
+    n_ff_shexp: int = 0         # MoE shared expert rows with a sigmoid gate (qwen2moe; 0: none)
 
 
 PRESETS = {
@@ -82,6 +83,11 @@ PRESETS = {
     # Phi-3-mini's head dimension (96) on the phi3 layout
     "phi3-d96": SynthConfig(arch="phi3", n_layers=4, n_embd=768, n_ff=2048, n_head=8, n_head_kv=8,
                             vocab=32000, freq_base=10000.0, wtype=12, rope_orig_ctx=512, rope_attn_factor=1.19),
+    # Qwen2-MoE-shaped (not a benchmark config): 8 experts, top-4, and a
+    # gated shared expert; qkv biases, NeoX rotation, unnormalised top-k weights
+    "qwen2moe": SynthConfig(arch="qwen2moe", n_layers=2, n_embd=1024, n_ff=768, n_head=8, n_head_kv=8,
+                            vocab=32000, freq_base=1000000.0, eps=1e-6, qkv_bias=1, n_experts=8,
+                            n_experts_per_tok=4, n_ff_shexp=2048, wtype=12, n_ctx_train=32768),
     "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
                            vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
                            wtype=12, n_ctx_train=32768),
@@ -106,6 +112,7 @@ class _CConfig(ctypes.Structure):
         ("attn_softcap", ctypes.c_float), ("final_softcap", ctypes.c_float),
         ("sliding_window", ctypes.c_int),
         ("rope_orig_ctx", ctypes.c_int), ("rope_attn_factor", ctypes.c_float),
+        ("n_ff_shexp", ctypes.c_int),
     ]
 
 
@@ -128,7 +135,7 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
                  cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm, cfg.attn_softcap,
-                 cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor)
+                 cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor, cfg.n_ff_shexp)
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:
@@ -149,7 +156,8 @@ def size_estimate(cfg: SynthConfig) -> int:
     rv = r4 if q8 else (r4 + r6) / 2
     ne = max(1, cfg.n_experts)
     per_layer = (E * (H * D + HKV * D) * r4 + E * HKV * D * rv + H * D * E * r4
-                 + ne * (2 * E * F * r4 + F * E * rv) + 4 * E * max(0, cfg.n_experts) + 8 * E)
+                 + ne * (2 * E * F * r4 + F * E * rv) + 4 * E * max(0, cfg.n_experts) + 8 * E
+                 + 2 * E * cfg.n_ff_shexp * r4 + cfg.n_ff_shexp * E * rv)
     total = cfg.vocab * E * r4 + cfg.vocab * E * (r4 if q8 else r6) + cfg.n_layers * per_layer
     return int(total * 1.03) + (64 << 20)
 

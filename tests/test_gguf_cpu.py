@@ -21,7 +21,8 @@ SUFFIXES = ["block_count", "context_length", "embedding_length", "feed_forward_l
             "attention.head_count", "attention.head_count_kv", "attention.layer_norm_rms_epsilon",
             "rope.freq_base", "rope.dimension_count", "expert_count", "expert_used_count", "vocab_size",
             "attn_logit_softcapping", "final_logit_softcapping", "attention.sliding_window",
-            "rope.scaling.type", "rope.scaling.original_context_length", "rope.scaling.attn_factor"]
+            "rope.scaling.type", "rope.scaling.original_context_length", "rope.scaling.attn_factor",
+            "expert_feed_forward_length", "expert_shared_feed_forward_length"]
 GENERAL = ["general.architecture", "general.name", "general.alignment", "tokenizer.ggml.model",
            "tokenizer.ggml.tokens", "tokenizer.ggml.scores", "tokenizer.ggml.token_type",
            "tokenizer.ggml.bos_token_id", "tokenizer.ggml.eos_token_id", "tokenizer.ggml.add_bos_token",
@@ -56,7 +57,7 @@ def _digest(fn, path, keys):
     return buf.raw[:n].decode()
 
 
-@pytest.mark.parametrize("name", ["tiny", "qwen7b", "mixtral", "gemma2", "phi3"])
+@pytest.mark.parametrize("name", ["tiny", "qwen7b", "mixtral", "gemma2", "phi3", "qwen2moe"])
 def test_gguf_digest_matches_reference(ref_lib, ours, synth_dir, name):
     from imurun_b200 import synth
     cfg = {"tiny": lambda: synth.preset("tiny"),
@@ -64,7 +65,8 @@ def test_gguf_digest_matches_reference(ref_lib, ours, synth_dir, name):
            "mixtral": lambda: synth.preset("mixtral", layers=1, n_embd=512, n_ff=1024, n_head=8,
                                                  n_head_kv=2),
            "gemma2": lambda: synth.preset("gemma2", layers=1),
-           "phi3": lambda: synth.preset("phi3", layers=1)}[name]()
+           "phi3": lambda: synth.preset("phi3", layers=1),
+           "qwen2moe": lambda: synth.preset("qwen2moe", layers=1)}[name]()
     path = synth.cached(cfg, synth_dir)
     arch_line = _digest(ours.fbx_gguf_digest, path, ["general.architecture"]).splitlines()[-1]
     arch = arch_line.split(" ", 3)[3]

@@ -10,7 +10,9 @@ itself (oracle/_ref, compiled from the reference's sources), which runs both:
 * phi3 (src/model.cpp:253, 310-316, 522-530): fused q|k|v and gate|up
   tensors, longrope factors (the long set: the 1024-position context exceeds
   the file's 512-position original context) and the rotation scale; also at
-  Phi-3-mini's head dimension 96 ("phi3-d96").
+  Phi-3-mini's head dimension 96 ("phi3-d96");
+* qwen2moe (src/model.cpp:303-308, 1582-1599): routed experts plus a shared
+  expert every token takes, scaled by the sigmoid of its own one-row gate.
 
 Teacher-forced like tests/test_gpu_model.py: a 192-id prompt (past the
 window), then 8 single-token steps, with the f32 cache on the SIMT kernels and
@@ -47,7 +49,7 @@ def gpu():
 
 
 @pytest.mark.parametrize("kv_f32", [0, 1])
-@pytest.mark.parametrize("preset", ["gemma2", "phi3", "phi3-d96"])
+@pytest.mark.parametrize("preset", ["gemma2", "phi3", "phi3-d96", "qwen2moe"])
 def test_arch_variant_vs_reference(gpu, reference, synth_dir, monkeypatch, preset, kv_f32):
     from imurun_b200 import synth
     from imurun_b200.native import Model
@@ -63,12 +65,13 @@ def test_arch_variant_vs_reference(gpu, reference, synth_dir, monkeypatch, prese
     assert compare_steps(g, r, f"{preset} kv_f32={kv_f32}", rel_max=rel_max) >= frac
 
 
-@pytest.mark.parametrize("preset", ["gemma2", "phi3-d96"])
+@pytest.mark.parametrize("preset", ["gemma2", "phi3-d96", "qwen2moe"])
 def test_batch_equals_single_decodes(gpu, synth_dir, preset):
     """Batched decode (rank CTAs + merge) equals single-token decode (one
     cluster per kv head) bit for bit: gemma2 with the soft cap and the window
     on, at contexts on both sides of the 64-position window; phi3 with head
-    dimension 96."""
+    dimension 96; qwen2moe with its routed experts grouped per expert and the
+    shared expert over the whole batch."""
     from imurun_b200 import synth
     from imurun_b200.native import Model
     path = synth.cached(synth.preset(preset), synth_dir)
