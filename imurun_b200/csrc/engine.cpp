@@ -531,10 +531,19 @@ bool Engine::load(const std::string& path, int n_ctx, std::string* err) {
             !dev_vec(p + "attn_q.bias", &L.bq, false, tp_rank_ * c.q_dim(), sq) ||
             !dev_vec(p + "attn_k.bias", &L.bk, false, tp_rank_ * c.kv_dim(), skv) ||
             !dev_vec(p + "attn_v.bias", &L.bv, false, tp_rank_ * c.kv_dim(), skv) ||
+            !dev_vec(p + "attn_output.bias", &L.bo, false) ||
             !dev_vec(p + "attn_q_norm.weight", &L.q_norm, false) ||
             !dev_vec(p + "attn_k_norm.weight", &L.k_norm, false))
             return false;
         if (L.q_norm && L.k_norm) c.qk_norm = true;
+        if (g.find(p + "attn_qkv.bias")) {   // fused q|k|v bias (src/model.cpp:348): this rank's slices
+            const int Qm = c.n_head_model * c.head_dim, KVm = c.n_head_kv_model * c.head_dim;
+            const int Q = c.q_dim(), KV = c.kv_dim();
+            if (!dev_vec(p + "attn_qkv.bias", &L.bq, true, tp_rank_ * Q, Q) ||
+                !dev_vec(p + "attn_qkv.bias", &L.bk, true, Qm + tp_rank_ * KV, KV) ||
+                !dev_vec(p + "attn_qkv.bias", &L.bv, true, Qm + KVm + tp_rank_ * KV, KV))
+                return false;
+        }
     }
     {
         const Tensor* t = g.find("output_norm.weight");
@@ -1118,6 +1127,8 @@ bool Engine::step_ready() {
     if (c.n_experts > 0) { step_why_ = "mixture of experts"; return false; }
     if (tp_world_ > 1) { step_why_ = "tensor parallel"; return false; }
     if (c.qk_norm) { step_why_ = "q/k norm"; return false; }
+    for (const DevLayer& L : layers_)
+        if (L.bo) { step_why_ = "attention output bias"; return false; }
     if (c.post_norms || c.gelu || c.attn_softcap > 0.0f || c.final_softcap > 0.0f || c.sliding_window > 0 ||
         c.embd_scale != 1.0f) {
         step_why_ = "gemma2 layer form";
@@ -1438,18 +1449,19 @@ bool Engine::run_layers(int T, int max_ctx, bool distinct, std::string* err, int
             const bool tp = tp_world_ > 1, post = L.post_attn_norm != nullptr;
             float* oy = tp || post ? tp_tmp_ : x_;
             const int oepi = tp || post ? EPI_STORE : EPI_ADD;
+            const float* bo = tp_rank_ == 0 ? L.bo : nullptr;   // partial sums of other ranks carry none
             const DevW* wo[1] = {&L.wo};
             if (probe_ && !probe_float(1, attn_, T, Q, err)) return false;
             if (fusable(wo, 1, T)) {
                 const GemvPro pro{PRO_QUANT, attn_, Q, nullptr, 0, nullptr, 0.0f};
                 if (probe_) dump_img_ = probe_img_;
-                const bool ok = gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err, &pro);
+                const bool ok = gemv(L.wo, a, T, oy, E, bo, oepi, nullptr, 0, nullptr, err, &pro);
                 dump_img_ = nullptr;
                 if (!ok || (probe_ && !probe_image(1, T, Q, err))) return false;
             } else {
                 CKP(PC_NORMQ, 0, fbk_quantize_rows(attn_, Q, T, Q, &a, want32_q_, wantk_q_, stream_));
                 if (probe_ && !probe_planes(1, a, T, Q, want32_q_, wantk_q_, err)) return false;
-                if (!gemv(L.wo, a, T, oy, E, nullptr, oepi, nullptr, 0, nullptr, err)) return false;
+                if (!gemv(L.wo, a, T, oy, E, bo, oepi, nullptr, 0, nullptr, err)) return false;
             }
             if (tp && !tp_reduce_add(T, err)) return false;
             if (post) CKP(PC_NORMQ, 0, fbk_rmsnorm_add(x_, E, tp_tmp_, E, L.post_attn_norm, c.eps, T, E, stream_));

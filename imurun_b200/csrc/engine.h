@@ -96,6 +96,7 @@ struct DevLayer {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
     float *post_attn_norm = nullptr, *post_ffn_norm = nullptr;   // gemma2
+    float* bo = nullptr;   // attn_output.bias (added once: by rank 0 under tensor parallelism)
 };
 
 // Debug record of one layer's int8 activations (Engine::layer_probe). Stage

@@ -348,6 +348,7 @@ typedef struct fish_synth_config {
     // MoE: rows of a shared expert every token takes (0: none), with a
     // one-row F32 sigmoid gate (qwen2moe)
     int n_ff_shexp;
+    int o_bias;                  // 1: attn_output.bias
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -385,7 +386,9 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
         add(p + "attn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
         if (phi3) {
             add(p + "attn_qkv.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>((H + 2 * HKV) * D)}, tm, 0, wstd);
+            if (c->qkv_bias) add(p + "attn_qkv.bias", {static_cast<uint64_t>((H + 2 * HKV) * D)}, T_F32, 0, wstd);
             add(p + "attn_output.weight", {static_cast<uint64_t>(H * D), static_cast<uint64_t>(E)}, tm, 0, wstd);
+            if (c->o_bias) add(p + "attn_output.bias", {static_cast<uint64_t>(E)}, T_F32, 0, wstd);
             add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, 1, 0);
             add(p + "ffn_up.weight", {static_cast<uint64_t>(E), static_cast<uint64_t>(2 * F)}, tm, 0, wstd);
             add(p + "ffn_down.weight", {static_cast<uint64_t>(F), static_cast<uint64_t>(E)}, tv, 0, wstd);
@@ -404,6 +407,7 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
             add(p + "attn_k_norm.weight", {static_cast<uint64_t>(D)}, T_F32, 2, 0.1f);
         }
         add(p + "attn_output.weight", {static_cast<uint64_t>(H * D), static_cast<uint64_t>(E)}, tm, 0, wstd);
+        if (c->o_bias) add(p + "attn_output.bias", {static_cast<uint64_t>(E)}, T_F32, 0, wstd);
         if (gemma2) add(p + "post_attention_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
         add(p + "ffn_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);
         if (gemma2) add(p + "post_ffw_norm.weight", {static_cast<uint64_t>(E)}, T_F32, nfill, nsd);

@@ -59,6 +59,7 @@ class SynthConfig:
     rope_orig_ctx: int = 0      # phi3 longrope: original context (0: n_ctx_train)
     rope_attn_factor: float = 0.0   # phi3 longrope: rotation scale (0: 1)
     n_ff_shexp: int = 0         # MoE shared expert rows with a sigmoid gate (qwen2moe; 0: none)
+    o_bias: int = 0             # 1: attn_output.bias
 
 
 PRESETS = {
@@ -88,6 +89,10 @@ PRESETS = {
     "qwen2moe": SynthConfig(arch="qwen2moe", n_layers=2, n_embd=1024, n_ff=768, n_head=8, n_head_kv=8,
                             vocab=32000, freq_base=1000000.0, eps=1e-6, qkv_bias=1, n_experts=8,
                             n_experts_per_tok=4, n_ff_shexp=2048, wtype=12, n_ctx_train=32768),
+    # phi3 layout with a fused q|k|v bias and an output-projection bias
+    "phi3-bias": SynthConfig(arch="phi3", n_layers=2, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=8,
+                             vocab=32000, freq_base=10000.0, wtype=12, qkv_bias=1, o_bias=1,
+                             rope_orig_ctx=512, rope_attn_factor=1.19),
     "mixtral": SynthConfig(n_layers=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8,
                            vocab=32000, freq_base=1000000.0, n_experts=8, n_experts_per_tok=2,
                            wtype=12, n_ctx_train=32768),
@@ -112,7 +117,7 @@ class _CConfig(ctypes.Structure):
         ("attn_softcap", ctypes.c_float), ("final_softcap", ctypes.c_float),
         ("sliding_window", ctypes.c_int),
         ("rope_orig_ctx", ctypes.c_int), ("rope_attn_factor", ctypes.c_float),
-        ("n_ff_shexp", ctypes.c_int),
+        ("n_ff_shexp", ctypes.c_int), ("o_bias", ctypes.c_int),
     ]
 
 
@@ -135,7 +140,8 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
                  cfg.vocab, cfg.n_ctx_train, cfg.eps, cfg.freq_base, cfg.n_experts,
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
                  cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm, cfg.attn_softcap,
-                 cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor, cfg.n_ff_shexp)
+                 cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor, cfg.n_ff_shexp,
+                 cfg.o_bias)
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

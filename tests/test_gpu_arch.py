@@ -10,7 +10,8 @@ itself (oracle/_ref, compiled from the reference's sources), which runs both:
 * phi3 (src/model.cpp:253, 310-316, 522-530): fused q|k|v and gate|up
   tensors, longrope factors (the long set: the 1024-position context exceeds
   the file's 512-position original context) and the rotation scale; also at
-  Phi-3-mini's head dimension 96 ("phi3-d96");
+  Phi-3-mini's head dimension 96 ("phi3-d96"), and with a fused q|k|v bias
+  and an output-projection bias ("phi3-bias", src/model.cpp:343-348);
 * qwen2moe (src/model.cpp:303-308, 1582-1599): routed experts plus a shared
   expert every token takes, scaled by the sigmoid of its own one-row gate.
 
@@ -49,7 +50,7 @@ def gpu():
 
 
 @pytest.mark.parametrize("kv_f32", [0, 1])
-@pytest.mark.parametrize("preset", ["gemma2", "phi3", "phi3-d96", "qwen2moe"])
+@pytest.mark.parametrize("preset", ["gemma2", "phi3", "phi3-d96", "phi3-bias", "qwen2moe"])
 def test_arch_variant_vs_reference(gpu, reference, synth_dir, monkeypatch, preset, kv_f32):
     from imurun_b200 import synth
     from imurun_b200.native import Model
