@@ -72,6 +72,10 @@ GGUFS = {
     "qwen7b": lambda synth: synth.preset("qwen7b", layers=1),
     "bpe-llama3": lambda synth: synth.preset("tiny", layers=1, bpe_pre="llama-bpe"),
     "bpe-qwen2": lambda synth: synth.preset("tiny", layers=1, bpe_pre="qwen2"),
+    # the GPT-2 family (digit runs of any length) and a pre-tokenizer name
+    # the reference does not list (its default split)
+    "bpe-gpt2": lambda synth: synth.preset("tiny", layers=1, bpe_pre="gpt-2"),
+    "bpe-unlisted": lambda synth: synth.preset("tiny", layers=1, bpe_pre="not-a-listed-pre"),
 }
 
 
