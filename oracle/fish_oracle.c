@@ -508,6 +508,15 @@ void or_silu_inplace(float* x, int n) {
     for (int i = 0; i < n; ++i) { const float v = x[i]; x[i] = v / (1.0f + expf(-v)); }
 }
 
+/* ops.cpp:32-38: the tanh form of GELU */
+void or_gelu_inplace(float* x, int n) {
+    const float k = 0.7978845608028654f;
+    for (int i = 0; i < n; ++i) {
+        const float v = x[i];
+        x[i] = 0.5f * v * (1.0f + tanhf(k * (v + 0.044715f * v * v * v)));
+    }
+}
+
 /* ops.cpp:40-55 */
 void or_softmax_inplace(float* x, int n) {
     if (n <= 0) return;
@@ -779,6 +788,12 @@ typedef struct {
     const or_tensor *wq, *wk, *wv, *wo, *wg, *wu, *wd;
     const or_tensor *gate_inp, *gate_exps, *up_exps, *down_exps;
     float *attn_norm, *ffn_norm, *bq, *bk, *bv, *q_norm, *k_norm;
+    /* row views of fused tensors (phi3 attn_qkv, gate|up ffn_up): rows of
+     * one output are independent, so a view's product is the fused one's */
+    or_tensor vq, vk, vv, vg, vu;
+    float *bo, *bqkv;                      /* attn_output.bias, attn_qkv.bias */
+    float *post_attn_norm, *post_ffn_norm; /* gemma2 */
+    const or_tensor *sh_gate, *sh_up, *sh_down, *sh_gate_inp;   /* qwen2moe shared expert */
 } or_layer;
 
 struct or_model {
@@ -792,6 +807,9 @@ struct or_model {
     float *k_cache, *v_cache;   /* [layer][n_ctx][kv_dim] */
     int kv_len;
     float* last_x;
+    /* gemma2 (model.cpp:488-496) and MoE options */
+    int gemma2, gelu, sliding_window, expert_weights_norm;
+    float embd_scale, attn_softcap, final_softcap;
 };
 
 static float* load_vec(const or_tensor* t) {
@@ -816,7 +834,8 @@ static double kv_f(const or_gguf* g, const char* arch, const char* k, double def
     return v ? v->f : def;
 }
 
-/* model.cpp:393-645 (llama / qwen2 / qwen3 / llama-MoE subset). */
+/* model.cpp:393-645 (llama / qwen2 / qwen3 / their MoE variants with the
+ * qwen2moe shared expert, gemma2, phi3). */
 or_model* or_model_load(const char* path, int n_ctx, int kv_f16, char* err, int cap) {
     or_model* m = (or_model*)calloc(1, sizeof(or_model));
     if (!gguf_open(path, &m->g, err, cap)) { or_model_free(m); return NULL; }
@@ -849,7 +868,18 @@ or_model* or_model_load(const char* path, int n_ctx, int kv_f16, char* err, int 
     if (c->n_experts > 0 && c->n_experts_per_tok <= 0) c->n_experts_per_tok = 2;
     if (c->n_experts_per_tok > c->n_experts) c->n_experts_per_tok = c->n_experts;
     c->rot_dim = (int)kv_u(g, arch, "rope.dimension_count", (uint64_t)c->head_dim);
-    c->neox = !strcmp(arch, "qwen2") || !strcmp(arch, "qwen3") || !strcmp(arch, "qwen2moe") || !strcmp(arch, "qwen3moe");
+    c->neox = !strcmp(arch, "qwen2") || !strcmp(arch, "qwen3") || !strcmp(arch, "qwen2moe") || !strcmp(arch, "qwen3moe") ||
+              !strcmp(arch, "gemma2") || !strcmp(arch, "phi3");
+    m->expert_weights_norm = (int)kv_u(g, arch, "expert_weights_norm", strcmp(arch, "qwen2moe") ? 1 : 0);
+    m->embd_scale = 1.0f;
+    if (!strcmp(arch, "gemma2")) {   /* model.cpp:488-496 */
+        m->gemma2 = 1;
+        m->gelu = 1;
+        m->embd_scale = sqrtf((float)c->n_embd);
+        m->attn_softcap = (float)kv_f(g, arch, "attn_logit_softcapping", 50.0);
+        m->final_softcap = (float)kv_f(g, arch, "final_logit_softcapping", 30.0);
+        m->sliding_window = (int)kv_u(g, arch, "attention.sliding_window", 4096);
+    }
     c->n_ctx = n_ctx > 0 ? (n_ctx < ctx_train ? n_ctx : ctx_train) : (ctx_train < 4096 ? ctx_train : 4096);
 
     or_rope_params rp;
@@ -863,7 +893,24 @@ or_model* or_model_load(const char* path, int n_ctx, int kv_f16, char* err, int 
     rp.yarn_attn_factor = 1.0f;
     rp.yarn_beta_fast = 32.0f;
     rp.yarn_beta_slow = 1.0f;
-    const or_tensor* rf = gguf_tensor(g, "rope_freqs.weight");
+    /* longrope (phi3, model.cpp:522-530): the long factor set beyond the
+     * original context, else the short one; the attention factor scales the
+     * rotation. Otherwise Llama-3 style rope_freqs (model.cpp:532-543). */
+    const or_tensor* rf = NULL;
+    {
+        char key[160];
+        snprintf(key, sizeof(key), "%s.rope.scaling.type", arch);
+        const or_kv* st = gguf_kv(g, key);
+        if (st && !strcmp(st->s, "longrope")) {
+            const int orig = (int)kv_u(g, arch, "rope.scaling.original_context_length", 0);
+            rf = (orig > 0 && c->n_ctx > orig) ? gguf_tensor(g, "rope_factors_long.weight")
+                                               : gguf_tensor(g, "rope_factors_short.weight");
+            if (!rf) rf = gguf_tensor(g, "rope_factors_short.weight");
+            rp.mscale = (float)kv_f(g, arch, "rope.scaling.attn_factor", 1.0);
+        } else {
+            rf = gguf_tensor(g, "rope_freqs.weight");
+        }
+    }
     if (rf) { m->rope_freqs = load_vec(rf); rp.freq_factors = m->rope_freqs; }
     const int rot = c->rot_dim > 0 && c->rot_dim < c->head_dim ? c->rot_dim : c->head_dim;
     c->rot_dim = rot;
@@ -872,6 +919,7 @@ or_model* or_model_load(const char* path, int n_ctx, int kv_f16, char* err, int 
     or_rope_build(m->rope_cos, m->rope_sin, c->n_ctx, &rp);
 
     m->out_norm = load_vec(gguf_tensor(g, "output_norm.weight"));
+    if (m->gemma2 && m->out_norm) for (int i = 0; i < c->n_embd; ++i) m->out_norm[i] += 1.0f;
     m->out_w = gguf_tensor(g, "output.weight");
     if (!m->out_w) { m->out_w = m->embd; c->tied_output = 1; }
     if (!m->out_norm) { snprintf(err, (size_t)cap, "missing output_norm.weight"); or_model_free(m); return NULL; }
@@ -889,6 +937,45 @@ or_model* or_model_load(const char* path, int n_ctx, int kv_f16, char* err, int 
         V(attn_norm, "attn_norm.weight"); V(ffn_norm, "ffn_norm.weight");
         V(bq, "attn_q.bias"); V(bk, "attn_k.bias"); V(bv, "attn_v.bias");
         V(q_norm, "attn_q_norm.weight"); V(k_norm, "attn_k_norm.weight");
+        V(bo, "attn_output.bias"); V(bqkv, "attn_qkv.bias");
+        V(post_attn_norm, "post_attention_norm.weight"); V(post_ffn_norm, "post_ffw_norm.weight");
+        T(sh_gate, "ffn_gate_shexp.weight"); T(sh_up, "ffn_up_shexp.weight"); T(sh_down, "ffn_down_shexp.weight");
+        T(sh_gate_inp, "ffn_gate_inp_shexp.weight");
+        if (m->gemma2) {   /* norm weights stored as w - 1 (model.cpp:241-245) */
+            float* nv[4] = {L->attn_norm, L->ffn_norm, L->post_attn_norm, L->post_ffn_norm};
+            for (int j = 0; j < 4; ++j) if (nv[j]) for (int e2 = 0; e2 < c->n_embd; ++e2) nv[j][e2] += 1.0f;
+        }
+        {
+            const or_tensor* f = NULL;
+            T(wq, "attn_qkv.weight");   /* phi3 fused q|k|v (model.cpp:253, 1665-1674) */
+            f = L->wq;
+            if (f) {
+                const int Qd = c->n_head * c->head_dim, KVd = c->n_head_kv * c->head_dim;
+                const uint64_t rb = or_row_bytes(f->type, f->ne[0]);
+                L->vq = *f; L->vq.ne[1] = (uint64_t)Qd;
+                L->vk = *f; L->vk.ne[1] = (uint64_t)KVd; L->vk.data = f->data + rb * (uint64_t)Qd;
+                L->vv = *f; L->vv.ne[1] = (uint64_t)KVd; L->vv.data = f->data + rb * (uint64_t)(Qd + KVd);
+                L->wq = &L->vq; L->wk = &L->vk; L->wv = &L->vv;
+                if (L->bqkv && !L->bq) {
+                    L->bq = (float*)malloc(sizeof(float) * (size_t)Qd);
+                    L->bk = (float*)malloc(sizeof(float) * (size_t)KVd);
+                    L->bv = (float*)malloc(sizeof(float) * (size_t)KVd);
+                    memcpy(L->bq, L->bqkv, sizeof(float) * (size_t)Qd);
+                    memcpy(L->bk, L->bqkv + Qd, sizeof(float) * (size_t)KVd);
+                    memcpy(L->bv, L->bqkv + Qd + KVd, sizeof(float) * (size_t)KVd);
+                }
+            } else {
+                T(wq, "attn_q.weight");
+            }
+        }
+        if (!L->wg && L->wu && c->n_experts == 0 && L->wu->ne[1] == 2 * (uint64_t)c->n_ff) {
+            /* phi3 fused gate|up: ffn_up holds 2 n_ff rows, gate first (model.cpp:1481-1489) */
+            const or_tensor* f = L->wu;
+            const uint64_t rb = or_row_bytes(f->type, f->ne[0]);
+            L->vg = *f; L->vg.ne[1] = (uint64_t)c->n_ff;
+            L->vu = *f; L->vu.ne[1] = (uint64_t)c->n_ff; L->vu.data = f->data + rb * (uint64_t)c->n_ff;
+            L->wg = &L->vg; L->wu = &L->vu;
+        }
 #undef T
 #undef V
         if (!L->attn_norm || !L->ffn_norm || !L->wq || !L->wk || !L->wv || !L->wo) {
@@ -913,6 +1000,7 @@ void or_model_free(or_model* m) {
             or_layer* L = &m->L[i];
             free(L->attn_norm); free(L->ffn_norm); free(L->bq); free(L->bk); free(L->bv);
             free(L->q_norm); free(L->k_norm);
+            free(L->bo); free(L->bqkv); free(L->post_attn_norm); free(L->post_ffn_norm);
         }
         free(m->L);
     }
@@ -945,14 +1033,14 @@ static const uint8_t* expert_ptr(const or_tensor* t, int e) {
 /* model.cpp:1474-1515 (separate gate / up). out[n_tok][n_in]. */
 static void ffn_block_acts(int tg, const void* wg, int tu, const void* wu, int td, const void* wd,
                            const float* x, int n_tok, int n_in, int n_ff, float* out, const void* xk, const void* x32,
-                           const void* hk, const void* h32) {
+                           const void* hk, const void* h32, int gelu) {
     float* g = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)n_ff);
     float* u = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)n_ff);
     matmul_acts(tg, wg, x, xk, x32, n_tok, n_in, n_ff, g);
     matmul_acts(tu, wu, x, xk, x32, n_tok, n_in, n_ff, u);
     for (int t = 0; t < n_tok; ++t) {
         float* gr = g + (size_t)t * n_ff;
-        or_silu_inplace(gr, n_ff);
+        if (gelu) or_gelu_inplace(gr, n_ff); else or_silu_inplace(gr, n_ff);
         for (int i = 0; i < n_ff; ++i) gr[i] *= u[(size_t)t * n_ff + i];
     }
     matmul_acts(td, wd, g, hk, h32, n_tok, n_ff, n_in, out);
@@ -986,7 +1074,7 @@ static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, 
             wsel[t * K + k] = lg[best];
             sum += lg[best];
         }
-        if (sum > 0.0f) for (int k = 0; k < K; ++k) wsel[t * K + k] /= sum;
+        if (m->expert_weights_norm && sum > 0.0f) for (int k = 0; k < K; ++k) wsel[t * K + k] /= sum;
     }
     for (int ex = 0; ex < NE; ++ex) {
         for (int t = 0; t < n_tok; ++t) {
@@ -1000,11 +1088,29 @@ static void moe_ffn(or_model* m, const or_layer* L, const float* xb, int n_tok, 
                                ov && ov->qk[2] ? (const uint8_t*)ov->qk[2] + (size_t)t * (E / 256) * sizeof(or_q8actk) : NULL,
                                ov && ov->q32[2] ? (const uint8_t*)ov->q32[2] + (size_t)t * (E / 32) * sizeof(or_q8act) : NULL,
                                ov && ov->qk[3] ? (const uint8_t*)ov->qk[3] + (size_t)r * (F / 256) * sizeof(or_q8actk) : NULL,
-                               ov && ov->q32[3] ? (const uint8_t*)ov->q32[3] + (size_t)r * (F / 32) * sizeof(or_q8act) : NULL);
+                               ov && ov->q32[3] ? (const uint8_t*)ov->q32[3] + (size_t)r * (F / 32) * sizeof(or_q8act) : NULL, 0);
                 const float w = wsel[t * K + k];
                 for (int i = 0; i < E; ++i) out[(size_t)t * E + i] += w * tmp[i];
             }
         }
+    }
+    /* the shared expert (qwen2moe, model.cpp:1582-1599): every token, scaled
+     * by the sigmoid of its one-row gate when the layer has one */
+    if (L->sh_gate && L->sh_up && L->sh_down) {
+        const int FS = (int)L->sh_gate->ne[1];
+        float* d = (float*)malloc(sizeof(float) * (size_t)n_tok * (size_t)E);
+        ffn_block_acts(L->sh_gate->type, L->sh_gate->data, L->sh_up->type, L->sh_up->data, L->sh_down->type,
+                       L->sh_down->data, xb, n_tok, E, FS, d, NULL, NULL, NULL, NULL, 0);
+        float* gate = (float*)malloc(sizeof(float) * (size_t)n_tok);
+        for (int t = 0; t < n_tok; ++t) gate[t] = 1.0f;
+        if (L->sh_gate_inp) {
+            or_matmul(L->sh_gate_inp->type, L->sh_gate_inp->data, xb, n_tok, E, 1, gate);
+            for (int t = 0; t < n_tok; ++t) gate[t] = 1.0f / (1.0f + expf(-gate[t]));
+        }
+        for (int t = 0; t < n_tok; ++t)
+            for (int i = 0; i < E; ++i) out[(size_t)t * E + i] += gate[t] * d[(size_t)t * E + i];
+        free(gate);
+        free(d);
     }
     free(sel);
     free(wsel);
@@ -1056,16 +1162,23 @@ static void layer_forward(or_model* m, int li, float* x, int n_tok, int pos0, fl
                 vc[(size_t)pos * KV + i] = kv_v;
             }
         }
-        or_attention(q, kc, vc, H, HKV, D, pos0, n_tok, at, scale, 0.0f, 0);
+        /* gemma2: score soft cap, sliding window on the even layers (model.cpp:1735-1739) */
+        const int window = (m->sliding_window > 0 && li % 2 == 0) ? m->sliding_window : 0;
+        or_attention(q, kc, vc, H, HKV, D, pos0, n_tok, at, scale, m->attn_softcap, window);
         matmul_acts(L->wo->type, L->wo->data, at, ak[1], a32[1], n_tok, Q, E, pr);
+        add_bias(pr, n_tok, E, L->bo);
+        if (L->post_attn_norm)
+            for (int t = 0; t < n_tok; ++t) or_rmsnorm(pr + (size_t)t * E, pr + (size_t)t * E, L->post_attn_norm, E, c->eps);
         for (size_t i = 0; i < (size_t)n_tok * E; ++i) x[i] += pr[i];
         for (int t = 0; t < n_tok; ++t) or_rmsnorm(xb + (size_t)t * E, x + (size_t)t * E, L->ffn_norm, E, c->eps);
         if (c->n_experts > 0) {
             moe_ffn(m, L, xb, n_tok, pr, ov);
         } else {
             ffn_block_acts(L->wg->type, L->wg->data, L->wu->type, L->wu->data, L->wd->type, L->wd->data,
-                           xb, n_tok, E, c->n_ff, pr, ak[2], a32[2], ak[3], a32[3]);
+                           xb, n_tok, E, c->n_ff, pr, ak[2], a32[2], ak[3], a32[3], m->gelu);
         }
+        if (L->post_ffn_norm)
+            for (int t = 0; t < n_tok; ++t) or_rmsnorm(pr + (size_t)t * E, pr + (size_t)t * E, L->post_ffn_norm, E, c->eps);
         for (size_t i = 0; i < (size_t)n_tok * E; ++i) x[i] += pr[i];
     }
 }
@@ -1088,6 +1201,8 @@ int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
     for (int t = 0; t < n_tok; ++t) {
         if (tokens[t] < 0 || tokens[t] >= c->vocab) return 0;
         or_dequant_row(m->embd->type, m->embd->data + (size_t)tokens[t] * erow, x + (size_t)t * E, (uint64_t)E);
+        if (m->embd_scale != 1.0f)   /* gemma2 (model.cpp:1624-1627) */
+            for (int i = 0; i < E; ++i) x[(size_t)t * E + i] *= m->embd_scale;
     }
     for (int li = 0; li < c->n_layers; ++li) layer_forward(m, li, x, n_tok, pos0, xb, q, k, v, at, pr, NULL);
     memcpy(m->last_x, x + (size_t)(n_tok - 1) * E, sizeof(float) * (size_t)E);
@@ -1096,6 +1211,8 @@ int or_model_forward(or_model* m, const int32_t* tokens, int n_tok, int pos0,
     for (int t = 0; t < rows; ++t) or_rmsnorm(xb + (size_t)t * E, x + (size_t)(first + t) * E, m->out_norm, E, c->eps);
     float* out = logits_all ? logits_all : logits;
     or_matmul(m->out_w->type, m->out_w->data, xb, rows, E, c->vocab, out);
+    if (m->final_softcap > 0.0f)   /* gemma2 (model.cpp:1802-1805) */
+        for (size_t i = 0; i < (size_t)rows * c->vocab; ++i) out[i] = m->final_softcap * tanhf(out[i] / m->final_softcap);
     if (logits_all && logits) memcpy(logits, logits_all + (size_t)(n_tok - 1) * c->vocab, sizeof(float) * (size_t)c->vocab);
     m->kv_len = pos0 + n_tok;
     free(x); free(xb); free(q); free(k); free(v); free(at); free(pr);

@@ -74,6 +74,7 @@ void or_matmul(int type, const void* w, const float* x, int n_tok, int n_in,
 /* ---- glue (ops.cpp:18-55) ----------------------------------------------------- */
 void or_rmsnorm(float* out, const float* x, const float* w, int n, float eps);
 void or_silu_inplace(float* x, int n);
+void or_gelu_inplace(float* x, int n);
 void or_softmax_inplace(float* x, int n);
 
 /* RoPE table (ops.cpp:75-124): cos/sin [n_ctx][rot_dim/2]. */
