@@ -43,7 +43,11 @@ BLK = {8: 32, 12: 256, 14: 256}
 
 # preset, prompt rows, sampled weight rows per matrix
 # (qwen3: the per-head q/k RMSNorm layers, not a benchmark config)
-CONFIGS = [("llama8b", 20, 24), ("qwen7b", 20, 24), ("mixtral", 18, 16), ("llama70b", 17, 16), ("qwen3", 19, 24)]
+# (gemma2: a 70-row prompt so the 64-position window of the even layers
+# bites; phi3-d96: fused q|k|v and gate|up at head dimension 96; qwen2moe:
+# routed experts plus the gated shared expert)
+CONFIGS = [("llama8b", 20, 24), ("qwen7b", 20, 24), ("mixtral", 18, 16), ("llama70b", 17, 16), ("qwen3", 19, 24),
+           ("gemma2", 70, 24), ("phi3-d96", 20, 24), ("qwen2moe", 18, 16)]
 
 
 @pytest.fixture(scope="module")
@@ -118,7 +122,7 @@ def _records(res):
     return qk, q32
 
 
-def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_exp, rows, rng, label):
+def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_exp, rows, rng, label, plus1=False):
     st = res["stages"]
     # the layer output on the same int8 activations: every element inside
     # the north-star bar
@@ -131,8 +135,8 @@ def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_e
     print(f"{label}: same activations max |d| {d.max():.3g}; own activations max |d| {d_own.max():.3g}, "
           f"{100 * inside:.2f}% inside the bar")
     assert d_own.max() <= 0.02 * np.abs(want_out).max(), f"{label}: {d_own.max()}"
-    an = om.tensor_f32(f"blk.{layer}.attn_norm.weight")
-    fn = om.tensor_f32(f"blk.{layer}.ffn_norm.weight")
+    an = om.tensor_f32(f"blk.{layer}.attn_norm.weight") + (1.0 if plus1 else 0.0)   # gemma2 stores w - 1
+    fn = om.tensor_f32(f"blk.{layer}.ffn_norm.weight") + (1.0 if plus1 else 0.0)
     # stage 0: the rows the GPU normalised are the test's input rows
     assert np.array_equal(st[0]["f"], x_in), label
     _check_records(oracle, st[0], _rms(oracle, x_in, an, eps), f"{label} attn-norm")
@@ -142,8 +146,9 @@ def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_e
         pytest.fail(f"{label}: the SwiGLU product was formed in a GEMV prologue (not the default path)")
     _check_records(oracle, st[3], st[3]["f"], f"{label} swiglu")
     p = f"blk.{layer}."
-    _check_block_sums(gpu, oracle, om, st[0], [p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"], rows,
-                      rng, label)
+    qkv = ([p + "attn_qkv.weight"] if om.tensor(p + "attn_qkv.weight") is not None
+           else [p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"])   # phi3: fused rows
+    _check_block_sums(gpu, oracle, om, st[0], qkv, rows, rng, label)
     _check_block_sums(gpu, oracle, om, st[1], [p + "attn_output.weight"], rows, rng, label)
     if n_exp:
         e = int(rng.integers(0, n_exp))
@@ -151,7 +156,9 @@ def _check_layer(gpu, oracle, om, res, x_in, want_out, same_out, layer, eps, n_e
                           label, expert=e)
         _check_block_sums(gpu, oracle, om, st[3], [p + "ffn_down_exps.weight"], rows, rng, label, expert=e)
     else:
-        _check_block_sums(gpu, oracle, om, st[2], [p + "ffn_gate.weight", p + "ffn_up.weight"], rows, rng, label)
+        gu = ([p + "ffn_gate.weight", p + "ffn_up.weight"] if om.tensor(p + "ffn_gate.weight") is not None
+              else [p + "ffn_up.weight"])   # phi3: gate|up in one tensor
+        _check_block_sums(gpu, oracle, om, st[2], gu, rows, rng, label)
         _check_block_sums(gpu, oracle, om, st[3], [p + "ffn_down.weight"], rows, rng, label)
     return float(d.max())
 
@@ -169,6 +176,9 @@ def test_layers_at_config_widths(gpu, oracle, synth_dir, monkeypatch, preset, P,
     t, (E, _, _), _ = om.tensor("token_embd.weight")
     emb = om.tensor_rows("token_embd.weight", ids)
     h = np.stack([oracle.dequant(t, r, E) for r in emb]).astype(np.float32)
+    plus1 = cfg.arch == "gemma2"
+    if plus1:
+        h = (h * np.float32(np.sqrt(np.float32(E)))).astype(np.float32)   # gemma2's embedding scale
     worst = []
     with Model(path, 256) as gm:
         for layer in range(cfg.n_layers):
@@ -177,13 +187,13 @@ def test_layers_at_config_widths(gpu, oracle, synth_dir, monkeypatch, preset, P,
             same = om.layer_acts(layer, h[:P], 0, *_records(res))
             want = om.layer(layer, h[:P], 0)
             worst.append(_check_layer(gpu, oracle, om, res, h[:P], want, same, layer, cfg.eps, cfg.n_experts, rows,
-                                      rng, f"{preset} layer {layer} prompt"))
+                                      rng, f"{preset} layer {layer} prompt", plus1))
             # one decode row: fused GEMV prologues, fused decode attention
             res1 = gm.layer_probe(layer, h[P:P + 1], P)
             same1 = om.layer_acts(layer, h[P:P + 1], P, *_records(res1))
             want1 = om.layer(layer, h[P:P + 1], P)
             worst.append(_check_layer(gpu, oracle, om, res1, h[P:P + 1], want1, same1, layer, cfg.eps, cfg.n_experts,
-                                      rows, rng, f"{preset} layer {layer} decode"))
+                                      rows, rng, f"{preset} layer {layer} decode", plus1))
             h = np.concatenate([want, want1])
     om.close()
     print(f"{preset}: max |d| per (layer, path) = {[round(w, 6) for w in worst]}")
