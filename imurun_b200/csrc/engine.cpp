@@ -575,25 +575,21 @@ bool Engine::upload_weights(std::string* err) {
     struct Job { const Tensor* t; DevW* w; size_t off; };
     std::vector<Job> jobs;
     size_t total = 0;
-    auto add = [&](const std::string&, DevW* w) {
+    // every bound matrix, uploaded from the GGUF tensor it names (a fused
+    // tensor's views each take their own rows)
+    auto add = [&](DevW* w) {
         if (w->type < 0) return;
         const Tensor* t = g.find(w->name);
         if (!t) return;
         jobs.push_back({t, w, total});
         total = align_up(total + w->expert_bytes * (size_t)w->n_exp, 256);
     };
-    add("token_embd.weight", &embd_);
-    if (!cfg_.tied_output) add("output.weight", &out_w_);
-    for (int i = 0; i < cfg_.n_layers; ++i) {
-        const std::string p = "blk." + std::to_string(i) + ".";
-        DevLayer& L = layers_[i];
-        add(p + "attn_q.weight", &L.wq); add(p + "attn_k.weight", &L.wk); add(p + "attn_v.weight", &L.wv);
-        add(p + "attn_output.weight", &L.wo);
-        add(p + "ffn_gate.weight", &L.wg); add(p + "ffn_up.weight", &L.wu); add(p + "ffn_down.weight", &L.wd);
-        add(p + "ffn_gate_inp.weight", &L.gate_inp); add(p + "ffn_gate_exps.weight", &L.gate_exps);
-        add(p + "ffn_up_exps.weight", &L.up_exps); add(p + "ffn_down_exps.weight", &L.down_exps);
-        add("", &L.shexp_gate); add("", &L.shexp_up); add("", &L.shexp_down); add("", &L.shexp_gate_inp);
-    }
+    add(&embd_);
+    if (!cfg_.tied_output) add(&out_w_);
+    for (DevLayer& L : layers_)
+        for (DevW* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd, &L.gate_inp, &L.gate_exps, &L.up_exps,
+                        &L.down_exps, &L.shexp_gate, &L.shexp_up, &L.shexp_down, &L.shexp_gate_inp})
+            add(w);
     weights_dev_bytes_ = total;
     CK(cudaMalloc(&warena_, total + 256));
     for (Job& j : jobs) j.w->d = warena_ + j.off;
