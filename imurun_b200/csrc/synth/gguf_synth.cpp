@@ -349,6 +349,7 @@ typedef struct fish_synth_config {
     // one-row F32 sigmoid gate (qwen2moe)
     int n_ff_shexp;
     int o_bias;                  // 1: attn_output.bias
+    int no_bos;                  // 1: tokenizer.ggml.add_bos_token = false (Qwen-style files)
 } fish_synth_config;
 
 __attribute__((visibility("default")))
@@ -504,7 +505,7 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
         ++n_kv;
         w.kv_u32("tokenizer.ggml.bos_token_id", static_cast<uint32_t>(bv.bos)); ++n_kv;
         w.kv_u32("tokenizer.ggml.eos_token_id", static_cast<uint32_t>(bv.eos)); ++n_kv;
-        w.kv_bool("tokenizer.ggml.add_bos_token", true); ++n_kv;
+        w.kv_bool("tokenizer.ggml.add_bos_token", !c->no_bos); ++n_kv;
     } else {
     // SentencePiece dummy vocabulary: <unk> <s> </s>, 256 byte tokens, then
     // "▁t<i>" pieces up to the vocabulary size.
@@ -527,7 +528,7 @@ int fish_synth_write(const char* path, const fish_synth_config* c, int n_threads
     w.kv_u32("tokenizer.ggml.bos_token_id", 1); ++n_kv;
     w.kv_u32("tokenizer.ggml.eos_token_id", 2); ++n_kv;
     w.kv_u32("tokenizer.ggml.unknown_token_id", 0); ++n_kv;
-    w.kv_bool("tokenizer.ggml.add_bos_token", true); ++n_kv;
+    w.kv_bool("tokenizer.ggml.add_bos_token", !c->no_bos); ++n_kv;
     }
     if (c->chat_template && c->chat_template[0]) { w.kv_str("tokenizer.chat_template", c->chat_template); ++n_kv; }
     std::memcpy(w.buf.data() + n_kv_pos, &n_kv, 8);

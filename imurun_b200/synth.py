@@ -60,6 +60,7 @@ class SynthConfig:
     rope_attn_factor: float = 0.0   # phi3 longrope: rotation scale (0: 1)
     n_ff_shexp: int = 0         # MoE shared expert rows with a sigmoid gate (qwen2moe; 0: none)
     o_bias: int = 0             # 1: attn_output.bias
+    no_bos: int = 0             # 1: tokenizer.ggml.add_bos_token false
 
 
 PRESETS = {
@@ -117,7 +118,7 @@ class _CConfig(ctypes.Structure):
         ("attn_softcap", ctypes.c_float), ("final_softcap", ctypes.c_float),
         ("sliding_window", ctypes.c_int),
         ("rope_orig_ctx", ctypes.c_int), ("rope_attn_factor", ctypes.c_float),
-        ("n_ff_shexp", ctypes.c_int), ("o_bias", ctypes.c_int),
+        ("n_ff_shexp", ctypes.c_int), ("o_bias", ctypes.c_int), ("no_bos", ctypes.c_int),
     ]
 
 
@@ -141,7 +142,7 @@ def write(path: str | os.PathLike, cfg: SynthConfig, threads: int = 0) -> Path:
                  cfg.n_experts_per_tok, cfg.qkv_bias, cfg.wtype, cfg.seed, cfg.wstd, cfg.router_std,
                  cfg.chat_template.encode(), cfg.bpe_pre.encode(), cfg.qk_norm, cfg.attn_softcap,
                  cfg.final_softcap, cfg.sliding_window, cfg.rope_orig_ctx, cfg.rope_attn_factor, cfg.n_ff_shexp,
-                 cfg.o_bias)
+                 cfg.o_bias, cfg.no_bos)
     err = ctypes.create_string_buffer(256)
     rc = fn(str(path).encode(), ctypes.byref(c), int(threads), err, 256)
     if rc != 0:

@@ -76,6 +76,9 @@ GGUFS = {
     # the reference does not list (its default split)
     "bpe-gpt2": lambda synth: synth.preset("tiny", layers=1, bpe_pre="gpt-2"),
     "bpe-unlisted": lambda synth: synth.preset("tiny", layers=1, bpe_pre="not-a-listed-pre"),
+    # a file that asks for no BOS (tokenizer.ggml.add_bos_token false, as
+    # Qwen's do): chat prompts and counts start without one
+    "bpe-qwen2-nobos": lambda synth: synth.preset("tiny", layers=1, bpe_pre="qwen2", no_bos=1),
 }
 
 
