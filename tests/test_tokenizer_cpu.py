@@ -27,7 +27,13 @@ P, I, CP = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
 TEXTS = ["Hello world", "  leading spaces", "tabs\tand\nnewlines", "héllo 世界 \U0001f642", "",
          "<s>hi</s>", "t300 t1000 t31999", "a", " ", "x" * 300]
 CHATS = [[("system", "Be brief."), ("user", "Hi there"), ("assistant", "Hello!"), ("user", "t300?")],
-         [("user", "éè and <s> tags")]]
+         [("user", "éè and <s> tags")],
+         # tool results, two system turns, an empty turn, a role no format
+         # names, and a conversation that ends on the assistant
+         [("system", "Tools: lookup"), ("user", "find t17"), ("assistant", "calling lookup"),
+          ("tool", "{\"t17\": 4}"), ("user", "and?")],
+         [("system", "one"), ("system", "two"), ("user", ""), ("function", "raw"), ("assistant", "ok")],
+         [("system", "only a system turn")]]
 
 
 @pytest.fixture(scope="module")
