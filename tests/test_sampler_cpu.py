@@ -16,7 +16,11 @@ P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 ARGS = [P, I, F, I, F, F, I, P, I, ctypes.c_uint64, I, P]
 PARAMS = [  # temperature, top_k, top_p, repeat_penalty, repeat_last_n
     (0.7, 40, 0.9, 1.1, 64), (1.0, 0, 1.0, 1.0, 64), (0.2, 5, 0.95, 1.3, 8), (1.5, 100, 0.5, 1.0, 64),
-    (0.0, 40, 0.9, 1.1, 64), (0.8, 1, 0.9, 1.1, 64), (1.0, 40, 0.0, 1.2, 0)]
+    (0.0, 40, 0.9, 1.1, 64), (0.8, 1, 0.9, 1.1, 64), (1.0, 40, 0.0, 1.2, 0),
+    # edges: a tiny temperature, top-k past the vocabulary, a penalty below 1,
+    # a window longer than the recent ids, a non-positive penalty (ignored)
+    (0.01, 0, 1.0, 1.0, 64), (1.0, 50000, 1.0, 1.0, 64), (0.7, 40, 0.9, 0.5, 64), (0.7, 40, 0.9, 1.1, 500),
+    (0.9, 20, 0.8, 0.0, 64)]
 
 
 @pytest.fixture(scope="module")
@@ -50,7 +54,7 @@ def test_sampler_matches_reference(libs, vocab, k):
     assert ours.fbx_sample(logits.ctypes.data, vocab, temp, top_k, top_p, pen, last_n, recent.ctypes.data,
                            recent.size, 4242 + k, n, got.ctypes.data) == 0
     assert np.array_equal(got, want), (list(got[:16]), list(want[:16]))
-    if temp > 0 and top_k != 1 and top_p >= 0.5:
+    if temp >= 0.5 and top_k != 1 and top_p >= 0.5 and pen >= 1.0:
         assert len(set(want.tolist())) > 1    # the draws do vary: the generator is exercised
 
 
