@@ -105,3 +105,47 @@ def test_synth_refuses_without_disk_space_and_leaves_no_partial_file(tmp_path, m
     with pytest.raises(RuntimeError, match="write failed"):
         synth.cached(synth.preset("tiny"), tmp_path)
     assert list(tmp_path.iterdir()) == []
+
+
+@pytest.mark.parametrize("damage", ["magic", "version", "truncated_header", "truncated_data", "huge_count",
+                                    "bad_type", "empty"])
+def test_damaged_files_rejected_like_reference(ref_lib, ours, synth_dir, tmp_path, damage):
+    """A damaged GGUF is refused by this library's reader exactly when the
+    reference's GgufFile refuses it (src/gguf.cpp), and when both accept it
+    they read the same directory: wrong magic or version, a header or data
+    cut short, an absurd tensor count, an unknown tensor type, an empty
+    file."""
+    import struct
+    from imurun_b200 import synth
+    src = synth.cached(synth.preset("tiny", layers=1), synth_dir)
+    b = bytearray(src.read_bytes())
+    if damage == "magic":
+        b[0:4] = b"GGUX"
+    elif damage == "version":
+        b[4:8] = struct.pack("<I", 99)
+    elif damage == "truncated_header":
+        b = b[:200]
+    elif damage == "truncated_data":
+        b = b[:len(b) - 4096]
+    elif damage == "huge_count":
+        b[8:16] = struct.pack("<Q", 1 << 40)
+    elif damage == "bad_type":
+        # the first tensor's type field: after its name, n_dims and dims
+        hdr_end = b.find(b"token_embd.weight")
+        assert hdr_end > 0
+        p = hdr_end + len(b"token_embd.weight")
+        n_dims = struct.unpack_from("<I", b, p)[0]
+        p += 4 + 8 * n_dims
+        b[p:p + 4] = struct.pack("<I", 250)
+    elif damage == "empty":
+        b = bytearray()
+    path = tmp_path / f"{damage}.gguf"
+    path.write_bytes(bytes(b))
+    keys = ["general.architecture"]
+    arr = (ctypes.c_char_p * 1)(*[k.encode() for k in keys])
+    want = ref_lib.ref_gguf_digest(str(path).encode(), ctypes.cast(arr, P), 1, None, 0)
+    got = ours.fbx_gguf_digest(str(path).encode(), ctypes.cast(arr, P), 1, None, 0)
+    assert (got < 0) == (want < 0), (damage, got, want)
+    if want >= 0:
+        assert _digest(ours.fbx_gguf_digest, path, keys).splitlines() == \
+            _digest(ref_lib.ref_gguf_digest, path, keys).splitlines()
