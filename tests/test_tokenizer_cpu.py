@@ -219,3 +219,21 @@ def test_chat_formats_match_reference(ref_lib, ours, synth_dir, name):
 
 def test_unreadable_file(ours):
     assert ours.fbx_tokenize_gguf(b"/nonexistent.gguf", b"hi", 1, None, 0) == -1
+
+
+def test_detokenize_edge_ids_match_reference(ref_lib, ours, ref_ctx, gguf):
+    """Ids the vocabulary does not hold (negative, past the end), control
+    tokens, byte tokens that do not form UTF-8, and an empty list: the same
+    bytes (or the same refusal) as the reference's fish_detokenize."""
+    vocab = 32000
+    cases = [[], [1], [2], [0], [-1], [vocab], [vocab + 5], [3, 4, 5], [3 + 0xC3], [3 + 0xE6, 3 + 0x97],
+             [1, 300, 2, 301], [259, -7, 260]]
+    for ids in cases:
+        a = np.ascontiguousarray(ids if ids else [0], np.int32)
+        n = len(ids)
+        want = ref_lib.fish_detokenize(ref_ctx, a.ctypes.data, n, None, 0)
+        got = ours.fbx_detokenize_gguf(str(gguf).encode(), a.ctypes.data, n, None, 0)
+        assert (got < 0) == (want < 0), (ids, got, want)
+        if want >= 0:
+            assert _str(ours.fbx_detokenize_gguf, str(gguf).encode(), a.ctypes.data, n) == \
+                _str(ref_lib.fish_detokenize, ref_ctx, a.ctypes.data, n), ids
