@@ -139,9 +139,9 @@ class Oracle:
         self.L.or_rmsnorm(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), x.size, eps)
         return out
 
-    def attention(self, q, kc, vc, H, HKV, D, pos0, n_tok, scale):
+    def attention(self, q, kc, vc, H, HKV, D, pos0, n_tok, scale, softcap=0.0, window=0):
         out = np.zeros((n_tok, H * D), np.float32)
-        self.L.or_attention(_ptr(q), _ptr(kc), _ptr(vc), H, HKV, D, pos0, n_tok, _ptr(out), scale, 0.0, 0)
+        self.L.or_attention(_ptr(q), _ptr(kc), _ptr(vc), H, HKV, D, pos0, n_tok, _ptr(out), scale, softcap, window)
         return out
 
     def fp16_round(self, x: np.ndarray) -> np.ndarray:
@@ -250,6 +250,7 @@ class Reference:
         L.ref_quantize_row.restype = I
         L.ref_rmsnorm.argtypes = [P, P, P, I, F]
         L.ref_attention.argtypes = [P, P, P, I, I, I, I, I, I, P, F]
+        L.ref_attention_capped.argtypes = [P, P, P, I, I, I, I, I, I, P, F, F, I]
         L.ref_rope_table.argtypes = [I, I, I, I, F, P, P]
         L.ref_kernel_name.restype = ctypes.c_char_p
         L.ref_set_threads.argtypes = [I]
@@ -300,9 +301,13 @@ class Reference:
         self.L.ref_rmsnorm(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), x.size, eps)
         return out
 
-    def attention(self, q, kc, vc, n_ctx, H, HKV, D, pos0, n_tok, scale):
+    def attention(self, q, kc, vc, n_ctx, H, HKV, D, pos0, n_tok, scale, softcap=0.0, window=0):
         out = np.zeros((n_tok, H * D), np.float32)
-        self.L.ref_attention(_ptr(q), _ptr(kc), _ptr(vc), n_ctx, H, HKV, D, pos0, n_tok, _ptr(out), scale)
+        if softcap or window:
+            self.L.ref_attention_capped(_ptr(q), _ptr(kc), _ptr(vc), n_ctx, H, HKV, D, pos0, n_tok, _ptr(out), scale,
+                                        softcap, window)
+        else:
+            self.L.ref_attention(_ptr(q), _ptr(kc), _ptr(vc), n_ctx, H, HKV, D, pos0, n_tok, _ptr(out), scale)
         return out
 
     def rope_table(self, n_ctx, D, rot, neox, base):

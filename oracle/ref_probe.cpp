@@ -60,6 +60,13 @@ __attribute__((visibility("default"))) void ref_attention(const float* q, const 
                                                           float* out, float scale) {
     attention_batch(q, k, v, n_ctx, n_head, n_head_kv, head_dim, pos0, n_tok, out, scale, 0.0f, 0);
 }
+/* The same with gemma2's score soft cap and sliding window. */
+__attribute__((visibility("default"))) void ref_attention_capped(const float* q, const float* k, const float* v,
+                                                                 int n_ctx, int n_head, int n_head_kv, int head_dim,
+                                                                 int pos0, int n_tok, float* out, float scale,
+                                                                 float softcap, int window) {
+    attention_batch(q, k, v, n_ctx, n_head, n_head_kv, head_dim, pos0, n_tok, out, scale, softcap, window);
+}
 __attribute__((visibility("default"))) void ref_rope_table(int n_ctx, int head_dim, int rot_dim, int neox,
                                                            float freq_base, float* cos_out, float* sin_out) {
     RopeParams p;

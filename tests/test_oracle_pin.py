@@ -237,3 +237,20 @@ def test_quality_metric_against_reference(oracle, reference, synth_dir, preset):
     print(f"{preset}: top-1 {top1:.3f}, KL mean {np.mean(kl):.2e} max {max(kl):.2e}")
     assert top1 >= 0.95
     assert np.mean(kl) <= 1e-4 and max(kl) <= 1e-3
+
+
+@pytest.mark.parametrize("n_tok,softcap,window", [(1, 0.5, 16), (5, 0.0, 8), (5, 2.0, 0), (7, 0.3, 40)])
+def test_live_reference_attention_softcap_window(oracle, reference, n_tok, softcap, window):
+    """Gemma-2's attention deltas in the restatement (ops.cpp attention_batch:
+    cap * tanh(score / cap), keys pos - window + 1 .. pos) against the
+    reference's own attention on the same rows."""
+    rng = np.random.default_rng(n_tok + window)
+    H, HKV, D, n_ctx, pos0 = 8, 4, 128, 64, 37
+    q = rng.standard_normal((n_tok, H * D)).astype(np.float32)
+    k = rng.standard_normal((n_ctx, HKV * D)).astype(np.float32)
+    v = rng.standard_normal((n_ctx, HKV * D)).astype(np.float32)
+    a = reference.attention(q, k, v, n_ctx, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D), softcap, window)
+    b = oracle.attention(q, k, v, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D), softcap, window)
+    assert np.abs(a - b).max() < 1e-5
+    plain = oracle.attention(q, k, v, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D))
+    assert np.abs(b - plain).max() > 1e-3   # the cap / window change the output
