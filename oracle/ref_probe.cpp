@@ -55,6 +55,10 @@ __attribute__((visibility("default"))) int ref_quantize_row(int type, const floa
 __attribute__((visibility("default"))) void ref_rmsnorm(float* out, const float* x, const float* w, int n, float eps) {
     rmsnorm(out, x, w, n, eps);
 }
+__attribute__((visibility("default"))) void ref_act(float* x, int n, int gelu) {
+    if (gelu) gelu_inplace(x, n);
+    else silu_inplace(x, n);
+}
 __attribute__((visibility("default"))) void ref_attention(const float* q, const float* k, const float* v, int n_ctx,
                                                           int n_head, int n_head_kv, int head_dim, int pos0, int n_tok,
                                                           float* out, float scale) {

@@ -254,3 +254,18 @@ def test_live_reference_attention_softcap_window(oracle, reference, n_tok, softc
     assert np.abs(a - b).max() < 1e-5
     plain = oracle.attention(q, k, v, H, HKV, D, pos0, n_tok, 1 / np.sqrt(D))
     assert np.abs(b - plain).max() > 1e-3   # the cap / window change the output
+
+
+def test_live_reference_activations(oracle, reference):
+    """SiLU and gemma2's tanh-form GELU (ops.cpp:25-38): the restatement's
+    values equal the reference's bit for bit over a wide input range."""
+    import ctypes
+    x = np.concatenate([np.linspace(-20, 20, 40001), np.random.default_rng(3).standard_normal(4096) * 4]).astype(np.float32)
+    reference.L.ref_act.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+    oracle.L.or_gelu_inplace.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    oracle.L.or_silu_inplace.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    for gelu in (0, 1):
+        a, b = x.copy(), x.copy()
+        reference.L.ref_act(a.ctypes.data, a.size, gelu)
+        (oracle.L.or_gelu_inplace if gelu else oracle.L.or_silu_inplace)(b.ctypes.data, b.size)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), gelu
